@@ -1,0 +1,340 @@
+"""Asynchronous speculative decoding coordinator (single request and batched).
+
+This restates the reference's two decode loops in one batched loop:
+
+* single request, ``single/eval_async_packed.py:796-1297``
+  (``run_d3d_generate_async``): submit the current block to the target, run
+  the packed all-outcome draft while the target verifies, commit
+  ``accepted + 1`` tokens, reuse the branch keyed
+  ``(commit_len, correction)`` or redraft from the anchor on a miss;
+* concurrent serving, ``serving/engine.py:148-227``: the same step over every
+  running request, strict admission up to ``concurrency``, prefill in groups,
+  draft micro-batches, and leak checks at the end.
+
+Decode accounting follows the reference: ``accept_length`` is the number of
+tokens committed per verify, anchor included
+(``single/eval_async_packed.py:1097,1150``); single-request throughput is
+decode-only (prefill and the first token excluded); concurrent throughput is
+end to end.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Callable, Dict, Iterable, List, Optional, Sequence, Tuple
+
+import torch
+
+from .backends import DraftBackend, SeqState, TargetBackend
+from .layout import BranchKey, branch_specs, full_rows, packed_layout
+from .sampling import is_greedy
+
+EOS_DEFAULT = (151643, 151645)
+
+
+@dataclass
+class DecodeConfig:
+    block_size: int = 16
+    anchor_num: int = 1
+    attention_mask_mode: str = "causal"
+    max_new_tokens: int = 512
+    temperature: float = 0.0
+    top_k: int = 0            # proposal top-k (sampling)
+    top_p: float = 1.0
+    draft_microbatch: int = 4
+    prefill_group: int = 4
+    ignore_eos: bool = False
+    eos: Tuple[int, ...] = EOS_DEFAULT
+    packed_accepted_counts: Optional[Tuple[int, ...]] = None
+    use_cond: bool = True     # feed target hidden to a conditioned drafter
+
+    def validate(self):
+        if self.block_size <= 1:
+            raise ValueError("--block-size must be > 1")
+        if self.anchor_num < 0:
+            raise ValueError("--anchor-num must be non-negative")
+        if not is_greedy(self.temperature) and self.top_k <= 0:
+            raise ValueError("temperature > 0 async sampling requires --proposal-top-k > 0")
+        return self
+
+
+@dataclass
+class RequestOutput:
+    index: int
+    tokens: List[int]
+    accepts: List[int]
+    sources: List[str]
+    hits: int
+    recoveries: int
+    latency_s: float
+
+
+class SpecDecoder:
+    """Drives a target backend and a draft backend through the async loop."""
+
+    def __init__(self, target: TargetBackend, draft: DraftBackend, cfg: DecodeConfig,
+                 overlap: bool = True):
+        self.t, self.d, self.cfg = target, draft, cfg.validate()
+        self.overlap = overlap
+        self.stats: Dict[str, float] = {}
+
+    # ------------------------------------------------------------ helpers
+    def _controlled(self, s: SeqState, block: torch.Tensor, top, anchor_pos: int):
+        if s.controlled is not None:
+            s.controlled.override(block, top, anchor_pos)
+
+    def _sample_cfg(self):
+        c = self.cfg
+        if is_greedy(c.temperature):
+            return None
+        return dict(temperature=c.temperature, top_k=c.top_k, top_p=c.top_p)
+
+    def _cond_rows(self, b: int, q: int, starts: Sequence[int]):
+        if not self.cfg.use_cond:
+            return None
+        cr = torch.zeros(b, q, dtype=torch.bool)
+        for st in starts:
+            cr[:, st] = True
+        return cr
+
+    # ----------------------------------------------------------- recovery
+    def recover(self, seqs: List[SeqState]) -> None:
+        """Draft ``[anchor, MASK x K-1]`` from each anchor in one forward
+        (``single/eval_async_packed.py:950-984``; ``serving/engine.py:54-62``)."""
+        k, a = self.cfg.block_size, self.cfg.anchor_num
+        for off in range(0, len(seqs), self.cfg.draft_microbatch):
+            group = seqs[off:off + self.cfg.draft_microbatch]
+            b = len(group)
+            ids = torch.full((b, k), self.d.mask_id, dtype=torch.long)
+            ids[:, 0] = torch.tensor([s.anchor for s in group])
+            pos = torch.stack([torch.arange(s.prefix, s.prefix + k) for s in group])
+            rows = torch.stack([full_rows(s.prefix + k, k) for s in group])
+            out = self.d.forward(group, ids, pos, rows, store=False, topk=a + 1 if a else 0,
+                                 cond_rows=self._cond_rows(b, k, [0]),
+                                 sample=self._sample_cfg())
+            toks = out["tokens"] if "tokens" in out else out["greedy"]
+            for i, s in enumerate(group):
+                blk = toks[i].clone().cpu()
+                blk[0] = s.anchor
+                top = out["top"][i].clone().cpu() if "top" in out else None
+                self._controlled(s, blk, top, s.prefix)
+                s.current, s.top = blk, top
+                if "q_ids" in out:
+                    s.q_ids, s.q_probs = out["q_ids"][i].cpu(), out["q_probs"][i].cpu()
+                s.recoveries += 1
+                s.source = "redraft"
+
+    # ------------------------------------------------------ packed outcomes
+    def predict(self, seqs: List[SeqState]) -> Dict[int, Dict[BranchKey, tuple]]:
+        """One packed forward per micro-batch: commit the pending block into the
+        draft KV and draft one continuation per (commit length, anchor)."""
+        k, a = self.cfg.block_size, self.cfg.anchor_num
+        results: Dict[int, Dict[BranchKey, tuple]] = {}
+        for off in range(0, len(seqs), self.cfg.draft_microbatch):
+            group = seqs[off:off + self.cfg.draft_microbatch]
+            layouts = []
+            for s in group:
+                top = None if s.top is None else s.top.tolist()
+                specs = branch_specs(s.current.tolist(), top, a, self.cfg.packed_accepted_counts)
+                layouts.append(packed_layout(s.current, specs, s.prefix, k, self.d.mask_id,
+                                             self.cfg.attention_mask_mode))
+            q = layouts[0].q_len
+            if any(l.q_len != q for l in layouts):
+                raise RuntimeError("packed layouts in one micro-batch must have equal length")
+            ids = torch.stack([l.input_ids for l in layouts])
+            pos = torch.stack([l.positions for l in layouts])
+            rows = torch.stack([l.rows for l in layouts])
+            seg_starts = [0] + [k + j * k for j in range(len(layouts[0].keys))]
+            out = self.d.forward(group, ids, pos, rows, store=True, topk=a + 1 if a else 0,
+                                 cond_rows=self._cond_rows(len(group), q, seg_starts),
+                                 sample=self._sample_cfg())
+            toks = out["tokens"] if "tokens" in out else out["greedy"]
+            for i, (s, lay) in enumerate(zip(group, layouts)):
+                self.d.trim(s, s.prefix + k)
+                outcomes = {}
+                for j, key in enumerate(lay.keys):
+                    sl = lay.segment(j)
+                    blk = toks[i, sl].clone().cpu()
+                    if key[1] is not None:
+                        blk[0] = key[1]
+                    top = out["top"][i, sl].clone().cpu() if "top" in out else None
+                    qq = None
+                    if "q_ids" in out:
+                        qq = (out["q_ids"][i, sl].cpu(), out["q_probs"][i, sl].cpu())
+                    outcomes[key] = (blk, top, qq)
+                results[s.index] = outcomes
+        return results
+
+    # ------------------------------------------------------------ main loop
+    def generate(self, prompts: Sequence[Sequence[int]], concurrency: int = 1,
+                 controlled: Optional[Callable[[int], object]] = None,
+                 on_step: Optional[Callable[[int], None]] = None) -> dict:
+        cfg = self.cfg
+        k = cfg.block_size
+        if concurrency < 1 or cfg.max_new_tokens < 1:
+            raise ValueError("positive concurrency and output length required")
+        waiting = iter(enumerate(prompts))
+        running: List[SeqState] = []
+        outputs: List[RequestOutput] = []
+        exhausted = False
+        started = time.perf_counter()
+        steps = 0
+        verify_tokens = 0
+        miss_rounds = 0
+        batch_sizes: List[int] = []
+        while running or not exhausted:
+            admitted: List[SeqState] = []
+            while len(running) + len(admitted) < concurrency and not exhausted:
+                try:
+                    idx, ids = next(waiting)
+                except StopIteration:
+                    exhausted = True
+                    break
+                s = SeqState(index=idx, prompt=[int(t) for t in ids], prefix=len(ids),
+                             born=time.perf_counter())
+                s.controlled = controlled(idx) if controlled is not None else None
+                admitted.append(s)
+            for off in range(0, len(admitted), cfg.prefill_group):
+                group = admitted[off:off + cfg.prefill_group]
+                anchors, hidden = self.t.prefill(group)
+                self.d.prefill(group, cfg.attention_mask_mode, k)
+                ready = []
+                for i, s in enumerate(group):
+                    s.anchor = int(anchors[i])
+                    s.cond = None if hidden is None or not cfg.use_cond else hidden[i]
+                    if not cfg.ignore_eos and s.anchor in cfg.eos:
+                        s.generated = [s.anchor]
+                        self._finish(s, outputs)
+                    else:
+                        ready.append(s)
+                self.recover(ready)
+                running.extend(ready)
+            if not running:
+                continue
+            batch_sizes.append(len(running))
+            # truncate blocks at the output budget (``eval_async_packed.py:1022-1030``)
+            blocks = []
+            for s in running:
+                room = cfg.max_new_tokens - len(s.generated)
+                blocks.append(s.current[:max(1, min(k, room))])
+            width = min(b.shape[0] for b in blocks)
+            block_t = torch.stack([b[:width] for b in blocks])
+            qq = None
+            if not is_greedy(cfg.temperature):
+                qq = (torch.stack([s.q_ids[1:width] for s in running]),
+                      torch.stack([s.q_probs[1:width] for s in running]))
+            self.t.submit_verify(running, block_t, qq)
+            predictions = self.predict(running) if width == k else {}
+            res = self.t.receive()
+            steps += 1
+            verify_tokens += width * len(running)
+            remaining, recover = [], []
+            for i, s in enumerate(running):
+                n = int(res.commit[i])
+                corr = int(res.correction[i])
+                emitted = block_t[i, :n].tolist()
+                room = cfg.max_new_tokens - len(s.generated)
+                emitted = emitted[:room]
+                stop = False
+                if not cfg.ignore_eos:
+                    for j, tok in enumerate(emitted):
+                        if tok in cfg.eos:
+                            emitted = emitted[:j + 1]
+                            stop = True
+                            break
+                s.generated.extend(emitted)
+                s.accepts.append(n)
+                s.sources.append(s.source)
+                s.prefix += n
+                s.anchor = corr
+                if res.hidden is not None and cfg.use_cond:
+                    s.cond = res.hidden[i]
+                if stop or len(s.generated) >= cfg.max_new_tokens:
+                    self._finish(s, outputs)
+                    continue
+                if not cfg.ignore_eos and corr in cfg.eos:
+                    s.generated.append(corr)
+                    self._finish(s, outputs)
+                    continue
+                key = (n, None if (n == k or cfg.anchor_num == 0) else corr)
+                sel = predictions.get(s.index, {}).get(key)
+                self.d.trim(s, s.prefix)
+                if sel is None:
+                    recover.append(s)
+                else:
+                    blk, top, q2 = sel
+                    blk = blk.clone()
+                    blk[0] = corr
+                    top = None if top is None else top.clone()
+                    self._controlled(s, blk, top, s.prefix)
+                    s.current, s.top = blk, top
+                    if q2 is not None:
+                        s.q_ids, s.q_probs = q2
+                    s.hits += 1
+                    s.source = "packed_full" if n == k else f"packed_outcome_{n}"
+                remaining.append(s)
+            running = remaining
+            miss_rounds += bool(recover)
+            self.recover(recover)
+            if on_step is not None:
+                on_step(steps)
+        elapsed = time.perf_counter() - started
+        outputs.sort(key=lambda o: o.index)
+        total = sum(len(o.tokens) for o in outputs)
+        accepts = [a for o in outputs for a in o.accepts]
+        return dict(outputs=outputs, elapsed_s=elapsed, output_tokens=total,
+                    tps=total / elapsed if elapsed > 0 else 0.0, steps=steps,
+                    verify_tokens=verify_tokens, miss_rounds=miss_rounds,
+                    mean_accept_length=(sum(accepts) / len(accepts)) if accepts else 0.0,
+                    decode_batch_sizes=batch_sizes)
+
+    def _finish(self, s: SeqState, outputs: List[RequestOutput]) -> None:
+        outputs.append(RequestOutput(s.index, list(s.generated), list(s.accepts),
+                                     list(s.sources), s.hits, s.recoveries,
+                                     time.perf_counter() - s.born))
+        self.t.release(s)
+        self.d.release(s)
+
+
+def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new_tokens: int,
+                eos: Tuple[int, ...] = EOS_DEFAULT, ignore_eos: bool = False,
+                concurrency: int = 1) -> dict:
+    """Target-only autoregressive decoding through the same verify path
+    (``single/eval_async_packed.py:1489-1535``; ``serving/baseline_ar.py``)."""
+    outs: List[List[int]] = []
+    started = time.perf_counter()
+    pending = list(enumerate(prompts))
+    results: Dict[int, List[int]] = {}
+    while pending:
+        group = pending[:concurrency]
+        pending = pending[concurrency:]
+        seqs = [SeqState(index=i, prompt=[int(t) for t in p], prefix=len(p)) for i, p in group]
+        anchors, _ = target.prefill(seqs)
+        live = []
+        for s, a in zip(seqs, anchors.tolist()):
+            s.anchor = int(a)
+            s.generated = [s.anchor]
+            if (not ignore_eos and s.anchor in eos) or max_new_tokens <= 1:
+                results[s.index] = s.generated[:max_new_tokens]
+                target.release(s)
+            else:
+                live.append(s)
+        while live:
+            blocks = torch.tensor([[s.anchor] for s in live], dtype=torch.long)
+            res = target.verify(live, blocks)
+            nxt = []
+            for i, s in enumerate(live):
+                s.prefix += 1
+                s.anchor = int(res.correction[i])
+                s.generated.append(s.anchor)
+                if (not ignore_eos and s.anchor in eos) or len(s.generated) >= max_new_tokens:
+                    results[s.index] = s.generated
+                    target.release(s)
+                else:
+                    nxt.append(s)
+            live = nxt
+    elapsed = time.perf_counter() - started
+    outs = [results[i] for i in range(len(prompts))]
+    total = sum(len(o) for o in outs)
+    return dict(outputs=outs, elapsed_s=elapsed, output_tokens=total,
+                tps=total / elapsed if elapsed > 0 else 0.0)
