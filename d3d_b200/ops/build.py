@@ -1,0 +1,77 @@
+"""Build and load the in-tree sm_100a extension ``d3d_b200_C``.
+
+The shared object is built into ``d3d_b200/ops/_build/`` (in the source tree,
+so it travels with the repository snapshot to the GPU machine) with
+``-gencode arch=compute_100a,code=sm_100a``.  :func:`load` imports the built
+``.so`` directly and only invokes the compiler when it is missing, or when
+``D3D_REBUILD=1``.
+"""
+from __future__ import annotations
+
+import importlib.machinery
+import importlib.util
+import os
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / "csrc"
+BUILD_DIR = HERE / "_build"
+NAME = "d3d_b200_C"
+
+SOURCES = ["bindings.cpp", "gemm_tcgen05.cu", "fused.cu", "attention.cu", "handoff.cu",
+           "train_kernels.cu"]
+
+CUDA_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo", "-O3", "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xptxas", "-v",
+]
+
+_mod = None
+
+
+def so_path() -> Path:
+    return BUILD_DIR / f"{NAME}.so"
+
+
+def build(verbose: bool = False):
+    """Compile the extension for sm_100a (works without a GPU)."""
+    import torch  # noqa: F401  (needed before cpp_extension)
+    from torch.utils import cpp_extension
+
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    srcs = [str(CSRC / s) for s in SOURCES if (CSRC / s).exists()]
+    mod = cpp_extension.load(
+        name=NAME,
+        sources=srcs,
+        extra_cflags=["-O3", "-std=c++17"],
+        extra_cuda_cflags=CUDA_FLAGS,
+        extra_include_paths=[str(CSRC)],
+        build_directory=str(BUILD_DIR),
+        verbose=verbose,
+        with_cuda=True,
+    )
+    return mod
+
+
+def load():
+    """Import the built extension (building it first if absent)."""
+    global _mod
+    if _mod is not None:
+        return _mod
+    import torch  # noqa: F401
+
+    path = so_path()
+    if os.environ.get("D3D_REBUILD") == "1" or not path.exists():
+        _mod = build()
+        return _mod
+    loader = importlib.machinery.ExtensionFileLoader(NAME, str(path))
+    spec = importlib.util.spec_from_file_location(NAME, str(path), loader=loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    sys.modules[NAME] = mod
+    _mod = mod
+    return mod

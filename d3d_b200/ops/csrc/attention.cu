@@ -1,0 +1,349 @@
+// Paged-KV attention with structured masks (sm_100a).
+//
+// One kernel serves every attention of the framework: target prefill and
+// verify (causal over the block), drafter prefill (causal / block-causal),
+// recovery drafting, and the packed all-outcome forward.  Each query row
+// carries three int32 numbers (lim, lo, hi): it sees key slots
+// ``k < lim  or  lo <= k < hi``.  Key tiles that no row of a CTA can see are
+// skipped without being loaded, which is what makes the packed forward (one
+// pending block + up to 46 branch segments) cheap: a branch row reads the
+// prefix, the accepted pending tokens and its own 16-token segment only.
+//
+// Layout: a CTA owns 64 "packed rows" of one (sequence, kv head): row r is
+// token r / g and query head h*g + r % g (g = GQA group), so K/V tiles are
+// loaded once for the whole group.  Four warps each run 16 rows through
+// mma.sync m16n8k16 (bf16 -> fp32) for S = QK^T and O += PV with an online
+// exp2 softmax.  Keys are split into chunks of ``chunk`` slots at fixed
+// absolute boundaries (grid z); a combine kernel merges the chunks in index
+// order.  Because chunk boundaries, the tile order inside a chunk and the
+// per-row arithmetic do not depend on how many queries share a launch, a
+// row's output is bit-identical whether it is verified in a block of 16 or
+// decoded alone — required for greedy token identity with AR decoding.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace d3d {
+
+constexpr int AT_ROWS = 64;
+constexpr int AT_KEYS = 64;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ bool visible(int k, int lim, int lo, int hi) { return k < lim || (k >= lo && k < hi); }
+
+template <int D>
+__global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+  constexpr int LD = D + 8;  // padded smem row (bank-conflict-free ldmatrix)
+  extern __shared__ __align__(16) uint8_t smem[];
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem);
+  __nv_bfloat16* Ks = Qs + AT_ROWS * LD;
+  __nv_bfloat16* Vs = Ks + AT_KEYS * LD;
+  __shared__ int s_rows[AT_ROWS][3];
+  __shared__ int s_range[3];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = a.Hq / a.Hkv;
+  const int b = blockIdx.y / a.Hkv, h = blockIdx.y % a.Hkv;
+  const int chunk_id = blockIdx.z;
+  const int R0 = blockIdx.x * AT_ROWS;
+  const int T = a.B * a.q_len;
+  const int kv_end = a.kv_end[b];
+
+  // ---- rows: descriptors, key range of this CTA
+  if (tid < AT_ROWS) {
+    const int R = R0 + tid;
+    const int t = R / g;
+    int lim = 0, lo = 0, hi = 0;
+    if (t < a.q_len) {
+      const int* rr = a.rows + static_cast<size_t>(b * a.q_len + t) * 3;
+      lim = min(rr[0], kv_end);
+      lo = rr[1];
+      hi = min(rr[2], kv_end);
+      if (hi <= lo) lo = hi = 0;
+    }
+    s_rows[tid][0] = lim;
+    s_rows[tid][1] = lo;
+    s_rows[tid][2] = hi;
+  }
+  if (tid == 0) {
+    s_range[0] = 0;
+    s_range[1] = 0x7fffffff;
+    s_range[2] = 0;
+  }
+  __syncthreads();
+  if (tid < AT_ROWS) {
+    atomicMax(&s_range[0], s_rows[tid][0]);
+    if (s_rows[tid][2] > s_rows[tid][1]) {
+      atomicMin(&s_range[1], s_rows[tid][1]);
+      atomicMax(&s_range[2], s_rows[tid][2]);
+    }
+  }
+  // ---- Q tile
+  for (int c = tid; c < AT_ROWS * (D / 8); c += 128) {
+    const int r = c / (D / 8), dc = (c % (D / 8)) * 8;
+    const int R = R0 + r;
+    const int t = R / g;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < a.q_len) {
+      const int qh = h * g + R % g;
+      v = *reinterpret_cast<const uint4*>(a.q + (static_cast<size_t>(b * a.q_len + t) * a.Hq + qh) * D + dc);
+    }
+    *reinterpret_cast<uint4*>(Qs + r * LD + dc) = v;
+  }
+  __syncthreads();
+  const int max_lim = s_range[0], min_lo = s_range[1], max_hi = s_range[2];
+
+  // per-thread rows of the mma fragments
+  const int ra = warp * 16 + (lane >> 2), rb = ra + 8;
+  const int limA = s_rows[ra][0], loA = s_rows[ra][1], hiA = s_rows[ra][2];
+  const int limB = s_rows[rb][0], loB = s_rows[rb][1], hiB = s_rows[rb][2];
+
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int row = warp * 16 + (lane & 15);
+    const int col = kk * 16 + (lane >> 4) * 8;
+    ldsm_x4(smem_u32(Qs + row * LD + col), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  const float sl2 = a.scale * 1.4426950408889634f;  // scale * log2(e)
+
+  const int kbeg = chunk_id * a.chunk;
+  const int kend = min(kbeg + a.chunk, kv_end);
+  const int* bt = a.block_table + static_cast<size_t>(b) * a.bt_stride;
+
+  for (int k0 = kbeg; k0 < kend; k0 += AT_KEYS) {
+    const bool need = k0 < max_lim || (k0 + AT_KEYS > min_lo && k0 < max_hi);
+    if (!need) continue;  // uniform across the CTA
+    // ---- load K/V tile (zeros beyond kv_end)
+    for (int c = tid; c < AT_KEYS * (D / 8); c += 128) {
+      const int kr = c / (D / 8), dc = (c % (D / 8)) * 8;
+      const int s = k0 + kr;
+      const uint32_t dk = smem_u32(Ks + kr * LD + dc), dv = smem_u32(Vs + kr * LD + dc);
+      if (s < kv_end) {
+        const long long page = bt[s / a.page_size];
+        const size_t off = ((page * a.page_size + s % a.page_size) * a.Hkv + h) * static_cast<size_t>(D) + dc;
+        cp_async16(dk, a.k_cache + off);
+        cp_async16(dv, a.v_cache + off);
+      } else {
+        *reinterpret_cast<uint4*>(Ks + kr * LD + dc) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(Vs + kr * LD + dc) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+
+    // ---- S = Q K^T (16 rows x 64 keys per warp)
+    float s[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int nb = 0; nb < 8; nb += 2) {
+        const int key = nb * 8 + (lane & 7) + (lane >> 4) * 8;
+        const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(Ks + key * LD + col), b0, b1, b2, b3);
+        mma16816(s[nb], qf[kk], b0, b1);
+        mma16816(s[nb + 1], qf[kk], b2, b3);
+      }
+    }
+    // ---- mask + online softmax
+    float tmA = -INFINITY, tmB = -INFINITY;
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = k0 + nb * 8 + (lane & 3) * 2 + e;
+        const bool inb = key < kend;
+        s[nb][e] = (inb && visible(key, limA, loA, hiA)) ? s[nb][e] * sl2 : -INFINITY;
+        s[nb][2 + e] = (inb && visible(key, limB, loB, hiB)) ? s[nb][2 + e] * sl2 : -INFINITY;
+        tmA = fmaxf(tmA, s[nb][e]);
+        tmB = fmaxf(tmB, s[nb][2 + e]);
+      }
+    }
+    tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 1));
+    tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 2));
+    tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 1));
+    tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 2));
+    const float nmA = fmaxf(mA, tmA), nmB = fmaxf(mB, tmB);
+    const float alA = (nmA == -INFINITY) ? 1.f : exp2f(mA - nmA);
+    const float alB = (nmB == -INFINITY) ? 1.f : exp2f(mB - nmB);
+    float sumA = 0.f, sumB = 0.f;
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float pa = s[nb][e] == -INFINITY ? 0.f : exp2f(s[nb][e] - nmA);
+        const float pb = s[nb][2 + e] == -INFINITY ? 0.f : exp2f(s[nb][2 + e] - nmB);
+        s[nb][e] = pa;
+        s[nb][2 + e] = pb;
+        sumA += pa;
+        sumB += pb;
+      }
+    }
+    sumA += __shfl_xor_sync(0xffffffffu, sumA, 1);
+    sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
+    sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
+    sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
+    lA = lA * alA + sumA;
+    lB = lB * alB + sumB;
+    mA = nmA;
+    mB = nmB;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= alA;
+      o[i][1] *= alA;
+      o[i][2] *= alB;
+      o[i][3] *= alB;
+    }
+    // ---- O += P V
+#pragma unroll
+    for (int kb = 0; kb < 4; ++kb) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(s[2 * kb][0], s[2 * kb][1]);
+      pa[1] = pack_bf16(s[2 * kb][2], s[2 * kb][3]);
+      pa[2] = pack_bf16(s[2 * kb + 1][0], s[2 * kb + 1][1]);
+      pa[3] = pack_bf16(s[2 * kb + 1][2], s[2 * kb + 1][3]);
+#pragma unroll
+      for (int nd = 0; nd < D / 8; nd += 2) {
+        const int key = kb * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int col = nd * 8 + (lane >> 4) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(Vs + key * LD + col), b0, b1, b2, b3);
+        mma16816(o[nd], pa, b0, b1);
+        mma16816(o[nd + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- write partial (or final) results
+  const int RA = R0 + ra, RB = R0 + rb;
+  const int tA = RA / g, tB = RB / g;
+  const int qhA = h * g + RA % g, qhB = h * g + RB % g;
+  const bool vA = tA < a.q_len, vB = tB < a.q_len;
+  const size_t tokA = static_cast<size_t>(b * a.q_len + tA), tokB = static_cast<size_t>(b * a.q_len + tB);
+  if (a.n_chunks == 1) {
+    const float iA = lA > 0.f ? 1.f / lA : 0.f, iB = lB > 0.f ? 1.f / lB : 0.f;
+#pragma unroll
+    for (int nd = 0; nd < D / 8; ++nd) {
+      const int d = nd * 8 + (lane & 3) * 2;
+      if (vA)
+        *reinterpret_cast<__nv_bfloat162*>(a.out + (tokA * a.Hq + qhA) * D + d) =
+            __floats2bfloat162_rn(o[nd][0] * iA, o[nd][1] * iA);
+      if (vB)
+        *reinterpret_cast<__nv_bfloat162*>(a.out + (tokB * a.Hq + qhB) * D + d) =
+            __floats2bfloat162_rn(o[nd][2] * iB, o[nd][3] * iB);
+    }
+  } else {
+    const size_t cbase = static_cast<size_t>(chunk_id) * T * a.Hq;
+#pragma unroll
+    for (int nd = 0; nd < D / 8; ++nd) {
+      const int d = nd * 8 + (lane & 3) * 2;
+      if (vA)
+        *reinterpret_cast<float2*>(a.part_o + (cbase + tokA * a.Hq + qhA) * D + d) = make_float2(o[nd][0], o[nd][1]);
+      if (vB)
+        *reinterpret_cast<float2*>(a.part_o + (cbase + tokB * a.Hq + qhB) * D + d) = make_float2(o[nd][2], o[nd][3]);
+    }
+    if ((lane & 3) == 0) {
+      if (vA) *reinterpret_cast<float2*>(a.part_ml + (cbase + tokA * a.Hq + qhA) * 2) = make_float2(mA, lA);
+      if (vB) *reinterpret_cast<float2*>(a.part_ml + (cbase + tokB * a.Hq + qhB) * 2) = make_float2(mB, lB);
+    }
+  }
+}
+
+// Merge key chunks in index order: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
+template <int D>
+__global__ void attn_combine_kernel(const AttnArgs a) {
+  const int T = a.B * a.q_len;
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= T * a.Hq) return;
+  const int tok = w / a.Hq, qh = w % a.Hq;
+  const int b = tok / a.q_len;
+  const int nc = min(a.n_chunks, (a.kv_end[b] + a.chunk - 1) / a.chunk);
+  float M = -INFINITY;
+  for (int c = 0; c < nc; ++c) M = fmaxf(M, a.part_ml[((static_cast<size_t>(c) * T + tok) * a.Hq + qh) * 2]);
+  constexpr int E = D / 32;
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  float L = 0.f;
+  if (M != -INFINITY) {
+    for (int c = 0; c < nc; ++c) {
+      const size_t idx = (static_cast<size_t>(c) * T + tok) * a.Hq + qh;
+      const float mc = a.part_ml[idx * 2];
+      if (mc == -INFINITY) continue;
+      const float f = exp2f(mc - M);
+      L += a.part_ml[idx * 2 + 1] * f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc[e] += a.part_o[idx * D + lane * E + e] * f;
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int e = 0; e < E; ++e)
+    a.out[(static_cast<size_t>(tok) * a.Hq + qh) * D + lane * E + e] = __float2bfloat16(acc[e] * inv);
+}
+
+template <int D>
+static void launch_attn(const AttnArgs& a, cudaStream_t st) {
+  constexpr int LD = D + 8;
+  const size_t smem = static_cast<size_t>(AT_ROWS + 2 * AT_KEYS) * LD * 2;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    attr = true;
+  }
+  const int g = a.Hq / a.Hkv;
+  dim3 grid((a.q_len * g + AT_ROWS - 1) / AT_ROWS, a.B * a.Hkv, a.n_chunks);
+  attn_kernel<D><<<grid, 128, smem, st>>>(a);
+  if (a.n_chunks > 1) {
+    const int warps = a.B * a.q_len * a.Hq;
+    attn_combine_kernel<D><<<(warps * 32 + 255) / 256, 256, 0, st>>>(a);
+  }
+}
+
+void attention(const AttnArgs& a, cudaStream_t st) {
+  if (a.B == 0 || a.q_len == 0) return;
+  switch (a.head_dim) {
+    case 32: launch_attn<32>(a, st); break;
+    case 64: launch_attn<64>(a, st); break;
+    case 128: launch_attn<128>(a, st); break;
+    default: break;
+  }
+}
+
+}  // namespace d3d

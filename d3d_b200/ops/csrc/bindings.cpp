@@ -1,0 +1,231 @@
+// PyTorch bindings of the d3d_b200 sm_100a kernels.  Every op runs on the
+// current CUDA stream and checks shapes/dtypes/alignment before launching.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "gemm.h"
+#include "kernels.h"
+
+using torch::Tensor;
+
+namespace {
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+#define CHECK_DT(t, dt) TORCH_CHECK((t).scalar_type() == (dt), #t " has wrong dtype")
+
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+inline __nv_bfloat16* bf(Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+inline const __nv_bfloat16* cbf(const Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
+inline int* status_ptr(const c10::optional<Tensor>& s) { return s ? s->data_ptr<int>() : nullptr; }
+
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s bound on every in-kernel wait
+
+d3d::GemmArgs base_args(const Tensor& x, const Tensor& w, int bt, const c10::optional<Tensor>& status) {
+  CHECK_CUDA(x);
+  CHECK_CUDA(w);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(w, torch::kBFloat16);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "gemm: x [M,K], w [N,K]");
+  TORCH_CHECK(x.size(1) == w.size(1), "gemm: K mismatch");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "gemm: inner dim must be contiguous");
+  d3d::GemmArgs a{};
+  a.x = cbf(x);
+  a.w = cbf(w);
+  a.M = static_cast<int>(x.size(0));
+  a.N = static_cast<int>(w.size(0));
+  a.K = static_cast<int>(x.size(1));
+  a.ldx = static_cast<int>(x.stride(0));
+  a.ldw = static_cast<int>(w.stride(0));
+  a.bt = bt;
+  a.splits = 1;
+  a.topk = 1;
+  a.status = status_ptr(status);
+  a.timeout_ns = kTimeoutNs;
+  return a;
+}
+
+void gemm_partial(Tensor x, Tensor w, Tensor out, int64_t splits, int64_t bt, c10::optional<Tensor> status) {
+  const c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, static_cast<int>(bt), status);
+  CHECK_DT(out, torch::kFloat32);
+  CHECK_CONTIG(out);
+  TORCH_CHECK(out.numel() >= splits * a.M * a.N, "gemm_partial: out too small");
+  a.mode = 0;
+  a.splits = static_cast<int>(splits);
+  a.out_f32 = out.data_ptr<float>();
+  if (a.M == 0) return;
+  d3d::gemm_launch(a, cur_stream());
+}
+
+void gemm_bf16(Tensor x, Tensor w, Tensor out, c10::optional<Tensor> residual, int64_t bt,
+               c10::optional<Tensor> status) {
+  const c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, static_cast<int>(bt), status);
+  CHECK_DT(out, torch::kBFloat16);
+  TORCH_CHECK(out.size(0) == a.M && out.size(1) == a.N && out.stride(1) == 1, "gemm_bf16: out shape");
+  a.mode = 1;
+  a.out_bf16 = bf(out);
+  a.ldc = static_cast<int>(out.stride(0));
+  if (residual) {
+    CHECK_DT(*residual, torch::kBFloat16);
+    TORCH_CHECK(residual->stride(1) == 1, "residual inner dim must be contiguous");
+    a.residual = cbf(*residual);
+    a.ldr = static_cast<int>(residual->stride(0));
+  }
+  if (a.M == 0) return;
+  d3d::gemm_launch(a, cur_stream());
+}
+
+void gemm_topk(Tensor x, Tensor w, Tensor topv, Tensor topi, int64_t k, int64_t bt, c10::optional<Tensor> status) {
+  const c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, static_cast<int>(bt), status);
+  const int kt = k <= 1 ? 1 : (k <= 2 ? 2 : 4);
+  const int ntiles = (a.N + 127) / 128;
+  CHECK_DT(topv, torch::kFloat32);
+  CHECK_DT(topi, torch::kInt32);
+  TORCH_CHECK(topv.numel() >= static_cast<int64_t>(a.M) * ntiles * kt && topi.numel() >= topv.numel(),
+              "gemm_topk: partial buffers too small");
+  a.mode = 2;
+  a.topk = kt;
+  a.topv = topv.data_ptr<float>();
+  a.topi = topi.data_ptr<int>();
+  if (a.M == 0) return;
+  d3d::gemm_launch(a, cur_stream());
+}
+
+void add_rmsnorm(c10::optional<Tensor> part, int64_t nsplit, Tensor residual, Tensor w, Tensor out, double eps) {
+  const c10::cuda::CUDAGuard g(residual.device());
+  CHECK_DT(residual, torch::kBFloat16);
+  CHECK_CONTIG(residual);
+  CHECK_CONTIG(out);
+  const int M = static_cast<int>(residual.size(0)), N = static_cast<int>(residual.size(1));
+  d3d::add_rmsnorm(part ? part->data_ptr<float>() : nullptr, static_cast<int>(nsplit), bf(residual), cbf(w), bf(out),
+                   M, N, static_cast<float>(eps), cur_stream());
+}
+
+void swiglu(Tensor part, int64_t nsplit, Tensor h) {
+  const c10::cuda::CUDAGuard g(h.device());
+  CHECK_CONTIG(h);
+  CHECK_DT(part, torch::kFloat32);
+  d3d::swiglu(part.data_ptr<float>(), static_cast<int>(nsplit), bf(h), static_cast<int>(h.size(0)),
+              static_cast<int>(h.size(1)), cur_stream());
+}
+
+void qkv_rope_kv(c10::optional<Tensor> part, c10::optional<Tensor> y, int64_t nsplit, Tensor q_norm, Tensor k_norm,
+                 Tensor inv_freq, Tensor positions, Tensor slots, Tensor q_out, Tensor k_cache, Tensor v_cache,
+                 int64_t Hq, int64_t Hkv, int64_t D, double eps) {
+  const c10::cuda::CUDAGuard g(q_out.device());
+  CHECK_DT(positions, torch::kInt64);
+  CHECK_DT(slots, torch::kInt64);
+  CHECK_CONTIG(q_out);
+  TORCH_CHECK(D == 32 || D == 64 || D == 128, "head_dim must be 32, 64 or 128");
+  d3d::QkvRopeArgs a{};
+  a.part = part ? part->data_ptr<float>() : nullptr;
+  a.y = y ? cbf(*y) : nullptr;
+  TORCH_CHECK(a.part || a.y, "qkv_rope_kv needs partials or bf16 input");
+  a.nsplit = static_cast<int>(nsplit);
+  a.M = static_cast<int>(positions.numel());
+  a.Hq = static_cast<int>(Hq);
+  a.Hkv = static_cast<int>(Hkv);
+  a.head_dim = static_cast<int>(D);
+  a.q_norm = cbf(q_norm);
+  a.k_norm = cbf(k_norm);
+  a.inv_freq = inv_freq.data_ptr<float>();
+  a.positions = positions.data_ptr<int64_t>();
+  a.slots = slots.data_ptr<int64_t>();
+  a.q_out = bf(q_out);
+  a.k_cache = bf(k_cache);
+  a.v_cache = bf(v_cache);
+  a.eps = static_cast<float>(eps);
+  d3d::qkv_rope_kv(a, cur_stream());
+}
+
+void embed(Tensor ids, Tensor table, c10::optional<Tensor> cond, c10::optional<Tensor> cond_rows, int64_t q_len,
+           Tensor out) {
+  const c10::cuda::CUDAGuard g(out.device());
+  CHECK_DT(ids, torch::kInt64);
+  CHECK_CONTIG(table);
+  CHECK_CONTIG(out);
+  TORCH_CHECK(table.size(1) % 8 == 0, "hidden size must be a multiple of 8");
+  d3d::embed(ids.data_ptr<int64_t>(), cbf(table), cond ? cbf(*cond) : nullptr,
+             cond_rows ? cond_rows->data_ptr<uint8_t>() : nullptr, static_cast<int>(q_len), bf(out),
+             static_cast<int>(ids.numel()), static_cast<int>(table.size(1)), cur_stream());
+}
+
+void topk_merge(Tensor tv, Tensor ti, int64_t M, int64_t ntiles, int64_t kt, int64_t k, c10::optional<Tensor> ov,
+                Tensor oi) {
+  const c10::cuda::CUDAGuard g(oi.device());
+  CHECK_DT(oi, torch::kInt64);
+  d3d::topk_merge(tv.data_ptr<float>(), ti.data_ptr<int>(), static_cast<int>(ntiles), static_cast<int>(kt),
+                  static_cast<int>(k), ov ? ov->data_ptr<float>() : nullptr, oi.data_ptr<int64_t>(),
+                  static_cast<int>(M), cur_stream());
+}
+
+void greedy_accept(Tensor blocks, Tensor post, Tensor commit, Tensor corr, c10::optional<Tensor> hidden,
+                   c10::optional<Tensor> hid_out) {
+  const c10::cuda::CUDAGuard g(blocks.device());
+  CHECK_DT(blocks, torch::kInt64);
+  CHECK_DT(post, torch::kInt64);
+  CHECK_CONTIG(blocks);
+  CHECK_CONTIG(post);
+  const int B = static_cast<int>(blocks.size(0)), K = static_cast<int>(blocks.size(1));
+  int H = 0;
+  if (hidden) H = static_cast<int>(hidden->size(-1));
+  d3d::greedy_accept(blocks.data_ptr<int64_t>(), post.data_ptr<int64_t>(), B, K, commit.data_ptr<int64_t>(),
+                     corr.data_ptr<int64_t>(), hidden ? cbf(*hidden) : nullptr,
+                     hid_out ? bf(*hid_out) : nullptr, H, cur_stream());
+}
+
+void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor rows, Tensor kv_end,
+               int64_t B, int64_t q_len, int64_t Hq, int64_t Hkv, int64_t page_size, double scale, int64_t chunk,
+               int64_t n_chunks, c10::optional<Tensor> part_o, c10::optional<Tensor> part_ml, Tensor out) {
+  const c10::cuda::CUDAGuard g(q.device());
+  CHECK_CONTIG(q);
+  CHECK_CONTIG(out);
+  CHECK_DT(block_table, torch::kInt32);
+  CHECK_DT(rows, torch::kInt32);
+  CHECK_DT(kv_end, torch::kInt32);
+  TORCH_CHECK(chunk % 64 == 0, "attention chunk must be a multiple of 64");
+  TORCH_CHECK(n_chunks == 1 || (part_o && part_ml), "split attention needs partial buffers");
+  d3d::AttnArgs a{};
+  a.q = cbf(q);
+  a.k_cache = cbf(k_cache);
+  a.v_cache = cbf(v_cache);
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_stride = static_cast<int>(block_table.stride(0));
+  a.rows = rows.data_ptr<int>();
+  a.kv_end = kv_end.data_ptr<int>();
+  a.B = static_cast<int>(B);
+  a.q_len = static_cast<int>(q_len);
+  a.Hq = static_cast<int>(Hq);
+  a.Hkv = static_cast<int>(Hkv);
+  a.head_dim = static_cast<int>(q.size(-1));
+  a.page_size = static_cast<int>(page_size);
+  a.scale = static_cast<float>(scale);
+  a.chunk = static_cast<int>(chunk);
+  a.n_chunks = static_cast<int>(n_chunks);
+  a.part_o = part_o ? part_o->data_ptr<float>() : nullptr;
+  a.part_ml = part_ml ? part_ml->data_ptr<float>() : nullptr;
+  a.out = bf(out);
+  d3d::attention(a, cur_stream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "d3d_b200 sm_100a kernels";
+  m.def("gemm_partial", &gemm_partial);
+  m.def("gemm_bf16", &gemm_bf16);
+  m.def("gemm_topk", &gemm_topk);
+  m.def("add_rmsnorm", &add_rmsnorm);
+  m.def("swiglu", &swiglu);
+  m.def("qkv_rope_kv", &qkv_rope_kv);
+  m.def("embed", &embed);
+  m.def("topk_merge", &topk_merge);
+  m.def("greedy_accept", &greedy_accept);
+  m.def("attention", &attention);
+  m.def("gemm_stages", &d3d::gemm_stages);
+}

@@ -1,0 +1,52 @@
+// Host-side interface of the tcgen05 GEMM (raw pointers; no torch headers so
+// the .cu files compile quickly and can be linked into any host program).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace d3d {
+
+struct GemmParams {
+  int M, N, K;
+  float* out_f32;
+  __nv_bfloat16* out_bf16;
+  int ldc;
+  const __nv_bfloat16* residual;
+  int ldr;
+  float* topv;
+  int* topi;
+  int ntiles;
+  int bt;
+  int stages;
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+struct GemmArgs {
+  const __nv_bfloat16* x;  // [M, K] activations (row stride ldx elements)
+  const __nv_bfloat16* w;  // [N, K] weights (row stride ldw elements)
+  int M, N, K, ldx, ldw;
+  int mode;      // 0 fp32 split-K partials, 1 bf16 (+residual), 2 fused top-k
+  int splits;    // split-K factor (mode 0 only)
+  int bt;        // token tile (MMA N), multiple of 16 in [16, 256]
+  int topk;      // mode 2: k <= 4
+  float* out_f32;              // mode 0: [splits, M, N]
+  __nv_bfloat16* out_bf16;     // mode 1: [M, ldc]
+  int ldc;
+  const __nv_bfloat16* residual;  // mode 1 optional [M, ldr]
+  int ldr;
+  float* topv;                 // mode 2: [M, ceil(N/128), kt]
+  int* topi;
+  int* status;                 // device error word (may be null)
+  unsigned long long timeout_ns;
+};
+
+void gemm_launch(const GemmArgs& a, cudaStream_t stream);
+int gemm_stages(int bt);
+size_t gemm_smem_bytes(int bt, int stages);
+void make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
+                       uint32_t box_inner, uint32_t box_outer);
+
+}  // namespace d3d

@@ -1,0 +1,57 @@
+// Host-side prototypes of the non-GEMM kernels (raw pointers, no torch).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace d3d {
+
+void add_rmsnorm(const float* part, int nsplit, __nv_bfloat16* residual, const __nv_bfloat16* w, __nv_bfloat16* out,
+                 int M, int N, float eps, cudaStream_t st);
+
+void swiglu(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, cudaStream_t st);
+
+struct QkvRopeArgs {
+  const float* part;        // [nsplit][M][(Hq+2Hkv)*D] fp32 partials, or null
+  const __nv_bfloat16* y;   // bf16 qkv when part is null
+  int nsplit, M, Hq, Hkv, head_dim;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* inv_freq;    // [D/2]
+  const int64_t* positions;  // [M]
+  const int64_t* slots;      // [M] physical KV slot (page * page_size + offset)
+  __nv_bfloat16* q_out;     // [M][Hq][D]
+  __nv_bfloat16* k_cache;   // [slots][Hkv][D]
+  __nv_bfloat16* v_cache;
+  float eps;
+};
+void qkv_rope_kv(const QkvRopeArgs& a, cudaStream_t st);
+
+void embed(const int64_t* ids, const __nv_bfloat16* table, const __nv_bfloat16* cond, const unsigned char* cond_rows,
+           int q_len, __nv_bfloat16* out, int M, int H, cudaStream_t st);
+
+void topk_merge(const float* tv, const int* ti, int ntiles, int kt, int k, float* ov, int64_t* oi, int M,
+                cudaStream_t st);
+
+void greedy_accept(const int64_t* blocks, const int64_t* post, int B, int K, int64_t* commit, int64_t* corr,
+                   const __nv_bfloat16* hidden, __nv_bfloat16* hid_out, int H, cudaStream_t st);
+
+struct AttnArgs {
+  const __nv_bfloat16* q;   // [T][Hq][D]
+  const __nv_bfloat16* k_cache;  // [slots][Hkv][D]
+  const __nv_bfloat16* v_cache;
+  const int* block_table;   // [B][bt_stride] page ids
+  int bt_stride;
+  const int* rows;          // [T][3] (lim, lo, hi) absolute slots
+  const int* kv_end;        // [B] keys beyond are never read
+  int B, q_len, Hq, Hkv, head_dim, page_size;
+  float scale;
+  int chunk;                // keys per split (multiple of 64); one split when >= max kv
+  int n_chunks;
+  float* part_o;            // [n_chunks][T][Hq][D]
+  float* part_ml;           // [n_chunks][T][Hq][2]
+  __nv_bfloat16* out;       // [T][Hq][D]
+};
+void attention(const AttnArgs& a, cudaStream_t st);
+
+}  // namespace d3d
