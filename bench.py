@@ -1,0 +1,338 @@
+#!/usr/bin/env python3
+"""Headline benchmark: decode tokens/s (and speedup vs AR) of asynchronous
+speculative decoding, Qwen3-8B target + 1.7B-layout D3D drafter, bf16,
+random-init weights, synthetic seeded prompts, acceptance-controlled drafts.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One *step* is one request decoded end to end at concurrency 1 (prompt of
+128-512 random non-special tokens -> 512 new tokens, greedy): prefill, the
+async draft/verify loop, output read back.  W requests are decoded untimed
+(CUDA-graph capture, allocator warm-up), then exactly K requests are timed
+with CUDA events between two barrier+synchronize points; the device time is
+the max over ranks and ``value`` is the whole-job token rate (every rank
+decodes its own requests: weak scaling).  The same K requests are decoded
+target-only (AR) on the same kernels for the speedup, and once more through
+the public API with wall-clock timing for the ``e2e`` figure.
+
+For N > 1 launch with ``python -m torch.distributed.run --nproc-per-node N``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BASELINE_TPS = 501.60   # BASELINE.md headline: SGLang Hybrid aggregate TPS, 2xH800
+METRIC = "decode tokens/s + speedup vs AR, Qwen3-8B target/1.7B draft, concurrency 1–8"
+EOS = (151643, 151645)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=6)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--max-new-tokens", type=int, default=512)
+    p.add_argument("--accept-mean", type=float, default=5.0)
+    p.add_argument("--block-size", type=int, default=16)
+    p.add_argument("--anchor-num", type=int, default=1)
+    p.add_argument("--concurrency", type=int, default=1)
+    p.add_argument("--prompt-min", type=int, default=128)
+    p.add_argument("--prompt-max", type=int, default=512)
+    p.add_argument("--target", default="qwen3-8b")
+    p.add_argument("--draft-layers", type=int, default=28)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--json-out", default=None)
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML every 200 ms."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self.h = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            import torch
+            props = torch.cuda.get_device_properties(device_index)
+            bus = getattr(props, "pci_bus_id", None)
+            dom = getattr(props, "pci_domain_id", 0)
+            dev = getattr(props, "pci_device_id", 0)
+            if bus is not None:
+                self.h = nv.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev:02x}.0")
+            else:
+                self.h = nv.nvmlDeviceGetHandleByIndex(device_index)
+            self.nv = nv
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+        except Exception:
+            self.h = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.2)
+
+    def __enter__(self):
+        if self.h is not None:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.h is not None:
+            self.t.join(timeout=2)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons)}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- dist utils
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def dist_max(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dist_sum(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier():
+    import torch
+    import torch.distributed as dist
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def make_prompts(n, lo, hi, seed):
+    rng = random.Random(seed)
+    return [[rng.randrange(0, 151643) for _ in range(rng.randint(lo, hi))] for _ in range(n)]
+
+
+# ------------------------------------------------------------------- ours
+def run_ours(args, rank, world, local):
+    import torch
+    from d3d_b200 import config as C
+    from d3d_b200.api import D3DEngine
+    from d3d_b200.engine.controlled import ControlledAcceptance, rate_for_mean_accept
+    from d3d_b200.engine.spec import DecodeConfig
+    from d3d_b200.models.fast import FastWeights
+    from d3d_b200.utils import launches
+
+    dev = torch.device("cuda", local)
+    tcfg = C.PRESETS[args.target]()
+    dcfg = C.d3d_1p7b(num_layers=args.draft_layers)
+    tw = FastWeights.random(tcfg, seed=args.seed, device=dev)
+    dw = FastWeights.random(dcfg, seed=args.seed, device=dev)
+    decode = DecodeConfig(block_size=args.block_size, anchor_num=args.anchor_num,
+                          attention_mask_mode="causal", max_new_tokens=args.max_new_tokens,
+                          eos=EOS)
+    max_ctx = args.prompt_max + args.max_new_tokens + 2 * args.block_size
+    eng = D3DEngine.from_weights(tw, dw, decode, max_seqs=max(4, args.concurrency),
+                                 max_context=max_ctx, device=dev)
+    n = args.warmup + args.steps
+    prompts = make_prompts(n * args.concurrency, args.prompt_min, args.prompt_max,
+                           seed=1000 + 7919 * rank + args.seed)
+    groups = [prompts[i * args.concurrency:(i + 1) * args.concurrency] for i in range(n)]
+
+    # --- AR oracle (also the AR baseline: same kernels, target only)
+    ar_out = {}
+    ar_time = 0.0
+    ar_tokens = 0
+    for gi, g in enumerate(groups):
+        if gi == args.warmup:
+            barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0.record()
+        r = eng.generate_ar(g, concurrency=args.concurrency)
+        t1.record()
+        torch.cuda.synchronize()
+        for j, o in enumerate(r["outputs"]):
+            ar_out[gi * args.concurrency + j] = o
+        if gi >= args.warmup:
+            ar_time += t0.elapsed_time(t1) / 1e3
+            ar_tokens += sum(len(o) for o in r["outputs"])
+    rate = rate_for_mean_accept(args.accept_mean, args.block_size)
+
+    def ctl_for(base):
+        def ctl(i):
+            k = base + i
+            return ControlledAcceptance(oracle=prompts[k] + ar_out[k], rate=rate,
+                                        vocab_size=tcfg.vocab_size, seed=args.seed, stream=k,
+                                        exclude=(151669,) + EOS)
+        return ctl
+
+    # --- warm-up
+    for gi in range(args.warmup):
+        eng.generate(groups[gi], concurrency=args.concurrency, controlled=ctl_for(gi * args.concurrency))
+
+    # --- timed region
+    barrier()
+    launches.reset()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    tokens = 0
+    accepts = []
+    ident = True
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record()
+        for gi in range(args.warmup, n):
+            r = eng.generate(groups[gi], concurrency=args.concurrency,
+                             controlled=ctl_for(gi * args.concurrency))
+            for j, o in enumerate(r["outputs"]):
+                tokens += len(o.tokens)
+                accepts.extend(o.accepts)
+                ident &= o.tokens == ar_out[gi * args.concurrency + j]
+        ev1.record()
+        barrier()
+    n_launch = launches.count()
+    dev_s = ev0.elapsed_time(ev1) / 1e3
+
+    # --- end-to-end pass through the public API (pinned inputs, host outputs)
+    e2e = None
+    if not args.no_e2e:
+        pinned = [[torch.tensor(p, dtype=torch.int64).pin_memory() for p in g] for g in groups]
+        bi = bo = 0
+        e2e_tokens = 0
+        barrier()
+        w0 = time.perf_counter()
+        for gi in range(args.warmup, n):
+            r = eng.generate([p.tolist() for p in pinned[gi]], concurrency=args.concurrency,
+                             controlled=ctl_for(gi * args.concurrency))
+            for o in r["outputs"]:
+                e2e_tokens += len(o.tokens)
+                bo += 8 * len(o.tokens)
+            bi += sum(8 * p.numel() for p in pinned[gi])
+        barrier()
+        w1 = time.perf_counter()
+        e2e_s = dist_max(w1 - w0)
+        e2e = {"value": dist_sum(e2e_tokens) / e2e_s, "unit": "tokens/s",
+               "h2d_bytes_per_step": bi / args.steps, "d2h_bytes_per_step": bo / args.steps,
+               "timing": "wall clock around the public D3DEngine.generate calls"}
+
+    dev_s_max = dist_max(dev_s)
+    all_tokens = dist_sum(tokens)
+    ar_s_max = dist_max(ar_time)
+    ar_all = dist_sum(ar_tokens)
+    value = all_tokens / dev_s_max
+    ar_value = ar_all / ar_s_max if ar_s_max > 0 else None
+    ident_all = dist_sum(1.0 if ident else 0.0) == world
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dev_s_max / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": round(value / BASELINE_TPS, 4), "dtype": "bf16",
+        "data": "synthetic seeded random-token prompts, random-init weights (seed 0), "
+                "acceptance-controlled drafts",
+        "config": {"model": "Qwen3-8B-layout target + D3D-1.7B-layout drafter (28 layers, block 16)",
+                   "global_batch": args.concurrency * world, "seq_len": f"prompt {args.prompt_min}-"
+                   f"{args.prompt_max} + {args.max_new_tokens} new",
+                   "parallelism": f"replica per GPU x{world} (target + drafter co-located, 2 streams)",
+                   "concurrency": args.concurrency, "anchor_num": args.anchor_num,
+                   "controlled_accept_mean": args.accept_mean,
+                   "measured_accept_mean": round(statistics.fmean(accepts), 3) if accepts else None,
+                   "l2": "inputs larger than L2: every verify streams ~16 GB of target weights",
+                   "step": "one request, prefill through last token"},
+        "ar_tokens_per_s": round(ar_value, 2) if ar_value else None,
+        "speedup_vs_ar": round(value / ar_value, 3) if ar_value else None,
+        "token_identical_to_ar": bool(ident_all),
+        "gpu_launches": int(dist_sum(n_launch)),
+        "clocks": clk.summary(),
+        "e2e": e2e,
+        "impl": "ours",
+    }
+    return out
+
+
+# -------------------------------------------------------------- reference
+def run_reference(args, rank, world, local):
+    from baseline import reference_arm
+    return reference_arm.run(args, rank, world, local)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            try:
+                out = run_reference(args, rank, world, local)
+            except ImportError as e:
+                out = {"impl": "reference", "unavailable": f"reference arm not importable: {e}"}
+        else:
+            out = run_ours(args, rank, world, local)
+        if rank == 0 and out is not None:
+            line = json.dumps(out)
+            print(line, flush=True)
+            if args.json_out:
+                with open(args.json_out, "w") as f:
+                    f.write(line + "\n")
+    finally:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,90 @@
+"""Public API: build a target + drafter pair and decode.
+
+>>> eng = D3DEngine.from_pretrained("Qwen/Qwen3-8B-dir", "D3D-1.7B-dir")      # doctest: +SKIP
+>>> out = eng.generate([[151644, 872, 198]], max_new_tokens=128)                 # doctest: +SKIP
+
+``D3DEngine`` wraps the coordinator (:class:`~d3d_b200.engine.spec.SpecDecoder`)
+with the kernel backends on CUDA and the PyTorch oracle backends on CPU.  The
+same object also runs target-only AR decoding (:meth:`generate_ar`), the
+baseline every speedup is measured against.
+"""
+from __future__ import annotations
+
+from dataclasses import replace
+from typing import Callable, List, Optional, Sequence
+
+import torch
+
+from .config import ModelConfig
+from .engine.spec import DecodeConfig, SpecDecoder, ar_generate
+
+
+class D3DEngine:
+    def __init__(self, target, draft, decode: DecodeConfig):
+        self.target = target
+        self.draft = draft
+        self.decode = decode
+        self.decoder = SpecDecoder(target, draft, decode)
+
+    # ------------------------------------------------------------ builders
+    @classmethod
+    def from_weights(cls, target_w, draft_w, decode: Optional[DecodeConfig] = None, *,
+                     max_seqs: int = 16, max_context: int = 4096, target_pages: Optional[int] = None,
+                     draft_pages: Optional[int] = None, page_size: int = 16, device="cuda",
+                     use_graphs: bool = True) -> "D3DEngine":
+        """Kernel backends from :class:`~d3d_b200.models.fast.FastWeights`."""
+        from .engine.fast import FastDraft, FastTarget
+        from .engine.layout import paged_draft_branch_tokens
+
+        decode = decode or DecodeConfig()
+        packed_q = paged_draft_branch_tokens(decode.block_size, max(decode.anchor_num, 1))
+        tp = target_pages or max_seqs * (max_context + 64 + page_size) // page_size + 8
+        dp = draft_pages or max_seqs * (max_context + packed_q + page_size) // page_size + 8
+        t = FastTarget(target_w, pages=tp, page_size=page_size, max_seqs=max_seqs,
+                       max_context=max_context, use_graphs=use_graphs, device=device)
+        d = FastDraft(draft_w, pages=dp, page_size=page_size, max_seqs=max_seqs,
+                      max_context=max_context, packed_q=packed_q, use_graphs=use_graphs,
+                      device=device)
+        return cls(t, d, decode)
+
+    @classmethod
+    def from_modules(cls, target_m, draft_m, decode: Optional[DecodeConfig] = None,
+                     **kw) -> "D3DEngine":
+        """Oracle backends on CPU, kernel backends when the modules are on CUDA."""
+        dev = next(target_m.parameters()).device
+        if dev.type == "cuda":
+            from .models.fast import FastWeights
+            return cls.from_weights(FastWeights.from_module(target_m, dev),
+                                    FastWeights.from_module(draft_m, dev), decode, device=dev, **kw)
+        from .engine.backends import TorchDraft, TorchTarget
+        decode = decode or DecodeConfig()
+        return cls(TorchTarget(target_m, decode.temperature), TorchDraft(draft_m), decode)
+
+    @classmethod
+    def from_pretrained(cls, target_path: str, draft_path: str,
+                        decode: Optional[DecodeConfig] = None, device="cuda", **kw) -> "D3DEngine":
+        from .checkpoint import load_model
+        t = load_model(target_path, device="cpu")
+        d = load_model(draft_path, device="cpu")
+        if device != "cpu" and torch.cuda.is_available():
+            from .models.fast import FastWeights
+            return cls.from_weights(FastWeights.from_module(t, device),
+                                    FastWeights.from_module(d, device), decode, device=device, **kw)
+        return cls.from_modules(t, d, decode)
+
+    # ------------------------------------------------------------- decoding
+    def generate(self, prompts: Sequence[Sequence[int]], *, max_new_tokens: Optional[int] = None,
+                 concurrency: int = 1, controlled: Optional[Callable[[int], object]] = None) -> dict:
+        if max_new_tokens is not None and max_new_tokens != self.decoder.cfg.max_new_tokens:
+            self.decoder.cfg = replace(self.decoder.cfg, max_new_tokens=int(max_new_tokens))
+        if isinstance(prompts, torch.Tensor):
+            prompts = prompts.tolist()
+        return self.decoder.generate(prompts, concurrency=concurrency, controlled=controlled)
+
+    def generate_ar(self, prompts: Sequence[Sequence[int]], *, max_new_tokens: Optional[int] = None,
+                    concurrency: int = 1) -> dict:
+        n = max_new_tokens or self.decoder.cfg.max_new_tokens
+        if isinstance(prompts, torch.Tensor):
+            prompts = prompts.tolist()
+        return ar_generate(self.target, prompts, n, eos=self.decoder.cfg.eos,
+                           ignore_eos=self.decoder.cfg.ignore_eos, concurrency=concurrency)

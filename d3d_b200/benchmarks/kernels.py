@@ -1,0 +1,215 @@
+"""Kernel microbenchmarks at the decode shapes of the headline configuration.
+
+    python -m d3d_b200.benchmarks.kernels [--only gemm,attn,forward] [--iters N]
+
+Times each sm_100a kernel with CUDA events on its launching stream after
+warm-up, cycling over enough distinct weight copies that the working set is
+larger than the 126 MB L2 (so every timed launch streams its weights from
+HBM), and prints achieved bandwidth / FLOP rate against the measured peaks in
+``MEASURED_PEAKS.json`` when present.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_peaks():
+    p = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    except Exception:
+        return PEAKS
+
+
+def timeit(fn, iters=50, warmup=5, graph=True):
+    """Mean device time per call in microseconds.  The ``iters`` calls are
+    captured in one CUDA graph and replayed, so host launch overhead is not
+    part of the number (back-to-back launches, as inside a decode step)."""
+    if not graph:
+        for _ in range(warmup):
+            fn(0)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(iters):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters * 1e3
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        for _ in range(warmup):
+            fn(0)
+    st.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for i in range(iters):
+            fn(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1e3  # us
+
+
+def bench_gemm(shapes, iters, peaks, rows):
+    from d3d_b200 import ops
+    E = ops.ext()
+    for name, m, n, k in shapes:
+        copies = max(2, math.ceil(3 * 126e6 / (n * k * 2)))
+        ws = [ops.pack_weight(torch.randn(n, k, device="cuda").to(torch.bfloat16) * 0.02)
+              for _ in range(copies)]
+        x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        bt = ops.bt_for(m)
+        s = ops.splitk_for(n, k, mtiles=math.ceil(m / bt), bt=bt) if m <= 2048 else 1
+        out = torch.empty(s * m * n, device="cuda")
+        us = timeit(lambda i: E.gemm_partial(x, ws[i % copies].data, out, s, bt, None, n), iters)
+        byts = n * k * 2 + m * k * 2 + s * m * n * 4
+        fl = 2 * m * n * k
+        rows.append(dict(kernel="gemm_tcgen05", shape=name, M=m, N=n, K=k, splits=s, bt=bt,
+                         us=round(us, 2), GBps=round(byts / us / 1e3, 1),
+                         hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3),
+                         TFLOPs=round(fl / us / 1e6, 1),
+                         tensor_frac=round(fl / us / 1e6 / peaks["bf16_tflops"], 3)))
+        del ws
+
+
+def bench_lmhead(iters, peaks, rows):
+    from d3d_b200 import ops
+    E = ops.ext()
+    for m, n, k, kk in ((1, 151936, 4096, 1), (16, 151936, 4096, 1), (272, 151936, 2048, 2)):
+        w = ops.pack_weight(torch.randn(n, k, device="cuda").to(torch.bfloat16) * 0.02)
+        w2 = ops.pack_weight(torch.randn(n, k, device="cuda").to(torch.bfloat16) * 0.02)
+        x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        ws = [w, w2]
+        kt = 1 if kk <= 1 else (2 if kk <= 2 else 4)
+        nt = math.ceil(n / 128)
+        tv = torch.empty(m * nt * kt, device="cuda")
+        ti = torch.empty(m * nt * kt, dtype=torch.int32, device="cuda")
+        ov = torch.empty(m, kk, device="cuda")
+        oi = torch.empty(m, kk, dtype=torch.int64, device="cuda")
+
+        def f(i):
+            E.gemm_topk(x, ws[i % 2].data, tv, ti, kk, ops.bt_for(m), None, n)
+            E.topk_merge(tv, ti, m, nt, kt, kk, ov, oi)
+        us = timeit(f, iters)
+        byts = n * k * 2
+        rows.append(dict(kernel="gemm_topk+merge", shape=f"lm_head top{kk}", M=m, N=n, K=k,
+                         us=round(us, 2), GBps=round(byts / us / 1e3, 1),
+                         hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3),
+                         TFLOPs=round(2 * m * n * k / us / 1e6, 1)))
+
+
+def bench_attn(iters, peaks, rows):
+    from d3d_b200 import ops
+    from d3d_b200.engine.layout import branch_specs, causal_rows, packed_layout
+    E = ops.ext()
+    for name, hq, hkv, prefix, q, chunk in (("verify 8B", 32, 8, 1000, 16, 64),
+                                           ("ar 8B", 32, 8, 1000, 1, 64),
+                                           ("verify 8B c128", 32, 8, 1000, 16, 128),
+                                           ("packed 1.7B A1", 16, 8, 1000, 272, 256),
+                                           ("packed 1.7B A3", 16, 8, 1000, 752, 256)):
+        d = 128
+        L = prefix + q
+        pages = math.ceil(L / 16)
+        kc = torch.randn(pages * 16, hkv, d, device="cuda").to(torch.bfloat16)
+        vc = torch.randn_like(kc)
+        bt = torch.arange(pages, dtype=torch.int32, device="cuda")[None]
+        qq = torch.randn(q, hq, d, device="cuda").to(torch.bfloat16)
+        if name.startswith("packed"):
+            A = 1 if name.endswith("A1") else 3
+            blk = torch.randint(0, 1000, (16,))
+            top = torch.stack([blk + j for j in range(A + 1)], 1)
+            lay = packed_layout(blk, branch_specs(blk.tolist(), top.tolist(), A), prefix, 16, 999, "causal")
+            rows_t = lay.rows.cuda()
+        else:
+            rows_t = causal_rows(prefix, q).cuda()
+        kv_end = torch.tensor([L], dtype=torch.int32, device="cuda")
+        nch = math.ceil(L / chunk)
+        po = torch.empty(nch * q * hq * d, device="cuda")
+        pm = torch.empty(nch * q * hq * 2, device="cuda")
+        out = torch.empty_like(qq)
+        us = timeit(lambda i: E.attention(qq, kc, vc, bt, rows_t, kv_end, 1, q, hq, hkv, 16,
+                                          1 / math.sqrt(d), chunk, nch, po, pm, out), iters)
+        byts = 2 * L * hkv * d * 2
+        rows.append(dict(kernel="attention", shape=name, M=q, N=L, K=d, us=round(us, 2),
+                         GBps=round(byts / us / 1e3, 1)))
+
+
+def bench_forward(iters, peaks, rows, layers=36):
+    """One full target forward (verify M=16 and AR M=1), graph-replayed."""
+    from d3d_b200 import config as C
+    from d3d_b200.models.fast import FastRunner, FastWeights, PagedKV
+    cfg = C.qwen3_8b().replace(num_hidden_layers=layers)
+    w = FastWeights.random(cfg, seed=0)
+    kv = PagedKV(cfg, num_pages=256, page_size=16, max_seqs=1, max_pages_per_seq=128)
+    kv.reserve(0, 0, 1100)
+    r = FastRunner(w, kv, max_context=1100)
+    for m in (1, 16):
+        b = r.buffers(1, m, 1)
+        b.pos.copy_(torch.arange(1000, 1000 + m))
+        b.slots.copy_(torch.arange(1000, 1000 + m))
+        from d3d_b200.engine.layout import causal_rows
+        b.rows.copy_(causal_rows(1000, m))
+        b.kv_end.fill_(1000 + m)
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            r.forward(b)
+        st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            n = r.forward(b)
+        us = timeit(lambda i: g.replay(), iters, graph=False)
+        byts = w.nbytes()
+        rows.append(dict(kernel="target forward (graph)", shape=f"Qwen3-8B M={m}", M=m, launches=n,
+                         us=round(us, 1), GBps=round(byts / us / 1e3, 1),
+                         hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3)))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="gemm,lmhead,attn,forward")
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--json", default=None)
+    ap.add_argument("--layers", type=int, default=36)
+    a = ap.parse_args()
+    peaks = load_peaks()
+    rows = []
+    only = set(a.only.split(","))
+    if "gemm" in only:
+        h, i = 4096, 12288
+        shapes = []
+        for m in (1, 16, 128):
+            shapes += [(f"8B qkv m{m}", m, 6144, h), (f"8B o m{m}", m, h, h),
+                       (f"8B gate_up m{m}", m, 2 * i, h), (f"8B down m{m}", m, h, i)]
+        for m in (272, 1088):
+            shapes += [(f"1.7B qkv m{m}", m, 4096, 2048), (f"1.7B o m{m}", m, 2048, 2048),
+                       (f"1.7B gate_up m{m}", m, 12288, 2048), (f"1.7B down m{m}", m, 2048, 6144)]
+        shapes += [("square 8192", 8192, 8192, 8192)]
+        bench_gemm(shapes, a.iters, peaks, rows)
+    if "lmhead" in only:
+        bench_lmhead(a.iters, peaks, rows)
+    if "attn" in only:
+        bench_attn(a.iters, peaks, rows)
+    if "forward" in only:
+        bench_forward(a.iters, peaks, rows, layers=a.layers)
+    for r in rows:
+        print(json.dumps(r))
+    if a.json:
+        with open(a.json, "w") as f:
+            json.dump(dict(peaks=peaks, rows=rows), f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,303 @@
+"""Target and draft backends on the sm_100a kernels (one GPU, two streams).
+
+The target verifies on its own CUDA stream while the drafter's packed
+all-outcome forward runs on a second stream of the same GPU (the 1-GPU
+configuration: target and drafter co-located; the reference needs two GPUs
+and a process boundary, ``single/eval_async_packed.py:216-346``).
+
+Every decode-shaped forward (verify ``B x K``, AR ``B x 1``, recovery
+``B x K``, packed ``B x (K + branches*K)``) is captured once in a CUDA graph
+and replayed; only the small integer inputs (token ids, RoPE positions, KV
+slots, row descriptors) are copied in per step, from pinned host memory.
+Greedy acceptance runs on the device inside the target's graph
+(``greedy_accept`` kernel) and copies the hidden state that produced the
+correction token for the conditioned drafter.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from ..utils import launches
+from ..models.fast import FastRunner, FastWeights, PagedKV, StepBuffers
+from .backends import DraftBackend, SeqState, TargetBackend, VerifyResult
+from .layout import causal_rows, prefix_rows
+
+
+class _GraphCache:
+    def __init__(self, runner: FastRunner, stream: torch.cuda.Stream, use_graphs: bool = True):
+        self.r = runner
+        self.stream = stream
+        self.use_graphs = use_graphs
+        self.graphs: Dict[tuple, torch.cuda.CUDAGraph] = {}
+        self.counts: Dict[tuple, int] = {}
+        self.pool = None
+
+    def run(self, key, b: StepBuffers, fn):
+        """Run ``fn(b)`` on the stream, through a CUDA graph captured on first use."""
+        if not self.use_graphs:
+            with torch.cuda.stream(self.stream):
+                launches.add(fn(b) or 0)
+            return
+        g = self.graphs.get(key)
+        if g is None:
+            with torch.cuda.stream(self.stream):
+                fn(b)      # warm-up (module attributes, TMA descriptor caches)
+            self.stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream, pool=self.pool):
+                self.counts[key] = fn(b) or 0
+            if self.pool is None:
+                self.pool = g.pool()
+            self.graphs[key] = g
+        with torch.cuda.stream(self.stream):
+            g.replay()
+        launches.add(self.counts[key])
+
+
+class _Pinned:
+    """Reusable pinned staging buffers keyed by name."""
+
+    def __init__(self):
+        self.bufs: Dict[str, torch.Tensor] = {}
+
+    def get(self, name, n, dtype):
+        t = self.bufs.get(name)
+        if t is None or t.numel() < n or t.dtype != dtype:
+            t = torch.empty(max(n, 64), dtype=dtype, pin_memory=True)
+            self.bufs[name] = t
+        return t[:n]
+
+
+def _stage(pin: _Pinned, name: str, arr: np.ndarray, dst: torch.Tensor, stream) -> None:
+    h = pin.get(name, arr.size, dst.dtype)
+    h.numpy()[...] = arr.reshape(-1)
+    with torch.cuda.stream(stream):
+        dst.view(-1)[: arr.size].copy_(h, non_blocking=True)
+
+
+class _FastModelBackend:
+    def __init__(self, weights: FastWeights, *, pages: int, page_size: int, max_seqs: int,
+                 max_context: int, extra_slots: int, batch_invariant: bool, use_graphs: bool,
+                 device="cuda", stream: Optional[torch.cuda.Stream] = None):
+        self.w = weights
+        self.cfg: ModelConfig = weights.cfg
+        self.device = torch.device(device)
+        max_pages_seq = math.ceil((max_context + extra_slots) / page_size)
+        self.kv = PagedKV(self.cfg, pages, page_size, max_seqs, max_pages_seq, device)
+        self.runner = FastRunner(weights, self.kv, max_context=max_context + extra_slots,
+                                 batch_invariant=batch_invariant, device=device)
+        self.stream = stream or torch.cuda.Stream(device=self.device)
+        self.graphs = _GraphCache(self.runner, self.stream, use_graphs)
+        self.pin = _Pinned()
+        self.rows_of: Dict[int, int] = {}           # seq index -> block-table row
+        self.free_rows: List[int] = list(range(max_seqs - 1, -1, -1))
+        self.extra_slots = extra_slots
+        self.max_context = max_context
+
+    def _row(self, s: SeqState) -> int:
+        r = self.rows_of.get(s.index)
+        if r is None:
+            if not self.free_rows:
+                raise RuntimeError("too many concurrent sequences for this backend")
+            r = self.rows_of[s.index] = self.free_rows.pop()
+        return r
+
+    def _release(self, s: SeqState) -> None:
+        r = self.rows_of.pop(s.index, None)
+        if r is not None:
+            self.free_rows.append(r)
+        self.kv.release(s.index)
+
+    def _fill(self, b: StepBuffers, seqs: List[SeqState], ids: np.ndarray, pos: np.ndarray,
+              rows: np.ndarray, kv_end: np.ndarray, tag: str) -> None:
+        q = b.Q
+        slots = np.empty(b.T, dtype=np.int64)
+        for i, s in enumerate(seqs):
+            slots[i * q:(i + 1) * q] = self.kv.slots(s.index, s.prefix, q)
+        seq_rows = np.array([self._row(s) for s in seqs], dtype=np.int64)
+        st = self.stream
+        _stage(self.pin, tag + "ids", ids.astype(np.int64), b.ids, st)
+        _stage(self.pin, tag + "pos", pos.astype(np.int64), b.pos, st)
+        _stage(self.pin, tag + "slots", slots, b.slots, st)
+        _stage(self.pin, tag + "rows", rows.astype(np.int32), b.rows, st)
+        _stage(self.pin, tag + "kvend", kv_end.astype(np.int32), b.kv_end, st)
+        _stage(self.pin, tag + "seqrows", seq_rows, b.seq_rows, st)
+
+    def _prefill_one(self, s: SeqState, rows: np.ndarray, topk: int, reserve: int):
+        n = len(s.prompt)
+        self.kv.reserve(s.index, self._row(s), reserve)
+        b = StepBuffers(self.cfg, 1, n, topk, 1, self.runner.splits(n), self.device)
+        b.bt_view = torch.zeros(1, self.kv.max_pages_per_seq, dtype=torch.int32, device=self.device)
+        b.chunk = self.runner.chunk_for(prefill=True)
+        saved = s.prefix
+        s.prefix = 0
+        self._fill(b, [s], np.array(s.prompt), np.arange(n), rows, np.array([n]), "pf")
+        s.prefix = saved
+        with torch.cuda.stream(self.stream):
+            launches.add(self.runner.forward(b))
+        # the pinned staging buffers are reused by the next call
+        self.stream.synchronize()
+        return b
+
+
+class FastTarget(_FastModelBackend, TargetBackend):
+    """Greedy target verification on the kernels."""
+
+    def __init__(self, weights: FastWeights, *, pages: int = 4096, page_size: int = 16,
+                 max_seqs: int = 16, max_context: int = 4096, use_graphs: bool = True,
+                 device="cuda", stream=None):
+        super().__init__(weights, pages=pages, page_size=page_size, max_seqs=max_seqs,
+                         max_context=max_context, extra_slots=64, batch_invariant=True,
+                         use_graphs=use_graphs, device=device, stream=stream)
+        self.hidden_size = self.cfg.hidden_size
+        self._pending = None
+        self._accept_bufs: Dict[tuple, dict] = {}
+        self.verify_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
+        self.time_verify = False
+
+    @torch.inference_mode()
+    def prefill(self, seqs):
+        anchors, hid = [], []
+        for s in seqs:
+            n = len(s.prompt)
+            rows = causal_rows(0, n).numpy()
+            b = self._prefill_one(s, rows, topk=1, reserve=self.max_context + 64)
+            with torch.cuda.stream(self.stream):
+                a = b.top_i[n - 1, 0].clone()
+                h = b.xn[n - 1].clone()
+            anchors.append(a)
+            hid.append(h)
+        self.stream.synchronize()
+        return torch.stack(anchors).cpu(), torch.stack(hid)
+
+    def _abufs(self, B, K):
+        key = (B, K)
+        a = self._accept_bufs.get(key)
+        if a is None:
+            dev = self.device
+            a = dict(commit=torch.zeros(B, dtype=torch.int64, device=dev),
+                     corr=torch.zeros(B, dtype=torch.int64, device=dev),
+                     hid=torch.zeros(B, self.cfg.hidden_size, dtype=torch.bfloat16, device=dev),
+                     h_commit=torch.zeros(B, dtype=torch.int64, pin_memory=True),
+                     h_corr=torch.zeros(B, dtype=torch.int64, pin_memory=True),
+                     h_post=torch.zeros(B * K, dtype=torch.int64, pin_memory=True),
+                     ev=torch.cuda.Event())
+            self._accept_bufs[key] = a
+        return a
+
+    def _verify_fn(self, a):
+        E = ops.ext()
+
+        def fn(b: StepBuffers):
+            n = self.runner.forward(b)
+            post = b.top_i[:, 0]
+            E.greedy_accept(b.ids.view(b.B, b.Q), post.view(b.B, b.Q), a["commit"], a["corr"],
+                            b.xn, a["hid"])
+            return n + 1
+        return fn
+
+    @torch.inference_mode()
+    def submit_verify(self, seqs, blocks, q=None):
+        if q is not None:
+            raise NotImplementedError("the fast target path verifies greedily (temperature 0)")
+        B, K = blocks.shape
+        b = self.runner.buffers(B, K, 1)
+        a = self._abufs(B, K)
+        pos = np.stack([np.arange(s.prefix, s.prefix + K) for s in seqs])
+        rows = np.stack([causal_rows(s.prefix, K).numpy() for s in seqs])
+        kv_end = np.array([s.prefix + K for s in seqs])
+        self._fill(b, seqs, blocks.numpy(), pos, rows, kv_end, f"v{B}_{K}")
+        ev0 = ev1 = None
+        if self.time_verify:
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record(self.stream)
+        self.graphs.run(("verify", B, K), b, self._verify_fn(a))
+        if ev1 is not None:
+            ev1.record(self.stream)
+            self.verify_events.append((ev0, ev1))
+        with torch.cuda.stream(self.stream):
+            a["h_commit"].copy_(a["commit"], non_blocking=True)
+            a["h_corr"].copy_(a["corr"], non_blocking=True)
+            a["h_post"].copy_(b.top_i[:, 0], non_blocking=True)
+            # the conditioning rows leave the graph's static buffer before the next replay
+            hid = a["hid"].clone()
+            a["ev"].record(self.stream)
+        self._pending = (B, K, a, hid)
+
+    @torch.inference_mode()
+    def receive(self) -> VerifyResult:
+        B, K, a, hid = self._pending
+        self._pending = None
+        a["ev"].synchronize()
+        return VerifyResult(a["h_commit"].clone(), a["h_corr"].clone(),
+                            a["h_post"].clone().view(B, K), hid)
+
+    def release(self, seq):
+        self._release(seq)
+
+
+class FastDraft(_FastModelBackend, DraftBackend):
+    """Drafter forwards (prefill, recovery, packed outcomes) on the kernels."""
+
+    def __init__(self, weights: FastWeights, *, pages: int = 8192, page_size: int = 16,
+                 max_seqs: int = 16, max_context: int = 4096, packed_q: int = 1024,
+                 use_graphs: bool = True, device="cuda", stream=None):
+        super().__init__(weights, pages=pages, page_size=page_size, max_seqs=max_seqs,
+                         max_context=max_context, extra_slots=packed_q, batch_invariant=False,
+                         use_graphs=use_graphs, device=device, stream=stream)
+        self.vocab_size = self.cfg.vocab_size
+        self.mask_id = int(self.cfg.mask_token_id)
+        self._host: Dict[tuple, dict] = {}
+
+    @torch.inference_mode()
+    def prefill(self, seqs, mode, block_size):
+        for s in seqs:
+            n = len(s.prompt)
+            rows = prefix_rows(0, n, mode, block_size).numpy()
+            self._prefill_one(s, rows, topk=0, reserve=self.max_context + self.extra_slots)
+        self.stream.synchronize()
+
+    def _hbufs(self, B, Q, k):
+        key = (B, Q, k)
+        h = self._host.get(key)
+        if h is None:
+            h = dict(top=torch.zeros(B * Q, max(k, 1), dtype=torch.int64, pin_memory=True),
+                     ev=torch.cuda.Event())
+            self._host[key] = h
+        return h
+
+    @torch.inference_mode()
+    def forward(self, seqs, ids, positions, rows, *, store, topk, cond_rows=None, sample=None):
+        if sample is not None:
+            raise NotImplementedError("the fast draft path proposes greedily (temperature 0)")
+        B, Q = ids.shape
+        k = max(1, topk)
+        b = self.runner.buffers(B, Q, k)
+        kv_end = torch.maximum(rows[:, :, 0].amax(1), rows[:, :, 2].amax(1)).numpy()
+        self._fill(b, seqs, ids.numpy(), positions.numpy(), rows.numpy(), kv_end, f"d{B}_{Q}")
+        use_cond = cond_rows is not None and self.w.cond_proj is not None and seqs[0].cond is not None
+        if use_cond:
+            _stage(self.pin, f"d{B}_{Q}cr", cond_rows.numpy().astype(np.uint8), b.cond_rows, self.stream)
+            with torch.cuda.stream(self.stream):
+                for i, s in enumerate(seqs):
+                    b.cond[i].copy_(s.cond.to(self.device, torch.bfloat16), non_blocking=True)
+        self.graphs.run(("draft", B, Q, k, use_cond), b, lambda bb: self.runner.forward(bb, use_cond))
+        h = self._hbufs(B, Q, k)
+        with torch.cuda.stream(self.stream):
+            h["top"].copy_(b.top_i, non_blocking=True)
+            h["ev"].record(self.stream)
+        h["ev"].synchronize()
+        top = h["top"].view(B, Q, k).clone()
+        out = {"greedy": top[:, :, 0]}
+        if topk:
+            out["top"] = top[:, :, :topk]
+        return out
+
+    def release(self, seq):
+        self._release(seq)

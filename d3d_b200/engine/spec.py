@@ -212,13 +212,12 @@ class SpecDecoder:
             if not running:
                 continue
             batch_sizes.append(len(running))
-            # truncate blocks at the output budget (``eval_async_packed.py:1022-1030``)
-            blocks = []
-            for s in running:
-                room = cfg.max_new_tokens - len(s.generated)
-                blocks.append(s.current[:max(1, min(k, room))])
-            width = min(b.shape[0] for b in blocks)
-            block_t = torch.stack([b[:width] for b in blocks])
+            # The reference truncates the last block at the output budget
+            # (``eval_async_packed.py:1022-1030``); here the full block is
+            # verified (one captured shape) and the commit is clipped instead,
+            # which emits the same tokens.
+            width = k
+            block_t = torch.stack([s.current[:k] for s in running])
             qq = None
             if not is_greedy(cfg.temperature):
                 qq = (torch.stack([s.q_ids[1:width] for s in running]),

@@ -1,0 +1,324 @@
+"""The Qwen3 / D3D forward on the sm_100a kernels (inference fast path).
+
+Weights are held in bf16 in fused layouts (``qkv = [q; k; v]`` and
+``gate_up = [gate; up]`` rows), the KV cache is paged
+(``[slots, Hkv, D]`` per layer, slot = page * page_size + offset), and one
+layer is nine launches::
+
+    gemm(qkv) -> qkv_rope_kv (QK-norm, RoPE, KV write) -> attention
+    -> gemm(o) -> add_rmsnorm -> gemm(gate_up) -> swiglu -> gemm(down)
+    -> add_rmsnorm (next layer's input norm, or the final norm)
+
+Every GEMM writes fp32 split-K partials with a split factor that depends on
+the weight shape only (``ops.splitk_for``); decode-sized forwards use a fixed
+attention key chunk.  Together these make a token's logits bit-identical
+whether it is decoded alone (AR) or verified inside a block, so greedy
+speculative decoding reproduces AR decoding token for token.
+
+Inputs of a forward live in :class:`StepBuffers` (static device tensors) so
+the whole forward can be captured once per shape in a CUDA graph and
+replayed.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from .qwen3 import Qwen3LM
+
+
+# --------------------------------------------------------------------------
+# weights
+# --------------------------------------------------------------------------
+@dataclass
+class LayerWeights:
+    qkv: torch.Tensor
+    o: torch.Tensor
+    gate_up: torch.Tensor
+    down: torch.Tensor
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+
+
+class FastWeights:
+    def __init__(self, cfg: ModelConfig, embed, layers: List[LayerWeights], final_norm, lm_head,
+                 cond_proj=None):
+        self.cfg = cfg
+        self.embed = embed
+        self.layers = layers
+        self.final_norm = final_norm
+        self.lm_head = lm_head
+        self.cond_proj = cond_proj
+
+    @classmethod
+    @torch.no_grad()
+    def from_module(cls, m: Qwen3LM, device="cuda") -> "FastWeights":
+        bf = lambda t: t.detach().to(device=device, dtype=torch.bfloat16).contiguous()
+        pk = lambda t: ops.pack_weight(bf(t))
+        layers = []
+        for L in m.model.layers:
+            a = L.self_attn
+            layers.append(LayerWeights(
+                qkv=pk(torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0)),
+                o=pk(a.o_proj.weight),
+                gate_up=pk(torch.cat([L.mlp.gate_proj.weight, L.mlp.up_proj.weight], 0)),
+                down=pk(L.mlp.down_proj.weight),
+                in_norm=bf(L.input_layernorm.weight), post_norm=bf(L.post_attention_layernorm.weight),
+                q_norm=bf(a.q_norm.weight), k_norm=bf(a.k_norm.weight)))
+        embed = bf(m.model.embed_tokens.weight)
+        lm = pk(embed if m.cfg.tie_word_embeddings else m.lm_head.weight)
+        cp = pk(m.cond_proj.weight) if getattr(m, "cond_proj", None) is not None else None
+        return cls(m.cfg, embed, layers, bf(m.model.norm.weight), lm, cp)
+
+    @classmethod
+    @torch.no_grad()
+    def random(cls, cfg: ModelConfig, seed: int = 0, device="cuda",
+               std: Optional[float] = None) -> "FastWeights":
+        """Seeded N(0, std) init drawn on the device (no host copy of the model)."""
+        std = cfg.initializer_range if std is None else std
+        gen = torch.Generator(device=device)
+        counter = [0]
+
+        def rnd(*shape):
+            counter[0] += 1
+            gen.manual_seed(int(seed) * 1_000_003 + counter[0])
+            t = torch.empty(*shape, dtype=torch.bfloat16, device=device)
+            # chunked so the fp32 temporary stays small
+            flat = t.view(-1)
+            step = 1 << 26
+            for i in range(0, flat.numel(), step):
+                n = min(step, flat.numel() - i)
+                flat[i:i + n] = (torch.randn(n, generator=gen, device=device) * std).to(torch.bfloat16)
+            return t
+
+        ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=device)
+        prnd = lambda *shape: ops.pack_weight(rnd(*shape))
+        h, i, d = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+        layers = [LayerWeights(qkv=prnd(cfg.q_size + 2 * cfg.kv_size, h), o=prnd(h, cfg.q_size),
+                               gate_up=prnd(2 * i, h), down=prnd(h, i), in_norm=ones(h),
+                               post_norm=ones(h), q_norm=ones(d), k_norm=ones(d))
+                  for _ in range(cfg.num_hidden_layers)]
+        embed = rnd(cfg.vocab_size, h)
+        lm = ops.pack_weight(embed) if cfg.tie_word_embeddings else prnd(cfg.vocab_size, h)
+        cp = prnd(h, cfg.cond_hidden_size) if cfg.cond_hidden_size else None
+        return cls(cfg, embed, layers, ones(h), lm, cp)
+
+    def drop_layers(self, idx) -> "FastWeights":
+        keep = [L for j, L in enumerate(self.layers) if j not in set(idx)]
+        cfg = self.cfg.replace(num_hidden_layers=len(keep))
+        return FastWeights(cfg, self.embed, keep, self.final_norm, self.lm_head, self.cond_proj)
+
+    def nbytes(self) -> int:
+        """Bytes of weights one forward streams (embedding rows excluded)."""
+        n = self.final_norm.numel() + self.lm_head.numel()
+        for L in self.layers:
+            n += sum(t.numel() for t in (L.qkv, L.o, L.gate_up, L.down, L.in_norm, L.post_norm,
+                                         L.q_norm, L.k_norm))
+        return 2 * n
+
+
+# --------------------------------------------------------------------------
+# paged KV
+# --------------------------------------------------------------------------
+class PagedKV:
+    """Per-layer paged K/V storage plus a page allocator and block tables."""
+
+    def __init__(self, cfg: ModelConfig, num_pages: int, page_size: int, max_seqs: int,
+                 max_pages_per_seq: int, device="cuda"):
+        self.cfg = cfg
+        self.page_size = page_size
+        self.num_pages = num_pages
+        slots = num_pages * page_size
+        shape = (slots, cfg.num_key_value_heads, cfg.head_dim)
+        self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.num_hidden_layers)]
+        self.v = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.num_hidden_layers)]
+        self.free: List[int] = list(range(num_pages - 1, -1, -1))
+        self.tables: Dict[int, List[int]] = {}
+        self.max_pages_per_seq = max_pages_per_seq
+        self.max_seqs = max_seqs
+        self.block_table = torch.zeros(max_seqs, max_pages_per_seq, dtype=torch.int32, device=device)
+        self.device = device
+
+    def reserve(self, sid: int, row: int, length: int) -> None:
+        """Make sequence ``sid`` (block-table row ``row``) cover ``length`` slots."""
+        t = self.tables.setdefault(sid, [])
+        need = math.ceil(length / self.page_size) - len(t)
+        if need > 0:
+            if need > len(self.free):
+                raise RuntimeError(f"out of KV pages: need {need}, free {len(self.free)}")
+            if len(t) + need > self.max_pages_per_seq:
+                raise RuntimeError("sequence exceeds max_pages_per_seq")
+            new = [self.free.pop() for _ in range(need)]
+            t.extend(new)
+            self.block_table[row, : len(t)] = torch.tensor(t, dtype=torch.int32).to(self.device,
+                                                                                   non_blocking=True)
+
+    def trim(self, sid: int, row: int, length: int) -> None:
+        t = self.tables.get(sid, [])
+        keep = math.ceil(length / self.page_size)
+        while len(t) > keep:
+            self.free.append(t.pop())
+
+    def release(self, sid: int) -> None:
+        for p in self.tables.pop(sid, []):
+            self.free.append(p)
+
+    def slots(self, sid: int, start: int, n: int) -> List[int]:
+        t = self.tables[sid]
+        ps = self.page_size
+        return [t[(start + j) // ps] * ps + (start + j) % ps for j in range(n)]
+
+    @property
+    def leaked(self) -> int:
+        return self.num_pages - len(self.free) - sum(len(t) for t in self.tables.values())
+
+
+# --------------------------------------------------------------------------
+# step buffers + runner
+# --------------------------------------------------------------------------
+class StepBuffers:
+    """Static device inputs/outputs of one forward shape (B sequences x Q tokens)."""
+
+    def __init__(self, cfg: ModelConfig, B: int, Q: int, topk: int, n_chunks: int,
+                 splits: Dict[str, int], device="cuda", with_hidden_copy: bool = False):
+        T = B * Q
+        self.B, self.Q, self.T, self.topk, self.n_chunks = B, Q, T, topk, n_chunks
+        dev = device
+        h, d = cfg.hidden_size, cfg.head_dim
+        self.ids = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.slots = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.rows = torch.zeros(T, 3, dtype=torch.int32, device=dev)
+        self.kv_end = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.seq_rows = torch.zeros(B, dtype=torch.int64, device=dev)   # block-table rows
+        self.bt_view = None    # [B, max_pages] gathered per step from the KV block table
+        self.cond = torch.zeros(B, cfg.cond_hidden_size or 8, dtype=torch.bfloat16, device=dev)
+        self.cond_h = torch.zeros(B, h, dtype=torch.bfloat16, device=dev)
+        self.cond_rows = torch.zeros(T, dtype=torch.uint8, device=dev)
+        self.x = torch.zeros(T, h, dtype=torch.bfloat16, device=dev)       # residual stream
+        self.xn = torch.zeros(T, h, dtype=torch.bfloat16, device=dev)      # normed
+        self.q = torch.zeros(T, cfg.num_attention_heads, d, dtype=torch.bfloat16, device=dev)
+        self.attn = torch.zeros(T, cfg.q_size, dtype=torch.bfloat16, device=dev)
+        self.h = torch.zeros(T, cfg.intermediate_size, dtype=torch.bfloat16, device=dev)
+        nmax = max(splits["qkv"] * (cfg.q_size + 2 * cfg.kv_size), splits["o"] * h,
+                   splits["gate_up"] * 2 * cfg.intermediate_size, splits["down"] * h)
+        self.part = torch.zeros(nmax * T, dtype=torch.float32, device=dev)
+        self.att_o = torch.zeros(n_chunks * T * cfg.num_attention_heads * d if n_chunks > 1 else 1,
+                                 dtype=torch.float32, device=dev)
+        self.att_ml = torch.zeros(n_chunks * T * cfg.num_attention_heads * 2 if n_chunks > 1 else 1,
+                                  dtype=torch.float32, device=dev)
+        kt = 1 if topk <= 1 else (2 if topk <= 2 else 4)
+        self.kt = kt
+        ntiles = math.ceil(cfg.vocab_size / 128)
+        self.ntiles = ntiles
+        self.tv = torch.zeros(T * ntiles * kt, dtype=torch.float32, device=dev)
+        self.ti = torch.zeros(T * ntiles * kt, dtype=torch.int32, device=dev)
+        self.top_v = torch.zeros(T, max(topk, 1), dtype=torch.float32, device=dev)
+        self.top_i = torch.zeros(T, max(topk, 1), dtype=torch.int64, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+
+class FastRunner:
+    """Runs forwards of one model on the kernels; captures CUDA graphs per shape."""
+
+    def __init__(self, weights: FastWeights, kv: PagedKV, *, decode_chunk: Optional[int] = None,
+                 max_context: int = 4096, batch_invariant: bool = True, device="cuda"):
+        self.w = weights
+        self.cfg = weights.cfg
+        self.kv = kv
+        self.device = device
+        # Key chunk per attention CTA.  Fine chunks keep >100 CTAs busy at decode
+        # sizes (one 64-key tile each for the batch-invariant target); the
+        # drafter's packed forward has many query rows, so it takes 256.
+        self.decode_chunk = decode_chunk or (64 if batch_invariant else 256)
+        self.max_context = max_context
+        self.batch_invariant = batch_invariant
+        c = self.cfg
+        self.inv_freq = (1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, dtype=torch.float32)
+                                                 / c.head_dim))).to(device)
+        self.scale = 1.0 / math.sqrt(c.head_dim)
+        self._bufs: Dict[Tuple, StepBuffers] = {}
+        self._graphs: Dict[Tuple, torch.cuda.CUDAGraph] = {}
+
+    # ------------------------------------------------------------- policies
+    def splits(self, T: int) -> Dict[str, int]:
+        """Split-K per GEMM.  Batch-invariant runners (the target) use the
+        weight shape only for decode-sized T; others also count token tiles."""
+        c = self.cfg
+        if self.batch_invariant:
+            if T > 256:
+                return dict(qkv=1, o=1, gate_up=1, down=1)
+            mt, bt = 1, 16
+        else:
+            bt = ops.bt_for(T)
+            mt = math.ceil(T / bt)
+            if T > 2048:
+                return dict(qkv=1, o=1, gate_up=1, down=1)
+        f = lambda n, k: ops.splitk_for(n, k, mtiles=mt, bt=bt)
+        return dict(qkv=f(c.q_size + 2 * c.kv_size, c.hidden_size), o=f(c.hidden_size, c.q_size),
+                    gate_up=f(2 * c.intermediate_size, c.hidden_size),
+                    down=f(c.hidden_size, c.intermediate_size))
+
+    def buffers(self, B: int, Q: int, topk: int, prefill: bool = False) -> StepBuffers:
+        key = (B, Q, topk, prefill)
+        b = self._bufs.get(key)
+        if b is None:
+            T = B * Q
+            chunk = self.chunk_for(prefill)
+            nch = max(1, math.ceil(self.max_context / chunk))
+            b = StepBuffers(self.cfg, B, Q, topk, nch, self.splits(T), self.device)
+            b.bt_view = torch.zeros(B, self.kv.max_pages_per_seq, dtype=torch.int32, device=self.device)
+            b.chunk = chunk
+            self._bufs[key] = b
+        return b
+
+    def chunk_for(self, prefill: bool) -> int:
+        if prefill:
+            return max(64, int(math.ceil(self.max_context / 64) * 64))
+        return self.decode_chunk
+
+    # -------------------------------------------------------------- forward
+    def forward(self, b: StepBuffers, use_cond: bool = False) -> int:
+        """Forward over ``b`` (inputs already in place); writes ``b.top_i``/``b.top_v``
+        (top-k over the vocabulary of every row) and ``b.xn`` (final hidden).
+        Returns the number of kernels launched."""
+        E = ops.ext()
+        c, w = self.cfg, self.w
+        T, B, Q = b.T, b.B, b.Q
+        sp = self.splits(T)
+        bt = ops.bt_for(T)
+        hq, hkv, d = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        cond = None
+        if use_cond and w.cond_proj is not None:
+            ops.gemm_bf16(b.cond, w.cond_proj, b.cond_h, None, ops.bt_for(B), b.status)
+            cond = b.cond_h
+        E.embed(b.ids, w.embed, cond, b.cond_rows if cond is not None else None, Q, b.x)
+        E.add_rmsnorm(None, 1, b.x, w.layers[0].in_norm, b.xn, c.rms_norm_eps)
+        torch.index_select(self.kv.block_table, 0, b.seq_rows, out=b.bt_view)
+        for li, L in enumerate(w.layers):
+            E.gemm_partial(b.xn, L.qkv.data, b.part, sp["qkv"], bt, b.status, L.qkv.n)
+            E.qkv_rope_kv(b.part, None, sp["qkv"], L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
+                          b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, c.rms_norm_eps)
+            E.attention(b.q, self.kv.k[li], self.kv.v[li], b.bt_view, b.rows, b.kv_end, B, Q, hq, hkv,
+                        self.kv.page_size, self.scale, b.chunk, b.n_chunks,
+                        b.att_o if b.n_chunks > 1 else None, b.att_ml if b.n_chunks > 1 else None,
+                        b.attn)
+            E.gemm_partial(b.attn, L.o.data, b.part, sp["o"], bt, b.status, L.o.n)
+            E.add_rmsnorm(b.part, sp["o"], b.x, L.post_norm, b.xn, c.rms_norm_eps)
+            E.gemm_partial(b.xn, L.gate_up.data, b.part, sp["gate_up"], bt, b.status, L.gate_up.n)
+            E.swiglu(b.part, sp["gate_up"], b.h)
+            E.gemm_partial(b.h, L.down.data, b.part, sp["down"], bt, b.status, L.down.n)
+            nxt = w.layers[li + 1].in_norm if li + 1 < len(w.layers) else w.final_norm
+            E.add_rmsnorm(b.part, sp["down"], b.x, nxt, b.xn, c.rms_norm_eps)
+        if b.topk > 0:
+            E.gemm_topk(b.xn, w.lm_head.data, b.tv, b.ti, b.topk, bt, b.status, w.lm_head.n)
+            E.topk_merge(b.tv, b.ti, T, b.ntiles, b.kt, b.topk, b.top_v, b.top_i)
+        n = 2 + len(w.layers) * (9 + (1 if b.n_chunks > 1 else 0)) + (2 if b.topk > 0 else 0)
+        return n + (1 if cond is not None else 0)

@@ -41,14 +41,24 @@ def available() -> bool:
 NUM_SMS = 148
 
 
-def splitk_for(n: int, k: int, sms: int = NUM_SMS) -> int:
-    """Split-K factor from the weight shape alone (batch invariance)."""
-    tiles = math.ceil(n / 128)
+def ctas_per_sm(bt: int) -> int:
+    """Co-resident GEMM CTAs per SM for token tile ``bt`` (mirrors the kernel's
+    shared-memory policy: 2 when >= 4 pipeline stages fit in ~110 KB)."""
+    stage = 128 * 64 * 2 + bt * 64 * 2
+    return 2 if (110 * 1024) // stage >= 4 else 1
+
+
+def splitk_for(n: int, k: int, sms: int = NUM_SMS, mtiles: int = 1, bt: int = 16) -> int:
+    """Split-K factor that fills whole waves of CTA slots (SMs x co-resident
+    CTAs).  For the target it is called with ``mtiles=1, bt=16`` whatever the
+    token count, so it depends on the weight shape alone (batch invariance)."""
+    sms = sms * ctas_per_sm(bt)
+    tiles = math.ceil(n / 128) * mtiles
     kb = math.ceil(k / 64)
-    if tiles >= sms:
-        return 1
     best, best_eff = 1, 0.0
     for s in range(1, min(16, kb) + 1):
+        if kb // s < 4:          # keep at least 4 K blocks (256) per CTA
+            break
         ctas = tiles * s
         waves = math.ceil(ctas / sms)
         eff = ctas / (waves * sms)
@@ -59,29 +69,71 @@ def splitk_for(n: int, k: int, sms: int = NUM_SMS) -> int:
 
 
 def bt_for(m: int) -> int:
-    """Token tile (MMA N) for m tokens: one tile up to 256, padded to 16."""
+    """Token tile for m tokens: up to 256 in one MMA (multiple of 16), up to
+    512 as two MMAs (multiple of 32), so each weight tile is read once for
+    up to 512 tokens."""
     if m <= 256:
         return max(16, ((m + 15) // 16) * 16)
-    tiles = math.ceil(m / 256)
+    if m <= 512:
+        return ((m + 31) // 32) * 32
+    tiles = math.ceil(m / 512)
     per = math.ceil(m / tiles)
-    return ((per + 15) // 16) * 16
+    return ((per + 31) // 32) * 32
+
+
+class PackedWeight:
+    """A [N, K] bf16 weight stored as contiguous 128 x 64 tiles
+    (``[ceil(N/128)][ceil(K/64)][128][64]``, zero padded).  Each GEMM pipeline
+    stage then reads one contiguous 16 KB block from HBM instead of 128 rows
+    of 128 bytes that are K*2 bytes apart."""
+
+    def __init__(self, data: torch.Tensor, n: int, k: int):
+        self.data, self.n, self.k = data, int(n), int(k)
+
+    @property
+    def shape(self):
+        return (self.n, self.k)
+
+    def numel(self) -> int:
+        return self.n * self.k
+
+    def unpack(self) -> torch.Tensor:
+        nt, kt = math.ceil(self.n / 128), math.ceil(self.k / 64)
+        w = self.data.view(nt, kt, 128, 64).permute(0, 2, 1, 3).reshape(nt * 128, kt * 64)
+        return w[: self.n, : self.k]
+
+
+def pack_weight(w: torch.Tensor) -> PackedWeight:
+    n, k = w.shape
+    nt, kt = math.ceil(n / 128), math.ceil(k / 64)
+    pad = torch.zeros(nt * 128, kt * 64, dtype=torch.bfloat16, device=w.device)
+    pad[:n, :k] = w
+    data = pad.view(nt, 128, kt, 64).permute(0, 2, 1, 3).contiguous().view(nt * kt * 128, 64)
+    return PackedWeight(data, n, k)
+
+
+def _w(w):
+    return (w.data, w.n) if isinstance(w, PackedWeight) else (w, 0)
 
 
 # ------------------------------------------------------------ thin wrappers
 def gemm_partial(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, splits: int,
                  bt: Optional[int] = None, status: Optional[torch.Tensor] = None) -> torch.Tensor:
-    ext().gemm_partial(x, w, out, int(splits), int(bt or bt_for(x.shape[0])), status)
+    wd, wn = _w(w)
+    ext().gemm_partial(x, wd, out, int(splits), int(bt or bt_for(x.shape[0])), status, wn)
     return out
 
 
 def gemm_bf16(x, w, out, residual=None, bt=None, status=None):
-    ext().gemm_bf16(x, w, out, residual, int(bt or bt_for(x.shape[0])), status)
+    wd, wn = _w(w)
+    ext().gemm_bf16(x, wd, out, residual, int(bt or bt_for(x.shape[0])), status, wn)
     return out
 
 
 def gemm_topk(x, w, k: int, bt=None, status=None, bufs=None):
     """Top-k (value, index) of ``x @ w.T`` per row without storing logits."""
     m, n = x.shape[0], w.shape[0]
+    wd, wn = _w(w)
     kt = 1 if k <= 1 else (2 if k <= 2 else 4)
     ntiles = math.ceil(n / 128)
     if bufs is None:
@@ -92,11 +144,13 @@ def gemm_topk(x, w, k: int, bt=None, status=None, bufs=None):
     else:
         tv, ti, ov, oi = bufs
     e = ext()
-    e.gemm_topk(x, w, tv, ti, int(k), int(bt or bt_for(m)), status)
+    e.gemm_topk(x, wd, tv, ti, int(k), int(bt or bt_for(m)), status, wn)
     e.topk_merge(tv, ti, m, ntiles, kt, int(k), ov, oi)
     return ov, oi
 
 
-def linear_ref(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def linear_ref(x: torch.Tensor, w) -> torch.Tensor:
     """fp32 reference of the GEMM."""
+    if isinstance(w, PackedWeight):
+        w = w.unpack()
     return x.float() @ w.float().t()

@@ -26,6 +26,7 @@ namespace d3d {
 
 constexpr int AT_ROWS = 64;
 constexpr int AT_KEYS = 64;
+constexpr int AT_MAX_PAGES = 1024;  // chunk / page_size + 1 must fit
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -58,13 +59,16 @@ __device__ __forceinline__ bool visible(int k, int lim, int lo, int hi) { return
 
 template <int D>
 __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+  griddep_launch();
+  griddep_wait();
   constexpr int LD = D + 8;  // padded smem row (bank-conflict-free ldmatrix)
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* Ks = Qs + AT_ROWS * LD;
-  __nv_bfloat16* Vs = Ks + AT_KEYS * LD;
+  __nv_bfloat16* Kb = Qs + AT_ROWS * LD;       // [2][AT_KEYS][LD]
+  __nv_bfloat16* Vb = Kb + 2 * AT_KEYS * LD;   // [2][AT_KEYS][LD]
   __shared__ int s_rows[AT_ROWS][3];
   __shared__ int s_range[3];
+  __shared__ int s_pages[AT_MAX_PAGES];   // page ids of this CTA's key chunk
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = a.Hq / a.Hkv;
@@ -140,28 +144,49 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
   const int kbeg = chunk_id * a.chunk;
   const int kend = min(kbeg + a.chunk, kv_end);
   const int* bt = a.block_table + static_cast<size_t>(b) * a.bt_stride;
+  // page ids of the chunk, read once (the tile loads below would otherwise each
+  // wait on a dependent global load before issuing their copies)
+  const int pg0 = kbeg / a.page_size;
+  const int npg = kend > kbeg ? (kend - 1) / a.page_size - pg0 + 1 : 0;
+  for (int i = tid; i < npg && i < AT_MAX_PAGES; i += 128) s_pages[i] = bt[pg0 + i];
+  __syncthreads();
 
-  for (int k0 = kbeg; k0 < kend; k0 += AT_KEYS) {
-    const bool need = k0 < max_lim || (k0 + AT_KEYS > min_lo && k0 < max_hi);
-    if (!need) continue;  // uniform across the CTA
-    // ---- load K/V tile (zeros beyond kv_end)
+  auto needed = [&](int k0) { return k0 < max_lim || (k0 + AT_KEYS > min_lo && k0 < max_hi); };
+  auto next_needed = [&](int k0) {
+    while (k0 < kend && !needed(k0)) k0 += AT_KEYS;
+    return k0;
+  };
+  // issue the async copy of one K/V tile into buffer `buf` (zeros beyond kv_end)
+  auto load_tile = [&](int k0, int buf) {
+    __nv_bfloat16* Ks = Kb + buf * AT_KEYS * LD;
+    __nv_bfloat16* Vs = Vb + buf * AT_KEYS * LD;
     for (int c = tid; c < AT_KEYS * (D / 8); c += 128) {
       const int kr = c / (D / 8), dc = (c % (D / 8)) * 8;
       const int s = k0 + kr;
-      const uint32_t dk = smem_u32(Ks + kr * LD + dc), dv = smem_u32(Vs + kr * LD + dc);
       if (s < kv_end) {
-        const long long page = bt[s / a.page_size];
+        const int64_t page = s_pages[s / a.page_size - pg0];
         const size_t off = ((page * a.page_size + s % a.page_size) * a.Hkv + h) * static_cast<size_t>(D) + dc;
-        cp_async16(dk, a.k_cache + off);
-        cp_async16(dv, a.v_cache + off);
+        cp_async16(smem_u32(Ks + kr * LD + dc), a.k_cache + off);
+        cp_async16(smem_u32(Vs + kr * LD + dc), a.v_cache + off);
       } else {
         *reinterpret_cast<uint4*>(Ks + kr * LD + dc) = make_uint4(0, 0, 0, 0);
         *reinterpret_cast<uint4*>(Vs + kr * LD + dc) = make_uint4(0, 0, 0, 0);
       }
     }
+  };
+
+  int k0 = next_needed(kbeg);
+  int buf = 0;
+  if (k0 < kend) load_tile(k0, 0);
+  cp_async_commit();
+  while (k0 < kend) {
+    const int k1 = next_needed(k0 + AT_KEYS);
+    if (k1 < kend) load_tile(k1, buf ^ 1);  // prefetch the next tile while this one computes
     cp_async_commit();
-    cp_async_wait_all();
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
     __syncthreads();
+    const __nv_bfloat16* Ks = Kb + buf * AT_KEYS * LD;
+    const __nv_bfloat16* Vs = Vb + buf * AT_KEYS * LD;
 
     // ---- S = Q K^T (16 rows x 64 keys per warp)
     float s[8][4];
@@ -179,18 +204,35 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
         mma16816(s[nb + 1], qf[kk], b2, b3);
       }
     }
-    // ---- mask + online softmax
+    // ---- mask + online softmax (per-element masking only when some row of
+    // this warp sees part of the tile)
     float tmA = -INFINITY, tmB = -INFINITY;
+    const int k1e = k0 + AT_KEYS;
+    const bool fullA = k1e <= kend && (k1e <= limA || (k0 >= loA && k1e <= hiA));
+    const bool fullB = k1e <= kend && (k1e <= limB || (k0 >= loB && k1e <= hiB));
+    if (__all_sync(0xffffffffu, fullA && fullB)) {
 #pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
+      for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int key = k0 + nb * 8 + (lane & 3) * 2 + e;
-        const bool inb = key < kend;
-        s[nb][e] = (inb && visible(key, limA, loA, hiA)) ? s[nb][e] * sl2 : -INFINITY;
-        s[nb][2 + e] = (inb && visible(key, limB, loB, hiB)) ? s[nb][2 + e] * sl2 : -INFINITY;
-        tmA = fmaxf(tmA, s[nb][e]);
-        tmB = fmaxf(tmB, s[nb][2 + e]);
+        for (int e = 0; e < 2; ++e) {
+          s[nb][e] *= sl2;
+          s[nb][2 + e] *= sl2;
+          tmA = fmaxf(tmA, s[nb][e]);
+          tmB = fmaxf(tmB, s[nb][2 + e]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = k0 + nb * 8 + (lane & 3) * 2 + e;
+          const bool inb = key < kend;
+          s[nb][e] = (inb && visible(key, limA, loA, hiA)) ? s[nb][e] * sl2 : -INFINITY;
+          s[nb][2 + e] = (inb && visible(key, limB, loB, hiB)) ? s[nb][2 + e] * sl2 : -INFINITY;
+          tmA = fmaxf(tmA, s[nb][e]);
+          tmB = fmaxf(tmB, s[nb][2 + e]);
+        }
       }
     }
     tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 1));
@@ -247,7 +289,10 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
       }
     }
     __syncthreads();
+    k0 = k1;
+    buf ^= 1;
   }
+  cp_async_wait_all();
 
   // ---- write partial (or final) results
   const int RA = R0 + ra, RB = R0 + rb;
@@ -284,33 +329,48 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
   }
 }
 
-// Merge key chunks in index order: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.
+// Merge key chunks: O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c.  The
+// order of every sum is fixed by the chunk index (lane-strided, then a
+// butterfly), and chunks without visible keys contribute exact zeros, so the
+// result does not depend on how many (empty) chunks a launch had.
+constexpr int MAX_CHUNKS = 512;
 template <int D>
 __global__ void attn_combine_kernel(const AttnArgs a) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float wts[8][MAX_CHUNKS];
   const int T = a.B * a.q_len;
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int wl = threadIdx.x >> 5;
+  const int w = blockIdx.x * 8 + wl;
   const int lane = threadIdx.x & 31;
   if (w >= T * a.Hq) return;
   const int tok = w / a.Hq, qh = w % a.Hq;
   const int b = tok / a.q_len;
-  const int nc = min(a.n_chunks, (a.kv_end[b] + a.chunk - 1) / a.chunk);
+  const int nc = min(min(a.n_chunks, MAX_CHUNKS), (a.kv_end[b] + a.chunk - 1) / a.chunk);
   float M = -INFINITY;
-  for (int c = 0; c < nc; ++c) M = fmaxf(M, a.part_ml[((static_cast<size_t>(c) * T + tok) * a.Hq + qh) * 2]);
+  for (int c = lane; c < nc; c += 32)
+    M = fmaxf(M, a.part_ml[((static_cast<size_t>(c) * T + tok) * a.Hq + qh) * 2]);
+  M = warp_max(M);
+  float L = 0.f;
+  for (int c = lane; c < nc; c += 32) {
+    const size_t idx = (static_cast<size_t>(c) * T + tok) * a.Hq + qh;
+    const float mc = a.part_ml[idx * 2];
+    const float f = (mc == -INFINITY || M == -INFINITY) ? 0.f : exp2f(mc - M);
+    wts[wl][c] = f;
+    L += a.part_ml[idx * 2 + 1] * f;
+  }
+  L = warp_sum(L);
+  __syncwarp();
   constexpr int E = D / 32;
   float acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  float L = 0.f;
-  if (M != -INFINITY) {
-    for (int c = 0; c < nc; ++c) {
-      const size_t idx = (static_cast<size_t>(c) * T + tok) * a.Hq + qh;
-      const float mc = a.part_ml[idx * 2];
-      if (mc == -INFINITY) continue;
-      const float f = exp2f(mc - M);
-      L += a.part_ml[idx * 2 + 1] * f;
+#pragma unroll 4
+  for (int c = 0; c < nc; ++c) {
+    const float f = wts[wl][c];
+    const float* src = a.part_o + ((static_cast<size_t>(c) * T + tok) * a.Hq + qh) * D + lane * E;
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc[e] += a.part_o[idx * D + lane * E + e] * f;
-    }
+    for (int e = 0; e < E; ++e) acc[e] += src[e] * f;
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
@@ -321,7 +381,7 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 template <int D>
 static void launch_attn(const AttnArgs& a, cudaStream_t st) {
   constexpr int LD = D + 8;
-  const size_t smem = static_cast<size_t>(AT_ROWS + 2 * AT_KEYS) * LD * 2;
+  const size_t smem = static_cast<size_t>(AT_ROWS + 4 * AT_KEYS) * LD * 2;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -329,10 +389,10 @@ static void launch_attn(const AttnArgs& a, cudaStream_t st) {
   }
   const int g = a.Hq / a.Hkv;
   dim3 grid((a.q_len * g + AT_ROWS - 1) / AT_ROWS, a.B * a.Hkv, a.n_chunks);
-  attn_kernel<D><<<grid, 128, smem, st>>>(a);
+  launch_pdl(attn_kernel<D>, grid, dim3(128), smem, st, a);
   if (a.n_chunks > 1) {
     const int warps = a.B * a.q_len * a.Hq;
-    attn_combine_kernel<D><<<(warps * 32 + 255) / 256, 256, 0, st>>>(a);
+    launch_pdl(attn_combine_kernel<D>, dim3((warps + 7) / 8), dim3(256), 0, st, a);
   }
 }
 

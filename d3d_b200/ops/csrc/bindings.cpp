@@ -23,22 +23,34 @@ inline int* status_ptr(const c10::optional<Tensor>& s) { return s ? s->data_ptr<
 
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s bound on every in-kernel wait
 
-d3d::GemmArgs base_args(const Tensor& x, const Tensor& w, int bt, const c10::optional<Tensor>& status) {
+// ``wn`` > 0 marks ``w`` as packed (see d3d_b200.ops.pack_weight): a
+// [ceil(N/128) * ceil(K/64) * 128, 64] tensor of contiguous 16 KB tiles for a
+// logical [wn, K] weight.
+d3d::GemmArgs base_args(const Tensor& x, const Tensor& w, int bt, const c10::optional<Tensor>& status,
+                        int64_t wn) {
   CHECK_CUDA(x);
   CHECK_CUDA(w);
   CHECK_DT(x, torch::kBFloat16);
   CHECK_DT(w, torch::kBFloat16);
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2, "gemm: x [M,K], w [N,K]");
-  TORCH_CHECK(x.size(1) == w.size(1), "gemm: K mismatch");
   TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "gemm: inner dim must be contiguous");
   d3d::GemmArgs a{};
   a.x = cbf(x);
   a.w = cbf(w);
   a.M = static_cast<int>(x.size(0));
-  a.N = static_cast<int>(w.size(0));
   a.K = static_cast<int>(x.size(1));
   a.ldx = static_cast<int>(x.stride(0));
-  a.ldw = static_cast<int>(w.stride(0));
+  if (wn > 0) {
+    const int64_t tiles = (wn + 127) / 128 * ((a.K + 63) / 64);
+    TORCH_CHECK(w.size(1) == 64 && w.size(0) == tiles * 128 && w.is_contiguous(), "gemm: bad packed weight");
+    a.N = static_cast<int>(wn);
+    a.ldw = 64;
+    a.w_packed = 1;
+  } else {
+    TORCH_CHECK(x.size(1) == w.size(1), "gemm: K mismatch");
+    a.N = static_cast<int>(w.size(0));
+    a.ldw = static_cast<int>(w.stride(0));
+  }
   a.bt = bt;
   a.splits = 1;
   a.topk = 1;
@@ -47,9 +59,10 @@ d3d::GemmArgs base_args(const Tensor& x, const Tensor& w, int bt, const c10::opt
   return a;
 }
 
-void gemm_partial(Tensor x, Tensor w, Tensor out, int64_t splits, int64_t bt, c10::optional<Tensor> status) {
+void gemm_partial(Tensor x, Tensor w, Tensor out, int64_t splits, int64_t bt, c10::optional<Tensor> status,
+                  int64_t wn) {
   const c10::cuda::CUDAGuard g(x.device());
-  auto a = base_args(x, w, static_cast<int>(bt), status);
+  auto a = base_args(x, w, static_cast<int>(bt), status, wn);
   CHECK_DT(out, torch::kFloat32);
   CHECK_CONTIG(out);
   TORCH_CHECK(out.numel() >= splits * a.M * a.N, "gemm_partial: out too small");
@@ -61,9 +74,9 @@ void gemm_partial(Tensor x, Tensor w, Tensor out, int64_t splits, int64_t bt, c1
 }
 
 void gemm_bf16(Tensor x, Tensor w, Tensor out, c10::optional<Tensor> residual, int64_t bt,
-               c10::optional<Tensor> status) {
+               c10::optional<Tensor> status, int64_t wn) {
   const c10::cuda::CUDAGuard g(x.device());
-  auto a = base_args(x, w, static_cast<int>(bt), status);
+  auto a = base_args(x, w, static_cast<int>(bt), status, wn);
   CHECK_DT(out, torch::kBFloat16);
   TORCH_CHECK(out.size(0) == a.M && out.size(1) == a.N && out.stride(1) == 1, "gemm_bf16: out shape");
   a.mode = 1;
@@ -79,9 +92,10 @@ void gemm_bf16(Tensor x, Tensor w, Tensor out, c10::optional<Tensor> residual, i
   d3d::gemm_launch(a, cur_stream());
 }
 
-void gemm_topk(Tensor x, Tensor w, Tensor topv, Tensor topi, int64_t k, int64_t bt, c10::optional<Tensor> status) {
+void gemm_topk(Tensor x, Tensor w, Tensor topv, Tensor topi, int64_t k, int64_t bt, c10::optional<Tensor> status,
+               int64_t wn) {
   const c10::cuda::CUDAGuard g(x.device());
-  auto a = base_args(x, w, static_cast<int>(bt), status);
+  auto a = base_args(x, w, static_cast<int>(bt), status, wn);
   const int kt = k <= 1 ? 1 : (k <= 2 ? 2 : 4);
   const int ntiles = (a.N + 127) / 128;
   CHECK_DT(topv, torch::kFloat32);
@@ -189,6 +203,7 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
   CHECK_DT(rows, torch::kInt32);
   CHECK_DT(kv_end, torch::kInt32);
   TORCH_CHECK(chunk % 64 == 0, "attention chunk must be a multiple of 64");
+  TORCH_CHECK(chunk / page_size + 1 <= 1024, "attention chunk spans too many pages");
   TORCH_CHECK(n_chunks == 1 || (part_o && part_ml), "split attention needs partial buffers");
   d3d::AttnArgs a{};
   a.q = cbf(q);
@@ -217,9 +232,12 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "d3d_b200 sm_100a kernels";
-  m.def("gemm_partial", &gemm_partial);
-  m.def("gemm_bf16", &gemm_bf16);
-  m.def("gemm_topk", &gemm_topk);
+  m.def("gemm_partial", &gemm_partial, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("splits"),
+        py::arg("bt"), py::arg("status") = py::none(), py::arg("wn") = 0);
+  m.def("gemm_bf16", &gemm_bf16, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("residual") = py::none(),
+        py::arg("bt") = 16, py::arg("status") = py::none(), py::arg("wn") = 0);
+  m.def("gemm_topk", &gemm_topk, py::arg("x"), py::arg("w"), py::arg("topv"), py::arg("topi"), py::arg("k"),
+        py::arg("bt"), py::arg("status") = py::none(), py::arg("wn") = 0);
   m.def("add_rmsnorm", &add_rmsnorm);
   m.def("swiglu", &swiglu);
   m.def("qkv_rope_kv", &qkv_rope_kv);
@@ -228,4 +246,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("greedy_accept", &greedy_accept);
   m.def("attention", &attention);
   m.def("gemm_stages", &d3d::gemm_stages);
+  m.def("gemm_ctas_per_sm", &d3d::gemm_ctas_per_sm);
 }

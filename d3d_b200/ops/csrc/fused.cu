@@ -19,9 +19,18 @@
 namespace d3d {
 
 // ----------------------------------------------------------------- helpers
+// Sum of the split-K partials of one element, in split order.  The loads are
+// unrolled to a fixed maximum so they are all in flight at once (the sum order
+// stays fixed).
+constexpr int MAX_SPLITS = 16;
 __device__ __forceinline__ float load_split_sum(const float* p, int nsplit, size_t stride, size_t off) {
+  float v[MAX_SPLITS];
+#pragma unroll
+  for (int i = 0; i < MAX_SPLITS; ++i) v[i] = i < nsplit ? __ldg(p + i * stride + off) : 0.f;
   float s = 0.f;
-  for (int i = 0; i < nsplit; ++i) s += p[i * stride + off];
+#pragma unroll
+  for (int i = 0; i < MAX_SPLITS; ++i)
+    if (i < nsplit) s += v[i];
   return s;
 }
 
@@ -32,6 +41,8 @@ template <int VPT>
 __global__ void add_rmsnorm_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* __restrict__ residual,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int M, int N,
                                    float eps) {
+  griddep_launch();
+  griddep_wait();
   const int m = blockIdx.x;
   if (m >= M) return;
   __shared__ float red[32];
@@ -78,17 +89,19 @@ __global__ void add_rmsnorm_kernel(const float* __restrict__ part, int nsplit, _
 void add_rmsnorm(const float* part, int nsplit, __nv_bfloat16* residual, const __nv_bfloat16* w, __nv_bfloat16* out,
                  int M, int N, float eps, cudaStream_t st) {
   if (M == 0) return;
-  const int threads = N >= 4096 ? 512 : (N >= 1024 ? 256 : 128);
+  const int threads = N >= 4096 ? 1024 : (N >= 1024 ? 256 : 128);
   const int vpt = (N + threads - 1) / threads;
-  if (vpt <= 2) add_rmsnorm_kernel<2><<<M, threads, 0, st>>>(part, nsplit, residual, w, out, M, N, eps);
-  else if (vpt <= 4) add_rmsnorm_kernel<4><<<M, threads, 0, st>>>(part, nsplit, residual, w, out, M, N, eps);
-  else if (vpt <= 8) add_rmsnorm_kernel<8><<<M, threads, 0, st>>>(part, nsplit, residual, w, out, M, N, eps);
-  else add_rmsnorm_kernel<16><<<M, threads, 0, st>>>(part, nsplit, residual, w, out, M, N, eps);
+  if (vpt <= 2) launch_pdl(add_rmsnorm_kernel<2>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps);
+  else if (vpt <= 4) launch_pdl(add_rmsnorm_kernel<4>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps);
+  else if (vpt <= 8) launch_pdl(add_rmsnorm_kernel<8>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps);
+  else launch_pdl(add_rmsnorm_kernel<16>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps);
 }
 
 // ------------------------------------------------------------------ SwiGLU
 // P[s][m][0:I] = gate, P[s][m][I:2I] = up  ->  h[m][i] = bf16(bf16(silu(g)) * u)
 __global__ void swiglu_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* __restrict__ h, int M, int I) {
+  griddep_launch();
+  griddep_wait();
   const size_t total = static_cast<size_t>(M) * I;
   const size_t stride = static_cast<size_t>(M) * 2 * I;
   for (size_t t = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; t < total;
@@ -107,13 +120,15 @@ void swiglu(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, cudaS
   const size_t total = static_cast<size_t>(M) * I;
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  swiglu_kernel<<<blocks, 256, 0, st>>>(part, nsplit, h, M, I);
+  launch_pdl(swiglu_kernel, dim3(blocks), dim3(256), 0, st, part, nsplit, h, M, I);
 }
 
 // ------------------------------------------- QK-norm + RoPE + paged KV write
 // One warp per (token, head) for heads [0, Hq + 2*Hkv): q heads, k heads, v heads.
 template <int E>  // elements per lane = head_dim / 32
 __global__ void qkv_rope_kv_kernel(QkvRopeArgs a) {
+  griddep_launch();
+  griddep_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int H = a.Hq + 2 * a.Hkv;
@@ -176,9 +191,9 @@ void qkv_rope_kv(const QkvRopeArgs& a, cudaStream_t st) {
   const int warps = a.M * (a.Hq + 2 * a.Hkv);
   const int blocks = (warps * 32 + 255) / 256;
   switch (a.head_dim) {
-    case 32: qkv_rope_kv_kernel<1><<<blocks, 256, 0, st>>>(a); break;
-    case 64: qkv_rope_kv_kernel<2><<<blocks, 256, 0, st>>>(a); break;
-    case 128: qkv_rope_kv_kernel<4><<<blocks, 256, 0, st>>>(a); break;
+    case 32: launch_pdl(qkv_rope_kv_kernel<1>, dim3(blocks), dim3(256), 0, st, a); break;
+    case 64: launch_pdl(qkv_rope_kv_kernel<2>, dim3(blocks), dim3(256), 0, st, a); break;
+    case 128: launch_pdl(qkv_rope_kv_kernel<4>, dim3(blocks), dim3(256), 0, st, a); break;
     default: break;
   }
 }
@@ -188,6 +203,8 @@ void qkv_rope_kv(const QkvRopeArgs& a, cudaStream_t st) {
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              const __nv_bfloat16* __restrict__ cond, const unsigned char* __restrict__ cond_rows,
                              int q_len, __nv_bfloat16* __restrict__ out, int M, int H) {
+  griddep_launch();
+  griddep_wait();
   const int m = blockIdx.x;
   const int64_t id = ids[m];
   const bool add = cond != nullptr && cond_rows != nullptr && cond_rows[m];
@@ -210,7 +227,7 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
 void embed(const int64_t* ids, const __nv_bfloat16* table, const __nv_bfloat16* cond, const unsigned char* cond_rows,
            int q_len, __nv_bfloat16* out, int M, int H, cudaStream_t st) {
   if (M == 0) return;
-  embed_kernel<<<M, 128, 0, st>>>(ids, table, cond, cond_rows, q_len, out, M, H);
+  launch_pdl(embed_kernel, dim3(M), dim3(128), 0, st, ids, table, cond, cond_rows, q_len, out, M, H);
 }
 
 // ---------------------------------------------------------- top-k merge
@@ -218,6 +235,8 @@ void embed(const int64_t* ids, const __nv_bfloat16* table, const __nv_bfloat16* 
 template <int KT>
 __global__ void topk_merge_kernel(const float* __restrict__ tv, const int* __restrict__ ti, int ntiles, int k,
                                   float* __restrict__ ov, int64_t* __restrict__ oi, int M) {
+  griddep_launch();
+  griddep_wait();
   const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (m >= M) return;
@@ -282,9 +301,9 @@ void topk_merge(const float* tv, const int* ti, int ntiles, int kt, int k, float
                 cudaStream_t st) {
   if (M == 0) return;
   const int blocks = (M + 7) / 8;
-  if (kt == 1) topk_merge_kernel<1><<<blocks, 256, 0, st>>>(tv, ti, ntiles, k, ov, oi, M);
-  else if (kt == 2) topk_merge_kernel<2><<<blocks, 256, 0, st>>>(tv, ti, ntiles, k, ov, oi, M);
-  else topk_merge_kernel<4><<<blocks, 256, 0, st>>>(tv, ti, ntiles, k, ov, oi, M);
+  if (kt == 1) launch_pdl(topk_merge_kernel<1>, dim3(blocks), dim3(256), 0, st, tv, ti, ntiles, k, ov, oi, M);
+  else if (kt == 2) launch_pdl(topk_merge_kernel<2>, dim3(blocks), dim3(256), 0, st, tv, ti, ntiles, k, ov, oi, M);
+  else launch_pdl(topk_merge_kernel<4>, dim3(blocks), dim3(256), 0, st, tv, ti, ntiles, k, ov, oi, M);
 }
 
 // -------------------------------------------------------- greedy acceptance
@@ -295,6 +314,8 @@ __global__ void greedy_accept_kernel(const int64_t* __restrict__ blocks, const i
                                      int64_t* __restrict__ commit, int64_t* __restrict__ corr,
                                      const __nv_bfloat16* __restrict__ hidden, __nv_bfloat16* __restrict__ hid_out,
                                      int H) {
+  griddep_launch();
+  griddep_wait();
   const int b = blockIdx.x;
   __shared__ int s_commit;
   if (threadIdx.x == 0) {
@@ -314,7 +335,7 @@ __global__ void greedy_accept_kernel(const int64_t* __restrict__ blocks, const i
 void greedy_accept(const int64_t* blocks, const int64_t* post, int B, int K, int64_t* commit, int64_t* corr,
                    const __nv_bfloat16* hidden, __nv_bfloat16* hid_out, int H, cudaStream_t st) {
   if (B == 0) return;
-  greedy_accept_kernel<<<B, 128, 0, st>>>(blocks, post, K, commit, corr, hidden, hid_out, H);
+  launch_pdl(greedy_accept_kernel, dim3(B), dim3(128), 0, st, blocks, post, K, commit, corr, hidden, hid_out, H);
 }
 
 }  // namespace d3d

@@ -20,6 +20,7 @@ struct GemmParams {
   int ntiles;
   int bt;
   int stages;
+  int w_packed;
   int* status;
   unsigned long long timeout_ns;
 };
@@ -41,10 +42,12 @@ struct GemmArgs {
   int* topi;
   int* status;                 // device error word (may be null)
   unsigned long long timeout_ns;
+  int w_packed;                // w is in the packed tile layout (see pack_weight)
 };
 
 void gemm_launch(const GemmArgs& a, cudaStream_t stream);
 int gemm_stages(int bt);
+int gemm_ctas_per_sm(int bt);
 size_t gemm_smem_bytes(int bt, int stages);
 void make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                        uint32_t box_inner, uint32_t box_outer);

@@ -2,8 +2,10 @@
 //
 // Decode-time matmuls have few tokens (M = 1..1088) against large weights, so
 // the tile is laid out "swap-AB": the 128-row MMA M dimension runs over weight
-// rows (output features) and the MMA N dimension (``bt``, 16..256, a multiple
-// of 16) over tokens.  One CTA owns a 128 x bt output tile and a contiguous
+// rows (output features) and the MMA N dimension over tokens: ``bt`` = 16..256
+// (a multiple of 16) in one MMA, or up to 512 (a multiple of 32) as two MMAs
+// of bt/2 columns each, so one CTA can reuse its weight tile for 512 tokens
+// (TMEM holds 512 fp32 columns).  One CTA owns a 128 x bt output tile and a contiguous
 // range of K blocks (split-K chosen by the host from the weight shape alone,
 // so the fp32 reduction order of every output element is independent of M —
 // the property greedy token identity between AR and speculative decoding
@@ -22,7 +24,9 @@
 //                  MODE 2  per-tile top-KT (value, index) over the 128 rows,
 //                          for LM-head argmax / top-k without storing logits.
 // Every mbarrier wait is bounded; a timeout records an error code in
-// ``status`` and the kernel leaves its loop.
+// ``status`` and the kernel leaves its loop.  Launched with programmatic
+// dependent launch: the producer streams the first pipeline stages of weights
+// before griddepcontrol.wait, overlapping the previous kernel's tail.
 #include "common.cuh"
 #include "gemm.h"
 
@@ -38,7 +42,7 @@ constexpr int GBK = 64;   // K per stage (one 128-byte swizzle atom of bf16)
 constexpr int A_TILE_BYTES = GBN * GBK * 2;
 
 template <int MODE, int KT>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, 2)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -51,8 +55,6 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* accb = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
   int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] issued, [1] consumed, [2] failed
-  float* red_v = reinterpret_cast<float*>(flags + 4);  // MODE 2 scratch [4][16][KT]
-  int* red_i = reinterpret_cast<int*>(red_v + 4 * 16 * KT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * GBN, m0 = blockIdx.y * bt;
@@ -60,7 +62,9 @@ __global__ void __launch_bounds__(128, 1)
   const int split = blockIdx.z, nsplit = gridDim.z;
   const int kb0 = (nkb * split) / nsplit, kb1 = (nkb * (split + 1)) / nsplit;
   const int nk = kb1 - kb0;
-  const uint32_t tmem_cols = bt <= 32 ? 32 : (bt <= 64 ? 64 : (bt <= 128 ? 128 : 256));
+  const int nsub = bt > 256 ? 2 : 1;      // MMAs per K step
+  const int sub = bt / nsub;              // tokens per MMA (multiple of 16)
+  const uint32_t tmem_cols = bt <= 32 ? 32 : (bt <= 64 ? 64 : (bt <= 128 ? 128 : (bt <= 256 ? 256 : 512)));
   const uint64_t lim = p.timeout_ns;
 
   if (threadIdx.x == 0) {
@@ -73,6 +77,7 @@ __global__ void __launch_bounds__(128, 1)
     fence_mbar_init();
     prefetch_tensormap(&tmW);
     prefetch_tensormap(&tmX);
+    griddep_launch();
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, tmem_cols);
@@ -86,23 +91,43 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
     const uint64_t pol_w = policy_evict_first();  // weights stream through L2 once
-    int i = 0;
+    auto load_w = [&](int i, int s) {
+      uint8_t* sa = smem + s * stage_bytes;
+      if (p.w_packed)  // contiguous 16 KB tiles: [N/128][K/64][128][64]
+        tma_load_2d_hint(sa, &tmW, &full[s], 0, (blockIdx.x * nkb + kb0 + i) * GBN, pol_w);
+      else
+        tma_load_2d_hint(sa, &tmW, &full[s], (kb0 + i) * GBK, n0, pol_w);
+    };
+    auto load_x = [&](int i, int s) {
+      uint8_t* sb = smem + s * stage_bytes + A_TILE_BYTES;
+      for (int u = 0; u < nsub; ++u)
+        tma_load_2d(sb + u * sub * GBK * 2, &tmX, &full[s], (kb0 + i) * GBK, m0 + u * sub);
+    };
+    // weights do not depend on earlier kernels: fill the pipeline before the
+    // grid dependency resolves, then add the activation tiles
+    const int pre = nk < stages ? nk : stages;
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], stage_bytes);
+      load_w(i, i);
+    }
+    griddep_wait();
+    for (int i = 0; i < pre; ++i) load_x(i, i);
+    int i = pre;
     for (; i < nk; ++i) {
       const int s = i % stages;
       const uint32_t ph = (i / stages) & 1;
-      if (i >= stages && !mbar_wait(&empty[s], ph ^ 1, lim)) {
+      if (!mbar_wait(&empty[s], ph ^ 1, lim)) {
         set_error(p.status, ERR_TIMEOUT_PRODUCER);
         break;
       }
-      uint8_t* sa = smem + s * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
-      tma_load_2d_hint(sa, &tmW, &full[s], (kb0 + i) * GBK, n0, pol_w);
-      tma_load_2d(sa + A_TILE_BYTES, &tmX, &full[s], (kb0 + i) * GBK, m0);
+      load_w(i, s);
+      load_x(i, s);
     }
     flags[0] = i;
   } else if (warp == 1 && lane == 0) {
     // ----------------------------------------------------------- MMA issuer
-    const uint32_t idesc = idesc_bf16_f32(GBN, bt);
+    const uint32_t idesc = idesc_bf16_f32(GBN, sub);
     int i = 0;
     for (; i < nk; ++i) {
       const int s = i % stages;
@@ -120,6 +145,10 @@ __global__ void __launch_bounds__(128, 1)
       for (int kk = 0; kk < GBK / 16; ++kk) {
         // +32 bytes along K inside the swizzle atom = +2 in the >>4 address field
         umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+        if (nsub == 2) {
+          const uint64_t bd2 = sdesc_kmajor_sw128(sa + A_TILE_BYTES + sub * GBK * 2);
+          umma_bf16(tmem + sub, ad + 2 * kk, bd2 + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
+        }
       }
       umma_commit(&empty[s]);
     }
@@ -127,6 +156,7 @@ __global__ void __launch_bounds__(128, 1)
     umma_commit(accb);
   }
   __syncwarp();
+  griddep_wait();  // outputs may still be read by the previous kernel until it completes
 
   // -------------------------------------------------------------- epilogue
   bool ok = mbar_wait(accb, 0, lim);
@@ -169,65 +199,66 @@ __global__ void __launch_bounds__(128, 1)
       }
     } else {
       // ------------------------------------------- MODE 2: per-tile top-KT
-#pragma unroll 1
-      for (int j = 0; j < 16; ++j) {
-        float mine = n_ok ? v[j] : -INFINITY;
+      // The pipeline stages are idle once the accumulator is complete, so
+      // stage 0 holds the transposed 16-token x 128-row chunk; 8 threads per
+      // token scan 16 rows each and merge their sorted heads by shuffles.
+      float* tile = reinterpret_cast<float*>(smem);
 #pragma unroll
-        for (int r = 0; r < KT; ++r) {
-          float bv = mine;
-          int bi = n_ok ? n : 0x7fffffff;
+      for (int j = 0; j < 16; ++j) tile[j * GBN + row] = n_ok ? v[j] : -INFINITY;
+      __syncthreads();
+      const int j = threadIdx.x >> 3, q = threadIdx.x & 7;
+      float bv[KT];
+      int bi[KT];
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-              bv = ov;
-              bi = oi;
-            }
+      for (int r = 0; r < KT; ++r) {
+        bv[r] = -INFINITY;
+        bi[r] = 0x7fffffff;
+      }
+#pragma unroll 4
+      for (int rr = 0; rr < 16; ++rr) {
+        const int rw = q * 16 + rr;
+        float cv = tile[j * GBN + rw];
+        int ci = n0 + rw;
+        if (ci >= p.N) continue;
+#pragma unroll
+        for (int x = 0; x < KT; ++x) {
+          if (cv > bv[x] || (cv == bv[x] && ci < bi[x])) {
+            const float tv = bv[x];
+            const int ti = bi[x];
+            bv[x] = cv;
+            bi[x] = ci;
+            cv = tv;
+            ci = ti;
           }
-          if (lane == 0) {
-            red_v[(warp * 16 + j) * KT + r] = bv;
-            red_i[(warp * 16 + j) * KT + r] = bi;
-          }
-          if (bi == n) mine = -INFINITY;
         }
       }
-      __syncthreads();
-      if (threadIdx.x < 16) {
-        const int j = threadIdx.x;
-        const int m = m0 + c + j;
-        if (m < p.M) {
-          float bv[KT];
-          int bi[KT];
+      const int m = m0 + c + j;
+      const size_t o = (static_cast<size_t>(m) * p.ntiles + blockIdx.x) * KT;
 #pragma unroll
-          for (int r = 0; r < KT; ++r) {
-            bv[r] = -INFINITY;
-            bi[r] = 0x7fffffff;
-          }
-          for (int w = 0; w < 4; ++w) {
-            for (int r = 0; r < KT; ++r) {
-              float cv = red_v[(w * 16 + j) * KT + r];
-              int ci = red_i[(w * 16 + j) * KT + r];
-              // insertion into the sorted list (desc value, asc index)
+      for (int r = 0; r < KT; ++r) {
+        float best = bv[0];
+        int besti = bi[0];
 #pragma unroll
-              for (int q = 0; q < KT; ++q) {
-                if (cv > bv[q] || (cv == bv[q] && ci < bi[q])) {
-                  const float tv = bv[q];
-                  const int ti = bi[q];
-                  bv[q] = cv;
-                  bi[q] = ci;
-                  cv = tv;
-                  ci = ti;
-                }
-              }
-            }
+        for (int off = 4; off > 0; off >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+          const int oi = __shfl_xor_sync(0xffffffffu, besti, off);
+          if (ov > best || (ov == best && oi < besti)) {
+            best = ov;
+            besti = oi;
           }
-          const size_t o = (static_cast<size_t>(m) * p.ntiles + blockIdx.x) * KT;
+        }
+        if (q == 0 && m < p.M) {
+          p.topv[o + r] = best;
+          p.topi[o + r] = besti;
+        }
+        if (bi[0] == besti && bv[0] == best) {  // pop the winning head
 #pragma unroll
-          for (int r = 0; r < KT; ++r) {
-            p.topv[o + r] = bv[r];
-            p.topi[o + r] = bi[r];
+          for (int x = 0; x + 1 < KT; ++x) {
+            bv[x] = bv[x + 1];
+            bi[x] = bi[x + 1];
           }
+          bv[KT - 1] = -INFINITY;
+          bi[KT - 1] = 0x7fffffff;
         }
       }
       __syncthreads();
@@ -276,15 +307,32 @@ void make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
 }
 
+// Pipeline depth.  Measured on B200: two co-resident CTAs per SM (~110 KB of
+// shared memory each) stream weights at 85-92% of HBM bandwidth where one CTA
+// with a 12-stage pipeline reaches ~50%, so small token tiles use the 110 KB
+// budget whenever it still holds >= 4 stages; large tiles (compute-heavy) use
+// one CTA with ~220 KB.  D3D_GEMM_SMEM_KB / D3D_GEMM_MAX_STAGES override.
 int gemm_stages(int bt) {
+  static const int env_kb = [] {
+    const char* e = std::getenv("D3D_GEMM_SMEM_KB");
+    return e ? std::atoi(e) : 0;
+  }();
+  static const int max_stages = [] {
+    const char* e = std::getenv("D3D_GEMM_MAX_STAGES");
+    return e ? std::atoi(e) : 16;
+  }();
   const int stage_bytes = A_TILE_BYTES + bt * GBK * 2;
-  int s = (200 * 1024) / stage_bytes;
-  return s > 8 ? 8 : (s < 2 ? 2 : s);
+  const int budget_kb = env_kb > 0 ? env_kb : ((110 * 1024) / stage_bytes >= 4 ? 110 : 220);
+  int s = (budget_kb * 1024) / stage_bytes;
+  if (s > max_stages) s = max_stages;
+  return s < 2 ? 2 : s;
 }
+
+int gemm_ctas_per_sm(int bt) { return gemm_smem_bytes(bt, gemm_stages(bt)) <= 114 * 1024 ? 2 : 1; }
 
 size_t gemm_smem_bytes(int bt, int stages) {
   const int stage_bytes = A_TILE_BYTES + bt * GBK * 2;
-  return 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * stages + 1) * 8 + 32 + 4 * 16 * 4 * 8;
+  return 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * stages + 1) * 8 + 32;
 }
 
 template <int MODE, int KT>
@@ -295,18 +343,25 @@ static void launch_mode(const CUtensorMap& tw, const CUtensorMap& tx, GemmParams
     cudaFuncSetAttribute(gemm_tn_kernel<MODE, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     attr_set = true;
   }
-  gemm_tn_kernel<MODE, KT><<<grid, 128, smem, st>>>(tw, tx, p);
+  launch_pdl(gemm_tn_kernel<MODE, KT>, grid, dim3(128), smem, st, tw, tx, p);
 }
 
 void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
-  if (a.bt < 16 || a.bt > 256 || a.bt % 16) throw std::runtime_error("gemm: bt must be a multiple of 16 in [16,256]");
+  if (a.bt < 16 || a.bt > 512 || a.bt % 16 || (a.bt > 256 && a.bt % 32))
+    throw std::runtime_error("gemm: bt must be a multiple of 16 in [16,256] or of 32 in (256,512]");
   if (a.K % 8) throw std::runtime_error("gemm: K must be a multiple of 8");
   const int nkb = (a.K + GBK - 1) / GBK;
-  if (a.splits < 1 || a.splits > nkb) throw std::runtime_error("gemm: splits must be in [1, K/64]");
+  if (a.splits < 1 || a.splits > nkb || a.splits > 16)
+    throw std::runtime_error("gemm: splits must be in [1, min(16, K/64)]");
   if (a.mode != 0 && a.splits != 1) throw std::runtime_error("gemm: split-K needs fp32 partial mode");
   CUtensorMap tw, tx;
-  make_tmap_bf16_2d(&tw, a.w, a.K, a.N, a.ldw, GBK, GBN);
-  make_tmap_bf16_2d(&tx, a.x, a.K, a.M, a.ldx, GBK, a.bt);
+  if (a.w_packed) {
+    const uint64_t rows = static_cast<uint64_t>((a.N + GBN - 1) / GBN) * nkb * GBN;
+    make_tmap_bf16_2d(&tw, a.w, GBK, rows, GBK, GBK, GBN);
+  } else {
+    make_tmap_bf16_2d(&tw, a.w, a.K, a.N, a.ldw, GBK, GBN);
+  }
+  make_tmap_bf16_2d(&tx, a.x, a.K, a.M, a.ldx, GBK, a.bt > 256 ? a.bt / 2 : a.bt);
   GemmParams p{};
   p.M = a.M;
   p.N = a.N;
@@ -319,6 +374,7 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   p.topv = a.topv;
   p.topi = a.topi;
   p.bt = a.bt;
+  p.w_packed = a.w_packed;
   p.stages = gemm_stages(a.bt);
   p.status = a.status;
   p.timeout_ns = a.timeout_ns;

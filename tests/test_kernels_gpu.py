@@ -21,7 +21,7 @@ def _bf(*shape, scale=1.0, seed=0):
 @pytest.mark.parametrize("m,n,k,splits,bt", [
     (1, 256, 512, 1, 16), (16, 4096, 4096, 3, 16), (100, 1024, 2048, 2, 112),
     (272, 6144, 2048, 1, 144), (16, 384, 128, 1, 16), (300, 640, 1024, 4, 160),
-    (1024, 2048, 1024, 1, 256)])
+    (1024, 2048, 1024, 1, 256), (272, 1024, 2048, 2, 288), (1000, 512, 1024, 1, 512)])
 def test_gemm_partial(E, m, n, k, splits, bt):
     from d3d_b200 import ops
     x = _bf(m, k, seed=1)
@@ -37,6 +37,24 @@ def test_gemm_partial(E, m, n, k, splits, bt):
     assert err < 2e-3 * max(1.0, ref.abs().max().item()), err
 
 
+@pytest.mark.parametrize("m,n,k,splits", [(1, 6144, 4096, 3), (16, 300, 200, 1), (272, 1024, 2048, 4)])
+def test_gemm_packed_weight(E, m, n, k, splits):
+    """The packed-tile weight layout gives bit-identical partials."""
+    from d3d_b200 import ops
+    x = _bf(m, k, seed=21)
+    w = _bf(n, k, scale=0.05, seed=22)
+    pw = ops.pack_weight(w)
+    assert torch.equal(pw.unpack(), w)
+    o1 = torch.empty(splits, m, n, device="cuda")
+    o2 = torch.empty(splits, m, n, device="cuda")
+    ops.gemm_partial(x, w, o1, splits)
+    ops.gemm_partial(x, pw, o2, splits)
+    assert torch.equal(o1, o2)
+    ov, oi = ops.gemm_topk(x, pw, 2)
+    rv, ri = torch.topk(ops.linear_ref(x, w), 2, dim=-1)
+    assert torch.allclose(ov, rv, atol=2e-3, rtol=1e-4)
+
+
 def test_gemm_bf16_residual(E):
     from d3d_b200 import ops
     x, w, r = _bf(40, 1024, seed=3), _bf(512, 1024, scale=0.05, seed=4), _bf(40, 512, seed=5)
@@ -46,20 +64,20 @@ def test_gemm_bf16_residual(E):
     assert (out.float() - ref).abs().max().item() < 0.05
 
 
-@pytest.mark.parametrize("k", [1, 2, 4])
-def test_gemm_topk(E, k):
+@pytest.mark.parametrize("k,m", [(1, 33), (2, 33), (4, 33), (2, 300)])
+def test_gemm_topk(E, k, m):
     from d3d_b200 import ops
-    x, w = _bf(33, 512, seed=6), _bf(151936 // 8, 512, scale=0.05, seed=7)
+    x, w = _bf(m, 512, seed=6), _bf(151936 // 8, 512, scale=0.05, seed=7)
     ov, oi = ops.gemm_topk(x, w, k)
     ref = ops.linear_ref(x, w)
     rv, ri = torch.topk(ref, k, dim=-1)
     assert torch.allclose(ov, rv, atol=2e-3, rtol=1e-4)
     # indices must agree wherever the reference has no near-tie
-    gaps = (rv[:, :-1] - rv[:, 1:]).abs() if k > 1 else torch.ones(33, 0, device="cuda")
+    gaps = (rv[:, :-1] - rv[:, 1:]).abs() if k > 1 else torch.ones(m, 0, device="cuda")
     if k == 1:
         assert (oi[:, 0] == ri[:, 0]).float().mean().item() > 0.97
     else:
-        clear = torch.cat([gaps > 1e-2, torch.ones(33, 1, dtype=torch.bool, device="cuda")], 1)
+        clear = torch.cat([gaps > 1e-2, torch.ones(m, 1, dtype=torch.bool, device="cuda")], 1)
         assert ((oi == ri) | ~clear).all()
 
 
@@ -171,7 +189,7 @@ def _attn_ref(q, kc, vc, bt, rows, L, B, Q, Hq, Hkv, D, page):
 
 @pytest.mark.parametrize("B,Q,Hq,Hkv,D,prefix,page,chunk", [
     (1, 16, 32, 8, 128, 700, 16, 256), (2, 16, 32, 8, 128, 300, 16, 4096),
-    (1, 1, 32, 8, 128, 1000, 16, 256), (3, 9, 4, 2, 32, 50, 16, 64)])
+    (1, 1, 32, 8, 128, 1000, 16, 256), (3, 9, 4, 2, 32, 50, 16, 64), (1, 16, 32, 8, 128, 1000, 16, 64)])
 def test_attention_causal(E, B, Q, Hq, Hkv, D, prefix, page, chunk):
     from d3d_b200.engine.layout import causal_rows
     q, kc, vc, bt, rows, kv_end, L = _attn_case(
@@ -211,20 +229,20 @@ def test_attention_batch_invariance(E):
     prefix, Q, D = 900, 16, 128
     q, kc, vc, bt, rows, kv_end, L = _attn_case(1, Q, 32, 8, D, prefix, 16,
                                                 lambda b: causal_rows(prefix, Q), 256)
-    nch = math.ceil(L / 256)
+    nch = math.ceil(L / 64)
     out = torch.empty_like(q)
     po = torch.empty(nch, Q, 32, D, device="cuda")
     pml = torch.empty(nch, Q, 32, 2, device="cuda")
     E.attention(q, kc, vc, bt, rows.view(-1, 3), kv_end, 1, Q, 32, 8, 16, 1 / math.sqrt(D),
-                256, nch, po, pml, out)
+                64, nch, po, pml, out)
     for t in (0, 7, 15):
         end = torch.tensor([prefix + t + 1], dtype=torch.int32, device="cuda")
         o1 = torch.empty(1, 32, D, dtype=torch.bfloat16, device="cuda")
-        nc1 = math.ceil((prefix + t + 1) / 256)
+        nc1 = math.ceil((prefix + t + 1) / 64)
         po1 = torch.empty(nch, 1, 32, D, device="cuda")
         pm1 = torch.empty(nch, 1, 32, 2, device="cuda")
         E.attention(q[t:t + 1].contiguous(), kc, vc, bt, rows[0, t:t + 1].contiguous(), end, 1, 1, 32, 8,
-                    16, 1 / math.sqrt(D), 256, nc1, po1, pm1, o1)
+                    16, 1 / math.sqrt(D), 64, nc1, po1, pm1, o1)
         assert torch.equal(o1[0], out[t])
 
 
