@@ -85,10 +85,13 @@ def bench_gemm(shapes, iters, peaks, rows):
         del ws
 
 
-def bench_lmhead(iters, peaks, rows):
+def bench_lmhead(iters, peaks, rows, only_m=None):
     from d3d_b200 import ops
     E = ops.ext()
-    for m, n, k, kk in ((1, 151936, 4096, 1), (16, 151936, 4096, 1), (272, 151936, 2048, 2)):
+    for m, n, k, kk in ((1, 151936, 4096, 1), (16, 151936, 4096, 1), (272, 151936, 2048, 2),
+                        (752, 151936, 2048, 4)):
+        if only_m is not None and m != only_m:
+            continue
         w = ops.pack_weight(torch.randn(n, k, device="cuda").to(torch.bfloat16) * 0.02)
         w2 = ops.pack_weight(torch.randn(n, k, device="cuda").to(torch.bfloat16) * 0.02)
         x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
@@ -183,6 +186,7 @@ def main():
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--json", default=None)
     ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--lm-m", type=int, default=None)
     a = ap.parse_args()
     peaks = load_peaks()
     rows = []
@@ -199,7 +203,7 @@ def main():
         shapes += [("square 8192", 8192, 8192, 8192)]
         bench_gemm(shapes, a.iters, peaks, rows)
     if "lmhead" in only:
-        bench_lmhead(a.iters, peaks, rows)
+        bench_lmhead(a.iters, peaks, rows, a.lm_m)
     if "attn" in only:
         bench_attn(a.iters, peaks, rows)
     if "forward" in only:

@@ -24,6 +24,7 @@ import torch
 from .. import ops
 from ..config import ModelConfig
 from ..utils import launches
+from ..utils.timing import NULL as _NULL_PROF
 from ..models.fast import FastRunner, FastWeights, PagedKV, StepBuffers
 from .backends import DraftBackend, SeqState, TargetBackend, VerifyResult
 from .layout import causal_rows, prefix_rows
@@ -95,6 +96,7 @@ class _FastModelBackend:
         self.stream = stream or torch.cuda.Stream(device=self.device)
         self.graphs = _GraphCache(self.runner, self.stream, use_graphs)
         self.pin = _Pinned()
+        self.prof = _NULL_PROF
         self.rows_of: Dict[int, int] = {}           # seq index -> block-table row
         self.free_rows: List[int] = list(range(max_seqs - 1, -1, -1))
         self.extra_slots = extra_slots
@@ -217,7 +219,9 @@ class FastTarget(_FastModelBackend, TargetBackend):
         if self.time_verify:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record(self.stream)
+        tok = self.prof.dev_begin(f"verify_B{B}_K{K}", self.stream)
         self.graphs.run(("verify", B, K), b, self._verify_fn(a))
+        self.prof.dev_end(tok)
         if ev1 is not None:
             ev1.record(self.stream)
             self.verify_events.append((ev0, ev1))
@@ -287,7 +291,9 @@ class FastDraft(_FastModelBackend, DraftBackend):
             with torch.cuda.stream(self.stream):
                 for i, s in enumerate(seqs):
                     b.cond[i].copy_(s.cond.to(self.device, torch.bfloat16), non_blocking=True)
+        tok = self.prof.dev_begin(f"draft_B{B}_Q{Q}", self.stream)
         self.graphs.run(("draft", B, Q, k, use_cond), b, lambda bb: self.runner.forward(bb, use_cond))
+        self.prof.dev_end(tok)
         h = self._hbufs(B, Q, k)
         with torch.cuda.stream(self.stream):
             h["top"].copy_(b.top_i, non_blocking=True)

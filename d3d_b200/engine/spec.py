@@ -25,6 +25,7 @@ from typing import Callable, Dict, Iterable, List, Optional, Sequence, Tuple
 
 import torch
 
+from ..utils.timing import StepProfiler
 from .backends import DraftBackend, SeqState, TargetBackend
 from .layout import BranchKey, branch_specs, full_rows, packed_layout
 from .sampling import is_greedy
@@ -77,6 +78,10 @@ class SpecDecoder:
         self.t, self.d, self.cfg = target, draft, cfg.validate()
         self.overlap = overlap
         self.stats: Dict[str, float] = {}
+        self.prof = StepProfiler(False)
+        for be in (target, draft):
+            if hasattr(be, "prof"):
+                be.prof = self.prof
 
     # ------------------------------------------------------------ helpers
     def _controlled(self, s: SeqState, block: torch.Tensor, top, anchor_pos: int):
@@ -222,12 +227,16 @@ class SpecDecoder:
             if not is_greedy(cfg.temperature):
                 qq = (torch.stack([s.q_ids[1:width] for s in running]),
                       torch.stack([s.q_probs[1:width] for s in running]))
-            self.t.submit_verify(running, block_t, qq)
-            predictions = self.predict(running) if width == k else {}
-            res = self.t.receive()
+            with self.prof.phase("submit_verify"):
+                self.t.submit_verify(running, block_t, qq)
+            with self.prof.phase("predict"):
+                predictions = self.predict(running) if width == k else {}
+            with self.prof.phase("receive"):
+                res = self.t.receive()
             steps += 1
             verify_tokens += width * len(running)
             remaining, recover = [], []
+            t_sel = time.perf_counter()
             for i, s in enumerate(running):
                 n = int(res.commit[i])
                 corr = int(res.correction[i])
@@ -272,9 +281,12 @@ class SpecDecoder:
                     s.hits += 1
                     s.source = "packed_full" if n == k else f"packed_outcome_{n}"
                 remaining.append(s)
+            if self.prof.enabled:
+                self.prof.host["select"] += time.perf_counter() - t_sel
             running = remaining
             miss_rounds += bool(recover)
-            self.recover(recover)
+            with self.prof.phase("recover"):
+                self.recover(recover)
             if on_step is not None:
                 on_step(steps)
         elapsed = time.perf_counter() - started

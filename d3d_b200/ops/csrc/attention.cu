@@ -58,14 +58,16 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 __device__ __forceinline__ bool visible(int k, int lim, int lo, int hi) { return k < lim || (k >= lo && k < hi); }
 
 template <int D>
-__global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(128, 4) attn_kernel(const AttnArgs a) {
+  // Row descriptors, kv_end and the block table are step inputs copied in
+  // before the forward starts, so they are read before the grid dependency
+  // resolves; q and the KV cache (written by earlier kernels) after it.
   griddep_launch();
-  griddep_wait();
   constexpr int LD = D + 8;  // padded smem row (bank-conflict-free ldmatrix)
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* Kb = Qs + AT_ROWS * LD;       // [2][AT_KEYS][LD]
-  __nv_bfloat16* Vb = Kb + 2 * AT_KEYS * LD;   // [2][AT_KEYS][LD]
+  __nv_bfloat16* Kb = Qs + AT_ROWS * LD;       // [AT_KEYS][LD]
+  __nv_bfloat16* Vb = Kb + AT_KEYS * LD;       // [AT_KEYS][LD]
   __shared__ int s_rows[AT_ROWS][3];
   __shared__ int s_range[3];
   __shared__ int s_pages[AT_MAX_PAGES];   // page ids of this CTA's key chunk
@@ -107,33 +109,38 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
       atomicMax(&s_range[2], s_rows[tid][2]);
     }
   }
-  // ---- Q tile
+  // page ids of this CTA's key chunk (clamped to the block-table row)
+  const int kbeg = chunk_id * a.chunk;
+  const int* bt = a.block_table + static_cast<size_t>(b) * a.bt_stride;
+  const int pg0 = kbeg / a.page_size;
+  const int npg_all = min((a.chunk + a.page_size - 1) / a.page_size + 1, a.bt_stride - pg0);
+  for (int i = tid; i < npg_all && i < AT_MAX_PAGES; i += 128) s_pages[i] = bt[pg0 + i];
+  __syncthreads();
+  const int max_lim = s_range[0], min_lo = s_range[1], max_hi = s_range[2];
+  griddep_wait();
+
+  // ---- Q tile (async, lands with the first K/V tile)
   for (int c = tid; c < AT_ROWS * (D / 8); c += 128) {
     const int r = c / (D / 8), dc = (c % (D / 8)) * 8;
     const int R = R0 + r;
     const int t = R / g;
-    uint4 v = make_uint4(0, 0, 0, 0);
     if (t < a.q_len) {
       const int qh = h * g + R % g;
-      v = *reinterpret_cast<const uint4*>(a.q + (static_cast<size_t>(b * a.q_len + t) * a.Hq + qh) * D + dc);
+      cp_async16(smem_u32(Qs + r * LD + dc), a.q + (static_cast<size_t>(b * a.q_len + t) * a.Hq + qh) * D + dc);
+    } else {
+      *reinterpret_cast<uint4*>(Qs + r * LD + dc) = make_uint4(0, 0, 0, 0);
     }
-    *reinterpret_cast<uint4*>(Qs + r * LD + dc) = v;
   }
-  __syncthreads();
-  const int max_lim = s_range[0], min_lo = s_range[1], max_hi = s_range[2];
 
   // per-thread rows of the mma fragments
   const int ra = warp * 16 + (lane >> 2), rb = ra + 8;
   const int limA = s_rows[ra][0], loA = s_rows[ra][1], hiA = s_rows[ra][2];
   const int limB = s_rows[rb][0], loB = s_rows[rb][1], hiB = s_rows[rb][2];
 
-  uint32_t qf[D / 16][4];
-#pragma unroll
-  for (int kk = 0; kk < D / 16; ++kk) {
-    const int row = warp * 16 + (lane & 15);
-    const int col = kk * 16 + (lane >> 4) * 8;
-    ldsm_x4(smem_u32(Qs + row * LD + col), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
-  }
+  // Q fragments are re-read from shared memory for every key tile (ldmatrix)
+  // instead of being pinned in registers: that keeps the kernel at <= 128
+  // registers, so four CTAs (16 warps) share an SM and hide mma latency.
+  const uint32_t q_base = smem_u32(Qs + (warp * 16 + (lane & 15)) * LD + (lane >> 4) * 8);
 
   float o[D / 8][4];
 #pragma unroll
@@ -141,15 +148,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
   float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
   const float sl2 = a.scale * 1.4426950408889634f;  // scale * log2(e)
 
-  const int kbeg = chunk_id * a.chunk;
   const int kend = min(kbeg + a.chunk, kv_end);
-  const int* bt = a.block_table + static_cast<size_t>(b) * a.bt_stride;
-  // page ids of the chunk, read once (the tile loads below would otherwise each
-  // wait on a dependent global load before issuing their copies)
-  const int pg0 = kbeg / a.page_size;
-  const int npg = kend > kbeg ? (kend - 1) / a.page_size - pg0 + 1 : 0;
-  for (int i = tid; i < npg && i < AT_MAX_PAGES; i += 128) s_pages[i] = bt[pg0 + i];
-  __syncthreads();
 
   auto needed = [&](int k0) { return k0 < max_lim || (k0 + AT_KEYS > min_lo && k0 < max_hi); };
   auto next_needed = [&](int k0) {
@@ -157,9 +156,9 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
     return k0;
   };
   // issue the async copy of one K/V tile into buffer `buf` (zeros beyond kv_end)
-  auto load_tile = [&](int k0, int buf) {
-    __nv_bfloat16* Ks = Kb + buf * AT_KEYS * LD;
-    __nv_bfloat16* Vs = Vb + buf * AT_KEYS * LD;
+  auto load_tile = [&](int k0) {
+    __nv_bfloat16* Ks = Kb;
+    __nv_bfloat16* Vs = Vb;
     for (int c = tid; c < AT_KEYS * (D / 8); c += 128) {
       const int kr = c / (D / 8), dc = (c % (D / 8)) * 8;
       const int s = k0 + kr;
@@ -175,18 +174,19 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
     }
   };
 
+  // One K/V tile buffer per CTA: latency is hidden by the other CTAs of the SM.
   int k0 = next_needed(kbeg);
-  int buf = 0;
-  if (k0 < kend) load_tile(k0, 0);
-  cp_async_commit();
-  while (k0 < kend) {
-    const int k1 = next_needed(k0 + AT_KEYS);
-    if (k1 < kend) load_tile(k1, buf ^ 1);  // prefetch the next tile while this one computes
+  if (k0 >= kend) {
     cp_async_commit();
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    cp_async_wait_all();
+  }
+  while (k0 < kend) {
+    load_tile(k0);
+    cp_async_commit();
+    cp_async_wait_all();
     __syncthreads();
-    const __nv_bfloat16* Ks = Kb + buf * AT_KEYS * LD;
-    const __nv_bfloat16* Vs = Vb + buf * AT_KEYS * LD;
+    const __nv_bfloat16* Ks = Kb;
+    const __nv_bfloat16* Vs = Vb;
 
     // ---- S = Q K^T (16 rows x 64 keys per warp)
     float s[8][4];
@@ -194,14 +194,16 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
     for (int nb = 0; nb < 8; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t qf[4];
+      ldsm_x4(q_base + kk * 32, qf[0], qf[1], qf[2], qf[3]);
 #pragma unroll
       for (int nb = 0; nb < 8; nb += 2) {
         const int key = nb * 8 + (lane & 7) + (lane >> 4) * 8;
         const int col = kk * 16 + ((lane >> 3) & 1) * 8;
         uint32_t b0, b1, b2, b3;
         ldsm_x4(smem_u32(Ks + key * LD + col), b0, b1, b2, b3);
-        mma16816(s[nb], qf[kk], b0, b1);
-        mma16816(s[nb + 1], qf[kk], b2, b3);
+        mma16816(s[nb], qf, b0, b1);
+        mma16816(s[nb + 1], qf, b2, b3);
       }
     }
     // ---- mask + online softmax (per-element masking only when some row of
@@ -289,10 +291,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
       }
     }
     __syncthreads();
-    k0 = k1;
-    buf ^= 1;
+    k0 = next_needed(k0 + AT_KEYS);
   }
-  cp_async_wait_all();
 
   // ---- write partial (or final) results
   const int RA = R0 + ra, RB = R0 + rb;
@@ -381,7 +381,7 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 template <int D>
 static void launch_attn(const AttnArgs& a, cudaStream_t st) {
   constexpr int LD = D + 8;
-  const size_t smem = static_cast<size_t>(AT_ROWS + 4 * AT_KEYS) * LD * 2;
+  const size_t smem = static_cast<size_t>(AT_ROWS + 2 * AT_KEYS) * LD * 2;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

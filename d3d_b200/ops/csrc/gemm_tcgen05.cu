@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(128, 2)
   const bool n_ok = n < p.N;
   const bool live = ok && nk > 0;
 
-  for (int c = 0; c < bt; c += 16) {
+  for (int c = 0; c < (MODE == 2 ? 0 : bt); c += 16) {
     float v[16];
     tmem_ld16(t_row + c, v);
     if (!live) {
@@ -197,68 +197,62 @@ __global__ void __launch_bounds__(128, 2)
           }
         }
       }
-    } else {
-      // ------------------------------------------- MODE 2: per-tile top-KT
-      // The pipeline stages are idle once the accumulator is complete, so
-      // stage 0 holds the transposed 16-token x 128-row chunk; 8 threads per
-      // token scan 16 rows each and merge their sorted heads by shuffles.
-      float* tile = reinterpret_cast<float*>(smem);
+    }
+  }
+  if constexpr (MODE == 2) {
+    // ------------------------------------------------- MODE 2: per-tile top-KT
+    // The accumulator is copied, transposed, into the idle pipeline stages
+    // ([column][129] floats: the padding keeps both the row-wise writes and
+    // the column-wise scans bank-conflict free); then every thread scans
+    // whole token columns on its own, so there is no cross-lane dependency
+    // chain.  Columns are processed in groups that fit the stage area.
+    float* tile = reinterpret_cast<float*>(smem);
+    constexpr int LDT = GBN + 1;
+    const int avail = stages * stage_bytes / (LDT * 4);
+    const int group = avail >= bt ? bt : (avail / 16) * 16;
+    for (int g0 = 0; g0 < bt; g0 += group) {
+      const int g1 = min(bt, g0 + group);
+      for (int c = g0; c < g1; c += 16) {
+        float v[16];
+        tmem_ld16(t_row + c, v);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) tile[j * GBN + row] = n_ok ? v[j] : -INFINITY;
+        for (int j = 0; j < 16; ++j) tile[(c - g0 + j) * LDT + row] = (live && n_ok) ? v[j] : -INFINITY;
+      }
       __syncthreads();
-      const int j = threadIdx.x >> 3, q = threadIdx.x & 7;
-      float bv[KT];
-      int bi[KT];
+      for (int j = g0 + threadIdx.x; j < g1; j += blockDim.x) {
+        const int m = m0 + j;
+        if (m >= p.M) continue;
+        const float* col = tile + (j - g0) * LDT;
+        float bv[KT];
+        int bi[KT];
 #pragma unroll
-      for (int r = 0; r < KT; ++r) {
-        bv[r] = -INFINITY;
-        bi[r] = 0x7fffffff;
-      }
-#pragma unroll 4
-      for (int rr = 0; rr < 16; ++rr) {
-        const int rw = q * 16 + rr;
-        float cv = tile[j * GBN + rw];
-        int ci = n0 + rw;
-        if (ci >= p.N) continue;
+        for (int r = 0; r < KT; ++r) {
+          bv[r] = -INFINITY;
+          bi[r] = 0x7fffffff;
+        }
+#pragma unroll 8
+        for (int rr = 0; rr < GBN; ++rr) {
+          float x = col[rr];
+          if (x > bv[KT - 1]) {   // strict: equal values keep the lower row
+            int xi = n0 + rr;
 #pragma unroll
-        for (int x = 0; x < KT; ++x) {
-          if (cv > bv[x] || (cv == bv[x] && ci < bi[x])) {
-            const float tv = bv[x];
-            const int ti = bi[x];
-            bv[x] = cv;
-            bi[x] = ci;
-            cv = tv;
-            ci = ti;
+            for (int q = 0; q < KT; ++q) {
+              if (x > bv[q]) {
+                const float t1 = bv[q];
+                const int t2 = bi[q];
+                bv[q] = x;
+                bi[q] = xi;
+                x = t1;
+                xi = t2;
+              }
+            }
           }
         }
-      }
-      const int m = m0 + c + j;
-      const size_t o = (static_cast<size_t>(m) * p.ntiles + blockIdx.x) * KT;
+        const size_t o = (static_cast<size_t>(m) * p.ntiles + blockIdx.x) * KT;
 #pragma unroll
-      for (int r = 0; r < KT; ++r) {
-        float best = bv[0];
-        int besti = bi[0];
-#pragma unroll
-        for (int off = 4; off > 0; off >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, best, off);
-          const int oi = __shfl_xor_sync(0xffffffffu, besti, off);
-          if (ov > best || (ov == best && oi < besti)) {
-            best = ov;
-            besti = oi;
-          }
-        }
-        if (q == 0 && m < p.M) {
-          p.topv[o + r] = best;
-          p.topi[o + r] = besti;
-        }
-        if (bi[0] == besti && bv[0] == best) {  // pop the winning head
-#pragma unroll
-          for (int x = 0; x + 1 < KT; ++x) {
-            bv[x] = bv[x + 1];
-            bi[x] = bi[x + 1];
-          }
-          bv[KT - 1] = -INFINITY;
-          bi[KT - 1] = 0x7fffffff;
+        for (int r = 0; r < KT; ++r) {
+          p.topv[o + r] = bv[r];
+          p.topi[o + r] = bi[r] < p.N ? bi[r] : 0x7fffffff;
         }
       }
       __syncthreads();
