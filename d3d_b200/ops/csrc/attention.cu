@@ -407,3 +407,93 @@ void attention(const AttnArgs& a, cudaStream_t st) {
 }
 
 }  // namespace d3d
+
+// ---------------------------------------------------------------------------
+// Allocation-free C entry point (declared and documented in
+// attention_noalloc.h; no counterpart in the reference).  It launches the same
+// two kernels as d3d::attention, with the split-KV partials placed in a
+// file-scope device array instead of caller- or allocator-provided memory.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+#include "attention_noalloc.h"
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_attn_scratch[D3D_ATTN_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_attn_scratch on the current device, looked up once per
+// device (host code only sees a host-side stand-in for the symbol).
+cudaError_t scratch_for_current_device(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+    const size_t smem128 = static_cast<size_t>(d3d::AT_ROWS + 2 * d3d::AT_KEYS) * (128 + 8) * 2;
+    const size_t smem64 = static_cast<size_t>(d3d::AT_ROWS + 2 * d3d::AT_KEYS) * (64 + 8) * 2;
+    const size_t smem32 = static_cast<size_t>(d3d::AT_ROWS + 2 * d3d::AT_KEYS) * (32 + 8) * 2;
+    if ((e = cudaFuncSetAttribute(d3d::attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem128))) != cudaSuccess)
+      return e;
+    if ((e = cudaFuncSetAttribute(d3d::attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem64))) != cudaSuccess)
+      return e;
+    if ((e = cudaFuncSetAttribute(d3d::attn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem32))) != cudaSuccess)
+      return e;
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int d3d_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
+                                     int bt_stride, const int* rows, const int* kv_end, int B, int q_len, int Hq,
+                                     int Hkv, int head_dim, int page_size, float scale, int chunk, int n_chunks,
+                                     void* out, cudaStream_t stream) {
+  if (!q || !k_cache || !v_cache || !block_table || !rows || !kv_end || !out) return D3D_NOALLOC_ERR_BAD_ARG;
+  if (B <= 0 || q_len <= 0 || Hkv <= 0 || Hq % Hkv != 0 || page_size <= 0 || bt_stride <= 0 || n_chunks < 1)
+    return D3D_NOALLOC_ERR_BAD_ARG;
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128) return D3D_NOALLOC_ERR_BAD_ARG;
+  if (chunk <= 0 || chunk % 64 != 0 || chunk / page_size + 1 > d3d::AT_MAX_PAGES) return D3D_NOALLOC_ERR_BAD_ARG;
+  const size_t T = static_cast<size_t>(B) * q_len;
+  const size_t part_o = n_chunks > 1 ? static_cast<size_t>(n_chunks) * T * Hq * head_dim : 0;
+  const size_t part_ml = n_chunks > 1 ? static_cast<size_t>(n_chunks) * T * Hq * 2 : 0;
+  if ((part_o + part_ml) * sizeof(float) > D3D_ATTN_NOALLOC_SCRATCH_BYTES) return D3D_NOALLOC_ERR_TOO_LARGE;
+  void* base = nullptr;
+  const cudaError_t e = scratch_for_current_device(&base);
+  if (e != cudaSuccess) return e == cudaErrorInvalidSymbol ? D3D_NOALLOC_ERR_SYMBOL : static_cast<int>(e);
+  d3d::AttnArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
+  a.block_table = block_table;
+  a.bt_stride = bt_stride;
+  a.rows = rows;
+  a.kv_end = kv_end;
+  a.B = B;
+  a.q_len = q_len;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.head_dim = head_dim;
+  a.page_size = page_size;
+  a.scale = scale;
+  a.chunk = chunk;
+  a.n_chunks = n_chunks;
+  a.part_o = n_chunks > 1 ? static_cast<float*>(base) : nullptr;
+  a.part_ml = n_chunks > 1 ? static_cast<float*>(base) + part_o : nullptr;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  d3d::attention(a, stream);
+  return static_cast<int>(cudaPeekAtLastError());
+}
