@@ -117,19 +117,21 @@ class _FastModelBackend:
         self.kv.release(s.index)
 
     def _fill(self, b: StepBuffers, seqs: List[SeqState], ids: np.ndarray, pos: np.ndarray,
-              rows: np.ndarray, kv_end: np.ndarray, tag: str) -> None:
+              rows: np.ndarray, kv_end: np.ndarray, tag: str, cond_rows=None) -> None:
+        """Write one forward's integer inputs into the pinned twin of ``b.inbuf``
+        and copy them to the device with a single transfer."""
         q = b.Q
-        slots = np.empty(b.T, dtype=np.int64)
         for i, s in enumerate(seqs):
-            slots[i * q:(i + 1) * q] = self.kv.slots(s.index, s.prefix, q)
-        seq_rows = np.array([self._row(s) for s in seqs], dtype=np.int64)
-        st = self.stream
-        _stage(self.pin, tag + "ids", ids.astype(np.int64), b.ids, st)
-        _stage(self.pin, tag + "pos", pos.astype(np.int64), b.pos, st)
-        _stage(self.pin, tag + "slots", slots, b.slots, st)
-        _stage(self.pin, tag + "rows", rows.astype(np.int32), b.rows, st)
-        _stage(self.pin, tag + "kvend", kv_end.astype(np.int32), b.kv_end, st)
-        _stage(self.pin, tag + "seqrows", seq_rows, b.seq_rows, st)
+            b.h_slots[i * q:(i + 1) * q] = self.kv.slots(s.index, s.prefix, q)
+        b.h_ids[:] = ids.reshape(-1)
+        b.h_pos[:] = pos.reshape(-1)
+        b.h_rows[:] = rows.reshape(-1, 3)
+        b.h_kv_end[:] = kv_end.reshape(-1)
+        b.h_seq_rows[:] = [self._row(s) for s in seqs]
+        if cond_rows is not None:
+            b.h_cond_rows[:] = cond_rows.reshape(-1)
+        with torch.cuda.stream(self.stream):
+            b.inbuf.copy_(b.inbuf_host, non_blocking=True)
 
     def _prefill_one(self, s: SeqState, rows: np.ndarray, topk: int, reserve: int):
         n = len(s.prompt)
@@ -284,10 +286,10 @@ class FastDraft(_FastModelBackend, DraftBackend):
         k = max(1, topk)
         b = self.runner.buffers(B, Q, k)
         kv_end = torch.maximum(rows[:, :, 0].amax(1), rows[:, :, 2].amax(1)).numpy()
-        self._fill(b, seqs, ids.numpy(), positions.numpy(), rows.numpy(), kv_end, f"d{B}_{Q}")
         use_cond = cond_rows is not None and self.w.cond_proj is not None and seqs[0].cond is not None
+        self._fill(b, seqs, ids.numpy(), positions.numpy(), rows.numpy(), kv_end, f"d{B}_{Q}",
+                   cond_rows.numpy().astype(np.uint8) if use_cond else None)
         if use_cond:
-            _stage(self.pin, f"d{B}_{Q}cr", cond_rows.numpy().astype(np.uint8), b.cond_rows, self.stream)
             with torch.cuda.stream(self.stream):
                 for i, s in enumerate(seqs):
                     b.cond[i].copy_(s.cond.to(self.device, torch.bfloat16), non_blocking=True)

@@ -24,6 +24,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import List, Optional, Sequence, Tuple
 
+import numpy as np
 import torch
 
 BranchKey = Tuple[int, Optional[int]]   # (commit length, anchor token or None for all-pass)
@@ -136,32 +137,46 @@ def branch_specs(pending_block: Sequence[int], top_tokens: Optional[Sequence[Seq
     return specs
 
 
-def packed_layout(pending_block: torch.Tensor, specs: Sequence[BranchKey], kv_len: int,
+def packed_layout(pending_block, specs: Sequence[BranchKey], kv_len: int,
                   seg: int, mask_id: int, mode: str) -> PackedLayout:
     """Build ids / RoPE positions / row descriptors of the packed forward.
 
     KV slots run contiguously from ``kv_len`` over all query rows (the
     reference stores the whole packed query and crops back to
     ``kv_len + pending_len`` afterwards); RoPE positions of branch j start at
-    ``kv_len + a_j``."""
-    dev = pending_block.device
-    p = int(pending_block.shape[0])
-    q = p + len(specs) * seg
-    ids = torch.full((q,), int(mask_id), dtype=torch.long, device=dev)
-    ids[:p] = pending_block
-    pos = torch.empty(q, dtype=torch.long, device=dev)
-    pos[:p] = torch.arange(kv_len, kv_len + p, device=dev)
-    rows = torch.empty(q, 3, dtype=torch.int32, device=dev)
-    rows[:p] = pending_rows(kv_len, p, mode, dev)
-    for j, (a, anchor) in enumerate(specs):
-        s = p + j * seg
-        if anchor is not None:
-            ids[s] = int(anchor)
-        pos[s:s + seg] = torch.arange(kv_len + a, kv_len + a + seg, device=dev)
-        rows[s:s + seg, 0] = kv_len + a
-        rows[s:s + seg, 1] = kv_len + s
-        rows[s:s + seg, 2] = kv_len + s + seg
-    return PackedLayout(ids, pos, rows, list(specs), p, seg, kv_len)
+    ``kv_len + a_j``.  Built with vectorised numpy (this runs on the host on
+    every decode step); the returned tensors share the numpy buffers."""
+    pend = np.asarray(pending_block.tolist() if isinstance(pending_block, torch.Tensor) else pending_block,
+                      dtype=np.int64)
+    p = int(pend.shape[0])
+    nb = len(specs)
+    q = p + nb * seg
+    ids = np.full(q, int(mask_id), dtype=np.int64)
+    ids[:p] = pend
+    pos = np.empty(q, dtype=np.int64)
+    pos[:p] = np.arange(kv_len, kv_len + p)
+    rows = np.zeros((q, 3), dtype=np.int32)
+    if mode == "causal":
+        rows[:p, 0] = np.arange(kv_len + 1, kv_len + p + 1)
+    elif mode == "block_causal":
+        rows[:p, 0] = kv_len + p
+    else:
+        raise ValueError(f"unsupported attention_mask_mode={mode!r}")
+    if nb:
+        acc = np.array([a for a, _ in specs], dtype=np.int64)
+        starts = p + np.arange(nb, dtype=np.int64) * seg
+        off = np.arange(seg, dtype=np.int64)
+        pos[p:] = (kv_len + acc[:, None] + off[None, :]).reshape(-1)
+        br = rows[p:].reshape(nb, seg, 3)
+        br[:, :, 0] = (kv_len + acc)[:, None]
+        br[:, :, 1] = (kv_len + starts)[:, None]
+        br[:, :, 2] = (kv_len + starts + seg)[:, None]
+        anchors = [(j, t) for j, (_, t) in enumerate(specs) if t is not None]
+        if anchors:
+            js = np.array([j for j, _ in anchors], dtype=np.int64)
+            ids[p + js * seg] = np.array([t for _, t in anchors], dtype=np.int64)
+    return PackedLayout(torch.from_numpy(ids), torch.from_numpy(pos), torch.from_numpy(rows),
+                        list(specs), p, seg, kv_len)
 
 
 def fused_commit_rows(kv_len: int, pending_len: int, block_len: int, mode: str,

@@ -70,6 +70,29 @@ class RequestOutput:
     latency_s: float
 
 
+class _Outcomes:
+    """The branches of one packed forward for one sequence, sliced on demand
+    (only the branch that matches the verification outcome is materialised)."""
+
+    def __init__(self, lay, out: Dict[str, torch.Tensor], i: int):
+        self.lay, self.out, self.i = lay, out, i
+        self.index = {key: j for j, key in enumerate(lay.keys)}
+
+    def get(self, key):
+        j = self.index.get(key)
+        if j is None:
+            return None
+        sl = self.lay.segment(j)
+        out, i = self.out, self.i
+        toks = out["tokens"] if "tokens" in out else out["greedy"]
+        blk = toks[i, sl].clone()
+        if key[1] is not None:
+            blk[0] = key[1]
+        top = out["top"][i, sl].clone() if "top" in out else None
+        qq = (out["q_ids"][i, sl], out["q_probs"][i, sl]) if "q_ids" in out else None
+        return blk, top, qq
+
+
 class SpecDecoder:
     """Drives a target backend and a draft backend through the async loop."""
 
@@ -130,11 +153,11 @@ class SpecDecoder:
                 s.source = "redraft"
 
     # ------------------------------------------------------ packed outcomes
-    def predict(self, seqs: List[SeqState]) -> Dict[int, Dict[BranchKey, tuple]]:
+    def predict(self, seqs: List[SeqState]) -> Dict[int, "_Outcomes"]:
         """One packed forward per micro-batch: commit the pending block into the
         draft KV and draft one continuation per (commit length, anchor)."""
         k, a = self.cfg.block_size, self.cfg.anchor_num
-        results: Dict[int, Dict[BranchKey, tuple]] = {}
+        results: Dict[int, _Outcomes] = {}
         for off in range(0, len(seqs), self.cfg.draft_microbatch):
             group = seqs[off:off + self.cfg.draft_microbatch]
             layouts = []
@@ -153,21 +176,9 @@ class SpecDecoder:
             out = self.d.forward(group, ids, pos, rows, store=True, topk=a + 1 if a else 0,
                                  cond_rows=self._cond_rows(len(group), q, seg_starts),
                                  sample=self._sample_cfg())
-            toks = out["tokens"] if "tokens" in out else out["greedy"]
             for i, (s, lay) in enumerate(zip(group, layouts)):
                 self.d.trim(s, s.prefix + k)
-                outcomes = {}
-                for j, key in enumerate(lay.keys):
-                    sl = lay.segment(j)
-                    blk = toks[i, sl].clone().cpu()
-                    if key[1] is not None:
-                        blk[0] = key[1]
-                    top = out["top"][i, sl].clone().cpu() if "top" in out else None
-                    qq = None
-                    if "q_ids" in out:
-                        qq = (out["q_ids"][i, sl].cpu(), out["q_probs"][i, sl].cpu())
-                    outcomes[key] = (blk, top, qq)
-                results[s.index] = outcomes
+                results[s.index] = _Outcomes(lay, out, i)
         return results
 
     # ------------------------------------------------------------ main loop
@@ -265,7 +276,8 @@ class SpecDecoder:
                     self._finish(s, outputs)
                     continue
                 key = (n, None if (n == k or cfg.anchor_num == 0) else corr)
-                sel = predictions.get(s.index, {}).get(key)
+                pr = predictions.get(s.index)
+                sel = pr.get(key) if pr is not None else None
                 self.d.trim(s, s.prefix)
                 if sel is None:
                     recover.append(s)

@@ -25,6 +25,7 @@ import math
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
 
+import numpy as np
 import torch
 
 from .. import ops
@@ -170,10 +171,12 @@ class PagedKV:
         for p in self.tables.pop(sid, []):
             self.free.append(p)
 
-    def slots(self, sid: int, start: int, n: int) -> List[int]:
-        t = self.tables[sid]
+    def slots(self, sid: int, start: int, n: int):
+        """Physical KV slots of logical positions start..start+n-1 (numpy int64)."""
+        t = np.asarray(self.tables[sid], dtype=np.int64)
         ps = self.page_size
-        return [t[(start + j) // ps] * ps + (start + j) % ps for j in range(n)]
+        lp = np.arange(start, start + n, dtype=np.int64)
+        return t[lp // ps] * ps + lp % ps
 
     @property
     def leaked(self) -> int:
@@ -192,16 +195,35 @@ class StepBuffers:
         self.B, self.Q, self.T, self.topk, self.n_chunks = B, Q, T, topk, n_chunks
         dev = device
         h, d = cfg.hidden_size, cfg.head_dim
-        self.ids = torch.zeros(T, dtype=torch.int64, device=dev)
-        self.pos = torch.zeros(T, dtype=torch.int64, device=dev)
-        self.slots = torch.zeros(T, dtype=torch.int64, device=dev)
-        self.rows = torch.zeros(T, 3, dtype=torch.int32, device=dev)
-        self.kv_end = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.seq_rows = torch.zeros(B, dtype=torch.int64, device=dev)   # block-table rows
+        # All integer step inputs live in one byte buffer (and a pinned host
+        # twin), so a forward needs a single host->device copy.
+        segs = [("ids", T, torch.int64), ("pos", T, torch.int64), ("slots", T, torch.int64),
+                ("seq_rows", B, torch.int64), ("rows", 3 * T, torch.int32), ("kv_end", B, torch.int32),
+                ("cond_rows", T, torch.uint8)]
+        offs, off = {}, 0
+        for name, n, dt in segs:
+            offs[name] = off
+            off += (n * torch.tensor([], dtype=dt).element_size() + 15) // 16 * 16
+        self.in_bytes = off
+        self.inbuf = torch.zeros(off, dtype=torch.uint8, device=dev)
+        self.inbuf_host = torch.zeros(off, dtype=torch.uint8, pin_memory=str(dev).startswith("cuda"))
+        views = {}
+        for name, n, dt in segs:
+            nb = n * torch.tensor([], dtype=dt).element_size()
+            views[name] = (self.inbuf[offs[name]:offs[name] + nb].view(dt),
+                           self.inbuf_host[offs[name]:offs[name] + nb].view(dt).numpy())
+        self.ids, self.h_ids = views["ids"]
+        self.pos, self.h_pos = views["pos"]
+        self.slots, self.h_slots = views["slots"]
+        self.seq_rows, self.h_seq_rows = views["seq_rows"]        # block-table rows
+        rows, self.h_rows = views["rows"]
+        self.rows = rows.view(T, 3)
+        self.h_rows = self.h_rows.reshape(T, 3)
+        self.kv_end, self.h_kv_end = views["kv_end"]
+        self.cond_rows, self.h_cond_rows = views["cond_rows"]
         self.bt_view = None    # [B, max_pages] gathered per step from the KV block table
         self.cond = torch.zeros(B, cfg.cond_hidden_size or 8, dtype=torch.bfloat16, device=dev)
         self.cond_h = torch.zeros(B, h, dtype=torch.bfloat16, device=dev)
-        self.cond_rows = torch.zeros(T, dtype=torch.uint8, device=dev)
         self.x = torch.zeros(T, h, dtype=torch.bfloat16, device=dev)       # residual stream
         self.xn = torch.zeros(T, h, dtype=torch.bfloat16, device=dev)      # normed
         self.q = torch.zeros(T, cfg.num_attention_heads, d, dtype=torch.bfloat16, device=dev)
