@@ -39,7 +39,7 @@ EOS = (151643, 151645)
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=6)
+    p.add_argument("--steps", type=int, default=4)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--max-new-tokens", type=int, default=512)
