@@ -1,0 +1,96 @@
+"""Single-request asynchronous speculative decoding
+(reference: ``single/eval_async_packed.py``, flags 1773-1812).
+
+    python -m d3d_b200.cli.single --verifier qwen3-8b --drafter d3d-1.7b \\
+        --block-size 16 --anchor-num 3 --max-new-tokens 512 --baseline \\
+        --output-json out/result.json --summary-json out/summary.json
+"""
+from __future__ import annotations
+
+import argparse
+import statistics
+import time
+
+from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
+from ..engine.spec import DecodeConfig
+from ..utils.io import write_json
+from ..utils.metrics import headline, source_stats, steps_from_output, summarize_acceptance
+from .common import add_data_args, add_model_args, build_engine, load_prompts
+
+
+def parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    add_model_args(p, "--verifier", "--drafter")
+    add_data_args(p)
+    p.add_argument("--max-new-tokens", type=int, default=512)
+    p.add_argument("--block-size", type=int, default=16)
+    p.add_argument("--anchor-num", type=int, default=3)
+    p.add_argument("--attention-mask-mode", choices=["causal", "block_causal"], default="causal")
+    p.add_argument("--packed-accepted-counts", default="all",
+                   help="'all' or a comma list of commit lengths to pre-draft")
+    p.add_argument("--temperature", type=float, default=0.0)
+    p.add_argument("--proposal-top-k", type=int, default=0)
+    p.add_argument("--proposal-top-p", type=float, default=1.0)
+    p.add_argument("--ignore-eos", action="store_true")
+    p.add_argument("--baseline", action="store_true", help="also run target-only AR decoding")
+    p.add_argument("--controlled-accept-mean", type=float, default=None,
+                   help="acceptance-controlled mode (needs --baseline's AR oracle)")
+    p.add_argument("--warmup-new-tokens", type=int, default=32)
+    p.add_argument("--output-json", default=None)
+    p.add_argument("--summary-json", default=None)
+    return p
+
+
+def main(argv=None):
+    a = parser().parse_args(argv)
+    counts = None if a.packed_accepted_counts == "all" else tuple(int(x) for x in a.packed_accepted_counts.split(","))
+    decode = DecodeConfig(block_size=a.block_size, anchor_num=a.anchor_num, attention_mask_mode=a.attention_mask_mode,
+                          max_new_tokens=a.max_new_tokens, temperature=a.temperature, top_k=a.proposal_top_k,
+                          top_p=a.proposal_top_p, ignore_eos=a.ignore_eos, packed_accepted_counts=counts)
+    prompts = load_prompts(a)
+    eng = build_engine(a, decode, max_seqs=2, max_context=max(len(p) for p in prompts) + a.max_new_tokens + 64)
+    ar = None
+    baseline_tps = None
+    if a.baseline or a.controlled_accept_mean is not None:
+        t0 = time.perf_counter()
+        ar = eng.generate_ar(prompts)
+        baseline_tps = ar["output_tokens"] / (time.perf_counter() - t0)
+    ctl = None
+    if a.controlled_accept_mean is not None:
+        rate = rate_for_mean_accept(a.controlled_accept_mean, a.block_size)
+        ctl = lambda i: ControlledAcceptance(prompts[i] + ar["outputs"][i], rate, 151936 if True else 0,
+                                             seed=a.seed, stream=i)
+    if a.warmup_new_tokens:
+        eng.generate(prompts[:1], max_new_tokens=a.warmup_new_tokens, controlled=ctl)
+    per = []
+    t0 = time.perf_counter()
+    for i, p in enumerate(prompts):
+        s0 = time.perf_counter()
+        r = eng.generate([p], max_new_tokens=a.max_new_tokens,
+                         controlled=(lambda j, i=i: ctl(i)) if ctl else None)
+        o = r["outputs"][0]
+        dt = time.perf_counter() - s0
+        steps = steps_from_output(o.accepts, a.block_size, o.tokens)
+        per.append({"index": i, "input_tokens": len(p), "output_tokens": len(o.tokens),
+                    "decode_tokens": max(len(o.tokens) - 1, 0), "decode_elapsed_s": dt,
+                    "tokens_per_s": max(len(o.tokens) - 1, 0) / dt if dt > 0 else 0.0,
+                    "tokens": o.tokens, "hits": o.hits, "recoveries": o.recoveries,
+                    "summary": summarize_acceptance(steps, a.block_size - 1),
+                    "sources": source_stats(o.sources, [a.block_size] * len(o.accepts), o.accepts),
+                    "matches_ar": (o.tokens == ar["outputs"][i]) if ar else None})
+    elapsed = time.perf_counter() - t0
+    dec = sum(x["decode_tokens"] for x in per)
+    dtime = sum(x["decode_elapsed_s"] for x in per)
+    tps = dec / dtime if dtime > 0 else 0.0
+    acc = statistics.fmean(s for x in per for s in [x["summary"]["avg_accept_length"]]) if per else 0.0
+    summary = {"headline": headline(tps, baseline_tps or 0.0, acc), "elapsed_s": elapsed,
+               "token_identical_to_ar": all(x["matches_ar"] for x in per) if ar else None,
+               "config": vars(a)}
+    write_json(a.output_json, {"summary": summary, "per_prompt": per})
+    write_json(a.summary_json, summary)
+    print(summary["headline"])
+    return summary
+
+
+if __name__ == "__main__":
+    main()
