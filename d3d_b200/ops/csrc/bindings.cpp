@@ -228,6 +228,52 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
   d3d::attention(a, cur_stream());
 }
 
+template <typename T>
+T* opt_ptr(const c10::optional<Tensor>& t) {
+  return t ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+void kl_ce_stats(c10::optional<Tensor> zt, Tensor zs, int64_t C, int64_t v0, c10::optional<Tensor> target,
+                 Tensor st) {
+  const c10::cuda::CUDAGuard g(zs.device());
+  CHECK_DT(zs, torch::kFloat32);
+  CHECK_DT(st, torch::kFloat32);
+  TORCH_CHECK(zs.stride(1) == 1, "logit chunk rows must be contiguous");
+  d3d::kl_ce_stats(opt_ptr<float>(zt), zs.data_ptr<float>(), static_cast<int>(zs.size(0)), static_cast<int>(C),
+                   static_cast<int>(zs.stride(0)), static_cast<int>(v0), opt_ptr<int64_t>(target),
+                   st.data_ptr<float>(), cur_stream());
+}
+
+void kl_ce_grad(c10::optional<Tensor> zt, Tensor zs, int64_t C, int64_t v0, c10::optional<Tensor> target,
+                Tensor lse_t, Tensor lse_s, c10::optional<Tensor> w_kl, c10::optional<Tensor> w_ce,
+                c10::optional<Tensor> dz, c10::optional<Tensor> dzT) {
+  const c10::cuda::CUDAGuard g(zs.device());
+  d3d::kl_ce_grad(opt_ptr<float>(zt), zs.data_ptr<float>(), static_cast<int>(zs.size(0)), static_cast<int>(C),
+                  static_cast<int>(zs.stride(0)), static_cast<int>(v0), opt_ptr<int64_t>(target),
+                  lse_t.data_ptr<float>(), lse_s.data_ptr<float>(), opt_ptr<float>(w_kl), opt_ptr<float>(w_ce),
+                  opt_ptr<__nv_bfloat16>(dz), dz ? static_cast<int>(dz->stride(0)) : 0,
+                  opt_ptr<__nv_bfloat16>(dzT), dzT ? static_cast<int>(dzT->stride(0)) : 0, cur_stream());
+}
+
+void adamw(Tensor p, Tensor grad, Tensor m, Tensor v, c10::optional<Tensor> out, double lr, double b1, double b2,
+           double eps, double wd, int64_t step, double grad_scale) {
+  const c10::cuda::CUDAGuard g(p.device());
+  CHECK_DT(p, torch::kFloat32);
+  CHECK_DT(grad, torch::kFloat32);
+  TORCH_CHECK(p.numel() == grad.numel() && p.numel() == m.numel() && p.numel() == v.numel(), "adamw: sizes");
+  TORCH_CHECK(!out || out->numel() == p.numel(), "adamw: out size");
+  d3d::adamw(p.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+             opt_ptr<__nv_bfloat16>(out), static_cast<size_t>(p.numel()), static_cast<float>(lr),
+             static_cast<float>(b1), static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd),
+             static_cast<int>(step), static_cast<float>(grad_scale), cur_stream());
+}
+
+void sumsq(Tensor x, Tensor out) {
+  const c10::cuda::CUDAGuard g(x.device());
+  CHECK_DT(x, torch::kFloat32);
+  d3d::sumsq(x.data_ptr<float>(), static_cast<size_t>(x.numel()), out.data_ptr<float>(), cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -246,5 +292,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("greedy_accept", &greedy_accept);
   m.def("attention", &attention);
   m.def("gemm_stages", &d3d::gemm_stages);
+  m.def("kl_ce_stats", &kl_ce_stats);
+  m.def("kl_ce_grad", &kl_ce_grad);
+  m.def("adamw", &adamw);
+  m.def("sumsq", &sumsq);
   m.def("gemm_ctas_per_sm", &d3d::gemm_ctas_per_sm);
 }

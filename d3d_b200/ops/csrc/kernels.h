@@ -54,4 +54,14 @@ struct AttnArgs {
 };
 void attention(const AttnArgs& a, cudaStream_t st);
 
+// ---- training kernels (train_kernels.cu)
+void kl_ce_stats(const float* zt, const float* zs, int N, int C, int ldz, int v0, const int64_t* target, float* st,
+                 cudaStream_t s);
+void kl_ce_grad(const float* zt, const float* zs, int N, int C, int ldz, int v0, const int64_t* target,
+                const float* lse_t, const float* lse_s, const float* w_kl, const float* w_ce, __nv_bfloat16* dz,
+                int ld_dz, __nv_bfloat16* dzT, int ld_dzT, cudaStream_t s);
+void adamw(float* p, const float* g, float* m, float* v, __nv_bfloat16* out, size_t n, float lr, float b1, float b2,
+           float eps, float wd, int step, float grad_scale, cudaStream_t s);
+void sumsq(const float* x, size_t n, float* out, cudaStream_t s);
+
 }  // namespace d3d

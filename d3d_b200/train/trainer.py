@@ -1,0 +1,209 @@
+"""Distillation of the block-diffusion drafter against a frozen target
+(reference: ``train/trainer.py``).
+
+One micro-step: pack anchor+MASK blocks (:mod:`.blocks`), prefill the clean
+sequence through the student without gradient, run the packed block forward
+against that KV, take the target's hidden states at the supervising
+positions, and minimise ``alpha_kl * KL(p_target || p_draft) + alpha_ce *
+CE(target greedy / response token)`` with position-decayed weights through
+the fused LM-head loss (:func:`.losses.lmhead_distill_loss`).  Gradients are
+reduce-scattered and applied by the sharded fused AdamW (:mod:`.optim`).
+
+Launch (one process per GPU):
+
+    python -m torch.distributed.run --nproc-per-node 8 -m d3d_b200.train \\
+        --draft-model d3d-1.7b --target-model qwen3-8b --data-path synthetic \\
+        --output-dir out/train --seq-len 2048 --batch-size 4 --lr 1e-4
+"""
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import random
+import time
+from pathlib import Path
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..checkpoint import expected_keys, write_state
+from .blocks import Example, build_packed_block_batch, synthetic_examples
+from .losses import decay_weights, lmhead_distill_loss, normalize_objective
+from .model_utils import clean_prefill, student_hidden, teacher_hidden
+from .optim import ShardedAdamW, cosine_lr
+
+
+def _init_dist(device_type: str):
+    if dist.is_initialized():
+        return dist.get_rank(), dist.get_world_size()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        backend = "nccl" if device_type == "cuda" else "gloo"
+        kw = {}
+        if backend == "nccl":
+            kw["device_id"] = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600), **kw)
+        return dist.get_rank(), dist.get_world_size()
+    return 0, 1
+
+
+def _all_sum(x: float, device) -> float:
+    if not dist.is_initialized():
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+def load_examples(path: str, n: int, seq_len: int, vocab: int, rng: random.Random,
+                  rank: int, world: int) -> List[Example]:
+    """``synthetic`` or a JSONL of ``{"prompt_ids": [...], "response_ids": [...]}``
+    (rank-strided rows, ``train/dataset.py:157-231``)."""
+    if path == "synthetic":
+        return synthetic_examples(n, seq_len, 0.25, vocab, rng)
+    rows = []
+    for i, line in enumerate(Path(path).read_text().splitlines()):
+        if line.strip() and i % world == rank:
+            d = json.loads(line)
+            rows.append(Example(d["prompt_ids"], d["response_ids"]))
+    return rows
+
+
+def _build(name: str, device, dtype, seed: int, layers: Optional[int] = None, mask_id: Optional[int] = None):
+    from ..cli.common import is_preset, model_config
+    from ..models.qwen3 import build_model
+    if is_preset(name):
+        return build_model(model_config(name, layers), seed=seed, dtype=dtype, device=device)
+    from ..checkpoint import load_model
+    return load_model(name, device=device, dtype=dtype, mask_token_id=mask_id)
+
+
+def save_checkpoint(model, opt: ShardedAdamW, out_dir: Path, step: int, cursor: int) -> None:
+    """HF-layout FP32 safetensors from the fp32 master shards (gathered),
+    plus this rank's optimizer shard and the trainer state, written atomically."""
+    rank = opt.rank
+    full = torch.empty(opt.padded, dtype=torch.float32, device=opt.master.device)
+    if opt.world > 1:
+        dist.all_gather_into_tensor(full, opt.master, group=opt.group)
+    else:
+        full[: opt.shard] = opt.master
+    ck = out_dir / f"step_{step:07d}"
+    tmp = out_dir / f".step_{step:07d}.tmp"
+    if rank == 0:
+        tmp.mkdir(parents=True, exist_ok=True)
+        state, off = {}, 0
+        names = [n for n, p in model.named_parameters() if p.requires_grad]
+        for n, p in zip(names, opt.params):
+            state[n] = full[off:off + p.numel()].view(p.shape).cpu().clone()
+            off += p.numel()
+        for n, p in model.named_parameters():
+            if n not in state:
+                state[n] = p.detach().float().cpu()
+        if model.cfg.tie_word_embeddings:
+            state.pop("lm_head.weight", None)
+        keep = set(expected_keys(model.cfg))
+        write_state({k: v for k, v in state.items() if k in keep}, tmp)
+        model.cfg.save(tmp)
+        (tmp / "trainer_state.json").write_text(json.dumps({"step": step, "data_cursor": cursor,
+                                                            "world": opt.world}))
+    if dist.is_initialized():
+        dist.barrier()
+    if rank == 0:
+        os.replace(tmp, ck)
+    if dist.is_initialized():
+        dist.barrier()
+    torch.save(opt.state_dict(), ck / f"optim_rank{rank:03d}.pt")
+
+
+def train(args) -> dict:
+    device = torch.device(args.device)
+    rank, world = _init_dist(device.type)
+    if device.type == "cuda":
+        device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(device)
+    torch.manual_seed(args.seed + rank)
+    rng = random.Random(args.seed * 1000 + rank)
+    cdt = torch.bfloat16 if (device.type == "cuda" and args.dtype == "bf16") else torch.float32
+    student = _build(args.draft_model, device, cdt, args.seed, args.draft_layers, args.mask_token_id)
+    student.train()
+    teacher = None
+    objective = normalize_objective(args.objective)
+    if args.target_model:
+        teacher = _build(args.target_model, device, cdt, args.seed + 1).eval()
+        for p in teacher.parameters():
+            p.requires_grad_(False)
+    if args.freeze_embeddings:
+        student.model.embed_tokens.weight.requires_grad_(False)
+    opt = ShardedAdamW(student.parameters(), lr=args.lr, weight_decay=args.weight_decay)
+    start = 0
+    if args.resume:
+        ck = Path(args.resume)
+        opt.load_state_dict(torch.load(ck / f"optim_rank{rank:03d}.pt"))
+        start = json.loads((ck / "trainer_state.json").read_text())["step"]
+    mask_id = int(student.cfg.mask_token_id)
+    vocab = min(student.cfg.vocab_size, 151643) - 2
+    examples = load_examples(args.data_path, args.batch_size * max(1, args.max_steps), args.seq_len, vocab,
+                             rng, rank, world)
+    out_dir = Path(args.output_dir)
+    if rank == 0:
+        out_dir.mkdir(parents=True, exist_ok=True)
+    a_kl = args.kl_weight if (teacher is not None and objective in ("forward_kl", "kl_ce")) else 0.0
+    a_ce = args.ce_weight if objective in ("ce", "kl_ce") else 0.0
+    log = []
+    cursor = start * args.batch_size
+    t_start = time.perf_counter()
+    for step in range(start, args.max_steps):
+        exs = [examples[(cursor + i) % len(examples)] for i in range(args.batch_size)]
+        cursor += args.batch_size
+        batch = build_packed_block_batch(exs, block_size=args.block_size, mask_token_id=mask_id,
+                                         max_anchors=args.parallel_anchors_per_example, rng=rng)
+        if device.type == "cuda":
+            torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        batch = batch.to(device)
+        cache = clean_prefill(student, batch)
+        hs = student_hidden(student, batch, cache)
+        act = batch.active
+        w = decay_weights(batch.offsets[act], args.loss_decay_gamma)
+        z = _all_sum(float(w.sum()), device)
+        w = w / max(z, 1e-6)
+        h_t = w_t = None
+        targets = batch.target_ids[act]
+        if teacher is not None:
+            th = teacher_hidden(teacher, batch)[act]
+            h_t, w_t = th, teacher.lm_weight
+            if args.ce_on_target_greedy:
+                targets = (teacher.logits(th).argmax(-1) if device.type != "cuda" else
+                           _greedy(th, w_t))
+        loss, kl, ce = lmhead_distill_loss(hs[act], student.lm_weight, h_t, w_t, targets,
+                                           (a_kl * w) if a_kl else None, (a_ce * w) if a_ce else None,
+                                           chunk=args.vocab_chunk)
+        loss.backward()
+        lr = cosine_lr(step, args.lr, args.warmup_steps, args.max_steps, args.min_lr_ratio)
+        gnorm = opt.step(args.grad_clip, lr)
+        opt.zero_grad()
+        if device.type == "cuda":
+            torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        rec = {"step": step + 1, "loss": _all_sum(float(loss.item()), device),
+               "kl": _all_sum(float((kl * w).sum().item()), device),
+               "ce": _all_sum(float((ce * w).sum().item()), device), "grad_norm": gnorm, "lr": lr,
+               "tokens": int(_all_sum(float(act.sum().item()), device)), "step_s": dt}
+        log.append(rec)
+        if rank == 0:
+            with open(out_dir / "training_metrics.jsonl", "a") as f:
+                f.write(json.dumps(rec) + "\n")
+            if args.log_every and (step + 1) % args.log_every == 0:
+                print(json.dumps(rec), flush=True)
+        if args.save_every and (step + 1) % args.save_every == 0:
+            save_checkpoint(student, opt, out_dir, step + 1, cursor)
+    if args.save_final:
+        save_checkpoint(student, opt, out_dir, args.max_steps, cursor)
+    return {"log": log, "elapsed_s": time.perf_counter() - t_start, "world": world}
+
+
+def _greedy(h, w) -> torch.Tensor:
+    from .. import ops
+    ov, oi = ops.gemm_topk(h.to(torch.bfloat16).contiguous(), w.contiguous(), 1)
+    return oi[:, 0]
