@@ -1,0 +1,88 @@
+"""Pruning on CPU: single-layer deletion scoring equals an explicit forward
+without the layer; the physical prune remaps tensors and records provenance
+(and refuses to overwrite); a recovery step runs; checkpoint choice ranks by
+accept length."""
+import json
+import random
+
+import pytest
+import torch
+
+from d3d_b200.checkpoint import load_model, save_model
+from d3d_b200.config import tiny_drafter
+from d3d_b200.models.qwen3 import build_model
+from d3d_b200.pruning.modeling import _inputs, evaluate_single_layer_removals, examples_from_sequences, \
+    hard_accept_length
+from d3d_b200.pruning.prune import prune_checkpoint
+from d3d_b200.pruning.recovery import make_student, recovery_step
+from d3d_b200.pruning.select_checkpoint import choose
+from d3d_b200.pruning.select_layer import select_layers
+from d3d_b200.train.blocks import synthetic_examples
+from d3d_b200.train.optim import ShardedAdamW
+
+
+def _model(layers=4):
+    return build_model(tiny_drafter(cond=False).replace(num_hidden_layers=layers), seed=3).eval()
+
+
+def _examples(k=8):
+    rng = random.Random(0)
+    seqs = [[rng.randrange(1000) for _ in range(50)] for _ in range(3)]
+    return examples_from_sequences(seqs, k, 2, rng)
+
+
+def test_removal_scores_match_explicit_skip():
+    m = _model()
+    ex = _examples()
+    full, cand = evaluate_single_layer_removals(m, ex, 8)
+    for j in range(4):
+        rs = []
+        for e in ex:
+            ids, pos, mask = _inputs(m, e, 8, "causal")
+            h = m(ids, pos, mask=mask, layer_skip=[j])
+            lg = m.logits(h[:, -8:])[0, 1:]
+            rs.append(hard_accept_length(lg.argmax(-1), torch.tensor(e.continuation)))
+        assert cand[j][0] == pytest.approx(sum(r[0] for r in rs) / len(rs))
+    assert 1.0 <= full[0] <= 8.0
+
+
+def test_prune_checkpoint_remaps_and_records(tmp_path):
+    m = _model()
+    save_model(m, tmp_path / "parent")
+    out = prune_checkpoint(tmp_path / "parent", tmp_path / "child", removed=1)
+    c = load_model(out)
+    assert c.cfg.num_hidden_layers == 3
+    sd_p, sd_c = m.state_dict(), c.state_dict()
+    for new, old in enumerate([0, 2, 3]):
+        a = sd_p[f"model.layers.{old}.mlp.down_proj.weight"]
+        assert torch.equal(sd_c[f"model.layers.{new}.mlp.down_proj.weight"], a)
+    prov = json.loads((out / "layer_prune.json").read_text())
+    assert prov["retained_original_layers"] == [0, 2, 3] and prov["removed_original_layer"] == 1
+    with pytest.raises(FileExistsError):
+        prune_checkpoint(tmp_path / "parent", tmp_path / "child", removed=0)
+    out2 = prune_checkpoint(out, tmp_path / "grandchild", removed=2)
+    assert json.loads((out2 / "layer_prune.json").read_text())["retained_original_layers"] == [0, 2]
+
+
+def test_progressive_select_and_recovery():
+    m = _model()
+    res = select_layers(m, _examples(), 8, drop=2)
+    assert len(res["retained_original_layers"]) == 2 and m.cfg.num_hidden_layers == 2
+    parent = _model()
+    for p in parent.parameters():
+        p.requires_grad_(False)
+    removed = res["history"][0]["removed_compact_layer"]
+    child = make_student(parent, removed)
+    opt = ShardedAdamW([p for p in child.parameters() if p.requires_grad], lr=1e-4)
+    rng = random.Random(1)
+    r = recovery_step(child, parent, removed, [i for i in range(4) if i != removed],
+                      synthetic_examples(2, 64, 0.25, 1000, rng), opt, block_size=8, anchors=4, rng=rng)
+    assert all(torch.isfinite(torch.tensor(v)) for v in r.values())
+
+
+def test_choose_checkpoint(tmp_path):
+    a, b = _model(), _model()
+    save_model(a, tmp_path / "step_10")
+    save_model(b, tmp_path / "step_20")
+    res = choose([str(tmp_path / "step_10"), str(tmp_path / "step_20")], _examples(), 8)
+    assert res["best"]["checkpoint"].endswith("step_10")   # tie -> earliest step
