@@ -1,1 +1,1 @@
-
+"""Adapters to other serving stacks (off the decode hot path)."""
