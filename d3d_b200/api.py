@@ -77,6 +77,32 @@ class D3DEngine:
                                     FastWeights.from_module(d, device), decode, device=device, **kw)
         return cls.from_modules(t, d, decode)
 
+    @classmethod
+    def from_remote_target(cls, draft_w, link, target_hidden_size: int,
+                           decode: Optional[DecodeConfig] = None, *, max_seqs: int = 16,
+                           max_context: int = 4096, draft_pages: Optional[int] = None,
+                           page_size: int = 16, device="cuda", use_graphs: bool = True) -> "D3DEngine":
+        """Drafter and coordinator on this GPU; the target is served by the
+        peer at the other end of ``link`` (:func:`open_pair_link`,
+        :func:`target_server`)."""
+        from .engine.disagg import P2PTarget
+        from .engine.fast import FastDraft
+        from .engine.layout import paged_draft_branch_tokens
+
+        decode = decode or DecodeConfig()
+        packed_q = paged_draft_branch_tokens(decode.block_size, max(decode.anchor_num, 1))
+        dp = draft_pages or max_seqs * (max_context + packed_q + page_size) // page_size + 8
+        d = FastDraft(draft_w, pages=dp, page_size=page_size, max_seqs=max_seqs,
+                      max_context=max_context, packed_q=packed_q, use_graphs=use_graphs, device=device)
+        t = P2PTarget(link, target_hidden_size, device,
+                      want_hidden=decode.use_cond and draft_w.cond_proj is not None)
+        return cls(t, d, decode)
+
+    def close(self) -> None:
+        """Stop a remote target's serving loop (no-op for local targets)."""
+        if hasattr(self.target, "close"):
+            self.target.close()
+
     # ------------------------------------------------------------- decoding
     def generate(self, prompts: Sequence[Sequence[int]], *, max_new_tokens: Optional[int] = None,
                  concurrency: int = 1, controlled: Optional[Callable[[int], object]] = None) -> dict:
@@ -93,3 +119,24 @@ class D3DEngine:
             prompts = prompts.tolist()
         return ar_generate(self.target, prompts, n, eos=self.decoder.cfg.eos,
                            ignore_eos=self.decoder.cfg.ignore_eos, concurrency=concurrency)
+
+
+def open_pair_link(peer: int, device, slot_bytes: Optional[int] = None, group=None):
+    """Collective over ``group``: map NVLink mailboxes between this rank and
+    ``peer`` (every rank of the group calls it, each with its own peer)."""
+    from .engine.disagg import DEFAULT_SLOT_BYTES
+    from .parallel.p2p import Link
+    return Link(peer, slot_bytes or DEFAULT_SLOT_BYTES, torch.device(device), group)
+
+
+def target_server(target_w, link, *, max_seqs: int = 16, max_context: int = 4096,
+                  target_pages: Optional[int] = None, page_size: int = 16, device="cuda",
+                  use_graphs: bool = True):
+    """The target side of a disaggregated pair: call ``.serve()`` on the result;
+    it returns when the drafter side calls :meth:`D3DEngine.close`."""
+    from .engine.disagg import P2PTargetServer
+    from .engine.fast import FastTarget
+    tp = target_pages or max_seqs * (max_context + 64 + page_size) // page_size + 8
+    t = FastTarget(target_w, pages=tp, page_size=page_size, max_seqs=max_seqs,
+                   max_context=max_context, use_graphs=use_graphs, device=device)
+    return P2PTargetServer(t, link)

@@ -150,22 +150,33 @@ def bench_attn(iters, peaks, rows):
                          GBps=round(byts / us / 1e3, 1)))
 
 
-def bench_forward(iters, peaks, rows, layers=36):
-    """One full target forward (verify M=16 and AR M=1), graph-replayed."""
+def bench_forward(iters, peaks, rows, layers=36, drafter=False):
+    """One full forward, graph-replayed: the target (verify M=16, AR M=1) or
+    the drafter's packed all-outcome forward (M=272, one anchor)."""
     from d3d_b200 import config as C
+    from d3d_b200.engine.layout import branch_specs, causal_rows, packed_layout
     from d3d_b200.models.fast import FastRunner, FastWeights, PagedKV
-    cfg = C.qwen3_8b().replace(num_hidden_layers=layers)
+    cfg = (C.d3d_1p7b() if drafter else C.qwen3_8b()).replace(num_hidden_layers=layers)
     w = FastWeights.random(cfg, seed=0)
     kv = PagedKV(cfg, num_pages=256, page_size=16, max_seqs=1, max_pages_per_seq=128)
-    kv.reserve(0, 0, 1100)
-    r = FastRunner(w, kv, max_context=1100)
-    for m in (1, 16):
-        b = r.buffers(1, m, 1)
-        b.pos.copy_(torch.arange(1000, 1000 + m))
+    kv.reserve(0, 0, 1900)
+    r = FastRunner(w, kv, max_context=1900, batch_invariant=not drafter)
+    shapes = (272,) if drafter else (1, 16)
+    for m in shapes:
+        b = r.buffers(1, m, 2 if drafter else 1)
+        if drafter:
+            blk = torch.randint(0, 1000, (16,))
+            lay = packed_layout(blk, branch_specs(blk.tolist(), torch.stack([blk, blk + 1], 1).tolist(), 1),
+                                1000, 16, 151669, "causal")
+            b.ids.copy_(lay.input_ids)
+            b.pos.copy_(lay.positions)
+            b.rows.copy_(lay.rows)
+            b.kv_end.fill_(1000 + m)
+        else:
+            b.pos.copy_(torch.arange(1000, 1000 + m))
+            b.rows.copy_(causal_rows(1000, m))
+            b.kv_end.fill_(1000 + m)
         b.slots.copy_(torch.arange(1000, 1000 + m))
-        from d3d_b200.engine.layout import causal_rows
-        b.rows.copy_(causal_rows(1000, m))
-        b.kv_end.fill_(1000 + m)
         st = torch.cuda.Stream()
         with torch.cuda.stream(st):
             r.forward(b)
@@ -175,7 +186,7 @@ def bench_forward(iters, peaks, rows, layers=36):
             n = r.forward(b)
         us = timeit(lambda i: g.replay(), iters, graph=False)
         byts = w.nbytes()
-        rows.append(dict(kernel="target forward (graph)", shape=f"Qwen3-8B M={m}", M=m, launches=n,
+        rows.append(dict(kernel="forward (graph)", shape=f"{'drafter' if drafter else 'Qwen3-8B'} M={m}", M=m, launches=n,
                          us=round(us, 1), GBps=round(byts / us / 1e3, 1),
                          hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3)))
 
@@ -187,6 +198,7 @@ def main():
     ap.add_argument("--json", default=None)
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--lm-m", type=int, default=None)
+    ap.add_argument("--drafter", action="store_true", help="forward: drafter packed M=272")
     a = ap.parse_args()
     peaks = load_peaks()
     rows = []
@@ -207,7 +219,8 @@ def main():
     if "attn" in only:
         bench_attn(a.iters, peaks, rows)
     if "forward" in only:
-        bench_forward(a.iters, peaks, rows, layers=a.layers)
+        bench_forward(a.iters, peaks, rows, layers=a.layers if not a.drafter else min(a.layers, 28),
+                      drafter=a.drafter)
     for r in rows:
         print(json.dumps(r))
     if a.json:

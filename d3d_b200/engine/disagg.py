@@ -1,0 +1,299 @@
+"""Disaggregated decode: the target on one GPU, the drafter on another.
+
+This is the reference's two-GPU arrangement (verifier process on its own
+device, drafter and coordinator in the main process,
+``single/eval_async_packed.py:56-346,796-1297``), built on the NVLink
+mailboxes of :mod:`d3d_b200.parallel.p2p` instead of a host Pipe:
+
+* the coordinator (:class:`~d3d_b200.engine.spec.SpecDecoder`) runs on the
+  drafter's rank with a :class:`P2PTarget` as its target backend;
+* :class:`P2PTargetServer` runs on the target's rank around a
+  :class:`~d3d_b200.engine.fast.FastTarget`.
+
+Every message is a run of int64 words in one mailbox slot, starting with an
+8-word header (the formats of :mod:`d3d_b200.serving.remote`):
+
+=========  ==========================================  ==========================================
+command    request (drafter -> target)                 reply (target -> drafter)
+=========  ==========================================  ==========================================
+PREFILL    [1, n, total] meta[n, 2] tokens[total]      [1, n, H] anchors[n] | hidden bf16 [n, H]
+VERIFY     [2, B, K] meta[B, 2] blocks[B, K]           [2, B, K, H] res[B, 2+K] | hidden bf16 [B, H]
+RELEASE    [3, seq id]                                 [3]
+CLOSE      [0]                                         (none)
+ERROR      --                                          [-1, nbytes] utf-8 traceback
+=========  ==========================================  ==========================================
+
+``meta`` rows are (sequence id, prefix length); ``res`` rows are (commit,
+correction, posterior[K]).  The bf16 hidden block starts at byte
+:func:`hidden_offset`.  The VERIFY reply is written by the ``accept_send``
+kernel straight from the verify graph's buffers into the drafter GPU's
+mailbox (acceptance, correction, hidden-state pick and the NVLink transfer in
+one launch); the drafter's ``handoff_wait`` kernel writes it into pinned host
+memory, so the coordinator reads it after one stream synchronize.
+"""
+from __future__ import annotations
+
+import traceback
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from .. import ops
+from .backends import SeqState, TargetBackend, VerifyResult
+
+CMD_CLOSE, CMD_PREFILL, CMD_VERIFY, CMD_RELEASE, CMD_ERROR = 0, 1, 2, 3, -1
+HDR = 8
+HEAD_WORDS = 512          # first 4 KB of a message; the rest is fetched on demand
+DEFAULT_SLOT_BYTES = 1 << 20
+
+
+def hidden_offset(n_words: int) -> int:
+    """Byte offset of the bf16 hidden block after ``n_words`` int64 words."""
+    return (8 * n_words + 255) // 256 * 256
+
+
+def _prefill_words(n: int) -> int:
+    return HDR + n
+
+
+def _verify_words(B: int, K: int) -> int:
+    return HDR + B * (2 + K)
+
+
+class P2PTargetServer:
+    """Serves a :class:`~d3d_b200.engine.fast.FastTarget` to the drafter rank
+    at the other end of ``link``."""
+
+    def __init__(self, backend, link, deadline_s: float = 600.0):
+        self.be = backend
+        self.link = link
+        self.deadline_s = deadline_s
+        self.seqs: Dict[int, SeqState] = {}
+        self.H = int(backend.hidden_size)
+        # fused path: the verify graph's accept kernel writes the reply into the
+        # drafter GPU's mailbox (a FastTarget on one end of an NVLink Link)
+        self.fused = bool(getattr(link, "supports_device_put", False)) and hasattr(backend, "runner")
+        pin = bool(getattr(link, "supports_device_put", False))
+        self.req = torch.empty(link.slot_bytes // 8, dtype=torch.int64, pin_memory=pin)
+        self.rep_host = torch.zeros(link.slot_bytes // 8, dtype=torch.int64, pin_memory=pin)
+        self.stream = getattr(backend, "stream", None)
+        self.served = 0
+
+    # ------------------------------------------------------------ replies
+    def _reply_host(self, n_words: int) -> None:
+        """Send the first ``n_words`` of ``rep_host`` (rounded to 16 bytes)."""
+        n = (n_words + 1) // 2 * 2
+        self.link.send(self.rep_host[:n], self.stream)
+        if self.stream is not None:
+            self.stream.synchronize()   # rep_host is reused by the next reply
+
+    def _send_error(self, exc: BaseException) -> None:
+        msg = ("".join(traceback.format_exception(exc))).encode()
+        cap = self.link.slot_bytes - 8 * HDR
+        msg = msg[:cap]
+        self.rep_host[:HDR] = 0
+        self.rep_host[0] = CMD_ERROR
+        self.rep_host[1] = len(msg)
+        body = self.rep_host[HDR:].view(torch.uint8)
+        body[: len(msg)] = torch.frombuffer(bytearray(msg), dtype=torch.uint8)
+        self._reply_host(HDR + (len(msg) + 7) // 8)
+
+    # ---------------------------------------------------------- commands
+    def _prefill(self, h) -> None:
+        n, total = int(h[1]), int(h[2])
+        meta = self.req[HDR:HDR + 2 * n].view(n, 2).tolist()
+        toks = self.req[HDR + 2 * n:HDR + 2 * n + total].tolist()
+        group, off = [], 0
+        for sid, ln in meta:
+            s = SeqState(index=sid, prompt=toks[off:off + ln], prefix=ln)
+            off += ln
+            self.seqs[sid] = s
+            group.append(s)
+        anchors, hidden = self.be.prefill(group)
+        words = _prefill_words(n)
+        ho = hidden_offset(words)
+        self.rep_host[:HDR] = 0
+        self.rep_host[0], self.rep_host[1], self.rep_host[2] = CMD_PREFILL, n, self.H
+        self.rep_host[HDR:HDR + n] = anchors.to(torch.int64).cpu()
+        hb = self.rep_host.view(torch.uint8)[ho:ho + 2 * n * self.H].view(torch.bfloat16)
+        hb.copy_(hidden.to(torch.bfloat16).reshape(-1).cpu())
+        self._reply_host((ho + 2 * n * self.H + 7) // 8)
+
+    def _verify(self, h) -> None:
+        B, K = int(h[1]), int(h[2])
+        meta = self.req[HDR:HDR + 2 * B].view(B, 2).tolist()
+        blocks = self.req[HDR + 2 * B:HDR + 2 * B + B * K].view(B, K).clone()
+        group = []
+        for sid, prefix in meta:
+            s = self.seqs[sid]
+            s.prefix = prefix
+            group.append(s)
+        if not self.fused:
+            r = self.be.verify(group, blocks)
+            words = _verify_words(B, K)
+            ho = hidden_offset(words)
+            self.rep_host[:HDR] = 0
+            self.rep_host[0], self.rep_host[1], self.rep_host[2], self.rep_host[3] = CMD_VERIFY, B, K, self.H
+            res = torch.cat([r.commit.view(B, 1).to(torch.int64).cpu(), r.correction.view(B, 1).to(torch.int64).cpu(),
+                             r.posterior.to(torch.int64).cpu().view(B, K)], 1)
+            self.rep_host[HDR:words] = res.reshape(-1)
+            hb = self.rep_host.view(torch.uint8)[ho:ho + 2 * B * self.H].view(torch.bfloat16)
+            if r.hidden is not None:
+                hb.copy_(r.hidden.to(torch.bfloat16).reshape(-1).cpu())
+            self._reply_host((ho + 2 * B * self.H + 7) // 8)
+            return
+        seq = self.link.send_seq + 1
+        self.link.send_seq = seq
+        out_ptr = self.link.outbox.slot_ptr(seq)
+        hid_ptr = out_ptr + hidden_offset(_verify_words(B, K))
+        flag_ptr = self.link.outbox.flag_ptr
+        E = ops.ext()
+
+        def sink(ids, post, xn):
+            E.accept_send(ids, post, xn, out_ptr, hid_ptr, flag_ptr, seq)
+
+        self.be.submit_verify(group, blocks, sink=sink)
+
+    def serve(self, poll=None) -> None:
+        """Answer requests until CLOSE.  ``poll()`` is called whenever a
+        bounded wait for the next request ran out (it may raise to stop)."""
+        while True:
+            self.link.recv(self.req[:HEAD_WORDS], self.stream, deadline_s=self.deadline_s, poll=poll)
+            h = self.req[:HDR].tolist()
+            cmd = h[0]
+            if cmd == CMD_PREFILL:
+                words = HDR + 2 * h[1] + h[2]
+                if words > HEAD_WORDS:
+                    self.link.fetch(self.req[HEAD_WORDS:words], 8 * HEAD_WORDS, self.stream)
+            if cmd == CMD_CLOSE:
+                return
+            try:
+                if cmd == CMD_VERIFY:
+                    self._verify(h)
+                elif cmd == CMD_PREFILL:
+                    self._prefill(h)
+                elif cmd == CMD_RELEASE:
+                    s = self.seqs.pop(int(h[1]), None)
+                    if s is not None:
+                        self.be.release(s)
+                    self.rep_host[:HDR] = 0
+                    self.rep_host[0] = CMD_RELEASE
+                    self._reply_host(HDR)
+                else:
+                    raise ValueError(f"unknown target command {cmd}")
+                self.served += 1
+            except Exception as exc:  # reported to the drafter; the server keeps serving
+                self._send_error(exc)
+
+
+class P2PTarget(TargetBackend):
+    """Drafter-side target backend whose target is served over ``link``."""
+
+    def __init__(self, link, hidden_size: int, device=None, deadline_s: float = 600.0,
+                 want_hidden: bool = True):
+        self.link = link
+        self.want_hidden = want_hidden
+        self.hidden_size = int(hidden_size)
+        gpu = bool(getattr(link, "supports_device_put", False))
+        self.device = torch.device(device) if device is not None else torch.device("cpu")
+        self.deadline_s = deadline_s
+        self.stream = torch.cuda.Stream(device=self.device, priority=-1) if gpu else None
+        words = link.slot_bytes // 8
+        self.req = torch.zeros(words, dtype=torch.int64, pin_memory=gpu)
+        self.rep = torch.zeros(words, dtype=torch.int64, pin_memory=gpu)
+        self._pending: Optional[tuple] = None
+        self.closed = False
+
+    def _send(self, n_words: int) -> None:
+        n = (n_words + 1) // 2 * 2
+        # the put kernel reads the pinned request directly
+        self.link.send(self.req[:n], self.stream)
+
+    def _recv(self, expect: int, head_words: int = HEAD_WORDS):
+        head_words = min(max(head_words, HDR), self.rep.numel())
+        head_words += head_words % 2
+        self.link.recv(self.rep[:head_words], self.stream, deadline_s=self.deadline_s)
+        cmd = int(self.rep[0])
+        if cmd == CMD_ERROR:
+            nb = int(self.rep[1])
+            if HDR + (nb + 7) // 8 > head_words:
+                self.link.fetch(self.rep[head_words:HDR + (nb + 7) // 8 + 1], 8 * head_words, self.stream)
+            msg = bytes(self.rep[HDR:].view(torch.uint8)[:nb].tolist()).decode(errors="replace")
+            raise RuntimeError("target service failed:\n" + msg)
+        if cmd != expect:
+            raise RuntimeError(f"target protocol error: expected {expect}, got {cmd}")
+        return self.rep
+
+    def _bf16_block(self, words: int, rows: int, have_words: int) -> torch.Tensor:
+        """The hidden block of the last reply, fetched if it was not in the head."""
+        ho = hidden_offset(words)
+        nb = 2 * rows * self.hidden_size
+        end = (ho + nb + 15) // 16 * 16
+        if end > 8 * have_words:
+            lo = 8 * have_words
+            self.link.fetch(self.rep.view(torch.uint8)[lo:end], lo, self.stream)
+        return self.rep.view(torch.uint8)[ho:ho + nb].view(torch.bfloat16).view(rows, self.hidden_size)
+
+    def prefill(self, seqs: List[SeqState]):
+        n = len(seqs)
+        toks = [t for s in seqs for t in s.prompt]
+        need = HDR + 2 * n + len(toks)
+        if 8 * need > self.link.slot_bytes:
+            raise ValueError("prompts exceed the mailbox slot; raise slot_bytes")
+        self.req[:HDR] = 0
+        self.req[0], self.req[1], self.req[2] = CMD_PREFILL, n, len(toks)
+        self.req[HDR:HDR + 2 * n] = torch.tensor([[s.index, len(s.prompt)] for s in seqs]).view(-1)
+        self.req[HDR + 2 * n:need] = torch.tensor(toks, dtype=torch.int64)
+        self._send(need)
+        r = self._recv(CMD_PREFILL)
+        anchors = r[HDR:HDR + n].clone()
+        hid = self._bf16_block(_prefill_words(n), n, HEAD_WORDS).clone()
+        return anchors, hid
+
+    def submit_verify(self, seqs, blocks, q=None):
+        if q is not None:
+            raise NotImplementedError("the disaggregated target verifies greedily (temperature 0)")
+        if self._pending is not None:
+            raise RuntimeError("target already has an outstanding verify")
+        B, K = blocks.shape
+        need = HDR + 2 * B + B * K
+        self.req[:HDR] = 0
+        self.req[0], self.req[1], self.req[2] = CMD_VERIFY, B, K
+        meta = np.array([[s.index, s.prefix] for s in seqs], dtype=np.int64).reshape(-1)
+        rn = self.req.numpy()
+        rn[HDR:HDR + 2 * B] = meta
+        rn[HDR + 2 * B:need] = blocks.numpy().reshape(-1)
+        self._send(need)
+        self._pending = (B, K)
+
+    def receive(self) -> VerifyResult:
+        if self._pending is None:
+            raise RuntimeError("no outstanding target request")
+        B, K = self._pending
+        self._pending = None
+        words = _verify_words(B, K)
+        r = self._recv(CMD_VERIFY, words)
+        res = r[HDR:words].view(B, 2 + K).clone()
+        hid = self._bf16_block(words, B, words + words % 2).clone() if self.want_hidden else None
+        return VerifyResult(res[:, 0], res[:, 1], res[:, 2:], hid)
+
+    def verify(self, seqs, blocks, q=None):
+        self.submit_verify(seqs, blocks, q)
+        return self.receive()
+
+    def release(self, seq: SeqState) -> None:
+        self.req[:HDR] = 0
+        self.req[0], self.req[1] = CMD_RELEASE, seq.index
+        self._send(HDR)
+        self._recv(CMD_RELEASE, HDR)
+
+    def close(self) -> None:
+        """Ends the server's current ``serve()`` call (it may be called again)."""
+        if True:
+            self.closed = True
+            self.req[:HDR] = 0
+            self.req[0] = CMD_CLOSE
+            self._send(HDR)
+            if self.stream is not None:
+                self.stream.synchronize()

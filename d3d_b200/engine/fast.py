@@ -207,7 +207,11 @@ class FastTarget(_FastModelBackend, TargetBackend):
         return fn
 
     @torch.inference_mode()
-    def submit_verify(self, seqs, blocks, q=None):
+    def submit_verify(self, seqs, blocks, q=None, sink=None):
+        """Enqueue one verify of ``blocks`` [B, K].  With ``sink`` given, it is
+        called on the target stream right after the verify graph as
+        ``sink(ids [B, K], posterior [B, K], hidden [B*K, H])`` (device views
+        of the graph's buffers) and nothing is copied back to this host."""
         if q is not None:
             raise NotImplementedError("the fast target path verifies greedily (temperature 0)")
         B, K = blocks.shape
@@ -224,9 +228,15 @@ class FastTarget(_FastModelBackend, TargetBackend):
         tok = self.prof.dev_begin(f"verify_B{B}_K{K}", self.stream)
         self.graphs.run(("verify", B, K), b, self._verify_fn(a))
         self.prof.dev_end(tok)
+        if sink is not None:
+            with torch.cuda.stream(self.stream):
+                sink(b.ids.view(B, K), b.top_i[:, 0].view(B, K), b.xn)
+            launches.add(1)
         if ev1 is not None:
             ev1.record(self.stream)
             self.verify_events.append((ev0, ev1))
+        if sink is not None:
+            return
         with torch.cuda.stream(self.stream):
             a["h_commit"].copy_(a["commit"], non_blocking=True)
             a["h_corr"].copy_(a["corr"], non_blocking=True)

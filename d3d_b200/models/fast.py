@@ -283,7 +283,8 @@ class FastRunner:
             mt = math.ceil(T / bt)
             if T > 2048:
                 return dict(qkv=1, o=1, gate_up=1, down=1)
-        f = lambda n, k: ops.splitk_for(n, k, mtiles=mt, bt=bt)
+        m = 0 if self.batch_invariant else T
+        f = lambda n, k: ops.splitk_for(n, k, mtiles=mt, bt=bt, m=m)
         return dict(qkv=f(c.q_size + 2 * c.kv_size, c.hidden_size), o=f(c.hidden_size, c.q_size),
                     gate_up=f(2 * c.intermediate_size, c.hidden_size),
                     down=f(c.hidden_size, c.intermediate_size))

@@ -48,15 +48,18 @@ def ctas_per_sm(bt: int) -> int:
     return 2 if (110 * 1024) // stage >= 4 else 1
 
 
-def splitk_for(n: int, k: int, sms: int = NUM_SMS, mtiles: int = 1, bt: int = 16) -> int:
+def splitk_for(n: int, k: int, sms: int = NUM_SMS, mtiles: int = 1, bt: int = 16, m: int = 0) -> int:
     """Split-K factor that fills whole waves of CTA slots (SMs x co-resident
     CTAs).  For the target it is called with ``mtiles=1, bt=16`` whatever the
-    token count, so it depends on the weight shape alone (batch invariance)."""
+    token count, so it depends on the weight shape alone (batch invariance).
+    With ``m`` tokens given, the fp32 partials (splits * m * n * 4 bytes) are
+    kept no larger than the bf16 weight (n * k * 2 bytes)."""
     sms = sms * ctas_per_sm(bt)
     tiles = math.ceil(n / 128) * mtiles
     kb = math.ceil(k / 64)
+    cap = max(1, k // (2 * m)) if m > 0 else 16
     best, best_eff = 1, 0.0
-    for s in range(1, min(16, kb) + 1):
+    for s in range(1, min(16, kb, cap) + 1):
         if kb // s < 4:          # keep at least 4 K blocks (256) per CTA
             break
         ctas = tiles * s

@@ -274,6 +274,81 @@ void sumsq(Tensor x, Tensor out) {
   d3d::sumsq(x.data_ptr<float>(), static_cast<size_t>(x.numel()), out.data_ptr<float>(), cur_stream());
 }
 
+// ---------------------------------------------------------------- handoff
+// Mailboxes are raw device allocations (not from the caching allocator) so
+// that CUDA IPC maps exactly them; Python holds them as integers and views
+// them as uint8 tensors.
+int64_t mailbox_alloc(int64_t nbytes, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  return reinterpret_cast<int64_t>(d3d::mailbox_alloc(static_cast<size_t>(nbytes)));
+}
+void mailbox_free(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  d3d::mailbox_free(reinterpret_cast<void*>(ptr));
+}
+Tensor mailbox_view(int64_t ptr, int64_t nbytes, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(torch::kCUDA, static_cast<c10::DeviceIndex>(device));
+  return torch::from_blob(reinterpret_cast<void*>(ptr), {nbytes}, opts);
+}
+py::bytes ipc_handle(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  unsigned char h[64];
+  d3d::ipc_get_handle(reinterpret_cast<void*>(ptr), h);
+  return py::bytes(reinterpret_cast<const char*>(h), 64);
+}
+int64_t ipc_open(py::bytes handle, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  std::string s = handle;
+  TORCH_CHECK(s.size() == 64, "ipc handle must be 64 bytes");
+  return reinterpret_cast<int64_t>(d3d::ipc_open_handle(reinterpret_cast<const unsigned char*>(s.data())));
+}
+void ipc_close(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  d3d::ipc_close_handle(reinterpret_cast<void*>(ptr));
+}
+void handoff_put(Tensor src, int64_t dst_ptr, int64_t flag_ptr, int64_t seq, c10::optional<Tensor> ticket) {
+  TORCH_CHECK(!ticket || ticket->is_cuda(), "handoff_put: ticket must be on the GPU");
+  const c10::cuda::CUDAGuard g(ticket ? ticket->device() : at::cuda::current_device());
+  TORCH_CHECK(src.is_cuda() || src.is_pinned(), "handoff_put: src must be on the GPU or pinned");
+  CHECK_CONTIG(src);
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0, "handoff_put: src not 16-byte aligned");
+  const size_t nbytes = static_cast<size_t>(src.numel()) * src.element_size();
+  TORCH_CHECK(nbytes % 16 == 0 && dst_ptr % 16 == 0, "handoff_put: 16-byte sizes and addresses");
+  d3d::handoff_put(src.data_ptr(), reinterpret_cast<void*>(dst_ptr), nbytes, reinterpret_cast<int64_t*>(flag_ptr),
+                   seq, ticket ? reinterpret_cast<unsigned int*>(ticket->data_ptr<int>()) : nullptr, cur_stream());
+}
+void handoff_wait(Tensor flag, int64_t seq, c10::optional<Tensor> src, c10::optional<Tensor> dst, Tensor status) {
+  const c10::cuda::CUDAGuard g(flag.device());
+  CHECK_DT(flag, torch::kInt64);
+  CHECK_DT(status, torch::kInt32);
+  // the kernel writes status and dst directly: device memory or pinned host memory only
+  TORCH_CHECK(status.is_cuda() || status.is_pinned(), "handoff_wait: status must be on the GPU or pinned");
+  TORCH_CHECK(!dst || dst->is_cuda() || dst->is_pinned(), "handoff_wait: dst must be on the GPU or pinned");
+  TORCH_CHECK(!dst || dst->is_contiguous(), "handoff_wait: dst must be contiguous");
+  TORCH_CHECK(!dst || reinterpret_cast<uintptr_t>(dst->data_ptr()) % 16 == 0, "handoff_wait: dst not 16-byte aligned");
+  size_t nbytes = 0;
+  if (src && dst) {
+    nbytes = static_cast<size_t>(dst->numel()) * dst->element_size();
+    TORCH_CHECK(static_cast<size_t>(src->numel()) * src->element_size() >= nbytes && nbytes % 16 == 0,
+                "handoff_wait: payload sizes");
+  }
+  d3d::handoff_wait(flag.data_ptr<int64_t>(), seq, src ? src->data_ptr() : nullptr, dst ? dst->data_ptr() : nullptr,
+                    nbytes, status.data_ptr<int>(), kTimeoutNs, cur_stream());
+}
+void accept_send(Tensor blocks, Tensor post, c10::optional<Tensor> hidden, int64_t out_ptr, int64_t hid_ptr,
+                 int64_t flag_ptr, int64_t seq) {
+  const c10::cuda::CUDAGuard g(blocks.device());
+  CHECK_DT(blocks, torch::kInt64);
+  CHECK_DT(post, torch::kInt64);
+  CHECK_CONTIG(blocks);
+  CHECK_CONTIG(post);
+  const int B = static_cast<int>(blocks.size(0)), K = static_cast<int>(blocks.size(1));
+  const int H = hidden ? static_cast<int>(hidden->size(-1)) : 0;
+  d3d::accept_send(blocks.data_ptr<int64_t>(), post.data_ptr<int64_t>(), B, K, hidden ? cbf(*hidden) : nullptr, H,
+                   reinterpret_cast<int64_t*>(out_ptr), reinterpret_cast<__nv_bfloat16*>(hid_ptr),
+                   reinterpret_cast<int64_t*>(flag_ptr), seq, cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -297,4 +372,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
   m.def("gemm_ctas_per_sm", &d3d::gemm_ctas_per_sm);
+  m.def("mailbox_alloc", &mailbox_alloc);
+  m.def("mailbox_free", &mailbox_free);
+  m.def("mailbox_view", &mailbox_view);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("handoff_put", &handoff_put, py::arg("src"), py::arg("dst_ptr"), py::arg("flag_ptr"), py::arg("seq"),
+        py::arg("ticket") = py::none());
+  m.def("handoff_wait", &handoff_wait, py::arg("flag"), py::arg("seq"), py::arg("src"), py::arg("dst"),
+        py::arg("status"));
+  m.def("accept_send", &accept_send);
 }

@@ -19,18 +19,20 @@
 namespace d3d {
 
 // ----------------------------------------------------------------- helpers
-// Sum of the split-K partials of one element, in split order.  The loads are
-// unrolled to a fixed maximum so they are all in flight at once (the sum order
-// stays fixed).
-constexpr int MAX_SPLITS = 16;
+// Sum of the split-K partials of one element, in split order (loads issued
+// four at a time; the additions stay in split order).
 __device__ __forceinline__ float load_split_sum(const float* p, int nsplit, size_t stride, size_t off) {
-  float v[MAX_SPLITS];
-#pragma unroll
-  for (int i = 0; i < MAX_SPLITS; ++i) v[i] = i < nsplit ? __ldg(p + i * stride + off) : 0.f;
   float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < MAX_SPLITS; ++i)
-    if (i < nsplit) s += v[i];
+  int i = 0;
+  for (; i + 4 <= nsplit; i += 4) {
+    const float a = __ldg(p + (i + 0) * stride + off), b = __ldg(p + (i + 1) * stride + off);
+    const float c = __ldg(p + (i + 2) * stride + off), d = __ldg(p + (i + 3) * stride + off);
+    s += a;
+    s += b;
+    s += c;
+    s += d;
+  }
+  for (; i < nsplit; ++i) s += __ldg(p + i * stride + off);
   return s;
 }
 

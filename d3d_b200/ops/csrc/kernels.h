@@ -65,3 +65,18 @@ void adamw(float* p, const float* g, float* m, float* v, __nv_bfloat16* out, siz
 void sumsq(const float* x, size_t n, float* out, cudaStream_t s);
 
 }  // namespace d3d
+
+namespace d3d {
+// ---- cross-GPU handoff (handoff.cu)
+void handoff_put(const void* src, void* dst_peer, size_t nbytes, int64_t* flag_peer, int64_t seq,
+                 unsigned int* ticket, cudaStream_t st);
+void handoff_wait(const int64_t* flag, int64_t seq, const void* src, void* dst, size_t nbytes, int* status,
+                  unsigned long long limit_ns, cudaStream_t st);
+void accept_send(const int64_t* blocks, const int64_t* post, int B, int K, const __nv_bfloat16* hidden, int H,
+                 int64_t* out_peer, __nv_bfloat16* hid_peer, int64_t* flag_peer, int64_t seq, cudaStream_t st);
+void* mailbox_alloc(size_t nbytes);
+void mailbox_free(void* p);
+void ipc_get_handle(void* p, unsigned char* out64);
+void* ipc_open_handle(const unsigned char* in64);
+void ipc_close_handle(void* p);
+}  // namespace d3d
