@@ -81,10 +81,12 @@ class D3DEngine:
     def from_remote_target(cls, draft_w, link, target_hidden_size: int,
                            decode: Optional[DecodeConfig] = None, *, max_seqs: int = 16,
                            max_context: int = 4096, draft_pages: Optional[int] = None,
-                           page_size: int = 16, device="cuda", use_graphs: bool = True) -> "D3DEngine":
+                           page_size: int = 16, device="cuda", use_graphs: bool = True,
+                           deadline_s: float = 600.0) -> "D3DEngine":
         """Drafter and coordinator on this GPU; the target is served by the
         peer at the other end of ``link`` (:func:`open_pair_link`,
-        :func:`target_server`)."""
+        :func:`target_server`).  A reply that does not arrive within
+        ``deadline_s`` raises ``TimeoutError``."""
         from .engine.disagg import P2PTarget
         from .engine.fast import FastDraft
         from .engine.layout import paged_draft_branch_tokens
@@ -94,7 +96,7 @@ class D3DEngine:
         dp = draft_pages or max_seqs * (max_context + packed_q + page_size) // page_size + 8
         d = FastDraft(draft_w, pages=dp, page_size=page_size, max_seqs=max_seqs,
                       max_context=max_context, packed_q=packed_q, use_graphs=use_graphs, device=device)
-        t = P2PTarget(link, target_hidden_size, device,
+        t = P2PTarget(link, target_hidden_size, device, deadline_s=deadline_s,
                       want_hidden=decode.use_cond and draft_w.cond_proj is not None)
         return cls(t, d, decode)
 
@@ -131,12 +133,13 @@ def open_pair_link(peer: int, device, slot_bytes: Optional[int] = None, group=No
 
 def target_server(target_w, link, *, max_seqs: int = 16, max_context: int = 4096,
                   target_pages: Optional[int] = None, page_size: int = 16, device="cuda",
-                  use_graphs: bool = True):
+                  use_graphs: bool = True, deadline_s: float = 600.0):
     """The target side of a disaggregated pair: call ``.serve()`` on the result;
-    it returns when the drafter side calls :meth:`D3DEngine.close`."""
+    it returns when the drafter side calls :meth:`D3DEngine.close`, and raises
+    ``TimeoutError`` after ``deadline_s`` without a request."""
     from .engine.disagg import P2PTargetServer
     from .engine.fast import FastTarget
     tp = target_pages or max_seqs * (max_context + 64 + page_size) // page_size + 8
     t = FastTarget(target_w, pages=tp, page_size=page_size, max_seqs=max_seqs,
                    max_context=max_context, use_graphs=use_graphs, device=device)
-    return P2PTargetServer(t, link)
+    return P2PTargetServer(t, link, deadline_s=deadline_s)

@@ -85,6 +85,44 @@ def bench_gemm(shapes, iters, peaks, rows):
         del ws
 
 
+DRAFTER_SHAPES = (("qkv", 4096, 2048), ("o", 2048, 2048), ("gate_up", 12288, 2048), ("down", 2048, 6144))
+
+
+def bench_gemm_sweep(m, iters, peaks, rows, shapes=DRAFTER_SHAPES):
+    """Every (token tile, split-K) configuration of the drafter's GEMMs at ``m``
+    tokens: fp32 partials for every split count, bf16 output for split 1.
+    ``partial_MB`` is what the consuming kernel reads back."""
+    from d3d_b200 import ops
+    E = ops.ext()
+    bts = sorted({ops.bt_for(m), 256, 192, 144, 128, 96, 64, 48, 32, 16}, reverse=True)
+    for name, n, k in shapes:
+        copies = max(2, math.ceil(3 * 126e6 / (n * k * 2)))
+        ws = [ops.pack_weight(torch.randn(n, k, device="cuda").to(torch.bfloat16) * 0.02)
+              for _ in range(copies)]
+        x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        kb = math.ceil(k / 64)
+        out = torch.empty(16 * m * n, device="cuda")
+        yb = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        for bt in bts:
+            if bt > 256 and bt % 32:
+                continue
+            if bt > m and bt != ops.bt_for(m):
+                continue
+            for s in range(1, 17):
+                if kb // s < 4:
+                    break
+                us = timeit(lambda i: E.gemm_partial(x, ws[i % copies].data, out, s, bt, None, n), iters)
+                rows.append(dict(kernel="gemm_sweep", shape=name, M=m, N=n, K=k, bt=bt, splits=s, mode="f32",
+                                 ctas=math.ceil(n / 128) * math.ceil(m / bt) * s, us=round(us, 2),
+                                 partial_MB=round(s * m * n * 4 / 1e6, 2),
+                                 TFLOPs=round(2 * m * n * k / us / 1e6, 1)))
+            us = timeit(lambda i: E.gemm_bf16(x, ws[i % copies].data, yb, None, bt, None, n), iters)
+            rows.append(dict(kernel="gemm_sweep", shape=name, M=m, N=n, K=k, bt=bt, splits=1, mode="bf16",
+                             ctas=math.ceil(n / 128) * math.ceil(m / bt), us=round(us, 2), partial_MB=0,
+                             TFLOPs=round(2 * m * n * k / us / 1e6, 1)))
+        del ws
+
+
 def bench_lmhead(iters, peaks, rows, only_m=None):
     from d3d_b200 import ops
     E = ops.ext()
@@ -199,6 +237,7 @@ def main():
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--lm-m", type=int, default=None)
     ap.add_argument("--drafter", action="store_true", help="forward: drafter packed M=272")
+    ap.add_argument("--sweep-m", type=int, default=272, help="gemm_sweep: token count")
     a = ap.parse_args()
     peaks = load_peaks()
     rows = []
@@ -218,6 +257,8 @@ def main():
         bench_lmhead(a.iters, peaks, rows, a.lm_m)
     if "attn" in only:
         bench_attn(a.iters, peaks, rows)
+    if "gemm_sweep" in only:
+        bench_gemm_sweep(a.sweep_m, a.iters, peaks, rows)
     if "forward" in only:
         bench_forward(a.iters, peaks, rows, layers=a.layers if not a.drafter else min(a.layers, 28),
                       drafter=a.drafter)

@@ -69,7 +69,7 @@ class FastWeights:
             layers.append(LayerWeights(
                 qkv=pk(torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0)),
                 o=pk(a.o_proj.weight),
-                gate_up=pk(torch.cat([L.mlp.gate_proj.weight, L.mlp.up_proj.weight], 0)),
+                gate_up=ops.pack_gate_up(bf(L.mlp.gate_proj.weight), bf(L.mlp.up_proj.weight)),
                 down=pk(L.mlp.down_proj.weight),
                 in_norm=bf(L.input_layernorm.weight), post_norm=bf(L.post_attention_layernorm.weight),
                 q_norm=bf(a.q_norm.weight), k_norm=bf(a.k_norm.weight)))
@@ -103,7 +103,8 @@ class FastWeights:
         prnd = lambda *shape: ops.pack_weight(rnd(*shape))
         h, i, d = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
         layers = [LayerWeights(qkv=prnd(cfg.q_size + 2 * cfg.kv_size, h), o=prnd(h, cfg.q_size),
-                               gate_up=prnd(2 * i, h), down=prnd(h, i), in_norm=ones(h),
+                               gate_up=ops.pack_gate_up(*rnd(2 * i, h).chunk(2)), down=prnd(h, i),
+                               in_norm=ones(h),
                                post_norm=ones(h), q_norm=ones(d), k_norm=ones(d))
                   for _ in range(cfg.num_hidden_layers)]
         embed = rnd(cfg.vocab_size, h)
@@ -229,9 +230,12 @@ class StepBuffers:
         self.q = torch.zeros(T, cfg.num_attention_heads, d, dtype=torch.bfloat16, device=dev)
         self.attn = torch.zeros(T, cfg.q_size, dtype=torch.bfloat16, device=dev)
         self.h = torch.zeros(T, cfg.intermediate_size, dtype=torch.bfloat16, device=dev)
-        nmax = max(splits["qkv"] * (cfg.q_size + 2 * cfg.kv_size), splits["o"] * h,
-                   splits["gate_up"] * 2 * cfg.intermediate_size, splits["down"] * h)
+        sp = {g: (v[1] if isinstance(v, tuple) else v) for g, v in splits.items()}
+        width = dict(qkv=cfg.q_size + 2 * cfg.kv_size, o=h, gate_up=2 * cfg.intermediate_size, down=h)
+        # fp32 split-K partials only for GEMMs that split; the others write bf16 directly
+        nmax = max([sp[g] * width[g] for g in width if sp[g] > 1] + [1])
         self.part = torch.zeros(nmax * T, dtype=torch.float32, device=dev)
+        self.qkv = torch.zeros(T if sp["qkv"] == 1 else 1, width["qkv"], dtype=torch.bfloat16, device=dev)
         self.att_o = torch.zeros(n_chunks * T * cfg.num_attention_heads * d if n_chunks > 1 else 1,
                                  dtype=torch.float32, device=dev)
         self.att_ml = torch.zeros(n_chunks * T * cfg.num_attention_heads * 2 if n_chunks > 1 else 1,
@@ -268,26 +272,39 @@ class FastRunner:
         self.scale = 1.0 / math.sqrt(c.head_dim)
         self._bufs: Dict[Tuple, StepBuffers] = {}
         self._graphs: Dict[Tuple, torch.cuda.CUDAGraph] = {}
+        self.tuned: Dict[int, Dict[str, Tuple[int, int]]] = {}
 
     # ------------------------------------------------------------- policies
-    def splits(self, T: int) -> Dict[str, int]:
-        """Split-K per GEMM.  Batch-invariant runners (the target) use the
-        weight shape only for decode-sized T; others also count token tiles."""
+    GEMMS = ("qkv", "o", "gate_up", "down")
+
+    def plan(self, T: int) -> Dict[str, Tuple[int, int]]:
+        """(token tile, split-K) per GEMM of a T-token forward.
+
+        Batch-invariant runners (the target) take the split from the weight
+        shape alone for decode-sized T, so a token's reduction order does not
+        depend on how many tokens share the forward.  Other runners (the
+        drafter) use ``self.tuned`` -- per-T plans measured on the device --
+        when present, else the wave-filling heuristic.  A split of 1 makes the
+        GEMM write bf16 directly (residual add / SwiGLU in its epilogue); the
+        rounding is the same as reducing one partial."""
         c = self.cfg
+        shapes = dict(qkv=(c.q_size + 2 * c.kv_size, c.hidden_size), o=(c.hidden_size, c.q_size),
+                      gate_up=(2 * c.intermediate_size, c.hidden_size),
+                      down=(c.hidden_size, c.intermediate_size))
+        bt = ops.bt_for(T)
         if self.batch_invariant:
             if T > 256:
-                return dict(qkv=1, o=1, gate_up=1, down=1)
-            mt, bt = 1, 16
-        else:
-            bt = ops.bt_for(T)
-            mt = math.ceil(T / bt)
-            if T > 2048:
-                return dict(qkv=1, o=1, gate_up=1, down=1)
-        m = 0 if self.batch_invariant else T
-        f = lambda n, k: ops.splitk_for(n, k, mtiles=mt, bt=bt, m=m)
-        return dict(qkv=f(c.q_size + 2 * c.kv_size, c.hidden_size), o=f(c.hidden_size, c.q_size),
-                    gate_up=f(2 * c.intermediate_size, c.hidden_size),
-                    down=f(c.hidden_size, c.intermediate_size))
+                return {g: (bt, 1) for g in self.GEMMS}
+            return {g: (bt, ops.splitk_for(n, k, mtiles=1, bt=16)) for g, (n, k) in shapes.items()}
+        if T in self.tuned:
+            return dict(self.tuned[T])
+        if T > 2048:
+            return {g: (bt, 1) for g in self.GEMMS}
+        mt = math.ceil(T / bt)
+        return {g: (bt, ops.splitk_for(n, k, mtiles=mt, bt=bt, m=T)) for g, (n, k) in shapes.items()}
+
+    def splits(self, T: int) -> Dict[str, int]:
+        return {g: v[1] for g, v in self.plan(T).items()}
 
     def buffers(self, B: int, Q: int, topk: int, prefill: bool = False) -> StepBuffers:
         key = (B, Q, topk, prefill)
@@ -296,7 +313,7 @@ class FastRunner:
             T = B * Q
             chunk = self.chunk_for(prefill)
             nch = max(1, math.ceil(self.max_context / chunk))
-            b = StepBuffers(self.cfg, B, Q, topk, nch, self.splits(T), self.device)
+            b = StepBuffers(self.cfg, B, Q, topk, nch, self.plan(T), self.device)
             b.bt_view = torch.zeros(B, self.kv.max_pages_per_seq, dtype=torch.int32, device=self.device)
             b.chunk = chunk
             self._bufs[key] = b
@@ -315,7 +332,7 @@ class FastRunner:
         E = ops.ext()
         c, w = self.cfg, self.w
         T, B, Q = b.T, b.B, b.Q
-        sp = self.splits(T)
+        pl = self.plan(T)
         bt = ops.bt_for(T)
         hq, hkv, d = c.num_attention_heads, c.num_key_value_heads, c.head_dim
         cond = None
@@ -325,23 +342,49 @@ class FastRunner:
         E.embed(b.ids, w.embed, cond, b.cond_rows if cond is not None else None, Q, b.x)
         E.add_rmsnorm(None, 1, b.x, w.layers[0].in_norm, b.xn, c.rms_norm_eps)
         torch.index_select(self.kv.block_table, 0, b.seq_rows, out=b.bt_view)
+        n = 3
+        eps = c.rms_norm_eps
         for li, L in enumerate(w.layers):
-            E.gemm_partial(b.xn, L.qkv.data, b.part, sp["qkv"], bt, b.status, L.qkv.n)
-            E.qkv_rope_kv(b.part, None, sp["qkv"], L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
-                          b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, c.rms_norm_eps)
+            gbt, s = pl["qkv"]
+            if s == 1:
+                E.gemm_bf16(b.xn, L.qkv.data, b.qkv, None, gbt, b.status, L.qkv.n)
+                E.qkv_rope_kv(None, b.qkv, 1, L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
+                              b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps)
+            else:
+                E.gemm_partial(b.xn, L.qkv.data, b.part, s, gbt, b.status, L.qkv.n)
+                E.qkv_rope_kv(b.part, None, s, L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
+                              b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps)
             E.attention(b.q, self.kv.k[li], self.kv.v[li], b.bt_view, b.rows, b.kv_end, B, Q, hq, hkv,
                         self.kv.page_size, self.scale, b.chunk, b.n_chunks,
                         b.att_o if b.n_chunks > 1 else None, b.att_ml if b.n_chunks > 1 else None,
                         b.attn)
-            E.gemm_partial(b.attn, L.o.data, b.part, sp["o"], bt, b.status, L.o.n)
-            E.add_rmsnorm(b.part, sp["o"], b.x, L.post_norm, b.xn, c.rms_norm_eps)
-            E.gemm_partial(b.xn, L.gate_up.data, b.part, sp["gate_up"], bt, b.status, L.gate_up.n)
-            E.swiglu(b.part, sp["gate_up"], b.h)
-            E.gemm_partial(b.h, L.down.data, b.part, sp["down"], bt, b.status, L.down.n)
+            n += 3 + (1 if b.n_chunks > 1 else 0)
+            gbt, s = pl["o"]
+            if s == 1:   # residual added in the epilogue, in place
+                E.gemm_bf16(b.attn, L.o.data, b.x, b.x, gbt, b.status, L.o.n)
+                E.add_rmsnorm(None, 1, b.x, L.post_norm, b.xn, eps)
+            else:
+                E.gemm_partial(b.attn, L.o.data, b.part, s, gbt, b.status, L.o.n)
+                E.add_rmsnorm(b.part, s, b.x, L.post_norm, b.xn, eps)
+            gbt, s = pl["gate_up"]
+            if s == 1:
+                E.gemm_swiglu(b.xn, L.gate_up.data, b.h, gbt, b.status, L.gate_up.n)
+                n += 3
+            else:
+                E.gemm_partial(b.xn, L.gate_up.data, b.part, s, gbt, b.status, L.gate_up.n)
+                E.swiglu(b.part, s, b.h, True)
+                n += 4
             nxt = w.layers[li + 1].in_norm if li + 1 < len(w.layers) else w.final_norm
-            E.add_rmsnorm(b.part, sp["down"], b.x, nxt, b.xn, c.rms_norm_eps)
+            gbt, s = pl["down"]
+            if s == 1:
+                E.gemm_bf16(b.h, L.down.data, b.x, b.x, gbt, b.status, L.down.n)
+                E.add_rmsnorm(None, 1, b.x, nxt, b.xn, eps)
+            else:
+                E.gemm_partial(b.h, L.down.data, b.part, s, gbt, b.status, L.down.n)
+                E.add_rmsnorm(b.part, s, b.x, nxt, b.xn, eps)
+            n += 2
         if b.topk > 0:
             E.gemm_topk(b.xn, w.lm_head.data, b.tv, b.ti, b.topk, bt, b.status, w.lm_head.n)
             E.topk_merge(b.tv, b.ti, T, b.ntiles, b.kt, b.topk, b.top_v, b.top_i)
-        n = 2 + len(w.layers) * (9 + (1 if b.n_chunks > 1 else 0)) + (2 if b.topk > 0 else 0)
+        n += 2 if b.topk > 0 else 0
         return n + (1 if cond is not None else 0)

@@ -115,6 +115,24 @@ def pack_weight(w: torch.Tensor) -> PackedWeight:
     return PackedWeight(data, n, k)
 
 
+def gate_up_order(i: int) -> torch.Tensor:
+    """Row order of the interleaved gate|up weight: row ``32w + j`` of tile t
+    is gate row ``64t + 16w + j`` (j < 16) or up row ``I + 64t + 16w + j - 16``,
+    so the SwiGLU epilogue pairs lanes j and j + 16 of one warp."""
+    if i % 64:
+        raise ValueError("interleaved gate|up needs intermediate_size % 64 == 0")
+    r = torch.arange(2 * i)
+    t, w, j = r // 128, (r % 128) // 32, r % 32
+    base = 64 * t + 16 * w
+    return torch.where(j < 16, base + j, i + base + j - 16)
+
+
+def pack_gate_up(gate: torch.Tensor, up: torch.Tensor) -> PackedWeight:
+    """Pack ``[gate; up]`` ([2I, K]) in the interleaved row order."""
+    w = torch.cat([gate, up], 0)
+    return pack_weight(w[gate_up_order(gate.shape[0]).to(w.device)])
+
+
 def _w(w):
     return (w.data, w.n) if isinstance(w, PackedWeight) else (w, 0)
 
@@ -130,6 +148,13 @@ def gemm_partial(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, splits: in
 def gemm_bf16(x, w, out, residual=None, bt=None, status=None):
     wd, wn = _w(w)
     ext().gemm_bf16(x, wd, out, residual, int(bt or bt_for(x.shape[0])), status, wn)
+    return out
+
+
+def gemm_swiglu(x, w: PackedWeight, out, bt=None, status=None):
+    """``out = silu(x @ gate.T) * (x @ up.T)`` for an interleaved gate|up
+    weight (:func:`pack_gate_up`), in the GEMM epilogue."""
+    ext().gemm_swiglu(x, w.data, out, int(bt or bt_for(x.shape[0])), status, w.n)
     return out
 
 

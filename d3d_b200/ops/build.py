@@ -57,15 +57,29 @@ def build(verbose: bool = False):
     return mod
 
 
+def stale_sources() -> list:
+    """Kernel sources changed after the shared object was built."""
+    path = so_path()
+    if not path.exists():
+        return []
+    t = path.stat().st_mtime
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh"))
+    return [p.name for p in deps if p.exists() and p.stat().st_mtime > t + 1.0]
+
+
 def load():
-    """Import the built extension (building it first if absent)."""
+    """Import the built extension (building it first if absent).  A shared
+    object older than its sources is rebuilt when a compiler is at hand
+    (``D3D_REBUILD=1`` forces it) and refused otherwise, so a stale binary
+    never runs against newer Python code."""
     global _mod
     if _mod is not None:
         return _mod
     import torch  # noqa: F401
 
     path = so_path()
-    if os.environ.get("D3D_REBUILD") == "1" or not path.exists():
+    stale = stale_sources()
+    if os.environ.get("D3D_REBUILD") == "1" or not path.exists() or stale:
         _mod = build()
         return _mod
     loader = importlib.machinery.ExtensionFileLoader(NAME, str(path))

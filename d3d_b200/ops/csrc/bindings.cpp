@@ -92,6 +92,20 @@ void gemm_bf16(Tensor x, Tensor w, Tensor out, c10::optional<Tensor> residual, i
   d3d::gemm_launch(a, cur_stream());
 }
 
+// SwiGLU fused into the GEMM epilogue: w is the interleaved gate|up weight
+// (d3d_b200.ops.pack_gate_up) of logical shape [wn = 2I, K]; out is [M, I].
+void gemm_swiglu(Tensor x, Tensor w, Tensor out, int64_t bt, c10::optional<Tensor> status, int64_t wn) {
+  const c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, static_cast<int>(bt), status, wn);
+  CHECK_DT(out, torch::kBFloat16);
+  TORCH_CHECK(out.size(0) == a.M && 2 * out.size(1) == a.N && out.stride(1) == 1, "gemm_swiglu: out shape");
+  a.mode = 3;
+  a.out_bf16 = bf(out);
+  a.ldc = static_cast<int>(out.stride(0));
+  if (a.M == 0) return;
+  d3d::gemm_launch(a, cur_stream());
+}
+
 void gemm_topk(Tensor x, Tensor w, Tensor topv, Tensor topi, int64_t k, int64_t bt, c10::optional<Tensor> status,
                int64_t wn) {
   const c10::cuda::CUDAGuard g(x.device());
@@ -120,12 +134,12 @@ void add_rmsnorm(c10::optional<Tensor> part, int64_t nsplit, Tensor residual, Te
                    M, N, static_cast<float>(eps), cur_stream());
 }
 
-void swiglu(Tensor part, int64_t nsplit, Tensor h) {
+void swiglu(Tensor part, int64_t nsplit, Tensor h, bool interleaved) {
   const c10::cuda::CUDAGuard g(h.device());
   CHECK_CONTIG(h);
   CHECK_DT(part, torch::kFloat32);
   d3d::swiglu(part.data_ptr<float>(), static_cast<int>(nsplit), bf(h), static_cast<int>(h.size(0)),
-              static_cast<int>(h.size(1)), cur_stream());
+              static_cast<int>(h.size(1)), interleaved, cur_stream());
 }
 
 void qkv_rope_kv(c10::optional<Tensor> part, c10::optional<Tensor> y, int64_t nsplit, Tensor q_norm, Tensor k_norm,
@@ -308,7 +322,7 @@ void ipc_close(int64_t ptr, int64_t device) {
 }
 void handoff_put(Tensor src, int64_t dst_ptr, int64_t flag_ptr, int64_t seq, c10::optional<Tensor> ticket) {
   TORCH_CHECK(!ticket || ticket->is_cuda(), "handoff_put: ticket must be on the GPU");
-  const c10::cuda::CUDAGuard g(ticket ? ticket->device() : at::cuda::current_device());
+  const c10::cuda::CUDAGuard g(ticket ? ticket->device() : at::Device(at::kCUDA, at::cuda::current_device()));
   TORCH_CHECK(src.is_cuda() || src.is_pinned(), "handoff_put: src must be on the GPU or pinned");
   CHECK_CONTIG(src);
   TORCH_CHECK(reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0, "handoff_put: src not 16-byte aligned");
@@ -360,7 +374,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_topk", &gemm_topk, py::arg("x"), py::arg("w"), py::arg("topv"), py::arg("topi"), py::arg("k"),
         py::arg("bt"), py::arg("status") = py::none(), py::arg("wn") = 0);
   m.def("add_rmsnorm", &add_rmsnorm);
-  m.def("swiglu", &swiglu);
+  m.def("swiglu", &swiglu, py::arg("part"), py::arg("nsplit"), py::arg("h"), py::arg("interleaved") = false);
+  m.def("gemm_swiglu", &gemm_swiglu, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("bt"),
+        py::arg("status") = py::none(), py::arg("wn") = 0);
   m.def("qkv_rope_kv", &qkv_rope_kv);
   m.def("embed", &embed);
   m.def("topk_merge", &topk_merge);

@@ -13,34 +13,70 @@
 // LM-head top-k merge and greedy acceptance.  Rounding points mirror the
 // Hugging Face Qwen3 module order (bf16 after every op) except RoPE, which is
 // evaluated in fp32 and rounded once.
+#include <stdexcept>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace d3d {
 
 // ----------------------------------------------------------------- helpers
-// Sum of the split-K partials of one element, in split order (loads issued
-// four at a time; the additions stay in split order).
+// Sum of the split-K partials of one element (or of 4 consecutive elements),
+// in split order.  Every load is issued before the first addition, so a
+// thread waits for one memory round trip whatever the split count.
+constexpr int MAX_SPLITS = 16;
+
+template <int S = MAX_SPLITS>
 __device__ __forceinline__ float load_split_sum(const float* p, int nsplit, size_t stride, size_t off) {
+  float v[S];
+#pragma unroll
+  for (int i = 0; i < S; ++i)
+    if (i < nsplit) v[i] = __ldg(p + i * stride + off);
   float s = 0.f;
-  int i = 0;
-  for (; i + 4 <= nsplit; i += 4) {
-    const float a = __ldg(p + (i + 0) * stride + off), b = __ldg(p + (i + 1) * stride + off);
-    const float c = __ldg(p + (i + 2) * stride + off), d = __ldg(p + (i + 3) * stride + off);
-    s += a;
-    s += b;
-    s += c;
-    s += d;
-  }
-  for (; i < nsplit; ++i) s += __ldg(p + i * stride + off);
+#pragma unroll
+  for (int i = 0; i < S; ++i)
+    if (i < nsplit) s += v[i];
   return s;
+}
+
+template <int S>
+__device__ __forceinline__ float4 load_split_sum4(const float* p, int nsplit, size_t stride, size_t off) {
+  float4 v[S];
+#pragma unroll
+  for (int i = 0; i < S; ++i)
+    if (i < nsplit) v[i] = __ldg(reinterpret_cast<const float4*>(p + i * stride + off));
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < S; ++i)
+    if (i < nsplit) {
+      s.x += v[i].x;
+      s.y += v[i].y;
+      s.z += v[i].z;
+      s.w += v[i].w;
+    }
+  return s;
+}
+
+__device__ __forceinline__ void ld_bf16x4(const __nv_bfloat16* p, float* f) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) f[j] = __bfloat162float(b[j]);
+}
+
+__device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, const float* f) {
+  __align__(8) __nv_bfloat16 b[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) b[j] = __float2bfloat16(f[j]);
+  *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(b);
 }
 
 // ------------------------------------------------------- add + RMSNorm
 // x = bf16(residual + bf16(sum_s P[s])) (or x = residual when P is null);
 // residual <- x; out = w * bf16(x * rsqrt(mean(x^2) + eps)).
-template <int VPT>
-__global__ void add_rmsnorm_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* __restrict__ residual,
+// One block per row, 4 consecutive elements per thread and vector.
+template <int V, int S>
+__global__ void __launch_bounds__(512) add_rmsnorm_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* __restrict__ residual,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int M, int N,
                                    float eps) {
   griddep_launch();
@@ -48,24 +84,34 @@ __global__ void add_rmsnorm_kernel(const float* __restrict__ part, int nsplit, _
   const int m = blockIdx.x;
   if (m >= M) return;
   __shared__ float red[32];
-  float xv[VPT];
+  float xv[V][4];
   float ss = 0.f;
   const size_t stride = static_cast<size_t>(M) * N;
+  float4 ps[V];
+  if (part) {
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int n = threadIdx.x + i * blockDim.x;
-    float x = 0.f;
+    for (int i = 0; i < V; ++i) {
+      const int n = 4 * (threadIdx.x + i * blockDim.x);
+      if (n < N) ps[i] = load_split_sum4<S>(part, nsplit, stride, static_cast<size_t>(m) * N + n);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int n = 4 * (threadIdx.x + i * blockDim.x);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) xv[i][j] = 0.f;
     if (n < N) {
       const size_t off = static_cast<size_t>(m) * N + n;
-      x = __bfloat162float(residual[off]);
+      ld_bf16x4(residual + off, xv[i]);
       if (part) {
-        const float y = bf16r(load_split_sum(part, nsplit, stride, off));
-        x = bf16r(x + y);
-        residual[off] = __float2bfloat16(x);
+        const float y[4] = {ps[i].x, ps[i].y, ps[i].z, ps[i].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) xv[i][j] = bf16r(xv[i][j] + bf16r(y[j]));
+        st_bf16x4(residual + off, xv[i]);
       }
     }
-    xv[i] = x;
-    ss += x * x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss += xv[i][j] * xv[i][j];
   }
   ss = warp_sum(ss);
   const int wid = threadIdx.x >> 5, lid = threadIdx.x & 31;
@@ -79,55 +125,90 @@ __global__ void add_rmsnorm_kernel(const float* __restrict__ part, int nsplit, _
   __syncthreads();
   const float r = rsqrtf(red[0] / N + eps);
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int n = threadIdx.x + i * blockDim.x;
+  for (int i = 0; i < V; ++i) {
+    const int n = 4 * (threadIdx.x + i * blockDim.x);
     if (n < N) {
-      const float y = bf16r(xv[i] * r) * __bfloat162float(w[n]);
-      out[static_cast<size_t>(m) * N + n] = __float2bfloat16(y);
+      float wv[4], y[4];
+      ld_bf16x4(w + n, wv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) y[j] = bf16r(xv[i][j] * r) * wv[j];
+      st_bf16x4(out + static_cast<size_t>(m) * N + n, y);
     }
   }
 }
 
+// S: compile-time bound on the split count (registers for the in-flight loads)
+#define D3D_SPLIT_DISPATCH(nsplit, CALL)                       \
+  do {                                                         \
+    if ((nsplit) <= 4) { constexpr int S = 4; CALL; }          \
+    else if ((nsplit) <= 8) { constexpr int S = 8; CALL; }     \
+    else { constexpr int S = MAX_SPLITS; CALL; }               \
+  } while (0)
+
 void add_rmsnorm(const float* part, int nsplit, __nv_bfloat16* residual, const __nv_bfloat16* w, __nv_bfloat16* out,
                  int M, int N, float eps, cudaStream_t st) {
   if (M == 0) return;
-  const int threads = N >= 4096 ? 1024 : (N >= 1024 ? 256 : 128);
-  const int vpt = (N + threads - 1) / threads;
-  if (vpt <= 2) launch_pdl(add_rmsnorm_kernel<2>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps);
-  else if (vpt <= 4) launch_pdl(add_rmsnorm_kernel<4>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps);
-  else if (vpt <= 8) launch_pdl(add_rmsnorm_kernel<8>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps);
-  else launch_pdl(add_rmsnorm_kernel<16>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps);
+  if (N % 4) throw std::runtime_error("add_rmsnorm: hidden size must be a multiple of 4");
+  if (nsplit > MAX_SPLITS) throw std::runtime_error("add_rmsnorm: too many splits");
+  const int vec = N / 4;
+  const int threads = vec >= 512 ? 512 : (vec + 31) / 32 * 32;
+  const int v = (vec + threads - 1) / threads;
+  const int ns = part ? nsplit : 1;
+  if (v <= 1) D3D_SPLIT_DISPATCH(ns, launch_pdl(add_rmsnorm_kernel<1, S>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps));
+  else if (v <= 2) D3D_SPLIT_DISPATCH(ns, launch_pdl(add_rmsnorm_kernel<2, S>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps));
+  else if (v <= 4) D3D_SPLIT_DISPATCH(ns, launch_pdl(add_rmsnorm_kernel<4, S>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps));
+  else if (v <= 8) D3D_SPLIT_DISPATCH(ns, launch_pdl(add_rmsnorm_kernel<8, S>, dim3(M), dim3(threads), 0, st, part, nsplit, residual, w, out, M, N, eps));
+  else throw std::runtime_error("add_rmsnorm: hidden size above 16384");
 }
 
 // ------------------------------------------------------------------ SwiGLU
 // P[s][m][0:I] = gate, P[s][m][I:2I] = up  ->  h[m][i] = bf16(bf16(silu(g)) * u)
-__global__ void swiglu_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* __restrict__ h, int M, int I) {
+// With ``interleaved`` the columns come from the interleaved gate|up weight
+// (ops.pack_gate_up): h[i] takes gate column 128t + 32w + l and up column
+// 128t + 32w + 16 + l for i = 64t + 16w + l.  Four consecutive columns per
+// thread (they stay consecutive under the interleave).
+template <int S>
+__global__ void __launch_bounds__(256, 2)
+    swiglu_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* __restrict__ h, int M, int I,
+                  bool interleaved) {
   griddep_launch();
   griddep_wait();
-  const size_t total = static_cast<size_t>(M) * I;
+  const int I4 = I / 4;
+  const size_t total = static_cast<size_t>(M) * I4;
   const size_t stride = static_cast<size_t>(M) * 2 * I;
   for (size_t t = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; t < total;
        t += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t m = t / I, i = t % I;
-    const size_t off = m * 2 * I + i;
-    const float g = bf16r(load_split_sum(part, nsplit, stride, off));
-    const float u = bf16r(load_split_sum(part, nsplit, stride, off + I));
-    const float s = bf16r(g / (1.f + expf(-g)));
-    h[t] = __float2bfloat16(s * u);
+    const size_t m = t / I4, i = (t % I4) * 4;
+    const size_t gcol = interleaved ? (i / 64) * 128 + ((i % 64) / 16) * 32 + (i % 16) : i;
+    const size_t ucol = interleaved ? gcol + 16 : i + I;
+    const float4 g4 = load_split_sum4<S>(part, nsplit, stride, m * 2 * I + gcol);
+    const float4 u4 = load_split_sum4<S>(part, nsplit, stride, m * 2 * I + ucol);
+    const float g[4] = {g4.x, g4.y, g4.z, g4.w}, u[4] = {u4.x, u4.y, u4.z, u4.w};
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gb = bf16r(g[j]);
+      const float sl = bf16r(gb / (1.f + expf(-gb)));
+      o[j] = sl * bf16r(u[j]);
+    }
+    st_bf16x4(h + m * I + i, o);
   }
 }
 
-void swiglu(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, cudaStream_t st) {
+void swiglu(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, bool interleaved, cudaStream_t st) {
   if (M == 0) return;
-  const size_t total = static_cast<size_t>(M) * I;
+  if (I % 4) throw std::runtime_error("swiglu: intermediate size must be a multiple of 4");
+  if (interleaved && I % 64) throw std::runtime_error("swiglu: interleaved gate|up needs I % 64 == 0");
+  if (nsplit > MAX_SPLITS) throw std::runtime_error("swiglu: too many splits");
+  const size_t total = static_cast<size_t>(M) * (I / 4);
   int blocks = static_cast<int>((total + 255) / 256);
-  if (blocks > 148 * 16) blocks = 148 * 16;
-  launch_pdl(swiglu_kernel, dim3(blocks), dim3(256), 0, st, part, nsplit, h, M, I);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  D3D_SPLIT_DISPATCH(nsplit, launch_pdl(swiglu_kernel<S>, dim3(blocks), dim3(256), 0, st, part, nsplit, h, M, I, interleaved));
 }
 
 // ------------------------------------------- QK-norm + RoPE + paged KV write
 // One warp per (token, head) for heads [0, Hq + 2*Hkv): q heads, k heads, v heads.
-template <int E>  // elements per lane = head_dim / 32
+template <int E, int S>  // E: elements per lane = head_dim / 32; S: split bound
 __global__ void qkv_rope_kv_kernel(QkvRopeArgs a) {
   griddep_launch();
   griddep_wait();
@@ -140,10 +221,21 @@ __global__ void qkv_rope_kv_kernel(QkvRopeArgs a) {
   const int N = H * D;
   const size_t stride = static_cast<size_t>(a.M) * N;
   float x[E];
+  const size_t off0 = static_cast<size_t>(m) * N + h * D + lane * E;
+  if constexpr (E == 4) {
+    if (a.part) {
+      const float4 s4 = load_split_sum4<S>(a.part, a.nsplit, stride, off0);
+      x[0] = bf16r(s4.x);
+      x[1] = bf16r(s4.y);
+      x[2] = bf16r(s4.z);
+      x[3] = bf16r(s4.w);
+    } else {
+      ld_bf16x4(a.y + off0, x);
+    }
+  } else {
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const size_t off = static_cast<size_t>(m) * N + h * D + lane * E + e;
-    x[e] = bf16r(a.part ? load_split_sum(a.part, a.nsplit, stride, off) : __bfloat162float(a.y[off]));
+    for (int e = 0; e < E; ++e)
+      x[e] = bf16r(a.part ? load_split_sum<S>(a.part, a.nsplit, stride, off0 + e) : __bfloat162float(a.y[off0 + e]));
   }
   const int64_t slot = a.slots[m];
   if (h >= a.Hq + a.Hkv) {  // v head: straight to the cache
@@ -192,11 +284,13 @@ void qkv_rope_kv(const QkvRopeArgs& a, cudaStream_t st) {
   if (a.M == 0) return;
   const int warps = a.M * (a.Hq + 2 * a.Hkv);
   const int blocks = (warps * 32 + 255) / 256;
+  if (a.part && a.nsplit > MAX_SPLITS) throw std::runtime_error("qkv_rope_kv: too many splits");
+  const int ns = a.part ? a.nsplit : 1;
   switch (a.head_dim) {
-    case 32: launch_pdl(qkv_rope_kv_kernel<1>, dim3(blocks), dim3(256), 0, st, a); break;
-    case 64: launch_pdl(qkv_rope_kv_kernel<2>, dim3(blocks), dim3(256), 0, st, a); break;
-    case 128: launch_pdl(qkv_rope_kv_kernel<4>, dim3(blocks), dim3(256), 0, st, a); break;
-    default: break;
+    case 32: D3D_SPLIT_DISPATCH(ns, launch_pdl(qkv_rope_kv_kernel<1, S>, dim3(blocks), dim3(256), 0, st, a)); break;
+    case 64: D3D_SPLIT_DISPATCH(ns, launch_pdl(qkv_rope_kv_kernel<2, S>, dim3(blocks), dim3(256), 0, st, a)); break;
+    case 128: D3D_SPLIT_DISPATCH(ns, launch_pdl(qkv_rope_kv_kernel<4, S>, dim3(blocks), dim3(256), 0, st, a)); break;
+    default: throw std::runtime_error("qkv_rope_kv: head_dim must be 32, 64 or 128");
   }
 }
 

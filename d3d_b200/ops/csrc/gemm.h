@@ -19,6 +19,7 @@ struct GemmParams {
   int* topi;
   int ntiles;
   int bt;
+  int splits;
   int stages;
   int w_packed;
   int* status;
@@ -29,12 +30,12 @@ struct GemmArgs {
   const __nv_bfloat16* x;  // [M, K] activations (row stride ldx elements)
   const __nv_bfloat16* w;  // [N, K] weights (row stride ldw elements)
   int M, N, K, ldx, ldw;
-  int mode;      // 0 fp32 split-K partials, 1 bf16 (+residual), 2 fused top-k
+  int mode;      // 0 fp32 split-K partials, 1 bf16 (+residual), 2 fused top-k, 3 SwiGLU (interleaved gate|up)
   int splits;    // split-K factor (mode 0 only)
   int bt;        // token tile (MMA N), multiple of 16 in [16, 256]
   int topk;      // mode 2: k <= 4
   float* out_f32;              // mode 0: [splits, M, N]
-  __nv_bfloat16* out_bf16;     // mode 1: [M, ldc]
+  __nv_bfloat16* out_bf16;     // mode 1: [M, ldc]; mode 3: [M, ldc] with N/2 columns
   int ldc;
   const __nv_bfloat16* residual;  // mode 1 optional [M, ldr]
   int ldr;

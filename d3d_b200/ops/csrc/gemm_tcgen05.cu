@@ -4,29 +4,38 @@
 // the tile is laid out "swap-AB": the 128-row MMA M dimension runs over weight
 // rows (output features) and the MMA N dimension over tokens: ``bt`` = 16..256
 // (a multiple of 16) in one MMA, or up to 512 (a multiple of 32) as two MMAs
-// of bt/2 columns each, so one CTA can reuse its weight tile for 512 tokens
-// (TMEM holds 512 fp32 columns).  One CTA owns a 128 x bt output tile and a contiguous
-// range of K blocks (split-K chosen by the host from the weight shape alone,
-// so the fp32 reduction order of every output element is independent of M —
-// the property greedy token identity between AR and speculative decoding
-// rests on).
+// of bt/2 columns each.  A work unit is a 128 x bt output tile and a
+// contiguous range of K blocks (split-K chosen by the host from the weight
+// shape alone, so the fp32 reduction order of every output element is
+// independent of M -- the property greedy token identity between AR and
+// speculative decoding rests on).
 //
-// Per CTA (128 threads):
+// The kernel is persistent: min(units, SMs x CTAs-per-SM) CTAs walk the units
+// round-robin (unit order: weight tile, then token tile, then split, so CTAs
+// running side by side share weight tiles in L2).  Per CTA (192 threads):
 //   warp 0 lane 0  TMA producer: W tile [128 x 64] and X tile [bt x 64] per
-//                  stage, 128-byte swizzle, mbarrier complete_tx;
-//   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma (K = 16 each) per stage into a
-//                  TMEM accumulator (128 lanes x bt fp32 columns), then
-//                  tcgen05.commit to free the stage;
-//   all 4 warps    epilogue: tcgen05.ld 32x32b (warp w owns TMEM lanes
-//                  32w..32w+31 = output rows) and one of three stores:
+//                  stage, 128-byte swizzle, mbarrier complete_tx, one
+//                  continuous pipeline across units;
+//   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma (K = 16 each) per stage into
+//                  one of two TMEM accumulators (128 lanes x bt fp32 columns),
+//                  tcgen05.commit frees the stage; after a unit's last stage
+//                  it commits the accumulator to the epilogue;
+//   warps 2..5     epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes
+//                  32(w%4)..+31 = output rows), hands the accumulator back,
+//                  then stores -- overlapping the next unit's main loop:
 //                  MODE 0  fp32 split-K partials  P[split][M][N]
 //                  MODE 1  bf16 Y (+ bf16 residual, rounded like two bf16 ops)
 //                  MODE 2  per-tile top-KT (value, index) over the 128 rows,
-//                          for LM-head argmax / top-k without storing logits.
+//                          for LM-head argmax / top-k without storing logits
+//                  MODE 3  SwiGLU of an interleaved gate|up weight: tile row
+//                          32w+i holds gate row 64t+16w+i (i < 16) or the
+//                          matching up row (i >= 16), so lane i pairs with
+//                          lane i+16 of the same warp: h = silu(g) * u, bf16.
 // Every mbarrier wait is bounded; a timeout records an error code in
-// ``status`` and the kernel leaves its loop.  Launched with programmatic
-// dependent launch: the producer streams the first pipeline stages of weights
-// before griddepcontrol.wait, overlapping the previous kernel's tail.
+// ``status``, raises a CTA-wide abort flag and every role leaves its loop;
+// teardown waits (bounded) for issued TMA loads and MMAs before TMEM is
+// freed.  Launched with programmatic dependent launch: the producer streams
+// the first stages of weights before griddepcontrol.wait.
 #include "common.cuh"
 #include "gemm.h"
 
@@ -40,9 +49,33 @@ namespace d3d {
 constexpr int GBN = 128;  // weight rows per tile (MMA M)
 constexpr int GBK = 64;   // K per stage (one 128-byte swizzle atom of bf16)
 constexpr int A_TILE_BYTES = GBN * GBK * 2;
+constexpr int GEMM_THREADS = 192;
+
+__host__ __device__ inline int acc_cols_for(int bt) {
+  if (bt > 256) return 512;
+  int c = 32;
+  while (c < bt) c <<= 1;
+  return c;
+}
+__host__ __device__ inline int num_acc_for(int bt) { return (bt <= 256 && 2 * acc_cols_for(bt) <= 512) ? 2 : 1; }
+
+struct UnitCoord {
+  int n_t, m_t, split, kb0, kb1;
+};
+
+__device__ __forceinline__ UnitCoord unit_coord(int t, int ntm, int nsplit, int nkb) {
+  UnitCoord u;
+  u.split = t % nsplit;
+  const int r = t / nsplit;
+  u.m_t = r % ntm;
+  u.n_t = r / ntm;
+  u.kb0 = (nkb * u.split) / nsplit;
+  u.kb1 = (nkb * (u.split + 1)) / nsplit;
+  return u;
+}
 
 template <int MODE, int KT>
-__global__ void __launch_bounds__(128, 2)
+__global__ void __launch_bounds__(GEMM_THREADS, 2)
     gemm_tn_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -50,21 +83,29 @@ __global__ void __launch_bounds__(128, 2)
   const int bt = p.bt;
   const int stages = p.stages;
   const int stage_bytes = A_TILE_BYTES + bt * GBK * 2;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
+  // MODE 2 cross-warp merge areas, double-buffered: [2][4 warps][bt][KT] (value, index)
+  const int marea = MODE == 2 ? 4 * bt * KT : 0;
+  float* mval = reinterpret_cast<float*>(smem + stages * stage_bytes);
+  int* midx = reinterpret_cast<int*>(mval + 2 * marea);
+  uint64_t* full = reinterpret_cast<uint64_t*>(midx + 2 * marea);
   uint64_t* empty = full + stages;
-  uint64_t* accb = empty + stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
-  int* flags = reinterpret_cast<int*>(tmem_slot + 1);  // [0] issued, [1] consumed, [2] failed
+  uint64_t* accf = empty + stages;  // [2] accumulator ready for the epilogue
+  uint64_t* acce = accf + 2;        // [2] accumulator drained by the epilogue
+  uint64_t* mfull = acce + 2;       // [2] MODE 2: the four warps' candidates are in
+  uint64_t* mempty = mfull + 2;     // [2] MODE 2: merge area read, may be rewritten
+  uint64_t* done = mempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort [1] issued [2] consumed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * GBN, m0 = blockIdx.y * bt;
   const int nkb = (p.K + GBK - 1) / GBK;
-  const int split = blockIdx.z, nsplit = gridDim.z;
-  const int kb0 = (nkb * split) / nsplit, kb1 = (nkb * (split + 1)) / nsplit;
-  const int nk = kb1 - kb0;
-  const int nsub = bt > 256 ? 2 : 1;      // MMAs per K step
-  const int sub = bt / nsub;              // tokens per MMA (multiple of 16)
-  const uint32_t tmem_cols = bt <= 32 ? 32 : (bt <= 64 ? 64 : (bt <= 128 ? 128 : (bt <= 256 ? 256 : 512)));
+  const int ntn = (p.N + GBN - 1) / GBN, ntm = (p.M + bt - 1) / bt, nsplit = p.splits;
+  const int units = ntn * ntm * nsplit;
+  const int nsub = bt > 256 ? 2 : 1;  // MMAs per K step
+  const int sub = bt / nsub;          // tokens per MMA (multiple of 16)
+  const int acc_cols = acc_cols_for(bt);
+  const int nacc = num_acc_for(bt);
+  const uint32_t tmem_cols = static_cast<uint32_t>(acc_cols * nacc);
   const uint64_t lim = p.timeout_ns;
 
   if (threadIdx.x == 0) {
@@ -72,14 +113,20 @@ __global__ void __launch_bounds__(128, 2)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accb, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf[a], 1);
+      mbar_init(&acce[a], 4);
+      mbar_init(&mfull[a], 4);
+      mbar_init(&mempty[a], 1);
+    }
+    mbar_init(done, 1);
     flags[0] = flags[1] = flags[2] = 0;
     fence_mbar_init();
     prefetch_tensormap(&tmW);
     prefetch_tensormap(&tmX);
     griddep_launch();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
@@ -88,187 +135,276 @@ __global__ void __launch_bounds__(128, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ------------------------------------------------------------ producer
-    const uint64_t pol_w = policy_evict_first();  // weights stream through L2 once
-    auto load_w = [&](int i, int s) {
-      uint8_t* sa = smem + s * stage_bytes;
-      if (p.w_packed)  // contiguous 16 KB tiles: [N/128][K/64][128][64]
-        tma_load_2d_hint(sa, &tmW, &full[s], 0, (blockIdx.x * nkb + kb0 + i) * GBN, pol_w);
-      else
-        tma_load_2d_hint(sa, &tmW, &full[s], (kb0 + i) * GBK, n0, pol_w);
-    };
-    auto load_x = [&](int i, int s) {
-      uint8_t* sb = smem + s * stage_bytes + A_TILE_BYTES;
-      for (int u = 0; u < nsub; ++u)
-        tma_load_2d(sb + u * sub * GBK * 2, &tmX, &full[s], (kb0 + i) * GBK, m0 + u * sub);
-    };
-    // weights do not depend on earlier kernels: fill the pipeline before the
-    // grid dependency resolves, then add the activation tiles
-    const int pre = nk < stages ? nk : stages;
-    for (int i = 0; i < pre; ++i) {
-      mbar_arrive_expect_tx(&full[i], stage_bytes);
-      load_w(i, i);
-    }
-    griddep_wait();
-    for (int i = 0; i < pre; ++i) load_x(i, i);
-    int i = pre;
-    for (; i < nk; ++i) {
-      const int s = i % stages;
-      const uint32_t ph = (i / stages) & 1;
-      if (!mbar_wait(&empty[s], ph ^ 1, lim)) {
-        set_error(p.status, ERR_TIMEOUT_PRODUCER);
-        break;
+  auto fail = [&](int code) {
+    set_error(p.status, code);
+    flags[0] = 1;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      const uint64_t pol_w = policy_evict_first();  // weights stream through L2 once
+      auto load_w = [&](const UnitCoord& u, int kb, int s) {
+        uint8_t* sa = smem + s * stage_bytes;
+        if (p.w_packed)  // contiguous 16 KB tiles: [N/128][K/64][128][64]
+          tma_load_2d_hint(sa, &tmW, &full[s], 0, (u.n_t * nkb + kb) * GBN, pol_w);
+        else
+          tma_load_2d_hint(sa, &tmW, &full[s], kb * GBK, u.n_t * GBN, pol_w);
+      };
+      auto load_x = [&](const UnitCoord& u, int kb, int s) {
+        uint8_t* sb = smem + s * stage_bytes + A_TILE_BYTES;
+        for (int v = 0; v < nsub; ++v)
+          tma_load_2d(sb + v * sub * GBK * 2, &tmX, &full[s], kb * GBK, u.m_t * bt + v * sub);
+      };
+      uint32_t it = 0;
+      int pre = 0;
+      if (static_cast<int>(blockIdx.x) < units) {
+        // weights do not depend on earlier kernels: fill the pipeline before
+        // the grid dependency resolves, then add the activation tiles
+        const UnitCoord u0 = unit_coord(blockIdx.x, ntm, nsplit, nkb);
+        pre = min(u0.kb1 - u0.kb0, stages);
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], stage_bytes);
+          load_w(u0, u0.kb0 + i, i);
+        }
+        griddep_wait();
+        for (int i = 0; i < pre; ++i) load_x(u0, u0.kb0 + i, i);
+        it = pre;
+      } else {
+        griddep_wait();
       }
-      mbar_arrive_expect_tx(&full[s], stage_bytes);
-      load_w(i, s);
-      load_x(i, s);
+      bool first = true;
+      for (int t = blockIdx.x; t < units && !flags[0]; t += gridDim.x, first = false) {
+        const UnitCoord u = unit_coord(t, ntm, nsplit, nkb);
+        for (int kb = u.kb0 + (first ? pre : 0); kb < u.kb1; ++kb, ++it) {
+          const int s = it % stages;
+          if (!mbar_wait(&empty[s], ((it / stages) & 1) ^ 1, lim)) {
+            fail(ERR_TIMEOUT_PRODUCER);
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], stage_bytes);
+          load_w(u, kb, s);
+          load_x(u, kb, s);
+        }
+      }
+      flags[1] = static_cast<int>(it);
     }
-    flags[0] = i;
-  } else if (warp == 1 && lane == 0) {
-    // ----------------------------------------------------------- MMA issuer
-    const uint32_t idesc = idesc_bf16_f32(GBN, sub);
-    int i = 0;
-    for (; i < nk; ++i) {
-      const int s = i % stages;
-      const uint32_t ph = (i / stages) & 1;
-      if (!mbar_wait(&full[s], ph, lim)) {
-        set_error(p.status, ERR_TIMEOUT_MMA);
-        flags[2] = 1;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // -------------------------------------------------------- MMA issuer
+      const uint32_t idesc = idesc_bf16_f32(GBN, sub);
+      uint32_t it = 0;
+      int ti = 0;
+      for (int t = blockIdx.x; t < units && !flags[0]; t += gridDim.x, ++ti) {
+        const UnitCoord u = unit_coord(t, ntm, nsplit, nkb);
+        const int a = ti % nacc, use = ti / nacc;
+        if (!mbar_wait(&acce[a], (use & 1) ^ 1, lim)) {
+          fail(ERR_TIMEOUT_MMA);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t td = tmem + static_cast<uint32_t>(a * acc_cols);
+        bool ok = true;
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+          const int s = it % stages;
+          if (!mbar_wait(&full[s], (it / stages) & 1, lim)) {
+            fail(ERR_TIMEOUT_MMA);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * stage_bytes);
+          const uint64_t ad = sdesc_kmajor_sw128(sa);
+          const uint64_t bd = sdesc_kmajor_sw128(sa + A_TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < GBK / 16; ++kk) {
+            // +32 bytes along K inside the swizzle atom = +2 in the >>4 address field
+            const uint32_t acc = (kb > u.kb0 || kk > 0) ? 1u : 0u;
+            umma_bf16(td, ad + 2 * kk, bd + 2 * kk, idesc, acc);
+            if (nsub == 2) {
+              const uint64_t bd2 = sdesc_kmajor_sw128(sa + A_TILE_BYTES + sub * GBK * 2);
+              umma_bf16(td + sub, ad + 2 * kk, bd2 + 2 * kk, idesc, acc);
+            }
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&accf[a]);
+      }
+      flags[2] = static_cast<int>(it);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    griddep_wait();  // outputs may still be read by the previous kernel until it completes
+    const int q = warp & 3;           // TMEM lane quadrant of this warp
+    const int row = q * 32 + lane;    // weight row within the tile
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    int ti = 0;
+    for (int t = blockIdx.x; t < units; t += gridDim.x, ++ti) {
+      const UnitCoord u = unit_coord(t, ntm, nsplit, nkb);
+      const int a = ti % nacc, use = ti / nacc;
+      bool ok = !flags[0] && mbar_wait(&accf[a], use & 1, lim);
+      if (!ok) {
+        if (!flags[0]) fail(ERR_TIMEOUT_EPILOGUE);
         break;
       }
       tc_fence_after();
-      const uint32_t sa = smem_u32(smem + s * stage_bytes);
-      const uint64_t ad = sdesc_kmajor_sw128(sa);
-      const uint64_t bd = sdesc_kmajor_sw128(sa + A_TILE_BYTES);
+      const uint32_t tacc = t_lane + static_cast<uint32_t>(a * acc_cols);
+      const int n0 = u.n_t * GBN, m0 = u.m_t * bt;
+      const int n = n0 + row;
+      const bool n_ok = n < p.N;
+      if constexpr (MODE == 0 || MODE == 1 || MODE == 3) {
+        // MODE 3 output column of this lane (lanes 0..15 of each warp write)
+        const int hcol = u.n_t * (GBN / 2) + q * 16 + (lane & 15);
+        const int cols = min(bt, p.M - m0);
+        for (int c = 0; c < cols; c += 16) {
+          float v[16];
+          tmem_ld16(tacc + c, v);
+          if constexpr (MODE == 0) {
+            if (n_ok) {
+              float* base = p.out_f32 + static_cast<size_t>(u.split) * p.M * p.N;
 #pragma unroll
-      for (int kk = 0; kk < GBK / 16; ++kk) {
-        // +32 bytes along K inside the swizzle atom = +2 in the >>4 address field
-        umma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
-        if (nsub == 2) {
-          const uint64_t bd2 = sdesc_kmajor_sw128(sa + A_TILE_BYTES + sub * GBK * 2);
-          umma_bf16(tmem + sub, ad + 2 * kk, bd2 + 2 * kk, idesc, (i | kk) != 0 ? 1u : 0u);
-        }
-      }
-      umma_commit(&empty[s]);
-    }
-    flags[1] = i;
-    umma_commit(accb);
-  }
-  __syncwarp();
-  griddep_wait();  // outputs may still be read by the previous kernel until it completes
-
-  // -------------------------------------------------------------- epilogue
-  bool ok = mbar_wait(accb, 0, lim);
-  if (!ok) set_error(p.status, ERR_TIMEOUT_EPILOGUE);
-  __syncwarp();
-  tc_fence_after();
-  const int row = warp * 32 + lane;
-  const int n = n0 + row;
-  const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  const bool n_ok = n < p.N;
-  const bool live = ok && nk > 0;
-
-  for (int c = 0; c < (MODE == 2 ? 0 : bt); c += 16) {
-    float v[16];
-    tmem_ld16(t_row + c, v);
-    if (!live) {
+              for (int j = 0; j < 16; ++j) {
+                const int m = m0 + c + j;
+                if (c + j < cols) base[static_cast<size_t>(m) * p.N + n] = v[j];
+              }
+            }
+          } else if constexpr (MODE == 1) {
+            if (n_ok) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = 0.f;
-    }
-    if constexpr (MODE == 0) {
-      if (n_ok) {
-        float* base = p.out_f32 + static_cast<size_t>(split) * p.M * p.N;
+              for (int j = 0; j < 16; ++j) {
+                const int m = m0 + c + j;
+                if (c + j < cols) {
+                  float y = v[j];
+                  if (p.residual) y = bf16r(y) + __bfloat162float(p.residual[static_cast<size_t>(m) * p.ldr + n]);
+                  p.out_bf16[static_cast<size_t>(m) * p.ldc + n] = __float2bfloat16(y);
+                }
+              }
+            }
+          } else {
+            float uu[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c + j;
-          if (m < p.M) base[static_cast<size_t>(m) * p.N + n] = v[j];
-        }
-      }
-    } else if constexpr (MODE == 1) {
-      if (n_ok) {
+            for (int j = 0; j < 16; ++j) uu[j] = __shfl_down_sync(0xffffffffu, v[j], 16);
+            if (lane < 16 && 2 * hcol < p.N) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c + j;
-          if (m < p.M) {
-            float y = v[j];
-            if (p.residual) y = bf16r(y) + __bfloat162float(p.residual[static_cast<size_t>(m) * p.ldr + n]);
-            p.out_bf16[static_cast<size_t>(m) * p.ldc + n] = __float2bfloat16(y);
-          }
-        }
-      }
-    }
-  }
-  if constexpr (MODE == 2) {
-    // ------------------------------------------------- MODE 2: per-tile top-KT
-    // The accumulator is copied, transposed, into the idle pipeline stages
-    // ([column][129] floats: the padding keeps both the row-wise writes and
-    // the column-wise scans bank-conflict free); then every thread scans
-    // whole token columns on its own, so there is no cross-lane dependency
-    // chain.  Columns are processed in groups that fit the stage area.
-    float* tile = reinterpret_cast<float*>(smem);
-    constexpr int LDT = GBN + 1;
-    const int avail = stages * stage_bytes / (LDT * 4);
-    const int group = avail >= bt ? bt : (avail / 16) * 16;
-    for (int g0 = 0; g0 < bt; g0 += group) {
-      const int g1 = min(bt, g0 + group);
-      for (int c = g0; c < g1; c += 16) {
-        float v[16];
-        tmem_ld16(t_row + c, v);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) tile[(c - g0 + j) * LDT + row] = (live && n_ok) ? v[j] : -INFINITY;
-      }
-      __syncthreads();
-      for (int j = g0 + threadIdx.x; j < g1; j += blockDim.x) {
-        const int m = m0 + j;
-        if (m >= p.M) continue;
-        const float* col = tile + (j - g0) * LDT;
-        float bv[KT];
-        int bi[KT];
-#pragma unroll
-        for (int r = 0; r < KT; ++r) {
-          bv[r] = -INFINITY;
-          bi[r] = 0x7fffffff;
-        }
-#pragma unroll 8
-        for (int rr = 0; rr < GBN; ++rr) {
-          float x = col[rr];
-          if (x > bv[KT - 1]) {   // strict: equal values keep the lower row
-            int xi = n0 + rr;
-#pragma unroll
-            for (int q = 0; q < KT; ++q) {
-              if (x > bv[q]) {
-                const float t1 = bv[q];
-                const int t2 = bi[q];
-                bv[q] = x;
-                bi[q] = xi;
-                x = t1;
-                xi = t2;
+              for (int j = 0; j < 16; ++j) {
+                const int m = m0 + c + j;
+                if (c + j < cols) {
+                  const float g = bf16r(v[j]);
+                  const float sl = bf16r(g / (1.f + expf(-g)));
+                  p.out_bf16[static_cast<size_t>(m) * p.ldc + hcol] = __float2bfloat16(sl * bf16r(uu[j]));
+                }
               }
             }
           }
         }
-        const size_t o = (static_cast<size_t>(m) * p.ntiles + blockIdx.x) * KT;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[a]);
+      } else {
+        // ------------------------------------------ MODE 2: per-tile top-KT
+        // Per token column: KT rounds of a warp max (redux.sync on an
+        // order-preserving key) over the warp's 32 rows, the lowest row
+        // winning ties.  The four warps' candidates go to a shared-memory
+        // merge area (double-buffered by unit); warp 2 merges them, one
+        // column per lane, and writes the tile's top-KT.  The hand-offs are
+        // mbarriers with bounded waits, never an unbounded named barrier.
+        const int cols = min(bt, p.M - m0);
+        const int b2 = ti & 1, use2 = ti >> 1;
+        float* mv = mval + b2 * marea;
+        int* mi = midx + b2 * marea;
+        if (!mbar_wait(&mempty[b2], (use2 & 1) ^ 1, lim)) {
+          fail(ERR_TIMEOUT_EPILOGUE);
+          break;
+        }
+        for (int c = 0; c < cols; c += 16) {
+          float v[16];
+          tmem_ld16(tacc + c, v);
 #pragma unroll
-        for (int r = 0; r < KT; ++r) {
-          p.topv[o + r] = bv[r];
-          p.topi[o + r] = bi[r] < p.N ? bi[r] : 0x7fffffff;
+          for (int j = 0; j < 16; ++j) {
+            uint32_t key = n_ok ? float_key(v[j]) : 0u;
+#pragma unroll
+            for (int r = 0; r < KT; ++r) {
+              const uint32_t mx = __reduce_max_sync(0xffffffffu, key);
+              const uint32_t win = __ballot_sync(0xffffffffu, key == mx && mx != 0u);
+              const int wl = win ? __ffs(win) - 1 : 0;
+              if (lane == 0) {
+                const int o = (q * bt + c + j) * KT + r;
+                mv[o] = mx ? key_float(mx) : -INFINITY;
+                mi[o] = mx ? n0 + q * 32 + wl : 0x7fffffff;
+              }
+              if (lane == wl && win) key = 0u;
+            }
+          }
+        }
+        // TMEM is free once every lane's loads are done
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&acce[a]);
+          mbar_arrive(&mfull[b2]);   // release semantics publish the candidates
+        }
+        if (warp == 2) {
+          if (!mbar_wait(&mfull[b2], use2 & 1, lim)) {
+            fail(ERR_TIMEOUT_EPILOGUE);
+            break;
+          }
+          for (int j = lane; j < cols; j += 32) {
+            float bv[KT];
+            int bi[KT];
+#pragma unroll
+            for (int r = 0; r < KT; ++r) {
+              bv[r] = -INFINITY;
+              bi[r] = 0x7fffffff;
+            }
+            for (int w = 0; w < 4; ++w) {
+#pragma unroll
+              for (int r = 0; r < KT; ++r) {
+                float x = mv[(w * bt + j) * KT + r];
+                int xi = mi[(w * bt + j) * KT + r];
+#pragma unroll
+                for (int z = 0; z < KT; ++z) {
+                  if (x > bv[z] || (x == bv[z] && xi < bi[z])) {
+                    const float t1 = bv[z];
+                    const int t2 = bi[z];
+                    bv[z] = x;
+                    bi[z] = xi;
+                    x = t1;
+                    xi = t2;
+                  }
+                }
+              }
+            }
+            const size_t o = (static_cast<size_t>(m0 + j) * p.ntiles + u.n_t) * KT;
+#pragma unroll
+            for (int r = 0; r < KT; ++r) {
+              p.topv[o + r] = bv[r];
+              p.topi[o + r] = bi[r] < p.N ? bi[r] : 0x7fffffff;
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&mempty[b2]);
         }
       }
-      __syncthreads();
     }
   }
 
   // ---------------------------------------------------------------- teardown
-  tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && flags[2]) {
+  if (threadIdx.x == 32) {
+    // every MMA this thread issued has retired before TMEM is released
+    umma_commit(done);
+    if (!mbar_wait(done, 0, lim)) set_error(p.status, ERR_TIMEOUT_MMA);
+  }
+  if (threadIdx.x == 0 && flags[0]) {
     // drain TMA loads that were issued but never consumed, so no copy lands
     // in shared memory after the CTA has exited
-    for (int i = flags[1]; i < flags[0]; ++i) mbar_wait(&full[i % stages], (i / stages) & 1, lim);
+    for (int i = flags[2]; i < flags[1]; ++i) mbar_wait(&full[i % stages], (i / stages) & 1, lim);
   }
+  tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, tmem_cols);
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, tmem_cols);
 }
 
 // ------------------------------------------------------------------ host side
@@ -305,8 +441,9 @@ void make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64
 // shared memory each) stream weights at 85-92% of HBM bandwidth where one CTA
 // with a 12-stage pipeline reaches ~50%, so small token tiles use the 110 KB
 // budget whenever it still holds >= 4 stages; large tiles (compute-heavy) use
-// one CTA with ~220 KB.  D3D_GEMM_SMEM_KB / D3D_GEMM_MAX_STAGES override.
-int gemm_stages(int bt) {
+// one CTA with ~220 KB.  ``reserve`` bytes (the top-k merge areas) come off
+// the budget.  D3D_GEMM_SMEM_KB / D3D_GEMM_MAX_STAGES override.
+static int stages_for(int bt, int reserve) {
   static const int env_kb = [] {
     const char* e = std::getenv("D3D_GEMM_SMEM_KB");
     return e ? std::atoi(e) : 0;
@@ -316,28 +453,45 @@ int gemm_stages(int bt) {
     return e ? std::atoi(e) : 16;
   }();
   const int stage_bytes = A_TILE_BYTES + bt * GBK * 2;
-  const int budget_kb = env_kb > 0 ? env_kb : ((110 * 1024) / stage_bytes >= 4 ? 110 : 220);
-  int s = (budget_kb * 1024) / stage_bytes;
+  const int small = 110 * 1024 - reserve;
+  const int budget = env_kb > 0 ? env_kb * 1024 - reserve : (small / stage_bytes >= 4 ? small : 220 * 1024 - reserve);
+  int s = budget / stage_bytes;
   if (s > max_stages) s = max_stages;
   return s < 2 ? 2 : s;
 }
 
+int gemm_stages(int bt) { return stages_for(bt, 0); }
+
+static size_t smem_bytes(int bt, int stages, int reserve) {
+  const int stage_bytes = A_TILE_BYTES + bt * GBK * 2;
+  return 1024 + static_cast<size_t>(stages) * stage_bytes + reserve + (2 * stages + 9) * 8 + 32;
+}
+
+size_t gemm_smem_bytes(int bt, int stages) { return smem_bytes(bt, stages, 0); }
+
 int gemm_ctas_per_sm(int bt) { return gemm_smem_bytes(bt, gemm_stages(bt)) <= 114 * 1024 ? 2 : 1; }
 
-size_t gemm_smem_bytes(int bt, int stages) {
-  const int stage_bytes = A_TILE_BYTES + bt * GBK * 2;
-  return 1024 + static_cast<size_t>(stages) * stage_bytes + (2 * stages + 1) * 8 + 32;
+static int num_sms() {
+  static int n = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  return n;
 }
 
 template <int MODE, int KT>
-static void launch_mode(const CUtensorMap& tw, const CUtensorMap& tx, GemmParams p, dim3 grid, size_t smem,
+static void launch_mode(const CUtensorMap& tw, const CUtensorMap& tx, GemmParams p, int units, size_t smem,
                         cudaStream_t st) {
   static bool attr_set = false;  // per template instance
   if (!attr_set) {
     cudaFuncSetAttribute(gemm_tn_kernel<MODE, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     attr_set = true;
   }
-  launch_pdl(gemm_tn_kernel<MODE, KT>, grid, dim3(128), smem, st, tw, tx, p);
+  const int per_sm = smem <= 114 * 1024 ? 2 : 1;
+  int grid = num_sms() * per_sm;
+  if (grid > units) grid = units;
+  launch_pdl(gemm_tn_kernel<MODE, KT>, dim3(grid), dim3(GEMM_THREADS), smem, st, tw, tx, p);
 }
 
 void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
@@ -356,6 +510,9 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
     make_tmap_bf16_2d(&tw, a.w, a.K, a.N, a.ldw, GBK, GBN);
   }
   make_tmap_bf16_2d(&tx, a.x, a.K, a.M, a.ldx, GBK, a.bt > 256 ? a.bt / 2 : a.bt);
+  const int kt = a.mode == 2 ? (a.topk <= 1 ? 1 : (a.topk <= 2 ? 2 : 4)) : 1;
+  if (a.mode == 2 && a.topk > 4) throw std::runtime_error("gemm: fused top-k supports k <= 4");
+  const int reserve = a.mode == 2 ? 2 * 4 * a.bt * kt * 8 : 0;
   GemmParams p{};
   p.M = a.M;
   p.N = a.N;
@@ -368,22 +525,27 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   p.topv = a.topv;
   p.topi = a.topi;
   p.bt = a.bt;
+  p.splits = a.splits;
   p.w_packed = a.w_packed;
-  p.stages = gemm_stages(a.bt);
+  p.stages = stages_for(a.bt, reserve);
   p.status = a.status;
   p.timeout_ns = a.timeout_ns;
   const int ntn = (a.N + GBN - 1) / GBN;
   p.ntiles = ntn;
-  dim3 grid(ntn, (a.M + a.bt - 1) / a.bt, a.splits);
-  const size_t smem = gemm_smem_bytes(a.bt, p.stages);
+  const int units = ntn * ((a.M + a.bt - 1) / a.bt) * a.splits;
+  const size_t smem = smem_bytes(a.bt, p.stages, reserve);
+  if (smem > 232448) throw std::runtime_error("gemm: shared memory budget exceeded");
   switch (a.mode) {
-    case 0: launch_mode<0, 1>(tw, tx, p, grid, smem, stream); break;
-    case 1: launch_mode<1, 1>(tw, tx, p, grid, smem, stream); break;
+    case 0: launch_mode<0, 1>(tw, tx, p, units, smem, stream); break;
+    case 1: launch_mode<1, 1>(tw, tx, p, units, smem, stream); break;
     case 2:
-      if (a.topk == 1) launch_mode<2, 1>(tw, tx, p, grid, smem, stream);
-      else if (a.topk == 2) launch_mode<2, 2>(tw, tx, p, grid, smem, stream);
-      else if (a.topk <= 4) launch_mode<2, 4>(tw, tx, p, grid, smem, stream);
-      else throw std::runtime_error("gemm: fused top-k supports k <= 4");
+      if (kt == 1) launch_mode<2, 1>(tw, tx, p, units, smem, stream);
+      else if (kt == 2) launch_mode<2, 2>(tw, tx, p, units, smem, stream);
+      else launch_mode<2, 4>(tw, tx, p, units, smem, stream);
+      break;
+    case 3:
+      if (a.N % GBN) throw std::runtime_error("gemm: SwiGLU epilogue needs 2*I to be a multiple of 128");
+      launch_mode<3, 1>(tw, tx, p, units, smem, stream);
       break;
     default: throw std::runtime_error("gemm: bad mode");
   }

@@ -9,7 +9,7 @@ namespace d3d {
 void add_rmsnorm(const float* part, int nsplit, __nv_bfloat16* residual, const __nv_bfloat16* w, __nv_bfloat16* out,
                  int M, int N, float eps, cudaStream_t st);
 
-void swiglu(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, cudaStream_t st);
+void swiglu(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, bool interleaved, cudaStream_t st);
 
 struct QkvRopeArgs {
   const float* part;        // [nsplit][M][(Hq+2Hkv)*D] fp32 partials, or null

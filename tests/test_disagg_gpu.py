@@ -57,7 +57,7 @@ def _worker(rank, port, out_path):
         cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=48, ignore_eos=True)
         if rank == 0:
             tw = FastWeights.from_module(build_model(tiny_target(), seed=0), dev)
-            srv = target_server(tw, link, max_seqs=4, max_context=512, device=dev)
+            srv = target_server(tw, link, max_seqs=4, max_context=512, device=dev, deadline_s=60)
             ar = ar_generate(srv.be, prompts, 48, ignore_eos=True)["outputs"]
             dist.broadcast_object_list([ar], src=0)
             srv.serve()
@@ -67,7 +67,8 @@ def _worker(rank, port, out_path):
             dist.broadcast_object_list(box, src=0)
             ar = box[0]
             dw = FastWeights.from_module(build_model(tiny_drafter(cond=True), seed=1), dev)
-            eng = D3DEngine.from_remote_target(dw, link, 128, cfg, max_seqs=4, max_context=512, device=dev)
+            eng = D3DEngine.from_remote_target(dw, link, 128, cfg, max_seqs=4, max_context=512, device=dev,
+                                               deadline_s=60)
             res = eng.generate(prompts, concurrency=2)
             eng.close()
             other = [None]

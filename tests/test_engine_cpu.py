@@ -70,3 +70,23 @@ def test_sampling_runs(pair):
     for o in res["outputs"]:
         assert len(o.tokens) == 24
         assert all(0 <= x < 1024 for x in o.tokens)
+
+
+def test_gate_up_interleave_order():
+    """The interleaved gate|up row order is a permutation that puts gate row
+    64t+16w+j and its up row in lanes j and j+16 of warp w of tile t."""
+    from d3d_b200 import ops
+    i = 384
+    order = ops.gate_up_order(i)
+    assert sorted(order.tolist()) == list(range(2 * i))
+    for t in range(2 * i // 128):
+        for w in range(4):
+            for j in range(16):
+                r = 128 * t + 32 * w + j
+                assert order[r] == 64 * t + 16 * w + j
+                assert order[r + 16] == i + 64 * t + 16 * w + j
+    g = torch.randn(i, 64).to(torch.bfloat16)
+    u = torch.randn(i, 64).to(torch.bfloat16)
+    pw = ops.pack_gate_up(g, u)
+    full = torch.cat([g, u], 0)
+    assert torch.equal(pw.unpack(), full[order])

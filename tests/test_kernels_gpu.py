@@ -124,6 +124,49 @@ def test_swiglu(E):
     assert (h.float() - ref).abs().max().item() < 0.05
 
 
+@pytest.mark.parametrize("m,i,k,bt", [(1, 384, 128, 16), (16, 6144, 2048, 16), (272, 6144, 2048, 96),
+                                       (300, 1024, 512, 288)])
+def test_gemm_swiglu_epilogue(E, m, i, k, bt):
+    """SwiGLU in the GEMM epilogue (interleaved gate|up weight) equals the
+    split-1 partial GEMM followed by the interleaved SwiGLU kernel, and tracks
+    the fp32 reference silu(x g^T) * (x u^T)."""
+    from d3d_b200 import ops
+    x = _bf(m, k, seed=31)
+    g, u = _bf(i, k, scale=0.05, seed=32), _bf(i, k, scale=0.05, seed=33)
+    w = ops.pack_gate_up(g, u)
+    h = torch.empty(m, i, dtype=torch.bfloat16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.gemm_swiglu(x, w, h, bt, status)
+    part = torch.empty(1, m, 2 * i, device="cuda")
+    ops.gemm_partial(x, w, part, 1, bt)
+    h2 = torch.empty_like(h)
+    E.swiglu(part, 1, h2, True)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(h, h2)
+    gf = (x.float() @ g.float().t()).to(torch.bfloat16).float()
+    uf = (x.float() @ u.float().t()).to(torch.bfloat16).float()
+    ref = torch.nn.functional.silu(gf).to(torch.bfloat16).float() * uf
+    assert (h.float() - ref).abs().max().item() < 0.02 * max(1.0, ref.abs().max().item())
+
+
+def test_swiglu_interleaved_splits(E):
+    from d3d_b200 import ops
+    m, i, k = 9, 512, 256
+    x = _bf(m, k, seed=34)
+    g, u = _bf(i, k, scale=0.05, seed=35), _bf(i, k, scale=0.05, seed=36)
+    part = torch.empty(3, m, 2 * i, device="cuda")
+    ops.gemm_partial(x, ops.pack_gate_up(g, u), part, 3)
+    h = torch.empty(m, i, dtype=torch.bfloat16, device="cuda")
+    E.swiglu(part, 3, h, True)
+    order = ops.gate_up_order(i).cuda()
+    plain = torch.empty_like(part)
+    plain[:, :, order] = part
+    h2 = torch.empty_like(h)
+    E.swiglu(plain, 3, h2, False)
+    assert torch.equal(h, h2)
+
+
 @pytest.mark.parametrize("D", [32, 128])
 def test_qkv_rope_kv(E, D):
     from d3d_b200.models.qwen3 import rope_cos_sin, rotate_half
