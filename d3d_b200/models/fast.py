@@ -22,6 +22,7 @@ replayed.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
 
@@ -230,12 +231,12 @@ class StepBuffers:
         self.q = torch.zeros(T, cfg.num_attention_heads, d, dtype=torch.bfloat16, device=dev)
         self.attn = torch.zeros(T, cfg.q_size, dtype=torch.bfloat16, device=dev)
         self.h = torch.zeros(T, cfg.intermediate_size, dtype=torch.bfloat16, device=dev)
-        sp = {g: (v[1] if isinstance(v, tuple) else v) for g, v in splits.items()}
         width = dict(qkv=cfg.q_size + 2 * cfg.kv_size, o=h, gate_up=2 * cfg.intermediate_size, down=h)
-        # fp32 split-K partials only for GEMMs that split; the others write bf16 directly
-        nmax = max([sp[g] * width[g] for g in width if sp[g] > 1] + [1])
+        pl = {g: (v if isinstance(v, tuple) else (0, v, False)) for g, v in splits.items() if g in width}
+        # fp32 split-K partials for the GEMMs that reduce partials; direct ones write bf16
+        nmax = max([pl[g][1] * width[g] for g in width if not pl[g][2]] + [1])
         self.part = torch.zeros(nmax * T, dtype=torch.float32, device=dev)
-        self.qkv = torch.zeros(T if sp["qkv"] == 1 else 1, width["qkv"], dtype=torch.bfloat16, device=dev)
+        self.qkv = torch.zeros(T if pl["qkv"][2] else 1, width["qkv"], dtype=torch.bfloat16, device=dev)
         self.att_o = torch.zeros(n_chunks * T * cfg.num_attention_heads * d if n_chunks > 1 else 1,
                                  dtype=torch.float32, device=dev)
         self.att_ml = torch.zeros(n_chunks * T * cfg.num_attention_heads * 2 if n_chunks > 1 else 1,
@@ -272,39 +273,127 @@ class FastRunner:
         self.scale = 1.0 / math.sqrt(c.head_dim)
         self._bufs: Dict[Tuple, StepBuffers] = {}
         self._graphs: Dict[Tuple, torch.cuda.CUDAGraph] = {}
-        self.tuned: Dict[int, Dict[str, Tuple[int, int]]] = {}
+        self.tuned: Dict[int, Dict[str, object]] = {}
 
     # ------------------------------------------------------------- policies
     GEMMS = ("qkv", "o", "gate_up", "down")
 
-    def plan(self, T: int) -> Dict[str, Tuple[int, int]]:
-        """(token tile, split-K) per GEMM of a T-token forward.
+    def _shapes(self) -> Dict[str, Tuple[int, int]]:
+        c = self.cfg
+        return dict(qkv=(c.q_size + 2 * c.kv_size, c.hidden_size), o=(c.hidden_size, c.q_size),
+                    gate_up=(2 * c.intermediate_size, c.hidden_size),
+                    down=(c.hidden_size, c.intermediate_size))
+
+    def plan(self, T: int, tune: bool = False) -> Dict[str, Tuple[int, int, bool]]:
+        """(token tile, split-K, direct) per GEMM of a T-token forward, plus the
+        LM head's token tile under ``"lm_bt"``.
 
         Batch-invariant runners (the target) take the split from the weight
         shape alone for decode-sized T, so a token's reduction order does not
-        depend on how many tokens share the forward.  Other runners (the
-        drafter) use ``self.tuned`` -- per-T plans measured on the device --
-        when present, else the wave-filling heuristic.  A split of 1 makes the
-        GEMM write bf16 directly (residual add / SwiGLU in its epilogue); the
-        rounding is the same as reducing one partial."""
-        c = self.cfg
-        shapes = dict(qkv=(c.q_size + 2 * c.kv_size, c.hidden_size), o=(c.hidden_size, c.q_size),
-                      gate_up=(2 * c.intermediate_size, c.hidden_size),
-                      down=(c.hidden_size, c.intermediate_size))
+        depend on how many tokens share the forward, and always reduce fp32
+        partials.  Other runners (the drafter) measure their plan on the
+        device when decode buffers for a new T are made (``tune``;
+        :meth:`_autotune`, off with D3D_AUTOTUNE=0), else use the
+        wave-filling heuristic (prefill).
+        ``direct`` GEMMs write bf16 themselves (residual add / SwiGLU in the
+        epilogue; same rounding as reducing one partial)."""
         bt = ops.bt_for(T)
+        shapes = self._shapes()
         if self.batch_invariant:
             if T > 256:
-                return {g: (bt, 1) for g in self.GEMMS}
-            return {g: (bt, ops.splitk_for(n, k, mtiles=1, bt=16)) for g, (n, k) in shapes.items()}
+                pl = {g: (bt, 1, False) for g in self.GEMMS}
+            else:
+                pl = {g: (bt, ops.splitk_for(n, k, mtiles=1, bt=16), False) for g, (n, k) in shapes.items()}
+            pl["lm_bt"] = bt
+            return pl
+        if tune and T not in self.tuned and 64 <= T <= 2048 and os.environ.get("D3D_AUTOTUNE", "1") != "0" \
+                and torch.cuda.is_available() and not torch.cuda.is_current_stream_capturing():
+            self.tuned[T] = self._autotune(T)
         if T in self.tuned:
             return dict(self.tuned[T])
         if T > 2048:
-            return {g: (bt, 1) for g in self.GEMMS}
-        mt = math.ceil(T / bt)
-        return {g: (bt, ops.splitk_for(n, k, mtiles=mt, bt=bt, m=T)) for g, (n, k) in shapes.items()}
+            pl = {g: (bt, 1, False) for g in self.GEMMS}
+        else:
+            mt = math.ceil(T / bt)
+            pl = {g: (bt, ops.splitk_for(n, k, mtiles=mt, bt=bt, m=T), False) for g, (n, k) in shapes.items()}
+        pl["lm_bt"] = bt
+        return pl
+
+    @torch.no_grad()
+    def _autotune(self, T: int, reps: int = 6) -> Dict[str, object]:
+        """Time candidate (token tile, split-K, direct) configurations of each
+        GEMM at T tokens on this device and keep the fastest.  Weights cycle
+        over the model's layers so every timed launch streams from HBM; a
+        partial-reducing configuration is charged for reading its partials
+        back (at 6 TB/s)."""
+        E = ops.ext()
+        dev = self.device
+        L = self.w.layers
+        shapes = self._shapes()
+        maxk = max(k for _, k in shapes.values())
+        maxn = max(n for n, _ in shapes.values())
+        x = (torch.randn(T, maxk, device=dev) * 0.1).to(torch.bfloat16)
+        part = torch.empty(16 * T * maxn, device=dev)
+        yb = torch.zeros(T, maxn, dtype=torch.bfloat16, device=dev)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+        def timed(fn):
+            fn(0)
+            fn(1)
+            e0.record()
+            for i in range(reps):
+                fn(i + 2)
+            e1.record()
+            e1.synchronize()
+            return e0.elapsed_time(e1) / reps * 1e-3
+
+        base = ops.bt_for(T)
+        bts = sorted({b for b in (base, ops.bt_for((T + 1) // 2), ops.bt_for((T + 2) // 3), 96, 64, 48, 32)
+                      if b <= max(base, 16)}, reverse=True)
+        plan: Dict[str, object] = {}
+        for g, (n, k) in shapes.items():
+            w = lambda i: getattr(L[i % len(L)], g)
+            xk = x[:, :k]
+            kb = math.ceil(k / 64)
+            best = None
+            for bt in bts:
+                for s in range(1, 17):
+                    if kb // s < 4:
+                        break
+                    t = timed(lambda i: E.gemm_partial(xk, w(i).data, part, s, bt, st, n))
+                    t += s * T * n * 4 / 6e12
+                    if best is None or t < best[0]:
+                        best = (t, bt, s, False)
+                if g == "gate_up":
+                    h = yb[:, : n // 2]
+                    t = timed(lambda i: E.gemm_swiglu(xk, w(i).data, h, bt, st, n))
+                else:
+                    t = timed(lambda i: E.gemm_bf16(xk, w(i).data, yb[:, :n], None, bt, st, n))
+                if t < best[0]:
+                    best = (t, bt, 1, True)
+            plan[g] = best[1:]
+        if self.w.lm_head is not None:
+            lm = self.w.lm_head
+            nt = math.ceil(lm.n / 128)
+            tv = torch.empty(T * nt * 2, device=dev)
+            ti = torch.empty(T * nt * 2, dtype=torch.int32, device=dev)
+            xh = x[:, : self.cfg.hidden_size]
+            best = None
+            for bt in sorted({base, ops.bt_for((T + 1) // 2), ops.bt_for((T + 2) // 3)}):
+                t = timed(lambda i: E.gemm_topk(xh, lm.data, tv, ti, 2, bt, st, lm.n))
+                if best is None or t < best[0]:
+                    best = (t, bt)
+            plan["lm_bt"] = best[1]
+        else:
+            plan["lm_bt"] = base
+        torch.cuda.synchronize()
+        if int(st.item()) != 0:
+            raise RuntimeError(f"GEMM autotune: kernel reported error {int(st.item())}")
+        return plan
 
     def splits(self, T: int) -> Dict[str, int]:
-        return {g: v[1] for g, v in self.plan(T).items()}
+        return {g: v[1] for g, v in self.plan(T).items() if g in self.GEMMS}
 
     def buffers(self, B: int, Q: int, topk: int, prefill: bool = False) -> StepBuffers:
         key = (B, Q, topk, prefill)
@@ -313,7 +402,7 @@ class FastRunner:
             T = B * Q
             chunk = self.chunk_for(prefill)
             nch = max(1, math.ceil(self.max_context / chunk))
-            b = StepBuffers(self.cfg, B, Q, topk, nch, self.plan(T), self.device)
+            b = StepBuffers(self.cfg, B, Q, topk, nch, self.plan(T, tune=not prefill), self.device)
             b.bt_view = torch.zeros(B, self.kv.max_pages_per_seq, dtype=torch.int32, device=self.device)
             b.chunk = chunk
             self._bufs[key] = b
@@ -345,8 +434,8 @@ class FastRunner:
         n = 3
         eps = c.rms_norm_eps
         for li, L in enumerate(w.layers):
-            gbt, s = pl["qkv"]
-            if s == 1:
+            gbt, s, direct = pl["qkv"]
+            if direct:
                 E.gemm_bf16(b.xn, L.qkv.data, b.qkv, None, gbt, b.status, L.qkv.n)
                 E.qkv_rope_kv(None, b.qkv, 1, L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
                               b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps)
@@ -359,15 +448,15 @@ class FastRunner:
                         b.att_o if b.n_chunks > 1 else None, b.att_ml if b.n_chunks > 1 else None,
                         b.attn)
             n += 3 + (1 if b.n_chunks > 1 else 0)
-            gbt, s = pl["o"]
-            if s == 1:   # residual added in the epilogue, in place
+            gbt, s, direct = pl["o"]
+            if direct:   # residual added in the epilogue, in place
                 E.gemm_bf16(b.attn, L.o.data, b.x, b.x, gbt, b.status, L.o.n)
                 E.add_rmsnorm(None, 1, b.x, L.post_norm, b.xn, eps)
             else:
                 E.gemm_partial(b.attn, L.o.data, b.part, s, gbt, b.status, L.o.n)
                 E.add_rmsnorm(b.part, s, b.x, L.post_norm, b.xn, eps)
-            gbt, s = pl["gate_up"]
-            if s == 1:
+            gbt, s, direct = pl["gate_up"]
+            if direct:
                 E.gemm_swiglu(b.xn, L.gate_up.data, b.h, gbt, b.status, L.gate_up.n)
                 n += 3
             else:
@@ -375,8 +464,8 @@ class FastRunner:
                 E.swiglu(b.part, s, b.h, True)
                 n += 4
             nxt = w.layers[li + 1].in_norm if li + 1 < len(w.layers) else w.final_norm
-            gbt, s = pl["down"]
-            if s == 1:
+            gbt, s, direct = pl["down"]
+            if direct:
                 E.gemm_bf16(b.h, L.down.data, b.x, b.x, gbt, b.status, L.down.n)
                 E.add_rmsnorm(None, 1, b.x, nxt, b.xn, eps)
             else:
@@ -384,7 +473,7 @@ class FastRunner:
                 E.add_rmsnorm(b.part, s, b.x, nxt, b.xn, eps)
             n += 2
         if b.topk > 0:
-            E.gemm_topk(b.xn, w.lm_head.data, b.tv, b.ti, b.topk, bt, b.status, w.lm_head.n)
+            E.gemm_topk(b.xn, w.lm_head.data, b.tv, b.ti, b.topk, pl["lm_bt"], b.status, w.lm_head.n)
             E.topk_merge(b.tv, b.ti, T, b.ntiles, b.kt, b.topk, b.top_v, b.top_i)
         n += 2 if b.topk > 0 else 0
         return n + (1 if cond is not None else 0)

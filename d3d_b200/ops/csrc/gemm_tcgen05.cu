@@ -488,8 +488,14 @@ static void launch_mode(const CUtensorMap& tw, const CUtensorMap& tx, GemmParams
     cudaFuncSetAttribute(gemm_tn_kernel<MODE, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448);
     attr_set = true;
   }
+  // persistent grid (one CTA per resident slot) unless D3D_GEMM_GRID=units
+  // asks for one CTA per work unit
+  static const bool per_unit = [] {
+    const char* e = std::getenv("D3D_GEMM_GRID");
+    return e && std::string(e) == "units";
+  }();
   const int per_sm = smem <= 114 * 1024 ? 2 : 1;
-  int grid = num_sms() * per_sm;
+  int grid = per_unit ? units : num_sms() * per_sm;
   if (grid > units) grid = units;
   launch_pdl(gemm_tn_kernel<MODE, KT>, dim3(grid), dim3(GEMM_THREADS), smem, st, tw, tx, p);
 }
