@@ -359,7 +359,7 @@ class FastRunner:
             best = None
             for bt in bts:
                 for s in range(1, 17):
-                    if kb // s < 4:
+                    if s > 1 and kb // s < 4:
                         break
                     t = timed(lambda i: E.gemm_partial(xk, w(i).data, part, s, bt, st, n))
                     t += s * T * n * 4 / 6e12
