@@ -18,10 +18,13 @@ import torch
 from . import build as _build
 
 _EXT = None
+_EXT_OVERRIDE = None   # instrumentation hook (benchmarks.ablate): stands in for the extension
 
 
 def ext():
     global _EXT
+    if _EXT_OVERRIDE is not None:
+        return _EXT_OVERRIDE
     if _EXT is None:
         try:
             _EXT = _build.load()
