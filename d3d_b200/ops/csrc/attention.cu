@@ -19,6 +19,8 @@
 // per-row arithmetic do not depend on how many queries share a launch, a
 // row's output is bit-identical whether it is verified in a block of 16 or
 // decoded alone — required for greedy token identity with AR decoding.
+#include <stdexcept>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -379,7 +381,7 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 }
 
 template <int D>
-static void launch_attn(const AttnArgs& a, cudaStream_t st) {
+static void launch_attn_split(const AttnArgs& a, cudaStream_t st) {
   constexpr int LD = D + 8;
   const size_t smem = static_cast<size_t>(AT_ROWS + 2 * AT_KEYS) * LD * 2;
   static bool attr = false;
@@ -396,22 +398,430 @@ static void launch_attn(const AttnArgs& a, cudaStream_t st) {
   }
 }
 
-void attention(const AttnArgs& a, cudaStream_t st) {
+// Split-KV attention with fp32 partials and a combine kernel (used by the
+// allocation-free entry point, which supplies the partial buffers itself).
+void attention_split(const AttnArgs& a, cudaStream_t st) {
   if (a.B == 0 || a.q_len == 0) return;
   switch (a.head_dim) {
-    case 32: launch_attn<32>(a, st); break;
-    case 64: launch_attn<64>(a, st); break;
-    case 128: launch_attn<128>(a, st); break;
+    case 32: launch_attn_split<32>(a, st); break;
+    case 64: launch_attn_split<64>(a, st); break;
+    case 128: launch_attn_split<128>(a, st); break;
     default: break;
   }
 }
 
+
+// ===========================================================================
+// Cluster attention (the default path).
+//
+// A thread-block cluster of CL = 8 CTAs owns one (row tile, sequence, kv
+// head).  Keys are cut into chunks of 64 slots at fixed absolute boundaries;
+// chunk c belongs to the CTA of cluster rank c % CL, which runs its chunks in
+// increasing order through the same mma.sync online softmax as above, with
+// an NT-deep ring of cp.async K/V tiles so several tiles are in flight.  The
+// CTAs then merge their (m, l, O) states through distributed shared memory:
+// rank r combines rows 8r..8r+7 over ranks 0..7 in rank order and writes the
+// bf16 output.  No fp32 partials reach HBM and there is no second launch.
+// Every reduction order is a function of absolute key positions only, so a
+// row's output is the same whatever else shares the launch (batch
+// invariance), as with the split path.
+// ===========================================================================
+constexpr int CL = 8;
+constexpr int CL_MAX_PAGES = 1024;   // page ids of one CTA's chunks
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 ld_dsmem2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int D, int NT>
+__global__ void __launch_bounds__(128, 1) attn_cluster_kernel(const AttnArgs a) {
+  griddep_launch();
+  constexpr int LD = D + 8;
+  extern __shared__ __align__(16) uint8_t smem[];
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem);
+  __nv_bfloat16* ring = Qs + AT_ROWS * LD;  // NT x {K [64][LD], V [64][LD]}
+  // after the key loop the ring holds this CTA's state: O [64][D], m [64], l [64] (fp32)
+  float* red_o = reinterpret_cast<float*>(ring);
+  float* red_m = red_o + AT_ROWS * D;
+  float* red_l = red_m + AT_ROWS;
+  __shared__ int s_rows[AT_ROWS][3];
+  __shared__ int s_range[3];
+  __shared__ int s_pages[CL_MAX_PAGES];
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = a.Hq / a.Hkv;
+  const int b = blockIdx.y / a.Hkv, h = blockIdx.y % a.Hkv;
+  const int rank = static_cast<int>(cluster_rank());
+  const int R0 = blockIdx.x * AT_ROWS;
+  const int kv_end = a.kv_end[b];
+
+  // ---- rows: descriptors and the union of their key ranges
+  if (tid < AT_ROWS) {
+    const int R = R0 + tid;
+    const int t = R / g;
+    int lim = 0, lo = 0, hi = 0;
+    if (t < a.q_len) {
+      const int* rr = a.rows + static_cast<size_t>(b * a.q_len + t) * 3;
+      lim = min(rr[0], kv_end);
+      lo = rr[1];
+      hi = min(rr[2], kv_end);
+      if (hi <= lo) lo = hi = 0;
+    }
+    s_rows[tid][0] = lim;
+    s_rows[tid][1] = lo;
+    s_rows[tid][2] = hi;
+  }
+  if (tid == 0) {
+    s_range[0] = 0;
+    s_range[1] = 0x7fffffff;
+    s_range[2] = 0;
+  }
+  __syncthreads();
+  if (tid < AT_ROWS) {
+    atomicMax(&s_range[0], s_rows[tid][0]);
+    if (s_rows[tid][2] > s_rows[tid][1]) {
+      atomicMin(&s_range[1], s_rows[tid][1]);
+      atomicMax(&s_range[2], s_rows[tid][2]);
+    }
+  }
+  // ---- page ids of this CTA's chunks (chunk c = rank + CL * i, 64 / page_size pages each)
+  const int ppc = AT_KEYS / a.page_size;
+  const int nch = (kv_end + AT_KEYS - 1) / AT_KEYS;
+  int nmy = nch > rank ? (nch - rank + CL - 1) / CL : 0;
+  if (nmy * ppc > CL_MAX_PAGES) nmy = CL_MAX_PAGES / ppc;  // host rejects contexts this long
+  const int* bt = a.block_table + static_cast<size_t>(b) * a.bt_stride;
+  for (int idx = tid; idx < nmy * ppc; idx += 128) {
+    const int pg = (rank + CL * (idx / ppc)) * ppc + idx % ppc;
+    s_pages[idx] = pg < a.bt_stride ? bt[pg] : 0;
+  }
+  __syncthreads();
+  const int max_lim = s_range[0], min_lo = s_range[1], max_hi = s_range[2];
+  griddep_wait();
+
+  // ---- Q tile (its own cp.async group, ahead of the K/V tiles)
+  for (int c = tid; c < AT_ROWS * (D / 8); c += 128) {
+    const int r = c / (D / 8), dc = (c % (D / 8)) * 8;
+    const int R = R0 + r;
+    const int t = R / g;
+    if (t < a.q_len) {
+      const int qh = h * g + R % g;
+      cp_async16(smem_u32(Qs + r * LD + dc), a.q + (static_cast<size_t>(b * a.q_len + t) * a.Hq + qh) * D + dc);
+    } else {
+      *reinterpret_cast<uint4*>(Qs + r * LD + dc) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  cp_async_commit();
+
+  const int ra = warp * 16 + (lane >> 2), rb = ra + 8;
+  const int limA = s_rows[ra][0], loA = s_rows[ra][1], hiA = s_rows[ra][2];
+  const int limB = s_rows[rb][0], loB = s_rows[rb][1], hiB = s_rows[rb][2];
+  const uint32_t q_base = smem_u32(Qs + (warp * 16 + (lane & 15)) * LD + (lane >> 4) * 8);
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+  const float sl2 = a.scale * 1.4426950408889634f;  // scale * log2(e)
+
+  auto k0_of = [&](int i) { return (rank + CL * i) * AT_KEYS; };
+  auto needed = [&](int k0) { return k0 < max_lim || (k0 + AT_KEYS > min_lo && k0 < max_hi); };
+  auto next_needed = [&](int i) {
+    while (i < nmy && !needed(k0_of(i))) ++i;
+    return i;
+  };
+  auto load_tile = [&](int i, int buf) {
+    __nv_bfloat16* Ks = ring + buf * 2 * AT_KEYS * LD;
+    __nv_bfloat16* Vs = Ks + AT_KEYS * LD;
+    const int k0 = k0_of(i);
+    for (int c = tid; c < AT_KEYS * (D / 8); c += 128) {
+      const int kr = c / (D / 8), dc = (c % (D / 8)) * 8;
+      const int s = k0 + kr;
+      if (s < kv_end) {
+        const int64_t page = s_pages[i * ppc + kr / a.page_size];
+        const size_t off = ((page * a.page_size + s % a.page_size) * a.Hkv + h) * static_cast<size_t>(D) + dc;
+        cp_async16(smem_u32(Ks + kr * LD + dc), a.k_cache + off);
+        cp_async16(smem_u32(Vs + kr * LD + dc), a.v_cache + off);
+      } else {
+        *reinterpret_cast<uint4*>(Ks + kr * LD + dc) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(Vs + kr * LD + dc) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+
+  int cons = next_needed(0), iss = cons;
+#pragma unroll
+  for (int p = 0; p < NT; ++p) {
+    if (iss < nmy) {
+      load_tile(iss, p);
+      iss = next_needed(iss + 1);
+    }
+    cp_async_commit();
+  }
+  for (int j = 0; cons < nmy; ++j) {
+    cp_async_wait<NT - 1>();  // Q and tile j have landed
+    __syncthreads();
+    const __nv_bfloat16* Ks = ring + (j % NT) * 2 * AT_KEYS * LD;
+    const __nv_bfloat16* Vs = Ks + AT_KEYS * LD;
+    const int k0 = k0_of(cons);
+    const int kend = min(k0 + AT_KEYS, kv_end);
+
+    // ---- S = Q K^T (16 rows x 64 keys per warp)
+    float s[8][4];
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t qf[4];
+      ldsm_x4(q_base + kk * 32, qf[0], qf[1], qf[2], qf[3]);
+#pragma unroll
+      for (int nb = 0; nb < 8; nb += 2) {
+        const int key = nb * 8 + (lane & 7) + (lane >> 4) * 8;
+        const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(Ks + key * LD + col), b0, b1, b2, b3);
+        mma16816(s[nb], qf, b0, b1);
+        mma16816(s[nb + 1], qf, b2, b3);
+      }
+    }
+    // ---- mask + online softmax
+    float tmA = -INFINITY, tmB = -INFINITY;
+    const int k1e = k0 + AT_KEYS;
+    const bool fullA = k1e <= kend && (k1e <= limA || (k0 >= loA && k1e <= hiA));
+    const bool fullB = k1e <= kend && (k1e <= limB || (k0 >= loB && k1e <= hiB));
+    if (__all_sync(0xffffffffu, fullA && fullB)) {
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          s[nb][e] *= sl2;
+          s[nb][2 + e] *= sl2;
+          tmA = fmaxf(tmA, s[nb][e]);
+          tmB = fmaxf(tmB, s[nb][2 + e]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = k0 + nb * 8 + (lane & 3) * 2 + e;
+          const bool inb = key < kend;
+          s[nb][e] = (inb && visible(key, limA, loA, hiA)) ? s[nb][e] * sl2 : -INFINITY;
+          s[nb][2 + e] = (inb && visible(key, limB, loB, hiB)) ? s[nb][2 + e] * sl2 : -INFINITY;
+          tmA = fmaxf(tmA, s[nb][e]);
+          tmB = fmaxf(tmB, s[nb][2 + e]);
+        }
+      }
+    }
+    tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 1));
+    tmA = fmaxf(tmA, __shfl_xor_sync(0xffffffffu, tmA, 2));
+    tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 1));
+    tmB = fmaxf(tmB, __shfl_xor_sync(0xffffffffu, tmB, 2));
+    const float nmA = fmaxf(mA, tmA), nmB = fmaxf(mB, tmB);
+    const float alA = (nmA == -INFINITY) ? 1.f : exp2f(mA - nmA);
+    const float alB = (nmB == -INFINITY) ? 1.f : exp2f(mB - nmB);
+    float sumA = 0.f, sumB = 0.f;
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float pa = s[nb][e] == -INFINITY ? 0.f : exp2f(s[nb][e] - nmA);
+        const float pb = s[nb][2 + e] == -INFINITY ? 0.f : exp2f(s[nb][2 + e] - nmB);
+        s[nb][e] = pa;
+        s[nb][2 + e] = pb;
+        sumA += pa;
+        sumB += pb;
+      }
+    }
+    sumA += __shfl_xor_sync(0xffffffffu, sumA, 1);
+    sumA += __shfl_xor_sync(0xffffffffu, sumA, 2);
+    sumB += __shfl_xor_sync(0xffffffffu, sumB, 1);
+    sumB += __shfl_xor_sync(0xffffffffu, sumB, 2);
+    lA = lA * alA + sumA;
+    lB = lB * alB + sumB;
+    mA = nmA;
+    mB = nmB;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= alA;
+      o[i][1] *= alA;
+      o[i][2] *= alB;
+      o[i][3] *= alB;
+    }
+    // ---- O += P V
+#pragma unroll
+    for (int kb = 0; kb < 4; ++kb) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16(s[2 * kb][0], s[2 * kb][1]);
+      pa[1] = pack_bf16(s[2 * kb][2], s[2 * kb][3]);
+      pa[2] = pack_bf16(s[2 * kb + 1][0], s[2 * kb + 1][1]);
+      pa[3] = pack_bf16(s[2 * kb + 1][2], s[2 * kb + 1][3]);
+#pragma unroll
+      for (int nd = 0; nd < D / 8; nd += 2) {
+        const int key = kb * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int col = nd * 8 + (lane >> 4) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(Vs + key * LD + col), b0, b1, b2, b3);
+        mma16816(o[nd], pa, b0, b1);
+        mma16816(o[nd + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();  // every warp is done with buffer j % NT
+    if (iss < nmy) {
+      load_tile(iss, j % NT);
+      iss = next_needed(iss + 1);
+    }
+    cp_async_commit();
+    cons = next_needed(cons + 1);
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- this CTA's state -> shared memory (overwrites the ring)
+#pragma unroll
+  for (int nd = 0; nd < D / 8; ++nd) {
+    const int d = nd * 8 + (lane & 3) * 2;
+    *reinterpret_cast<float2*>(red_o + ra * D + d) = make_float2(o[nd][0], o[nd][1]);
+    *reinterpret_cast<float2*>(red_o + rb * D + d) = make_float2(o[nd][2], o[nd][3]);
+  }
+  if ((lane & 3) == 0) {
+    red_m[ra] = mA;
+    red_l[ra] = lA;
+    red_m[rb] = mB;
+    red_l[rb] = lB;
+  }
+  cluster_sync_all();
+
+  // ---- merge: rank r finalises rows 8r .. 8r+7 over ranks 0..CL-1, in rank order
+  {
+    constexpr int RPR = AT_ROWS / CL;   // rows per rank
+    constexpr int TPR = 128 / RPR;      // threads per row
+    constexpr int DPT = D / TPR;        // dims per thread (even)
+    const int row = rank * RPR + tid / TPR;
+    const int d0 = (tid % TPR) * DPT;
+    float mj[CL], lj[CL];
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < CL; ++j) {
+      mj[j] = ld_dsmem(dsmem_addr(red_m + row, j));
+      lj[j] = ld_dsmem(dsmem_addr(red_l + row, j));
+      M = fmaxf(M, mj[j]);
+    }
+    float L = 0.f;
+    float wj[CL];
+#pragma unroll
+    for (int j = 0; j < CL; ++j) {
+      wj[j] = (mj[j] == -INFINITY) ? 0.f : exp2f(mj[j] - M);
+      L += wj[j] * lj[j];
+    }
+    float acc[DPT];
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < CL; ++j) {
+      const uint32_t base = dsmem_addr(red_o + row * D + d0, j);
+#pragma unroll
+      for (int e = 0; e < DPT; e += 2) {
+        const float2 v = ld_dsmem2(base + e * 4);
+        acc[e] += wj[j] * v.x;
+        acc[e + 1] += wj[j] * v.y;
+      }
+    }
+    const int R = R0 + row;
+    const int t = R / g;
+    if (t < a.q_len) {
+      const int qh = h * g + R % g;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      __nv_bfloat16* dst = a.out + (static_cast<size_t>(b * a.q_len + t) * a.Hq + qh) * D + d0;
+#pragma unroll
+      for (int e = 0; e < DPT; e += 2)
+        *reinterpret_cast<__nv_bfloat162*>(dst + e) = __floats2bfloat162_rn(acc[e] * inv, acc[e + 1] * inv);
+    }
+  }
+  cluster_sync_all();  // no CTA leaves while another still reads its shared memory
+}
+
+template <int D, int NT>
+static void launch_attn_cluster(const AttnArgs& a, cudaStream_t st) {
+  constexpr int LD = D + 8;
+  const size_t smem = static_cast<size_t>(AT_ROWS + NT * 2 * AT_KEYS) * LD * 2;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_cluster_kernel<D, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    attr = true;
+  }
+  const int g = a.Hq / a.Hkv;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.q_len * g + AT_ROWS - 1) / AT_ROWS, a.B * a.Hkv, CL);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr2[2];
+  attr2[0].id = cudaLaunchAttributeClusterDimension;
+  attr2[0].val.clusterDim.x = 1;
+  attr2[0].val.clusterDim.y = 1;
+  attr2[0].val.clusterDim.z = CL;
+  attr2[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr2[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr2;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, attn_cluster_kernel<D, NT>, a);
+}
+
+template <int D>
+static void launch_attn_cluster_nt(const AttnArgs& a, cudaStream_t st) {
+  // few clusters: one 160 KB CTA per SM with four tiles in flight; many
+  // clusters: two CTAs per SM with two tiles each
+  const long clusters = static_cast<long>((a.q_len * (a.Hq / a.Hkv) + AT_ROWS - 1) / AT_ROWS) * a.B * a.Hkv;
+  if (clusters <= 16) launch_attn_cluster<D, 4>(a, st);
+  else launch_attn_cluster<D, 2>(a, st);
+}
+
+void attention(const AttnArgs& a, cudaStream_t st) {
+  if (a.B == 0 || a.q_len == 0) return;
+  if (AT_KEYS % a.page_size != 0) throw std::runtime_error("attention: page size must divide 64");
+  // the CTA of rank 0 holds every 8th chunk: its page ids must fit CL_MAX_PAGES
+  const long max_chunks = (static_cast<long>(a.bt_stride) * a.page_size + AT_KEYS - 1) / AT_KEYS;
+  if ((max_chunks + CL - 1) / CL * (AT_KEYS / a.page_size) > CL_MAX_PAGES)
+    throw std::runtime_error("attention: context too long for the cluster path");
+  switch (a.head_dim) {
+    case 32: launch_attn_cluster_nt<32>(a, st); break;
+    case 64: launch_attn_cluster_nt<64>(a, st); break;
+    case 128: launch_attn_cluster_nt<128>(a, st); break;
+    default: throw std::runtime_error("attention: head_dim must be 32, 64 or 128");
+  }
+}
 }  // namespace d3d
 
 // ---------------------------------------------------------------------------
 // Allocation-free C entry point (declared and documented in
-// attention_noalloc.h; no counterpart in the reference).  It launches the same
-// two kernels as d3d::attention, with the split-KV partials placed in a
+// attention_noalloc.h; no counterpart in the reference).  It launches the
+// split-KV kernels (attention_split) with their fp32 partials placed in a
 // file-scope device array instead of caller- or allocator-provided memory.
 // ---------------------------------------------------------------------------
 #include <mutex>
@@ -494,6 +904,6 @@ extern "C" int d3d_attention_noalloc(const void* q, const void* k_cache, const v
   a.part_o = n_chunks > 1 ? static_cast<float*>(base) : nullptr;
   a.part_ml = n_chunks > 1 ? static_cast<float*>(base) + part_o : nullptr;
   a.out = static_cast<__nv_bfloat16*>(out);
-  d3d::attention(a, stream);
+  d3d::attention_split(a, stream);
   return static_cast<int>(cudaPeekAtLastError());
 }

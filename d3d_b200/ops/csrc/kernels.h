@@ -52,7 +52,8 @@ struct AttnArgs {
   float* part_ml;           // [n_chunks][T][Hq][2]
   __nv_bfloat16* out;       // [T][Hq][D]
 };
-void attention(const AttnArgs& a, cudaStream_t st);
+void attention(const AttnArgs& a, cudaStream_t st);        // cluster kernel (no partial buffers)
+void attention_split(const AttnArgs& a, cudaStream_t st);  // split-KV + combine (uses part_o / part_ml)
 
 // ---- training kernels (train_kernels.cu)
 void kl_ce_stats(const float* zt, const float* zs, int N, int C, int ldz, int v0, const int64_t* target, float* st,
