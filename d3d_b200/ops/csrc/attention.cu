@@ -442,14 +442,17 @@ __device__ __forceinline__ uint32_t dsmem_addr(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
   return r;
 }
+// Remote shared-memory loads.  No "memory" clobber: they read state published
+// before the cluster barrier, and without it the compiler issues all of them
+// before the first use, so a thread waits for one round trip, not one per load.
 __device__ __forceinline__ float ld_dsmem(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ float2 ld_dsmem2(uint32_t addr) {
   float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  asm volatile("ld.shared::cluster.v2.f32 {%0,%1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
   return v;
 }
 template <int N>
@@ -723,14 +726,20 @@ __global__ void __launch_bounds__(128, 1) attn_cluster_kernel(const AttnArgs a) 
     constexpr int DPT = D / TPR;        // dims per thread (even)
     const int row = rank * RPR + tid / TPR;
     const int d0 = (tid % TPR) * DPT;
+    // every remote load of this thread is issued before any of them is used
     float mj[CL], lj[CL];
-    float M = -INFINITY;
+    float2 ov[CL][DPT / 2];
 #pragma unroll
     for (int j = 0; j < CL; ++j) {
       mj[j] = ld_dsmem(dsmem_addr(red_m + row, j));
       lj[j] = ld_dsmem(dsmem_addr(red_l + row, j));
-      M = fmaxf(M, mj[j]);
+      const uint32_t base = dsmem_addr(red_o + row * D + d0, j);
+#pragma unroll
+      for (int e = 0; e < DPT / 2; ++e) ov[j][e] = ld_dsmem2(base + e * 8);
     }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < CL; ++j) M = fmaxf(M, mj[j]);
     float L = 0.f;
     float wj[CL];
 #pragma unroll
@@ -743,12 +752,10 @@ __global__ void __launch_bounds__(128, 1) attn_cluster_kernel(const AttnArgs a) 
     for (int e = 0; e < DPT; ++e) acc[e] = 0.f;
 #pragma unroll
     for (int j = 0; j < CL; ++j) {
-      const uint32_t base = dsmem_addr(red_o + row * D + d0, j);
 #pragma unroll
-      for (int e = 0; e < DPT; e += 2) {
-        const float2 v = ld_dsmem2(base + e * 4);
-        acc[e] += wj[j] * v.x;
-        acc[e + 1] += wj[j] * v.y;
+      for (int e = 0; e < DPT / 2; ++e) {
+        acc[2 * e] += wj[j] * ov[j][e].x;
+        acc[2 * e + 1] += wj[j] * ov[j][e].y;
       }
     }
     const int R = R0 + row;
@@ -802,8 +809,18 @@ static void launch_attn_cluster_nt(const AttnArgs& a, cudaStream_t st) {
   else launch_attn_cluster<D, 2>(a, st);
 }
 
+// Dispatch: decode-shaped launches (one 64-row tile per sequence and kv head:
+// verify blocks and single tokens) take the cluster kernel; larger query
+// counts (prefill, the drafter's packed forward) take the split-KV kernels,
+// whose CTAs run independently (no cluster barrier to wait at when the rows
+// of a tile need uneven numbers of key tiles) when partial buffers are given.
 void attention(const AttnArgs& a, cudaStream_t st) {
   if (a.B == 0 || a.q_len == 0) return;
+  const bool one_tile = a.q_len * (a.Hq / a.Hkv) <= AT_ROWS;
+  if (!one_tile && (a.n_chunks == 1 || (a.part_o && a.part_ml))) {
+    attention_split(a, st);
+    return;
+  }
   if (AT_KEYS % a.page_size != 0) throw std::runtime_error("attention: page size must divide 64");
   // the CTA of rank 0 holds every 8th chunk: its page ids must fit CL_MAX_PAGES
   const long max_chunks = (static_cast<long>(a.bt_stride) * a.page_size + AT_KEYS - 1) / AT_KEYS;
