@@ -20,6 +20,7 @@
 // row's output is bit-identical whether it is verified in a block of 16 or
 // decoded alone — required for greedy token identity with AR decoding.
 #include <stdexcept>
+#include <string>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -804,8 +805,15 @@ template <int D>
 static void launch_attn_cluster_nt(const AttnArgs& a, cudaStream_t st) {
   // few clusters: one 160 KB CTA per SM with four tiles in flight; many
   // clusters: two CTAs per SM with two tiles each
+  // D3D_ATTN_NT=2|4 overrides (the 87 KB two-tile CTA leaves room for a
+  // GEMM CTA on the same SM to prefetch weights under programmatic launch)
+  static const int nt_env = [] {
+    const char* e = std::getenv("D3D_ATTN_NT");
+    return e ? std::atoi(e) : 0;
+  }();
   const long clusters = static_cast<long>((a.q_len * (a.Hq / a.Hkv) + AT_ROWS - 1) / AT_ROWS) * a.B * a.Hkv;
-  if (clusters <= 16) launch_attn_cluster<D, 4>(a, st);
+  const int nt = nt_env == 2 || nt_env == 4 ? nt_env : (clusters <= 16 ? 4 : 2);
+  if (nt == 4) launch_attn_cluster<D, 4>(a, st);
   else launch_attn_cluster<D, 2>(a, st);
 }
 
@@ -816,8 +824,12 @@ static void launch_attn_cluster_nt(const AttnArgs& a, cudaStream_t st) {
 // of a tile need uneven numbers of key tiles) when partial buffers are given.
 void attention(const AttnArgs& a, cudaStream_t st) {
   if (a.B == 0 || a.q_len == 0) return;
+  static const bool force_split = [] {
+    const char* e = std::getenv("D3D_ATTN_PATH");
+    return e && std::string(e) == "split";
+  }();
   const bool one_tile = a.q_len * (a.Hq / a.Hkv) <= AT_ROWS;
-  if (!one_tile && (a.n_chunks == 1 || (a.part_o && a.part_ml))) {
+  if ((!one_tile || force_split) && (a.n_chunks == 1 || (a.part_o && a.part_ml))) {
     attention_split(a, st);
     return;
   }
