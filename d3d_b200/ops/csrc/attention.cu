@@ -462,26 +462,21 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 template <int D, int NT>
-__global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(128, 1) attn_cluster_kernel(const AttnArgs a) {
   griddep_launch();
   constexpr int LD = D + 8;
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* ring = Qs + AT_ROWS * LD;  // NT x {K [64][LD], V [64][LD]}
-  // after the key loop the ring holds this CTA's two states (one per key
-  // half): O [2][64][D], m [2][64], l [2][64] (fp32)
-  static_assert(NT >= 2, "the merge state needs two ring slots");
-  static_assert((2 * AT_ROWS * D + 4 * AT_ROWS) * 4 <= NT * 2 * AT_KEYS * LD * 2, "merge state exceeds the ring");
+  // after the key loop the ring holds this CTA's state: O [64][D], m [64], l [64] (fp32)
   float* red_o = reinterpret_cast<float*>(ring);
-  float* red_m = red_o + 2 * AT_ROWS * D;
-  float* red_l = red_m + 2 * AT_ROWS;
+  float* red_m = red_o + AT_ROWS * D;
+  float* red_l = red_m + AT_ROWS;
   __shared__ int s_rows[AT_ROWS][3];
   __shared__ int s_range[3];
   __shared__ int s_pages[CL_MAX_PAGES];
 
-  // 8 warps: warp w takes rows 16(w%4)..+15 and keys 32(w/4)..+31 of every tile
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rg = warp & 3, kh = warp >> 2;
   const int g = a.Hq / a.Hkv;
   const int b = blockIdx.y / a.Hkv, h = blockIdx.y % a.Hkv;
   const int rank = static_cast<int>(cluster_rank());
@@ -523,7 +518,7 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
   int nmy = nch > rank ? (nch - rank + CL - 1) / CL : 0;
   if (nmy * ppc > CL_MAX_PAGES) nmy = CL_MAX_PAGES / ppc;  // host rejects contexts this long
   const int* bt = a.block_table + static_cast<size_t>(b) * a.bt_stride;
-  for (int idx = tid; idx < nmy * ppc; idx += 256) {
+  for (int idx = tid; idx < nmy * ppc; idx += 128) {
     const int pg = (rank + CL * (idx / ppc)) * ppc + idx % ppc;
     s_pages[idx] = pg < a.bt_stride ? bt[pg] : 0;
   }
@@ -532,7 +527,7 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
   griddep_wait();
 
   // ---- Q tile (its own cp.async group, ahead of the K/V tiles)
-  for (int c = tid; c < AT_ROWS * (D / 8); c += 256) {
+  for (int c = tid; c < AT_ROWS * (D / 8); c += 128) {
     const int r = c / (D / 8), dc = (c % (D / 8)) * 8;
     const int R = R0 + r;
     const int t = R / g;
@@ -545,10 +540,10 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
   }
   cp_async_commit();
 
-  const int ra = rg * 16 + (lane >> 2), rb = ra + 8;
+  const int ra = warp * 16 + (lane >> 2), rb = ra + 8;
   const int limA = s_rows[ra][0], loA = s_rows[ra][1], hiA = s_rows[ra][2];
   const int limB = s_rows[rb][0], loB = s_rows[rb][1], hiB = s_rows[rb][2];
-  const uint32_t q_base = smem_u32(Qs + (rg * 16 + (lane & 15)) * LD + (lane >> 4) * 8);
+  const uint32_t q_base = smem_u32(Qs + (warp * 16 + (lane & 15)) * LD + (lane >> 4) * 8);
 
   float o[D / 8][4];
 #pragma unroll
@@ -566,7 +561,7 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
     __nv_bfloat16* Ks = ring + buf * 2 * AT_KEYS * LD;
     __nv_bfloat16* Vs = Ks + AT_KEYS * LD;
     const int k0 = k0_of(i);
-    for (int c = tid; c < AT_KEYS * (D / 8); c += 256) {
+    for (int c = tid; c < AT_KEYS * (D / 8); c += 128) {
       const int kr = c / (D / 8), dc = (c % (D / 8)) * 8;
       const int s = k0 + kr;
       if (s < kv_end) {
@@ -598,18 +593,17 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
     const int k0 = k0_of(cons);
     const int kend = min(k0 + AT_KEYS, kv_end);
 
-    // ---- S = Q K^T (16 rows x 32 keys per warp)
-    const int kw = kh * 32;  // first key of this warp's half within the tile
-    float s[4][4];
+    // ---- S = Q K^T (16 rows x 64 keys per warp)
+    float s[8][4];
 #pragma unroll
-    for (int nb = 0; nb < 4; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+    for (int nb = 0; nb < 8; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       uint32_t qf[4];
       ldsm_x4(q_base + kk * 32, qf[0], qf[1], qf[2], qf[3]);
 #pragma unroll
-      for (int nb = 0; nb < 4; nb += 2) {
-        const int key = kw + nb * 8 + (lane & 7) + (lane >> 4) * 8;
+      for (int nb = 0; nb < 8; nb += 2) {
+        const int key = nb * 8 + (lane & 7) + (lane >> 4) * 8;
         const int col = kk * 16 + ((lane >> 3) & 1) * 8;
         uint32_t b0, b1, b2, b3;
         ldsm_x4(smem_u32(Ks + key * LD + col), b0, b1, b2, b3);
@@ -619,12 +613,12 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
     }
     // ---- mask + online softmax
     float tmA = -INFINITY, tmB = -INFINITY;
-    const int h0 = k0 + kw, h1 = h0 + 32;
-    const bool fullA = h1 <= kend && (h1 <= limA || (h0 >= loA && h1 <= hiA));
-    const bool fullB = h1 <= kend && (h1 <= limB || (h0 >= loB && h1 <= hiB));
+    const int k1e = k0 + AT_KEYS;
+    const bool fullA = k1e <= kend && (k1e <= limA || (k0 >= loA && k1e <= hiA));
+    const bool fullB = k1e <= kend && (k1e <= limB || (k0 >= loB && k1e <= hiB));
     if (__all_sync(0xffffffffu, fullA && fullB)) {
 #pragma unroll
-      for (int nb = 0; nb < 4; ++nb) {
+      for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           s[nb][e] *= sl2;
@@ -635,10 +629,10 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
       }
     } else {
 #pragma unroll
-      for (int nb = 0; nb < 4; ++nb) {
+      for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int key = h0 + nb * 8 + (lane & 3) * 2 + e;
+          const int key = k0 + nb * 8 + (lane & 3) * 2 + e;
           const bool inb = key < kend;
           s[nb][e] = (inb && visible(key, limA, loA, hiA)) ? s[nb][e] * sl2 : -INFINITY;
           s[nb][2 + e] = (inb && visible(key, limB, loB, hiB)) ? s[nb][2 + e] * sl2 : -INFINITY;
@@ -656,7 +650,7 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
     const float alB = (nmB == -INFINITY) ? 1.f : exp2f(mB - nmB);
     float sumA = 0.f, sumB = 0.f;
 #pragma unroll
-    for (int nb = 0; nb < 4; ++nb) {
+    for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const float pa = s[nb][e] == -INFINITY ? 0.f : exp2f(s[nb][e] - nmA);
@@ -682,9 +676,9 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
       o[i][2] *= alB;
       o[i][3] *= alB;
     }
-    // ---- O += P V (this warp's 32 keys)
+    // ---- O += P V
 #pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
+    for (int kb = 0; kb < 4; ++kb) {
       uint32_t pa[4];
       pa[0] = pack_bf16(s[2 * kb][0], s[2 * kb][1]);
       pa[1] = pack_bf16(s[2 * kb][2], s[2 * kb][3]);
@@ -692,7 +686,7 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
       pa[3] = pack_bf16(s[2 * kb + 1][2], s[2 * kb + 1][3]);
 #pragma unroll
       for (int nd = 0; nd < D / 8; nd += 2) {
-        const int key = kw + kb * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int key = kb * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
         const int col = nd * 8 + (lane >> 4) * 8;
         uint32_t b0, b1, b2, b3;
         ldsm_x4_t(smem_u32(Vs + key * LD + col), b0, b1, b2, b3);
@@ -711,52 +705,46 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
   cp_async_wait<0>();
   __syncthreads();
 
-  // ---- this CTA's two states -> shared memory (overwrites the ring)
-  {
-    float* ro = red_o + kh * AT_ROWS * D;
+  // ---- this CTA's state -> shared memory (overwrites the ring)
 #pragma unroll
-    for (int nd = 0; nd < D / 8; ++nd) {
-      const int d = nd * 8 + (lane & 3) * 2;
-      *reinterpret_cast<float2*>(ro + ra * D + d) = make_float2(o[nd][0], o[nd][1]);
-      *reinterpret_cast<float2*>(ro + rb * D + d) = make_float2(o[nd][2], o[nd][3]);
-    }
-    if ((lane & 3) == 0) {
-      red_m[kh * AT_ROWS + ra] = mA;
-      red_l[kh * AT_ROWS + ra] = lA;
-      red_m[kh * AT_ROWS + rb] = mB;
-      red_l[kh * AT_ROWS + rb] = lB;
-    }
+  for (int nd = 0; nd < D / 8; ++nd) {
+    const int d = nd * 8 + (lane & 3) * 2;
+    *reinterpret_cast<float2*>(red_o + ra * D + d) = make_float2(o[nd][0], o[nd][1]);
+    *reinterpret_cast<float2*>(red_o + rb * D + d) = make_float2(o[nd][2], o[nd][3]);
+  }
+  if ((lane & 3) == 0) {
+    red_m[ra] = mA;
+    red_l[ra] = lA;
+    red_m[rb] = mB;
+    red_l[rb] = lB;
   }
   cluster_sync_all();
 
-  // ---- merge: rank r finalises rows 8r .. 8r+7 over the 2 x CL states
-  // (rank-major, key half minor) with 128 of the 256 threads
-  if (tid < 128) {
+  // ---- merge: rank r finalises rows 8r .. 8r+7 over ranks 0..CL-1, in rank order
+  {
     constexpr int RPR = AT_ROWS / CL;   // rows per rank
     constexpr int TPR = 128 / RPR;      // threads per row
     constexpr int DPT = D / TPR;        // dims per thread (even)
-    constexpr int NS = 2 * CL;          // states per row
     const int row = rank * RPR + tid / TPR;
     const int d0 = (tid % TPR) * DPT;
     // every remote load of this thread is issued before any of them is used
-    float mj[NS], lj[NS];
-    float2 ov[NS][DPT / 2];
+    float mj[CL], lj[CL];
+    float2 ov[CL][DPT / 2];
 #pragma unroll
-    for (int j = 0; j < NS; ++j) {
-      const int r = j >> 1, hf = j & 1;
-      mj[j] = ld_dsmem(dsmem_addr(red_m + hf * AT_ROWS + row, r));
-      lj[j] = ld_dsmem(dsmem_addr(red_l + hf * AT_ROWS + row, r));
-      const uint32_t base = dsmem_addr(red_o + (hf * AT_ROWS + row) * D + d0, r);
+    for (int j = 0; j < CL; ++j) {
+      mj[j] = ld_dsmem(dsmem_addr(red_m + row, j));
+      lj[j] = ld_dsmem(dsmem_addr(red_l + row, j));
+      const uint32_t base = dsmem_addr(red_o + row * D + d0, j);
 #pragma unroll
       for (int e = 0; e < DPT / 2; ++e) ov[j][e] = ld_dsmem2(base + e * 8);
     }
     float M = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < NS; ++j) M = fmaxf(M, mj[j]);
+    for (int j = 0; j < CL; ++j) M = fmaxf(M, mj[j]);
     float L = 0.f;
-    float wj[NS];
+    float wj[CL];
 #pragma unroll
-    for (int j = 0; j < NS; ++j) {
+    for (int j = 0; j < CL; ++j) {
       wj[j] = (mj[j] == -INFINITY) ? 0.f : exp2f(mj[j] - M);
       L += wj[j] * lj[j];
     }
@@ -764,7 +752,7 @@ __global__ void __launch_bounds__(256, 1) attn_cluster_kernel(const AttnArgs a) 
 #pragma unroll
     for (int e = 0; e < DPT; ++e) acc[e] = 0.f;
 #pragma unroll
-    for (int j = 0; j < NS; ++j) {
+    for (int j = 0; j < CL; ++j) {
 #pragma unroll
       for (int e = 0; e < DPT / 2; ++e) {
         acc[2 * e] += wj[j] * ov[j][e].x;
@@ -798,7 +786,7 @@ static void launch_attn_cluster(const AttnArgs& a, cudaStream_t st) {
   const int g = a.Hq / a.Hkv;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.q_len * g + AT_ROWS - 1) / AT_ROWS, a.B * a.Hkv, CL);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(128);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr2[2];
