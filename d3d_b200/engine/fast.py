@@ -85,14 +85,14 @@ def _stage(pin: _Pinned, name: str, arr: np.ndarray, dst: torch.Tensor, stream) 
 class _FastModelBackend:
     def __init__(self, weights: FastWeights, *, pages: int, page_size: int, max_seqs: int,
                  max_context: int, extra_slots: int, batch_invariant: bool, use_graphs: bool,
-                 device="cuda", stream: Optional[torch.cuda.Stream] = None):
+                 device="cuda", stream: Optional[torch.cuda.Stream] = None, tp=None):
         self.w = weights
         self.cfg: ModelConfig = weights.cfg
         self.device = torch.device(device)
         max_pages_seq = math.ceil((max_context + extra_slots) / page_size)
         self.kv = PagedKV(self.cfg, pages, page_size, max_seqs, max_pages_seq, device)
         self.runner = FastRunner(weights, self.kv, max_context=max_context + extra_slots,
-                                 batch_invariant=batch_invariant, device=device)
+                                 batch_invariant=batch_invariant, device=device, tp=tp)
         self.stream = stream or torch.cuda.Stream(device=self.device)
         self.graphs = _GraphCache(self.runner, self.stream, use_graphs)
         self.pin = _Pinned()
@@ -155,10 +155,13 @@ class FastTarget(_FastModelBackend, TargetBackend):
 
     def __init__(self, weights: FastWeights, *, pages: int = 4096, page_size: int = 16,
                  max_seqs: int = 16, max_context: int = 4096, use_graphs: bool = True,
-                 device="cuda", stream=None):
+                 device="cuda", stream=None, tp=None):
+        """``tp``: a :class:`~d3d_b200.parallel.tp.TPGroup` when ``weights`` is one
+        shard of a tensor-parallel target (every rank of the group then runs
+        the same calls in the same order)."""
         super().__init__(weights, pages=pages, page_size=page_size, max_seqs=max_seqs,
                          max_context=max_context, extra_slots=64, batch_invariant=True,
-                         use_graphs=use_graphs, device=device, stream=stream)
+                         use_graphs=use_graphs, device=device, stream=stream, tp=tp)
         self.hidden_size = self.cfg.hidden_size
         self._pending = None
         self._accept_bufs: Dict[tuple, dict] = {}

@@ -79,26 +79,32 @@ class FastWeights:
         cp = pk(m.cond_proj.weight) if getattr(m, "cond_proj", None) is not None else None
         return cls(m.cfg, embed, layers, bf(m.model.norm.weight), lm, cp)
 
+    @staticmethod
+    @torch.no_grad()
+    def seeded_randn(shape, key: int, std: float, device="cuda") -> torch.Tensor:
+        """bf16 N(0, std) tensor drawn on the device from generator seed ``key``
+        (in chunks, so the fp32 temporary stays small)."""
+        gen = torch.Generator(device=device)
+        gen.manual_seed(int(key))
+        t = torch.empty(*shape, dtype=torch.bfloat16, device=device)
+        flat = t.view(-1)
+        step = 1 << 26
+        for i in range(0, flat.numel(), step):
+            n = min(step, flat.numel() - i)
+            flat[i:i + n] = (torch.randn(n, generator=gen, device=device) * std).to(torch.bfloat16)
+        return t
+
     @classmethod
     @torch.no_grad()
     def random(cls, cfg: ModelConfig, seed: int = 0, device="cuda",
                std: Optional[float] = None) -> "FastWeights":
         """Seeded N(0, std) init drawn on the device (no host copy of the model)."""
         std = cfg.initializer_range if std is None else std
-        gen = torch.Generator(device=device)
         counter = [0]
 
         def rnd(*shape):
             counter[0] += 1
-            gen.manual_seed(int(seed) * 1_000_003 + counter[0])
-            t = torch.empty(*shape, dtype=torch.bfloat16, device=device)
-            # chunked so the fp32 temporary stays small
-            flat = t.view(-1)
-            step = 1 << 26
-            for i in range(0, flat.numel(), step):
-                n = min(step, flat.numel() - i)
-                flat[i:i + n] = (torch.randn(n, generator=gen, device=device) * std).to(torch.bfloat16)
-            return t
+            return cls.seeded_randn(shape, int(seed) * 1_000_003 + counter[0], std, device)
 
         ones = lambda n: torch.ones(n, dtype=torch.bfloat16, device=device)
         prnd = lambda *shape: ops.pack_weight(rnd(*shape))
@@ -256,11 +262,12 @@ class FastRunner:
     """Runs forwards of one model on the kernels; captures CUDA graphs per shape."""
 
     def __init__(self, weights: FastWeights, kv: PagedKV, *, decode_chunk: Optional[int] = None,
-                 max_context: int = 4096, batch_invariant: bool = True, device="cuda"):
+                 max_context: int = 4096, batch_invariant: bool = True, device="cuda", tp=None):
         self.w = weights
-        self.cfg = weights.cfg
+        self.cfg = weights.cfg          # per-rank shapes under tensor parallelism
         self.kv = kv
         self.device = device
+        self.tp = tp                    # d3d_b200.parallel.tp.TPGroup or None
         # Key chunk per attention CTA.  Fine chunks keep >100 CTAs busy at decode
         # sizes (one 64-key tile each for the batch-invariant target); the
         # drafter's packed forward has many query rows, so it takes 256.
@@ -303,7 +310,8 @@ class FastRunner:
             if T > 256:
                 pl = {g: (bt, 1, False) for g in self.GEMMS}
             else:
-                pl = {g: (bt, ops.splitk_for(n, k, mtiles=1, bt=16), False) for g, (n, k) in shapes.items()}
+                pl = {g: (bt, min(16, ops.splitk_for(n, k, mtiles=1, bt=16)), False)
+                      for g, (n, k) in shapes.items()}
             pl["lm_bt"] = bt
             return pl
         if tune and T not in self.tuned and 64 <= T <= 2048 and os.environ.get("D3D_AUTOTUNE", "1") != "0" \
@@ -433,6 +441,10 @@ class FastRunner:
         torch.index_select(self.kv.block_table, 0, b.seq_rows, out=b.bt_view)
         n = 3
         eps = c.rms_norm_eps
+        tp = self.tp
+        if tp is not None:
+            tp.bump()
+            n += 1
         for li, L in enumerate(w.layers):
             gbt, s, direct = pl["qkv"]
             if direct:
@@ -449,7 +461,13 @@ class FastRunner:
                         b.attn)
             n += 3 + (1 if b.n_chunks > 1 else 0)
             gbt, s, direct = pl["o"]
-            if direct:   # residual added in the epilogue, in place
+            if tp is not None:   # row-parallel: partials exchanged, reduced in the norm
+                xo = 2 * li
+                E.gemm_partial(b.attn, L.o.data, tp.part_view(xo, s * T * c.hidden_size), s, gbt, b.status, L.o.n)
+                tp.signal(xo)
+                tp.add_rmsnorm(xo, xo, s, b.x, L.post_norm, b.xn, eps)
+                n += 1
+            elif direct:   # residual added in the epilogue, in place
                 E.gemm_bf16(b.attn, L.o.data, b.x, b.x, gbt, b.status, L.o.n)
                 E.add_rmsnorm(None, 1, b.x, L.post_norm, b.xn, eps)
             else:
@@ -465,7 +483,14 @@ class FastRunner:
                 n += 4
             nxt = w.layers[li + 1].in_norm if li + 1 < len(w.layers) else w.final_norm
             gbt, s, direct = pl["down"]
-            if direct:
+            if tp is not None:
+                xd = 2 * li + 1
+                E.gemm_partial(b.h, L.down.data, tp.part_view(xd, s * T * c.hidden_size), s, gbt, b.status,
+                               L.down.n)
+                tp.signal(xd)
+                tp.add_rmsnorm(xd, xd, s, b.x, nxt, b.xn, eps)
+                n += 1
+            elif direct:
                 E.gemm_bf16(b.h, L.down.data, b.x, b.x, gbt, b.status, L.down.n)
                 E.add_rmsnorm(None, 1, b.x, nxt, b.xn, eps)
             else:
@@ -475,5 +500,11 @@ class FastRunner:
         if b.topk > 0:
             E.gemm_topk(b.xn, w.lm_head.data, b.tv, b.ti, b.topk, pl["lm_bt"], b.status, w.lm_head.n)
             E.topk_merge(b.tv, b.ti, T, b.ntiles, b.kt, b.topk, b.top_v, b.top_i)
+            if tp is not None:   # vocab-parallel: merge the ranks' candidates (global ids)
+                xl = 2 * len(w.layers)
+                E.tp_publish_topk(b.top_v, b.top_i, tp.rank * c.vocab_size, tp.cand_view())
+                tp.signal(xl)
+                tp.merge_topk(xl, T, b.topk, b.top_v, b.top_i)
+                n += 3
         n += 2 if b.topk > 0 else 0
         return n + (1 if cond is not None else 0)

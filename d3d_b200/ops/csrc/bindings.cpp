@@ -363,6 +363,71 @@ void accept_send(Tensor blocks, Tensor post, c10::optional<Tensor> hidden, int64
                    reinterpret_cast<int64_t*>(flag_ptr), seq, cur_stream());
 }
 
+// ------------------------------------------------------------ tensor parallel
+// ``ptrs`` is an int64 CPU tensor [2, tp]: row 0 = every rank's flag array,
+// row 1 = every rank's exchange region (device addresses valid in this process).
+d3d::TpArgs tp_args(Tensor ptrs, int64_t rank, Tensor epoch, c10::optional<Tensor> status) {
+  TORCH_CHECK(ptrs.dim() == 2 && ptrs.size(0) == 2 && ptrs.size(1) <= d3d::TP_MAX, "tp: bad pointer table");
+  CHECK_DT(ptrs, torch::kInt64);
+  CHECK_DT(epoch, torch::kInt64);
+  d3d::TpArgs a{};
+  a.tp = static_cast<int>(ptrs.size(1));
+  a.rank = static_cast<int>(rank);
+  TORCH_CHECK(a.rank >= 0 && a.rank < a.tp, "tp: rank out of range");
+  auto p = ptrs.contiguous().cpu();
+  const int64_t* v = p.data_ptr<int64_t>();
+  for (int j = 0; j < a.tp; ++j) {
+    a.flags[j] = reinterpret_cast<int64_t*>(v[j]);
+    a.parts[j] = reinterpret_cast<uint8_t*>(v[a.tp + j]);
+  }
+  a.epoch = epoch.data_ptr<int64_t>();
+  a.status = status_ptr(status);
+  a.timeout_ns = kTimeoutNs;
+  return a;
+}
+
+void tp_epoch_bump(Tensor epoch) {
+  const c10::cuda::CUDAGuard g(epoch.device());
+  d3d::tp_epoch_bump(epoch.data_ptr<int64_t>(), cur_stream());
+}
+
+void tp_signal(Tensor ptrs, int64_t rank, Tensor epoch, int64_t x) {
+  const c10::cuda::CUDAGuard g(epoch.device());
+  d3d::tp_signal(tp_args(ptrs, rank, epoch, c10::nullopt), static_cast<int>(x), cur_stream());
+}
+
+void add_rmsnorm_tp(Tensor ptrs, int64_t rank, Tensor epoch, int64_t x, int64_t part_off, int64_t nsplit,
+                    Tensor residual, Tensor w, Tensor out, double eps, c10::optional<Tensor> status) {
+  const c10::cuda::CUDAGuard g(residual.device());
+  CHECK_DT(residual, torch::kBFloat16);
+  CHECK_CONTIG(residual);
+  CHECK_CONTIG(out);
+  TORCH_CHECK(part_off % 16 == 0, "add_rmsnorm_tp: partial offset must be 16-byte aligned");
+  d3d::add_rmsnorm_tp(tp_args(ptrs, rank, epoch, status), static_cast<int>(x), static_cast<size_t>(part_off),
+                      static_cast<int>(nsplit), bf(residual), cbf(w), bf(out), static_cast<int>(residual.size(0)),
+                      static_cast<int>(residual.size(1)), static_cast<float>(eps), cur_stream());
+}
+
+void tp_publish_topk(Tensor lv, Tensor li, int64_t id_offset, Tensor cand) {
+  const c10::cuda::CUDAGuard g(lv.device());
+  CHECK_DT(lv, torch::kFloat32);
+  CHECK_DT(li, torch::kInt64);
+  CHECK_CONTIG(lv);
+  CHECK_CONTIG(li);
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(cand.data_ptr()) % 16 == 0, "tp_publish_topk: slot alignment");
+  d3d::tp_publish_topk(lv.data_ptr<float>(), li.data_ptr<int64_t>(), static_cast<int>(lv.size(0)),
+                       static_cast<int>(lv.size(1)), id_offset, cand.data_ptr<uint8_t>(), cur_stream());
+}
+
+void topk_merge_tp(Tensor ptrs, int64_t rank, Tensor epoch, int64_t x, int64_t cand_off, int64_t M, int64_t k,
+                   c10::optional<Tensor> ov, Tensor oi, c10::optional<Tensor> status) {
+  const c10::cuda::CUDAGuard g(oi.device());
+  CHECK_DT(oi, torch::kInt64);
+  d3d::topk_merge_tp(tp_args(ptrs, rank, epoch, status), static_cast<int>(x), static_cast<size_t>(cand_off),
+                     static_cast<int>(M), static_cast<int>(k), ov ? ov->data_ptr<float>() : nullptr,
+                     oi.data_ptr<int64_t>(), cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -399,4 +464,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("handoff_wait", &handoff_wait, py::arg("flag"), py::arg("seq"), py::arg("src"), py::arg("dst"),
         py::arg("status"));
   m.def("accept_send", &accept_send);
+  m.def("tp_epoch_bump", &tp_epoch_bump);
+  m.def("tp_signal", &tp_signal);
+  m.def("add_rmsnorm_tp", &add_rmsnorm_tp, py::arg("ptrs"), py::arg("rank"), py::arg("epoch"), py::arg("x"),
+        py::arg("part_off"), py::arg("nsplit"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"),
+        py::arg("status") = py::none());
+  m.def("tp_publish_topk", &tp_publish_topk);
+  m.def("topk_merge_tp", &topk_merge_tp, py::arg("ptrs"), py::arg("rank"), py::arg("epoch"), py::arg("x"),
+        py::arg("cand_off"), py::arg("M"), py::arg("k"), py::arg("ov"), py::arg("oi"), py::arg("status") = py::none());
 }

@@ -81,3 +81,23 @@ void ipc_get_handle(void* p, unsigned char* out64);
 void* ipc_open_handle(const unsigned char* in64);
 void ipc_close_handle(void* p);
 }  // namespace d3d
+
+namespace d3d {
+// ---- tensor-parallel exchange (tp.cu)
+constexpr int TP_MAX = 8;
+struct TpArgs {
+  int tp, rank;
+  int64_t* epoch;                 // this rank's forward counter (device)
+  int64_t* flags[TP_MAX];         // every rank's flag array (peer-mapped): [exchange][source rank]
+  uint8_t* parts[TP_MAX];         // every rank's exchange region (peer-mapped)
+  int* status;
+  unsigned long long timeout_ns;
+};
+void tp_epoch_bump(int64_t* epoch, cudaStream_t st);
+void tp_signal(const TpArgs& a, int x, cudaStream_t st);
+void add_rmsnorm_tp(const TpArgs& a, int x, size_t part_off, int nsplit, __nv_bfloat16* residual,
+                    const __nv_bfloat16* w, __nv_bfloat16* out, int M, int N, float eps, cudaStream_t st);
+void tp_publish_topk(const float* lv, const int64_t* li, int M, int k, int64_t id_offset, uint8_t* cand,
+                     cudaStream_t st);
+void topk_merge_tp(const TpArgs& a, int x, size_t cand_off, int M, int k, float* ov, int64_t* oi, cudaStream_t st);
+}  // namespace d3d
