@@ -65,10 +65,16 @@ class P2PTargetServer:
     """Serves a :class:`~d3d_b200.engine.fast.FastTarget` to the drafter rank
     at the other end of ``link``."""
 
-    def __init__(self, backend, link, deadline_s: float = 600.0):
+    def __init__(self, backend, link, deadline_s: float = 600.0, replies: str = "all"):
+        """``replies="ack"`` is for the ranks of a tensor-parallel target other
+        than rank 0: they run every command but answer only RELEASE (an
+        acknowledgement), since rank 0's replies carry the results."""
         self.be = backend
         self.link = link
         self.deadline_s = deadline_s
+        if replies not in ("all", "ack"):
+            raise ValueError("replies must be 'all' or 'ack'")
+        self.replies = replies
         self.seqs: Dict[int, SeqState] = {}
         self.H = int(backend.hidden_size)
         # fused path: the verify graph's accept kernel writes the reply into the
@@ -111,6 +117,8 @@ class P2PTargetServer:
             self.seqs[sid] = s
             group.append(s)
         anchors, hidden = self.be.prefill(group)
+        if self.replies != "all":
+            return
         words = _prefill_words(n)
         ho = hidden_offset(words)
         self.rep_host[:HDR] = 0
@@ -129,6 +137,12 @@ class P2PTargetServer:
             s = self.seqs[sid]
             s.prefix = prefix
             group.append(s)
+        if self.replies != "all":
+            if self.fused:
+                self.be.submit_verify(group, blocks, sink=lambda ids, post, xn: None)
+            else:
+                self.be.verify(group, blocks)
+            return
         if not self.fused:
             r = self.be.verify(group, blocks)
             words = _verify_words(B, K)
@@ -184,6 +198,8 @@ class P2PTargetServer:
                     raise ValueError(f"unknown target command {cmd}")
                 self.served += 1
             except Exception as exc:  # reported to the drafter; the server keeps serving
+                if self.replies != "all":
+                    raise   # rank 0 of the group reports the failure (its exchange waits time out)
                 self._send_error(exc)
 
 
@@ -192,6 +208,11 @@ class P2PTarget(TargetBackend):
 
     def __init__(self, link, hidden_size: int, device=None, deadline_s: float = 600.0,
                  want_hidden: bool = True):
+        """``link`` may be a list: the links to every rank of a tensor-parallel
+        target (rank 0 first).  Requests go to all of them; results come from
+        rank 0, and RELEASE waits for every rank's acknowledgement."""
+        self.links = list(link) if isinstance(link, (list, tuple)) else [link]
+        link = self.links[0]
         self.link = link
         self.want_hidden = want_hidden
         self.hidden_size = int(hidden_size)
@@ -207,8 +228,9 @@ class P2PTarget(TargetBackend):
 
     def _send(self, n_words: int) -> None:
         n = (n_words + 1) // 2 * 2
-        # the put kernel reads the pinned request directly
-        self.link.send(self.req[:n], self.stream)
+        # the put kernels read the pinned request directly
+        for lk in self.links:
+            lk.send(self.req[:n], self.stream)
 
     def _recv(self, expect: int, head_words: int = HEAD_WORDS):
         head_words = min(max(head_words, HDR), self.rep.numel())
@@ -287,6 +309,10 @@ class P2PTarget(TargetBackend):
         self.req[0], self.req[1] = CMD_RELEASE, seq.index
         self._send(HDR)
         self._recv(CMD_RELEASE, HDR)
+        for lk in self.links[1:]:
+            lk.recv(self.rep[:HDR], self.stream, deadline_s=self.deadline_s)
+            if int(self.rep[0]) != CMD_RELEASE:
+                raise RuntimeError("tensor-parallel target rank did not acknowledge RELEASE")
 
     def close(self) -> None:
         """Ends the server's current ``serve()`` call (it may be called again)."""

@@ -111,3 +111,42 @@ def test_disaggregated_fault_reported_and_server_survives():
     r = _run("fault")
     assert r["first"] == "injected"
     assert r["after"] == r["local"]
+
+
+def _worker_group(rank, port, out_path):
+    """Ranks 0 and 1 serve as the two ranks of a (simulated) tensor-parallel
+    target -- rank 1 acknowledges only RELEASE -- and rank 2 drafts."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=3, timeout=datetime.timedelta(seconds=60))
+    torch.manual_seed(0)
+    from d3d_b200.config import tiny_drafter, tiny_target
+    from d3d_b200.engine.backends import TorchDraft, TorchTarget
+    from d3d_b200.engine.disagg import P2PTarget, P2PTargetServer
+    from d3d_b200.engine.spec import DecodeConfig, SpecDecoder, ar_generate
+    from d3d_b200.models.qwen3 import build_model
+    from d3d_b200.parallel.p2p import HostLink
+    try:
+        if rank < 2:
+            tgt = TorchTarget(build_model(tiny_target(), seed=0))
+            P2PTargetServer(tgt, HostLink(2, slot_bytes=1 << 16), replies="all" if rank == 0 else "ack").serve()
+        else:
+            remote = P2PTarget([HostLink(0, slot_bytes=1 << 16), HostLink(1, slot_bytes=1 << 16)], hidden_size=128)
+            drafter = TorchDraft(build_model(tiny_drafter(cond=True), seed=1))
+            cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=24, ignore_eos=True)
+            prompts = _prompts()
+            spec = SpecDecoder(remote, drafter, cfg).generate(prompts, concurrency=2)
+            local = ar_generate(TorchTarget(build_model(tiny_target(), seed=0)), prompts, 24, ignore_eos=True)
+            remote.close()
+            torch.save({"spec": [o.tokens for o in spec["outputs"]], "local": local["outputs"]}, out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_target_group_protocol_token_identical():
+    with tempfile.TemporaryDirectory() as d:
+        out = os.path.join(d, "out.pt")
+        mp.spawn(_worker_group, args=(_free_port(), out), nprocs=3, join=True)
+        r = torch.load(out)
+    assert r["spec"] == r["local"]
