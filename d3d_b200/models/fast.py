@@ -458,7 +458,7 @@ class FastRunner:
             E.attention(b.q, self.kv.k[li], self.kv.v[li], b.bt_view, b.rows, b.kv_end, B, Q, hq, hkv,
                         self.kv.page_size, self.scale, b.chunk, b.n_chunks,
                         b.att_o if b.n_chunks > 1 else None, b.att_ml if b.n_chunks > 1 else None,
-                        b.attn)
+                        b.attn, self.batch_invariant)
             n += 3 + (1 if b.n_chunks > 1 else 0)
             gbt, s, direct = pl["o"]
             if tp is not None:   # row-parallel: partials exchanged, reduced in the norm

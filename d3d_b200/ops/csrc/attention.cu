@@ -817,11 +817,13 @@ static void launch_attn_cluster_nt(const AttnArgs& a, cudaStream_t st) {
   else launch_attn_cluster<D, 2>(a, st);
 }
 
-// Dispatch: decode-shaped launches (one 64-row tile per sequence and kv head:
-// verify blocks and single tokens) take the cluster kernel; larger query
-// counts (prefill, the drafter's packed forward) take the split-KV kernels,
-// whose CTAs run independently (no cluster barrier to wait at when the rows
-// of a tile need uneven numbers of key tiles) when partial buffers are given.
+// Dispatch: batch-invariant callers (``invariant``: the target, whose verify
+// and AR forwards must agree bit for bit) and decode-shaped launches (one
+// 64-row tile per sequence and kv head) take the cluster kernel; larger
+// query counts of other callers (the drafter's packed forward) take the
+// split-KV kernels, whose CTAs run independently (no cluster barrier to wait
+// at when the rows of a tile need uneven numbers of key tiles) when partial
+// buffers are given.
 void attention(const AttnArgs& a, cudaStream_t st) {
   if (a.B == 0 || a.q_len == 0) return;
   static const bool force_split = [] {
@@ -829,7 +831,7 @@ void attention(const AttnArgs& a, cudaStream_t st) {
     return e && std::string(e) == "split";
   }();
   const bool one_tile = a.q_len * (a.Hq / a.Hkv) <= AT_ROWS;
-  if ((!one_tile || force_split) && (a.n_chunks == 1 || (a.part_o && a.part_ml))) {
+  if ((force_split || (!one_tile && !a.invariant)) && (a.n_chunks == 1 || (a.part_o && a.part_ml))) {
     attention_split(a, st);
     return;
   }

@@ -209,7 +209,8 @@ void greedy_accept(Tensor blocks, Tensor post, Tensor commit, Tensor corr, c10::
 
 void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor rows, Tensor kv_end,
                int64_t B, int64_t q_len, int64_t Hq, int64_t Hkv, int64_t page_size, double scale, int64_t chunk,
-               int64_t n_chunks, c10::optional<Tensor> part_o, c10::optional<Tensor> part_ml, Tensor out) {
+               int64_t n_chunks, c10::optional<Tensor> part_o, c10::optional<Tensor> part_ml, Tensor out,
+               bool invariant) {
   const c10::cuda::CUDAGuard g(q.device());
   CHECK_CONTIG(q);
   CHECK_CONTIG(out);
@@ -236,6 +237,7 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
   a.scale = static_cast<float>(scale);
   a.chunk = static_cast<int>(chunk);
   a.n_chunks = static_cast<int>(n_chunks);
+  a.invariant = invariant ? 1 : 0;
   a.part_o = part_o ? part_o->data_ptr<float>() : nullptr;
   a.part_ml = part_ml ? part_ml->data_ptr<float>() : nullptr;
   a.out = bf(out);
@@ -446,7 +448,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed", &embed);
   m.def("topk_merge", &topk_merge);
   m.def("greedy_accept", &greedy_accept);
-  m.def("attention", &attention);
+  m.def("attention", &attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
+        py::arg("rows"), py::arg("kv_end"), py::arg("B"), py::arg("q_len"), py::arg("Hq"), py::arg("Hkv"),
+        py::arg("page_size"), py::arg("scale"), py::arg("chunk"), py::arg("n_chunks"), py::arg("part_o"),
+        py::arg("part_ml"), py::arg("out"), py::arg("invariant") = false);
   m.def("gemm_stages", &d3d::gemm_stages);
   m.def("kl_ce_stats", &kl_ce_stats);
   m.def("kl_ce_grad", &kl_ce_grad);

@@ -48,6 +48,7 @@ struct AttnArgs {
   float scale;
   int chunk;                // keys per split (multiple of 64); one split when >= max kv
   int n_chunks;
+  int invariant;            // batch-invariant path: same kernel whatever q_len (target decode)
   float* part_o;            // [n_chunks][T][Hq][D]
   float* part_ml;           // [n_chunks][T][Hq][2]
   __nv_bfloat16* out;       // [T][Hq][D]
