@@ -176,6 +176,9 @@ class P2PTargetServer:
             self.link.recv(self.req[:HEAD_WORDS], self.stream, deadline_s=self.deadline_s, poll=poll)
             h = self.req[:HDR].tolist()
             cmd = h[0]
+            chk = getattr(self.be, "check_tp", None)
+            if chk is not None:
+                chk()   # a failed tensor-parallel exchange ends serving loudly
             if cmd == CMD_PREFILL:
                 words = HDR + 2 * h[1] + h[2]
                 if words > HEAD_WORDS:

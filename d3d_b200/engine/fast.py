@@ -163,8 +163,23 @@ class FastTarget(_FastModelBackend, TargetBackend):
                          max_context=max_context, extra_slots=64, batch_invariant=True,
                          use_graphs=use_graphs, device=device, stream=stream, tp=tp)
         self.hidden_size = self.cfg.hidden_size
+        self.tp = tp
         self._pending = None
         self._accept_bufs: Dict[tuple, dict] = {}
+        if tp is not None:
+            # every rank is ready before the first exchange, so no rank's
+            # bounded flag wait runs out while a peer still initialises
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.device)
+            if dist.is_initialized():
+                dist.barrier(group=tp.group)
+
+    def check_tp(self) -> None:
+        """Raise if a tensor-parallel exchange of this rank ran out of its
+        bounded wait (results since then are not valid)."""
+        if self.tp is not None and int(self.tp.status.item()) != 0:
+            raise RuntimeError(f"tensor-parallel exchange failed on rank {self.tp.rank} "
+                               f"(status {int(self.tp.status.item())})")
         self.verify_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
         self.time_verify = False
 

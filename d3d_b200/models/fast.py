@@ -463,10 +463,8 @@ class FastRunner:
             gbt, s, direct = pl["o"]
             if tp is not None:   # row-parallel: partials exchanged, reduced in the norm
                 xo = 2 * li
-                E.gemm_partial(b.attn, L.o.data, tp.part_view(xo, s * T * c.hidden_size), s, gbt, b.status, L.o.n)
-                tp.signal(xo)
+                tp.gemm(b.attn, L.o, xo, s, gbt)
                 tp.add_rmsnorm(xo, xo, s, b.x, L.post_norm, b.xn, eps)
-                n += 1
             elif direct:   # residual added in the epilogue, in place
                 E.gemm_bf16(b.attn, L.o.data, b.x, b.x, gbt, b.status, L.o.n)
                 E.add_rmsnorm(None, 1, b.x, L.post_norm, b.xn, eps)
@@ -485,11 +483,8 @@ class FastRunner:
             gbt, s, direct = pl["down"]
             if tp is not None:
                 xd = 2 * li + 1
-                E.gemm_partial(b.h, L.down.data, tp.part_view(xd, s * T * c.hidden_size), s, gbt, b.status,
-                               L.down.n)
-                tp.signal(xd)
+                tp.gemm(b.h, L.down, xd, s, gbt)
                 tp.add_rmsnorm(xd, xd, s, b.x, nxt, b.xn, eps)
-                n += 1
             elif direct:
                 E.gemm_bf16(b.h, L.down.data, b.x, b.x, gbt, b.status, L.down.n)
                 E.add_rmsnorm(None, 1, b.x, nxt, b.xn, eps)

@@ -388,6 +388,32 @@ d3d::TpArgs tp_args(Tensor ptrs, int64_t rank, Tensor epoch, c10::optional<Tenso
   return a;
 }
 
+// Row-parallel GEMM of a tensor-parallel rank: fp32 partials pushed into
+// every rank's exchange region at ``part_off`` (slot rank * splits + split),
+// flags raised for exchange ``x`` by the last CTA.
+void gemm_partial_tp(Tensor x, Tensor w, Tensor ptrs, int64_t rank, Tensor epoch, Tensor ticket, int64_t xidx,
+                     int64_t part_off, int64_t splits, int64_t bt, c10::optional<Tensor> status, int64_t wn) {
+  const c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, static_cast<int>(bt), status, wn);
+  const d3d::TpArgs t = tp_args(ptrs, rank, epoch, status);
+  CHECK_DT(ticket, torch::kInt32);
+  TORCH_CHECK(part_off % 16 == 0, "gemm_partial_tp: partial offset must be 16-byte aligned");
+  a.mode = 0;
+  a.splits = static_cast<int>(splits);
+  a.tp = t.tp;
+  a.tp_rank = t.rank;
+  a.tp_x = static_cast<int>(xidx);
+  for (int r = 0; r < t.tp; ++r) {
+    a.tp_out[r] = reinterpret_cast<float*>(t.parts[r] + part_off);
+    a.tp_flags[r] = t.flags[r];
+  }
+  a.tp_epoch = t.epoch;
+  a.tp_ticket = reinterpret_cast<unsigned int*>(ticket.data_ptr<int>());
+  a.out_f32 = a.tp_out[t.rank];
+  if (a.M == 0) return;
+  d3d::gemm_launch(a, cur_stream());
+}
+
 void tp_epoch_bump(Tensor epoch) {
   const c10::cuda::CUDAGuard g(epoch.device());
   d3d::tp_epoch_bump(epoch.data_ptr<int64_t>(), cur_stream());
@@ -470,6 +496,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status"));
   m.def("accept_send", &accept_send);
   m.def("tp_epoch_bump", &tp_epoch_bump);
+  m.def("gemm_partial_tp", &gemm_partial_tp, py::arg("x"), py::arg("w"), py::arg("ptrs"), py::arg("rank"),
+        py::arg("epoch"), py::arg("ticket"), py::arg("xidx"), py::arg("part_off"), py::arg("splits"),
+        py::arg("bt"), py::arg("status") = py::none(), py::arg("wn") = 0);
   m.def("tp_signal", &tp_signal);
   m.def("add_rmsnorm_tp", &add_rmsnorm_tp, py::arg("ptrs"), py::arg("rank"), py::arg("epoch"), py::arg("x"),
         py::arg("part_off"), py::arg("nsplit"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"),

@@ -24,6 +24,13 @@ struct GemmParams {
   int w_packed;
   int* status;
   unsigned long long timeout_ns;
+  // tensor-parallel push (MODE 0): partials of split s go to slot (tp_rank * splits + s)
+  // of every rank's exchange buffer; the last CTA raises flags[j][x * tp + tp_rank] = *epoch
+  int tp, tp_rank, tp_x;
+  float* tp_out[8];
+  int64_t* tp_flags[8];
+  int64_t* tp_epoch;
+  unsigned int* tp_ticket;
 };
 
 struct GemmArgs {
@@ -44,6 +51,12 @@ struct GemmArgs {
   int* status;                 // device error word (may be null)
   unsigned long long timeout_ns;
   int w_packed;                // w is in the packed tile layout (see pack_weight)
+  // tensor-parallel push (mode 0 only; tp = 0 disables): see GemmParams
+  int tp, tp_rank, tp_x;
+  float* tp_out[8];
+  int64_t* tp_flags[8];
+  int64_t* tp_epoch;
+  unsigned int* tp_ticket;
 };
 
 void gemm_launch(const GemmArgs& a, cudaStream_t stream);

@@ -261,12 +261,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
           float v[16];
           tmem_ld16(tacc + c, v);
           if constexpr (MODE == 0) {
-            if (n_ok) {
+            if (n_ok && p.tp == 0) {
               float* base = p.out_f32 + static_cast<size_t>(u.split) * p.M * p.N;
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 const int m = m0 + c + j;
                 if (c + j < cols) base[static_cast<size_t>(m) * p.N + n] = v[j];
+              }
+            } else if (n_ok) {
+              // tensor parallel: the same partial into every rank's exchange
+              // buffer (peer stores over NVLink), slot rank * splits + split
+              const size_t slot = static_cast<size_t>(p.tp_rank * p.splits + u.split) * p.M * p.N;
+              for (int r = 0; r < p.tp; ++r) {
+                float* base = p.tp_out[r] + slot;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int m = m0 + c + j;
+                  if (c + j < cols) base[static_cast<size_t>(m) * p.N + n] = v[j];
+                }
               }
             }
           } else if constexpr (MODE == 1) {
@@ -390,7 +402,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
   }
 
   // ---------------------------------------------------------------- teardown
+  if (MODE == 0 && p.tp > 0) __threadfence_system();  // this thread's peer stores, before the flags
   __syncthreads();
+  if (MODE == 0 && p.tp > 0 && threadIdx.x == 0) {
+    // the last CTA to finish publishes the exchange on every rank
+    const unsigned int t = atomicAdd(p.tp_ticket, 1u);
+    if (t == gridDim.x - 1) {
+      *p.tp_ticket = 0;
+      __threadfence_system();
+      const int64_t e = *p.tp_epoch;
+      for (int r = 0; r < p.tp; ++r) {
+        int64_t* f = p.tp_flags[r] + static_cast<size_t>(p.tp_x) * p.tp + p.tp_rank;
+        asm volatile("st.release.sys.global.s64 [%0], %1;" ::"l"(f), "l"(e) : "memory");
+      }
+    }
+  }
   if (threadIdx.x == 32) {
     // every MMA this thread issued has retired before TMEM is released
     umma_commit(done);
@@ -536,6 +562,19 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   p.stages = stages_for(a.bt, reserve);
   p.status = a.status;
   p.timeout_ns = a.timeout_ns;
+  p.tp = a.tp;
+  if (a.tp > 0) {
+    if (a.mode != 0 || a.tp > 8 || !a.tp_epoch || !a.tp_ticket)
+      throw std::runtime_error("gemm: tensor-parallel push needs mode 0, tp <= 8, epoch and ticket");
+    p.tp_rank = a.tp_rank;
+    p.tp_x = a.tp_x;
+    for (int r = 0; r < a.tp; ++r) {
+      p.tp_out[r] = a.tp_out[r];
+      p.tp_flags[r] = a.tp_flags[r];
+    }
+    p.tp_epoch = a.tp_epoch;
+    p.tp_ticket = a.tp_ticket;
+  }
   const int ntn = (a.N + GBN - 1) / GBN;
   p.ntiles = ntn;
   const int units = ntn * ((a.M + a.bt - 1) / a.bt) * a.splits;

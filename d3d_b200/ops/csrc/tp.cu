@@ -1,15 +1,17 @@
 // Tensor-parallel exchange kernels (sm_100a, one process per GPU).
 //
-// The target's row-parallel GEMMs (o_proj, down_proj) write fp32 split-K
-// partials into a per-rank exchange region that every peer has mapped
-// through CUDA IPC.  After the GEMM, tp_signal publishes "exchange x of
-// forward e is ready" on every rank with a system-scope release store, and
-// the consumer -- add_rmsnorm_tp, the residual add + RMSNorm of the next
-// sublayer -- waits (bounded, acquire) for all ranks' flags, then sums the
-// TP x S partials of each element in a fixed order (rank-major, then split),
-// reading the peers' partials over NVLink.  That is an all-reduce fused into
-// the reduction the single-GPU path already does, with the same
-// batch-invariant order.  The vocab-parallel LM head exchanges per-rank top-k
+// The target's row-parallel GEMMs (o_proj, down_proj) push their fp32
+// split-K partials from the GEMM epilogue into every rank's exchange region
+// (peer stores over NVLink into buffers mapped through CUDA IPC; see the
+// tensor-parallel branch of gemm_tcgen05.cu), and the GEMM's last CTA
+// publishes "exchange x of forward e is ready" on every rank with a
+// system-scope release store.  The consumer -- add_rmsnorm_tp, the residual
+// add + RMSNorm of the next sublayer -- waits (bounded, acquire) for all
+// ranks' flags, then sums the TP x S partials of each element from local
+// memory in a fixed order (rank-major, then split).  That is an all-reduce
+// fused into the GEMM epilogue and into the reduction the single-GPU path
+// already does, with the same batch-invariant order.  (tp_signal remains for
+// producers that are not GEMMs.)  The vocab-parallel LM head exchanges per-rank top-k
 // candidates the same way (topk_merge_tp).
 //
 // Exchange regions are double-buffered by exchange parity: rank A rewrites a
@@ -99,8 +101,10 @@ __global__ void __launch_bounds__(512) add_rmsnorm_tp_kernel(const TpArgs a, int
     if (n < N) {
       const size_t off = static_cast<size_t>(m) * N + n;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      // every rank pushed its splits into slots [rank][split] of this rank's buffer
+      const float* mine = reinterpret_cast<const float*>(a.parts[a.rank] + part_off);
       for (int r = 0; r < a.tp; ++r) {
-        const float* base = reinterpret_cast<const float*>(a.parts[r] + part_off);
+        const float* base = mine + static_cast<size_t>(r) * nsplit * stride;
         float4 v[16];
 #pragma unroll
         for (int s = 0; s < 16; ++s)

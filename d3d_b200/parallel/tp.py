@@ -74,6 +74,7 @@ class TPGroup:
         self.mem = E.mailbox_view(self.base, self.nbytes, self.device.index)
         self.epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.ticket = torch.zeros(1, dtype=torch.int32, device=self.device)   # last-CTA counter of the GEMMs
         handles: List = [None] * dist.get_world_size(group)
         dist.all_gather_object(handles, (self.rank, E.ipc_handle(self.base, self.device.index)), group=group)
         by_rank = {r: h for r, h in handles}
@@ -111,6 +112,14 @@ class TPGroup:
 
     def signal(self, x: int) -> None:
         self.ext.tp_signal(self.ptrs, self.rank, self.epoch, x)
+
+    def gemm(self, x_act, w, x: int, splits: int, bt: int) -> None:
+        """Row-parallel GEMM of exchange ``x``: partials pushed to every rank
+        (buffer parity ``x & 1``), flags raised by the GEMM's last CTA."""
+        if 4 * splits * self.size * x_act.shape[0] * w.n > self.part_bytes:
+            raise ValueError("row-parallel partials exceed the exchange buffer")
+        self.ext.gemm_partial_tp(x_act, w.data, self.ptrs, self.rank, self.epoch, self.ticket, x,
+                                 self.part_offset(x), splits, bt, self.status, w.n)
 
     def add_rmsnorm(self, x: int, parity: int, nsplit: int, residual, w, out, eps: float) -> None:
         self.ext.add_rmsnorm_tp(self.ptrs, self.rank, self.epoch, x, self.part_offset(parity), nsplit,
