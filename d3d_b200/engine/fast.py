@@ -166,6 +166,8 @@ class FastTarget(_FastModelBackend, TargetBackend):
         self.tp = tp
         self._pending = None
         self._accept_bufs: Dict[tuple, dict] = {}
+        self.verify_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
+        self.time_verify = False
         if tp is not None:
             # every rank is ready before the first exchange, so no rank's
             # bounded flag wait runs out while a peer still initialises
@@ -180,8 +182,6 @@ class FastTarget(_FastModelBackend, TargetBackend):
         if self.tp is not None and int(self.tp.status.item()) != 0:
             raise RuntimeError(f"tensor-parallel exchange failed on rank {self.tp.rank} "
                                f"(status {int(self.tp.status.item())})")
-        self.verify_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
-        self.time_verify = False
 
     @torch.inference_mode()
     def prefill(self, seqs):

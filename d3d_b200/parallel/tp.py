@@ -91,6 +91,10 @@ class TPGroup:
         self.ptrs = torch.tensor([[b for b in self.peer_bases],
                                   [b for b in self.peer_bases]], dtype=torch.int64)
         self.closed = False
+        # measurement only (D3D_TP_LOCAL=1): skip every cross-rank step (local
+        # partials, no flags) to time what the exchanges cost; results are wrong
+        import os
+        self.local_only = os.environ.get("D3D_TP_LOCAL") == "1"
 
     # --------------------------------------------------------------- layout
     def part_offset(self, parity: int) -> int:
@@ -111,6 +115,8 @@ class TPGroup:
         self.ext.tp_epoch_bump(self.epoch)
 
     def signal(self, x: int) -> None:
+        if self.local_only:
+            return
         self.ext.tp_signal(self.ptrs, self.rank, self.epoch, x)
 
     def gemm(self, x_act, w, x: int, splits: int, bt: int) -> None:
@@ -118,14 +124,23 @@ class TPGroup:
         (buffer parity ``x & 1``), flags raised by the GEMM's last CTA."""
         if 4 * splits * self.size * x_act.shape[0] * w.n > self.part_bytes:
             raise ValueError("row-parallel partials exceed the exchange buffer")
+        if self.local_only:
+            self.ext.gemm_partial(x_act, w.data, self.part_view(x, splits * x_act.shape[0] * w.n), splits, bt,
+                                  self.status, w.n)
+            return
         self.ext.gemm_partial_tp(x_act, w.data, self.ptrs, self.rank, self.epoch, self.ticket, x,
                                  self.part_offset(x), splits, bt, self.status, w.n)
 
     def add_rmsnorm(self, x: int, parity: int, nsplit: int, residual, w, out, eps: float) -> None:
+        if self.local_only:
+            self.ext.add_rmsnorm(self.part_view(parity, nsplit * residual.numel()), nsplit, residual, w, out, eps)
+            return
         self.ext.add_rmsnorm_tp(self.ptrs, self.rank, self.epoch, x, self.part_offset(parity), nsplit,
                                 residual, w, out, eps, self.status)
 
     def merge_topk(self, x: int, M: int, k: int, ov, oi) -> None:
+        if self.local_only:
+            return
         self.ext.topk_merge_tp(self.ptrs, self.rank, self.epoch, x, self.cand_off, M, k, ov, oi, self.status)
 
     def close(self) -> None:
