@@ -121,14 +121,26 @@ def run(args, rank, world, local):
         attn = "flash_attention_2"
     except ImportError:
         attn = "sdpa"
-    visible, worker_dev = ea._isolated_cuda_device(dev)
+    # Layout: with an even number of GPUs the reference runs in its stock
+    # two-GPU arrangement (its CLI defaults: verifier on one GPU, drafter on
+    # another), one pair per two ranks: the even rank drives the decode with
+    # its verifier process on the partner GPU, the odd rank only joins the
+    # collectives.  One GPU (or --layout replica): both on the rank's GPU.
+    layout = getattr(args, "layout", "auto")
+    pairs = world > 1 and world % 2 == 0 and layout in ("auto", "disagg")
+    active = not pairs or rank % 2 == 0
+    verifier_dev = f"cuda:{local + 1}" if pairs else dev
+    n = args.warmup + args.steps
+    if not active:
+        return _idle_rank(args, world, local, pairs, attn, barrier, dist_max, dist_sum, ClockSampler)
+    visible, worker_dev = ea._isolated_cuda_device(verifier_dev)
     verifier = ea.VerifierProcessClient(str(tgt_path), worker_dev, "bf16", attn, (), visible)
     drafter = es._load_model(str(drf_path), torch.bfloat16, attn_implementation=attn).to(dev).eval()
     es._disable_default_cache(drafter)
     verifier.wait_ready()
 
-    n = args.warmup + args.steps
-    prompts = make_prompts(n, args.prompt_min, args.prompt_max, seed=1000 + 7919 * rank + args.seed)
+    prompts = make_prompts(n, args.prompt_min, args.prompt_max,
+                           seed=1000 + 7919 * (rank // 2 if pairs else rank) + args.seed)
     ids = [torch.tensor([p], dtype=torch.long) for p in prompts]
 
     # --- AR baseline: target-only decoding through the reference verifier
@@ -205,7 +217,7 @@ def run(args, rank, world, local):
 
     opts = dict(block_size=args.block_size, denoising_steps=1, threshold=0.9, remasking="low_confidence",
                 top_k=0, top_p=1.0, target_top_k=0, target_top_p=1.0, return_stats=True,
-                verifier_device=dev, draft_device=dev, async_blocks=1, attention_mask_mode="causal",
+                verifier_device=verifier_dev, draft_device=dev, async_blocks=1, attention_mask_mode="causal",
                 anchor_num=args.anchor_num, packed_accepted_counts=None)
 
     def one(i):
@@ -236,7 +248,8 @@ def run(args, rank, world, local):
 
     dev_max = dist_max(dev_s)
     value = dist_sum(tokens) / dev_max
-    ar_value = dist_sum(ar_tokens) / dist_max(ar_time) if ar_time > 0 else None
+    ar_all, ar_max = dist_sum(ar_tokens), dist_max(ar_time)   # every rank, same order
+    ar_value = ar_all / ar_max if ar_max > 0 else None
     return {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -244,9 +257,11 @@ def run(args, rank, world, local):
         "vs_baseline": round(value / BASELINE_TPS, 4), "dtype": "bf16",
         "data": "synthetic seeded random-token prompts, random-init weights, acceptance-controlled drafts",
         "config": {"model": "Qwen3-8B-layout target + D3D-1.7B-layout drafter (reference classes)",
-                   "global_batch": world, "seq_len": f"prompt {args.prompt_min}-{args.prompt_max} + "
-                   f"{args.max_new_tokens} new", "parallelism": f"replica per GPU x{world} "
-                   "(reference verifier process + drafter on the same GPU)",
+                   "global_batch": world // 2 if pairs else world,
+                   "seq_len": f"prompt {args.prompt_min}-{args.prompt_max} + {args.max_new_tokens} new",
+                   "parallelism": (f"reference two-GPU pairs x{world // 2} (verifier process on one GPU, "
+                                   "drafter on the partner GPU)") if pairs else
+                   f"replica per GPU x{world} (reference verifier process + drafter on the same GPU)",
                    "concurrency": 1, "anchor_num": args.anchor_num,
                    "controlled_accept_mean": args.accept_mean,
                    "measured_accept_mean": round(statistics.fmean(accepts), 3) if accepts else None,
@@ -257,3 +272,18 @@ def run(args, rank, world, local):
         "token_identical_to_ar": bool(dist_sum(1.0 if ident else 0.0) == world),
         "clocks": clk.summary(),
     }
+
+
+def _idle_rank(args, world, local, pairs, attn, barrier, dist_max, dist_sum, ClockSampler):
+    """The odd rank of a pair: its GPU hosts the partner's verifier process;
+    it joins the same collectives as the active rank, with nothing to add."""
+    barrier()
+    with ClockSampler(local) as clk:
+        barrier()
+        barrier()
+    dist_max(0.0)
+    dist_sum(0)
+    dist_sum(0)
+    dist_max(0.0)
+    dist_sum(1.0)
+    return None
