@@ -74,6 +74,13 @@ class ControlledAcceptance:
     stream: int = 0                 # request index
     exclude: Sequence[int] = ()     # tokens never produced by corruption (e.g. MASK, EOS)
 
+    def __post_init__(self):
+        # draft_at and the alternatives row are pure functions of the position
+        # (and, for the anchor row, of the anchor token): memoised, since the
+        # same positions are rewritten by every branch that covers them
+        self._draft_cache = {}
+        self._row_cache = {}
+
     def keep(self, pos: int) -> bool:
         return uniform(self.seed, self.stream, pos) >= self.rate
 
@@ -90,10 +97,33 @@ class ControlledAcceptance:
         return int(self.oracle[pos]) if 0 <= pos < len(self.oracle) else None
 
     def draft_at(self, pos: int) -> int:
-        o = self.oracle_at(pos)
-        if o is None:
-            return self._corrupt(0, pos, 7)
-        return o if self.keep(pos) else self._corrupt(o, pos, 1)
+        v = self._draft_cache.get(pos)
+        if v is None:
+            o = self.oracle_at(pos)
+            if o is None:
+                v = self._corrupt(0, pos, 7)
+            else:
+                v = o if self.keep(pos) else self._corrupt(o, pos, 1)
+            self._draft_cache[pos] = v
+        return v
+
+    def _alts(self, pos: int, first: int, anchor_row: bool, w: int):
+        key = (pos, first, anchor_row, w)
+        row = self._row_cache.get(key)
+        if row is None:
+            o = self.oracle_at(pos)
+            alts = []
+            if not anchor_row and o is not None and o != first:
+                alts.append(o)
+            salt = 11
+            while len(alts) < w - 1:
+                c = self._corrupt(first, pos, salt)
+                salt += 1
+                if c not in alts and (o is None or c != o or anchor_row):
+                    alts.append(c)
+            row = [first] + alts[: w - 1]
+            self._row_cache[key] = row
+        return row
 
     def override(self, block: torch.Tensor, top: Optional[torch.Tensor], anchor_pos: int):
         """Rewrite drafts 1..K-1 of ``block`` (anchor at ``anchor_pos``) and its
@@ -103,20 +133,8 @@ class ControlledAcceptance:
         block[1:] = torch.tensor(vals, dtype=block.dtype, device=block.device)
         if top is not None:
             w = int(top.shape[-1])
-            rows = []
-            for i in range(k):
-                pos = anchor_pos + i
-                first = int(block[i])
-                o = self.oracle_at(pos)
-                alts = []
-                if i > 0 and o is not None and o != first:
-                    alts.append(o)
-                salt = 11
-                while len(alts) < w - 1:
-                    c = self._corrupt(first, pos, salt)
-                    salt += 1
-                    if c not in alts and (o is None or c != o or i == 0):
-                        alts.append(c)
-                rows.append([first] + alts[: w - 1])
+            first0 = int(block[0])
+            rows = [self._alts(anchor_pos, first0, True, w)]
+            rows += [self._alts(anchor_pos + i, vals[i - 1], False, w) for i in range(1, k)]
             top.copy_(torch.tensor(rows, dtype=top.dtype, device=top.device))
         return block, top

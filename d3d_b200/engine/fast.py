@@ -224,12 +224,18 @@ class FastTarget(_FastModelBackend, TargetBackend):
             return n + 1
         return fn
 
+    supports_gather = True
+
     @torch.inference_mode()
-    def submit_verify(self, seqs, blocks, q=None, sink=None):
+    def submit_verify(self, seqs, blocks, q=None, sink=None, gather=None):
         """Enqueue one verify of ``blocks`` [B, K].  With ``sink`` given, it is
         called on the target stream right after the verify graph as
         ``sink(ids [B, K], posterior [B, K], hidden [B*K, H])`` (device views
-        of the graph's buffers) and nothing is copied back to this host."""
+        of the graph's buffers) and nothing is copied back to this host.
+        ``gather``: ``[(src [R, k] device ids, dst positions in the flattened
+        [B*K] block, src rows)]`` -- block entries taken on the device from a
+        drafter forward still in flight (column 0 of ``src``), so the verify
+        can be enqueued before the host has the draft."""
         if q is not None:
             raise NotImplementedError("the fast target path verifies greedily (temperature 0)")
         B, K = blocks.shape
@@ -239,6 +245,14 @@ class FastTarget(_FastModelBackend, TargetBackend):
         rows = np.stack([causal_rows(s.prefix, K).numpy() for s in seqs])
         kv_end = np.array([s.prefix + K for s in seqs])
         self._fill(b, seqs, blocks.numpy(), pos, rows, kv_end, f"v{B}_{K}")
+        if gather:
+            with torch.cuda.stream(self.stream):
+                flat = b.ids.view(-1)
+                for src, dst, rws in gather:
+                    d = torch.as_tensor(dst, dtype=torch.int64).to(self.device, non_blocking=True)
+                    r = torch.as_tensor(rws, dtype=torch.int64).to(self.device, non_blocking=True)
+                    flat.index_copy_(0, d, src[:, 0].index_select(0, r))
+            launches.add(2 * len(gather))
         ev0 = ev1 = None
         if self.time_verify:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -289,6 +303,8 @@ class FastDraft(_FastModelBackend, DraftBackend):
         self.mask_id = int(self.cfg.mask_token_id)
         self._host: Dict[tuple, dict] = {}
 
+    supports_async = True
+
     @torch.inference_mode()
     def prefill(self, seqs, mode, block_size):
         for s in seqs:
@@ -307,7 +323,13 @@ class FastDraft(_FastModelBackend, DraftBackend):
         return h
 
     @torch.inference_mode()
-    def forward(self, seqs, ids, positions, rows, *, store, topk, cond_rows=None, sample=None):
+    def forward(self, seqs, ids, positions, rows, *, store, topk, cond_rows=None, sample=None,
+                wait: bool = True):
+        """One drafter forward.  With ``wait=False`` it returns a handle right
+        after enqueueing; ``handle.result()`` waits and gives the usual dict.
+        Either way the dict also carries ``"dev_top"``: the device top-k ids
+        [B*Q, k], valid until the next forward of the same shape is enqueued
+        (stream order makes device reads enqueued before that safe)."""
         if sample is not None:
             raise NotImplementedError("the fast draft path proposes greedily (temperature 0)")
         B, Q = ids.shape
@@ -328,12 +350,26 @@ class FastDraft(_FastModelBackend, DraftBackend):
         with torch.cuda.stream(self.stream):
             h["top"].copy_(b.top_i, non_blocking=True)
             h["ev"].record(self.stream)
-        h["ev"].synchronize()
-        top = h["top"].view(B, Q, k).clone()
-        out = {"greedy": top[:, :, 0]}
-        if topk:
-            out["top"] = top[:, :, :topk]
-        return out
+        handle = _PendingDraft(h, B, Q, k, topk, b.top_i)
+        return handle.result() if wait else handle
 
     def release(self, seq):
         self._release(seq)
+
+
+class _PendingDraft:
+    """A drafter forward in flight (``FastDraft.forward(..., wait=False)``)."""
+
+    def __init__(self, h, B, Q, k, topk, dev_top):
+        self.h, self.B, self.Q, self.k, self.topk, self.dev_top = h, B, Q, k, topk, dev_top
+        self._out = None
+
+    def result(self) -> dict:
+        if self._out is None:
+            self.h["ev"].synchronize()
+            top = self.h["top"].view(self.B, self.Q, self.k).clone()
+            out = {"greedy": top[:, :, 0], "dev_top": self.dev_top}
+            if self.topk:
+                out["top"] = top[:, :, :self.topk]
+            self._out = out
+        return self._out

@@ -72,11 +72,30 @@ class RequestOutput:
 
 class _Outcomes:
     """The branches of one packed forward for one sequence, sliced on demand
-    (only the branch that matches the verification outcome is materialised)."""
+    (only the branch that matches the verification outcome is materialised).
+    ``out`` may be a drafter forward still in flight (a handle with
+    ``result()``); it is resolved the first time a branch is read."""
 
-    def __init__(self, lay, out: Dict[str, torch.Tensor], i: int):
-        self.lay, self.out, self.i = lay, out, i
+    def __init__(self, lay, out, i: int, q_len: int = 0):
+        self.lay, self._out, self.i, self.q_len = lay, out, i, q_len
         self.index = {key: j for j, key in enumerate(lay.keys)}
+
+    @property
+    def out(self) -> Dict[str, torch.Tensor]:
+        if not isinstance(self._out, dict):
+            self._out = self._out.result()
+        return self._out
+
+    def has(self, key) -> bool:
+        return key in self.index
+
+    def device_rows(self, key):
+        """(device top-k ids of the forward, rows holding drafts 1..K-1 of
+        branch ``key``): what the target's verify input gathers on the device."""
+        sl = self.lay.segment(self.index[key])
+        src = self._out.dev_top if not isinstance(self._out, dict) else self._out["dev_top"]
+        base = self.i * self.q_len + sl.start
+        return src, list(range(base + 1, base + (sl.stop - sl.start)))
 
     def get(self, key):
         j = self.index.get(key)
@@ -153,9 +172,20 @@ class SpecDecoder:
                 s.source = "redraft"
 
     # ------------------------------------------------------ packed outcomes
-    def predict(self, seqs: List[SeqState]) -> Dict[int, "_Outcomes"]:
+    def _pipelined(self) -> bool:
+        """Whether the next verify may be enqueued behind a drafter forward still
+        in flight, its draft tokens gathered on the device (kernel backends of
+        one GPU, greedy)."""
+        return (is_greedy(self.cfg.temperature) and getattr(self.t, "supports_gather", False)
+                and getattr(self.d, "supports_async", False)
+                and getattr(self.t, "stream", None) is not None
+                and getattr(self.t, "stream", None) is getattr(self.d, "stream", None))
+
+    def predict(self, seqs: List[SeqState], wait: bool = True) -> Dict[int, "_Outcomes"]:
         """One packed forward per micro-batch: commit the pending block into the
-        draft KV and draft one continuation per (commit length, anchor)."""
+        draft KV and draft one continuation per (commit length, anchor).  With
+        ``wait=False`` (asynchronous drafter backends) the forwards are only
+        enqueued; each outcome resolves when first read."""
         k, a = self.cfg.block_size, self.cfg.anchor_num
         results: Dict[int, _Outcomes] = {}
         for off in range(0, len(seqs), self.cfg.draft_microbatch):
@@ -173,12 +203,13 @@ class SpecDecoder:
             pos = torch.stack([l.positions for l in layouts])
             rows = torch.stack([l.rows for l in layouts])
             seg_starts = [0] + [k + j * k for j in range(len(layouts[0].keys))]
+            kw = {} if wait else {"wait": False}
             out = self.d.forward(group, ids, pos, rows, store=True, topk=a + 1 if a else 0,
                                  cond_rows=self._cond_rows(len(group), q, seg_starts),
-                                 sample=self._sample_cfg())
+                                 sample=self._sample_cfg(), **kw)
             for i, (s, lay) in enumerate(zip(group, layouts)):
                 self.d.trim(s, s.prefix + k)
-                results[s.index] = _Outcomes(lay, out, i)
+                results[s.index] = _Outcomes(lay, out, i, q)
         return results
 
     # ------------------------------------------------------------ main loop
@@ -198,6 +229,7 @@ class SpecDecoder:
         verify_tokens = 0
         miss_rounds = 0
         batch_sizes: List[int] = []
+        preverified: Optional[torch.Tensor] = None   # block of a verify already enqueued
         while running or not exhausted:
             admitted: List[SeqState] = []
             while len(running) + len(admitted) < concurrency and not exhausted:
@@ -233,21 +265,27 @@ class SpecDecoder:
             # verified (one captured shape) and the commit is clipped instead,
             # which emits the same tokens.
             width = k
-            block_t = torch.stack([s.current[:k] for s in running])
             qq = None
-            if not is_greedy(cfg.temperature):
-                qq = (torch.stack([s.q_ids[1:width] for s in running]),
-                      torch.stack([s.q_probs[1:width] for s in running]))
-            with self.prof.phase("submit_verify"):
-                self.t.submit_verify(running, block_t, qq)
+            if preverified is not None:
+                # verify(t) was enqueued during the previous step, behind draft(t-1)
+                block_t, preverified = preverified, None
+            else:
+                block_t = torch.stack([s.current[:k] for s in running])
+                if not is_greedy(cfg.temperature):
+                    qq = (torch.stack([s.q_ids[1:width] for s in running]),
+                          torch.stack([s.q_probs[1:width] for s in running]))
+                with self.prof.phase("submit_verify"):
+                    self.t.submit_verify(running, block_t, qq)
+            pipe = self._pipelined()
             with self.prof.phase("predict"):
-                predictions = self.predict(running) if width == k else {}
+                predictions = self.predict(running, wait=not pipe) if width == k else {}
             with self.prof.phase("receive"):
                 res = self.t.receive()
             steps += 1
             verify_tokens += width * len(running)
             remaining, recover = [], []
             t_sel = time.perf_counter()
+            cont = []   # (sequence, commit length, correction, branch key)
             for i, s in enumerate(running):
                 n = int(res.commit[i])
                 corr = int(res.correction[i])
@@ -275,7 +313,25 @@ class SpecDecoder:
                     s.generated.append(corr)
                     self._finish(s, outputs)
                     continue
-                key = (n, None if (n == k or cfg.anchor_num == 0) else corr)
+                cont.append((s, n, corr, (n, None if (n == k or cfg.anchor_num == 0) else corr)))
+            # Every continuing sequence hit a drafted branch and nothing will be
+            # admitted: enqueue verify(t+1) now, behind draft(t) on the same
+            # stream, so the GPU goes straight on while the host selects.
+            nxt = None
+            if pipe and cont and (exhausted or len(cont) >= concurrency) and all(
+                    predictions.get(c[0].index) is not None and predictions[c[0].index].has(c[3])
+                    for c in cont):
+                nxt = torch.zeros(len(cont), k, dtype=torch.long)
+                gather = []
+                for r, (s, n, corr, key) in enumerate(cont):
+                    nxt[r, 0] = corr
+                    if s.controlled is not None:
+                        self._controlled(s, nxt[r], None, s.prefix)
+                    else:
+                        src, rows = predictions[s.index].device_rows(key)
+                        gather.append((src, [r * k + j for j in range(1, k)], rows))
+                self.t.submit_verify([c[0] for c in cont], nxt, gather=gather)
+            for r, (s, n, corr, key) in enumerate(cont):
                 pr = predictions.get(s.index)
                 sel = pr.get(key) if pr is not None else None
                 self.d.trim(s, s.prefix)
@@ -292,7 +348,13 @@ class SpecDecoder:
                         s.q_ids, s.q_probs = q2
                     s.hits += 1
                     s.source = "packed_full" if n == k else f"packed_outcome_{n}"
+                    if nxt is not None and s.controlled is None:
+                        nxt[r] = blk      # the host copy of what the device gathered
+                    elif nxt is not None and not torch.equal(nxt[r], blk):
+                        raise RuntimeError("pipelined verify input differs from the selected branch")
                 remaining.append(s)
+            if nxt is not None:
+                preverified = nxt
             if self.prof.enabled:
                 self.prof.host["select"] += time.perf_counter() - t_sel
             running = remaining

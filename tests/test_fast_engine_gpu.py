@@ -61,3 +61,29 @@ def test_fast_forward_tracks_oracle(fast_pair):
         rel = (hid[i].float().cpu() - h).norm() / h.norm()
         assert rel < 0.05, rel
         assert int(anchors[i]) == ref_a
+
+
+@pytest.mark.parametrize("controlled", [False, True])
+def test_pipelined_shared_stream_matches_ar(fast_pair, controlled):
+    """Target and drafter on one stream: each verify is enqueued behind the
+    drafter forward still in flight, its drafts gathered on the device (or
+    rewritten on the host in controlled mode); output equals AR."""
+    from d3d_b200.engine.controlled import ControlledAcceptance, rate_for_mean_accept
+    from d3d_b200.engine.fast import FastDraft, FastTarget
+    _, _, tw, dw = fast_pair
+    t = FastTarget(tw, pages=512, max_seqs=8, max_context=512)
+    d = FastDraft(dw, pages=2048, max_seqs=8, max_context=512, packed_q=1024, stream=t.stream)
+    prompts = _prompts(n=3, seed=7)
+    ar = ar_generate(t, prompts, max_new_tokens=48, ignore_eos=True)["outputs"]
+    cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=48, ignore_eos=True)
+    dec = SpecDecoder(t, d, cfg)
+    assert dec._pipelined()
+    ctl = None
+    if controlled:
+        rate = rate_for_mean_accept(4.0, 8)
+        ctl = lambda i: ControlledAcceptance(prompts[i] + ar[i], rate, 1024, stream=i, exclude=(1023,))
+    res = dec.generate(prompts, concurrency=3, controlled=ctl)
+    for o, ref in zip(res["outputs"], ar):
+        assert o.tokens == ref
+    if controlled:
+        assert sum(sum(o.accepts) for o in res["outputs"]) / sum(len(o.accepts) for o in res["outputs"]) > 2.0
