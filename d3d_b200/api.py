@@ -97,7 +97,7 @@ class D3DEngine:
         d = FastDraft(draft_w, pages=dp, page_size=page_size, max_seqs=max_seqs,
                       max_context=max_context, packed_q=packed_q, use_graphs=use_graphs, device=device)
         t = P2PTarget(link, target_hidden_size, device, deadline_s=deadline_s,
-                      want_hidden=decode.use_cond and draft_w.cond_proj is not None)
+                      want_hidden=decode.use_cond and draft_w.cond_proj is not None, draft_stream=d.stream)
         return cls(t, d, decode)
 
     def close(self) -> None:

@@ -104,7 +104,7 @@ def main():
         packed_q = paged_draft_branch_tokens(K, 1)
         dp = max(4, cc) * (max_ctx + packed_q + 16) // 16 + 8
         d = FastDraft(dw, pages=dp, max_seqs=max(4, cc), max_context=max_ctx, packed_q=packed_q, device=dev)
-        remote = P2PTarget(links, tcfg.hidden_size, dev, want_hidden=False)
+        remote = P2PTarget(links, tcfg.hidden_size, dev, want_hidden=False, draft_stream=d.stream)
         dec = SpecDecoder(remote, d, decode)
     shared = [None] * world
     dist.all_gather_object(shared, ar_out if rank == 0 else None)

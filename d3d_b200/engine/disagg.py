@@ -210,10 +210,14 @@ class P2PTarget(TargetBackend):
     """Drafter-side target backend whose target is served over ``link``."""
 
     def __init__(self, link, hidden_size: int, device=None, deadline_s: float = 600.0,
-                 want_hidden: bool = True):
+                 want_hidden: bool = True, draft_stream=None):
         """``link`` may be a list: the links to every rank of a tensor-parallel
         target (rank 0 first).  Requests go to all of them; results come from
-        rank 0, and RELEASE waits for every rank's acknowledgement."""
+        rank 0, and RELEASE waits for every rank's acknowledgement.
+        ``draft_stream``: the drafter's stream; with it (and GPU links) the
+        coordinator may submit a verify whose drafts are still being computed
+        -- the request is assembled on the device behind the drafter's
+        in-flight forward and sent from there (``gather``)."""
         self.links = list(link) if isinstance(link, (list, tuple)) else [link]
         link = self.links[0]
         self.link = link
@@ -228,6 +232,10 @@ class P2PTarget(TargetBackend):
         self.rep = torch.zeros(words, dtype=torch.int64, pin_memory=gpu)
         self._pending: Optional[tuple] = None
         self.closed = False
+        self.draft_stream = draft_stream
+        self.supports_gather = gpu and draft_stream is not None
+        self.dev_req = torch.zeros(HEAD_WORDS, dtype=torch.int64, device=self.device) if self.supports_gather \
+            else None
 
     def _send(self, n_words: int) -> None:
         n = (n_words + 1) // 2 * 2
@@ -276,7 +284,11 @@ class P2PTarget(TargetBackend):
         hid = self._bf16_block(_prefill_words(n), n, HEAD_WORDS).clone()
         return anchors, hid
 
-    def submit_verify(self, seqs, blocks, q=None):
+    def submit_verify(self, seqs, blocks, q=None, gather=None):
+        """Send a verify request.  ``gather`` (see ``FastTarget.submit_verify``):
+        the request is ordered after the drafter's work enqueued so far, its
+        listed block entries are taken on the device from the drafter's
+        output, and the put kernels send it from device memory."""
         if q is not None:
             raise NotImplementedError("the disaggregated target verifies greedily (temperature 0)")
         if self._pending is not None:
@@ -289,7 +301,25 @@ class P2PTarget(TargetBackend):
         rn = self.req.numpy()
         rn[HDR:HDR + 2 * B] = meta
         rn[HDR + 2 * B:need] = blocks.numpy().reshape(-1)
-        self._send(need)
+        if gather is None:
+            self._send(need)
+        else:
+            if not self.supports_gather or need > self.dev_req.numel():
+                raise RuntimeError("device-assembled requests need GPU links and a drafter stream")
+            n = (need + 1) // 2 * 2
+            with torch.cuda.stream(self.stream):
+                # ordered after the drafter's in-flight forward: a request never
+                # leaves before the drafts it carries exist
+                self.stream.wait_stream(self.draft_stream)
+                dev = self.dev_req[:n]
+                dev.copy_(self.req[:n], non_blocking=True)
+                body = self.dev_req[HDR + 2 * B:]
+                for src, dst, rws in gather:
+                    d = torch.as_tensor(dst, dtype=torch.int64).to(self.device, non_blocking=True)
+                    r = torch.as_tensor(rws, dtype=torch.int64).to(self.device, non_blocking=True)
+                    body.index_copy_(0, d, src[:, 0].index_select(0, r))
+            for lk in self.links:
+                lk.send(self.dev_req[:n], self.stream)
         self._pending = (B, K)
 
     def receive(self) -> VerifyResult:

@@ -178,8 +178,9 @@ class SpecDecoder:
         one GPU, greedy)."""
         return (is_greedy(self.cfg.temperature) and getattr(self.t, "supports_gather", False)
                 and getattr(self.d, "supports_async", False)
-                and getattr(self.t, "stream", None) is not None
-                and getattr(self.t, "stream", None) is getattr(self.d, "stream", None))
+                and getattr(self.d, "stream", None) is not None
+                and (getattr(self.t, "stream", None) is self.d.stream
+                     or getattr(self.t, "draft_stream", None) is self.d.stream))
 
     def predict(self, seqs: List[SeqState], wait: bool = True) -> Dict[int, "_Outcomes"]:
         """One packed forward per micro-batch: commit the pending block into the
