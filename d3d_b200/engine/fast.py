@@ -28,6 +28,12 @@ from ..utils.timing import NULL as _NULL_PROF
 from ..models.fast import FastRunner, FastWeights, PagedKV, StepBuffers
 from .backends import DraftBackend, SeqState, TargetBackend, VerifyResult
 from .layout import causal_rows, prefix_rows
+from .sampling import is_greedy, pq_accept_sparse
+
+
+def K_of(blocks) -> int:
+    """Block width (tokens per sequence) of a verify request."""
+    return int(blocks.shape[1])
 
 
 class _GraphCache:
@@ -155,10 +161,16 @@ class FastTarget(_FastModelBackend, TargetBackend):
 
     def __init__(self, weights: FastWeights, *, pages: int = 4096, page_size: int = 16,
                  max_seqs: int = 16, max_context: int = 4096, use_graphs: bool = True,
-                 device="cuda", stream=None, tp=None):
+                 device="cuda", stream=None, tp=None, temperature: float = 0.0, top_k: int = 0,
+                 top_p: float = 1.0, seed: int = 0):
         """``tp``: a :class:`~d3d_b200.parallel.tp.TPGroup` when ``weights`` is one
         shard of a tensor-parallel target (every rank of the group then runs
-        the same calls in the same order)."""
+        the same calls in the same order).
+
+        ``temperature > 0`` turns on lossless speculative sampling against the
+        target's distribution truncated to its ``top_k`` (1..4) tokens -- the
+        fused top-k epilogue of the LM head gives exactly those logits, so no
+        logits are materialised -- then ``top_p``."""
         super().__init__(weights, pages=pages, page_size=page_size, max_seqs=max_seqs,
                          max_context=max_context, extra_slots=64, batch_invariant=True,
                          use_graphs=use_graphs, device=device, stream=stream, tp=tp)
@@ -168,6 +180,15 @@ class FastTarget(_FastModelBackend, TargetBackend):
         self._accept_bufs: Dict[tuple, dict] = {}
         self.verify_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
         self.time_verify = False
+        self.temperature, self.top_k, self.top_p = float(temperature), int(top_k), float(top_p)
+        self.sampled = not is_greedy(self.temperature)
+        if self.sampled:
+            if not 1 <= self.top_k <= 4:
+                raise ValueError("sampled verification on the kernels needs target top_k in 1..4")
+            if tp is not None:
+                raise NotImplementedError("sampled verification with a tensor-parallel target")
+            self.gen = torch.Generator(device=self.device)
+            self.gen.manual_seed(int(seed))
         if tp is not None:
             # every rank is ready before the first exchange, so no rank's
             # bounded flag wait runs out while a peer still initialises
@@ -189,9 +210,14 @@ class FastTarget(_FastModelBackend, TargetBackend):
         for s in seqs:
             n = len(s.prompt)
             rows = causal_rows(0, n).numpy()
-            b = self._prefill_one(s, rows, topk=1, reserve=self.max_context + 64)
+            b = self._prefill_one(s, rows, topk=self.top_k if self.sampled else 1,
+                                  reserve=self.max_context + 64)
             with torch.cuda.stream(self.stream):
-                a = b.top_i[n - 1, 0].clone()
+                if self.sampled:
+                    pr = self._probs(b.top_v[n - 1:n])
+                    a = b.top_i[n - 1].gather(0, torch.multinomial(pr, 1, generator=self.gen)[0])[0]
+                else:
+                    a = b.top_i[n - 1, 0].clone()
                 h = b.xn[n - 1].clone()
             anchors.append(a)
             hid.append(h)
@@ -212,6 +238,35 @@ class FastTarget(_FastModelBackend, TargetBackend):
                      ev=torch.cuda.Event())
             self._accept_bufs[key] = a
         return a
+
+    def _probs(self, top_v: torch.Tensor) -> torch.Tensor:
+        """Sampling distribution over the top-k logits (temperature, then top-p)."""
+        sl = top_v.float() / self.temperature
+        if self.top_p < 1.0:
+            pr = torch.softmax(sl, -1)
+            remove = pr.cumsum(-1) > self.top_p
+            remove[..., 1:] = remove[..., :-1].clone()
+            remove[..., 0] = False
+            sl = sl.masked_fill(remove, float("-inf"))
+        return torch.softmax(sl, -1)
+
+    def _sampled_accept(self, b: StepBuffers, a: dict, q) -> None:
+        """Lossless acceptance of ``b``'s block against the verify forward's
+        top-k distribution (on the device; ``sampling.pq_accept_sparse``)."""
+        B, K = b.B, b.Q
+        vals = b.top_v.view(B, K, -1)[..., :self.top_k]
+        ids = b.top_i.view(B, K, -1)[..., :self.top_k]
+        dense = torch.zeros(B, K, self.cfg.vocab_size, device=self.device)
+        dense.scatter_(-1, ids, self._probs(vals))
+        qi = q[0].to(self.device, non_blocking=True)
+        qp = q[1].to(self.device, non_blocking=True)
+        u = torch.rand(B, K - 1, generator=self.gen, device=self.device)
+        cu = torch.rand(B, generator=self.gen, device=self.device)
+        commit, corr = pq_accept_sparse(b.ids.view(B, K), dense, qi, qp, u, cu)
+        a["commit"].copy_(commit)
+        a["corr"].copy_(corr)
+        rows = torch.arange(B, device=self.device) * K + commit - 1
+        a["hid"].copy_(b.xn.index_select(0, rows))
 
     def _verify_fn(self, a):
         E = ops.ext()
@@ -236,10 +291,13 @@ class FastTarget(_FastModelBackend, TargetBackend):
         [B*K] block, src rows)]`` -- block entries taken on the device from a
         drafter forward still in flight (column 0 of ``src``), so the verify
         can be enqueued before the host has the draft."""
-        if q is not None:
-            raise NotImplementedError("the fast target path verifies greedily (temperature 0)")
+        if (q is not None) != self.sampled and K_of(blocks) > 1:
+            raise ValueError("draft proposals (q) are required exactly when verification samples")
         B, K = blocks.shape
-        b = self.runner.buffers(B, K, 1)
+        sampled = self.sampled
+        if sampled and q is None:     # single-token verify (AR): only the next token is sampled
+            q = (torch.zeros(B, 0, 1, dtype=torch.long), torch.ones(B, 0, 1))
+        b = self.runner.buffers(B, K, self.top_k if sampled else 1)
         a = self._abufs(B, K)
         pos = np.stack([np.arange(s.prefix, s.prefix + K) for s in seqs])
         rows = np.stack([causal_rows(s.prefix, K).numpy() for s in seqs])
@@ -258,7 +316,12 @@ class FastTarget(_FastModelBackend, TargetBackend):
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record(self.stream)
         tok = self.prof.dev_begin(f"verify_B{B}_K{K}", self.stream)
-        self.graphs.run(("verify", B, K), b, self._verify_fn(a))
+        if sampled:
+            self.graphs.run(("verify_s", B, K, self.top_k), b, lambda bb: self.runner.forward(bb))
+            with torch.cuda.stream(self.stream):
+                self._sampled_accept(b, a, q)
+        else:
+            self.graphs.run(("verify", B, K), b, self._verify_fn(a))
         self.prof.dev_end(tok)
         if sink is not None:
             with torch.cuda.stream(self.stream):
@@ -330,10 +393,14 @@ class FastDraft(_FastModelBackend, DraftBackend):
         Either way the dict also carries ``"dev_top"``: the device top-k ids
         [B*Q, k], valid until the next forward of the same shape is enqueued
         (stream order makes device reads enqueued before that safe)."""
-        if sample is not None:
-            raise NotImplementedError("the fast draft path proposes greedily (temperature 0)")
         B, Q = ids.shape
         k = max(1, topk)
+        if sample is not None:
+            # proposals from the drafter's top-k (fused LM-head epilogue, k <= 4)
+            sk = int(sample.get("top_k") or 0)
+            if not 1 <= sk <= 4:
+                raise ValueError("sampled drafting on the kernels needs proposal top_k in 1..4")
+            k = max(k, sk)
         b = self.runner.buffers(B, Q, k)
         kv_end = torch.maximum(rows[:, :, 0].amax(1), rows[:, :, 2].amax(1)).numpy()
         use_cond = cond_rows is not None and self.w.cond_proj is not None and seqs[0].cond is not None
@@ -349,9 +416,35 @@ class FastDraft(_FastModelBackend, DraftBackend):
         h = self._hbufs(B, Q, k)
         with torch.cuda.stream(self.stream):
             h["top"].copy_(b.top_i, non_blocking=True)
+            if sample is not None:
+                sp, tok = self._propose(b.top_v[:, :sk], b.top_i[:, :sk], sample)
+                h["sp"] = sp.to("cpu")       # small; the sampled path is not pipelined
+                h["tok"] = tok.to("cpu")
+                h["sk"] = sk
+            else:
+                h["sk"] = 0
             h["ev"].record(self.stream)
         handle = _PendingDraft(h, B, Q, k, topk, b.top_i)
         return handle.result() if wait else handle
+
+    def _propose(self, vals, ids, sample):
+        """Sample one proposal per row from softmax(top-k logits / T) after
+        top-p; returns the proposal probabilities on the top-k support and
+        the sampled tokens (``sampling.sparse_proposal`` on the top-k)."""
+        if not hasattr(self, "gen"):
+            self.gen = torch.Generator(device=self.device)
+            self.gen.manual_seed(int(sample.get("seed", 0)))
+        sl = vals.float() / float(sample["temperature"])
+        tp = float(sample.get("top_p", 1.0))
+        if tp < 1.0:
+            pr = torch.softmax(sl, -1)
+            remove = pr.cumsum(-1) > tp
+            remove[..., 1:] = remove[..., :-1].clone()
+            remove[..., 0] = False
+            sl = sl.masked_fill(remove, float("-inf"))
+        sp = torch.softmax(sl, -1)
+        local = torch.multinomial(sp, 1, generator=self.gen)
+        return sp, ids.gather(1, local)[:, 0]
 
     def release(self, seq):
         self._release(seq)
@@ -371,5 +464,10 @@ class _PendingDraft:
             out = {"greedy": top[:, :, 0], "dev_top": self.dev_top}
             if self.topk:
                 out["top"] = top[:, :, :self.topk]
+            sk = self.h.get("sk", 0)
+            if sk:
+                out["tokens"] = self.h["tok"].view(self.B, self.Q).clone()
+                out["q_ids"] = top[:, :, :sk]
+                out["q_probs"] = self.h["sp"].view(self.B, self.Q, sk).clone()
             self._out = out
         return self._out

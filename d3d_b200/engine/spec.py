@@ -42,6 +42,8 @@ class DecodeConfig:
     temperature: float = 0.0
     top_k: int = 0            # proposal top-k (sampling)
     top_p: float = 1.0
+    target_top_k: int = 0     # target sampling truncation (0 = full vocabulary)
+    target_top_p: float = 1.0
     draft_microbatch: int = 4
     prefill_group: int = 4
     ignore_eos: bool = False

@@ -87,3 +87,28 @@ def test_pipelined_shared_stream_matches_ar(fast_pair, controlled):
         assert o.tokens == ref
     if controlled:
         assert sum(sum(o.accepts) for o in res["outputs"]) / sum(len(o.accepts) for o in res["outputs"]) > 2.0
+
+
+def test_sampled_kernel_path(fast_pair):
+    """Sampled speculative decoding on the kernels: runs end to end with
+    top-k (<= 4) proposals and target truncation, and at a temperature near
+    zero reproduces greedy AR decoding token for token."""
+    from d3d_b200.api import D3DEngine
+    _, _, tw, dw = fast_pair
+    prompts = _prompts(n=2, seed=11)
+    greedy = D3DEngine.from_weights(tw, dw, DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=32,
+                                                         ignore_eos=True), max_seqs=4, max_context=512)
+    ar = greedy.generate_ar(prompts)["outputs"]
+    cold = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=32, ignore_eos=True, temperature=2e-5,
+                        top_k=2, target_top_k=2)
+    eng = D3DEngine.from_weights(tw, dw, cold, max_seqs=4, max_context=512)
+    out = eng.generate(prompts)["outputs"]
+    assert [o.tokens for o in out] == ar
+    warm = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=32, ignore_eos=True, temperature=0.8,
+                        top_k=4, target_top_k=4, top_p=0.95, target_top_p=0.95)
+    eng2 = D3DEngine.from_weights(tw, dw, warm, max_seqs=4, max_context=512)
+    res = eng2.generate(prompts)
+    for o in res["outputs"]:
+        assert len(o.tokens) == 32 and all(0 <= t < 1024 for t in o.tokens)
+    sar = eng2.generate_ar(prompts)["outputs"]
+    assert all(len(t) == 32 for t in sar)
