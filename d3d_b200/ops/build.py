@@ -20,7 +20,7 @@ BUILD_DIR = HERE / "_build"
 NAME = "d3d_b200_C"
 
 SOURCES = ["bindings.cpp", "gemm_tcgen05.cu", "fused.cu", "attention.cu", "handoff.cu",
-           "train_kernels.cu", "tp.cu"]
+           "train_kernels.cu", "tp.cu", "fsdp.cu"]
 
 CUDA_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -456,6 +456,62 @@ void topk_merge_tp(Tensor ptrs, int64_t rank, Tensor epoch, int64_t x, int64_t c
                      oi.data_ptr<int64_t>(), cur_stream());
 }
 
+// ------------------------------------------------------ fused sharded optimizer
+// ``ptrs``: int64 CPU tensor [3, world] = every rank's gradient buffer,
+// parameter buffer and flag array (device addresses valid in this process).
+d3d::FsdpArgs fsdp_args(Tensor ptrs, int64_t rank, int64_t lo, int64_t shard, c10::optional<Tensor> status) {
+  TORCH_CHECK(ptrs.dim() == 2 && ptrs.size(0) == 3 && ptrs.size(1) <= d3d::FSDP_MAX, "fsdp: bad pointer table");
+  CHECK_DT(ptrs, torch::kInt64);
+  d3d::FsdpArgs a{};
+  a.world = static_cast<int>(ptrs.size(1));
+  a.rank = static_cast<int>(rank);
+  TORCH_CHECK(a.rank >= 0 && a.rank < a.world, "fsdp: rank out of range");
+  auto p = ptrs.contiguous().cpu();
+  const int64_t* v = p.data_ptr<int64_t>();
+  for (int j = 0; j < a.world; ++j) {
+    a.grads[j] = reinterpret_cast<float*>(v[j]);
+    a.params[j] = reinterpret_cast<__nv_bfloat16*>(v[a.world + j]);
+    a.flags[j] = reinterpret_cast<int64_t*>(v[2 * a.world + j]);
+  }
+  a.lo = static_cast<size_t>(lo);
+  a.shard = static_cast<size_t>(shard);
+  a.status = status_ptr(status);
+  a.timeout_ns = kTimeoutNs;
+  return a;
+}
+
+void fsdp_signal(Tensor ptrs, int64_t rank, int64_t lo, int64_t shard, int64_t phase, int64_t e, Tensor like) {
+  const c10::cuda::CUDAGuard g(like.device());
+  d3d::fsdp_signal(fsdp_args(ptrs, rank, lo, shard, c10::nullopt), static_cast<int>(phase), e, cur_stream());
+}
+
+void fsdp_reduce(Tensor ptrs, int64_t rank, int64_t lo, int64_t shard, int64_t e, Tensor gshard, Tensor sumsq,
+                 Tensor status) {
+  const c10::cuda::CUDAGuard g(gshard.device());
+  CHECK_DT(gshard, torch::kFloat32);
+  CHECK_DT(sumsq, torch::kFloat32);
+  TORCH_CHECK(gshard.numel() >= shard, "fsdp_reduce: shard buffer too small");
+  d3d::fsdp_reduce(fsdp_args(ptrs, rank, lo, shard, status), e, gshard.data_ptr<float>(), sumsq.data_ptr<float>(),
+                   cur_stream());
+}
+
+void fsdp_update(Tensor ptrs, int64_t rank, int64_t lo, int64_t shard, int64_t e, Tensor gshard, Tensor p, Tensor m,
+                 Tensor v, double lr, double b1, double b2, double eps, double wd, int64_t step, double scale,
+                 Tensor ticket, Tensor status) {
+  const c10::cuda::CUDAGuard g(p.device());
+  CHECK_DT(p, torch::kFloat32);
+  TORCH_CHECK(p.numel() == shard && m.numel() == shard && v.numel() == shard, "fsdp_update: shard sizes");
+  d3d::fsdp_update(fsdp_args(ptrs, rank, lo, shard, status), e, gshard.data_ptr<float>(), p.data_ptr<float>(),
+                   m.data_ptr<float>(), v.data_ptr<float>(), static_cast<float>(lr), static_cast<float>(b1),
+                   static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd), static_cast<int>(step),
+                   static_cast<float>(scale), reinterpret_cast<unsigned int*>(ticket.data_ptr<int>()), cur_stream());
+}
+
+void fsdp_wait(Tensor ptrs, int64_t rank, int64_t lo, int64_t shard, int64_t phase, int64_t e, Tensor status) {
+  const c10::cuda::CUDAGuard g(status.device());
+  d3d::fsdp_wait(fsdp_args(ptrs, rank, lo, shard, status), static_cast<int>(phase), e, cur_stream());
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -504,6 +560,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("part_off"), py::arg("nsplit"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"),
         py::arg("status") = py::none());
   m.def("tp_publish_topk", &tp_publish_topk);
+  m.def("fsdp_signal", &fsdp_signal);
+  m.def("fsdp_reduce", &fsdp_reduce);
+  m.def("fsdp_update", &fsdp_update);
+  m.def("fsdp_wait", &fsdp_wait);
   m.def("topk_merge_tp", &topk_merge_tp, py::arg("ptrs"), py::arg("rank"), py::arg("epoch"), py::arg("x"),
         py::arg("cand_off"), py::arg("M"), py::arg("k"), py::arg("ov"), py::arg("oi"), py::arg("status") = py::none());
 }

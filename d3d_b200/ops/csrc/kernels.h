@@ -102,3 +102,22 @@ void tp_publish_topk(const float* lv, const int64_t* li, int M, int k, int64_t i
                      cudaStream_t st);
 void topk_merge_tp(const TpArgs& a, int x, size_t cand_off, int M, int k, float* ov, int64_t* oi, cudaStream_t st);
 }  // namespace d3d
+
+namespace d3d {
+// ---- sharded optimizer step fused with its collectives (fsdp.cu)
+constexpr int FSDP_MAX = 8;
+struct FsdpArgs {
+  int world, rank;
+  size_t lo, shard;                 // this rank's element range of the flattened model
+  float* grads[FSDP_MAX];           // every rank's full fp32 gradient (peer-mapped)
+  __nv_bfloat16* params[FSDP_MAX];  // every rank's full bf16 parameters (peer-mapped)
+  int64_t* flags[FSDP_MAX];         // every rank's flags: [phase][source rank]
+  int* status;
+  unsigned long long timeout_ns;
+};
+void fsdp_signal(const FsdpArgs& a, int phase, int64_t e, cudaStream_t st);
+void fsdp_reduce(const FsdpArgs& a, int64_t e, float* gshard, float* sumsq, cudaStream_t st);
+void fsdp_update(const FsdpArgs& a, int64_t e, const float* gshard, float* p, float* m, float* v, float lr, float b1,
+                 float b2, float eps, float wd, int step, float scale, unsigned int* ticket, cudaStream_t st);
+void fsdp_wait(const FsdpArgs& a, int phase, int64_t e, cudaStream_t st);
+}  // namespace d3d

@@ -30,14 +30,14 @@ import torch.distributed as dist
 
 class ShardedAdamW:
     def __init__(self, params: Iterable[torch.nn.Parameter], lr: float = 1e-4, betas=(0.9, 0.999),
-                 eps: float = 1e-8, weight_decay: float = 0.0, group=None):
+                 eps: float = 1e-8, weight_decay: float = 0.0, group=None, align: int = 1):
         self.params: List[torch.nn.Parameter] = [p for p in params if p.requires_grad]
         self.lr, self.b1, self.b2, self.eps, self.wd = lr, betas[0], betas[1], eps, weight_decay
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.numel = sum(p.numel() for p in self.params)
-        self.shard = math.ceil(self.numel / self.world)
+        self.shard = math.ceil(self.numel / (self.world * align)) * align
         self.padded = self.shard * self.world
         dev = self.params[0].device
         flat = torch.zeros(self.padded, dtype=torch.float32, device=dev)

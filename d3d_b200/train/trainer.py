@@ -135,7 +135,12 @@ def train(args) -> dict:
             p.requires_grad_(False)
     if args.freeze_embeddings:
         student.model.embed_tokens.weight.requires_grad_(False)
-    opt = ShardedAdamW(student.parameters(), lr=args.lr, weight_decay=args.weight_decay)
+    if device.type == "cuda" and world > 1 and os.environ.get("D3D_FUSED_OPT", "1") != "0":
+        # reduce-scatter + AdamW + all-gather fused into kernels over NVLink peer memory
+        from ..parallel.fsdp import FusedShardedAdamW
+        opt = FusedShardedAdamW(student.parameters(), lr=args.lr, weight_decay=args.weight_decay)
+    else:
+        opt = ShardedAdamW(student.parameters(), lr=args.lr, weight_decay=args.weight_decay)
     start = 0
     if args.resume:
         ck = Path(args.resume)
