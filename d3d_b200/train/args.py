@@ -39,4 +39,14 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--save-final", action="store_true")
     p.add_argument("--resume", default=None, help="checkpoint directory written by --save-*")
     p.add_argument("--log-every", type=int, default=1)
+    # auxiliary objectives on the student logits (off by default)
+    p.add_argument("--hnce-weight", type=float, default=0.0, help="hard-negative CE weight")
+    p.add_argument("--hnce-top-k", type=int, default=16)
+    p.add_argument("--hnce-margin", type=float, default=0.0)
+    p.add_argument("--margin-weight", type=float, default=0.0, help="top-k target margin weight")
+    p.add_argument("--margin-top-k", type=int, default=16)
+    p.add_argument("--margin-value", type=float, default=1.0)
+    p.add_argument("--margin-hinge", action="store_true", help="hinge instead of softplus margin")
+    p.add_argument("--trajectory-weight", type=float, default=0.0,
+                   help="hidden-trajectory (block relation) distillation weight; needs --target-model")
     return p

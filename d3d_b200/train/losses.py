@@ -53,6 +53,51 @@ def ce_per_token(student_logits, targets):
     return F.cross_entropy(student_logits.float(), targets.long(), reduction="none")
 
 
+def _nontarget_topk(logits: torch.Tensor, targets: torch.Tensor, k: int):
+    """Target logit and the ``k`` largest non-target logits of each row."""
+    z = logits.float()
+    k = min(int(k), z.shape[-1] - 1)
+    zt = z.gather(-1, targets.long()[:, None])[:, 0]
+    v, i = torch.topk(z, k + 1, dim=-1)
+    v = v.masked_fill(i == targets.long()[:, None], float("-inf"))
+    return zt, torch.topk(v, k, dim=-1).values
+
+
+def hard_negative_ce_per_token(logits, targets, top_k: int = 16, margin: float = 0.0):
+    """CE of the target against only its ``top_k`` strongest competitors
+    (each shifted by ``margin``): ``log(1 + sum_j exp(z_j + margin - z_y))``
+    (reference ``train/objective_kernels.py:102-148``)."""
+    zt, neg = _nontarget_topk(logits, targets, top_k)
+    terms = torch.cat([torch.zeros_like(zt)[:, None], neg - zt[:, None] + float(margin)], -1)
+    return torch.logsumexp(terms, -1)
+
+
+def target_margin_per_token(logits, targets, top_k: int = 16, margin: float = 1.0, smooth: bool = True,
+                            temperature: float = 1.0):
+    """Mean penalty of the ``top_k`` strongest competitors that come within
+    ``margin`` of the target logit: softplus (smooth) or hinge
+    (reference ``train/objective_kernels.py:41-98``)."""
+    zt, neg = _nontarget_topk(logits, targets, top_k)
+    viol = neg - zt[:, None] + float(margin)
+    if smooth:
+        pen = F.softplus(viol / float(temperature)) * float(temperature)
+    else:
+        pen = F.relu(viol)
+    return pen.mean(-1)
+
+
+def ce_aux_per_token(logits, targets, *, ce_weight=1.0, hnce_weight=0.0, hnce_top_k=16, hnce_margin=0.0,
+                     margin_weight=0.0, margin_top_k=16, margin_value=1.0, margin_smooth=True):
+    """``ce_weight * CE + hnce_weight * hard-negative CE + margin_weight *
+    margin`` per token, plus the three terms (reference ``train/losses.py:124-159``)."""
+    ce = ce_per_token(logits, targets)
+    hn = hard_negative_ce_per_token(logits, targets, hnce_top_k, hnce_margin) if hnce_weight else \
+        torch.zeros_like(ce)
+    mg = target_margin_per_token(logits, targets, margin_top_k, margin_value, margin_smooth) if margin_weight \
+        else torch.zeros_like(ce)
+    return ce_weight * ce + hnce_weight * hn + margin_weight * mg, ce, hn, mg
+
+
 # --------------------------------------------------------------------------
 # fused LM-head KL + CE
 # --------------------------------------------------------------------------

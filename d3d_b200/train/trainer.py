@@ -30,7 +30,8 @@ import torch.distributed as dist
 
 from ..checkpoint import expected_keys, write_state
 from .blocks import Example, build_packed_block_batch, synthetic_examples
-from .losses import decay_weights, lmhead_distill_loss, normalize_objective
+from . import trajectory
+from .losses import ce_aux_per_token, decay_weights, lmhead_distill_loss, normalize_objective
 from .model_utils import clean_prefill, student_hidden, teacher_hidden
 from .optim import ShardedAdamW, cosine_lr
 
@@ -175,8 +176,10 @@ def train(args) -> dict:
         w = w / max(z, 1e-6)
         h_t = w_t = None
         targets = batch.target_ids[act]
+        th_all = None
         if teacher is not None:
-            th = teacher_hidden(teacher, batch)[act]
+            th_all = teacher_hidden(teacher, batch)
+            th = th_all[act]
             h_t, w_t = th, teacher.lm_weight
             if args.ce_on_target_greedy:
                 targets = (teacher.logits(th).argmax(-1) if device.type != "cuda" else
@@ -184,6 +187,17 @@ def train(args) -> dict:
         loss, kl, ce = lmhead_distill_loss(hs[act], student.lm_weight, h_t, w_t, targets,
                                            (a_kl * w) if a_kl else None, (a_ce * w) if a_ce else None,
                                            chunk=args.vocab_chunk)
+        if getattr(args, "hnce_weight", 0.0) or getattr(args, "margin_weight", 0.0):
+            # auxiliary objectives on materialised student logits of the supervised rows
+            logits = hs[act].float() @ student.lm_weight.float().t()
+            aux, _, _, _ = ce_aux_per_token(logits, targets, ce_weight=0.0, hnce_weight=args.hnce_weight,
+                                            hnce_top_k=args.hnce_top_k, hnce_margin=args.hnce_margin,
+                                            margin_weight=args.margin_weight, margin_top_k=args.margin_top_k,
+                                            margin_value=args.margin_value, margin_smooth=not args.margin_hinge)
+            loss = loss + (w * aux).sum()
+        if getattr(args, "trajectory_weight", 0.0) and th_all is not None:
+            loss = loss + args.trajectory_weight * _trajectory_term(student, teacher, batch, hs, th_all, device,
+                                                                    world)
         loss.backward()
         lr = cosine_lr(step, args.lr, args.warmup_steps, args.max_steps, args.min_lr_ratio)
         gnorm = opt.step(args.grad_clip, lr)
@@ -206,6 +220,29 @@ def train(args) -> dict:
     if args.save_final:
         save_checkpoint(student, opt, out_dir, args.max_steps, cursor)
     return {"log": log, "elapsed_s": time.perf_counter() - t_start, "world": world}
+
+
+def _argmax_rows(h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    if h.is_cuda:
+        return _greedy(h, w)
+    return (h.float() @ w.float().t()).argmax(-1)
+
+
+def _trajectory_term(student, teacher, batch, hs, th_all, device, world) -> torch.Tensor:
+    """Block-relation distillation over blocks the teacher drafts better
+    (``train/trajectory.py``), normalised by the global selected-block count."""
+    K = batch.block_size
+    B, Q = batch.active.shape
+    with torch.no_grad():
+        s_pred = _argmax_rows(hs.reshape(B * Q, -1).detach(), student.lm_weight).view(B, Q)
+        t_pred = _argmax_rows(th_all.reshape(B * Q, -1), teacher.lm_weight).view(B, Q)
+    valid = trajectory.by_block(batch.active, K)
+    tgt = trajectory.by_block(batch.target_ids, K)
+    s_acc = trajectory.block_accept_lengths(trajectory.by_block(s_pred, K)[..., 1:], tgt[..., 1:], valid[..., 1:])
+    t_acc = trajectory.block_accept_lengths(trajectory.by_block(t_pred, K)[..., 1:], tgt[..., 1:], valid[..., 1:])
+    sel = trajectory.selection_mask(t_acc, s_acc, valid.sum(-1), batch.block_keep)
+    lsum, cnt = trajectory.relational_loss(trajectory.by_block(hs, K), trajectory.by_block(th_all, K), valid, sel)
+    return trajectory.distributed_block_mean(lsum, _all_sum(float(cnt), device), world)
 
 
 def _greedy(h, w) -> torch.Tensor:
