@@ -299,9 +299,11 @@ class FastTarget(_FastModelBackend, TargetBackend):
             q = (torch.zeros(B, 0, 1, dtype=torch.long), torch.ones(B, 0, 1))
         b = self.runner.buffers(B, K, self.top_k if sampled else 1)
         a = self._abufs(B, K)
-        pos = np.stack([np.arange(s.prefix, s.prefix + K) for s in seqs])
-        rows = np.stack([causal_rows(s.prefix, K).numpy() for s in seqs])
-        kv_end = np.array([s.prefix + K for s in seqs])
+        pref = np.fromiter((s.prefix for s in seqs), dtype=np.int64, count=B)
+        pos = pref[:, None] + np.arange(K, dtype=np.int64)
+        rows = np.zeros((B, K, 3), dtype=np.int32)
+        rows[..., 0] = pos + 1                      # causal: row i sees slots [0, prefix + i]
+        kv_end = pref + K
         self._fill(b, seqs, blocks.numpy(), pos, rows, kv_end, f"v{B}_{K}")
         if gather:
             with torch.cuda.stream(self.stream):
