@@ -90,3 +90,104 @@ def test_gate_up_interleave_order():
     pw = ops.pack_gate_up(g, u)
     full = torch.cat([g, u], 0)
     assert torch.equal(pw.unpack(), full[order])
+
+
+class _SameStream:
+    """Stands in for a CUDA stream shared by target and drafter."""
+
+
+def _pipelined_pair():
+    from d3d_b200.config import tiny_drafter, tiny_target
+    from d3d_b200.engine.backends import TorchDraft, TorchTarget
+    from d3d_b200.models.qwen3 import build_model
+    stream = _SameStream()
+
+    class Target(TorchTarget):
+        supports_gather = True
+
+        def __init__(self, m):
+            super().__init__(m)
+            self.stream = stream
+            self.gathers = 0
+            self.pipelined = 0
+
+        def submit_verify(self, seqs, blocks, q=None, gather=None):
+            self.pipelined += gather is not None
+            blocks = blocks.clone()
+            for src, dst, rows in gather or ():
+                blocks.view(-1)[torch.tensor(dst)] = src[torch.tensor(rows), 0]
+                self.gathers += 1
+            super().submit_verify(seqs, blocks, q)
+
+    class Handle:
+        def __init__(self, out):
+            self.out, self.dev_top = out, out["dev_top"]
+
+        def result(self):
+            return self.out
+
+    class Draft(TorchDraft):
+        supports_async = True
+
+        def __init__(self, m):
+            super().__init__(m)
+            self.stream = stream
+
+        def forward(self, seqs, ids, positions, rows, *, store, topk, cond_rows=None, sample=None,
+                    wait=True):
+            out = super().forward(seqs, ids, positions, rows, store=store, topk=topk, cond_rows=cond_rows,
+                                  sample=sample)
+            b, q = out["greedy"].shape
+            out["dev_top"] = (out["top"] if "top" in out else out["greedy"][..., None]).reshape(b * q, -1)
+            return out if wait else Handle(out)
+
+    return Target(build_model(tiny_target(), seed=0)), Draft(build_model(tiny_drafter(cond=True), seed=1))
+
+
+@pytest.mark.parametrize("controlled", [False, True])
+def test_pipelined_coordinator_matches_ar(controlled):
+    """The pipelined step (next verify submitted before the draft is read,
+    drafts gathered from the in-flight output or rewritten by the controlled
+    injection) keeps greedy token identity."""
+    from d3d_b200.engine.backends import TorchTarget
+    from d3d_b200.engine.controlled import ControlledAcceptance, rate_for_mean_accept
+    from d3d_b200.engine.spec import DecodeConfig, SpecDecoder, ar_generate
+    from d3d_b200.config import tiny_target
+    from d3d_b200.models.qwen3 import build_model
+    tgt, drf = _pipelined_pair()
+    rng = random.Random(9)
+    prompts = [[rng.randrange(2, 1000) for _ in range(rng.randint(16, 48))] for _ in range(3)]
+    cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=40, ignore_eos=True)
+    ref = ar_generate(TorchTarget(build_model(tiny_target(), seed=0)), prompts, 40, ignore_eos=True)["outputs"]
+    ctl = None
+    if controlled:
+        rate = rate_for_mean_accept(4.0, 8)
+        ctl = lambda i: ControlledAcceptance(prompts[i] + ref[i], rate, 1024, stream=i, exclude=(1023,))
+    dec = SpecDecoder(tgt, drf, cfg)
+    assert dec._pipelined()
+    res = dec.generate(prompts, concurrency=3, controlled=ctl)
+    assert [o.tokens for o in res["outputs"]] == ref
+    if controlled:
+        assert tgt.pipelined > 0
+
+
+def test_device_rows_reproduce_selected_branch():
+    """The rows ``_Outcomes.device_rows`` hands to the device gather hold the
+    same drafts as the host-side branch (``_Outcomes.get``)."""
+    from d3d_b200.engine.layout import branch_specs, packed_layout
+    from d3d_b200.engine.spec import _Outcomes
+    k = 8
+    cur = torch.arange(100, 100 + k)
+    top = torch.stack([cur, cur + 50], 1)
+    lays = [packed_layout(cur + 3 * i, branch_specs((cur + 3 * i).tolist(), top.tolist(), 1), 40, k, 999, "causal")
+            for i in range(2)]
+    q = lays[0].q_len
+    greedy = torch.randint(0, 1000, (2, q))
+    out = {"greedy": greedy, "top": torch.stack([greedy, greedy + 1], -1),
+           "dev_top": torch.stack([greedy, greedy + 1], -1).reshape(2 * q, 2)}
+    for i, lay in enumerate(lays):
+        oc = _Outcomes(lay, out, i, q)
+        for key in lay.keys:
+            blk = oc.get(key)[0]
+            src, rows = oc.device_rows(key)
+            assert torch.equal(src[torch.tensor(rows), 0], blk[1:])
