@@ -392,7 +392,8 @@ d3d::TpArgs tp_args(Tensor ptrs, int64_t rank, Tensor epoch, c10::optional<Tenso
 // every rank's exchange region at ``part_off`` (slot rank * splits + split),
 // flags raised for exchange ``x`` by the last CTA.
 void gemm_partial_tp(Tensor x, Tensor w, Tensor ptrs, int64_t rank, Tensor epoch, Tensor ticket, int64_t xidx,
-                     int64_t part_off, int64_t splits, int64_t bt, c10::optional<Tensor> status, int64_t wn) {
+                     int64_t part_off, int64_t splits, int64_t bt, c10::optional<Tensor> status, int64_t wn,
+                     bool pull) {
   const c10::cuda::CUDAGuard g(x.device());
   auto a = base_args(x, w, static_cast<int>(bt), status, wn);
   const d3d::TpArgs t = tp_args(ptrs, rank, epoch, status);
@@ -403,6 +404,7 @@ void gemm_partial_tp(Tensor x, Tensor w, Tensor ptrs, int64_t rank, Tensor epoch
   a.tp = t.tp;
   a.tp_rank = t.rank;
   a.tp_x = static_cast<int>(xidx);
+  a.tp_pull = pull ? 1 : 0;
   for (int r = 0; r < t.tp; ++r) {
     a.tp_out[r] = reinterpret_cast<float*>(t.parts[r] + part_off);
     a.tp_flags[r] = t.flags[r];
@@ -425,14 +427,14 @@ void tp_signal(Tensor ptrs, int64_t rank, Tensor epoch, int64_t x) {
 }
 
 void add_rmsnorm_tp(Tensor ptrs, int64_t rank, Tensor epoch, int64_t x, int64_t part_off, int64_t nsplit,
-                    Tensor residual, Tensor w, Tensor out, double eps, c10::optional<Tensor> status) {
+                    Tensor residual, Tensor w, Tensor out, double eps, c10::optional<Tensor> status, bool pull) {
   const c10::cuda::CUDAGuard g(residual.device());
   CHECK_DT(residual, torch::kBFloat16);
   CHECK_CONTIG(residual);
   CHECK_CONTIG(out);
   TORCH_CHECK(part_off % 16 == 0, "add_rmsnorm_tp: partial offset must be 16-byte aligned");
   d3d::add_rmsnorm_tp(tp_args(ptrs, rank, epoch, status), static_cast<int>(x), static_cast<size_t>(part_off),
-                      static_cast<int>(nsplit), bf(residual), cbf(w), bf(out), static_cast<int>(residual.size(0)),
+                      static_cast<int>(nsplit), pull ? 1 : 0, bf(residual), cbf(w), bf(out), static_cast<int>(residual.size(0)),
                       static_cast<int>(residual.size(1)), static_cast<float>(eps), cur_stream());
 }
 
@@ -554,11 +556,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_epoch_bump", &tp_epoch_bump);
   m.def("gemm_partial_tp", &gemm_partial_tp, py::arg("x"), py::arg("w"), py::arg("ptrs"), py::arg("rank"),
         py::arg("epoch"), py::arg("ticket"), py::arg("xidx"), py::arg("part_off"), py::arg("splits"),
-        py::arg("bt"), py::arg("status") = py::none(), py::arg("wn") = 0);
+        py::arg("bt"), py::arg("status") = py::none(), py::arg("wn") = 0, py::arg("pull") = false);
   m.def("tp_signal", &tp_signal);
   m.def("add_rmsnorm_tp", &add_rmsnorm_tp, py::arg("ptrs"), py::arg("rank"), py::arg("epoch"), py::arg("x"),
         py::arg("part_off"), py::arg("nsplit"), py::arg("residual"), py::arg("w"), py::arg("out"), py::arg("eps"),
-        py::arg("status") = py::none());
+        py::arg("status") = py::none(), py::arg("pull") = false);
   m.def("tp_publish_topk", &tp_publish_topk);
   m.def("fsdp_signal", &fsdp_signal);
   m.def("fsdp_reduce", &fsdp_reduce);

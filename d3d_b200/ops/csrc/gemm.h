@@ -26,7 +26,7 @@ struct GemmParams {
   unsigned long long timeout_ns;
   // tensor-parallel push (MODE 0): partials of split s go to slot (tp_rank * splits + s)
   // of every rank's exchange buffer; the last CTA raises flags[j][x * tp + tp_rank] = *epoch
-  int tp, tp_rank, tp_x;
+  int tp, tp_rank, tp_x, tp_pull;
   float* tp_out[8];
   int64_t* tp_flags[8];
   int64_t* tp_epoch;
@@ -51,8 +51,9 @@ struct GemmArgs {
   int* status;                 // device error word (may be null)
   unsigned long long timeout_ns;
   int w_packed;                // w is in the packed tile layout (see pack_weight)
-  // tensor-parallel push (mode 0 only; tp = 0 disables): see GemmParams
-  int tp, tp_rank, tp_x;
+  // tensor-parallel exchange (mode 0 only; tp = 0 disables): see GemmParams;
+  // tp_pull = 1 stores only this rank's slot (peers read it) instead of pushing
+  int tp, tp_rank, tp_x, tp_pull;
   float* tp_out[8];
   int64_t* tp_flags[8];
   int64_t* tp_epoch;

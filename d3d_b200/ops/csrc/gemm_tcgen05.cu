@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
               // tensor parallel: the same partial into every rank's exchange
               // buffer (peer stores over NVLink), slot rank * splits + split
               const size_t slot = static_cast<size_t>(p.tp_rank * p.splits + u.split) * p.M * p.N;
-              for (int r = 0; r < p.tp; ++r) {
+              for (int r = p.tp_pull ? p.tp_rank : 0; r < (p.tp_pull ? p.tp_rank + 1 : p.tp); ++r) {
                 float* base = p.tp_out[r] + slot;
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
@@ -402,7 +402,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
   }
 
   // ---------------------------------------------------------------- teardown
-  if (MODE == 0 && p.tp > 0) __threadfence_system();  // this thread's peer stores, before the flags
+  if (MODE == 0 && p.tp > 0) {
+    // this thread's partial stores are visible (to peers' loads, or as peer
+    // stores) before the flags go up
+    if (p.tp_pull) __threadfence();
+    else __threadfence_system();
+  }
   __syncthreads();
   if (MODE == 0 && p.tp > 0 && threadIdx.x == 0) {
     // the last CTA to finish publishes the exchange on every rank
@@ -568,6 +573,7 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
       throw std::runtime_error("gemm: tensor-parallel push needs mode 0, tp <= 8, epoch and ticket");
     p.tp_rank = a.tp_rank;
     p.tp_x = a.tp_x;
+    p.tp_pull = a.tp_pull;
     for (int r = 0; r < a.tp; ++r) {
       p.tp_out[r] = a.tp_out[r];
       p.tp_flags[r] = a.tp_flags[r];

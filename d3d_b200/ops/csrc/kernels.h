@@ -96,7 +96,7 @@ struct TpArgs {
 };
 void tp_epoch_bump(int64_t* epoch, cudaStream_t st);
 void tp_signal(const TpArgs& a, int x, cudaStream_t st);
-void add_rmsnorm_tp(const TpArgs& a, int x, size_t part_off, int nsplit, __nv_bfloat16* residual,
+void add_rmsnorm_tp(const TpArgs& a, int x, size_t part_off, int nsplit, int pull, __nv_bfloat16* residual,
                     const __nv_bfloat16* w, __nv_bfloat16* out, int M, int N, float eps, cudaStream_t st);
 void tp_publish_topk(const float* lv, const int64_t* li, int M, int k, int64_t id_offset, uint8_t* cand,
                      cudaStream_t st);

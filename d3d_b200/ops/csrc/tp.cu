@@ -80,7 +80,7 @@ __host__ __device__ inline size_t cand_ids_off(int n) { return (static_cast<size
 
 // x = bf16(residual + bf16(sum_{rank, split} P)); residual <- x; out = w * bf16(x * rstd)
 template <int V>
-__global__ void __launch_bounds__(512) add_rmsnorm_tp_kernel(const TpArgs a, int x, size_t part_off, int nsplit,
+__global__ void __launch_bounds__(512) add_rmsnorm_tp_kernel(const TpArgs a, int x, size_t part_off, int nsplit, int pull,
                                                              __nv_bfloat16* __restrict__ residual,
                                                              const __nv_bfloat16* __restrict__ w,
                                                              __nv_bfloat16* __restrict__ out, int M, int N,
@@ -101,10 +101,11 @@ __global__ void __launch_bounds__(512) add_rmsnorm_tp_kernel(const TpArgs a, int
     if (n < N) {
       const size_t off = static_cast<size_t>(m) * N + n;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      // every rank pushed its splits into slots [rank][split] of this rank's buffer
-      const float* mine = reinterpret_cast<const float*>(a.parts[a.rank] + part_off);
+      // slots [rank][split]: all in this rank's buffer (pushed by the peers'
+      // GEMMs), or slot rank r in rank r's buffer (read over NVLink: pull)
       for (int r = 0; r < a.tp; ++r) {
-        const float* base = mine + static_cast<size_t>(r) * nsplit * stride;
+        const float* base = reinterpret_cast<const float*>(a.parts[pull ? r : a.rank] + part_off) +
+                            static_cast<size_t>(r) * nsplit * stride;
         float4 v[16];
 #pragma unroll
         for (int s = 0; s < 16; ++s)
@@ -218,7 +219,7 @@ void tp_signal(const TpArgs& a, int x, cudaStream_t st) {
   launch_pdl(tp_signal_kernel, dim3(1), dim3(32), 0, st, a, x);
 }
 
-void add_rmsnorm_tp(const TpArgs& a, int x, size_t part_off, int nsplit, __nv_bfloat16* residual,
+void add_rmsnorm_tp(const TpArgs& a, int x, size_t part_off, int nsplit, int pull, __nv_bfloat16* residual,
                     const __nv_bfloat16* w, __nv_bfloat16* out, int M, int N, float eps, cudaStream_t st) {
   if (M == 0) return;
   if (N % 4) throw std::runtime_error("add_rmsnorm_tp: hidden size must be a multiple of 4");
@@ -227,13 +228,13 @@ void add_rmsnorm_tp(const TpArgs& a, int x, size_t part_off, int nsplit, __nv_bf
   const int threads = vec >= 512 ? 512 : (vec + 31) / 32 * 32;
   const int v = (vec + threads - 1) / threads;
   if (v <= 1)
-    launch_pdl(add_rmsnorm_tp_kernel<1>, dim3(M), dim3(threads), 0, st, a, x, part_off, nsplit, residual, w, out, M,
+    launch_pdl(add_rmsnorm_tp_kernel<1>, dim3(M), dim3(threads), 0, st, a, x, part_off, nsplit, pull, residual, w, out, M,
                N, eps);
   else if (v <= 2)
-    launch_pdl(add_rmsnorm_tp_kernel<2>, dim3(M), dim3(threads), 0, st, a, x, part_off, nsplit, residual, w, out, M,
+    launch_pdl(add_rmsnorm_tp_kernel<2>, dim3(M), dim3(threads), 0, st, a, x, part_off, nsplit, pull, residual, w, out, M,
                N, eps);
   else if (v <= 4)
-    launch_pdl(add_rmsnorm_tp_kernel<4>, dim3(M), dim3(threads), 0, st, a, x, part_off, nsplit, residual, w, out, M,
+    launch_pdl(add_rmsnorm_tp_kernel<4>, dim3(M), dim3(threads), 0, st, a, x, part_off, nsplit, pull, residual, w, out, M,
                N, eps);
   else
     throw std::runtime_error("add_rmsnorm_tp: hidden size above 8192");

@@ -95,6 +95,10 @@ class TPGroup:
         # partials, no flags) to time what the exchanges cost; results are wrong
         import os
         self.local_only = os.environ.get("D3D_TP_LOCAL") == "1"
+        # exchange mode: "pull" (each rank's GEMM keeps its partials, consumers
+        # read the peers' over NVLink) or "push" (GEMM epilogues store into
+        # every rank's buffer); both raise the flags from the GEMM's last CTA
+        self.pull = os.environ.get("D3D_TP_MODE", "pull") != "push"
 
     # --------------------------------------------------------------- layout
     def part_offset(self, parity: int) -> int:
@@ -129,14 +133,14 @@ class TPGroup:
                                   self.status, w.n)
             return
         self.ext.gemm_partial_tp(x_act, w.data, self.ptrs, self.rank, self.epoch, self.ticket, x,
-                                 self.part_offset(x), splits, bt, self.status, w.n)
+                                 self.part_offset(x), splits, bt, self.status, w.n, self.pull)
 
     def add_rmsnorm(self, x: int, parity: int, nsplit: int, residual, w, out, eps: float) -> None:
         if self.local_only:
             self.ext.add_rmsnorm(self.part_view(parity, nsplit * residual.numel()), nsplit, residual, w, out, eps)
             return
         self.ext.add_rmsnorm_tp(self.ptrs, self.rank, self.epoch, x, self.part_offset(parity), nsplit,
-                                residual, w, out, eps, self.status)
+                                residual, w, out, eps, self.status, self.pull)
 
     def merge_topk(self, x: int, M: int, k: int, ov, oi) -> None:
         if self.local_only:
