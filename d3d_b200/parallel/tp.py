@@ -95,10 +95,16 @@ class TPGroup:
         # partials, no flags) to time what the exchanges cost; results are wrong
         import os
         self.local_only = os.environ.get("D3D_TP_LOCAL") == "1"
-        # exchange mode: "pull" (each rank's GEMM keeps its partials, consumers
-        # read the peers' over NVLink) or "push" (GEMM epilogues store into
-        # every rank's buffer); both raise the flags from the GEMM's last CTA
-        self.pull = os.environ.get("D3D_TP_MODE", "pull") != "push"
+        # exchange mode (measured on two B200s, 32B forward: pull 10.3 ms,
+        # pull_cta 11.3 ms, push 11.4 ms at M=1):
+        #   "pull"     each rank's GEMM keeps its partials, a one-thread kernel
+        #              raises the flags, consumers read the peers' partials;
+        #   "pull_cta" the same, flags raised by the GEMM's last CTA;
+        #   "push"     GEMM epilogues store into every rank's buffer, last CTA flags.
+        self.mode = os.environ.get("D3D_TP_MODE", "pull")
+        if self.mode not in ("pull", "pull_cta", "push"):
+            raise ValueError("D3D_TP_MODE must be pull, pull_cta or push")
+        self.pull = self.mode != "push"
 
     # --------------------------------------------------------------- layout
     def part_offset(self, parity: int) -> int:
@@ -131,6 +137,13 @@ class TPGroup:
         if self.local_only:
             self.ext.gemm_partial(x_act, w.data, self.part_view(x, splits * x_act.shape[0] * w.n), splits, bt,
                                   self.status, w.n)
+            return
+        if self.mode == "pull":
+            n = splits * x_act.shape[0] * w.n           # this rank's slots [rank][split] of buffer x & 1
+            off = self.part_offset(x) + 4 * self.rank * n
+            self.ext.gemm_partial(x_act, w.data, self.mem[off:off + 4 * n].view(torch.float32), splits, bt,
+                                  self.status, w.n)
+            self.signal(x)
             return
         self.ext.gemm_partial_tp(x_act, w.data, self.ptrs, self.rank, self.epoch, self.ticket, x,
                                  self.part_offset(x), splits, bt, self.status, w.n, self.pull)
