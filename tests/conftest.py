@@ -19,3 +19,11 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _seeded():
+    """Every test starts from the same random state (CPU and CUDA generators)."""
+    import torch
+    torch.manual_seed(1234)
+    yield

@@ -110,18 +110,22 @@ def test_add_rmsnorm(E):
     assert torch.equal(res, x)
     xf = x.float()
     ref = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16).float() * w.float()
-    assert (out.float() - ref).abs().max().item() < 0.05
+    ref = ref.to(torch.bfloat16).float()     # the kernel rounds its output to bf16 as well
+    assert ((out.float() - ref).abs() / ref.abs().clamp_min(1e-2)).max().item() < 2e-2
 
 
 def test_swiglu(E):
     m, i = 5, 3072
-    part = torch.randn(2, m, 2 * i, device="cuda")
+    gen = torch.Generator(device="cuda").manual_seed(41)
+    part = torch.randn(2, m, 2 * i, device="cuda", generator=gen)
     h = torch.empty(m, i, dtype=torch.bfloat16, device="cuda")
     E.swiglu(part, 2, h)
     p = part.sum(0).to(torch.bfloat16).float()
     g, u = p[:, :i], p[:, i:]
-    ref = torch.nn.functional.silu(g).to(torch.bfloat16).float() * u
-    assert (h.float() - ref).abs().max().item() < 0.05
+    # same rounding points as the module: bf16(silu(g)) * bf16(u), rounded once more
+    ref = (torch.nn.functional.silu(g).to(torch.bfloat16).float() * u).to(torch.bfloat16).float()
+    err = (h.float() - ref).abs() / ref.abs().clamp_min(1e-2)
+    assert err.max().item() < 2e-2
 
 
 @pytest.mark.parametrize("m,i,k,bt", [(1, 384, 128, 16), (16, 6144, 2048, 16), (272, 6144, 2048, 96),
