@@ -4,9 +4,13 @@
 work, CUDA-event pairs recorded on the stream that ran it; ``summary()``
 resolves the events (one synchronize) and reports milliseconds per phase.
 Device numbers are what the GPU spent between the two events on that stream.
+
+With ``D3D_NVTX=1`` every phase is also an NVTX range (``torch.cuda.nvtx``),
+so external timeline tools see the coordinator's phases, enabled or not.
 """
 from __future__ import annotations
 
+import os
 import time
 from collections import defaultdict
 from contextlib import contextmanager
@@ -20,17 +24,27 @@ class StepProfiler:
         self.count: Dict[str, int] = defaultdict(int)
         self.dev: Dict[str, List[Tuple[object, object]]] = defaultdict(list)
 
+    _nvtx = os.environ.get("D3D_NVTX") == "1"
+
     @contextmanager
     def phase(self, name: str):
-        if not self.enabled:
-            yield
-            return
-        t0 = time.perf_counter()
+        if self._nvtx:
+            import torch
+            torch.cuda.nvtx.range_push(name)
         try:
-            yield
+            if not self.enabled:
+                yield
+                return
+            t0 = time.perf_counter()
+            try:
+                yield
+            finally:
+                self.host[name] += time.perf_counter() - t0
+                self.count[name] += 1
         finally:
-            self.host[name] += time.perf_counter() - t0
-            self.count[name] += 1
+            if self._nvtx:
+                import torch
+                torch.cuda.nvtx.range_pop()
 
     def dev_begin(self, name: str, stream):
         if not self.enabled:
