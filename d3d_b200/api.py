@@ -109,20 +109,22 @@ class D3DEngine:
 
     # ------------------------------------------------------------- decoding
     def generate(self, prompts: Sequence[Sequence[int]], *, max_new_tokens: Optional[int] = None,
-                 concurrency: int = 1, controlled: Optional[Callable[[int], object]] = None) -> dict:
+                 concurrency: int = 1, controlled: Optional[Callable[[int], object]] = None,
+                 max_new: Optional[Sequence[int]] = None) -> dict:
+        """Speculative decoding.  ``max_new``: per-request output budgets."""
         if max_new_tokens is not None and max_new_tokens != self.decoder.cfg.max_new_tokens:
             self.decoder.cfg = replace(self.decoder.cfg, max_new_tokens=int(max_new_tokens))
         if isinstance(prompts, torch.Tensor):
             prompts = prompts.tolist()
-        return self.decoder.generate(prompts, concurrency=concurrency, controlled=controlled)
+        return self.decoder.generate(prompts, concurrency=concurrency, controlled=controlled, max_new=max_new)
 
     def generate_ar(self, prompts: Sequence[Sequence[int]], *, max_new_tokens: Optional[int] = None,
-                    concurrency: int = 1) -> dict:
+                    concurrency: int = 1, max_new: Optional[Sequence[int]] = None) -> dict:
         n = max_new_tokens or self.decoder.cfg.max_new_tokens
         if isinstance(prompts, torch.Tensor):
             prompts = prompts.tolist()
         return ar_generate(self.target, prompts, n, eos=self.decoder.cfg.eos,
-                           ignore_eos=self.decoder.cfg.ignore_eos, concurrency=concurrency)
+                           ignore_eos=self.decoder.cfg.ignore_eos, concurrency=concurrency, max_new=max_new)
 
 
 def open_pair_link(peer: int, device, slot_bytes: Optional[int] = None, group=None):

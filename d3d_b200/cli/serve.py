@@ -26,6 +26,8 @@ def parser():
     p.add_argument("--page-size", type=int, default=16)
     p.add_argument("--concurrency", default="1,4,8,16")
     p.add_argument("--max-new-tokens", type=int, default=256)
+    p.add_argument("--max-new-tokens-range", default=None,
+                   help="LO,HI: per-request output budgets drawn uniformly (seeded), e.g. 128,512")
     p.add_argument("--block-size", type=int, default=16)
     p.add_argument("--anchor-num", type=int, default=1)
     p.add_argument("--draft-microbatch", type=int, default=4)
@@ -41,6 +43,13 @@ def main(argv=None):
     a = parser().parse_args(argv)
     conc = [int(c) for c in a.concurrency.split(",")]
     prompts = load_prompts(a)
+    budgets = None
+    if a.max_new_tokens_range:
+        import random
+        lo, hi = (int(x) for x in a.max_new_tokens_range.split(","))
+        rng = random.Random(a.seed + 17)
+        budgets = [rng.randint(lo, hi) for _ in prompts]
+        a.max_new_tokens = hi
     check_paged_capacity([len(p) for p in prompts], a.max_new_tokens, conc, a.pages, a.page_size,
                          a.block_size, a.anchor_num)
     decode = DecodeConfig(block_size=a.block_size, anchor_num=a.anchor_num, max_new_tokens=a.max_new_tokens,
@@ -49,7 +58,7 @@ def main(argv=None):
                        pages=a.pages)
     ar = None
     if a.validate or a.baseline or a.controlled_accept_mean is not None:
-        ar = eng.generate_ar(prompts, concurrency=max(conc))
+        ar = eng.generate_ar(prompts, concurrency=max(conc), max_new=budgets)
     ctl = None
     if a.controlled_accept_mean is not None:
         rate = rate_for_mean_accept(a.controlled_accept_mean, a.block_size)
@@ -57,7 +66,7 @@ def main(argv=None):
     eng.generate(prompts[:1], max_new_tokens=16, controlled=ctl)           # warm-up
     rows = []
     for c in conc:
-        r = eng.generate(prompts, concurrency=c, controlled=ctl)
+        r = eng.generate(prompts, concurrency=c, controlled=ctl, max_new=budgets)
         row = {"concurrency": c, "tps": r["tps"], "elapsed_s": r["elapsed_s"], "output_tokens": r["output_tokens"],
                "mean_accept_length": r["mean_accept_length"], "miss_rounds": r["miss_rounds"],
                "max_batch": max(r["decode_batch_sizes"]) if r["decode_batch_sizes"] else 0}
@@ -65,7 +74,7 @@ def main(argv=None):
             row["token_identical_to_ar"] = all(o.tokens == ar["outputs"][o.index] for o in r["outputs"])
         if a.baseline:
             t0 = time.perf_counter()
-            b = eng.generate_ar(prompts, concurrency=c)
+            b = eng.generate_ar(prompts, concurrency=c, max_new=budgets)
             row["ar_tps"] = b["output_tokens"] / (time.perf_counter() - t0)
             row["speedup"] = row["tps"] / row["ar_tps"] if row["ar_tps"] else None
         rows.append(row)

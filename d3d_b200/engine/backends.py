@@ -50,6 +50,7 @@ class SeqState:
     controlled: Any = None
     born: float = 0.0
     slot: int = -1                        # batch slot in fixed-size engines
+    budget: int = 0                       # output tokens for this request (0 = the decoder default)
     extra: Dict[str, Any] = field(default_factory=dict)
 
 

@@ -218,7 +218,10 @@ class SpecDecoder:
     # ------------------------------------------------------------ main loop
     def generate(self, prompts: Sequence[Sequence[int]], concurrency: int = 1,
                  controlled: Optional[Callable[[int], object]] = None,
-                 on_step: Optional[Callable[[int], None]] = None) -> dict:
+                 on_step: Optional[Callable[[int], None]] = None,
+                 max_new: Optional[Sequence[int]] = None) -> dict:
+        """Decode every prompt (``concurrency`` at a time, closed loop).
+        ``max_new``: per-request output budgets (default: the config's)."""
         cfg = self.cfg
         k = cfg.block_size
         if concurrency < 1 or cfg.max_new_tokens < 1:
@@ -242,7 +245,8 @@ class SpecDecoder:
                     exhausted = True
                     break
                 s = SeqState(index=idx, prompt=[int(t) for t in ids], prefix=len(ids),
-                             born=time.perf_counter())
+                             born=time.perf_counter(),
+                             budget=int(max_new[idx]) if max_new is not None else cfg.max_new_tokens)
                 s.controlled = controlled(idx) if controlled is not None else None
                 admitted.append(s)
             for off in range(0, len(admitted), cfg.prefill_group):
@@ -293,7 +297,7 @@ class SpecDecoder:
                 n = int(res.commit[i])
                 corr = int(res.correction[i])
                 emitted = block_t[i, :n].tolist()
-                room = cfg.max_new_tokens - len(s.generated)
+                room = s.budget - len(s.generated)
                 emitted = emitted[:room]
                 stop = False
                 if not cfg.ignore_eos:
@@ -309,7 +313,7 @@ class SpecDecoder:
                 s.anchor = corr
                 if res.hidden is not None and cfg.use_cond:
                     s.cond = res.hidden[i]
-                if stop or len(s.generated) >= cfg.max_new_tokens:
+                if stop or len(s.generated) >= s.budget:
                     self._finish(s, outputs)
                     continue
                 if not cfg.ignore_eos and corr in cfg.eos:
@@ -386,41 +390,55 @@ class SpecDecoder:
 
 def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new_tokens: int,
                 eos: Tuple[int, ...] = EOS_DEFAULT, ignore_eos: bool = False,
-                concurrency: int = 1) -> dict:
+                concurrency: int = 1, max_new: Optional[Sequence[int]] = None) -> dict:
     """Target-only autoregressive decoding through the same verify path
-    (``single/eval_async_packed.py:1489-1535``; ``serving/baseline_ar.py``)."""
-    outs: List[List[int]] = []
+    (``single/eval_async_packed.py:1489-1535``; ``serving/baseline_ar.py``,
+    ``serving/baseline_concurrency.py``): up to ``concurrency`` requests in
+    flight, a finished request's place refilled at once (closed loop, like
+    :meth:`SpecDecoder.generate`).  ``max_new``: per-request budgets."""
     started = time.perf_counter()
-    pending = list(enumerate(prompts))
+    waiting = iter(enumerate(prompts))
+    exhausted = False
     results: Dict[int, List[int]] = {}
-    while pending:
-        group = pending[:concurrency]
-        pending = pending[concurrency:]
-        seqs = [SeqState(index=i, prompt=[int(t) for t in p], prefix=len(p)) for i, p in group]
-        anchors, _ = target.prefill(seqs)
-        live = []
-        for s, a in zip(seqs, anchors.tolist()):
-            s.anchor = int(a)
-            s.generated = [s.anchor]
-            if (not ignore_eos and s.anchor in eos) or max_new_tokens <= 1:
-                results[s.index] = s.generated[:max_new_tokens]
-                target.release(s)
-            else:
-                live.append(s)
-        while live:
-            blocks = torch.tensor([[s.anchor] for s in live], dtype=torch.long)
-            res = target.verify(live, blocks)
-            nxt = []
-            for i, s in enumerate(live):
-                s.prefix += 1
-                s.anchor = int(res.correction[i])
-                s.generated.append(s.anchor)
-                if (not ignore_eos and s.anchor in eos) or len(s.generated) >= max_new_tokens:
-                    results[s.index] = s.generated
+    live: List[SeqState] = []
+
+    def budget(i: int) -> int:
+        return int(max_new[i]) if max_new is not None else int(max_new_tokens)
+
+    while live or not exhausted:
+        new: List[SeqState] = []
+        while len(live) + len(new) < concurrency and not exhausted:
+            try:
+                i, p = next(waiting)
+            except StopIteration:
+                exhausted = True
+                break
+            new.append(SeqState(index=i, prompt=[int(t) for t in p], prefix=len(p), budget=budget(i)))
+        if new:
+            anchors, _ = target.prefill(new)
+            for s, a in zip(new, anchors.tolist()):
+                s.anchor = int(a)
+                s.generated = [s.anchor]
+                if (not ignore_eos and s.anchor in eos) or s.budget <= 1:
+                    results[s.index] = s.generated[:s.budget]
                     target.release(s)
                 else:
-                    nxt.append(s)
-            live = nxt
+                    live.append(s)
+        if not live:
+            continue
+        blocks = torch.tensor([[s.anchor] for s in live], dtype=torch.long)
+        res = target.verify(live, blocks)
+        nxt = []
+        for i, s in enumerate(live):
+            s.prefix += 1
+            s.anchor = int(res.correction[i])
+            s.generated.append(s.anchor)
+            if (not ignore_eos and s.anchor in eos) or len(s.generated) >= s.budget:
+                results[s.index] = s.generated
+                target.release(s)
+            else:
+                nxt.append(s)
+        live = nxt
     elapsed = time.perf_counter() - started
     outs = [results[i] for i in range(len(prompts))]
     total = sum(len(o) for o in outs)

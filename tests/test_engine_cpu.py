@@ -191,3 +191,32 @@ def test_device_rows_reproduce_selected_branch():
             blk = oc.get(key)[0]
             src, rows = oc.device_rows(key)
             assert torch.equal(src[torch.tensor(rows), 0], blk[1:])
+
+
+def test_per_request_budgets_and_closed_loop_ar():
+    """Per-request output budgets: speculative output matches closed-loop AR
+    with the same budgets, and every request stops at its own budget."""
+    from d3d_b200.config import tiny_drafter, tiny_target
+    from d3d_b200.engine.backends import TorchDraft, TorchTarget
+    from d3d_b200.engine.spec import DecodeConfig, SpecDecoder, ar_generate
+    from d3d_b200.models.qwen3 import build_model
+    rng = random.Random(4)
+    prompts = [[rng.randrange(2, 1000) for _ in range(rng.randint(12, 30))] for _ in range(4)]
+    budgets = [5, 17, 9, 1]
+    tgt = TorchTarget(build_model(tiny_target(), seed=0))
+    drf = TorchDraft(build_model(tiny_drafter(cond=True), seed=1))
+    cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=32, ignore_eos=True)
+    res = SpecDecoder(tgt, drf, cfg).generate(prompts, concurrency=2, max_new=budgets)
+    ar = ar_generate(tgt, prompts, 32, ignore_eos=True, concurrency=3, max_new=budgets)["outputs"]
+    assert [len(o.tokens) for o in res["outputs"]] == budgets
+    assert [o.tokens for o in res["outputs"]] == ar
+
+
+def test_serve_cli_tiny_pair(tmp_path):
+    from d3d_b200.cli import serve
+    rows = serve.main(["--target", "tiny-target", "--draft", "tiny-drafter", "--device", "cpu",
+                       "--pages", "256", "--concurrency", "1,2", "--max-new-tokens-range", "6,14",
+                       "--block-size", "8", "--max-samples", "3", "--prompt-min", "10", "--prompt-max", "20",
+                       "--validate", "--ignore-eos", "--output-json", str(tmp_path / "s.json")])
+    assert [r["concurrency"] for r in rows] == [1, 2]
+    assert all(r["token_identical_to_ar"] for r in rows)
