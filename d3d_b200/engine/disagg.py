@@ -234,7 +234,7 @@ class P2PTarget(TargetBackend):
         self.closed = False
         self.draft_stream = draft_stream
         self.supports_gather = gpu and draft_stream is not None
-        self.dev_req = torch.zeros(HEAD_WORDS, dtype=torch.int64, device=self.device) if self.supports_gather \
+        self.dev_req = torch.zeros(words, dtype=torch.int64, device=self.device) if self.supports_gather \
             else None
 
     def _send(self, n_words: int) -> None:

@@ -116,6 +116,13 @@ class _FastModelBackend:
             r = self.rows_of[s.index] = self.free_rows.pop()
         return r
 
+    def leak_check(self) -> None:
+        """Raise if a sequence still holds pages or the allocator lost some
+        (called when a decode run has finished every request)."""
+        if self.kv.tables or self.kv.leaked:
+            raise RuntimeError(f"KV pages leaked: {len(self.kv.tables)} sequences still allocated, "
+                               f"{self.kv.leaked} pages unaccounted for")
+
     def _release(self, s: SeqState) -> None:
         r = self.rows_of.pop(s.index, None)
         if r is not None:

@@ -371,6 +371,10 @@ class SpecDecoder:
             if on_step is not None:
                 on_step(steps)
         elapsed = time.perf_counter() - started
+        for be in (self.t, self.d):      # every request released its pages (reference: serving/engine.py:216-218)
+            check = getattr(be, "leak_check", None)
+            if check is not None:
+                check()
         outputs.sort(key=lambda o: o.index)
         total = sum(len(o.tokens) for o in outputs)
         accepts = [a for o in outputs for a in o.accepts]
