@@ -436,7 +436,7 @@ class FastRunner:
         if use_cond and w.cond_proj is not None:
             ops.gemm_bf16(b.cond, w.cond_proj, b.cond_h, None, ops.bt_for(B), b.status)
             cond = b.cond_h
-        E.embed(b.ids, w.embed, cond, b.cond_rows if cond is not None else None, Q, b.x)
+        E.embed(b.ids, w.embed, cond, b.cond_rows if cond is not None else None, Q, b.x, b.status)
         E.add_rmsnorm(None, 1, b.x, w.layers[0].in_norm, b.xn, c.rms_norm_eps)
         torch.index_select(self.kv.block_table, 0, b.seq_rows, out=b.bt_view)
         n = 3
@@ -450,15 +450,15 @@ class FastRunner:
             if direct:
                 E.gemm_bf16(b.xn, L.qkv.data, b.qkv, None, gbt, b.status, L.qkv.n)
                 E.qkv_rope_kv(None, b.qkv, 1, L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
-                              b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps)
+                              b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps, b.status)
             else:
                 E.gemm_partial(b.xn, L.qkv.data, b.part, s, gbt, b.status, L.qkv.n)
                 E.qkv_rope_kv(b.part, None, s, L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
-                              b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps)
+                              b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps, b.status)
             E.attention(b.q, self.kv.k[li], self.kv.v[li], b.bt_view, b.rows, b.kv_end, B, Q, hq, hkv,
                         self.kv.page_size, self.scale, b.chunk, b.n_chunks,
                         b.att_o if b.n_chunks > 1 else None, b.att_ml if b.n_chunks > 1 else None,
-                        b.attn, self.batch_invariant)
+                        b.attn, self.batch_invariant, b.status)
             n += 3 + (1 if b.n_chunks > 1 else 0)
             gbt, s, direct = pl["o"]
             if tp is not None:   # row-parallel: partials exchanged, reduced in the norm

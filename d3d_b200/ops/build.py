@@ -16,8 +16,11 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
-BUILD_DIR = HERE / "_build"
-NAME = "d3d_b200_C"
+# D3D_DEBUG=1 selects a separate debug build (device bounds checks on the
+# indices the kernels take from step inputs: KV slots, pages, token ids)
+DEBUG = os.environ.get("D3D_DEBUG") == "1"
+BUILD_DIR = HERE / ("_build_debug" if DEBUG else "_build")
+NAME = "d3d_b200_C_debug" if DEBUG else "d3d_b200_C"
 
 SOURCES = ["bindings.cpp", "gemm_tcgen05.cu", "fused.cu", "attention.cu", "handoff.cu",
            "train_kernels.cu", "tp.cu", "fsdp.cu"]
@@ -48,7 +51,7 @@ def build(verbose: bool = False):
         name=NAME,
         sources=srcs,
         extra_cflags=["-O3", "-std=c++17"],
-        extra_cuda_cflags=CUDA_FLAGS,
+        extra_cuda_cflags=CUDA_FLAGS + (["-DD3D_DEBUG_BOUNDS"] if DEBUG else []),
         extra_include_paths=[str(CSRC)],
         build_directory=str(BUILD_DIR),
         verbose=verbose,
@@ -88,4 +91,21 @@ def load():
     loader.exec_module(mod)
     sys.modules[NAME] = mod
     _mod = mod
+    return mod
+
+
+def load_debug():
+    """The debug build (bounds-checked kernels), built on first use into
+    ``_build_debug`` whatever ``D3D_DEBUG`` says; returns the module."""
+    import subprocess
+    path = HERE / "_build_debug" / "d3d_b200_C_debug.so"
+    if not path.exists():
+        env = dict(os.environ, D3D_DEBUG="1")
+        subprocess.run([sys.executable, "-c", "from d3d_b200.ops import build; build.build()"], env=env,
+                       check=True, cwd=str(HERE.parents[1]))
+    name = "d3d_b200_C_debug"
+    loader = importlib.machinery.ExtensionFileLoader(name, str(path))
+    spec = importlib.util.spec_from_file_location(name, str(path), loader=loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
     return mod

@@ -165,9 +165,10 @@ __global__ void __launch_bounds__(128, 4) attn_kernel(const AttnArgs a) {
     for (int c = tid; c < AT_KEYS * (D / 8); c += 128) {
       const int kr = c / (D / 8), dc = (c % (D / 8)) * 8;
       const int s = k0 + kr;
-      if (s < kv_end) {
-        const int64_t page = s_pages[s / a.page_size - pg0];
-        const size_t off = ((page * a.page_size + s % a.page_size) * a.Hkv + h) * static_cast<size_t>(D) + dc;
+      const int64_t page = s < kv_end ? s_pages[s / a.page_size - pg0] : 0;
+      const int64_t krow = page * a.page_size + s % a.page_size;
+      if (s < kv_end && D3D_IN_BOUNDS(krow, a.num_slots, a.status)) {
+        const size_t off = (krow * a.Hkv + h) * static_cast<size_t>(D) + dc;
         cp_async16(smem_u32(Ks + kr * LD + dc), a.k_cache + off);
         cp_async16(smem_u32(Vs + kr * LD + dc), a.v_cache + off);
       } else {
@@ -564,9 +565,10 @@ __global__ void __launch_bounds__(128, 1) attn_cluster_kernel(const AttnArgs a) 
     for (int c = tid; c < AT_KEYS * (D / 8); c += 128) {
       const int kr = c / (D / 8), dc = (c % (D / 8)) * 8;
       const int s = k0 + kr;
-      if (s < kv_end) {
-        const int64_t page = s_pages[i * ppc + kr / a.page_size];
-        const size_t off = ((page * a.page_size + s % a.page_size) * a.Hkv + h) * static_cast<size_t>(D) + dc;
+      const int64_t page = s < kv_end ? s_pages[i * ppc + kr / a.page_size] : 0;
+      const int64_t krow = page * a.page_size + s % a.page_size;
+      if (s < kv_end && D3D_IN_BOUNDS(krow, a.num_slots, a.status)) {
+        const size_t off = (krow * a.Hkv + h) * static_cast<size_t>(D) + dc;
         cp_async16(smem_u32(Ks + kr * LD + dc), a.k_cache + off);
         cp_async16(smem_u32(Vs + kr * LD + dc), a.v_cache + off);
       } else {

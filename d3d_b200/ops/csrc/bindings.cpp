@@ -144,7 +144,7 @@ void swiglu(Tensor part, int64_t nsplit, Tensor h, bool interleaved) {
 
 void qkv_rope_kv(c10::optional<Tensor> part, c10::optional<Tensor> y, int64_t nsplit, Tensor q_norm, Tensor k_norm,
                  Tensor inv_freq, Tensor positions, Tensor slots, Tensor q_out, Tensor k_cache, Tensor v_cache,
-                 int64_t Hq, int64_t Hkv, int64_t D, double eps) {
+                 int64_t Hq, int64_t Hkv, int64_t D, double eps, c10::optional<Tensor> status) {
   const c10::cuda::CUDAGuard g(q_out.device());
   CHECK_DT(positions, torch::kInt64);
   CHECK_DT(slots, torch::kInt64);
@@ -168,11 +168,13 @@ void qkv_rope_kv(c10::optional<Tensor> part, c10::optional<Tensor> y, int64_t ns
   a.k_cache = bf(k_cache);
   a.v_cache = bf(v_cache);
   a.eps = static_cast<float>(eps);
+  a.num_slots = k_cache.size(0);
+  a.status = status_ptr(status);
   d3d::qkv_rope_kv(a, cur_stream());
 }
 
 void embed(Tensor ids, Tensor table, c10::optional<Tensor> cond, c10::optional<Tensor> cond_rows, int64_t q_len,
-           Tensor out) {
+           Tensor out, c10::optional<Tensor> status) {
   const c10::cuda::CUDAGuard g(out.device());
   CHECK_DT(ids, torch::kInt64);
   CHECK_CONTIG(table);
@@ -180,7 +182,8 @@ void embed(Tensor ids, Tensor table, c10::optional<Tensor> cond, c10::optional<T
   TORCH_CHECK(table.size(1) % 8 == 0, "hidden size must be a multiple of 8");
   d3d::embed(ids.data_ptr<int64_t>(), cbf(table), cond ? cbf(*cond) : nullptr,
              cond_rows ? cond_rows->data_ptr<uint8_t>() : nullptr, static_cast<int>(q_len), bf(out),
-             static_cast<int>(ids.numel()), static_cast<int>(table.size(1)), cur_stream());
+             static_cast<int>(ids.numel()), static_cast<int>(table.size(1)), cur_stream(), table.size(0),
+             status_ptr(status));
 }
 
 void topk_merge(Tensor tv, Tensor ti, int64_t M, int64_t ntiles, int64_t kt, int64_t k, c10::optional<Tensor> ov,
@@ -210,7 +213,7 @@ void greedy_accept(Tensor blocks, Tensor post, Tensor commit, Tensor corr, c10::
 void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor rows, Tensor kv_end,
                int64_t B, int64_t q_len, int64_t Hq, int64_t Hkv, int64_t page_size, double scale, int64_t chunk,
                int64_t n_chunks, c10::optional<Tensor> part_o, c10::optional<Tensor> part_ml, Tensor out,
-               bool invariant) {
+               bool invariant, c10::optional<Tensor> status) {
   const c10::cuda::CUDAGuard g(q.device());
   CHECK_CONTIG(q);
   CHECK_CONTIG(out);
@@ -241,6 +244,8 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
   a.part_o = part_o ? part_o->data_ptr<float>() : nullptr;
   a.part_ml = part_ml ? part_ml->data_ptr<float>() : nullptr;
   a.out = bf(out);
+  a.num_slots = k_cache.size(0);
+  a.status = status_ptr(status);
   d3d::attention(a, cur_stream());
 }
 
@@ -528,14 +533,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu", &swiglu, py::arg("part"), py::arg("nsplit"), py::arg("h"), py::arg("interleaved") = false);
   m.def("gemm_swiglu", &gemm_swiglu, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("bt"),
         py::arg("status") = py::none(), py::arg("wn") = 0);
-  m.def("qkv_rope_kv", &qkv_rope_kv);
-  m.def("embed", &embed);
+  m.def("qkv_rope_kv", &qkv_rope_kv, py::arg("part"), py::arg("y"), py::arg("nsplit"), py::arg("q_norm"),
+        py::arg("k_norm"), py::arg("inv_freq"), py::arg("positions"), py::arg("slots"), py::arg("q_out"),
+        py::arg("k_cache"), py::arg("v_cache"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("eps"),
+        py::arg("status") = py::none());
+  m.def("embed", &embed, py::arg("ids"), py::arg("table"), py::arg("cond"), py::arg("cond_rows"), py::arg("q_len"),
+        py::arg("out"), py::arg("status") = py::none());
   m.def("topk_merge", &topk_merge);
   m.def("greedy_accept", &greedy_accept);
   m.def("attention", &attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
         py::arg("rows"), py::arg("kv_end"), py::arg("B"), py::arg("q_len"), py::arg("Hq"), py::arg("Hkv"),
         py::arg("page_size"), py::arg("scale"), py::arg("chunk"), py::arg("n_chunks"), py::arg("part_o"),
-        py::arg("part_ml"), py::arg("out"), py::arg("invariant") = false);
+        py::arg("part_ml"), py::arg("out"), py::arg("invariant") = false, py::arg("status") = py::none());
   m.def("gemm_stages", &d3d::gemm_stages);
   m.def("kl_ce_stats", &kl_ce_stats);
   m.def("kl_ce_grad", &kl_ce_grad);

@@ -59,6 +59,7 @@ enum : int {
   ERR_TIMEOUT_EPILOGUE = 3,
   ERR_TIMEOUT_FLAG = 4,
   ERR_BAD_ARG = 5,
+  ERR_BOUNDS = 6,     // debug builds: an index was outside its buffer (the access was skipped)
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -70,6 +71,20 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 __device__ __forceinline__ void set_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
+
+// Debug-build bounds checks (build with D3D_DEBUG=1, which defines
+// D3D_DEBUG_BOUNDS): ``D3D_IN_BOUNDS(i, n, status)`` is true when 0 <= i < n;
+// otherwise it records ERR_BOUNDS and the caller skips the access (n <= 0
+// means the size is unknown and nothing is checked).  In normal builds it is
+// the constant true and costs nothing.
+#ifdef D3D_DEBUG_BOUNDS
+#define D3D_IN_BOUNDS(i, n, status) \
+  ((static_cast<long long>(n) <= 0 ||  /* size unknown to the caller: no check */ \
+    (static_cast<long long>(i) >= 0 && static_cast<long long>(i) < static_cast<long long>(n))) \
+       ? true : (::d3d::set_error((status), ::d3d::ERR_BOUNDS), false))
+#else
+#define D3D_IN_BOUNDS(i, n, status) true
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

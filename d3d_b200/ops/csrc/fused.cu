@@ -238,6 +238,7 @@ __global__ void qkv_rope_kv_kernel(QkvRopeArgs a) {
       x[e] = bf16r(a.part ? load_split_sum<S>(a.part, a.nsplit, stride, off0 + e) : __bfloat162float(a.y[off0 + e]));
   }
   const int64_t slot = a.slots[m];
+  if (h >= a.Hq && !D3D_IN_BOUNDS(slot, a.num_slots, a.status)) return;   // debug builds only
   if (h >= a.Hq + a.Hkv) {  // v head: straight to the cache
     const int hv = h - a.Hq - a.Hkv;
     __nv_bfloat16* dst = a.v_cache + (slot * a.Hkv + hv) * D + lane * E;
@@ -298,11 +299,12 @@ void qkv_rope_kv(const QkvRopeArgs& a, cudaStream_t st) {
 // out[m] = table[ids[m]] (+ cond[m / q_len] where cond_rows[m])
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              const __nv_bfloat16* __restrict__ cond, const unsigned char* __restrict__ cond_rows,
-                             int q_len, __nv_bfloat16* __restrict__ out, int M, int H) {
+                             int q_len, __nv_bfloat16* __restrict__ out, int M, int H, long long vocab, int* status) {
   griddep_launch();
   griddep_wait();
   const int m = blockIdx.x;
-  const int64_t id = ids[m];
+  int64_t id = ids[m];
+  if (!D3D_IN_BOUNDS(id, vocab, status)) id = 0;   // debug builds only
   const bool add = cond != nullptr && cond_rows != nullptr && cond_rows[m];
   const int b = m / q_len;
   for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
@@ -321,9 +323,9 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
 }
 
 void embed(const int64_t* ids, const __nv_bfloat16* table, const __nv_bfloat16* cond, const unsigned char* cond_rows,
-           int q_len, __nv_bfloat16* out, int M, int H, cudaStream_t st) {
+           int q_len, __nv_bfloat16* out, int M, int H, cudaStream_t st, long long vocab, int* status) {
   if (M == 0) return;
-  launch_pdl(embed_kernel, dim3(M), dim3(128), 0, st, ids, table, cond, cond_rows, q_len, out, M, H);
+  launch_pdl(embed_kernel, dim3(M), dim3(128), 0, st, ids, table, cond, cond_rows, q_len, out, M, H, vocab, status);
 }
 
 // ---------------------------------------------------------- top-k merge

@@ -24,11 +24,13 @@ struct QkvRopeArgs {
   __nv_bfloat16* k_cache;   // [slots][Hkv][D]
   __nv_bfloat16* v_cache;
   float eps;
+  long long num_slots;      // KV cache rows (debug bounds checks)
+  int* status;              // error word (debug bounds checks; may be null)
 };
 void qkv_rope_kv(const QkvRopeArgs& a, cudaStream_t st);
 
 void embed(const int64_t* ids, const __nv_bfloat16* table, const __nv_bfloat16* cond, const unsigned char* cond_rows,
-           int q_len, __nv_bfloat16* out, int M, int H, cudaStream_t st);
+           int q_len, __nv_bfloat16* out, int M, int H, cudaStream_t st, long long vocab = 0, int* status = nullptr);
 
 void topk_merge(const float* tv, const int* ti, int ntiles, int kt, int k, float* ov, int64_t* oi, int M,
                 cudaStream_t st);
@@ -52,6 +54,8 @@ struct AttnArgs {
   float* part_o;            // [n_chunks][T][Hq][D]
   float* part_ml;           // [n_chunks][T][Hq][2]
   __nv_bfloat16* out;       // [T][Hq][D]
+  long long num_slots;      // KV cache rows (debug bounds checks)
+  int* status;              // error word (debug bounds checks; may be null)
 };
 void attention(const AttnArgs& a, cudaStream_t st);        // cluster kernel (no partial buffers)
 void attention_split(const AttnArgs& a, cudaStream_t st);  // split-KV + combine (uses part_o / part_ml)
