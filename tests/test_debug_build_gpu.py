@@ -29,8 +29,9 @@ def test_debug_build_matches_normal_build():
     for mod in (E, D):
         st = torch.zeros(1, dtype=torch.int32, device="cuda")
         out = torch.empty_like(qq)
-        mod.attention(qq, kc, vc, bt, rows, kv_end, 1, q, hq, hkv, 16, 1 / math.sqrt(d), 64,
-                      math.ceil(L / 64), None, None, out, True, st)
+        # batch-invariant path (cluster kernel): no split-KV partial buffers
+        mod.attention(qq, kc, vc, bt, rows, kv_end, 1, q, hq, hkv, 16, 1 / math.sqrt(d), 64, 1, None, None,
+                      out, True, st)
         emb = torch.empty(12, 256, dtype=torch.bfloat16, device="cuda")
         mod.embed(ids, table, None, None, 12, emb, st)
         torch.cuda.synchronize()
