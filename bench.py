@@ -31,7 +31,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_TPS = 501.60   # BASELINE.md headline: SGLang Hybrid aggregate TPS, 2xH800
+BASELINE_TPS = 501.60   # published headline: SGLang Hybrid aggregate TPS, 2xH800 (README.md:251-253 of the reference)
 METRIC = "decode tokens/s + speedup vs AR, Qwen3-8B target/1.7B draft, concurrency 1–8"
 EOS = (151643, 151645)
 
