@@ -34,3 +34,23 @@ def test_local_config_and_shards_reassemble():
     g0[ops.gate_up_order(il)] = L0.gate_up.unpack()
     assert torch.equal(g0[:il], gu[:il]) and torch.equal(g0[il:], gu[I:I + il])
     assert torch.equal(torch.cat([sh[0].lm_head.unpack(), sh[1].lm_head.unpack()]), full.lm_head.unpack())
+
+
+def test_random_shard_shapes():
+    """A directly drawn shard has the per-rank shapes and a full, replicated
+    embedding identical on every rank."""
+    from d3d_b200.config import tiny_target
+    from d3d_b200.parallel.tp import local_config, random_shard
+    cfg = tiny_target().replace(tie_word_embeddings=False)
+    lc = local_config(cfg, 2)
+    s0 = random_shard(cfg, 2, 0, seed=3, device="cpu")
+    s1 = random_shard(cfg, 2, 1, seed=3, device="cpu")
+    d = cfg.head_dim
+    assert s0.layers[0].qkv.shape == ((lc.num_attention_heads + 2 * lc.num_key_value_heads) * d, cfg.hidden_size)
+    assert s0.layers[0].o.shape == (cfg.hidden_size, lc.num_attention_heads * d)
+    assert s0.layers[0].gate_up.shape == (2 * lc.intermediate_size, cfg.hidden_size)
+    assert s0.layers[0].down.shape == (cfg.hidden_size, lc.intermediate_size)
+    assert s0.lm_head.shape == (cfg.vocab_size // 2, cfg.hidden_size)
+    assert s0.embed.shape == (cfg.vocab_size, cfg.hidden_size)
+    assert torch.equal(s0.embed, s1.embed)
+    assert not torch.equal(s0.layers[0].qkv.data, s1.layers[0].qkv.data)
