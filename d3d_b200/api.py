@@ -135,15 +135,29 @@ def open_pair_link(peer: int, device, slot_bytes: Optional[int] = None, group=No
     return Link(peer, slot_bytes or DEFAULT_SLOT_BYTES, torch.device(device), group)
 
 
+def load_target_shard(path: str, tp: int, rank: int, device="cuda"):
+    """One rank's :class:`~d3d_b200.models.fast.FastWeights` of a
+    tensor-parallel target, read slice by slice from an HF checkpoint."""
+    from .checkpoint import load_tp_shard
+    from .models.fast import FastWeights
+    from .parallel.tp import local_config
+    cfg = ModelConfig.from_pretrained(path)
+    w = FastWeights.from_state(local_config(cfg, tp), load_tp_shard(path, rank, tp, device=device), device)
+    w.tp = (tp, rank, cfg)
+    return w
+
+
 def target_server(target_w, link, *, max_seqs: int = 16, max_context: int = 4096,
                   target_pages: Optional[int] = None, page_size: int = 16, device="cuda",
-                  use_graphs: bool = True, deadline_s: float = 600.0):
+                  use_graphs: bool = True, deadline_s: float = 600.0, tp=None, replies: str = "all"):
     """The target side of a disaggregated pair: call ``.serve()`` on the result;
     it returns when the drafter side calls :meth:`D3DEngine.close`, and raises
-    ``TimeoutError`` after ``deadline_s`` without a request."""
+    ``TimeoutError`` after ``deadline_s`` without a request.  For one rank of
+    a tensor-parallel target pass its ``TPGroup`` as ``tp`` (and
+    ``replies="ack"`` on every rank but 0)."""
     from .engine.disagg import P2PTargetServer
     from .engine.fast import FastTarget
-    tp = target_pages or max_seqs * (max_context + 64 + page_size) // page_size + 8
-    t = FastTarget(target_w, pages=tp, page_size=page_size, max_seqs=max_seqs,
-                   max_context=max_context, use_graphs=use_graphs, device=device)
-    return P2PTargetServer(t, link, deadline_s=deadline_s)
+    pages = target_pages or max_seqs * (max_context + 64 + page_size) // page_size + 8
+    t = FastTarget(target_w, pages=pages, page_size=page_size, max_seqs=max_seqs,
+                   max_context=max_context, use_graphs=use_graphs, device=device, tp=tp)
+    return P2PTargetServer(t, link, deadline_s=deadline_s, replies=replies)

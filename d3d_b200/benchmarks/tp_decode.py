@@ -40,6 +40,8 @@ def parse():
     p.add_argument("--accept-mean", type=float, default=5.0)
     p.add_argument("--concurrency", type=int, default=1)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--target-path", default=None, help="HF checkpoint (each rank reads only its slices)")
+    p.add_argument("--draft-path", default=None, help="HF checkpoint of the drafter")
     return p.parse_args()
 
 
@@ -79,8 +81,13 @@ def main():
     ar_out, ar_time, ar_tokens = {}, 0.0, 0
     if not drafter:
         grp = TPGroup(rank, T, dev, group=tp_group, num_layers=tcfg.num_hidden_layers) if T > 1 else None
-        w = random_shard(tcfg, T, rank, seed=a.seed, device=dev) if T > 1 else \
-            FastWeights.random(tcfg, seed=a.seed, device=dev)
+        if a.target_path:
+            from d3d_b200.api import load_target_shard
+            w = load_target_shard(a.target_path, T, rank, device=dev)
+            tcfg = w.tp[2]
+        else:
+            w = random_shard(tcfg, T, rank, seed=a.seed, device=dev) if T > 1 else \
+                FastWeights.random(tcfg, seed=a.seed, device=dev)
         link = Link(1, DEFAULT_SLOT_BYTES, dev, group=pairs[rank])
         pages = max(4, cc) * (max_ctx + 64 + 16) // 16 + 8
         tgt = FastTarget(w, pages=pages, max_seqs=max(4, cc), max_context=max_ctx, device=dev, tp=grp)
@@ -100,7 +107,11 @@ def main():
         srv = P2PTargetServer(tgt, link, replies="all" if rank == 0 else "ack")
     else:
         links = [Link(0, DEFAULT_SLOT_BYTES, dev, group=pairs[j]) for j in range(T)]
-        dw = FastWeights.random(dcfg, seed=a.seed, device=dev)
+        if a.draft_path:
+            from d3d_b200.checkpoint import load_model
+            dw = FastWeights.from_module(load_model(a.draft_path), dev)
+        else:
+            dw = FastWeights.random(dcfg, seed=a.seed, device=dev)
         packed_q = paged_draft_branch_tokens(K, 1)
         dp = max(4, cc) * (max_ctx + packed_q + 16) // 16 + 8
         d = FastDraft(dw, pages=dp, max_seqs=max(4, cc), max_context=max_ctx, packed_q=packed_q, device=dev)

@@ -164,15 +164,38 @@ def load_tp_shard(path: str | Path, rank: int, world: int, device="cuda",
 
     Column-parallel (split output rows): q/k/v, gate/up, and the LM head
     (vocab-parallel).  Row-parallel (split input columns): o, down.  Norms
-    and embeddings are replicated."""
+    and embeddings are replicated.  Slices are read straight from the
+    safetensors files (only this rank's part of a split tensor is read), one
+    tensor at a time, so host memory stays at one tensor."""
     cfg = ModelConfig.from_pretrained(path)
     if cfg.num_key_value_heads % world or cfg.num_attention_heads % world:
         raise ValueError("heads must divide the tensor-parallel world size")
+    path = Path(path)
+    wm = _shard_files(path)
+    want = set(expected_keys(cfg))
+    if cfg.tie_word_embeddings:
+        want.discard("lm_head.weight")
+    by_file: Dict[str, list] = {}
+    for k in want:
+        if k not in wm:
+            raise KeyError(f"checkpoint {path} is missing tensor {k}")
+        by_file.setdefault(wm[k], []).append(k)
     out = {}
-    for k, t in read_state(path, expected_keys(cfg).keys()).items():
-        if any(s in k for s in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj")) or k == "lm_head.weight":
-            t = t.chunk(world, 0)[rank]
-        elif "o_proj" in k or "down_proj" in k:
-            t = t.chunk(world, 1)[rank]
-        out[k] = t.to(device=device, dtype=dtype).contiguous()
+    for f, ks in by_file.items():
+        with _st().safe_open(str(path / f), "pt") as fh:
+            for k in sorted(ks):
+                sl = fh.get_slice(k)
+                shape = sl.get_shape()
+                if any(n in k for n in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj")) or k == "lm_head.weight":
+                    step = shape[0] // world
+                    t = sl[rank * step:(rank + 1) * step]
+                elif "o_proj" in k or "down_proj" in k:
+                    step = shape[1] // world
+                    t = sl[:, rank * step:(rank + 1) * step]
+                else:
+                    t = sl[:]
+                out[k] = t.to(device=device, dtype=dtype).contiguous()
+    if cfg.tie_word_embeddings:
+        v = cfg.vocab_size // world
+        out["lm_head.weight"] = out["model.embed_tokens.weight"][rank * v:(rank + 1) * v].contiguous()
     return out

@@ -79,6 +79,31 @@ class FastWeights:
         cp = pk(m.cond_proj.weight) if getattr(m, "cond_proj", None) is not None else None
         return cls(m.cfg, embed, layers, bf(m.model.norm.weight), lm, cp)
 
+    @classmethod
+    @torch.no_grad()
+    def from_state(cls, cfg: ModelConfig, state: Dict[str, torch.Tensor], device="cuda") -> "FastWeights":
+        """Kernel layouts from a Hugging-Face-named state dict whose tensors
+        already have ``cfg``'s (possibly per-rank) shapes -- e.g. one rank's
+        slices from ``checkpoint.load_tp_shard`` with a ``parallel.tp.local_config``."""
+        bf = lambda t: t.to(device=device, dtype=torch.bfloat16).contiguous()
+        pk = lambda t: ops.pack_weight(bf(t))
+        layers = []
+        for n in range(cfg.num_hidden_layers):
+            p = f"model.layers.{n}."
+            g = lambda k: state[p + k]
+            layers.append(LayerWeights(
+                qkv=pk(torch.cat([g("self_attn.q_proj.weight"), g("self_attn.k_proj.weight"),
+                                  g("self_attn.v_proj.weight")], 0)),
+                o=pk(g("self_attn.o_proj.weight")),
+                gate_up=ops.pack_gate_up(bf(g("mlp.gate_proj.weight")), bf(g("mlp.up_proj.weight"))),
+                down=pk(g("mlp.down_proj.weight")),
+                in_norm=bf(g("input_layernorm.weight")), post_norm=bf(g("post_attention_layernorm.weight")),
+                q_norm=bf(g("self_attn.q_norm.weight")), k_norm=bf(g("self_attn.k_norm.weight"))))
+        embed = bf(state["model.embed_tokens.weight"])
+        lm = pk(state["lm_head.weight"]) if "lm_head.weight" in state else ops.pack_weight(embed)
+        cp = pk(state["cond_proj.weight"]) if "cond_proj.weight" in state else None
+        return cls(cfg, embed, layers, bf(state["model.norm.weight"]), lm, cp)
+
     @staticmethod
     @torch.no_grad()
     def seeded_randn(shape, key: int, std: float, device="cuda") -> torch.Tensor:

@@ -54,3 +54,28 @@ def test_random_shard_shapes():
     assert s0.embed.shape == (cfg.vocab_size, cfg.hidden_size)
     assert torch.equal(s0.embed, s1.embed)
     assert not torch.equal(s0.layers[0].qkv.data, s1.layers[0].qkv.data)
+
+
+def test_sliced_checkpoint_shards_equal_sharded_full_weights(tmp_path):
+    """Reading one rank's slices from the safetensors checkpoint gives the
+    same kernel weights as loading everything and sharding."""
+    from d3d_b200.api import load_target_shard
+    from d3d_b200.checkpoint import save_model
+    from d3d_b200.config import tiny_target
+    from d3d_b200.models.fast import FastWeights
+    from d3d_b200.models.qwen3 import build_model
+    from d3d_b200.parallel.tp import shard_weights
+    for tied in (False, True):
+        cfg = tiny_target().replace(tie_word_embeddings=tied)
+        m = build_model(cfg, seed=5)
+        d = tmp_path / f"ck{int(tied)}"
+        save_model(m, d)
+        full = FastWeights.from_module(m, "cpu")
+        for r in range(2):
+            a = load_target_shard(str(d), 2, r, device="cpu")
+            b = shard_weights(full, 2, r)
+            for la, lb in zip(a.layers, b.layers):
+                for name in ("qkv", "o", "gate_up", "down"):
+                    assert torch.equal(getattr(la, name).data, getattr(lb, name).data), (tied, r, name)
+            assert torch.equal(a.lm_head.data, b.lm_head.data)
+            assert torch.equal(a.embed, b.embed)
