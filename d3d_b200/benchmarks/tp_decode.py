@@ -67,7 +67,7 @@ def main():
     drafter = rank == T
     tp_group = dist.new_group(list(range(T)))
     pairs = [dist.new_group([j, T]) for j in range(T)]
-    tcfg = C.PRESETS[a.target]()
+    tcfg = C.ModelConfig.from_pretrained(a.target_path) if a.target_path else C.PRESETS[a.target]()
     dcfg = C.d3d_1p7b(num_layers=a.draft_layers)
     K = 16
     decode = DecodeConfig(block_size=K, anchor_num=1, max_new_tokens=a.max_new_tokens, eos=EOS)
@@ -84,7 +84,6 @@ def main():
         if a.target_path:
             from d3d_b200.api import load_target_shard
             w = load_target_shard(a.target_path, T, rank, device=dev)
-            tcfg = w.tp[2]
         else:
             w = random_shard(tcfg, T, rank, seed=a.seed, device=dev) if T > 1 else \
                 FastWeights.random(tcfg, seed=a.seed, device=dev)
