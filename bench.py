@@ -280,14 +280,27 @@ def run_disagg(args, rank, world, local):
         eng.close()
 
     phase(range(args.warmup))
-    tokens, accepts, ident = 0, [], True
+    tokens, accepts, ident, dsteps = 0, [], True, 0
 
     def check(gi, r):
-        nonlocal tokens, ident
+        nonlocal tokens, ident, dsteps
+        dsteps += r["steps"]
         for j, o in enumerate(r["outputs"]):
             tokens += len(o.tokens)
             accepts.extend(o.accepts)
             ident &= o.tokens == ar_out[gi * cc + j]
+
+    # device timers (CUDA events around each captured forward) for the
+    # exposed-handoff figure: step time minus the slower of verify and draft
+    from d3d_b200.utils.timing import StepProfiler
+    prof = StepProfiler(True)
+    if is_target:
+        srv.be.prof = prof
+    else:
+        eng.decoder.prof = prof
+        for be in (eng.decoder.t, eng.decoder.d):
+            if hasattr(be, "prof"):
+                be.prof = prof
 
     barrier()
     launches.reset()
@@ -302,6 +315,29 @@ def run_disagg(args, rank, world, local):
         barrier()
     n_launch = launches.count()
     dev_s = ev0.elapsed_time(ev1) / 1e3
+    if is_target:
+        srv.be.prof = StepProfiler(False)
+    else:
+        eng.decoder.prof = StepProfiler(False)
+        for be in (eng.decoder.t, eng.decoder.d):
+            if hasattr(be, "prof"):
+                be.prof = eng.decoder.prof
+
+    def _busiest(prefix):
+        dev = prof.summary()["device"]
+        rows = [v for k, v in dev.items() if k.startswith(prefix)]
+        return max(rows, key=lambda v: v["n"])["ms_each"] if rows else 0.0
+
+    mine = (_busiest("verify_") if is_target else _busiest("draft_"), dsteps, dev_s)
+    timers = [None] * world
+    dist.all_gather_object(timers, mine)
+    verify_ms = statistics.fmean(t[0] for i, t in enumerate(timers) if i % 2 == 0)
+    draft_ms = statistics.fmean(t[0] for i, t in enumerate(timers) if i % 2 == 1)
+    step_ms = statistics.fmean(1e3 * t[2] / max(1, t[1]) for i, t in enumerate(timers) if i % 2 == 1)
+    handoff = {"step_ms": round(step_ms, 3), "verify_ms": round(verify_ms, 3), "draft_ms": round(draft_ms, 3),
+               "exposed_ms": round(step_ms - max(verify_ms, draft_ms), 3),
+               "note": "per decode step: step time minus the slower of the concurrent verify and packed "
+                       "draft forwards (CUDA events), averaged over pairs"}
 
     e2e = None
     if not args.no_e2e:
@@ -365,6 +401,7 @@ def run_disagg(args, rank, world, local):
         "ar_tokens_per_s": round(ar_value, 2) if ar_value else None,
         "speedup_vs_ar": round(value / ar_value, 3) if ar_value else None,
         "speedup_note": "per pair (2 GPUs) vs target-only AR on one GPU, as the reference reports it",
+        "handoff": handoff,
         "token_identical_to_ar": bool(ident_all),
         "gpu_launches": n_launch_all,
         "clocks": clk.summary(),
