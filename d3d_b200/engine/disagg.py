@@ -11,7 +11,9 @@ mailboxes of :mod:`d3d_b200.parallel.p2p` instead of a host Pipe:
   :class:`~d3d_b200.engine.fast.FastTarget`.
 
 Every message is a run of int64 words in one mailbox slot, starting with an
-8-word header (the formats of :mod:`d3d_b200.serving.remote`):
+8-word header (the same messages travel over ``torch.distributed`` between
+CPU processes through :class:`~d3d_b200.parallel.p2p.HostLink`,
+:mod:`d3d_b200.serving.remote`):
 
 =========  ==========================================  ==========================================
 command    request (drafter -> target)                 reply (target -> drafter)
