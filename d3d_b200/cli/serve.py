@@ -62,7 +62,8 @@ def main(argv=None):
     ctl = None
     if a.controlled_accept_mean is not None:
         rate = rate_for_mean_accept(a.controlled_accept_mean, a.block_size)
-        ctl = lambda i: ControlledAcceptance(prompts[i] + ar["outputs"][i], rate, 151936, seed=a.seed, stream=i)
+        ctl = lambda i: ControlledAcceptance(prompts[i] + ar["outputs"][i], rate, int(eng.draft.vocab_size),
+                                             seed=a.seed, stream=i)
     eng.generate(prompts[:1], max_new_tokens=16, controlled=ctl)           # warm-up
     rows = []
     for c in conc:

@@ -31,6 +31,10 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--temperature", type=float, default=0.0)
     p.add_argument("--proposal-top-k", type=int, default=0)
     p.add_argument("--proposal-top-p", type=float, default=1.0)
+    p.add_argument("--target-top-k", type=int, default=0, help="target sampling truncation (kernel path: 1..4)")
+    p.add_argument("--target-top-p", type=float, default=1.0)
+    p.add_argument("--collect-stage-timings", action="store_true",
+                   help="host time per coordinator phase and device time per captured forward")
     p.add_argument("--ignore-eos", action="store_true")
     p.add_argument("--baseline", action="store_true", help="also run target-only AR decoding")
     p.add_argument("--controlled-accept-mean", type=float, default=None,
@@ -46,7 +50,8 @@ def main(argv=None):
     counts = None if a.packed_accepted_counts == "all" else tuple(int(x) for x in a.packed_accepted_counts.split(","))
     decode = DecodeConfig(block_size=a.block_size, anchor_num=a.anchor_num, attention_mask_mode=a.attention_mask_mode,
                           max_new_tokens=a.max_new_tokens, temperature=a.temperature, top_k=a.proposal_top_k,
-                          top_p=a.proposal_top_p, ignore_eos=a.ignore_eos, packed_accepted_counts=counts)
+                          top_p=a.proposal_top_p, ignore_eos=a.ignore_eos, packed_accepted_counts=counts,
+                          target_top_k=a.target_top_k, target_top_p=a.target_top_p)
     prompts = load_prompts(a)
     eng = build_engine(a, decode, max_seqs=2, max_context=max(len(p) for p in prompts) + a.max_new_tokens + 64)
     ar = None
@@ -58,10 +63,13 @@ def main(argv=None):
     ctl = None
     if a.controlled_accept_mean is not None:
         rate = rate_for_mean_accept(a.controlled_accept_mean, a.block_size)
-        ctl = lambda i: ControlledAcceptance(prompts[i] + ar["outputs"][i], rate, 151936 if True else 0,
-                                             seed=a.seed, stream=i)
+        vocab = int(eng.draft.vocab_size)      # drafter and target share the vocabulary
+        ctl = lambda i: ControlledAcceptance(prompts[i] + ar["outputs"][i], rate, vocab, seed=a.seed, stream=i)
     if a.warmup_new_tokens:
         eng.generate(prompts[:1], max_new_tokens=a.warmup_new_tokens, controlled=ctl)
+    if a.collect_stage_timings:
+        eng.decoder.prof.enabled = True
+        eng.decoder.prof.reset()
     per = []
     t0 = time.perf_counter()
     for i, p in enumerate(prompts):
@@ -86,6 +94,8 @@ def main(argv=None):
     summary = {"headline": headline(tps, baseline_tps or 0.0, acc), "elapsed_s": elapsed,
                "token_identical_to_ar": all(x["matches_ar"] for x in per) if ar else None,
                "config": vars(a)}
+    if a.collect_stage_timings:
+        summary["stage_timings"] = eng.decoder.prof.summary()
     write_json(a.output_json, {"summary": summary, "per_prompt": per})
     write_json(a.summary_json, summary)
     print(summary["headline"])

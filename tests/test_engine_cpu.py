@@ -220,3 +220,19 @@ def test_serve_cli_tiny_pair(tmp_path):
                        "--validate", "--ignore-eos", "--output-json", str(tmp_path / "s.json")])
     assert [r["concurrency"] for r in rows] == [1, 2]
     assert all(r["token_identical_to_ar"] for r in rows)
+
+
+def test_single_cli_controlled_with_stage_timings(tmp_path):
+    """The single-request CLI in controlled mode on the tiny pair (the
+    corruption draws stay inside the model's vocabulary) with stage timings."""
+    import json
+    from d3d_b200.cli import single
+    out = tmp_path / "single.json"
+    single.main(["--verifier", "tiny-target", "--drafter", "tiny-drafter", "--device", "cpu",
+                 "--max-new-tokens", "12", "--block-size", "8", "--anchor-num", "1", "--max-samples", "2",
+                 "--prompt-min", "8", "--prompt-max", "16", "--baseline", "--controlled-accept-mean", "3",
+                 "--collect-stage-timings", "--ignore-eos", "--warmup-new-tokens", "4",
+                 "--output-json", str(out)])
+    d = json.loads(out.read_text())
+    assert d["summary"]["token_identical_to_ar"] is True
+    assert "host_ms" in d["summary"]["stage_timings"]
