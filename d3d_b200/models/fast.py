@@ -1,4 +1,6 @@
 """The Qwen3 / D3D forward on the sm_100a kernels (inference fast path).
+Reference counterparts: the paged runner ``serving/backend.py:44-136`` and
+the vendored Qwen3 ``serving/vendor/ssd/models/qwen3.py:14-325``.
 
 Weights are held in bf16 in fused layouts (``qkv = [q; k; v]`` and
 ``gate_up = [gate; up]`` rows), the KV cache is paged

@@ -1,4 +1,6 @@
-// Paged-KV attention with structured masks (sm_100a).
+// Paged-KV attention with structured masks (sm_100a).  Reference
+// counterparts: serving/vendor/ssd/layers/attention.py:8-53 (FlashAttention-2
+// and dense-mask SDPA calls) and the mask builders of single/eval_sync.py:194-275.
 //
 // One kernel serves every attention of the framework: target prefill and
 // verify (causal over the block), drafter prefill (causal / block-causal),

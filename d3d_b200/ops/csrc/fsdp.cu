@@ -1,4 +1,5 @@
 // Sharded-optimizer step fused with its collectives over NVLink (sm_100a).
+// The reference shards with FSDP2 through Accelerate (train/runtime.py:70-114).
 //
 // Every rank keeps its full fp32 gradient and its full bf16 parameter copy in
 // device buffers that all peers have mapped through CUDA IPC.  Rank r owns

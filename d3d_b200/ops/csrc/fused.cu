@@ -1,4 +1,8 @@
 // Memory-bound fused kernels of the decoder layer (sm_100a).
+// Reference counterparts: serving/vendor/ssd/layers/layernorm.py:5-98 (add +
+// RMSNorm), rotary_embedding.py:6-73, activation.py:6-14 (SiLU-mul), the
+// head-wise QK-norm of serving/vendor/ssd/models/qwen3.py, and the greedy match of
+// single/eval_async_packed.py:170-175.
 //
 // Each GEMM of the layer writes fp32 split-K partials; the kernel that consumes
 // them reduces the splits in a fixed order and fuses what follows the matmul:

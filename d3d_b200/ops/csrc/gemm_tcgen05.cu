@@ -1,4 +1,7 @@
 // Weight-stationary tcgen05 GEMM for sm_100a:  Y[M, N] = X[M, K] · W[N, K]^T.
+// It stands in for the reference's linear layers (serving/vendor/ssd/layers/
+// linear.py:42-199) and its chunked LM-head greedy / top-k selection
+// (serving/backend.py:78-95), with the top-k fused into the epilogue.
 //
 // Decode-time matmuls have few tokens (M = 1..1088) against large weights, so
 // the tile is laid out "swap-AB": the 128-row MMA M dimension runs over weight

@@ -1,4 +1,6 @@
-// Cross-GPU handoff over NVLink peer memory (sm_100a).
+// Cross-GPU handoff over NVLink peer memory (sm_100a).  It replaces the
+// reference's host Pipe between the drafter and the verifier process
+// (single/eval_async_packed.py:216-346, serving/target_process.py:9-139).
 //
 // A mailbox is a device allocation [flag (int64, own 128-byte line) |
 // payload] owned by the receiving GPU and mapped into the sender's process

@@ -1,4 +1,6 @@
-// Tensor-parallel exchange kernels (sm_100a, one process per GPU).
+// Tensor-parallel exchange kernels (sm_100a, one process per GPU).  The
+// reference's tensor-parallel layers exist but run at tp_size=1
+// (serving/vendor/ssd/layers/linear.py:68-199, embed_head.py:9-116).
 //
 // The target's row-parallel GEMMs (o_proj, down_proj) push their fp32
 // split-K partials from the GEMM epilogue into every rank's exchange region

@@ -1,5 +1,7 @@
 // Training kernels (sm_100a): distillation loss over vocabulary chunks and
-// the sharded AdamW update.
+// the sharded AdamW update (reference: train/objective_kernels.py:7-37 full-vocab
+// KL in PyTorch, train/losses.py:209-315 chunked CE, AdamW via FSDP2 in
+// train/runtime.py:70-114).
 //
 // The LM-head loss never materialises [N, V] logits.  The vocabulary is
 // walked in chunks of C columns; for each chunk the teacher and student
