@@ -236,3 +236,23 @@ def test_single_cli_controlled_with_stage_timings(tmp_path):
     d = json.loads(out.read_text())
     assert d["summary"]["token_identical_to_ar"] is True
     assert "host_ms" in d["summary"]["stage_timings"]
+
+
+def test_gemm_policies():
+    """Token tiles and split-K choices: tiles cover the tokens within the MMA
+    limits, and the target's split depends on the weight shape only."""
+    from d3d_b200 import ops
+    for m in (1, 15, 16, 17, 255, 256, 257, 272, 511, 512, 513, 1088, 4096):
+        bt = ops.bt_for(m)
+        assert bt % 16 == 0 and 16 <= bt <= 512
+        if bt > 256:
+            assert bt % 32 == 0
+        tiles = -(-m // bt)
+        assert tiles * bt >= m and (tiles - 1) * bt < m
+    for n, k in ((6144, 4096), (4096, 4096), (24576, 4096), (4096, 12288), (151936, 4096)):
+        s = ops.splitk_for(n, k, mtiles=1, bt=16)
+        assert 1 <= s <= 16 and (k // 64) // s >= 4 or s == 1
+        assert s == ops.splitk_for(n, k, mtiles=1, bt=16)
+    # the drafter cap keeps fp32 partials no larger than the weight
+    s = ops.splitk_for(2048, 2048, mtiles=1, bt=288, m=272)
+    assert s * 272 * 2048 * 4 <= 2048 * 2048 * 2 * 2
