@@ -167,6 +167,26 @@ def train(args) -> dict:
         if device.type == "cuda":
             torch.cuda.synchronize()
         t0 = time.perf_counter()
+        if batch is None:
+            # nothing to supervise on this rank this step: take part in every
+            # collective with zeros, so the ranks stay matched (the reference
+            # runs a dummy forward/backward, train/trainer.py:103-146)
+            _all_sum(0.0, device)
+            if getattr(args, "trajectory_weight", 0.0) and teacher is not None:
+                _all_sum(0.0, device)
+            lr = cosine_lr(step, args.lr, args.warmup_steps, args.max_steps, args.min_lr_ratio)
+            opt.zero_grad()
+            gnorm = opt.step(args.grad_clip, lr)
+            rec = {"step": step + 1, "loss": _all_sum(0.0, device), "kl": _all_sum(0.0, device),
+                   "ce": _all_sum(0.0, device), "grad_norm": gnorm, "lr": lr,
+                   "tokens": int(_all_sum(0.0, device)), "step_s": time.perf_counter() - t0, "empty_rank": True}
+            log.append(rec)
+            if rank == 0:
+                with open(out_dir / "training_metrics.jsonl", "a") as f:
+                    f.write(json.dumps(rec) + "\n")
+            if args.save_every and (step + 1) % args.save_every == 0:
+                save_checkpoint(student, opt, out_dir, step + 1, cursor)
+            continue
         batch = batch.to(device)
         cache = clean_prefill(student, batch)
         hs = student_hidden(student, batch, cache)

@@ -152,3 +152,50 @@ def test_trainer_checkpoint_roundtrip(tmp_path):
     a.save_final = False
     r2 = train(a)
     assert [x["step"] for x in r2["log"]] == [3]
+
+
+def _empty_rank_worker(rank, port, out_dir):
+    import datetime
+    import json
+    import os
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["RANK"], os.environ["WORLD_SIZE"], os.environ["LOCAL_RANK"] = str(rank), "2", str(rank)
+    from d3d_b200.train.args import parser
+    from d3d_b200.train.trainer import train
+    # rank 1 reads only one-token responses: no anchor, nothing to supervise
+    data = os.path.join(out_dir, "data.jsonl")
+    args = parser().parse_args([
+        "--draft-model", "tiny-drafter", "--target-model", "tiny-target", "--output-dir", out_dir,
+        "--data-path", data, "--max-steps", "2", "--batch-size", "1", "--device", "cpu", "--dtype", "fp32",
+        "--parallel-anchors-per-example", "2", "--vocab-chunk", "256", "--save-every", "2"])
+    out = train(args)
+    with open(os.path.join(out_dir, f"log{rank}.json"), "w") as f:
+        json.dump(out["log"], f)
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def test_rank_with_empty_batches_keeps_collectives_matched(tmp_path):
+    import json
+    import random
+    import socket
+    import torch.multiprocessing as mp
+    rng = random.Random(0)
+    rows = []
+    for i in range(4):
+        resp = [rng.randrange(2, 1000) for _ in range(12)] if i % 2 == 0 else [5]
+        rows.append(json.dumps({"prompt_ids": [rng.randrange(2, 1000) for _ in range(8)], "response_ids": resp}))
+    (tmp_path / "data.jsonl").write_text("\n".join(rows) + "\n")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_empty_rank_worker, args=(port, str(tmp_path)), nprocs=2, join=True)
+    l0 = json.loads((tmp_path / "log0.json").read_text())
+    l1 = json.loads((tmp_path / "log1.json").read_text())
+    assert len(l0) == len(l1) == 2
+    assert all(r.get("empty_rank") for r in l1) and not any(r.get("empty_rank") for r in l0)
+    assert all(a["grad_norm"] == b["grad_norm"] for a, b in zip(l0, l1))
+    assert (tmp_path / "trainer_state.json").exists() or any(tmp_path.glob("**/trainer_state.json"))
