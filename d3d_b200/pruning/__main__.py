@@ -33,6 +33,91 @@ def _eval_examples(cfg, n, block, seed):
     return examples_from_sequences(seqs, block, 2, rng)
 
 
+class DataWindow:
+    """Recovery data: a seeded permutation of a JSONL file's rows read as a
+    sliding window from a cursor (no wrap-around: an exhausted window returns
+    nothing), or fresh synthetic sequences (``pruning/data.py:52-98``)."""
+
+    def __init__(self, path: str, seed: int, vocab: int, seq_len: int = 128):
+        self.synthetic = path == "synthetic"
+        self.vocab, self.seq_len = vocab, seq_len
+        self.rng = random.Random(seed)
+        if not self.synthetic:
+            from ..train.blocks import Example
+            rows = [json.loads(x) for x in Path(path).read_text().splitlines() if x.strip()]
+            perm = list(range(len(rows)))
+            random.Random(seed).shuffle(perm)
+            self.rows = [Example(rows[i]["prompt_ids"], rows[i]["response_ids"]) for i in perm]
+
+    def take(self, start: int, n: int):
+        if self.synthetic:
+            return synthetic_examples(n, self.seq_len, 0.25, self.vocab, random.Random(self.rng.random() + start))
+        return self.rows[start:start + n]
+
+
+def _agree(ok: bool, device) -> bool:
+    """Every rank continues only if every rank has data for this step (MIN
+    all-reduce before any collective of the step; ``pruning/train_recovery.py:157-190``)."""
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        return ok
+    t = torch.tensor([1 if ok else 0], dtype=torch.int64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def _recovery(a) -> list:
+    """Recovery training of a pruned child against its parent: multi-rank
+    under ``torch.distributed.run`` (sharded optimizer), agreed stop when any
+    rank runs out of data, atomic step checkpoints carrying the next data
+    cursor (``pruning/train_recovery.py:39-534``)."""
+    import os
+    from ..train.blocks import build_packed_block_batch
+    from ..train.trainer import _init_dist
+    device = torch.device(a.device)
+    rank, world = _init_dist(device.type)
+    if device.type == "cuda":
+        device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(device)
+    parent = load_model(a.parent, device=device).eval()
+    for q in parent.parameters():
+        q.requires_grad_(False)
+    child = load_model(a.child, device=device)
+    prov = json.loads((Path(a.child) / "layer_prune.json").read_text())
+    child.model.embed_tokens.weight.requires_grad_(False)
+    opt = ShardedAdamW(child.parameters(), lr=a.lr)
+    rng = random.Random(a.seed * 1000 + rank)
+    window = DataWindow(a.data_path, a.seed, min(child.cfg.vocab_size, 151643) - 2)
+    cursor = a.data_cursor
+    out = Path(a.output)
+
+    def save(dst: Path, log):
+        if rank == 0:
+            save_model(child, dst)
+            (dst / "layer_prune.json").write_text(json.dumps(prov, indent=2))
+            write_json(str(dst / "recovery_log.json"), log)
+            write_json(str(dst / "trainer_state.json"), {"next_data_cursor": cursor, "steps": len(log)})
+
+    log = []
+    for step in range(a.steps):
+        exs = window.take(cursor + rank * a.batch_size, a.batch_size)
+        ok = len(exs) > 0 and build_packed_block_batch(exs, block_size=a.block_size, mask_token_id=int(
+            child.cfg.mask_token_id), max_anchors=8, rng=random.Random(0)) is not None
+        if not _agree(ok, device):
+            break
+        cursor += world * a.batch_size
+        rec = recovery_step(child, parent, prov["removed_compact_layer"], list(range(parent.cfg.num_hidden_layers)),
+                            exs, opt, block_size=a.block_size, anchors=8, rng=rng)
+        rec["next_data_cursor"] = cursor
+        log.append(rec)
+        if a.save_every and (step + 1) % a.save_every == 0:
+            save(out.with_name(out.name + f".step{step + 1}"), log)
+    save(out, log)
+    if log and rank == 0:
+        print(json.dumps(log[-1]))
+    return log
+
+
 def main(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("stage", choices=["select", "prune", "train", "choose"])
@@ -49,6 +134,10 @@ def main(argv=None):
     p.add_argument("--lr", type=float, default=1e-5)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
+    p.add_argument("--data-path", default="synthetic", help="train: synthetic or JSONL of prompt_ids/response_ids")
+    p.add_argument("--batch-size", type=int, default=2, help="train: sequences per rank per step")
+    p.add_argument("--data-cursor", type=int, default=0, help="train: first row of the permuted data window")
+    p.add_argument("--save-every", type=int, default=0, help="train: atomic step checkpoints")
     a = p.parse_args(argv)
     if a.stage == "select":
         m = load_model(a.checkpoint, device=a.device).eval()
@@ -61,25 +150,7 @@ def main(argv=None):
     elif a.stage == "prune":
         print(prune_from_selection(a.selection, a.output))
     elif a.stage == "train":
-        parent = load_model(a.parent, device=a.device).eval()
-        for q in parent.parameters():
-            q.requires_grad_(False)
-        child = load_model(a.child, device=a.device)
-        prov = json.loads((Path(a.child) / "layer_prune.json").read_text())
-        child.model.embed_tokens.weight.requires_grad_(False)
-        opt = ShardedAdamW(child.parameters(), lr=a.lr)
-        rng = random.Random(a.seed)
-        vocab = min(child.cfg.vocab_size, 151643) - 2
-        log = []
-        for _ in range(a.steps):
-            exs = synthetic_examples(2, 128, 0.25, vocab, rng)
-            log.append(recovery_step(child, parent, prov["removed_compact_layer"],
-                                     list(range(parent.cfg.num_hidden_layers)), exs, opt,
-                                     block_size=a.block_size, anchors=8, rng=rng))
-        save_model(child, a.output)
-        (Path(a.output) / "layer_prune.json").write_text(json.dumps(prov, indent=2))
-        write_json(str(Path(a.output) / "recovery_log.json"), log)
-        print(json.dumps(log[-1]))
+        _recovery(a)
     else:
         m = load_model(a.checkpoints[0], device="cpu")
         res = choose(a.checkpoints, _eval_examples(m.cfg, a.samples, a.block_size, a.seed), a.block_size, a.device)

@@ -71,7 +71,8 @@ def recovery_step(student: Qwen3LM, teacher: Qwen3LM, removed_original: int, ret
     loss.backward()
     norm = opt.step(grad_clip)
     opt.zero_grad()
-    return {"loss": float(loss), "ar": float(ar), "ce": float(ce), "kl": float(kl), "hidden_mse": float(hmse),
+    return {"loss": float(loss.detach()), "ar": float(ar.detach()), "ce": float(ce.detach()),
+            "kl": float(kl.detach()), "hidden_mse": float(hmse.detach()),
             "grad_norm": norm}
 
 

@@ -86,3 +86,41 @@ def test_choose_checkpoint(tmp_path):
     save_model(b, tmp_path / "step_20")
     res = choose([str(tmp_path / "step_10"), str(tmp_path / "step_20")], _examples(), 8)
     assert res["best"]["checkpoint"].endswith("step_10")   # tie -> earliest step
+
+
+def _recovery_worker(rank, port, root):
+    import os
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["RANK"], os.environ["WORLD_SIZE"], os.environ["LOCAL_RANK"] = str(rank), "2", str(rank)
+    import torch.distributed as dist
+    from d3d_b200.pruning.__main__ import main
+    main(["train", "--parent", f"{root}/parent", "--child", f"{root}/child", "--output", f"{root}/recovered",
+          "--data-path", f"{root}/data.jsonl", "--batch-size", "1", "--steps", "10", "--block-size", "8",
+          "--device", "cpu", "--save-every", "1"])
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def test_distributed_recovery_stops_together_and_records_cursor(tmp_path):
+    """Two gloo ranks: the 5-row window runs out for rank 1 at step 3, both
+    ranks stop there, and the checkpoints carry the next data cursor."""
+    import socket
+    import torch.multiprocessing as mp
+    m = _model()
+    save_model(m, tmp_path / "parent")
+    prune_checkpoint(tmp_path / "parent", tmp_path / "child", removed=1)
+    rng = random.Random(2)
+    rows = [json.dumps({"prompt_ids": [rng.randrange(2, 1000) for _ in range(10)],
+                        "response_ids": [rng.randrange(2, 1000) for _ in range(20)]}) for _ in range(5)]
+    (tmp_path / "data.jsonl").write_text("\n".join(rows) + "\n")
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_recovery_worker, args=(port, str(tmp_path)), nprocs=2, join=True)
+    state = json.loads((tmp_path / "recovered" / "trainer_state.json").read_text())
+    assert state == {"next_data_cursor": 4, "steps": 2}
+    assert json.loads((tmp_path / "recovered.step1" / "trainer_state.json").read_text())["next_data_cursor"] == 2
+    assert load_model(tmp_path / "recovered").cfg.num_hidden_layers == 3
+    assert (tmp_path / "recovered" / "layer_prune.json").exists()
