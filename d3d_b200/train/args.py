@@ -47,6 +47,8 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--margin-top-k", type=int, default=16)
     p.add_argument("--margin-value", type=float, default=1.0)
     p.add_argument("--margin-hinge", action="store_true", help="hinge instead of softplus margin")
+    p.add_argument("--ar-weight", type=float, default=0.0,
+                   help="next-token CE of the student on the clean sequences (fused LM-head loss)")
     p.add_argument("--trajectory-weight", type=float, default=0.0,
                    help="hidden-trajectory (block relation) distillation weight; needs --target-model")
     return p

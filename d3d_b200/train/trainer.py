@@ -172,6 +172,8 @@ def train(args) -> dict:
             # collective with zeros, so the ranks stay matched (the reference
             # runs a dummy forward/backward, train/trainer.py:103-146)
             _all_sum(0.0, device)
+            if getattr(args, "ar_weight", 0.0):
+                _all_sum(0.0, device)
             if getattr(args, "trajectory_weight", 0.0) and teacher is not None:
                 _all_sum(0.0, device)
             lr = cosine_lr(step, args.lr, args.warmup_steps, args.max_steps, args.min_lr_ratio)
@@ -215,6 +217,17 @@ def train(args) -> dict:
                                             margin_weight=args.margin_weight, margin_top_k=args.margin_top_k,
                                             margin_value=args.margin_value, margin_smooth=not args.margin_hinge)
             loss = loss + (w * aux).sum()
+        if getattr(args, "ar_weight", 0.0):
+            # clean autoregressive loss (reference: train/losses.py:380-468), mean over
+            # every rank's valid next-token positions, through the fused LM-head CE
+            hc = student(batch.clean_ids)[:, :-1]
+            pos = torch.arange(hc.shape[1], device=device)[None]
+            valid = pos < (batch.clean_lens[:, None] - 1)
+            n_ar = _all_sum(float(valid.sum()), device)
+            w_ar = torch.full((int(valid.sum()),), args.ar_weight / max(n_ar, 1.0), device=device)
+            ar_loss, _, _ = lmhead_distill_loss(hc[valid], student.lm_weight, None, None,
+                                                batch.clean_ids[:, 1:][valid], None, w_ar, chunk=args.vocab_chunk)
+            loss = loss + ar_loss
         if getattr(args, "trajectory_weight", 0.0) and th_all is not None:
             loss = loss + args.trajectory_weight * _trajectory_term(student, teacher, batch, hs, th_all, device,
                                                                     world)

@@ -48,7 +48,7 @@ def test_trainer_with_aux_and_trajectory(tmp_path):
     args = build_parser().parse_args([
         "--draft-model", "tiny-drafter", "--target-model", "tiny-target", "--output-dir", str(tmp_path),
         "--max-steps", "2", "--batch-size", "2", "--seq-len", "64", "--device", "cpu", "--dtype", "fp32",
-        "--hnce-weight", "0.5", "--margin-weight", "0.5", "--trajectory-weight", "1.0",
+        "--hnce-weight", "0.5", "--margin-weight", "0.5", "--trajectory-weight", "1.0", "--ar-weight", "0.5",
         "--parallel-anchors-per-example", "4", "--vocab-chunk", "256"])
     out = train(args)
     assert len(out["log"]) == 2 and all(math.isfinite(r["loss"]) for r in out["log"])
