@@ -32,6 +32,8 @@ def parser():
     p.add_argument("--anchor-num", type=int, default=1)
     p.add_argument("--draft-microbatch", type=int, default=4)
     p.add_argument("--ignore-eos", action="store_true")
+    p.add_argument("--backup", choices=["neural", "fast"], default="neural",
+                   help="on a branch miss: redraft (neural) or verify a random block at once (fast)")
     p.add_argument("--validate", action="store_true", help="check token identity against AR decoding")
     p.add_argument("--baseline", action="store_true", help="AR baseline at each concurrency")
     p.add_argument("--controlled-accept-mean", type=float, default=None)
@@ -53,7 +55,7 @@ def main(argv=None):
     check_paged_capacity([len(p) for p in prompts], a.max_new_tokens, conc, a.pages, a.page_size,
                          a.block_size, a.anchor_num)
     decode = DecodeConfig(block_size=a.block_size, anchor_num=a.anchor_num, max_new_tokens=a.max_new_tokens,
-                          draft_microbatch=a.draft_microbatch, ignore_eos=a.ignore_eos)
+                          draft_microbatch=a.draft_microbatch, ignore_eos=a.ignore_eos, backup=a.backup)
     eng = build_engine(a, decode, max_seqs=max(conc), max_context=max(len(p) for p in prompts) + a.max_new_tokens + 64,
                        pages=a.pages)
     ar = None

@@ -50,6 +50,8 @@ class DecodeConfig:
     eos: Tuple[int, ...] = EOS_DEFAULT
     packed_accepted_counts: Optional[Tuple[int, ...]] = None
     use_cond: bool = True     # feed target hidden to a conditioned drafter
+    backup: str = "neural"    # on a branch miss: "neural" redraft, or "fast" random block (greedy only)
+    backup_seed: int = 42
 
     def validate(self):
         if self.block_size <= 1:
@@ -58,6 +60,10 @@ class DecodeConfig:
             raise ValueError("--anchor-num must be non-negative")
         if not is_greedy(self.temperature) and self.top_k <= 0:
             raise ValueError("temperature > 0 async sampling requires --proposal-top-k > 0")
+        if self.backup not in ("neural", "fast"):
+            raise ValueError("--backup must be neural or fast")
+        if self.backup == "fast" and not is_greedy(self.temperature):
+            raise ValueError("the fast backup (random block on a miss) is greedy only")
         return self
 
 
@@ -173,6 +179,47 @@ class SpecDecoder:
                 s.recoveries += 1
                 s.source = "redraft"
 
+    def fast_backup(self, seqs: List[SeqState]) -> None:
+        """On a miss, verify ``[anchor, random x K-1]`` at once instead of
+        redrafting on the critical path: greedy verification needs token ids
+        only, and commits at least the anchor.  The drafter's view of the
+        anchor (its top tokens, for the next step's branches) is computed in
+        the next :meth:`predict`, off the critical path
+        (``serving/engine.py:64-92``, ``backup="fast"``)."""
+        k = self.cfg.block_size
+        if not hasattr(self, "_backup_gen"):
+            self._backup_gen = torch.Generator().manual_seed(int(self.cfg.backup_seed))
+        for s in seqs:
+            blk = torch.randint(int(self.d.vocab_size), (k,), generator=self._backup_gen)
+            blk[0] = s.anchor
+            s.current, s.top = blk, None
+            s.extra["needs_seed"] = True
+            s.extra["fast_backups"] = s.extra.get("fast_backups", 0) + 1
+            s.source = "fast_backup"
+
+    def _seed_tops(self, seqs: List[SeqState]) -> None:
+        """The drafter's top tokens after each fast-backup anchor (``[anchor,
+        MASK x K-1]`` rows, KV not stored), without touching the random block
+        being verified."""
+        k, a = self.cfg.block_size, self.cfg.anchor_num
+        for off in range(0, len(seqs), self.cfg.draft_microbatch):
+            group = seqs[off:off + self.cfg.draft_microbatch]
+            b = len(group)
+            ids = torch.full((b, k), self.d.mask_id, dtype=torch.long)
+            ids[:, 0] = torch.tensor([s.anchor for s in group])
+            pos = torch.stack([torch.arange(s.prefix, s.prefix + k) for s in group])
+            rows = torch.stack([full_rows(s.prefix + k, k) for s in group])
+            out = self.d.forward(group, ids, pos, rows, store=False, topk=a + 1 if a else 0,
+                                 cond_rows=self._cond_rows(b, k, [0]))
+            for i, s in enumerate(group):
+                top = out["top"][i].clone().cpu() if "top" in out else None
+                if top is not None and s.controlled is not None:
+                    seed = out["greedy"][i].clone().cpu()
+                    seed[0] = s.anchor
+                    self._controlled(s, seed, top, s.prefix)
+                s.top = top
+                s.extra["needs_seed"] = False
+
     # ------------------------------------------------------ packed outcomes
     def _pipelined(self) -> bool:
         """Whether the next verify may be enqueued behind a drafter forward still
@@ -190,6 +237,9 @@ class SpecDecoder:
         ``wait=False`` (asynchronous drafter backends) the forwards are only
         enqueued; each outcome resolves when first read."""
         k, a = self.cfg.block_size, self.cfg.anchor_num
+        seeds = [s for s in seqs if s.extra.get("needs_seed")]
+        if seeds:
+            self._seed_tops(seeds)
         results: Dict[int, _Outcomes] = {}
         for off in range(0, len(seqs), self.cfg.draft_microbatch):
             group = seqs[off:off + self.cfg.draft_microbatch]
@@ -367,7 +417,10 @@ class SpecDecoder:
             running = remaining
             miss_rounds += bool(recover)
             with self.prof.phase("recover"):
-                self.recover(recover)
+                if cfg.backup == "fast":
+                    self.fast_backup(recover)
+                else:
+                    self.recover(recover)
             if on_step is not None:
                 on_step(steps)
         elapsed = time.perf_counter() - started

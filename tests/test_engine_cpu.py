@@ -256,3 +256,24 @@ def test_gemm_policies():
     # the drafter cap keeps fp32 partials no larger than the weight
     s = ops.splitk_for(2048, 2048, mtiles=1, bt=288, m=272)
     assert s * 272 * 2048 * 4 <= 2048 * 2048 * 2 * 2
+
+
+def test_fast_backup_on_misses_keeps_token_identity():
+    """backup="fast": a miss verifies [anchor, random...] immediately (no
+    redraft) and seeds the next step's branches off the critical path;
+    greedy output still equals AR."""
+    from d3d_b200.config import tiny_drafter, tiny_target
+    from d3d_b200.engine.backends import TorchDraft, TorchTarget
+    from d3d_b200.engine.spec import DecodeConfig, SpecDecoder, ar_generate
+    from d3d_b200.models.qwen3 import build_model
+    rng = random.Random(12)
+    prompts = [[rng.randrange(2, 1000) for _ in range(rng.randint(12, 30))] for _ in range(3)]
+    tgt = TorchTarget(build_model(tiny_target(), seed=0))
+    drf = TorchDraft(build_model(tiny_drafter(cond=True), seed=1))
+    cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=40, ignore_eos=True, backup="fast")
+    res = SpecDecoder(tgt, drf, cfg).generate(prompts, concurrency=2)
+    ar = ar_generate(tgt, prompts, 40, ignore_eos=True)["outputs"]
+    assert [o.tokens for o in res["outputs"]] == ar
+    assert any("fast_backup" in o.sources for o in res["outputs"])
+    with pytest.raises(ValueError):
+        DecodeConfig(backup="fast", temperature=0.7, top_k=2).validate()
