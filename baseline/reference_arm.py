@@ -103,7 +103,7 @@ def run(args, rank, world, local):
     import single.eval_sync as es
 
     sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
-    from bench import ClockSampler, barrier, dist_max, dist_sum, make_prompts, METRIC
+    from bench import BASELINE_NOTE, ClockSampler, barrier, dist_max, dist_sum, make_prompts, METRIC
     from d3d_b200.engine.controlled import ControlledAcceptance, rate_for_mean_accept
 
     dev = f"cuda:{local}"
@@ -254,7 +254,7 @@ def run(args, rank, world, local):
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * dev_max / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": round(value / BASELINE_TPS, 4), "dtype": "bf16",
+        "vs_baseline": round(value / BASELINE_TPS, 4), "vs_baseline_note": BASELINE_NOTE, "dtype": "bf16",
         "data": "synthetic seeded random-token prompts, random-init weights, acceptance-controlled drafts",
         "config": {"model": "Qwen3-8B-layout target + D3D-1.7B-layout drafter (reference classes)",
                    "global_batch": world // 2 if pairs else world,
@@ -268,8 +268,12 @@ def run(args, rank, world, local):
                    "attn_implementation": attn, "oracle": "greedy continuation from 16-token verifies",
                    "step": "one request, prefill through last token"},
         "ar_tokens_per_s": round(ar_value, 2) if ar_value else None,
+        "ar_timing": "host perf_counter around each request's one-token verify loop (the reference's "
+                     "run_ar_baseline is synchronous per token), after a synchronize",
         "speedup_vs_ar": round(value / ar_value, 3) if ar_value else None,
         "token_identical_to_ar": bool(dist_sum(1.0 if ident else 0.0) == world),
+        "token_identical_note": "the reference's outputs against its own greedy continuation from 16-token "
+                                "verifies (its kernels are not batch-invariant, so one-token AR can differ)",
         "clocks": clk.summary(),
     }
 

@@ -1,6 +1,10 @@
 """Kernel microbenchmarks at the decode shapes of the headline configuration.
 
     python -m d3d_b200.benchmarks.kernels [--only gemm,attn,forward] [--iters N]
+    python -m d3d_b200.benchmarks.kernels --only forward_eager [--drafter] [--layers N]
+
+``forward_eager`` runs one untimed eager forward after one warm-up forward:
+the small, few-launch case that profiler captures of single kernels use.
 
 Times each sm_100a kernel with CUDA events on its launching stream after
 warm-up, cycling over enough distinct weight copies that the working set is
@@ -229,6 +233,45 @@ def bench_forward(iters, peaks, rows, layers=36, drafter=False):
                          hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3)))
 
 
+def forward_eager(layers, drafter, context=1000):
+    """One warm-up forward then one eager forward of the target's verify
+    (M=16) or the drafter's packed all-outcome forward (M=272); nothing is
+    timed.  Launch ``k`` of kernel family ``f`` in the second forward is
+    launch ``layers + k`` of ``f`` overall, which is what ``ncu -s`` skips."""
+    from d3d_b200 import config as C
+    from d3d_b200.engine.layout import branch_specs, causal_rows, packed_layout
+    from d3d_b200.models.fast import FastRunner, FastWeights, PagedKV
+    cfg = (C.d3d_1p7b() if drafter else C.qwen3_8b()).replace(num_hidden_layers=layers)
+    w = FastWeights.random(cfg, seed=0)
+    L = context
+    pages = (L + 1024) // 16 + 8
+    kv = PagedKV(cfg, num_pages=pages, page_size=16, max_seqs=1, max_pages_per_seq=pages)
+    kv.reserve(0, 0, L + 900)
+    r = FastRunner(w, kv, max_context=L + 900, batch_invariant=not drafter)
+    if drafter:
+        blk = torch.randint(0, 1000, (16,))
+        lay = packed_layout(blk, branch_specs(blk.tolist(), torch.stack([blk, blk + 1], 1).tolist(), 1),
+                            L, 16, 151669, "causal")
+        b = r.buffers(1, lay.q_len, 2)
+        b.ids.copy_(lay.input_ids)
+        b.pos.copy_(lay.positions)
+        b.rows.copy_(lay.rows)
+        m = lay.q_len
+    else:
+        m = 16
+        b = r.buffers(1, m, 1)
+        b.pos.copy_(torch.arange(L, L + m))
+        b.rows.copy_(causal_rows(L, m))
+    b.kv_end.fill_(L + m)
+    b.slots.copy_(torch.arange(L, L + m))
+    r.forward(b)
+    torch.cuda.synchronize()
+    n = r.forward(b)
+    torch.cuda.synchronize()
+    print(json.dumps(dict(kernel="forward (eager, untimed)", drafter=drafter, layers=layers, M=m,
+                          launches=n, status=int(b.status.item()))))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,lmhead,attn,forward")
@@ -259,6 +302,8 @@ def main():
         bench_attn(a.iters, peaks, rows)
     if "gemm_sweep" in only:
         bench_gemm_sweep(a.sweep_m, a.iters, peaks, rows)
+    if "forward_eager" in only:
+        forward_eager(a.layers, a.drafter)
     if "forward" in only:
         bench_forward(a.iters, peaks, rows, layers=a.layers if not a.drafter else min(a.layers, 28),
                       drafter=a.drafter)

@@ -94,15 +94,23 @@ def load():
     return mod
 
 
-def load_debug():
-    """The debug build (bounds-checked kernels), built on first use into
-    ``_build_debug`` whatever ``D3D_DEBUG`` says; returns the module."""
+def build_debug():
+    """Compile the debug build (bounds-checked kernels) into ``_build_debug``
+    in a child process (the build variant is chosen at import time)."""
     import subprocess
+    env = dict(os.environ, D3D_DEBUG="1")
+    subprocess.run([sys.executable, "-c", "from d3d_b200.ops import build; build.build()"], env=env,
+                   check=True, cwd=str(HERE.parents[1]))
+
+
+def load_debug():
+    """The debug build (bounds-checked kernels), built on first use (or when
+    older than its sources) into ``_build_debug`` whatever ``D3D_DEBUG``
+    says; returns the module."""
     path = HERE / "_build_debug" / "d3d_b200_C_debug.so"
-    if not path.exists():
-        env = dict(os.environ, D3D_DEBUG="1")
-        subprocess.run([sys.executable, "-c", "from d3d_b200.ops import build; build.build()"], env=env,
-                       check=True, cwd=str(HERE.parents[1]))
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh"))
+    if not path.exists() or any(p.exists() and p.stat().st_mtime > path.stat().st_mtime + 1.0 for p in deps):
+        build_debug()
     name = "d3d_b200_C_debug"
     loader = importlib.machinery.ExtensionFileLoader(name, str(path))
     spec = importlib.util.spec_from_file_location(name, str(path), loader=loader)

@@ -21,6 +21,7 @@
 // per-row arithmetic do not depend on how many queries share a launch, a
 // row's output is bit-identical whether it is verified in a block of 16 or
 // decoded alone — required for greedy token identity with AR decoding.
+#include <atomic>
 #include <stdexcept>
 #include <string>
 
@@ -385,32 +386,49 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 }
 
 template <int D>
-static void launch_attn_split(const AttnArgs& a, cudaStream_t st) {
-  constexpr int LD = D + 8;
-  const size_t smem = static_cast<size_t>(AT_ROWS + 2 * AT_KEYS) * LD * 2;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    attr = true;
-  }
-  const int g = a.Hq / a.Hkv;
-  dim3 grid((a.q_len * g + AT_ROWS - 1) / AT_ROWS, a.B * a.Hkv, a.n_chunks);
-  launch_pdl(attn_kernel<D>, grid, dim3(128), smem, st, a);
-  if (a.n_chunks > 1) {
-    const int warps = a.B * a.q_len * a.Hq;
-    launch_pdl(attn_combine_kernel<D>, dim3((warps + 7) / 8), dim3(256), 0, st, a);
-  }
+constexpr size_t attn_split_smem() {
+  return static_cast<size_t>(AT_ROWS + 2 * AT_KEYS) * (D + 8) * 2;
 }
 
-// Split-KV attention with fp32 partials and a combine kernel (used by the
-// allocation-free entry point, which supplies the partial buffers itself).
-void attention_split(const AttnArgs& a, cudaStream_t st) {
-  if (a.B == 0 || a.q_len == 0) return;
+// The dynamic shared-memory limit is a per-device property of a kernel: it
+// is raised once on every device (bit ``dev`` of a per-kernel atomic mask;
+// two threads racing on the first call both set the same value).
+template <int D>
+static cudaError_t ensure_attn_split_attr() {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(attn_split_smem<D>()));
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
+
+template <int D>
+static cudaError_t launch_attn_split(const AttnArgs& a, cudaStream_t st) {
+  cudaError_t e = ensure_attn_split_attr<D>();
+  if (e != cudaSuccess) return e;
+  const int g = a.Hq / a.Hkv;
+  dim3 grid((a.q_len * g + AT_ROWS - 1) / AT_ROWS, a.B * a.Hkv, a.n_chunks);
+  e = launch_pdl(attn_kernel<D>, grid, dim3(128), attn_split_smem<D>(), st, a);
+  if (e != cudaSuccess || a.n_chunks <= 1) return e;
+  const int warps = a.B * a.q_len * a.Hq;
+  return launch_pdl(attn_combine_kernel<D>, dim3((warps + 7) / 8), dim3(256), 0, st, a);
+}
+
+// Split-KV attention with fp32 partials and a combine kernel.  Returns the
+// status of its own launches (not a sticky error of earlier, unrelated work).
+cudaError_t attention_split(const AttnArgs& a, cudaStream_t st) {
+  if (a.B == 0 || a.q_len == 0) return cudaSuccess;
+  if (a.n_chunks > MAX_CHUNKS) return cudaErrorInvalidValue;
   switch (a.head_dim) {
-    case 32: launch_attn_split<32>(a, st); break;
-    case 64: launch_attn_split<64>(a, st); break;
-    case 128: launch_attn_split<128>(a, st); break;
-    default: break;
+    case 32: return launch_attn_split<32>(a, st);
+    case 64: return launch_attn_split<64>(a, st);
+    case 128: return launch_attn_split<128>(a, st);
+    default: return cudaErrorInvalidValue;
   }
 }
 
@@ -836,7 +854,8 @@ void attention(const AttnArgs& a, cudaStream_t st) {
   }();
   const bool one_tile = a.q_len * (a.Hq / a.Hkv) <= AT_ROWS;
   if ((force_split || (!one_tile && !a.invariant)) && (a.n_chunks == 1 || (a.part_o && a.part_ml))) {
-    attention_split(a, st);
+    const cudaError_t e = attention_split(a, st);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("attention (split-KV): ") + cudaGetErrorString(e));
     return;
   }
   if (AT_KEYS % a.page_size != 0) throw std::runtime_error("attention: page size must divide 64");
@@ -863,6 +882,8 @@ void attention(const AttnArgs& a, cudaStream_t st) {
 
 #include "attention_noalloc.h"
 
+static_assert(D3D_ATTN_NOALLOC_MAX_CHUNKS == d3d::MAX_CHUNKS, "combine kernel chunk limit");
+
 namespace {
 
 static __device__ __align__(256) unsigned char g_attn_scratch[D3D_ATTN_NOALLOC_SCRATCH_BYTES];
@@ -872,7 +893,8 @@ std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of g_attn_scratch on the current device, looked up once per
-// device (host code only sees a host-side stand-in for the symbol).
+// device (host code only sees a host-side stand-in for the symbol).  The
+// kernels' shared-memory limit is raised per device by the launch path.
 cudaError_t scratch_for_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -883,18 +905,6 @@ cudaError_t scratch_for_current_device(void** out) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_attn_scratch);
     if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
-    const size_t smem128 = static_cast<size_t>(d3d::AT_ROWS + 2 * d3d::AT_KEYS) * (128 + 8) * 2;
-    const size_t smem64 = static_cast<size_t>(d3d::AT_ROWS + 2 * d3d::AT_KEYS) * (64 + 8) * 2;
-    const size_t smem32 = static_cast<size_t>(d3d::AT_ROWS + 2 * d3d::AT_KEYS) * (32 + 8) * 2;
-    if ((e = cudaFuncSetAttribute(d3d::attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(smem128))) != cudaSuccess)
-      return e;
-    if ((e = cudaFuncSetAttribute(d3d::attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(smem64))) != cudaSuccess)
-      return e;
-    if ((e = cudaFuncSetAttribute(d3d::attn_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(smem32))) != cudaSuccess)
-      return e;
     g_scratch_addr[dev] = p;
   }
   *out = g_scratch_addr[dev];
@@ -903,15 +913,21 @@ cudaError_t scratch_for_current_device(void** out) {
 
 }  // namespace
 
-extern "C" int d3d_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
-                                     int bt_stride, const int* rows, const int* kv_end, int B, int q_len, int Hq,
-                                     int Hkv, int head_dim, int page_size, float scale, int chunk, int n_chunks,
-                                     void* out, cudaStream_t stream) {
+extern "C" int d3d_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, long long num_slots,
+                                     const int* block_table, int bt_stride, const int* rows, const int* kv_end, int B,
+                                     int q_len, int Hq, int Hkv, int head_dim, int page_size, float scale, int chunk,
+                                     int n_chunks, void* out, cudaStream_t stream) {
   if (!q || !k_cache || !v_cache || !block_table || !rows || !kv_end || !out) return D3D_NOALLOC_ERR_BAD_ARG;
-  if (B <= 0 || q_len <= 0 || Hkv <= 0 || Hq % Hkv != 0 || page_size <= 0 || bt_stride <= 0 || n_chunks < 1)
+  if (B <= 0 || q_len <= 0 || Hkv <= 0 || Hq % Hkv != 0 || bt_stride <= 0 || num_slots <= 0)
     return D3D_NOALLOC_ERR_BAD_ARG;
   if (head_dim != 32 && head_dim != 64 && head_dim != 128) return D3D_NOALLOC_ERR_BAD_ARG;
-  if (chunk <= 0 || chunk % 64 != 0 || chunk / page_size + 1 > d3d::AT_MAX_PAGES) return D3D_NOALLOC_ERR_BAD_ARG;
+  // a 64-key tile spans whole pages, and a chunk spans whole tiles
+  if (page_size <= 0 || d3d::AT_KEYS % page_size != 0) return D3D_NOALLOC_ERR_BAD_ARG;
+  if (chunk <= 0 || chunk % d3d::AT_KEYS != 0 || chunk % page_size != 0 ||
+      chunk / page_size + 1 > d3d::AT_MAX_PAGES)
+    return D3D_NOALLOC_ERR_BAD_ARG;
+  // the combine kernel merges at most D3D_ATTN_NOALLOC_MAX_CHUNKS chunks
+  if (n_chunks < 1 || n_chunks > D3D_ATTN_NOALLOC_MAX_CHUNKS) return D3D_NOALLOC_ERR_BAD_ARG;
   const size_t T = static_cast<size_t>(B) * q_len;
   const size_t part_o = n_chunks > 1 ? static_cast<size_t>(n_chunks) * T * Hq * head_dim : 0;
   const size_t part_ml = n_chunks > 1 ? static_cast<size_t>(n_chunks) * T * Hq * 2 : 0;
@@ -939,6 +955,7 @@ extern "C" int d3d_attention_noalloc(const void* q, const void* k_cache, const v
   a.part_o = n_chunks > 1 ? static_cast<float*>(base) : nullptr;
   a.part_ml = n_chunks > 1 ? static_cast<float*>(base) + part_o : nullptr;
   a.out = static_cast<__nv_bfloat16*>(out);
-  d3d::attention_split(a, stream);
-  return static_cast<int>(cudaPeekAtLastError());
+  a.num_slots = num_slots;
+  a.status = nullptr;
+  return static_cast<int>(d3d::attention_split(a, stream));
 }

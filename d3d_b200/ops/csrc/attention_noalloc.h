@@ -31,13 +31,23 @@
 //   * No cudaMalloc, cudaFree or other allocating routine is called.
 //
 // Arguments mirror the allocating binding: q [B*q_len, Hq, D] bf16,
-// k_cache / v_cache [slots, Hkv, D] bf16, block_table [B, bt_stride] int32,
-// rows [B*q_len, 3] int32 (lim, lo, hi), kv_end [B] int32, out like q.
-// Returns 0 on success, a D3D_NOALLOC_ERR_* code, or a cudaError_t value.
+// k_cache / v_cache [num_slots, Hkv, D] bf16, block_table [B, bt_stride]
+// int32, rows [B*q_len, 3] int32 (lim, lo, hi), kv_end [B] int32, out like q.
+// Shape rules (violations return D3D_NOALLOC_ERR_BAD_ARG, nothing launched):
+//   * page_size divides 64 (a 64-key tile spans whole pages); chunk is a
+//     multiple of 64 and of page_size;
+//   * 1 <= n_chunks <= D3D_ATTN_NOALLOC_MAX_CHUNKS.
+// The caller's duty, not checked: n_chunks * chunk >= kv_end[b] for every
+// sequence b.  Chunk c covers keys [c*chunk, (c+1)*chunk); keys at or beyond
+// n_chunks * chunk are not attended to.
+// Returns 0 on success, a D3D_NOALLOC_ERR_* code, or the cudaError_t of this
+// call's own kernel launches (errors of earlier, unrelated work are not
+// reported here).
 #pragma once
 #include <cuda_runtime.h>
 
 #define D3D_ATTN_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define D3D_ATTN_NOALLOC_MAX_CHUNKS 512
 
 #define D3D_NOALLOC_ERR_TOO_LARGE 1001
 #define D3D_NOALLOC_ERR_BAD_ARG 1002
@@ -48,9 +58,9 @@ extern "C" {
 #endif
 
 __attribute__((visibility("default"))) int d3d_attention_noalloc(
-    const void* q, const void* k_cache, const void* v_cache, const int* block_table, int bt_stride,
-    const int* rows, const int* kv_end, int B, int q_len, int Hq, int Hkv, int head_dim, int page_size,
-    float scale, int chunk, int n_chunks, void* out, cudaStream_t stream);
+    const void* q, const void* k_cache, const void* v_cache, long long num_slots, const int* block_table,
+    int bt_stride, const int* rows, const int* kv_end, int B, int q_len, int Hq, int Hkv, int head_dim,
+    int page_size, float scale, int chunk, int n_chunks, void* out, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -213,7 +213,7 @@ void greedy_accept(Tensor blocks, Tensor post, Tensor commit, Tensor corr, c10::
 void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor rows, Tensor kv_end,
                int64_t B, int64_t q_len, int64_t Hq, int64_t Hkv, int64_t page_size, double scale, int64_t chunk,
                int64_t n_chunks, c10::optional<Tensor> part_o, c10::optional<Tensor> part_ml, Tensor out,
-               bool invariant, c10::optional<Tensor> status) {
+               bool invariant, c10::optional<Tensor> status, bool force_split) {
   const c10::cuda::CUDAGuard g(q.device());
   CHECK_CONTIG(q);
   CHECK_CONTIG(out);
@@ -223,6 +223,8 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
   TORCH_CHECK(chunk % 64 == 0, "attention chunk must be a multiple of 64");
   TORCH_CHECK(chunk / page_size + 1 <= 1024, "attention chunk spans too many pages");
   TORCH_CHECK(n_chunks == 1 || (part_o && part_ml), "split attention needs partial buffers");
+  TORCH_CHECK(n_chunks >= 1 && n_chunks <= 512, "attention: 1 <= n_chunks <= 512 (the combine kernel's limit)");
+  TORCH_CHECK(64 % page_size == 0, "attention: page size must divide 64");
   d3d::AttnArgs a{};
   a.q = cbf(q);
   a.k_cache = cbf(k_cache);
@@ -246,6 +248,11 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
   a.out = bf(out);
   a.num_slots = k_cache.size(0);
   a.status = status_ptr(status);
+  if (force_split) {
+    const cudaError_t e = d3d::attention_split(a, cur_stream());
+    TORCH_CHECK(e == cudaSuccess, "attention (split-KV): ", cudaGetErrorString(e));
+    return;
+  }
   d3d::attention(a, cur_stream());
 }
 
@@ -544,7 +551,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention", &attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
         py::arg("rows"), py::arg("kv_end"), py::arg("B"), py::arg("q_len"), py::arg("Hq"), py::arg("Hkv"),
         py::arg("page_size"), py::arg("scale"), py::arg("chunk"), py::arg("n_chunks"), py::arg("part_o"),
-        py::arg("part_ml"), py::arg("out"), py::arg("invariant") = false, py::arg("status") = py::none());
+        py::arg("part_ml"), py::arg("out"), py::arg("invariant") = false, py::arg("status") = py::none(),
+        py::arg("force_split") = false);
   m.def("gemm_stages", &d3d::gemm_stages);
   m.def("kl_ce_stats", &kl_ce_stats);
   m.def("kl_ce_grad", &kl_ce_grad);

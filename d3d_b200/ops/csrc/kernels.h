@@ -58,7 +58,7 @@ struct AttnArgs {
   int* status;              // error word (debug bounds checks; may be null)
 };
 void attention(const AttnArgs& a, cudaStream_t st);        // cluster kernel (no partial buffers)
-void attention_split(const AttnArgs& a, cudaStream_t st);  // split-KV + combine (uses part_o / part_ml)
+cudaError_t attention_split(const AttnArgs& a, cudaStream_t st);  // split-KV + combine (uses part_o / part_ml)
 
 // ---- training kernels (train_kernels.cu)
 void kl_ce_stats(const float* zt, const float* zs, int N, int C, int ldz, int v0, const int64_t* target, float* st,
