@@ -163,6 +163,8 @@ def bench_attn(iters, peaks, rows):
     for name, hq, hkv, prefix, q, chunk in (("verify 8B", 32, 8, 1000, 16, 64),
                                            ("ar 8B", 32, 8, 1000, 1, 64),
                                            ("verify 8B c128", 32, 8, 1000, 16, 128),
+                                           ("verify 8B c256", 32, 8, 1000, 16, 256),
+                                           ("ar 8B c256", 32, 8, 1000, 1, 256),
                                            ("packed 1.7B A1", 16, 8, 1000, 272, 256),
                                            ("packed 1.7B A3", 16, 8, 1000, 752, 256)):
         d = 128

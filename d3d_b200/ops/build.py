@@ -22,7 +22,7 @@ DEBUG = os.environ.get("D3D_DEBUG") == "1"
 BUILD_DIR = HERE / ("_build_debug" if DEBUG else "_build")
 NAME = "d3d_b200_C_debug" if DEBUG else "d3d_b200_C"
 
-SOURCES = ["bindings.cpp", "gemm_tcgen05.cu", "fused.cu", "attention.cu", "handoff.cu",
+SOURCES = ["bindings.cpp", "gemm_tcgen05.cu", "fused.cu", "attention.cu", "attention_tc.cu", "handoff.cu",
            "train_kernels.cu", "tp.cu", "fsdp.cu"]
 
 CUDA_FLAGS = [

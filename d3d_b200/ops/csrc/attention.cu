@@ -419,6 +419,19 @@ static cudaError_t launch_attn_split(const AttnArgs& a, cudaStream_t st) {
   return launch_pdl(attn_combine_kernel<D>, dim3((warps + 7) / 8), dim3(256), 0, st, a);
 }
 
+cudaError_t attention_combine(const AttnArgs& a, cudaStream_t st) {
+  if (a.n_chunks <= 1) return cudaSuccess;
+  if (a.n_chunks > MAX_CHUNKS) return cudaErrorInvalidValue;
+  const int warps = a.B * a.q_len * a.Hq;
+  const dim3 grid((warps + 7) / 8);
+  switch (a.head_dim) {
+    case 32: return launch_pdl(attn_combine_kernel<32>, grid, dim3(256), 0, st, a);
+    case 64: return launch_pdl(attn_combine_kernel<64>, grid, dim3(256), 0, st, a);
+    case 128: return launch_pdl(attn_combine_kernel<128>, grid, dim3(256), 0, st, a);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 // Split-KV attention with fp32 partials and a combine kernel.  Returns the
 // status of its own launches (not a sticky error of earlier, unrelated work).
 cudaError_t attention_split(const AttnArgs& a, cudaStream_t st) {
@@ -848,6 +861,13 @@ static void launch_attn_cluster_nt(const AttnArgs& a, cudaStream_t st) {
 // buffers are given.
 void attention(const AttnArgs& a, cudaStream_t st) {
   if (a.B == 0 || a.q_len == 0) return;
+  // the tcgen05/TMEM kernel serves every shape it supports (head_dim 64/128,
+  // GQA group dividing 128, whole-tile pages); the mma.sync kernels below
+  // remain for the others (e.g. head_dim 32 test models)
+  if (attention_tc_supported(a)) {
+    attention_tc(a, st);
+    return;
+  }
   static const bool force_split = [] {
     const char* e = std::getenv("D3D_ATTN_PATH");
     return e && std::string(e) == "split";

@@ -256,6 +256,22 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
   d3d::attention(a, cur_stream());
 }
 
+// Whether d3d::attention takes the tcgen05/TMEM kernel for this shape.
+bool attention_uses_tc(int64_t Hq, int64_t Hkv, int64_t head_dim, int64_t page_size, int64_t chunk,
+                       int64_t n_chunks) {
+  d3d::AttnArgs a{};
+  a.Hq = static_cast<int>(Hq);
+  a.Hkv = static_cast<int>(Hkv);
+  a.head_dim = static_cast<int>(head_dim);
+  a.page_size = static_cast<int>(page_size);
+  a.chunk = static_cast<int>(chunk);
+  a.n_chunks = static_cast<int>(n_chunks);
+  float dummy = 0.f;
+  a.part_o = a.part_ml = &dummy;
+  a.num_slots = 1;
+  return d3d::attention_tc_supported(a);
+}
+
 template <typename T>
 T* opt_ptr(const c10::optional<Tensor>& t) {
   return t ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
@@ -548,6 +564,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out"), py::arg("status") = py::none());
   m.def("topk_merge", &topk_merge);
   m.def("greedy_accept", &greedy_accept);
+  m.def("attention_uses_tc", &attention_uses_tc);
   m.def("attention", &attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
         py::arg("rows"), py::arg("kv_end"), py::arg("B"), py::arg("q_len"), py::arg("Hq"), py::arg("Hkv"),
         py::arg("page_size"), py::arg("scale"), py::arg("chunk"), py::arg("n_chunks"), py::arg("part_o"),

@@ -66,5 +66,9 @@ int gemm_ctas_per_sm(int bt);
 size_t gemm_smem_bytes(int bt, int stages);
 void make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_elems,
                        uint32_t box_inner, uint32_t box_outer);
+// 3-D bf16 tensor map with 128-byte swizzle: dims {d0, d1, d2} (d0 contiguous),
+// strides of d1 and d2 in elements, box {b0, b1, b2} (b0 * 2 bytes <= 128).
+void make_tmap_bf16_3d(CUtensorMap* tm, const void* base, const uint64_t dims[3], const uint64_t strides_elems[2],
+                       const uint32_t box[3]);
 
 }  // namespace d3d

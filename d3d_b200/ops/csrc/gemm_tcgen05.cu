@@ -471,6 +471,23 @@ void make_tmap_bf16_2d(CUtensorMap* tm, const void* base, uint64_t inner, uint64
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
 }
 
+void make_tmap_bf16_3d(CUtensorMap* tm, const void* base, const uint64_t dims[3], const uint64_t strides_elems[2],
+                       const uint32_t box[3]) {
+  init_encode();
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
+  for (int i = 0; i < 2; ++i)
+    if ((strides_elems[i] * 2) % 16 != 0) throw std::runtime_error("TMA strides must be multiples of 16 bytes");
+  if (box[0] * 2 > 128) throw std::runtime_error("TMA box row exceeds the 128-byte swizzle span");
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides_elems[0] * 2, strides_elems[1] * 2};
+  cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, st, bx, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3d) failed: " + std::to_string(int(r)));
+}
+
 // Pipeline depth.  Measured on B200: two co-resident CTAs per SM (~110 KB of
 // shared memory each) stream weights at 85-92% of HBM bandwidth where one CTA
 // with a 12-stage pipeline reaches ~50%, so small token tiles use the 110 KB

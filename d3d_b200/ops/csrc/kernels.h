@@ -59,6 +59,9 @@ struct AttnArgs {
 };
 void attention(const AttnArgs& a, cudaStream_t st);        // cluster kernel (no partial buffers)
 cudaError_t attention_split(const AttnArgs& a, cudaStream_t st);  // split-KV + combine (uses part_o / part_ml)
+cudaError_t attention_combine(const AttnArgs& a, cudaStream_t st);  // merge part_o / part_ml chunks into out
+bool attention_tc_supported(const AttnArgs& a);              // shapes the tcgen05 kernel serves
+void attention_tc(const AttnArgs& a, cudaStream_t st);       // tcgen05/TMEM kernel (+ combine when split)
 
 // ---- training kernels (train_kernels.cu)
 void kl_ce_stats(const float* zt, const float* zs, int N, int C, int ldz, int v0, const int64_t* target, float* st,
