@@ -2,6 +2,7 @@
 progressive pruning (reference: ``scripts/prune.sh``).
 
     select  --checkpoint DIR --output selection.json [--drop 1]
+            (data-parallel under torch.distributed.run: one process per device)
     prune   --selection selection.json --output DIR
     train   --parent DIR --child DIR --output DIR [--steps N]
     choose  --checkpoints DIR [DIR ...] --output best.json
@@ -64,6 +65,19 @@ def _agree(ok: bool, device) -> bool:
     t = torch.tensor([1 if ok else 0], dtype=torch.int64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MIN)
     return bool(t.item())
+
+
+def _eval_device(a):
+    """Rank and device of an evaluation stage: under ``torch.distributed.run``
+    one process per device (``LOCAL_RANK``), examples sharded across ranks."""
+    import os
+    from ..train.trainer import _init_dist
+    device = torch.device(a.device)
+    rank, _ = _init_dist(device.type)
+    if device.type == "cuda":
+        device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(device)
+    return rank, device
 
 
 def _recovery(a) -> list:
@@ -140,22 +154,26 @@ def main(argv=None):
     p.add_argument("--save-every", type=int, default=0, help="train: atomic step checkpoints")
     a = p.parse_args(argv)
     if a.stage == "select":
-        m = load_model(a.checkpoint, device=a.device).eval()
+        rank, device = _eval_device(a)
+        m = load_model(a.checkpoint, device=device).eval()
         depth = m.cfg.num_hidden_layers
         res = select_layers(m, _eval_examples(m.cfg, a.samples, a.block_size, a.seed), a.block_size, a.drop)
         h = res["history"][0]
-        write_selection(Path(a.output), a.checkpoint, depth, h["removed_compact_layer"],
-                        [i for i in range(depth) if i != h["removed_compact_layer"]], m.cfg.mask_token_id, res)
-        print(json.dumps({"removed": [x["removed_original_layer"] for x in res["history"]]}))
+        if rank == 0:
+            write_selection(Path(a.output), a.checkpoint, depth, h["removed_compact_layer"],
+                            [i for i in range(depth) if i != h["removed_compact_layer"]], m.cfg.mask_token_id, res)
+            print(json.dumps({"removed": [x["removed_original_layer"] for x in res["history"]]}))
     elif a.stage == "prune":
         print(prune_from_selection(a.selection, a.output))
     elif a.stage == "train":
         _recovery(a)
     else:
+        rank, device = _eval_device(a)
         m = load_model(a.checkpoints[0], device="cpu")
-        res = choose(a.checkpoints, _eval_examples(m.cfg, a.samples, a.block_size, a.seed), a.block_size, a.device)
-        write_json(a.output, res)
-        print(json.dumps(res["best"]))
+        res = choose(a.checkpoints, _eval_examples(m.cfg, a.samples, a.block_size, a.seed), a.block_size, device)
+        if rank == 0:
+            write_json(a.output, res)
+            print(json.dumps(res["best"]))
 
 
 if __name__ == "__main__":

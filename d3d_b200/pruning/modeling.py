@@ -43,11 +43,24 @@ def _inputs(model: Qwen3LM, ex: EvalExample, block_size: int, mode: str):
     return ids, pos, mask
 
 
+def _mean(rs):
+    return (sum(r[0] for r in rs) / len(rs), sum(r[1] for r in rs) / len(rs))
+
+
 @torch.no_grad()
 def evaluate_single_layer_removals(model: Qwen3LM, examples: Sequence[EvalExample], block_size: int,
                                    mode: str = "causal") -> Tuple[Tuple[float, float], Dict[int, Tuple[float, float]]]:
     """Mean (accept length, token accuracy) of the full model and of every
     single-layer deletion."""
+    full, cands = score_single_layer_removals(model, examples, block_size, mode)
+    return _mean(full), {j: _mean(rs) for j, rs in cands.items()}
+
+
+@torch.no_grad()
+def score_single_layer_removals(model: Qwen3LM, examples: Sequence[EvalExample], block_size: int,
+                                mode: str = "causal"):
+    """Per-example (accept length, token accuracy) of the full model and of
+    every single-layer deletion: ``(full[i], {j: cand_j[i]})`` in example order."""
     L = model.cfg.num_hidden_layers
     full: List[Tuple[int, float]] = []
     cands: Dict[int, List[Tuple[int, float]]] = {j: [] for j in range(L)}
@@ -71,8 +84,7 @@ def evaluate_single_layer_removals(model: Qwen3LM, examples: Sequence[EvalExampl
             for layer in model.model.layers[j + 1:]:
                 h = layer(h, cos, sin, mask, None, False)
             cands[j].append(score(h))
-    mean = lambda rs: (sum(r[0] for r in rs) / len(rs), sum(r[1] for r in rs) / len(rs))
-    return mean(full), {j: mean(rs) for j, rs in cands.items()}
+    return full, cands
 
 
 def examples_from_sequences(seqs: Sequence[Sequence[int]], block_size: int, per_seq: int,

@@ -25,15 +25,23 @@ def score_checkpoint(path, examples: Sequence[EvalExample], block_size: int, dev
 
 
 def _score_full(model, examples, block_size):
+    """Mean (accept length, token accuracy) over ``examples``; under
+    ``torch.distributed`` each rank scores examples rank::world and the rows
+    are gathered in example order (``pruning/select_checkpoint.py:98-120``)."""
     import torch
+    import torch.distributed as dist
     from .modeling import _inputs, hard_accept_length
+    from .select_layer import gather_in_order
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
     rs = []
     with torch.no_grad():
-        for ex in examples:
+        for ex in list(examples)[rank::world]:
             ids, pos, mask = _inputs(model, ex, block_size, "causal")
             h = model(ids, pos, mask=mask)
             lg = model.logits(h[:, -block_size:])[0, 1:]
             rs.append(hard_accept_length(lg.argmax(-1), torch.tensor(ex.continuation, device=ids.device)))
+    rs = gather_in_order(rs, world, rank)
     return (sum(r[0] for r in rs) / len(rs), sum(r[1] for r in rs) / len(rs)), None
 
 

@@ -124,3 +124,44 @@ def test_distributed_recovery_stops_together_and_records_cursor(tmp_path):
     assert json.loads((tmp_path / "recovered.step1" / "trainer_state.json").read_text())["next_data_cursor"] == 2
     assert load_model(tmp_path / "recovered").cfg.num_hidden_layers == 3
     assert (tmp_path / "recovered" / "layer_prune.json").exists()
+
+
+def _select_worker(rank, port, root):
+    import os
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+    from d3d_b200.pruning.__main__ import main
+    main(["select", "--checkpoint", f"{root}/parent", "--output", f"{root}/sel2.json", "--samples", "5",
+          "--block-size", "8", "--device", "cpu", "--drop", "2"])
+    main(["choose", "--checkpoints", f"{root}/parent", f"{root}/parent_b", "--output", f"{root}/best2.json",
+          "--samples", "5", "--block-size", "8", "--device", "cpu"])
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def test_data_parallel_selection_equals_single_process(tmp_path):
+    """Layer selection and checkpoint choice on two gloo ranks (examples
+    sharded rank::2, rows gathered in example order) give exactly the
+    single-process result: same removed layers, same means, same ranking."""
+    import socket
+    import torch.multiprocessing as mp
+    from d3d_b200.pruning.__main__ import main
+    save_model(_model(), tmp_path / "parent")
+    save_model(build_model(tiny_drafter(cond=False).replace(num_hidden_layers=4), seed=9), tmp_path / "parent_b")
+    main(["select", "--checkpoint", str(tmp_path / "parent"), "--output", str(tmp_path / "sel1.json"),
+          "--samples", "5", "--block-size", "8", "--device", "cpu", "--drop", "2"])
+    main(["choose", "--checkpoints", str(tmp_path / "parent"), str(tmp_path / "parent_b"), "--output",
+          str(tmp_path / "best1.json"), "--samples", "5", "--block-size", "8", "--device", "cpu"])
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_select_worker, args=(port, str(tmp_path)), nprocs=2, join=True)
+    one = json.loads((tmp_path / "sel1.json").read_text())
+    two = json.loads((tmp_path / "sel2.json").read_text())
+    assert one["metrics"]["history"] == two["metrics"]["history"]
+    assert one["metrics"]["history"][0]["samples"] == 10
+    b1 = json.loads((tmp_path / "best1.json").read_text())
+    b2 = json.loads((tmp_path / "best2.json").read_text())
+    assert b1["ranking"] == b2["ranking"]
