@@ -224,7 +224,6 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Ten
   TORCH_CHECK(chunk / page_size + 1 <= 1024, "attention chunk spans too many pages");
   TORCH_CHECK(n_chunks == 1 || (part_o && part_ml), "split attention needs partial buffers");
   TORCH_CHECK(n_chunks >= 1 && n_chunks <= 512, "attention: 1 <= n_chunks <= 512 (the combine kernel's limit)");
-  TORCH_CHECK(64 % page_size == 0, "attention: page size must divide 64");
   d3d::AttnArgs a{};
   a.q = cbf(q);
   a.k_cache = cbf(k_cache);

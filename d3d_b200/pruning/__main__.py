@@ -44,16 +44,21 @@ class DataWindow:
         self.vocab, self.seq_len = vocab, seq_len
         self.rng = random.Random(seed)
         if not self.synthetic:
-            from ..train.blocks import Example
-            rows = [json.loads(x) for x in Path(path).read_text().splitlines() if x.strip()]
-            perm = list(range(len(rows)))
-            random.Random(seed).shuffle(perm)
-            self.rows = [Example(rows[i]["prompt_ids"], rows[i]["response_ids"]) for i in perm]
+            from ..train.data import JsonlIndex
+            self.index = JsonlIndex(path)            # byte offsets; rows parsed when taken
+            self.perm = list(range(len(self.index)))
+            random.Random(seed).shuffle(self.perm)
 
     def take(self, start: int, n: int):
         if self.synthetic:
             return synthetic_examples(n, self.seq_len, 0.25, self.vocab, random.Random(self.rng.random() + start))
-        return self.rows[start:start + n]
+        from ..train.data import encode_row
+        out = []
+        for i in self.perm[start:start + n]:
+            ex = encode_row(self.index.row(i))
+            if ex is not None:
+                out.append(ex)
+        return out
 
 
 def _agree(ok: bool, device) -> bool:

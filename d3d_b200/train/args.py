@@ -21,6 +21,11 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--loss-decay-gamma", type=float, default=15.5)
     p.add_argument("--batch-size", type=int, default=4, help="sequences per rank per step")
     p.add_argument("--seq-len", type=int, default=2048, help="synthetic sequence length")
+    p.add_argument("--tokenizer", default=None, help="tokenizer directory (chat / text JSONL rows)")
+    p.add_argument("--max-examples", type=int, default=0, help="use the first N rows of the file (0 = all)")
+    p.add_argument("--max-prompt-len", type=int, default=4096)
+    p.add_argument("--max-seq-len", type=int, default=8192)
+    p.add_argument("--enable-thinking-template", action="store_true")
     p.add_argument("--parallel-anchors-per-example", type=int, default=32)
     p.add_argument("--max-steps", type=int, default=10)
     p.add_argument("--lr", type=float, default=1e-4)

@@ -45,7 +45,13 @@ class PackedTrainBatch:
         return int(self.active.sum())
 
     def to(self, device) -> "PackedTrainBatch":
-        kw = {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in self.__dict__.items()}
+        kw = {k: (v.to(device, non_blocking=True) if isinstance(v, torch.Tensor) else v)
+              for k, v in self.__dict__.items()}
+        return PackedTrainBatch(**kw)
+
+    def pin(self) -> "PackedTrainBatch":
+        """Page-locked host copy (asynchronous host-to-device transfer)."""
+        kw = {k: (v.pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in self.__dict__.items()}
         return PackedTrainBatch(**kw)
 
 

@@ -29,6 +29,7 @@ import torch
 import torch.distributed as dist
 
 from ..checkpoint import expected_keys, write_state
+from .data import IndexedExamples, Prefetcher, RowLimits, worker_rng
 from .blocks import Example, build_packed_block_batch, synthetic_examples
 from . import trajectory
 from .losses import ce_aux_per_token, decay_weights, lmhead_distill_loss, normalize_objective
@@ -57,18 +58,36 @@ def _all_sum(x: float, device) -> float:
     return float(t.item())
 
 
-def load_examples(path: str, n: int, seq_len: int, vocab: int, rng: random.Random,
-                  rank: int, world: int) -> List[Example]:
-    """``synthetic`` or a JSONL of ``{"prompt_ids": [...], "response_ids": [...]}``
-    (rank-strided rows, ``train/dataset.py:157-231``)."""
-    if path == "synthetic":
-        return synthetic_examples(n, seq_len, 0.25, vocab, rng)
-    rows = []
-    for i, line in enumerate(Path(path).read_text().splitlines()):
-        if line.strip() and i % world == rank:
-            d = json.loads(line)
-            rows.append(Example(d["prompt_ids"], d["response_ids"]))
-    return rows
+def _batch_source(args, rank: int, world: int, vocab: int, rng: random.Random, mask_id: int, cursor: int):
+    """``make(step) -> (examples, packed batch, cursor after)``, called in
+    step order on the prefetch thread.  ``synthetic`` draws seeded random
+    sequences; a JSONL path goes through the byte-offset index (rank-strided
+    rows, chat-template split, ``train/dataset.py:157-231``)."""
+    state = {"cursor": cursor}
+    if args.data_path == "synthetic":
+        pool = synthetic_examples(args.batch_size * max(1, args.max_steps), args.seq_len, 0.25, vocab, rng)
+
+        def take(c, n):
+            return [pool[(c + i) % len(pool)] for i in range(n)], c + n
+    else:
+        tok = None
+        if getattr(args, "tokenizer", None):
+            from transformers import AutoTokenizer
+            tok = AutoTokenizer.from_pretrained(args.tokenizer)
+        src = IndexedExamples(args.data_path, rank, world, tok,
+                              RowLimits(args.max_prompt_len, args.max_seq_len, args.enable_thinking_template),
+                              args.max_examples)
+        take = src.take
+
+    def make(step):
+        exs, state["cursor"] = take(state["cursor"], args.batch_size)
+        batch = build_packed_block_batch(exs, block_size=args.block_size, mask_token_id=mask_id,
+                                         max_anchors=args.parallel_anchors_per_example,
+                                         rng=worker_rng(args.seed, rank, step)) if exs else None
+        if batch is not None and torch.cuda.is_available() and args.device.startswith("cuda"):
+            batch = batch.pin()
+        return exs, batch, state["cursor"]
+    return make
 
 
 def _build(name: str, device, dtype, seed: int, layers: Optional[int] = None, mask_id: Optional[int] = None):
@@ -142,28 +161,27 @@ def train(args) -> dict:
         opt = FusedShardedAdamW(student.parameters(), lr=args.lr, weight_decay=args.weight_decay)
     else:
         opt = ShardedAdamW(student.parameters(), lr=args.lr, weight_decay=args.weight_decay)
-    start = 0
+    start, cursor0 = 0, None
     if args.resume:
         ck = Path(args.resume)
         opt.load_state_dict(torch.load(ck / f"optim_rank{rank:03d}.pt"))
-        start = json.loads((ck / "trainer_state.json").read_text())["step"]
+        st = json.loads((ck / "trainer_state.json").read_text())
+        start, cursor0 = st["step"], st.get("data_cursor")
     mask_id = int(student.cfg.mask_token_id)
     vocab = min(student.cfg.vocab_size, 151643) - 2
-    examples = load_examples(args.data_path, args.batch_size * max(1, args.max_steps), args.seq_len, vocab,
-                             rng, rank, world)
+    make_batch = _batch_source(args, rank, world, vocab, rng, mask_id,
+                               start * args.batch_size if cursor0 is None else cursor0)
+    prefetch = Prefetcher(make_batch, start, args.max_steps, depth=2)
     out_dir = Path(args.output_dir)
     if rank == 0:
         out_dir.mkdir(parents=True, exist_ok=True)
     a_kl = args.kl_weight if (teacher is not None and objective in ("forward_kl", "kl_ce")) else 0.0
     a_ce = args.ce_weight if objective in ("ce", "kl_ce") else 0.0
     log = []
-    cursor = start * args.batch_size
+    cursor = start * args.batch_size if cursor0 is None else cursor0
     t_start = time.perf_counter()
     for step in range(start, args.max_steps):
-        exs = [examples[(cursor + i) % len(examples)] for i in range(args.batch_size)]
-        cursor += args.batch_size
-        batch = build_packed_block_batch(exs, block_size=args.block_size, mask_token_id=mask_id,
-                                         max_anchors=args.parallel_anchors_per_example, rng=rng)
+        _, (exs, batch, cursor) = prefetch.get()   # packed on the host thread, ahead of the device
         if device.type == "cuda":
             torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -252,6 +270,7 @@ def train(args) -> dict:
             save_checkpoint(student, opt, out_dir, step + 1, cursor)
     if args.save_final:
         save_checkpoint(student, opt, out_dir, args.max_steps, cursor)
+    prefetch.close()
     return {"log": log, "elapsed_s": time.perf_counter() - t_start, "world": world}
 
 
