@@ -156,7 +156,7 @@ def bench_lmhead(iters, peaks, rows, only_m=None):
                          TFLOPs=round(2 * m * n * k / us / 1e6, 1)))
 
 
-def bench_attn(iters, peaks, rows):
+def bench_attn(iters, peaks, rows, only=None, graph=True):
     from d3d_b200 import ops
     from d3d_b200.engine.layout import branch_specs, causal_rows, packed_layout
     E = ops.ext()
@@ -167,6 +167,8 @@ def bench_attn(iters, peaks, rows):
                                            ("ar 8B c256", 32, 8, 1000, 1, 256),
                                            ("packed 1.7B A1", 16, 8, 1000, 272, 256),
                                            ("packed 1.7B A3", 16, 8, 1000, 752, 256)):
+        if only and name != only:
+            continue
         d = 128
         L = prefix + q
         pages = math.ceil(L / 16)
@@ -188,7 +190,7 @@ def bench_attn(iters, peaks, rows):
         pm = torch.empty(nch * q * hq * 2, device="cuda")
         out = torch.empty_like(qq)
         us = timeit(lambda i: E.attention(qq, kc, vc, bt, rows_t, kv_end, 1, q, hq, hkv, 16,
-                                          1 / math.sqrt(d), chunk, nch, po, pm, out), iters)
+                                          1 / math.sqrt(d), chunk, nch, po, pm, out), iters, graph=graph)
         byts = 2 * L * hkv * d * 2
         rows.append(dict(kernel="attention", shape=name, M=q, N=L, K=d, us=round(us, 2),
                          GBps=round(byts / us / 1e3, 1)))
@@ -283,6 +285,8 @@ def main():
     ap.add_argument("--lm-m", type=int, default=None)
     ap.add_argument("--drafter", action="store_true", help="forward: drafter packed M=272")
     ap.add_argument("--sweep-m", type=int, default=272, help="gemm_sweep: token count")
+    ap.add_argument("--attn-case", default=None, help="attn: run only this shape (e.g. 'packed 1.7B A1')")
+    ap.add_argument("--no-graph", action="store_true", help="eager launches (for profiler captures)")
     a = ap.parse_args()
     peaks = load_peaks()
     rows = []
@@ -301,7 +305,7 @@ def main():
     if "lmhead" in only:
         bench_lmhead(a.iters, peaks, rows, a.lm_m)
     if "attn" in only:
-        bench_attn(a.iters, peaks, rows)
+        bench_attn(a.iters, peaks, rows, a.attn_case, not a.no_graph)
     if "gemm_sweep" in only:
         bench_gemm_sweep(a.sweep_m, a.iters, peaks, rows)
     if "forward_eager" in only:

@@ -298,6 +298,12 @@ class FastRunner:
         # Key chunk per attention CTA.  Fine chunks keep >100 CTAs busy at decode
         # sizes (one 64-key tile each for the batch-invariant target); the
         # drafter's packed forward has many query rows, so it takes 256.
+        # D3D_TARGET_CHUNK / D3D_DRAFT_CHUNK override (0 = one chunk over the
+        # whole context, no combine pass); the target's chunk must be the same
+        # for every forward of a runner (AR and verify), which it is.
+        env = os.environ.get("D3D_TARGET_CHUNK" if batch_invariant else "D3D_DRAFT_CHUNK")
+        if decode_chunk is None and env is not None:
+            decode_chunk = int(env) if int(env) > 0 else -1
         self.decode_chunk = decode_chunk or (64 if batch_invariant else 256)
         self.max_context = max_context
         self.batch_invariant = batch_invariant
@@ -444,7 +450,7 @@ class FastRunner:
         return b
 
     def chunk_for(self, prefill: bool) -> int:
-        if prefill:
+        if prefill or self.decode_chunk < 0:
             return max(64, int(math.ceil(self.max_context / 64) * 64))
         return self.decode_chunk
 
