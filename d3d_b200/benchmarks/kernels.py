@@ -276,6 +276,45 @@ def forward_eager(layers, drafter, context=1000):
                           launches=n, status=int(b.status.item()))))
 
 
+def train_kernels(iters, peaks, rows, n_tok=4096, chunk=16384, hidden=2048):
+    """The training step's own kernels at distillation shapes: online-LSE
+    KL+CE statistics and gradient over one vocabulary chunk of fp32 logits
+    (``n_tok`` rows), the fused AdamW update and the squared-norm reduction
+    over the 1.7B drafter's parameter count / 8 ranks (eager launches)."""
+    from d3d_b200 import ops
+    E = ops.ext()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    zs = torch.randn(n_tok, chunk, device="cuda", generator=g)
+    zt = torch.randn(n_tok, chunk, device="cuda", generator=g)
+    tgt = torch.randint(0, chunk, (n_tok,), device="cuda", generator=g)
+    st = torch.zeros(n_tok, 8, device="cuda")
+    st[:, 0] = st[:, 4] = -math.inf
+    us = timeit(lambda i: E.kl_ce_stats(zt, zs, chunk, 0, tgt, st), iters, graph=False)
+    byts = 2 * n_tok * chunk * 4
+    rows.append(dict(kernel="kl_ce_stats", shape=f"{n_tok}x{chunk}", us=round(us, 2), GBps=round(byts / us / 1e3, 1),
+                     hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3)))
+    lse = torch.randn(n_tok, device="cuda", generator=g)
+    w = torch.rand(n_tok, device="cuda", generator=g)
+    dz = torch.empty(n_tok, chunk, dtype=torch.bfloat16, device="cuda")
+    us = timeit(lambda i: E.kl_ce_grad(zt, zs, chunk, 0, tgt, lse, lse, w, w, dz, None), iters, graph=False)
+    byts = 2 * n_tok * chunk * 4 + n_tok * chunk * 2
+    rows.append(dict(kernel="kl_ce_grad", shape=f"{n_tok}x{chunk}", us=round(us, 2), GBps=round(byts / us / 1e3, 1),
+                     hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3)))
+    n = 1_720_000_000 // 8
+    p = torch.zeros(n, device="cuda")
+    gr = torch.randn(n, device="cuda", generator=g)
+    m1, v1 = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    out = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    us = timeit(lambda i: E.adamw(p, gr, m1, v1, out, 1e-4, 0.9, 0.95, 1e-8, 0.0, i + 1, 1.0), iters, graph=False)
+    byts = n * (4 * 4 + 3 * 4 + 2)
+    rows.append(dict(kernel="adamw", shape=f"{n} params", us=round(us, 2), GBps=round(byts / us / 1e3, 1),
+                     hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3)))
+    sq = torch.zeros(1, device="cuda")
+    us = timeit(lambda i: E.sumsq(gr, sq), iters, graph=False)
+    rows.append(dict(kernel="sumsq", shape=f"{n} floats", us=round(us, 2), GBps=round(n * 4 / us / 1e3, 1),
+                     hbm_frac=round(n * 4 / us / 1e3 / peaks["hbm_gbs"], 3)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,lmhead,attn,forward")
@@ -308,6 +347,8 @@ def main():
         bench_attn(a.iters, peaks, rows, a.attn_case, not a.no_graph)
     if "gemm_sweep" in only:
         bench_gemm_sweep(a.sweep_m, a.iters, peaks, rows)
+    if "train_kernels" in only:
+        train_kernels(a.iters, peaks, rows)
     if "forward_eager" in only:
         forward_eager(a.layers, a.drafter)
     if "forward" in only:

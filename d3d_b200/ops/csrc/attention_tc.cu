@@ -16,18 +16,23 @@
 //                    key tiles no row of the CTA can see are never loaded;
 //   warp 1, lane 0   MMA issuer: S_j = Q K_j^T (M=128, N=64, K=d: K-major
 //                    A and B) into one of two TMEM S buffers; then, once the
-//                    softmax warps have written P_j, O_j = P_j V_j (M=128,
+//                    softmax warps have written P_j, O += P_j V_j (M=128,
 //                    N=d, K=64; V is read N-major straight from the ring)
-//                    into one of two TMEM O buffers.  S_{j+1} is issued
-//                    before O_j so the softmax of tile j+1 overlaps PV_j;
+//                    into one TMEM O accumulator that lives across tiles.
+//                    S_{j+1} is issued before PV_j, so the softmax of tile
+//                    j+1 overlaps PV_j;
 //   warps 2..9       softmax: warp w reads TMEM lane quadrant w % 4 (its 32
 //                    rows); warps 2-5 own key columns 0-31 and d columns
 //                    0..d/2-1, warps 6-9 the other halves.  Each thread
 //                    loads its row's 64 scores, takes the row max over all
-//                    64 (both halves agree on it), masks with (lim, lo, hi),
-//                    writes bf16 P for its 32 keys into a swizzled shared
-//                    tile (the A operand of PV), and folds O_j into fp32
-//                    registers: o = o * 2^(m_old - m_new) + O_j.
+//                    64 (both halves agree on it), masks with (lim, lo, hi)
+//                    and writes bf16 P = 2^(s - m) for its 32 keys into a
+//                    swizzled shared tile (the A operand of PV).  The
+//                    reference max m of a row only moves when the row's
+//                    running max exceeds it by more than 2^8; then the row's
+//                    O columns are rescaled in TMEM (after PV_{j-1} has
+//                    retired) before P_j is published.  Every decision
+//                    depends on the row's own scores only.
 // Keys are cut into chunks at fixed absolute boundaries (grid z); a chunk's
 // tiles run in increasing key order; chunk results are merged by the
 // fixed-order combine kernel.  A row's result therefore depends only on its
@@ -65,9 +70,18 @@ struct TaCfg {
   static constexpr int OFF_P = OFF_KV + TA_STAGES * STAGE;
   static constexpr int SMEM = OFF_P + 2 * P_BYTES + 1024;  // + 1024-byte alignment slack
   static constexpr int COL_S = 0;                          // TMEM: S buffers, 2 x 64 columns
-  static constexpr int COL_O = 128;                        // TMEM: O buffers, 2 x D columns
-  static constexpr uint32_t TMEM_COLS = (128 + 2 * D) <= 256 ? 256u : 512u;
+  static constexpr int COL_O = 128;                        // TMEM: O accumulator, D columns
+  static constexpr uint32_t TMEM_COLS = (128 + D) <= 256 ? 256u : 512u;
 };
+
+// 2^x on the MUFU unit (PTX ex2.approx, subnormal results flushed to zero;
+// 2^-inf = +0).  Softmax weights are rounded to bf16 right after, so the
+// instruction's approximation error is below that rounding.
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <int D>
 __global__ void __launch_bounds__(TA_THREADS, 1)
@@ -82,7 +96,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   __shared__ int s_pages[TA_MAX_PAGES];
   __shared__ float s_lpart[2][TA_ROWS];
   __shared__ uint64_t q_full, kv_full[TA_STAGES], kv_empty[TA_STAGES];
-  __shared__ uint64_t s_full[2], s_free[2], p_full[2], o_full[2], o_free[2], done;
+  __shared__ uint64_t s_full[2], s_free[2], p_full[2], o_done, done;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int flags[4];  // [0] abort  [1] tiles issued (TMA)  [2] tiles consumed (MMA)  [3] Q issued
 
@@ -127,9 +141,8 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 8);
       mbar_init(&p_full[i], 8);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 8);
     }
+    mbar_init(&o_done, 1);       // one phase per PV product, waited in order
     mbar_init(&done, 1);
     flags[0] = flags[1] = flags[2] = flags[3] = 0;
     fence_mbar_init();
@@ -143,12 +156,6 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     const int* bt = a.block_table + static_cast<size_t>(b) * a.bt_stride;
     const int npg = kend > kbeg ? min((kend - 1) / ps - pg0 + 1, a.bt_stride - pg0) : 0;
     for (int i = tid; i < npg && i < TA_MAX_PAGES; i += TA_THREADS) s_pages[i] = bt[pg0 + i];
-    // Pages past kv_end are never loaded, so their part of a ring stage keeps
-    // older contents: zero the ring once so those are finite (a masked key
-    // contributes P = 0, and 0 * finite = 0 in the PV product).
-    uint4* ring = reinterpret_cast<uint4*>(smem + C::OFF_KV);
-    for (int i = tid; i < TA_STAGES * C::STAGE / 16; i += TA_THREADS) ring[i] = make_uint4(0, 0, 0, 0);
-    fence_proxy_async_smem();
   }
   if (warp == 1) {
     tmem_alloc(&tmem_slot, C::TMEM_COLS);
@@ -179,29 +186,44 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
   const uint64_t lim = lim_ns;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------- TMA
-      griddep_wait();
-      if (kend > kbeg) {
-        mbar_arrive_expect_tx(&q_full, C::NH * C::Q_HALF);
-        for (int hf = 0; hf < C::NH; ++hf)
-          tma_load_3d(smem + hf * C::Q_HALF, &tmQ, &q_full, hf * 64, h * g, b * a.q_len + R0 / g);
-        flags[3] = 1;
+    // --------------------------------------------------------------- TMA
+    // lane 0 issues the copies; the whole warp zeroes the V rows of boxes
+    // past kv_end (never loaded: a masked key contributes P = 0, and
+    // 0 * finite = 0 in the PV product, so those rows must hold finite values)
+    griddep_wait();
+    if (lane == 0 && kend > kbeg) {
+      mbar_arrive_expect_tx(&q_full, C::NH * C::Q_HALF);
+      for (int hf = 0; hf < C::NH; ++hf)
+        tma_load_3d(smem + hf * C::Q_HALF, &tmQ, &q_full, hf * 64, h * g, b * a.q_len + R0 / g);
+      flags[3] = 1;
+    }
+    int j = 0;
+    for (int k0 = next_tile(kbeg); k0 < kend && !flags[0]; k0 = next_tile(k0 + TA_KEYS), ++j) {
+      const int s = j % TA_STAGES;
+      bool ok = mbar_wait(&kv_empty[s], ((j / TA_STAGES) & 1) ^ 1, lim);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) fail(ERR_TIMEOUT_PRODUCER);
+        break;
       }
-      int j = 0;
-      for (int k0 = next_tile(kbeg); k0 < kend && !flags[0]; k0 = next_tile(k0 + TA_KEYS), ++j) {
-        const int s = j % TA_STAGES;
-        if (!mbar_wait(&kv_empty[s], ((j / TA_STAGES) & 1) ^ 1, lim)) {
-          fail(ERR_TIMEOUT_PRODUCER);
-          break;
+      uint8_t* st = smem + C::OFF_KV + s * C::STAGE;
+      int boxes = 0;
+      for (int i = 0; i < TA_KEYS / kb; ++i) {
+        if (k0 + i * kb < kv_end) {
+          ++boxes;
+          continue;
         }
-        int boxes = 0;
-        for (int i = 0; i < TA_KEYS / kb; ++i) boxes += (k0 + i * kb < kv_end) ? 1 : 0;
+        for (int hf = 0; hf < C::NH; ++hf) {
+          uint4* z = reinterpret_cast<uint4*>(st + (C::NH + hf) * C::KV_HALF + i * kb * 128);
+          for (int e = lane; e < kb * 8; e += 32) z[e] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
         mbar_arrive_expect_tx(&kv_full[s], static_cast<uint32_t>(boxes * 2 * C::NH * kb * 128));
-        uint8_t* st = smem + C::OFF_KV + s * C::STAGE;
-        for (int i = 0; i < TA_KEYS / kb; ++i) {
+        for (int i = 0; i < boxes; ++i) {
           const int key = k0 + i * kb;
-          if (key >= kv_end) break;
           const int slot = s_pages[key / ps - pg0] * ps + key % ps;
           for (int hf = 0; hf < C::NH; ++hf) {
             tma_load_3d(st + hf * C::KV_HALF + i * kb * 128, &tmK, &kv_full[s], hf * 64, h, slot);
@@ -244,7 +266,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       };
       auto issue_o = [&](int j) -> bool {
         const int s = j % TA_STAGES, buf = j & 1;
-        if (!mbar_wait(&p_full[buf], (j >> 1) & 1, lim) || !mbar_wait(&o_free[buf], ((j >> 1) & 1) ^ 1, lim)) {
+        if (!mbar_wait(&p_full[buf], (j >> 1) & 1, lim)) {
           fail(ERR_TIMEOUT_MMA);
           return false;
         }
@@ -253,9 +275,9 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         const uint32_t v_addr = smem_u32(smem + C::OFF_KV + s * C::STAGE + C::NH * C::KV_HALF);
 #pragma unroll
         for (int kk = 0; kk < TA_KEYS / 16; ++kk)
-          umma_bf16(tmem + C::COL_O + buf * D, sdesc_kmajor_sw128(p_addr + kk * 32),
-                    sdesc_mnmajor_sw128(v_addr + kk * 16 * 128, C::KV_HALF), idesc_o, kk > 0 ? 1u : 0u);
-        umma_commit(&o_full[buf]);
+          umma_bf16(tmem + C::COL_O, sdesc_kmajor_sw128(p_addr + kk * 32),
+                    sdesc_mnmajor_sw128(v_addr + kk * 16 * 128, C::KV_HALF), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&o_done);
         umma_commit(&kv_empty[s]);
         return true;
       };
@@ -271,40 +293,22 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
     const int ch = (warp - 2) >> 2;          // column half
     const int row = qd * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(qd * 32) << 16);
+    const uint32_t t_o = t_lane + C::COL_O + ch * (D / 2);
     const int lim_r = s_rows[row][0], lo_r = s_rows[row][1], hi_r = s_rows[row][2];
     const float sl2 = a.scale * 1.4426950408889634f;  // scale * log2(e)
     constexpr int DH = D / 2;
-    float o[DH];
-#pragma unroll
-    for (int i = 0; i < DH; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    constexpr float RESCALE = 8.f;           // move the reference max when it is exceeded by 2^8
+    float m = -INFINITY, l = 0.f;
     uint8_t* prow_base = smem + C::OFF_P + row * 128;
     bool ok = true;
 
     // every lane waits; the warp follows lane 0's verdict so warp-collective
-    // TMEM loads stay converged
+    // TMEM accesses stay converged
     auto warp_wait = [&](uint64_t* bar, uint32_t parity) -> bool {
       bool w = mbar_wait(bar, parity, lim);
       w = __shfl_sync(0xffffffffu, w && !flags[0], 0);
       if (!w && lane == 0 && !flags[0]) fail(ERR_TIMEOUT_EPILOGUE);
       return w;
-    };
-    auto acc_o = [&](int i, float al) -> bool {
-      const int buf = i & 1;
-      if (!warp_wait(&o_full[buf], (i >> 1) & 1)) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < DH; c += 32) {
-        uint32_t r[32];
-        tmem_ld32_nowait(t_lane + C::COL_O + buf * D + ch * DH + c, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o[c + e] = o[c + e] * al + __uint_as_float(r[e]);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free[buf]);
-      return true;
     };
 
     int j = 0;
@@ -319,40 +323,70 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[buf]);
-      float s[64];
-      const int k1 = k0 + TA_KEYS;
-      const bool full = k1 <= kend && (k1 <= lim_r || (k0 >= lo_r && k1 <= hi_r));
-      float tm = -INFINITY;
+      // Visible keys of this row inside the tile, as tile columns:
+      // [0, va) U [vb, ve)  (from k < lim  or  lo <= k < hi, clipped to kend).
+      const int kc = kend - k0;
+      const int va = max(0, min(min(lim_r, kend) - k0, TA_KEYS));
+      const int vb = max(0, min(lo_r - k0, TA_KEYS));
+      const int ve = max(vb, min(min(hi_r, kend) - k0, TA_KEYS));
+      const bool full = kc >= TA_KEYS && (va == TA_KEYS || (vb == 0 && ve == TA_KEYS));
+      // row max over the raw scores (scale > 0 commutes with max)
+      float tr = -INFINITY;
       if (full) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          s[c] = __uint_as_float(sr[c]) * sl2;
-          tm = fmaxf(tm, s[c]);
-        }
+        for (int c = 0; c < 64; ++c) tr = fmaxf(tr, __uint_as_float(sr[c]));
       } else {
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const int key = k0 + c;
-          const bool vis = key < kend && (key < lim_r || (key >= lo_r && key < hi_r));
-          s[c] = vis ? __uint_as_float(sr[c]) * sl2 : -INFINITY;
-          tm = fmaxf(tm, s[c]);
+          const bool vis = c < va || static_cast<unsigned>(c - vb) < static_cast<unsigned>(ve - vb);
+          sr[c] = vis ? sr[c] : 0xff800000u;          // -inf
+          tr = fmaxf(tr, __uint_as_float(sr[c]));
         }
       }
-      const float nm = fmaxf(m, tm);
-      const float alpha = nm == -INFINITY ? 1.f : exp2f(m - nm);
+      const float tm = tr * sl2;
+      // reference max: set on the first visible scores, moved only by > 2^8
+      float alpha = 1.f;
+      if (m == -INFINITY) {
+        m = tm;
+      } else if (tm > m + RESCALE) {
+        alpha = ex2_ftz(m - tm);
+        m = tm;
+      }
       float sum = 0.f;
       uint32_t pk[16];
+      if (m == -INFINITY) {        // nothing visible yet: P = 0
 #pragma unroll
-      for (int e = 0; e < 32; e += 2) {
-        const float x0 = ch ? s[32 + e] : s[e], x1 = ch ? s[33 + e] : s[e + 1];   // static indices
-        const float p0 = x0 == -INFINITY ? 0.f : exp2f(x0 - nm);
-        const float p1 = x1 == -INFINITY ? 0.f : exp2f(x1 - nm);
-        sum += p0 + p1;
-        __nv_bfloat162 v = __floats2bfloat162_rn(p0, p1);
-        pk[e >> 1] = *reinterpret_cast<uint32_t*>(&v);
+        for (int e = 0; e < 16; ++e) pk[e] = 0u;
+      } else {
+        // p = 2^(raw * scale*log2e - m); a masked key (raw = -inf) gives 0
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float x0 = __uint_as_float(ch ? sr[32 + e] : sr[e]);    // static indices
+          const float x1 = __uint_as_float(ch ? sr[33 + e] : sr[e + 1]);
+          const float p0 = ex2_ftz(fmaf(x0, sl2, -m));
+          const float p1 = ex2_ftz(fmaf(x1, sl2, -m));
+          sum += p0 + p1;
+          __nv_bfloat162 v = __floats2bfloat162_rn(p0, p1);
+          pk[e >> 1] = *reinterpret_cast<uint32_t*>(&v);
+        }
       }
       l = l * alpha + sum;
-      m = nm;
+      // PV_{j-1} has retired before P_j is published (the O rescale below and
+      // the reuse of P buffer (j & 1), last read by PV_{j-2}, rely on it)
+      if (j > 0 && !(ok = warp_wait(&o_done, (j - 1) & 1))) break;
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < DH; c += 32) {
+          uint32_t r[32];
+          tmem_ld32_nowait(t_o + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          tmem_st32(t_o + c, r);
+        }
+        tmem_wait_st();
+      }
       // P row: keys 32ch..32ch+31 = 16-byte chunks 4ch..4ch+3, 128-byte swizzle
       uint8_t* prow = prow_base + buf * C::P_BYTES;
 #pragma unroll
@@ -361,12 +395,27 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
         *reinterpret_cast<uint4*>(prow + chunk * 16) = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
       fence_proxy_async_smem();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[buf]);
-      if (j > 0 && !(ok = acc_o(j - 1, alpha_prev))) break;
-      alpha_prev = alpha;
     }
-    if (ok && j > 0) ok = acc_o(j - 1, alpha_prev);
+    // the last PV product, then this thread's O columns
+    float o[DH];
+    if (ok && j > 0) ok = warp_wait(&o_done, (j - 1) & 1);
+    if (ok && j > 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < DH; c += 32) {
+        uint32_t r[32];
+        tmem_ld32_nowait(t_o + c, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[c + e] = __uint_as_float(r[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < DH; ++e) o[e] = 0.f;
+    }
 
     // ---- combine the two column halves' row sums (fixed order: half 0 + half 1)
     s_lpart[ch][row] = l;
