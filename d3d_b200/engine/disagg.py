@@ -358,3 +358,180 @@ class P2PTarget(TargetBackend):
             self._send(HDR)
             if self.stream is not None:
                 self.stream.synchronize()
+
+
+class BatchedTargetServer:
+    """One target serving several drafter ranks, each at the end of its own
+    link (the multi-GPU layout: target on T GPUs, tensor-parallel, drafters
+    on the other GPUs, one request stream each).
+
+    Every drafter keeps exactly one request outstanding (the coordinator
+    sends a verify, then waits for its reply), so the server works in rounds:
+    it takes one message from each drafter still open, runs all PREFILLs of
+    the round as one batched prefill and all VERIFYs as one batched verify
+    (one forward over every drafter's blocks), and answers each drafter in
+    its own mailbox -- on GPU links by one fused accept+send launch per
+    drafter on its rows of the verify output.  Sequence ids are made unique
+    per drafter before they reach the backend.  The ranks of a
+    tensor-parallel target all run the same rounds (every drafter sends to
+    every rank), so their forwards and exchanges stay in step; only rank 0
+    answers (``replies="ack"`` elsewhere, which still acknowledges RELEASE).
+    ``serve()`` returns when every drafter has sent CLOSE."""
+
+    ID_STRIDE = 1 << 32
+
+    def __init__(self, backend, links, deadline_s: float = 600.0, replies: str = "all"):
+        self.be = backend
+        self.subs = [P2PTargetServer(backend, lk, deadline_s=deadline_s, replies=replies) for lk in links]
+        self.replies = replies
+        self.deadline_s = deadline_s
+        self.seqs: Dict[int, SeqState] = {}
+        self.H = int(backend.hidden_size)
+        self.served = 0
+        self.rounds = 0
+
+    def _gid(self, d: int, sid: int) -> int:
+        return d * self.ID_STRIDE + int(sid)
+
+    def _recv(self, d: int, poll=None) -> list:
+        sub = self.subs[d]
+        sub.link.recv(sub.req[:HEAD_WORDS], sub.stream, deadline_s=self.deadline_s, poll=poll)
+        h = sub.req[:HDR].tolist()
+        if h[0] == CMD_PREFILL:
+            words = HDR + 2 * h[1] + h[2]
+            if words > HEAD_WORDS:
+                sub.link.fetch(sub.req[HEAD_WORDS:words], 8 * HEAD_WORDS, sub.stream)
+        return h
+
+    # ---------------------------------------------------------- commands
+    def _prefill(self, items) -> None:
+        group, spans = [], []
+        for d, h in items:
+            sub = self.subs[d]
+            n, total = int(h[1]), int(h[2])
+            meta = sub.req[HDR:HDR + 2 * n].view(n, 2).tolist()
+            toks = sub.req[HDR + 2 * n:HDR + 2 * n + total].tolist()
+            off = 0
+            for sid, ln in meta:
+                s = SeqState(index=self._gid(d, sid), prompt=toks[off:off + ln], prefix=ln)
+                off += ln
+                self.seqs[s.index] = s
+                group.append(s)
+            spans.append((d, len(group) - n, n))
+        anchors, hidden = self.be.prefill(group)
+        if self.replies != "all":
+            return
+        anchors = anchors.to(torch.int64).cpu()
+        hidden = hidden.to(torch.bfloat16).cpu()
+        for d, r0, n in spans:
+            sub = self.subs[d]
+            words = _prefill_words(n)
+            ho = hidden_offset(words)
+            sub.rep_host[:HDR] = 0
+            sub.rep_host[0], sub.rep_host[1], sub.rep_host[2] = CMD_PREFILL, n, self.H
+            sub.rep_host[HDR:HDR + n] = anchors[r0:r0 + n]
+            hb = sub.rep_host.view(torch.uint8)[ho:ho + 2 * n * self.H].view(torch.bfloat16)
+            hb.copy_(hidden[r0:r0 + n].reshape(-1))
+            sub._reply_host((ho + 2 * n * self.H + 7) // 8)
+
+    def _verify(self, items) -> None:
+        group, blocks, spans, K = [], [], [], None
+        for d, h in items:
+            sub = self.subs[d]
+            B, k = int(h[1]), int(h[2])
+            if K is not None and k != K:
+                raise ValueError("drafters verify blocks of different sizes in one round")
+            K = k
+            meta = sub.req[HDR:HDR + 2 * B].view(B, 2).tolist()   # (sequence id, prefix)
+            blocks.append(sub.req[HDR + 2 * B:HDR + 2 * B + B * K].view(B, K).clone())
+            for sid, prefix in meta:
+                s = self.seqs[self._gid(d, sid)]
+                s.prefix = prefix
+                group.append(s)
+            spans.append((d, len(group) - B, B))
+        blocks = torch.cat(blocks)
+        fused = self.subs[0].fused
+        if self.replies != "all":
+            if fused:
+                self.be.submit_verify(group, blocks, sink=lambda ids, post, xn: None)
+            else:
+                self.be.verify(group, blocks)
+            return
+        if not fused:
+            r = self.be.verify(group, blocks)
+            for d, r0, B in spans:
+                sub = self.subs[d]
+                words = _verify_words(B, K)
+                ho = hidden_offset(words)
+                sub.rep_host[:HDR] = 0
+                sub.rep_host[0], sub.rep_host[1], sub.rep_host[2], sub.rep_host[3] = CMD_VERIFY, B, K, self.H
+                res = torch.cat([r.commit[r0:r0 + B].view(B, 1).to(torch.int64).cpu(),
+                                 r.correction[r0:r0 + B].view(B, 1).to(torch.int64).cpu(),
+                                 r.posterior[r0:r0 + B].to(torch.int64).cpu().view(B, K)], 1)
+                sub.rep_host[HDR:words] = res.reshape(-1)
+                if r.hidden is not None:
+                    hb = sub.rep_host.view(torch.uint8)[ho:ho + 2 * B * self.H].view(torch.bfloat16)
+                    hb.copy_(r.hidden[r0:r0 + B].to(torch.bfloat16).reshape(-1).cpu())
+                sub._reply_host((ho + 2 * B * self.H + 7) // 8)
+            return
+        outs = []
+        for d, r0, B in spans:
+            lk = self.subs[d].link
+            seq = lk.send_seq + 1
+            lk.send_seq = seq
+            out_ptr = lk.outbox.slot_ptr(seq)
+            outs.append((r0, B, out_ptr, out_ptr + hidden_offset(_verify_words(B, K)), lk.outbox.flag_ptr, seq))
+        E = ops.ext()
+
+        def sink(ids, post, xn):
+            for r0, B, out_ptr, hid_ptr, flag_ptr, seq in outs:
+                E.accept_send(ids[r0:r0 + B], post[r0:r0 + B], xn[r0 * K:(r0 + B) * K], out_ptr, hid_ptr,
+                              flag_ptr, seq)
+
+        self.be.submit_verify(group, blocks, sink=sink)
+
+    def _release(self, d: int, sid: int) -> None:
+        s = self.seqs.pop(self._gid(d, sid), None)
+        if s is not None:
+            self.be.release(s)
+        sub = self.subs[d]
+        sub.rep_host[:HDR] = 0
+        sub.rep_host[0] = CMD_RELEASE
+        sub._reply_host(HDR)
+
+    def serve(self, poll=None) -> None:
+        active = list(range(len(self.subs)))
+        while active:
+            msgs = [(d, self._recv(d, poll)) for d in active]
+            chk = getattr(self.be, "check_tp", None)
+            if chk is not None:
+                chk()   # a failed tensor-parallel exchange ends serving loudly
+            self.rounds += 1
+            by = {}
+            for d, h in msgs:
+                by.setdefault(h[0], []).append((d, h))
+            batches = [(self._prefill, by.pop(CMD_PREFILL, []))]
+            by_k = {}
+            for d, h in by.pop(CMD_VERIFY, []):     # one batched verify per block size
+                by_k.setdefault(int(h[2]), []).append((d, h))
+            batches += [(self._verify, by_k[k]) for k in sorted(by_k)]
+            for run, items in batches:
+                if not items:
+                    continue
+                try:
+                    run(items)
+                    self.served += len(items)
+                except Exception as exc:  # every drafter of the batch hears about it
+                    if self.replies != "all":
+                        raise
+                    for d, _ in items:
+                        self.subs[d]._send_error(exc)
+            for d, h in by.pop(CMD_RELEASE, []):
+                self._release(d, int(h[1]))
+                self.served += 1
+            closed = {d for d, _ in by.pop(CMD_CLOSE, [])}
+            for kind, items in by.items():
+                for d, _ in items:
+                    if self.replies == "all":
+                        self.subs[d]._send_error(ValueError(f"unknown target command {kind}"))
+            active = [d for d in active if d not in closed]
