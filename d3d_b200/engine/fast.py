@@ -146,6 +146,30 @@ class _FastModelBackend:
         with torch.cuda.stream(self.stream):
             b.inbuf.copy_(b.inbuf_host, non_blocking=True)
 
+    @torch.inference_mode()
+    def hidden_states(self, ids: torch.Tensor) -> torch.Tensor:
+        """Final-norm hidden states ``[B, L, H]`` of one causal forward over
+        ``ids`` ``[B, L]`` (every row of every sequence; no LM head, no KV
+        kept afterwards).  Used for the frozen teacher of distillation."""
+        B, L = ids.shape
+        seqs = [SeqState(index=-(i + 1), prompt=[], prefix=0) for i in range(B)]
+        try:
+            for s in seqs:
+                self.kv.reserve(s.index, self._row(s), L)
+            b = self.runner.buffers(B, L, 0, prefill=True)
+            rows = np.broadcast_to(causal_rows(0, L).numpy()[None], (B, L, 3))
+            pos = np.broadcast_to(np.arange(L, dtype=np.int64)[None], (B, L))
+            self._fill(b, seqs, ids.cpu().numpy(), pos, rows, np.full(B, L, dtype=np.int64), "hs")
+            with torch.cuda.stream(self.stream):
+                launches.add(self.runner.forward(b))
+                out = b.xn.view(B, L, -1).clone()
+            torch.cuda.current_stream(self.device).wait_stream(self.stream)
+            out.record_stream(torch.cuda.current_stream(self.device))
+            return out
+        finally:
+            for s in seqs:
+                self._release(s)
+
     def _prefill_one(self, s: SeqState, rows: np.ndarray, topk: int, reserve: int):
         n = len(s.prompt)
         self.kv.reserve(s.index, self._row(s), reserve)

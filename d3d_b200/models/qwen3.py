@@ -96,16 +96,74 @@ class DenseKVCache:
         return c
 
 
+class _TcLinearFn(torch.autograd.Function):
+    """``y = x W^T`` and its gradients on the tcgen05 GEMM of
+    ``ops/csrc/gemm_tcgen05.cu`` (bf16 operands, fp32 accumulation):
+
+    * forward  ``y[m, n]  = sum_k x[m, k] W[n, k]``          (bf16 out);
+    * backward ``dx[m, k] = sum_n dy[m, n] W^T[k, n]``        (bf16 out);
+    * backward ``dW[n, k] = sum_m dy^T[n, m] x^T[k, m]``      (fp32 out).
+
+    The kernel contracts over the contiguous dimension of both operands, so
+    the backward products read transposed copies (one copy kernel each)."""
+
+    @staticmethod
+    def forward(ctx, x2, w):
+        from .. import ops
+        y = torch.empty(x2.shape[0], w.shape[0], dtype=torch.bfloat16, device=x2.device)
+        ops.gemm_bf16(x2, w, y)
+        ctx.save_for_backward(x2, w)
+        return y
+
+    @staticmethod
+    def backward(ctx, gy):
+        from .. import ops
+        x2, w = ctx.saved_tensors
+        gy = gy.to(torch.bfloat16).contiguous()
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty_like(x2)
+            ops.gemm_bf16(gy, w.t().contiguous(), dx)
+        if ctx.needs_input_grad[1]:
+            dw32 = torch.empty(w.shape, dtype=torch.float32, device=w.device)
+            ops.gemm_partial(gy.t().contiguous(), x2.t().contiguous(), dw32, 1)
+            dw = dw32.to(w.dtype)
+        return dx, dw
+
+
+# tcgen05 linears for bf16 CUDA tensors (D3D_TC_LINEAR=0 uses torch's GEMM)
+TC_LINEAR = True
+
+
+class Linear(nn.Linear):
+    """``nn.Linear`` (same parameters and names) whose bf16 CUDA path runs on
+    the framework's tcgen05 GEMM, forward and backward; other devices and
+    dtypes use ``F.linear``."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        rows = x.numel() // max(1, self.in_features)
+        # TMA rows of every operand (forward and both backward products) must be
+        # multiples of 16 bytes: in, out features and token count multiples of 8
+        if (TC_LINEAR and x.is_cuda and x.dtype == torch.bfloat16 and self.weight.dtype == torch.bfloat16
+                and self.bias is None and self.in_features % 8 == 0 and self.out_features % 8 == 0
+                and rows > 0 and rows % 8 == 0):
+            import os
+            if os.environ.get("D3D_TC_LINEAR", "1") != "0":
+                x2 = x.reshape(-1, self.in_features).contiguous()
+                return _TcLinearFn.apply(x2, self.weight).view(*x.shape[:-1], self.out_features)
+        return F.linear(x, self.weight, self.bias)
+
+
 class Attention(nn.Module):
     def __init__(self, cfg: ModelConfig, layer_idx: int):
         super().__init__()
         self.cfg = cfg
         self.layer_idx = layer_idx
         h, d = cfg.hidden_size, cfg.head_dim
-        self.q_proj = nn.Linear(h, cfg.q_size, bias=cfg.attention_bias)
-        self.k_proj = nn.Linear(h, cfg.kv_size, bias=cfg.attention_bias)
-        self.v_proj = nn.Linear(h, cfg.kv_size, bias=cfg.attention_bias)
-        self.o_proj = nn.Linear(cfg.q_size, h, bias=cfg.attention_bias)
+        self.q_proj = Linear(h, cfg.q_size, bias=cfg.attention_bias)
+        self.k_proj = Linear(h, cfg.kv_size, bias=cfg.attention_bias)
+        self.v_proj = Linear(h, cfg.kv_size, bias=cfg.attention_bias)
+        self.o_proj = Linear(cfg.q_size, h, bias=cfg.attention_bias)
         self.q_norm = RMSNorm(d, cfg.rms_norm_eps)
         self.k_norm = RMSNorm(d, cfg.rms_norm_eps)
 
@@ -141,9 +199,9 @@ class Attention(nn.Module):
 class MLP(nn.Module):
     def __init__(self, cfg: ModelConfig):
         super().__init__()
-        self.gate_proj = nn.Linear(cfg.hidden_size, cfg.intermediate_size, bias=False)
-        self.up_proj = nn.Linear(cfg.hidden_size, cfg.intermediate_size, bias=False)
-        self.down_proj = nn.Linear(cfg.intermediate_size, cfg.hidden_size, bias=False)
+        self.gate_proj = Linear(cfg.hidden_size, cfg.intermediate_size, bias=False)
+        self.up_proj = Linear(cfg.hidden_size, cfg.intermediate_size, bias=False)
+        self.down_proj = Linear(cfg.intermediate_size, cfg.hidden_size, bias=False)
 
     def forward(self, x):
         return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))

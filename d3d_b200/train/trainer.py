@@ -153,6 +153,13 @@ def train(args) -> dict:
         teacher = _build(args.target_model, device, cdt, args.seed + 1).eval()
         for p in teacher.parameters():
             p.requires_grad_(False)
+        if device.type == "cuda" and os.environ.get("D3D_FAST_TEACHER", "1") != "0":
+            # the frozen teacher's forward runs on the sm_100a inference kernels
+            from .model_utils import FastTeacher
+            max_len = args.seq_len if args.data_path == "synthetic" else args.max_seq_len
+            module = teacher
+            teacher = FastTeacher(module, max(1, args.batch_size), max_len, device)
+            del module
     if args.freeze_embeddings:
         student.model.embed_tokens.weight.requires_grad_(False)
     if device.type == "cuda" and world > 1 and os.environ.get("D3D_FUSED_OPT", "1") != "0":

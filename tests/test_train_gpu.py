@@ -65,3 +65,44 @@ def test_trainer_step_bf16_gpu(tmp_path):
     r = train(a)
     losses = [x["loss"] for x in r["log"]]
     assert all(torch.isfinite(torch.tensor(l)) for l in losses)
+
+
+def test_fast_teacher_matches_module():
+    """The teacher forward on the inference kernels (batched, causal, every
+    position) tracks the PyTorch module's final-norm hidden states."""
+    import torch
+    from d3d_b200.config import tiny_target, qwen3_8b
+    from d3d_b200.models.qwen3 import build_model
+    from d3d_b200.train.model_utils import FastTeacher
+    dev = torch.device("cuda")
+    for cfg in (tiny_target(), qwen3_8b().replace(num_hidden_layers=2, vocab_size=4096)):
+        m = build_model(cfg, seed=4, dtype=torch.bfloat16, device=dev).eval()
+        ft = FastTeacher(m, max_batch=3, max_len=300, device=dev)
+        ids = torch.randint(0, cfg.vocab_size - 2, (3, 300), device=dev)
+        with torch.no_grad():
+            ref = m(ids).float()
+        out = ft(ids).float()
+        rel = (out - ref).norm() / ref.norm()
+        assert out.shape == ref.shape and rel < 3e-2, rel
+        assert torch.equal(ft(ids[:, :200]), ft(ids[:, :200]))   # padded shapes reuse buffers
+
+
+def test_tc_linear_forward_backward_matches_fp32():
+    """The tcgen05 linear of the training model: output and both gradients
+    against an fp32 PyTorch reference of the same bf16 inputs."""
+    import torch
+    from d3d_b200.models.qwen3 import Linear
+    torch.manual_seed(0)
+    for (m, k, n) in ((256, 2048, 4096), (72, 128, 384), (1024, 6144, 2048)):
+        lin = Linear(k, n, bias=False).cuda().to(torch.bfloat16)
+        x = (torch.randn(2, m // 2, k, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_(True)
+        gy = torch.randn(2, m // 2, n, device="cuda").to(torch.bfloat16)
+        y = lin(x)
+        y.backward(gy)
+        xf = x.detach().float().reshape(m, k)
+        wf = lin.weight.detach().float()
+        gf = gy.float().reshape(m, n)
+        for got, ref in ((y.float().reshape(m, n), xf @ wf.t()), (x.grad.float().reshape(m, k), gf @ wf),
+                         (lin.weight.grad.float(), gf.t() @ xf)):
+            rel = (got - ref).norm() / ref.norm()
+            assert rel < 1e-2, (m, k, n, rel.item())
