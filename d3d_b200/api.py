@@ -47,7 +47,7 @@ class D3DEngine:
         dp = draft_pages or max_seqs * (max_context + packed_q + page_size) // page_size + 8
         t = FastTarget(target_w, pages=tp, page_size=page_size, max_seqs=max_seqs,
                        max_context=max_context, use_graphs=use_graphs, device=device,
-                       temperature=decode.temperature, top_k=decode.target_top_k or decode.top_k,
+                       temperature=decode.temperature, top_k=decode.target_top_k,
                        top_p=decode.target_top_p)
         d = FastDraft(draft_w, pages=dp, page_size=page_size, max_seqs=max_seqs,
                       max_context=max_context, packed_q=packed_q, use_graphs=use_graphs,

@@ -199,9 +199,13 @@ class FastTarget(_FastModelBackend, TargetBackend):
         the same calls in the same order).
 
         ``temperature > 0`` turns on lossless speculative sampling against the
-        target's distribution truncated to its ``top_k`` (1..4) tokens -- the
-        fused top-k epilogue of the LM head gives exactly those logits, so no
-        logits are materialised -- then ``top_p``."""
+        target's distribution.  With ``top_k`` in 1..4 the fused top-k
+        epilogue of the LM head gives exactly the logits of the truncated
+        distribution (no logits are materialised); with ``top_k = 0`` (the
+        full vocabulary, the reference's default) or ``top_k > 4`` the LM-head
+        GEMM writes the fp32 logits of the verified rows (B*K rows, about 10
+        MB for a 16-token block) and the distribution is formed on the device
+        (temperature, top-k, then ``top_p``)."""
         super().__init__(weights, pages=pages, page_size=page_size, max_seqs=max_seqs,
                          max_context=max_context, extra_slots=64, batch_invariant=True,
                          use_graphs=use_graphs, device=device, stream=stream, tp=tp)
@@ -213,9 +217,12 @@ class FastTarget(_FastModelBackend, TargetBackend):
         self.time_verify = False
         self.temperature, self.top_k, self.top_p = float(temperature), int(top_k), float(top_p)
         self.sampled = not is_greedy(self.temperature)
+        self.full_vocab = self.sampled and not 1 <= self.top_k <= 4
+        # LM-head mode of sampled forwards: fused top-k (1..4) or full logits (-1)
+        self.lm_k = -1 if self.full_vocab else self.top_k
         if self.sampled:
-            if not 1 <= self.top_k <= 4:
-                raise ValueError("sampled verification on the kernels needs target top_k in 1..4")
+            if self.top_k < 0:
+                raise ValueError("target top_k must be >= 0")
             if tp is not None:
                 raise NotImplementedError("sampled verification with a tensor-parallel target")
             self.gen = torch.Generator(device=self.device)
@@ -241,10 +248,13 @@ class FastTarget(_FastModelBackend, TargetBackend):
         for s in seqs:
             n = len(s.prompt)
             rows = causal_rows(0, n).numpy()
-            b = self._prefill_one(s, rows, topk=self.top_k if self.sampled else 1,
+            b = self._prefill_one(s, rows, topk=self.lm_k if self.sampled else 1,
                                   reserve=self.max_context + 64)
             with torch.cuda.stream(self.stream):
-                if self.sampled:
+                if self.full_vocab:
+                    pr = self._probs_full(b.logits[n - 1:n])
+                    a = torch.multinomial(pr, 1, generator=self.gen)[0, 0]
+                elif self.sampled:
                     pr = self._probs(b.top_v[n - 1:n])
                     a = b.top_i[n - 1].gather(0, torch.multinomial(pr, 1, generator=self.gen)[0])[0]
                 else:
@@ -281,14 +291,35 @@ class FastTarget(_FastModelBackend, TargetBackend):
             sl = sl.masked_fill(remove, float("-inf"))
         return torch.softmax(sl, -1)
 
+    def _probs_full(self, logits: torch.Tensor) -> torch.Tensor:
+        """Sampling distribution over the whole vocabulary from fp32 logits
+        ``[..., V]``: temperature, then top-k (when > 0), then top-p."""
+        sl = logits.float() / self.temperature
+        if self.top_k > 0:
+            kth = sl.topk(self.top_k, dim=-1).values[..., -1:]
+            sl = sl.masked_fill(sl < kth, float("-inf"))
+        if self.top_p < 1.0:
+            srt, idx = sl.sort(dim=-1, descending=True)
+            pr = torch.softmax(srt, -1)
+            remove = pr.cumsum(-1) > self.top_p
+            remove[..., 1:] = remove[..., :-1].clone()
+            remove[..., 0] = False
+            sl = sl.scatter(-1, idx, srt.masked_fill(remove, float("-inf")))
+        return torch.softmax(sl, -1)
+
     def _sampled_accept(self, b: StepBuffers, a: dict, q) -> None:
         """Lossless acceptance of ``b``'s block against the verify forward's
-        top-k distribution (on the device; ``sampling.pq_accept_sparse``)."""
+        distribution (top-k truncated, or the full vocabulary from the
+        logits) on the device (``sampling.pq_accept_sparse``)."""
         B, K = b.B, b.Q
-        vals = b.top_v.view(B, K, -1)[..., :self.top_k]
-        ids = b.top_i.view(B, K, -1)[..., :self.top_k]
-        dense = torch.zeros(B, K, self.cfg.vocab_size, device=self.device)
-        dense.scatter_(-1, ids, self._probs(vals))
+        if self.full_vocab:
+            dense = self._probs_full(b.logits.view(B, K, -1))
+            b.top_i[:, 0].copy_(b.logits.argmax(-1))     # the posterior (argmax) the result reports
+        else:
+            vals = b.top_v.view(B, K, -1)[..., :self.top_k]
+            ids = b.top_i.view(B, K, -1)[..., :self.top_k]
+            dense = torch.zeros(B, K, self.cfg.vocab_size, device=self.device)
+            dense.scatter_(-1, ids, self._probs(vals))
         qi = q[0].to(self.device, non_blocking=True)
         qp = q[1].to(self.device, non_blocking=True)
         u = torch.rand(B, K - 1, generator=self.gen, device=self.device)
@@ -328,7 +359,7 @@ class FastTarget(_FastModelBackend, TargetBackend):
         sampled = self.sampled
         if sampled and q is None:     # single-token verify (AR): only the next token is sampled
             q = (torch.zeros(B, 0, 1, dtype=torch.long), torch.ones(B, 0, 1))
-        b = self.runner.buffers(B, K, self.top_k if sampled else 1)
+        b = self.runner.buffers(B, K, self.lm_k if sampled else 1)
         a = self._abufs(B, K)
         pref = np.fromiter((s.prefix for s in seqs), dtype=np.int64, count=B)
         pos = pref[:, None] + np.arange(K, dtype=np.int64)
@@ -350,7 +381,7 @@ class FastTarget(_FastModelBackend, TargetBackend):
             ev0.record(self.stream)
         tok = self.prof.dev_begin(f"verify_B{B}_K{K}", self.stream)
         if sampled:
-            self.graphs.run(("verify_s", B, K, self.top_k), b, lambda bb: self.runner.forward(bb))
+            self.graphs.run(("verify_s", B, K, self.lm_k), b, lambda bb: self.runner.forward(bb))
             with torch.cuda.stream(self.stream):
                 self._sampled_accept(b, a, q)
         else:

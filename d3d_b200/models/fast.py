@@ -280,6 +280,9 @@ class StepBuffers:
         self.ntiles = ntiles
         self.tv = torch.zeros(T * ntiles * kt, dtype=torch.float32, device=dev)
         self.ti = torch.zeros(T * ntiles * kt, dtype=torch.int32, device=dev)
+        # topk < 0: the LM head writes fp32 logits of every row (full-vocabulary
+        # sampling) instead of the fused top-k
+        self.logits = torch.zeros(T, cfg.vocab_size, dtype=torch.float32, device=dev) if topk < 0 else None
         self.top_v = torch.zeros(T, max(topk, 1), dtype=torch.float32, device=dev)
         self.top_i = torch.zeros(T, max(topk, 1), dtype=torch.int64, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -535,4 +538,9 @@ class FastRunner:
                 tp.merge_topk(xl, T, b.topk, b.top_v, b.top_i)
                 n += 3
         n += 2 if b.topk > 0 else 0
+        if b.topk < 0:
+            if tp is not None:
+                raise NotImplementedError("full-vocabulary logits with a tensor-parallel LM head")
+            E.gemm_partial(b.xn, w.lm_head.data, b.logits, 1, pl["lm_bt"], b.status, w.lm_head.n)
+            n += 1
         return n + (1 if cond is not None else 0)

@@ -112,3 +112,64 @@ def test_sampled_kernel_path(fast_pair):
         assert len(o.tokens) == 32 and all(0 <= t < 1024 for t in o.tokens)
     sar = eng2.generate_ar(prompts)["outputs"]
     assert all(len(t) == 32 for t in sar)
+
+
+def test_full_vocab_sampled_verify_is_lossless():
+    """Full-vocabulary sampled verification on the kernel path (target
+    top_k = 0): over many draws, the token emitted at the first drafted
+    position (the draft if accepted, else the residual correction) follows
+    the target distribution p exactly -- checked against p with a
+    chi-square bound -- whatever the proposal q."""
+    import math
+    import torch
+    from d3d_b200.config import tiny_target
+    from d3d_b200.engine.fast import FastTarget
+    from d3d_b200.models.fast import FastWeights
+    from d3d_b200.models.qwen3 import build_model
+    dev = torch.device("cuda")
+    tgt = FastTarget(FastWeights.from_module(build_model(tiny_target(), seed=0), dev), pages=64, max_seqs=2,
+                     max_context=128, device=dev, temperature=1.0, top_k=0, seed=3)
+    assert tgt.full_vocab
+    K, V = 4, tgt.cfg.vocab_size
+    b = tgt.runner.buffers(1, K, -1)
+    a = tgt._abufs(1, K)
+    g = torch.Generator(device=dev).manual_seed(0)
+    logits = torch.randn(K, V, device=dev, generator=g) * 2.0
+    b.logits.copy_(logits)
+    p0 = torch.softmax(logits[0], -1)
+    draft = int(p0.argsort(descending=True)[3])          # a plausible but not top token
+    b.ids.view(1, K).copy_(torch.tensor([[5, draft, 7, 9]], device=dev))
+    # proposal: q puts 0.6 on the draft, the rest on three other ids
+    q_ids = torch.tensor([[[draft, 11, 12, 13]] * (K - 1)])
+    q_p = torch.tensor([[[0.6, 0.2, 0.1, 0.1]] * (K - 1)])
+    n = 20000
+    out = torch.empty(n, dtype=torch.long)
+    for i in range(n):
+        tgt._sampled_accept(b, a, (q_ids, q_p))
+        commit, corr = int(a["commit"][0]), int(a["corr"][0])
+        out[i] = draft if commit >= 2 else corr
+    counts = torch.bincount(out, minlength=V).double()
+    exp = p0.double().cpu() * n
+    big = exp >= 20
+    chi = (((counts[big] - exp[big]) ** 2) / exp[big]).sum().item()
+    rest_o, rest_e = counts[~big].sum().item(), exp[~big].sum().item()
+    chi += (rest_o - rest_e) ** 2 / max(rest_e, 1e-9)
+    dof = int(big.sum()) + 1
+    assert chi < dof + 6 * math.sqrt(2 * dof), (chi, dof)
+
+
+def test_full_vocab_sampled_decoding_runs():
+    import torch
+    from d3d_b200.api import D3DEngine
+    from d3d_b200.config import tiny_drafter, tiny_target
+    from d3d_b200.engine.spec import DecodeConfig
+    from d3d_b200.models.qwen3 import build_model
+    dev = torch.device("cuda")
+    eng = D3DEngine.from_modules(build_model(tiny_target(), seed=0, device=dev),
+                                 build_model(tiny_drafter(), seed=1, device=dev),
+                                 DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=24, ignore_eos=True,
+                                              temperature=0.8, top_k=4, target_top_k=0),
+                                 max_seqs=2, max_context=256)
+    assert eng.target.full_vocab
+    out = eng.generate([[3, 4, 5, 6, 7, 8, 9, 10]])["outputs"][0]
+    assert len(out.tokens) == 24 and all(0 <= t < tiny_target().vocab_size for t in out.tokens)
