@@ -298,16 +298,18 @@ class FastRunner:
         self.kv = kv
         self.device = device
         self.tp = tp                    # d3d_b200.parallel.tp.TPGroup or None
-        # Key chunk per attention CTA.  Fine chunks keep >100 CTAs busy at decode
-        # sizes (one 64-key tile each for the batch-invariant target); the
-        # drafter's packed forward has many query rows, so it takes 256.
+        # Key chunk per attention CTA (a fixed absolute split of the keys, so a
+        # row's attention does not depend on the batch it is computed in).
         # D3D_TARGET_CHUNK / D3D_DRAFT_CHUNK override (0 = one chunk over the
         # whole context, no combine pass); the target's chunk must be the same
         # for every forward of a runner (AR and verify), which it is.
         env = os.environ.get("D3D_TARGET_CHUNK" if batch_invariant else "D3D_DRAFT_CHUNK")
         if decode_chunk is None and env is not None:
             decode_chunk = int(env) if int(env) > 0 else -1
-        self.decode_chunk = decode_chunk or (64 if batch_invariant else 256)
+        # measured best on B200 (in-graph forward, ~1000-token contexts): 128 keys
+        # per CTA for the target's verify / AR forwards, 512 for the drafter's
+        # packed forward
+        self.decode_chunk = decode_chunk or (128 if batch_invariant else 512)
         self.max_context = max_context
         self.batch_invariant = batch_invariant
         c = self.cfg
