@@ -17,12 +17,12 @@ import json
 import torch
 
 FAMILIES = {
-    "gemm": ("gemm_partial", "gemm_bf16", "gemm_swiglu"),
+    "gemm": ("gemm_partial", "gemm_bf16", "gemm_swiglu", "gemm_partial_fin"),
     "lm_head": ("gemm_topk", "topk_merge"),
     "attention": ("attention",),
-    "add_rmsnorm": ("add_rmsnorm",),
+    "add_rmsnorm": ("add_rmsnorm", "tile_sumsq"),
     "qkv_rope_kv": ("qkv_rope_kv",),
-    "swiglu": ("swiglu",),
+    "swiglu": ("swiglu", "swiglu_rowscale"),
 }
 
 

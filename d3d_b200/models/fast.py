@@ -60,6 +60,29 @@ class FastWeights:
         self.final_norm = final_norm
         self.lm_head = lm_head
         self.cond_proj = cond_proj
+        # True once the input / post-attention RMSNorm weights are folded into
+        # the qkv / gate|up weights (column scale); see fold_norms
+        self.folded = False
+
+    @torch.no_grad()
+    def fold_norms(self) -> "FastWeights":
+        """Fold each layer's RMSNorm weights into the GEMM that consumes the
+        normalised activations (in place, idempotent):
+        ``rmsnorm(x) * g @ W^T = r(x) * (x @ (W diag(g))^T)``, so the fused
+        forward feeds the residual stream itself to the qkv and gate|up GEMMs
+        and applies the per-row scale ``r`` in their reduce kernels.  Layers
+        whose norm weights are all ones (random init) need no repacking."""
+        if self.folded:
+            return self
+        for L in self.layers:
+            for attr, g in (("qkv", L.in_norm), ("gate_up", L.post_norm)):
+                if bool((g == 1).all()):
+                    continue
+                w = getattr(L, attr)
+                full = w.unpack().float() * g.float()[None, :]
+                setattr(L, attr, ops.pack_weight(full.to(torch.bfloat16)))   # row order kept (interleaved)
+        self.folded = True
+        return self
 
     @classmethod
     @torch.no_grad()
@@ -225,7 +248,7 @@ class StepBuffers:
     """Static device inputs/outputs of one forward shape (B sequences x Q tokens)."""
 
     def __init__(self, cfg: ModelConfig, B: int, Q: int, topk: int, n_chunks: int,
-                 splits: Dict[str, int], device="cuda", with_hidden_copy: bool = False):
+                 splits: Dict[str, int], device="cuda", with_hidden_copy: bool = False, fused_norm: bool = False):
         T = B * Q
         self.B, self.Q, self.T, self.topk, self.n_chunks = B, Q, T, topk, n_chunks
         dev = device
@@ -267,8 +290,15 @@ class StepBuffers:
         width = dict(qkv=cfg.q_size + 2 * cfg.kv_size, o=h, gate_up=2 * cfg.intermediate_size, down=h)
         pl = {g: (v if isinstance(v, tuple) else (0, v, False)) for g, v in splits.items() if g in width}
         # fp32 split-K partials for the GEMMs that reduce partials; direct ones write bf16
-        nmax = max([pl[g][1] * width[g] for g in width if not pl[g][2]] + [1])
+        nmax = max([pl[g][1] * width[g] for g in width if fused_norm or not pl[g][2]] + [1])
         self.part = torch.zeros(nmax * T, dtype=torch.float32, device=dev)
+        # fused norms: per-tile row sums of squares of the residual stream after
+        # attention (ss_post) and after the MLP / embedding (ss_in), and the
+        # split-K tickets of the GEMMs that reduce into the residual
+        ht = math.ceil(h / 128)
+        self.ss_in = torch.zeros(ht * T if fused_norm else 1, dtype=torch.float32, device=dev)
+        self.ss_post = torch.zeros(ht * T if fused_norm else 1, dtype=torch.float32, device=dev)
+        self.ticket = torch.zeros(ht * math.ceil(T / 16) if fused_norm else 1, dtype=torch.int32, device=dev)
         self.qkv = torch.zeros(T if pl["qkv"][2] else 1, width["qkv"], dtype=torch.bfloat16, device=dev)
         self.att_o = torch.zeros(n_chunks * T * cfg.num_attention_heads * d if n_chunks > 1 else 1,
                                  dtype=torch.float32, device=dev)
@@ -312,6 +342,14 @@ class FastRunner:
         self.decode_chunk = decode_chunk or (128 if batch_invariant else 512)
         self.max_context = max_context
         self.batch_invariant = batch_invariant
+        # residual + RMSNorm fused into the o / down GEMMs and the qkv / SwiGLU
+        # reduce kernels (D3D_FUSE_NORM=0: separate add+RMSNorm kernels);
+        # tensor-parallel runners keep the exchange-fused norm
+        self.fused_norm = tp is None and os.environ.get("D3D_FUSE_NORM", "1") != "0"
+        if self.fused_norm:
+            weights.fold_norms()
+        elif weights.folded:
+            raise ValueError("weights with folded norms need the fused-norm forward")
         c = self.cfg
         self.inv_freq = (1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, dtype=torch.float32)
                                                  / c.head_dim))).to(device)
@@ -448,11 +486,52 @@ class FastRunner:
             T = B * Q
             chunk = self.chunk_for(prefill)
             nch = max(1, math.ceil(self.max_context / chunk))
-            b = StepBuffers(self.cfg, B, Q, topk, nch, self.plan(T, tune=not prefill), self.device)
+            b = StepBuffers(self.cfg, B, Q, topk, nch, self.plan(T, tune=not prefill), self.device,
+                            fused_norm=self.fused_norm)
             b.bt_view = torch.zeros(B, self.kv.max_pages_per_seq, dtype=torch.int32, device=self.device)
             b.chunk = chunk
             self._bufs[key] = b
         return b
+
+    def _layers_fused(self, b: StepBuffers, E, hq: int, hkv: int, d: int, B: int, Q: int, pl, eps: float) -> int:
+        """The decoder layers with the residual add and RMSNorm fused into the
+        GEMMs (weights from :meth:`FastWeights.fold_norms`): the o / down
+        GEMMs reduce their split-K partials into the residual stream ``x``
+        inside the kernel and leave per-tile row sums of squares; the qkv /
+        SwiGLU reduce kernels apply the RMSNorm row scale.  The last layer's
+        down projection ends in the final add + RMSNorm (``xn``, the hidden
+        state the LM head and the handoffs read).  Returns the launch count."""
+        w, H = self.w, self.cfg.hidden_size
+        n = 0
+        last = len(w.layers) - 1
+        for li, L in enumerate(w.layers):
+            gbt, s, direct = pl["qkv"]
+            if direct:
+                E.gemm_bf16(b.x, L.qkv.data, b.qkv, None, gbt, b.status, L.qkv.n)
+                E.qkv_rope_kv(None, b.qkv, 1, L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
+                              b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps, b.status, b.ss_in, H)
+            else:
+                E.gemm_partial(b.x, L.qkv.data, b.part, s, gbt, b.status, L.qkv.n)
+                E.qkv_rope_kv(b.part, None, s, L.q_norm, L.k_norm, self.inv_freq, b.pos, b.slots,
+                              b.q, self.kv.k[li], self.kv.v[li], hq, hkv, d, eps, b.status, b.ss_in, H)
+            E.attention(b.q, self.kv.k[li], self.kv.v[li], b.bt_view, b.rows, b.kv_end, B, Q, hq, hkv,
+                        self.kv.page_size, self.scale, b.chunk, b.n_chunks,
+                        b.att_o if b.n_chunks > 1 else None, b.att_ml if b.n_chunks > 1 else None,
+                        b.attn, self.batch_invariant, b.status)
+            gbt, s, _ = pl["o"]
+            E.gemm_partial_fin(b.attn, L.o.data, b.part, s, gbt, b.status, L.o.n, b.x, b.ss_post, b.ticket)
+            gbt, s, _ = pl["gate_up"]
+            E.gemm_partial(b.x, L.gate_up.data, b.part, s, gbt, b.status, L.gate_up.n)
+            E.swiglu_rowscale(b.part, s, b.h, b.ss_post, H, eps)
+            gbt, s, _ = pl["down"]
+            if li < last:
+                E.gemm_partial_fin(b.h, L.down.data, b.part, s, gbt, b.status, L.down.n, b.x, b.ss_in, b.ticket)
+                n += 8 + (1 if b.n_chunks > 1 else 0)
+            else:
+                E.gemm_partial(b.h, L.down.data, b.part, s, gbt, b.status, L.down.n)
+                E.add_rmsnorm(b.part, s, b.x, w.final_norm, b.xn, eps)
+                n += 9 + (1 if b.n_chunks > 1 else 0)
+        return n
 
     def chunk_for(self, prefill: bool) -> int:
         if prefill or self.decode_chunk < 0:
@@ -475,7 +554,10 @@ class FastRunner:
             ops.gemm_bf16(b.cond, w.cond_proj, b.cond_h, None, ops.bt_for(B), b.status)
             cond = b.cond_h
         E.embed(b.ids, w.embed, cond, b.cond_rows if cond is not None else None, Q, b.x, b.status)
-        E.add_rmsnorm(None, 1, b.x, w.layers[0].in_norm, b.xn, c.rms_norm_eps)
+        if self.fused_norm:
+            E.tile_sumsq(b.x, b.ss_in)
+        else:
+            E.add_rmsnorm(None, 1, b.x, w.layers[0].in_norm, b.xn, c.rms_norm_eps)
         torch.index_select(self.kv.block_table, 0, b.seq_rows, out=b.bt_view)
         n = 3
         eps = c.rms_norm_eps
@@ -483,7 +565,9 @@ class FastRunner:
         if tp is not None:
             tp.bump()
             n += 1
-        for li, L in enumerate(w.layers):
+        if self.fused_norm:
+            n += self._layers_fused(b, E, hq, hkv, d, B, Q, pl, eps)
+        for li, L in enumerate(w.layers if not self.fused_norm else []):
             gbt, s, direct = pl["qkv"]
             if direct:
                 E.gemm_bf16(b.xn, L.qkv.data, b.qkv, None, gbt, b.status, L.qkv.n)

@@ -73,6 +73,35 @@ void gemm_partial(Tensor x, Tensor w, Tensor out, int64_t splits, int64_t bt, c1
   d3d::gemm_launch(a, cur_stream());
 }
 
+// fp32 split-K partials reduced inside the GEMM: the last unit of each output
+// tile adds the split sum to the bf16 residual ``resid`` [M, N] in place and
+// writes the tile's per-row sums of squares ``sumsq`` [ceil(N/128), M];
+// ``ticket`` is an int32 [>= ceil(N/128) * ceil(M/bt)] buffer of zeros.
+void gemm_partial_fin(Tensor x, Tensor w, Tensor part, int64_t splits, int64_t bt, c10::optional<Tensor> status,
+                      int64_t wn, Tensor resid, Tensor sumsq, Tensor ticket) {
+  const c10::cuda::CUDAGuard g(x.device());
+  auto a = base_args(x, w, static_cast<int>(bt), status, wn);
+  CHECK_DT(part, torch::kFloat32);
+  CHECK_CONTIG(part);
+  CHECK_DT(resid, torch::kBFloat16);
+  CHECK_DT(sumsq, torch::kFloat32);
+  CHECK_DT(ticket, torch::kInt32);
+  TORCH_CHECK(part.numel() >= splits * a.M * a.N, "gemm_partial_fin: partials too small");
+  TORCH_CHECK(resid.size(0) == a.M && resid.size(1) == a.N && resid.stride(1) == 1, "gemm_partial_fin: residual");
+  const int ntn = (a.N + 127) / 128, ntm = (a.M + static_cast<int>(bt) - 1) / static_cast<int>(bt);
+  TORCH_CHECK(sumsq.numel() >= static_cast<int64_t>(ntn) * a.M, "gemm_partial_fin: sumsq too small");
+  TORCH_CHECK(ticket.numel() >= static_cast<int64_t>(ntn) * ntm, "gemm_partial_fin: ticket too small");
+  a.mode = 4;
+  a.splits = static_cast<int>(splits);
+  a.out_f32 = part.data_ptr<float>();
+  a.fin_x = bf(resid);
+  a.fin_ldx = static_cast<int>(resid.stride(0));
+  a.fin_sumsq = sumsq.data_ptr<float>();
+  a.fin_ticket = reinterpret_cast<unsigned int*>(ticket.data_ptr<int>());
+  if (a.M == 0) return;
+  d3d::gemm_launch(a, cur_stream());
+}
+
 void gemm_bf16(Tensor x, Tensor w, Tensor out, c10::optional<Tensor> residual, int64_t bt,
                c10::optional<Tensor> status, int64_t wn) {
   const c10::cuda::CUDAGuard g(x.device());
@@ -142,9 +171,31 @@ void swiglu(Tensor part, int64_t nsplit, Tensor h, bool interleaved) {
               static_cast<int>(h.size(1)), interleaved, cur_stream());
 }
 
+void swiglu_rowscale(Tensor part, int64_t nsplit, Tensor h, Tensor rsq, int64_t rsq_n, double eps) {
+  const c10::cuda::CUDAGuard g(h.device());
+  CHECK_CONTIG(h);
+  CHECK_DT(part, torch::kFloat32);
+  CHECK_DT(rsq, torch::kFloat32);
+  const int M = static_cast<int>(h.size(0));
+  const int tiles = static_cast<int>((rsq_n + 127) / 128);
+  TORCH_CHECK(rsq.numel() >= static_cast<int64_t>(tiles) * M, "swiglu_rowscale: sums of squares too small");
+  d3d::swiglu_rowscale(part.data_ptr<float>(), static_cast<int>(nsplit), bf(h), M, static_cast<int>(h.size(1)),
+                       rsq.data_ptr<float>(), tiles, static_cast<int>(rsq_n), static_cast<float>(eps), cur_stream());
+}
+
+void tile_sumsq(Tensor x, Tensor out) {
+  const c10::cuda::CUDAGuard g(x.device());
+  CHECK_CONTIG(x);
+  CHECK_DT(out, torch::kFloat32);
+  const int M = static_cast<int>(x.size(0)), N = static_cast<int>(x.size(1));
+  TORCH_CHECK(out.numel() >= static_cast<int64_t>((N + 127) / 128) * M, "tile_sumsq: out too small");
+  d3d::tile_sumsq(cbf(x), M, N, out.data_ptr<float>(), cur_stream());
+}
+
 void qkv_rope_kv(c10::optional<Tensor> part, c10::optional<Tensor> y, int64_t nsplit, Tensor q_norm, Tensor k_norm,
                  Tensor inv_freq, Tensor positions, Tensor slots, Tensor q_out, Tensor k_cache, Tensor v_cache,
-                 int64_t Hq, int64_t Hkv, int64_t D, double eps, c10::optional<Tensor> status) {
+                 int64_t Hq, int64_t Hkv, int64_t D, double eps, c10::optional<Tensor> status,
+                 c10::optional<Tensor> rsq, int64_t rsq_n) {
   const c10::cuda::CUDAGuard g(q_out.device());
   CHECK_DT(positions, torch::kInt64);
   CHECK_DT(slots, torch::kInt64);
@@ -170,6 +221,13 @@ void qkv_rope_kv(c10::optional<Tensor> part, c10::optional<Tensor> y, int64_t ns
   a.eps = static_cast<float>(eps);
   a.num_slots = k_cache.size(0);
   a.status = status_ptr(status);
+  if (rsq) {
+    CHECK_DT(*rsq, torch::kFloat32);
+    a.rsq = rsq->data_ptr<float>();
+    a.rsq_n = static_cast<int>(rsq_n);
+    a.rsq_tiles = static_cast<int>((rsq_n + 127) / 128);
+    TORCH_CHECK(rsq->numel() >= static_cast<int64_t>(a.rsq_tiles) * a.M, "qkv_rope_kv: sums of squares too small");
+  }
   d3d::qkv_rope_kv(a, cur_stream());
 }
 
@@ -558,12 +616,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_rope_kv", &qkv_rope_kv, py::arg("part"), py::arg("y"), py::arg("nsplit"), py::arg("q_norm"),
         py::arg("k_norm"), py::arg("inv_freq"), py::arg("positions"), py::arg("slots"), py::arg("q_out"),
         py::arg("k_cache"), py::arg("v_cache"), py::arg("Hq"), py::arg("Hkv"), py::arg("D"), py::arg("eps"),
-        py::arg("status") = py::none());
+        py::arg("status") = py::none(), py::arg("rsq") = py::none(), py::arg("rsq_n") = 0);
+  m.def("swiglu_rowscale", &swiglu_rowscale);
+  m.def("tile_sumsq", &tile_sumsq);
   m.def("embed", &embed, py::arg("ids"), py::arg("table"), py::arg("cond"), py::arg("cond_rows"), py::arg("q_len"),
         py::arg("out"), py::arg("status") = py::none());
   m.def("topk_merge", &topk_merge);
   m.def("greedy_accept", &greedy_accept);
   m.def("attention_uses_tc", &attention_uses_tc);
+  m.def("gemm_partial_fin", &gemm_partial_fin);
   m.def("attention", &attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
         py::arg("rows"), py::arg("kv_end"), py::arg("B"), py::arg("q_len"), py::arg("Hq"), py::arg("Hkv"),
         py::arg("page_size"), py::arg("scale"), py::arg("chunk"), py::arg("n_chunks"), py::arg("part_o"),

@@ -171,6 +171,78 @@ void add_rmsnorm(const float* part, int nsplit, __nv_bfloat16* residual, const _
 // (ops.pack_gate_up): h[i] takes gate column 128t + 32w + l and up column
 // 128t + 32w + 16 + l for i = 64t + 16w + l.  Four consecutive columns per
 // thread (they stay consecutive under the interleave).
+// RMSNorm row scale from per-tile sums of squares (tiles of 128 columns):
+// r = rsqrt(sum_t rsq[t][m] / n + eps).  Every lane of the calling warp gets
+// the same value; the summation order (lane-strided, then a butterfly) is
+// fixed, so a row's scale does not depend on the other rows of the launch.
+__device__ __forceinline__ float row_scale(const float* rsq, int tiles, int M, int m, int n, float eps) {
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+  for (int t = lane; t < tiles; t += 32) s += rsq[static_cast<size_t>(t) * M + m];
+  s = warp_sum(s);
+  return rsqrtf(s / n + eps);
+}
+
+template <int S>
+__global__ void __launch_bounds__(256)
+    swiglu_rowscale_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* __restrict__ h, int M, int I,
+                           const float* __restrict__ rsq, int rsq_tiles, int rsq_n, float eps) {
+  griddep_launch();
+  griddep_wait();
+  const int m = blockIdx.y;
+  const float r = row_scale(rsq, rsq_tiles, M, m, rsq_n, eps);
+  const size_t stride = static_cast<size_t>(M) * 2 * I;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4; i < I; i += gridDim.x * blockDim.x * 4) {
+    const size_t gcol = static_cast<size_t>(i / 64) * 128 + ((i % 64) / 16) * 32 + (i % 16);
+    const float4 g4 = load_split_sum4<S>(part, nsplit, stride, static_cast<size_t>(m) * 2 * I + gcol);
+    const float4 u4 = load_split_sum4<S>(part, nsplit, stride, static_cast<size_t>(m) * 2 * I + gcol + 16);
+    const float g[4] = {g4.x, g4.y, g4.z, g4.w}, u[4] = {u4.x, u4.y, u4.z, u4.w};
+    float o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gb = bf16r(g[j] * r);
+      const float sl = bf16r(gb / (1.f + expf(-gb)));
+      o[j] = sl * bf16r(u[j] * r);
+    }
+    st_bf16x4(h + static_cast<size_t>(m) * I + i, o);
+  }
+}
+
+void swiglu_rowscale(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, const float* rsq, int rsq_tiles,
+                     int rsq_n, float eps, cudaStream_t st) {
+  if (M == 0) return;
+  if (I % 64) throw std::runtime_error("swiglu_rowscale: interleaved gate|up needs I % 64 == 0");
+  if (nsplit > MAX_SPLITS) throw std::runtime_error("swiglu_rowscale: too many splits");
+  const int bx = (I / 4 + 255) / 256;
+  D3D_SPLIT_DISPATCH(nsplit, launch_pdl(swiglu_rowscale_kernel<S>, dim3(bx, M), dim3(256), 0, st, part, nsplit, h,
+                                        M, I, rsq, rsq_tiles, rsq_n, eps));
+}
+
+__global__ void tile_sumsq_kernel(const __nv_bfloat16* __restrict__ x, int M, int N, float* __restrict__ out) {
+  griddep_launch();
+  griddep_wait();
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int tiles = (N + 127) / 128;
+  if (w >= tiles * M) return;
+  const int t = w / M, m = w % M;
+  float s = 0.f;
+  for (int j = 0; j < 4; ++j) {
+    const int n = t * 128 + j * 32 + lane;
+    if (n < N) {
+      const float v = __bfloat162float(x[static_cast<size_t>(m) * N + n]);
+      s += v * v;
+    }
+  }
+  s = warp_sum(s);
+  if (lane == 0) out[static_cast<size_t>(t) * M + m] = s;
+}
+
+void tile_sumsq(const __nv_bfloat16* x, int M, int N, float* out, cudaStream_t st) {
+  if (M == 0) return;
+  const int warps = ((N + 127) / 128) * M;
+  launch_pdl(tile_sumsq_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, st, x, M, N, out);
+}
+
 template <int S>
 __global__ void __launch_bounds__(256, 2)
     swiglu_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* __restrict__ h, int M, int I,
@@ -226,20 +298,25 @@ __global__ void qkv_rope_kv_kernel(QkvRopeArgs a) {
   const size_t stride = static_cast<size_t>(a.M) * N;
   float x[E];
   const size_t off0 = static_cast<size_t>(m) * N + h * D + lane * E;
+  // RMSNorm scale of the GEMM input row when its norm weight is folded into qkv
+  const float rs = a.rsq ? row_scale(a.rsq, a.rsq_tiles, a.M, m, a.rsq_n, a.eps) : 1.f;
   if constexpr (E == 4) {
     if (a.part) {
       const float4 s4 = load_split_sum4<S>(a.part, a.nsplit, stride, off0);
-      x[0] = bf16r(s4.x);
-      x[1] = bf16r(s4.y);
-      x[2] = bf16r(s4.z);
-      x[3] = bf16r(s4.w);
+      x[0] = bf16r(s4.x * rs);
+      x[1] = bf16r(s4.y * rs);
+      x[2] = bf16r(s4.z * rs);
+      x[3] = bf16r(s4.w * rs);
     } else {
       ld_bf16x4(a.y + off0, x);
+#pragma unroll
+      for (int e = 0; e < E; ++e) x[e] = a.rsq ? bf16r(x[e] * rs) : x[e];
     }
   } else {
 #pragma unroll
     for (int e = 0; e < E; ++e)
-      x[e] = bf16r(a.part ? load_split_sum<S>(a.part, a.nsplit, stride, off0 + e) : __bfloat162float(a.y[off0 + e]));
+      x[e] = bf16r((a.part ? load_split_sum<S>(a.part, a.nsplit, stride, off0 + e) : __bfloat162float(a.y[off0 + e])) *
+                   rs);
   }
   const int64_t slot = a.slots[m];
   if (h >= a.Hq && !D3D_IN_BOUNDS(slot, a.num_slots, a.status)) return;   // debug builds only

@@ -31,13 +31,21 @@ struct GemmParams {
   int64_t* tp_flags[8];
   int64_t* tp_epoch;
   unsigned int* tp_ticket;
+  // MODE 4 (split-K partials + in-kernel finalize): the last unit of an output
+  // tile to finish reduces the splits in split order, adds them to the bf16
+  // residual fin_x (in place) and writes the tile's per-row sum of squares
+  __nv_bfloat16* fin_x;
+  int fin_ldx;
+  float* fin_sumsq;          // [ceil(N/128)][M]
+  unsigned int* fin_ticket;  // [ceil(N/128) * ceil(M/bt)], zero, reset after use
 };
 
 struct GemmArgs {
   const __nv_bfloat16* x;  // [M, K] activations (row stride ldx elements)
   const __nv_bfloat16* w;  // [N, K] weights (row stride ldw elements)
   int M, N, K, ldx, ldw;
-  int mode;      // 0 fp32 split-K partials, 1 bf16 (+residual), 2 fused top-k, 3 SwiGLU (interleaved gate|up)
+  int mode;      // 0 fp32 split-K partials, 1 bf16 (+residual), 2 fused top-k, 3 SwiGLU (interleaved gate|up),
+                 // 4 fp32 partials + in-kernel split reduce into a residual (+ row sums of squares)
   int splits;    // split-K factor (mode 0 only)
   int bt;        // token tile (MMA N), multiple of 16 in [16, 256]
   int topk;      // mode 2: k <= 4
@@ -58,6 +66,10 @@ struct GemmArgs {
   int64_t* tp_flags[8];
   int64_t* tp_epoch;
   unsigned int* tp_ticket;
+  __nv_bfloat16* fin_x;        // mode 4: residual [M, fin_ldx] updated in place
+  int fin_ldx;
+  float* fin_sumsq;            // mode 4: [ceil(N/128)][M] per-tile row sums of squares
+  unsigned int* fin_ticket;    // mode 4: [ceil(N/128) * ceil(M/bt)] zeroed counters
 };
 
 void gemm_launch(const GemmArgs& a, cudaStream_t stream);

@@ -90,15 +90,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
   const int marea = MODE == 2 ? 4 * bt * KT : 0;
   float* mval = reinterpret_cast<float*>(smem + stages * stage_bytes);
   int* midx = reinterpret_cast<int*>(mval + 2 * marea);
-  uint64_t* full = reinterpret_cast<uint64_t*>(midx + 2 * marea);
+  // MODE 4: the four epilogue warps' per-column partial sums of squares [4][bt]
+  float* fss = reinterpret_cast<float*>(midx + 2 * marea);
+  uint64_t* full = reinterpret_cast<uint64_t*>(fss + (MODE == 4 ? 4 * bt : 0));
   uint64_t* empty = full + stages;
   uint64_t* accf = empty + stages;  // [2] accumulator ready for the epilogue
   uint64_t* acce = accf + 2;        // [2] accumulator drained by the epilogue
   uint64_t* mfull = acce + 2;       // [2] MODE 2: the four warps' candidates are in
   uint64_t* mempty = mfull + 2;     // [2] MODE 2: merge area read, may be rewritten
   uint64_t* done = mempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* finb = done + 1;        // MODE 4: the four epilogue warps meet here (bounded waits)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(finb + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort [1] issued [2] consumed
+                                                                         // [3] MODE 4: this CTA finalizes
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nkb = (p.K + GBK - 1) / GBK;
@@ -123,7 +127,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
       mbar_init(&mempty[a], 1);
     }
     mbar_init(done, 1);
-    flags[0] = flags[1] = flags[2] = 0;
+    mbar_init(finb, 4);
+    flags[0] = flags[1] = flags[2] = flags[3] = 0;
     fence_mbar_init();
     prefetch_tensormap(&tmW);
     prefetch_tensormap(&tmX);
@@ -242,6 +247,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
     const int q = warp & 3;           // TMEM lane quadrant of this warp
     const int row = q * 32 + lane;    // weight row within the tile
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    uint32_t fph = 0;   // MODE 4: completed phases of finb
+    // the four epilogue warps meet (lane 0 of each arrives; every lane waits,
+    // bounded); false when the wait ran out or the CTA aborted
+    auto fsync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(finb);
+      bool w = mbar_wait(finb, fph & 1, lim);
+      ++fph;
+      w = __shfl_sync(0xffffffffu, w && !flags[0], 0);
+      if (!w && lane == 0 && !flags[0]) fail(ERR_TIMEOUT_EPILOGUE);
+      return w;
+    };
     int ti = 0;
     for (int t = blockIdx.x; t < units; t += gridDim.x, ++ti) {
       const UnitCoord u = unit_coord(t, ntm, nsplit, nkb);
@@ -256,14 +273,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
       const int n0 = u.n_t * GBN, m0 = u.m_t * bt;
       const int n = n0 + row;
       const bool n_ok = n < p.N;
-      if constexpr (MODE == 0 || MODE == 1 || MODE == 3) {
+      if constexpr (MODE == 0 || MODE == 1 || MODE == 3 || MODE == 4) {
         // MODE 3 output column of this lane (lanes 0..15 of each warp write)
         const int hcol = u.n_t * (GBN / 2) + q * 16 + (lane & 15);
         const int cols = min(bt, p.M - m0);
         for (int c = 0; c < cols; c += 16) {
           float v[16];
           tmem_ld16(tacc + c, v);
-          if constexpr (MODE == 0) {
+          if constexpr (MODE == 0 || MODE == 4) {
             if (n_ok && p.tp == 0) {
               float* base = p.out_f32 + static_cast<size_t>(u.split) * p.M * p.N;
 #pragma unroll
@@ -316,6 +333,45 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acce[a]);
+        if constexpr (MODE == 4) {
+          // ---- in-kernel split-K reduction: the last unit of this output
+          // tile to store its partials sums all splits (split order), adds
+          // them to the residual (rounded like two bf16 ops) and writes the
+          // tile's per-row sum of squares of the new residual.
+          __threadfence();
+          if (!fsync()) break;
+          const int tile = u.n_t * ntm + u.m_t;
+          if (threadIdx.x == 64) {
+            const unsigned int tk = atomicAdd(p.fin_ticket + tile, 1u);
+            flags[3] = (tk == static_cast<unsigned int>(nsplit - 1)) ? 1 : 0;
+          }
+          if (!fsync()) break;
+          if (flags[3]) {
+            __threadfence();
+            const size_t sstride = static_cast<size_t>(p.M) * p.N;
+            for (int c = 0; c < cols; ++c) {
+              const int m = m0 + c;
+              float ss = 0.f;
+              if (n_ok) {
+                const float* src = p.out_f32 + static_cast<size_t>(m) * p.N + n;
+                float y = 0.f;
+                for (int sp = 0; sp < nsplit; ++sp) y += __ldcg(src + sp * sstride);
+                __nv_bfloat16* xp = p.fin_x + static_cast<size_t>(m) * p.fin_ldx + n;
+                const float xv = bf16r(__bfloat162float(*xp) + bf16r(y));
+                *xp = __float2bfloat16(xv);
+                ss = xv * xv;
+              }
+              ss = warp_sum(ss);
+              if (lane == 0) fss[q * bt + c] = ss;
+            }
+            if (!fsync()) break;
+            for (int c = threadIdx.x - 64; c < cols; c += 128)
+              p.fin_sumsq[static_cast<size_t>(u.n_t) * p.M + m0 + c] =
+                  ((fss[c] + fss[bt + c]) + fss[2 * bt + c]) + fss[3 * bt + c];
+            if (threadIdx.x == 64) p.fin_ticket[tile] = 0u;   // ready for the next launch
+            if (!fsync()) break;                              // fss may be rewritten by the next tile
+          }
+        }
       } else {
         // ------------------------------------------ MODE 2: per-tile top-KT
         // Per token column: KT rounds of a warp max (redux.sync on an
@@ -515,7 +571,7 @@ int gemm_stages(int bt) { return stages_for(bt, 0); }
 
 static size_t smem_bytes(int bt, int stages, int reserve) {
   const int stage_bytes = A_TILE_BYTES + bt * GBK * 2;
-  return 1024 + static_cast<size_t>(stages) * stage_bytes + reserve + (2 * stages + 9) * 8 + 32;
+  return 1024 + static_cast<size_t>(stages) * stage_bytes + reserve + (2 * stages + 10) * 8 + 48;
 }
 
 size_t gemm_smem_bytes(int bt, int stages) { return smem_bytes(bt, stages, 0); }
@@ -558,7 +614,9 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   const int nkb = (a.K + GBK - 1) / GBK;
   if (a.splits < 1 || a.splits > nkb || a.splits > 16)
     throw std::runtime_error("gemm: splits must be in [1, min(16, K/64)]");
-  if (a.mode != 0 && a.splits != 1) throw std::runtime_error("gemm: split-K needs fp32 partial mode");
+  if (a.mode != 0 && a.mode != 4 && a.splits != 1) throw std::runtime_error("gemm: split-K needs fp32 partial mode");
+  if (a.mode == 4 && (!a.fin_x || !a.fin_sumsq || !a.fin_ticket || a.out_f32 == nullptr))
+    throw std::runtime_error("gemm: mode 4 needs partials, residual, sums-of-squares and tickets");
   CUtensorMap tw, tx;
   if (a.w_packed) {
     const uint64_t rows = static_cast<uint64_t>((a.N + GBN - 1) / GBN) * nkb * GBN;
@@ -569,7 +627,7 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   make_tmap_bf16_2d(&tx, a.x, a.K, a.M, a.ldx, GBK, a.bt > 256 ? a.bt / 2 : a.bt);
   const int kt = a.mode == 2 ? (a.topk <= 1 ? 1 : (a.topk <= 2 ? 2 : 4)) : 1;
   if (a.mode == 2 && a.topk > 4) throw std::runtime_error("gemm: fused top-k supports k <= 4");
-  const int reserve = a.mode == 2 ? 2 * 4 * a.bt * kt * 8 : 0;
+  const int reserve = a.mode == 2 ? 2 * 4 * a.bt * kt * 8 : (a.mode == 4 ? 4 * a.bt * 4 : 0);
   GemmParams p{};
   p.M = a.M;
   p.N = a.N;
@@ -588,6 +646,11 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   p.status = a.status;
   p.timeout_ns = a.timeout_ns;
   p.tp = a.tp;
+  p.fin_x = a.fin_x;
+  p.fin_ldx = a.fin_ldx;
+  p.fin_sumsq = a.fin_sumsq;
+  p.fin_ticket = a.fin_ticket;
+  if (a.tp > 0 && a.mode == 4) throw std::runtime_error("gemm: mode 4 is not tensor-parallel");
   if (a.tp > 0) {
     if (a.mode != 0 || a.tp > 8 || !a.tp_epoch || !a.tp_ticket)
       throw std::runtime_error("gemm: tensor-parallel push needs mode 0, tp <= 8, epoch and ticket");
@@ -618,6 +681,7 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
       if (a.N % GBN) throw std::runtime_error("gemm: SwiGLU epilogue needs 2*I to be a multiple of 128");
       launch_mode<3, 1>(tw, tx, p, units, smem, stream);
       break;
+    case 4: launch_mode<4, 1>(tw, tx, p, units, smem, stream); break;
     default: throw std::runtime_error("gemm: bad mode");
   }
 }

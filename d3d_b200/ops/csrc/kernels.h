@@ -26,8 +26,20 @@ struct QkvRopeArgs {
   float eps;
   long long num_slots;      // KV cache rows (debug bounds checks)
   int* status;              // error word (debug bounds checks; may be null)
+  // optional RMSNorm row scale of the GEMM input (the norm weight folded into
+  // the qkv weight): r[m] = rsqrt(sum_t rsq[t][m] / rsq_n + eps), rsq [rsq_tiles][M]
+  const float* rsq;
+  int rsq_tiles, rsq_n;
 };
 void qkv_rope_kv(const QkvRopeArgs& a, cudaStream_t st);
+
+// SwiGLU of split-K partials of an interleaved gate|up weight whose input
+// RMSNorm weight is folded in: h = silu(r*g) * (r*u), r from per-tile sums of
+// squares rsq [rsq_tiles][M] of the GEMM input (n elements per row).
+void swiglu_rowscale(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, const float* rsq, int rsq_tiles,
+                     int rsq_n, float eps, cudaStream_t st);
+// Per-tile (128 columns) row sums of squares of x [M, N] into out [ceil(N/128)][M].
+void tile_sumsq(const __nv_bfloat16* x, int M, int N, float* out, cudaStream_t st);
 
 void embed(const int64_t* ids, const __nv_bfloat16* table, const __nv_bfloat16* cond, const unsigned char* cond_rows,
            int q_len, __nv_bfloat16* out, int M, int H, cudaStream_t st, long long vocab = 0, int* status = nullptr);
