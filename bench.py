@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--json-out", default=None)
+    p.add_argument("--watchdog-s", type=float, default=1500.0,
+                   help="N>1: dump stacks and exit a rank still running after this many seconds")
     p.add_argument("--layout", choices=["auto", "replica", "disagg", "tp"], default="auto",
                    help="N>1: 'tp' = target tensor-parallel over N/2 GPUs + one drafter per other GPU; "
                         "'disagg' = pairs of GPUs (target GPU + drafter GPU, NVLink handoff); "
@@ -640,6 +642,11 @@ def run_reference(args, rank, world, local):
 def main():
     args = parse()
     rank, world, local = dist_setup()
+    if world > 1:
+        # a rank stuck past the watchdog prints every thread's stack and exits,
+        # so a multi-GPU run never holds its GPUs silently
+        import faulthandler
+        faulthandler.dump_traceback_later(args.watchdog_s, exit=True)
     try:
         if args.impl == "reference":
             try:

@@ -35,6 +35,8 @@ def _worker(rank, world, T, port, out_dir):
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     import datetime
+    import faulthandler
+    faulthandler.dump_traceback_later(240, exit=True)   # a stuck worker reports where, then exits
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
@@ -74,10 +76,11 @@ def _worker(rank, world, T, port, out_dir):
                 grp.close()
         else:
             me = rank - T
+            # links first: the target ranks build theirs before the broadcast
+            links = [Link(0, 1 << 16, dev, group=pair[(t, me)]) for t in range(T)]
             box = [None]
             dist.broadcast_object_list(box, src=0)
             ar = box[0][2 * me:2 * me + 2]
-            links = [Link(0, 1 << 16, dev, group=pair[(t, me)]) for t in range(T)]
             dw = FastWeights.from_module(build_model(tiny_drafter(cond=True), seed=1), dev)
             eng = D3DEngine.from_remote_target(dw, links, 128, cfg, max_seqs=4, max_context=512, device=dev,
                                                deadline_s=60)

@@ -34,6 +34,8 @@ def _worker(rank, port, out_path):
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     import datetime
+    import faulthandler
+    faulthandler.dump_traceback_later(240, exit=True)   # a stuck worker reports where, then exits
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
