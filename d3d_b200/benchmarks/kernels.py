@@ -276,7 +276,7 @@ def forward_eager(layers, drafter, context=1000):
                           launches=n, status=int(b.status.item()))))
 
 
-def train_kernels(iters, peaks, rows, n_tok=4096, chunk=16384, hidden=2048):
+def train_kernels(iters, peaks, rows, n_tok=4096, chunk=16384, hidden=2048, n_params=1_720_000_000 // 8):
     """The training step's own kernels at distillation shapes: online-LSE
     KL+CE statistics and gradient over one vocabulary chunk of fp32 logits
     (``n_tok`` rows), the fused AdamW update and the squared-norm reduction
@@ -300,7 +300,7 @@ def train_kernels(iters, peaks, rows, n_tok=4096, chunk=16384, hidden=2048):
     byts = 2 * n_tok * chunk * 4 + n_tok * chunk * 2
     rows.append(dict(kernel="kl_ce_grad", shape=f"{n_tok}x{chunk}", us=round(us, 2), GBps=round(byts / us / 1e3, 1),
                      hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3)))
-    n = 1_720_000_000 // 8
+    n = int(n_params)
     p = torch.zeros(n, device="cuda")
     gr = torch.randn(n, device="cuda", generator=g)
     m1, v1 = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
@@ -326,6 +326,8 @@ def main():
     ap.add_argument("--sweep-m", type=int, default=272, help="gemm_sweep: token count")
     ap.add_argument("--attn-case", default=None, help="attn: run only this shape (e.g. 'packed 1.7B A1')")
     ap.add_argument("--no-graph", action="store_true", help="eager launches (for profiler captures)")
+    ap.add_argument("--adamw-n", type=int, default=1_720_000_000 // 8,
+                    help="train_kernels: parameters per rank of the AdamW / squared-norm cases")
     a = ap.parse_args()
     peaks = load_peaks()
     rows = []
@@ -348,7 +350,7 @@ def main():
     if "gemm_sweep" in only:
         bench_gemm_sweep(a.sweep_m, a.iters, peaks, rows)
     if "train_kernels" in only:
-        train_kernels(a.iters, peaks, rows)
+        train_kernels(a.iters, peaks, rows, n_params=a.adamw_n)
     if "forward_eager" in only:
         forward_eager(a.layers, a.drafter)
     if "forward" in only:
