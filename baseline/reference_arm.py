@@ -177,7 +177,7 @@ def run(args, rank, world, local):
         oracle[i] = gen
 
     # --- identical controlled-acceptance injection on the reference's draft outputs
-    rate = rate_for_mean_accept(args.accept_mean, args.block_size)
+    rate = rate_for_mean_accept(args.accept_mean, args.block_size) if args.accept_mean > 0 else 0.0
     current = {"i": 0}
 
     def ctl():
@@ -212,8 +212,9 @@ def run(args, rank, world, local):
                 tops[key][0].copy_(t.to(tops[key].device))
         return cands, tops, probs
 
-    ea.d3d_draft_from_anchor = draft_from_anchor
-    ea.d3d_draft_all_outcomes_packed = all_outcomes
+    if args.accept_mean > 0:     # 0 = natural acceptance: the reference's drafts as they are
+        ea.d3d_draft_from_anchor = draft_from_anchor
+        ea.d3d_draft_all_outcomes_packed = all_outcomes
 
     opts = dict(block_size=args.block_size, denoising_steps=1, threshold=0.9, remasking="low_confidence",
                 top_k=0, top_p=1.0, target_top_k=0, target_top_p=1.0, return_stats=True,

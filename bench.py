@@ -46,7 +46,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--max-new-tokens", type=int, default=512)
-    p.add_argument("--accept-mean", type=float, default=5.0)
+    p.add_argument("--accept-mean", type=float, default=5.0,
+                   help="controlled mean accepted length; 0 = natural acceptance (no injection)")
     p.add_argument("--block-size", type=int, default=16)
     p.add_argument("--anchor-num", type=int, default=1)
     p.add_argument("--concurrency", type=int, default=1)
@@ -120,9 +121,11 @@ def run_ours(args, rank, world, local):
         if gi >= args.warmup:
             ar_time += t0.elapsed_time(t1) / 1e3
             ar_tokens += sum(len(o) for o in r["outputs"])
-    rate = rate_for_mean_accept(args.accept_mean, args.block_size)
+    rate = rate_for_mean_accept(args.accept_mean, args.block_size) if args.accept_mean > 0 else 0.0
 
     def ctl_for(base):
+        if args.accept_mean <= 0:     # natural acceptance: the drafter's own proposals
+            return None
         def ctl(i):
             k = base + i
             return ControlledAcceptance(oracle=prompts[k] + ar_out[k], rate=rate,
@@ -266,9 +269,11 @@ def run_disagg(args, rank, world, local):
     shared = [None] * world
     dist.all_gather_object(shared, ar_out if is_target else None)
     ar_out = shared[2 * pair]
-    rate = rate_for_mean_accept(args.accept_mean, args.block_size)
+    rate = rate_for_mean_accept(args.accept_mean, args.block_size) if args.accept_mean > 0 else 0.0
 
     def ctl_for(base):
+        if args.accept_mean <= 0:     # natural acceptance: the drafter's own proposals
+            return None
         def ctl(i):
             k = base + i
             return ControlledAcceptance(oracle=prompts[k] + ar_out[k], rate=rate, vocab_size=tcfg.vocab_size,
@@ -490,9 +495,11 @@ def run_tp_layout(args, rank, world, local):
     shared = [None] * world
     dist.all_gather_object(shared, ar_out if rank == 0 else None)
     ar_out = shared[0]
-    rate = rate_for_mean_accept(args.accept_mean, args.block_size)
+    rate = rate_for_mean_accept(args.accept_mean, args.block_size) if args.accept_mean > 0 else 0.0
 
     def ctl_for(base):
+        if args.accept_mean <= 0:     # natural acceptance: the drafter's own proposals
+            return None
         def ctl(i):
             k = base + i
             return ControlledAcceptance(oracle=prompts[me][k] + ar_out[(me, k)], rate=rate,
