@@ -173,7 +173,8 @@ class _FastModelBackend:
     def _prefill_one(self, s: SeqState, rows: np.ndarray, topk: int, reserve: int):
         n = len(s.prompt)
         self.kv.reserve(s.index, self._row(s), reserve)
-        b = StepBuffers(self.cfg, 1, n, topk, 1, self.runner.splits(n), self.device)
+        b = StepBuffers(self.cfg, 1, n, topk, 1, self.runner.splits(n), self.device,
+                        fused_norm=self.runner.fused_norm)
         b.bt_view = torch.zeros(1, self.kv.max_pages_per_seq, dtype=torch.int32, device=self.device)
         b.chunk = self.runner.chunk_for(prefill=True)
         saved = s.prefix

@@ -360,6 +360,7 @@ class FastRunner:
 
     # ------------------------------------------------------------- policies
     GEMMS = ("qkv", "o", "gate_up", "down")
+    FIN_MAX_T = int(os.environ.get("D3D_FIN_MAX_T", "64"))
 
     def _shapes(self) -> Dict[str, Tuple[int, int]]:
         c = self.cfg
@@ -504,6 +505,10 @@ class FastRunner:
         w, H = self.w, self.cfg.hidden_size
         n = 0
         last = len(w.layers) - 1
+        # decode-sized forwards reduce the o / down splits inside the GEMM (the
+        # last unit of a tile does it, no extra launch); larger ones with the
+        # stand-alone kernel, whose results are bit-identical
+        fin = b.T <= self.FIN_MAX_T
         for li, L in enumerate(w.layers):
             gbt, s, direct = pl["qkv"]
             if direct:
@@ -519,14 +524,22 @@ class FastRunner:
                         b.att_o if b.n_chunks > 1 else None, b.att_ml if b.n_chunks > 1 else None,
                         b.attn, self.batch_invariant, b.status)
             gbt, s, _ = pl["o"]
-            E.gemm_partial_fin(b.attn, L.o.data, b.part, s, gbt, b.status, L.o.n, b.x, b.ss_post, b.ticket)
+            if fin:
+                E.gemm_partial_fin(b.attn, L.o.data, b.part, s, gbt, b.status, L.o.n, b.x, b.ss_post, b.ticket)
+            else:
+                E.gemm_partial(b.attn, L.o.data, b.part, s, gbt, b.status, L.o.n)
+                E.residual_split_reduce(b.part, s, b.x, b.ss_post)
             gbt, s, _ = pl["gate_up"]
             E.gemm_partial(b.x, L.gate_up.data, b.part, s, gbt, b.status, L.gate_up.n)
             E.swiglu_rowscale(b.part, s, b.h, b.ss_post, H, eps)
             gbt, s, _ = pl["down"]
-            if li < last:
+            if li < last and fin:
                 E.gemm_partial_fin(b.h, L.down.data, b.part, s, gbt, b.status, L.down.n, b.x, b.ss_in, b.ticket)
                 n += 8 + (1 if b.n_chunks > 1 else 0)
+            elif li < last:
+                E.gemm_partial(b.h, L.down.data, b.part, s, gbt, b.status, L.down.n)
+                E.residual_split_reduce(b.part, s, b.x, b.ss_in)
+                n += 10 + (1 if b.n_chunks > 1 else 0)
             else:
                 E.gemm_partial(b.h, L.down.data, b.part, s, gbt, b.status, L.down.n)
                 E.add_rmsnorm(b.part, s, b.x, w.final_norm, b.xn, eps)

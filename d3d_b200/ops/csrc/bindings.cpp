@@ -183,6 +183,19 @@ void swiglu_rowscale(Tensor part, int64_t nsplit, Tensor h, Tensor rsq, int64_t 
                        rsq.data_ptr<float>(), tiles, static_cast<int>(rsq_n), static_cast<float>(eps), cur_stream());
 }
 
+void residual_split_reduce(Tensor part, int64_t nsplit, Tensor x, Tensor sumsq) {
+  const c10::cuda::CUDAGuard g(x.device());
+  CHECK_CONTIG(x);
+  CHECK_DT(part, torch::kFloat32);
+  CHECK_DT(sumsq, torch::kFloat32);
+  const int M = static_cast<int>(x.size(0)), N = static_cast<int>(x.size(1));
+  TORCH_CHECK(N % 4 == 0, "residual_split_reduce: row length must be a multiple of 4");
+  TORCH_CHECK(part.numel() >= nsplit * static_cast<int64_t>(M) * N, "residual_split_reduce: partials too small");
+  TORCH_CHECK(sumsq.numel() >= static_cast<int64_t>((N + 127) / 128) * M, "residual_split_reduce: sumsq too small");
+  d3d::residual_split_reduce(part.data_ptr<float>(), static_cast<int>(nsplit), bf(x), M, N, sumsq.data_ptr<float>(),
+                             cur_stream());
+}
+
 void tile_sumsq(Tensor x, Tensor out) {
   const c10::cuda::CUDAGuard g(x.device());
   CHECK_CONTIG(x);
@@ -619,6 +632,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status") = py::none(), py::arg("rsq") = py::none(), py::arg("rsq_n") = 0);
   m.def("swiglu_rowscale", &swiglu_rowscale);
   m.def("tile_sumsq", &tile_sumsq);
+  m.def("residual_split_reduce", &residual_split_reduce);
   m.def("embed", &embed, py::arg("ids"), py::arg("table"), py::arg("cond"), py::arg("cond_rows"), py::arg("q_len"),
         py::arg("out"), py::arg("status") = py::none());
   m.def("topk_merge", &topk_merge);

@@ -311,6 +311,64 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
+// One row m of one 128-column tile t of a split-K result, done by one warp:
+// y = sum over splits (split order) of part[s][m][n]; the bf16 residual
+// x[m][n] becomes bf16(x + bf16(y)) (two bf16 ops); lane l owns columns
+// 128t + 4l .. +3, sums their squares in column order, and the warp reduces
+// with a fixed butterfly into sumsq[t][m].  Used by the GEMM's in-kernel
+// split reduction and by the stand-alone kernel, which therefore produce
+// bit-identical residuals and sums of squares.
+__device__ __forceinline__ void split_reduce_row(const float* part, int nsplit, size_t sstride, int N,
+                                                 __nv_bfloat16* x, int ldx, float* sumsq, int M, int m, int t,
+                                                 int lane) {
+  constexpr int SMAX = 16;
+  const int n = t * 128 + 4 * lane;
+  float ss = 0.f;
+  if (n + 3 < N) {
+    float4 v[SMAX];
+    const float* src = part + static_cast<size_t>(m) * N + n;
+#pragma unroll
+    for (int s = 0; s < SMAX; ++s)
+      if (s < nsplit) v[s] = __ldcg(reinterpret_cast<const float4*>(src + s * sstride));
+    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < SMAX; ++s)
+      if (s < nsplit) {
+        y.x += v[s].x;
+        y.y += v[s].y;
+        y.z += v[s].z;
+        y.w += v[s].w;
+      }
+    __nv_bfloat16* xp = x + static_cast<size_t>(m) * ldx + n;
+    const uint2 raw = *reinterpret_cast<const uint2*>(xp);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+    const float o0 = bf16r(__low2float(a) + bf16r(y.x)), o1 = bf16r(__high2float(a) + bf16r(y.y));
+    const float o2 = bf16r(__low2float(b) + bf16r(y.z)), o3 = bf16r(__high2float(b) + bf16r(y.w));
+    __nv_bfloat162 ra = __floats2bfloat162_rn(o0, o1), rb = __floats2bfloat162_rn(o2, o3);
+    uint2 w;
+    w.x = *reinterpret_cast<uint32_t*>(&ra);
+    w.y = *reinterpret_cast<uint32_t*>(&rb);
+    *reinterpret_cast<uint2*>(xp) = w;
+    ss = ((o0 * o0 + o1 * o1) + o2 * o2) + o3 * o3;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if (n + e < N) {
+        float y = 0.f;
+        for (int s = 0; s < nsplit; ++s) y += __ldcg(part + s * sstride + static_cast<size_t>(m) * N + n + e);
+        __nv_bfloat16* xp = x + static_cast<size_t>(m) * ldx + n + e;
+        const float o = bf16r(__bfloat162float(*xp) + bf16r(y));
+        *xp = __float2bfloat16(o);
+        ss += o * o;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) sumsq[static_cast<size_t>(t) * M + m] = ss;
+}
+
 // Order-preserving map float -> uint32 (larger float -> larger key; finite
 // inputs never map to 0, which callers use as "empty").
 __device__ __forceinline__ uint32_t float_key(float f) {

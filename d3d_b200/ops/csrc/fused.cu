@@ -218,6 +218,29 @@ void swiglu_rowscale(const float* part, int nsplit, __nv_bfloat16* h, int M, int
                                         M, I, rsq, rsq_tiles, rsq_n, eps));
 }
 
+// Split-K reduction into the residual with per-tile row sums of squares, one
+// warp per (row, 128-column tile): the stand-alone form of the GEMM's
+// in-kernel reduction (same per-element and per-tile order, so the results
+// are bit-identical whichever of the two a forward uses).
+__global__ void residual_split_reduce_kernel(const float* __restrict__ part, int nsplit, __nv_bfloat16* x, int M,
+                                             int N, float* __restrict__ sumsq) {
+  griddep_launch();
+  griddep_wait();
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int tiles = (N + 127) / 128;
+  if (w >= tiles * M) return;
+  split_reduce_row(part, nsplit, static_cast<size_t>(M) * N, N, x, N, sumsq, M, w % M, w / M, lane);
+}
+
+void residual_split_reduce(const float* part, int nsplit, __nv_bfloat16* x, int M, int N, float* sumsq,
+                           cudaStream_t st) {
+  if (M == 0) return;
+  if (nsplit > MAX_SPLITS) throw std::runtime_error("residual_split_reduce: too many splits");
+  const int warps = ((N + 127) / 128) * M;
+  launch_pdl(residual_split_reduce_kernel, dim3((warps * 32 + 255) / 256), dim3(256), 0, st, part, nsplit, x, M, N,
+             sumsq);
+}
+
 __global__ void tile_sumsq_kernel(const __nv_bfloat16* __restrict__ x, int M, int N, float* __restrict__ out) {
   griddep_launch();
   griddep_wait();

@@ -90,9 +90,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
   const int marea = MODE == 2 ? 4 * bt * KT : 0;
   float* mval = reinterpret_cast<float*>(smem + stages * stage_bytes);
   int* midx = reinterpret_cast<int*>(mval + 2 * marea);
-  // MODE 4: the four epilogue warps' per-column partial sums of squares [4][bt]
-  float* fss = reinterpret_cast<float*>(midx + 2 * marea);
-  uint64_t* full = reinterpret_cast<uint64_t*>(fss + (MODE == 4 ? 4 * bt : 0));
+  uint64_t* full = reinterpret_cast<uint64_t*>(midx + 2 * marea);
   uint64_t* empty = full + stages;
   uint64_t* accf = empty + stages;  // [2] accumulator ready for the epilogue
   uint64_t* acce = accf + 2;        // [2] accumulator drained by the epilogue
@@ -348,28 +346,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
           if (!fsync()) break;
           if (flags[3]) {
             __threadfence();
-            const size_t sstride = static_cast<size_t>(p.M) * p.N;
-            for (int c = 0; c < cols; ++c) {
-              const int m = m0 + c;
-              float ss = 0.f;
-              if (n_ok) {
-                const float* src = p.out_f32 + static_cast<size_t>(m) * p.N + n;
-                float y = 0.f;
-                for (int sp = 0; sp < nsplit; ++sp) y += __ldcg(src + sp * sstride);
-                __nv_bfloat16* xp = p.fin_x + static_cast<size_t>(m) * p.fin_ldx + n;
-                const float xv = bf16r(__bfloat162float(*xp) + bf16r(y));
-                *xp = __float2bfloat16(xv);
-                ss = xv * xv;
-              }
-              ss = warp_sum(ss);
-              if (lane == 0) fss[q * bt + c] = ss;
-            }
-            if (!fsync()) break;
-            for (int c = threadIdx.x - 64; c < cols; c += 128)
-              p.fin_sumsq[static_cast<size_t>(u.n_t) * p.M + m0 + c] =
-                  ((fss[c] + fss[bt + c]) + fss[2 * bt + c]) + fss[3 * bt + c];
+            // warp q takes token columns q, q+4, ...; lane l the tile's rows
+            // 4l..4l+3 (16-byte loads, every split's load in flight before the
+            // adds), so one warp finishes a column and its sum of squares
+            // (residual_split_reduce in fused.cu computes the same values)
+            for (int c = q; c < cols; c += 4)
+              split_reduce_row(p.out_f32, nsplit, static_cast<size_t>(p.M) * p.N, p.N, p.fin_x, p.fin_ldx,
+                               p.fin_sumsq, p.M, m0 + c, u.n_t, lane);
             if (threadIdx.x == 64) p.fin_ticket[tile] = 0u;   // ready for the next launch
-            if (!fsync()) break;                              // fss may be rewritten by the next tile
           }
         }
       } else {
@@ -627,7 +611,7 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   make_tmap_bf16_2d(&tx, a.x, a.K, a.M, a.ldx, GBK, a.bt > 256 ? a.bt / 2 : a.bt);
   const int kt = a.mode == 2 ? (a.topk <= 1 ? 1 : (a.topk <= 2 ? 2 : 4)) : 1;
   if (a.mode == 2 && a.topk > 4) throw std::runtime_error("gemm: fused top-k supports k <= 4");
-  const int reserve = a.mode == 2 ? 2 * 4 * a.bt * kt * 8 : (a.mode == 4 ? 4 * a.bt * 4 : 0);
+  const int reserve = a.mode == 2 ? 2 * 4 * a.bt * kt * 8 : 0;
   GemmParams p{};
   p.M = a.M;
   p.N = a.N;

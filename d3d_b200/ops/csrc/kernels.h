@@ -38,6 +38,11 @@ void qkv_rope_kv(const QkvRopeArgs& a, cudaStream_t st);
 // squares rsq [rsq_tiles][M] of the GEMM input (n elements per row).
 void swiglu_rowscale(const float* part, int nsplit, __nv_bfloat16* h, int M, int I, const float* rsq, int rsq_tiles,
                      int rsq_n, float eps, cudaStream_t st);
+// x [M, N] (bf16, in place) += split-K partials part [nsplit][M][N] (split order,
+// rounded like two bf16 ops) and per-tile row sums of squares into sumsq
+// [ceil(N/128)][M]: the stand-alone form of the GEMM's in-kernel reduction.
+void residual_split_reduce(const float* part, int nsplit, __nv_bfloat16* x, int M, int N, float* sumsq,
+                           cudaStream_t st);
 // Per-tile (128 columns) row sums of squares of x [M, N] into out [ceil(N/128)][M].
 void tile_sumsq(const __nv_bfloat16* x, int M, int N, float* out, cudaStream_t st);
 

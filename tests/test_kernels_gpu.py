@@ -303,3 +303,34 @@ def test_greedy_accept_and_topk_merge(E):
     E.greedy_accept(blocks, post, commit, corr, hid, hout)
     assert commit.tolist() == [3, 1] and corr.tolist() == [4, 3]
     assert torch.equal(hout[0], hid[2]) and torch.equal(hout[1], hid[4])
+
+
+@pytest.mark.parametrize("m,splits", [(1, 9), (16, 9), (40, 3), (16, 1)])
+def test_gemm_in_kernel_split_reduce(E, m, splits):
+    """The o/down GEMM's in-kernel split-K reduction into the residual equals
+    the stand-alone reduce kernel bit for bit (residual and per-tile row sums
+    of squares), and tracks the fp32 reference."""
+    from d3d_b200 import ops
+    n, k = 4096, 4096
+    g = torch.Generator(device="cuda").manual_seed(m + splits)
+    w = ops.pack_weight((torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16))
+    xin = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    res = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+    bt = ops.bt_for(m)
+    part = torch.zeros(splits * m * n, device="cuda")
+    x1, x2 = res.clone(), res.clone()
+    ss1 = torch.zeros(32 * m, device="cuda")
+    ss2 = torch.zeros(32 * m, device="cuda")
+    ticket = torch.zeros(32 * ((m + bt - 1) // bt), dtype=torch.int32, device="cuda")
+    for _ in range(2):      # tickets reset themselves between launches
+        x1.copy_(res)
+        E.gemm_partial_fin(xin, w.data, part, splits, bt, None, w.n, x1, ss1, ticket)
+    E.gemm_partial(xin, w.data, part, splits, bt, None, w.n)
+    E.residual_split_reduce(part, splits, x2, ss2)
+    torch.cuda.synchronize()
+    assert torch.equal(x1, x2) and torch.equal(ss1, ss2)
+    assert int(ticket.abs().sum()) == 0
+    ref = res.float() + xin.float() @ w.unpack().float().t()
+    assert (x1.float() - ref).abs().max().item() < 0.1
+    ss_ref = (x1.float() ** 2).view(m, 32, 128).sum(-1).t().reshape(-1)
+    assert torch.allclose(ss1, ss_ref, rtol=1e-4, atol=1e-3)
