@@ -343,9 +343,11 @@ class FastRunner:
         self.max_context = max_context
         self.batch_invariant = batch_invariant
         # residual + RMSNorm fused into the o / down GEMMs and the qkv / SwiGLU
-        # reduce kernels (D3D_FUSE_NORM=0: separate add+RMSNorm kernels);
-        # tensor-parallel runners keep the exchange-fused norm
-        self.fused_norm = tp is None and os.environ.get("D3D_FUSE_NORM", "1") != "0"
+        # reduce kernels (D3D_FUSE_NORM=0: separate add+RMSNorm kernels) for the
+        # target, whose decode forwards are small; the drafter's packed forward
+        # (hundreds of rows) keeps its autotuned direct epilogues and separate
+        # norms; tensor-parallel runners keep the exchange-fused norm
+        self.fused_norm = tp is None and batch_invariant and os.environ.get("D3D_FUSE_NORM", "1") != "0"
         if self.fused_norm:
             weights.fold_norms()
         elif weights.folded:
