@@ -116,10 +116,10 @@ def test_sampled_kernel_path(fast_pair):
 
 def test_full_vocab_sampled_verify_is_lossless():
     """Full-vocabulary sampled verification on the kernel path (target
-    top_k = 0): over many draws, the token emitted at the first drafted
-    position (the draft if accepted, else the residual correction) follows
-    the target distribution p exactly -- checked against p with a
-    chi-square bound -- whatever the proposal q."""
+    top_k = 0): with each draft sampled from the proposal q, the token
+    emitted at the first drafted position (the draft if accepted, else the
+    residual correction) follows the target distribution p exactly --
+    checked against p with a chi-square bound over many draws."""
     import math
     import torch
     from d3d_b200.config import tiny_target
@@ -137,17 +137,22 @@ def test_full_vocab_sampled_verify_is_lossless():
     logits = torch.randn(K, V, device=dev, generator=g) * 2.0
     b.logits.copy_(logits)
     p0 = torch.softmax(logits[0], -1)
-    draft = int(p0.argsort(descending=True)[3])          # a plausible but not top token
-    b.ids.view(1, K).copy_(torch.tensor([[5, draft, 7, 9]], device=dev))
-    # proposal: q puts 0.6 on the draft, the rest on three other ids
-    q_ids = torch.tensor([[[draft, 11, 12, 13]] * (K - 1)])
-    q_p = torch.tensor([[[0.6, 0.2, 0.1, 0.1]] * (K - 1)])
+    # proposal q over four ids (a plausible token and three others); each
+    # trial's draft is sampled from q, as the drafter does
+    support = [int(p0.argsort(descending=True)[3]), 11, 12, 13]
+    qw = torch.tensor([0.6, 0.2, 0.1, 0.1])
+    q_ids = torch.tensor([[support] * (K - 1)])
+    q_p = qw.expand(1, K - 1, 4).clone()
     n = 20000
+    drafts = torch.multinomial(qw, n, replacement=True, generator=torch.Generator().manual_seed(1))
     out = torch.empty(n, dtype=torch.long)
+    ids = b.ids.view(1, K)
     for i in range(n):
+        x1 = support[int(drafts[i])]
+        ids.copy_(torch.tensor([[5, x1, 7, 9]]), non_blocking=True)
         tgt._sampled_accept(b, a, (q_ids, q_p))
         commit, corr = int(a["commit"][0]), int(a["corr"][0])
-        out[i] = draft if commit >= 2 else corr
+        out[i] = x1 if commit >= 2 else corr
     counts = torch.bincount(out, minlength=V).double()
     exp = p0.double().cpu() * n
     big = exp >= 20
