@@ -6,8 +6,8 @@
 // The LM-head loss never materialises [N, V] logits.  The vocabulary is
 // walked in chunks of C columns; for each chunk the teacher and student
 // logit tiles are produced by the tcgen05 GEMM (fp32, [N, C]) and folded into
-// per-row running statistics by kl_ce_stats_kernel (fixed chunk order, so the
-// result is deterministic):
+// per-row running statistics by kl_ce_stats_kernel in one pass (online max,
+// fixed chunk and lane order, so the result is deterministic):
 //   M_t, S_t = max and sum of exp(z_t - M_t)               (teacher LSE)
 //   A_tt     = sum exp(z_t - M_t) * z_t
 //   A_ts     = sum exp(z_t - M_t) * z_s
@@ -37,8 +37,50 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float om, float os
   m = nm;
 }
 
-// One warp per row.  zt/zs: [N, ldz] fp32 chunk logits (columns [0, C)),
+// Online fold of one logit into a lane's running (max, sum of exp) -- and,
+// for the teacher, the exp-weighted sums of its own and the student's logit.
+// The sums are rescaled only when the running max rises.
+__device__ __forceinline__ void fold_student(float y, float& ms, float& ss) {
+  if (y > ms) {
+    ss = ss * __expf(ms - y) + 1.f;
+    ms = y;
+  } else {
+    ss += __expf(y - ms);
+  }
+}
+__device__ __forceinline__ void fold_teacher(float x, float y, float& mt, float& st, float& att, float& ats) {
+  if (x > mt) {
+    const float f = __expf(mt - x);
+    st = st * f + 1.f;
+    att = att * f + x;
+    ats = ats * f + y;
+    mt = x;
+  } else {
+    const float e = __expf(x - mt);
+    st += e;
+    att += e * x;
+    ats += e * y;
+  }
+}
+// Merge another lane's state (m, s[, a, b]) into this one.
+__device__ __forceinline__ void merge_state(float& m, float& s, float& a, float& b, float om, float os, float oa,
+                                            float ob) {
+  const float nm = fmaxf(m, om);
+  if (nm == -INFINITY) return;
+  const float f1 = m == -INFINITY ? 0.f : __expf(m - nm);
+  const float f2 = om == -INFINITY ? 0.f : __expf(om - nm);
+  s = s * f1 + os * f2;
+  a = a * f1 + oa * f2;
+  b = b * f1 + ob * f2;
+  m = nm;
+}
+
+// One warp per row, one pass over the chunk (every logit read once; float4
+// loads when VEC).  zt/zs: [N, ldz] fp32 chunk logits (columns [0, C)); the
 // chunk covers vocabulary ids [v0, v0 + C).  zt may be null (CE only).
+// Lanes fold their columns (lane-strided), then a fixed butterfly merges the
+// lane states, so the result is deterministic.
+template <bool VEC>
 __global__ void kl_ce_stats_kernel(const float* __restrict__ zt, const float* __restrict__ zs, int N, int C,
                                    int ldz, int v0, const int64_t* __restrict__ target, float* __restrict__ st) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -46,34 +88,39 @@ __global__ void kl_ce_stats_kernel(const float* __restrict__ zt, const float* __
   if (row >= N) return;
   const float* a = zt ? zt + static_cast<size_t>(row) * ldz : nullptr;
   const float* b = zs + static_cast<size_t>(row) * ldz;
-  // pass 1: chunk maxima
-  float mt = -INFINITY, ms = -INFINITY;
-  for (int c = lane; c < C; c += 32) {
-    if (a) mt = fmaxf(mt, a[c]);
-    ms = fmaxf(ms, b[c]);
-  }
-  mt = warp_max(mt);
-  ms = warp_max(ms);
-  // pass 2: sums relative to the chunk maxima (lane-strided, then butterfly: fixed order)
-  float s_t = 0.f, att = 0.f, ats = 0.f, s_s = 0.f;
-  for (int c = lane; c < C; c += 32) {
-    const float y = b[c];
-    s_s += __expf(y - ms);
-    if (a) {
-      const float x = a[c];
-      const float e = __expf(x - mt);
-      s_t += e;
-      att += e * x;
-      ats += e * y;
+  float mt = -INFINITY, s_t = 0.f, att = 0.f, ats = 0.f, ms = -INFINITY, s_s = 0.f;
+  if (VEC) {
+    for (int c = lane * 4; c < C; c += 128) {
+      const float4 y4 = __ldcs(reinterpret_cast<const float4*>(b + c));
+      const float y[4] = {y4.x, y4.y, y4.z, y4.w};
+      if (a) {
+        const float4 x4 = __ldcs(reinterpret_cast<const float4*>(a + c));
+        const float x[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) fold_teacher(x[j], y[j], mt, s_t, att, ats);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) fold_student(y[j], ms, s_s);
+    }
+  } else {
+    for (int c = lane; c < C; c += 32) {
+      const float y = b[c];
+      if (a) fold_teacher(a[c], y, mt, s_t, att, ats);
+      fold_student(y, ms, s_s);
     }
   }
-  s_t = warp_sum(s_t);
-  att = warp_sum(att);
-  ats = warp_sum(ats);
-  s_s = warp_sum(s_s);
+  float dummy0 = 0.f, dummy1 = 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float omt = __shfl_xor_sync(0xffffffffu, mt, o), ost = __shfl_xor_sync(0xffffffffu, s_t, o);
+    const float oatt = __shfl_xor_sync(0xffffffffu, att, o), oats = __shfl_xor_sync(0xffffffffu, ats, o);
+    const float oms = __shfl_xor_sync(0xffffffffu, ms, o), oss = __shfl_xor_sync(0xffffffffu, s_s, o);
+    merge_state(mt, s_t, att, ats, omt, ost, oatt, oats);
+    merge_state(ms, s_s, dummy0, dummy1, oms, oss, 0.f, 0.f);
+  }
   if (lane == 0) {
     float* r = st + static_cast<size_t>(row) * ST_N;
-    if (a) {
+    if (a && mt != -INFINITY) {
       // rescale the running teacher accumulators to the new maximum
       float M = r[ST_M_T];
       const float nm = fmaxf(M, mt);
@@ -96,7 +143,10 @@ __global__ void kl_ce_stats_kernel(const float* __restrict__ zt, const float* __
 void kl_ce_stats(const float* zt, const float* zs, int N, int C, int ldz, int v0, const int64_t* target, float* st,
                  cudaStream_t s) {
   if (N == 0) return;
-  kl_ce_stats_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(zt, zs, N, C, ldz, v0, target, st);
+  const bool vec = C % 4 == 0 && ldz % 4 == 0 && (reinterpret_cast<uintptr_t>(zs) & 15) == 0 &&
+                   (zt == nullptr || (reinterpret_cast<uintptr_t>(zt) & 15) == 0);
+  if (vec) kl_ce_stats_kernel<true><<<(N * 32 + 255) / 256, 256, 0, s>>>(zt, zs, N, C, ldz, v0, target, st);
+  else kl_ce_stats_kernel<false><<<(N * 32 + 255) / 256, 256, 0, s>>>(zt, zs, N, C, ldz, v0, target, st);
 }
 
 // dz[n, c] = w_kl[n] (softmax_s - p_t) + w_ce[n] (softmax_s - onehot); lse_t/lse_s per row.
