@@ -607,6 +607,15 @@ void fsdp_update(Tensor ptrs, int64_t rank, int64_t lo, int64_t shard, int64_t e
                    static_cast<float>(scale), reinterpret_cast<unsigned int*>(ticket.data_ptr<int>()), cur_stream());
 }
 
+void fsdp_gather(Tensor ptrs, int64_t rank, int64_t off, int64_t n, Tensor dst) {
+  const c10::cuda::CUDAGuard g(dst.device());
+  CHECK_DT(dst, torch::kBFloat16);
+  CHECK_CONTIG(dst);
+  auto a = fsdp_args(ptrs, rank, 0, 0, c10::nullopt);
+  TORCH_CHECK(dst.numel() >= static_cast<int64_t>(a.world) * n, "fsdp_gather: destination too small");
+  d3d::fsdp_gather(a, static_cast<size_t>(off), static_cast<size_t>(n), bf(dst), cur_stream());
+}
+
 void fsdp_wait(Tensor ptrs, int64_t rank, int64_t lo, int64_t shard, int64_t phase, int64_t e, Tensor status) {
   const c10::cuda::CUDAGuard g(status.device());
   d3d::fsdp_wait(fsdp_args(ptrs, rank, lo, shard, status), static_cast<int>(phase), e, cur_stream());
@@ -638,6 +647,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("topk_merge", &topk_merge);
   m.def("greedy_accept", &greedy_accept);
   m.def("attention_uses_tc", &attention_uses_tc);
+  m.def("fsdp_gather", &fsdp_gather);
   m.def("gemm_partial_fin", &gemm_partial_fin);
   m.def("attention", &attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("block_table"),
         py::arg("rows"), py::arg("kv_end"), py::arg("B"), py::arg("q_len"), py::arg("Hq"), py::arg("Hkv"),

@@ -162,4 +162,35 @@ void fsdp_wait(const FsdpArgs& a, int phase, int64_t e, cudaStream_t st) {
   fsdp_wait_kernel<<<1, 32, 0, st>>>(a, phase, e);
 }
 
+// Parameter all-gather of sharded (FSDP-style) layers: dst[r * n + i] =
+// params[r][off + i] for every rank r -- rank r's shard of one layer, read
+// over NVLink from its parameter buffer (peer loads, 16-byte vectors when
+// the offsets allow).  Shards change only in the optimizer step, which the
+// trainer orders before the next forward on every rank, so no flag is needed.
+__global__ void fsdp_gather_kernel(FsdpArgs a, size_t off, size_t n, __nv_bfloat16* __restrict__ dst) {
+  griddep_launch();
+  griddep_wait();
+  const int r = blockIdx.y;
+  const __nv_bfloat16* src = a.params[r] + off;
+  __nv_bfloat16* out = dst + static_cast<size_t>(r) * n;
+  const bool vec = ((off | n) & 7) == 0;
+  if (vec) {
+    const size_t n8 = n / 8;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n8;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+      reinterpret_cast<uint4*>(out)[i] = __ldcv(reinterpret_cast<const uint4*>(src) + i);
+  } else {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x)
+      out[i] = src[i];
+  }
+}
+
+void fsdp_gather(const FsdpArgs& a, size_t off, size_t n, __nv_bfloat16* dst, cudaStream_t st) {
+  if (n == 0) return;
+  size_t per = (n / 8 + 255) / 256;
+  const int bx = static_cast<int>(per < 64 ? (per == 0 ? 1 : per) : 64);
+  launch_pdl(fsdp_gather_kernel, dim3(bx, a.world), dim3(256), 0, st, a, off, n, dst);
+}
+
 }  // namespace d3d

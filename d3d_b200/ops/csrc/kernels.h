@@ -144,4 +144,5 @@ void fsdp_reduce(const FsdpArgs& a, int64_t e, float* gshard, float* sumsq, cuda
 void fsdp_update(const FsdpArgs& a, int64_t e, const float* gshard, float* p, float* m, float* v, float lr, float b1,
                  float b2, float eps, float wd, int step, float scale, unsigned int* ticket, cudaStream_t st);
 void fsdp_wait(const FsdpArgs& a, int phase, int64_t e, cudaStream_t st);
+void fsdp_gather(const FsdpArgs& a, size_t off, size_t n, __nv_bfloat16* dst, cudaStream_t st);
 }  // namespace d3d

@@ -75,7 +75,8 @@ class FusedShardedAdamW(ShardedAdamW):
         self.closed = False
 
     @torch.no_grad()
-    def step(self, grad_clip: float = 0.0, lr: Optional[float] = None) -> float:
+    def step(self, grad_clip: float = 0.0, lr: Optional[float] = None,
+             extra_sumsq: Optional[torch.Tensor] = None) -> float:
         lr = self.lr if lr is None else lr
         self.step_count += 1
         e = self.step_count
@@ -93,6 +94,8 @@ class FusedShardedAdamW(ShardedAdamW):
         self.sq.zero_()
         E.fsdp_reduce(P, self.rank, self.lo, self.shard, e, self.gshard, self.sq, self.status)
         sq = self.sq.clone()
+        if extra_sumsq is not None:
+            sq += extra_sumsq
         if self.world > 1:
             dist.all_reduce(sq, group=self.group)
         mean = 1.0 / self.world
@@ -101,6 +104,7 @@ class FusedShardedAdamW(ShardedAdamW):
         clip = 1.0
         if grad_clip and grad_clip > 0 and norm > grad_clip:
             clip = grad_clip / (norm + 1e-6)
+        self.last_scale = mean * clip
         E.fsdp_update(P, self.rank, self.lo, self.shard, e, self.gshard, self.master, self.m, self.v, lr,
                       self.b1, self.b2, self.eps, self.wd, self.step_count, mean * clip, self.ticket, self.status)
         E.fsdp_wait(P, self.rank, self.lo, self.shard, 1, e, self.status)

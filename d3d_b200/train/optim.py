@@ -51,6 +51,7 @@ class ShardedAdamW:
         self.v = torch.zeros_like(self.master)
         self.step_count = 0
         self.last_grad_norm = 0.0
+        self.last_scale = 1.0 / self.world
 
     def zero_grad(self) -> None:
         for p in self.params:
@@ -67,7 +68,13 @@ class ShardedAdamW:
         return g
 
     @torch.no_grad()
-    def step(self, grad_clip: float = 0.0, lr: Optional[float] = None) -> float:
+    def step(self, grad_clip: float = 0.0, lr: Optional[float] = None,
+             extra_sumsq: Optional[torch.Tensor] = None) -> float:
+        """One AdamW step; returns the global gradient norm.  ``extra_sumsq``
+        is this rank's squared norm of gradients updated elsewhere (sharded
+        decoder layers): it joins the norm, and the gradient scale applied
+        here (1/world times the clip factor) is left in ``last_scale`` for
+        that other update."""
         lr = self.lr if lr is None else lr
         self.step_count += 1
         g = self._flat_grads()
@@ -84,6 +91,8 @@ class ShardedAdamW:
             ops.ext().sumsq(gs, sq)
         else:
             sq = (gs.double() ** 2).sum().float().reshape(1)
+        if extra_sumsq is not None:
+            sq = sq + extra_sumsq.to(sq.device)
         if self.world > 1:
             dist.all_reduce(sq, group=self.group)
         norm = math.sqrt(float(sq.item())) * mean
@@ -92,6 +101,7 @@ class ShardedAdamW:
         if grad_clip and grad_clip > 0 and norm > grad_clip:
             clip = grad_clip / (norm + 1e-6)
         scale = mean * clip
+        self.last_scale = scale
         out = torch.empty(self.shard, dtype=torch.bfloat16, device=gs.device)
         if cuda:
             from .. import ops

@@ -99,15 +99,18 @@ def _build(name: str, device, dtype, seed: int, layers: Optional[int] = None, ma
     return load_model(name, device=device, dtype=dtype, mask_token_id=mask_id)
 
 
-def save_checkpoint(model, opt: ShardedAdamW, out_dir: Path, step: int, cursor: int) -> None:
+def save_checkpoint(model, opt: ShardedAdamW, out_dir: Path, step: int, cursor: int, z3=None) -> None:
     """HF-layout FP32 safetensors from the fp32 master shards (gathered),
-    plus this rank's optimizer shard and the trainer state, written atomically."""
+    plus this rank's optimizer shard and the trainer state, written atomically.
+    With sharded decoder layers (``z3``) their master shards are gathered too
+    and each rank also keeps its layer-shard optimizer state."""
     rank = opt.rank
     full = torch.empty(opt.padded, dtype=torch.float32, device=opt.master.device)
     if opt.world > 1:
         dist.all_gather_into_tensor(full, opt.master, group=opt.group)
     else:
         full[: opt.shard] = opt.master
+    layers = z3.full_state("model.layers.") if z3 is not None else {}
     ck = out_dir / f"step_{step:07d}"
     tmp = out_dir / f".step_{step:07d}.tmp"
     if rank == 0:
@@ -117,6 +120,7 @@ def save_checkpoint(model, opt: ShardedAdamW, out_dir: Path, step: int, cursor: 
         for n, p in zip(names, opt.params):
             state[n] = full[off:off + p.numel()].view(p.shape).cpu().clone()
             off += p.numel()
+        state.update(layers)
         for n, p in model.named_parameters():
             if n not in state:
                 state[n] = p.detach().float().cpu()
@@ -134,6 +138,8 @@ def save_checkpoint(model, opt: ShardedAdamW, out_dir: Path, step: int, cursor: 
     if dist.is_initialized():
         dist.barrier()
     torch.save(opt.state_dict(), ck / f"optim_rank{rank:03d}.pt")
+    if z3 is not None:
+        torch.save(z3.state_dict(), ck / f"layers_rank{rank:03d}.pt")
 
 
 def train(args) -> dict:
@@ -162,6 +168,12 @@ def train(args) -> dict:
             del module
     if args.freeze_embeddings:
         student.model.embed_tokens.weight.requires_grad_(False)
+    z3 = None
+    if getattr(args, "fsdp", False):
+        # decoder layers live as per-rank shards; the optimizer below sees the rest
+        from ..parallel.zero3 import Zero3Layers
+        student.gradient_checkpointing = False      # the sharded layers recompute already
+        z3 = Zero3Layers(student.model.layers, lr=args.lr, weight_decay=args.weight_decay)
     if device.type == "cuda" and world > 1 and os.environ.get("D3D_FUSED_OPT", "1") != "0":
         # reduce-scatter + AdamW + all-gather fused into kernels over NVLink peer memory
         from ..parallel.fsdp import FusedShardedAdamW
@@ -172,6 +184,8 @@ def train(args) -> dict:
     if args.resume:
         ck = Path(args.resume)
         opt.load_state_dict(torch.load(ck / f"optim_rank{rank:03d}.pt"))
+        if z3 is not None:
+            z3.load_state_dict(torch.load(ck / f"layers_rank{rank:03d}.pt"))
         st = json.loads((ck / "trainer_state.json").read_text())
         start, cursor0 = st["step"], st.get("data_cursor")
     mask_id = int(student.cfg.mask_token_id)
@@ -203,7 +217,10 @@ def train(args) -> dict:
                 _all_sum(0.0, device)
             lr = cosine_lr(step, args.lr, args.warmup_steps, args.max_steps, args.min_lr_ratio)
             opt.zero_grad()
-            gnorm = opt.step(args.grad_clip, lr)
+            if z3 is not None:
+                passes = 1 + (1 if getattr(args, "ar_weight", 0.0) else 0)
+                z3.idle_exchanges(passes * len(z3.specs))
+            gnorm = _opt_step(opt, z3, args.grad_clip, lr)
             rec = {"step": step + 1, "loss": _all_sum(0.0, device), "kl": _all_sum(0.0, device),
                    "ce": _all_sum(0.0, device), "grad_norm": gnorm, "lr": lr,
                    "tokens": int(_all_sum(0.0, device)), "step_s": time.perf_counter() - t0, "empty_rank": True}
@@ -212,7 +229,7 @@ def train(args) -> dict:
                 with open(out_dir / "training_metrics.jsonl", "a") as f:
                     f.write(json.dumps(rec) + "\n")
             if args.save_every and (step + 1) % args.save_every == 0:
-                save_checkpoint(student, opt, out_dir, step + 1, cursor)
+                save_checkpoint(student, opt, out_dir, step + 1, cursor, z3)
             continue
         batch = batch.to(device)
         cache = clean_prefill(student, batch)
@@ -258,7 +275,7 @@ def train(args) -> dict:
                                                                     world)
         loss.backward()
         lr = cosine_lr(step, args.lr, args.warmup_steps, args.max_steps, args.min_lr_ratio)
-        gnorm = opt.step(args.grad_clip, lr)
+        gnorm = _opt_step(opt, z3, args.grad_clip, lr)
         opt.zero_grad()
         if device.type == "cuda":
             torch.cuda.synchronize()
@@ -274,11 +291,24 @@ def train(args) -> dict:
             if args.log_every and (step + 1) % args.log_every == 0:
                 print(json.dumps(rec), flush=True)
         if args.save_every and (step + 1) % args.save_every == 0:
-            save_checkpoint(student, opt, out_dir, step + 1, cursor)
+            save_checkpoint(student, opt, out_dir, step + 1, cursor, z3)
     if args.save_final:
-        save_checkpoint(student, opt, out_dir, args.max_steps, cursor)
+        save_checkpoint(student, opt, out_dir, args.max_steps, cursor, z3)
     prefetch.close()
+    if z3 is not None:
+        z3.close()
     return {"log": log, "elapsed_s": time.perf_counter() - t_start, "world": world}
+
+
+def _opt_step(opt, z3, grad_clip: float, lr: float) -> float:
+    """Optimizer step of the replicated parameters and, with sharded decoder
+    layers, of their shards -- one gradient norm and clip factor for both."""
+    if z3 is None:
+        return opt.step(grad_clip, lr)
+    gnorm = opt.step(grad_clip, lr, extra_sumsq=z3.sumsq())
+    z3.step(opt.last_scale, lr)
+    z3.zero_grad()
+    return gnorm
 
 
 def _argmax_rows(h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
