@@ -127,7 +127,7 @@ def bench_gemm_sweep(m, iters, peaks, rows, shapes=DRAFTER_SHAPES):
         del ws
 
 
-def bench_lmhead(iters, peaks, rows, only_m=None):
+def bench_lmhead(iters, peaks, rows, only_m=None, bts=None):
     from d3d_b200 import ops
     E = ops.ext()
     for m, n, k, kk in ((1, 151936, 4096, 1), (16, 151936, 4096, 1), (272, 151936, 2048, 2),
@@ -145,15 +145,16 @@ def bench_lmhead(iters, peaks, rows, only_m=None):
         ov = torch.empty(m, kk, device="cuda")
         oi = torch.empty(m, kk, dtype=torch.int64, device="cuda")
 
-        def f(i):
-            E.gemm_topk(x, ws[i % 2].data, tv, ti, kk, ops.bt_for(m), None, n)
-            E.topk_merge(tv, ti, m, nt, kt, kk, ov, oi)
-        us = timeit(f, iters)
-        byts = n * k * 2
-        rows.append(dict(kernel="gemm_topk+merge", shape=f"lm_head top{kk}", M=m, N=n, K=k,
-                         us=round(us, 2), GBps=round(byts / us / 1e3, 1),
-                         hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3),
-                         TFLOPs=round(2 * m * n * k / us / 1e6, 1)))
+        for bt in (bts or [ops.bt_for(m)]):
+            def f(i):
+                E.gemm_topk(x, ws[i % 2].data, tv, ti, kk, bt, None, n)
+                E.topk_merge(tv, ti, m, nt, kt, kk, ov, oi)
+            us = timeit(f, iters)
+            byts = n * k * 2
+            rows.append(dict(kernel="gemm_topk+merge", shape=f"lm_head top{kk}", M=m, N=n, K=k, bt=bt,
+                             us=round(us, 2), GBps=round(byts / us / 1e3, 1),
+                             hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3),
+                             TFLOPs=round(2 * m * n * k / us / 1e6, 1)))
 
 
 def bench_attn(iters, peaks, rows, only=None, graph=True):
@@ -322,6 +323,7 @@ def main():
     ap.add_argument("--json", default=None)
     ap.add_argument("--layers", type=int, default=36)
     ap.add_argument("--lm-m", type=int, default=None)
+    ap.add_argument("--lm-bt", default=None, help="lmhead: comma-separated token tiles to time")
     ap.add_argument("--drafter", action="store_true", help="forward: drafter packed M=272")
     ap.add_argument("--sweep-m", type=int, default=272, help="gemm_sweep: token count")
     ap.add_argument("--attn-case", default=None, help="attn: run only this shape (e.g. 'packed 1.7B A1')")
@@ -344,7 +346,8 @@ def main():
         shapes += [("square 8192", 8192, 8192, 8192)]
         bench_gemm(shapes, a.iters, peaks, rows)
     if "lmhead" in only:
-        bench_lmhead(a.iters, peaks, rows, a.lm_m)
+        bench_lmhead(a.iters, peaks, rows, a.lm_m,
+                     [int(b) for b in a.lm_bt.split(",")] if a.lm_bt else None)
     if "attn" in only:
         bench_attn(a.iters, peaks, rows, a.attn_case, not a.no_graph)
     if "gemm_sweep" in only:

@@ -34,6 +34,7 @@ def _steps(dev, rank, world):
     b = build_model(tiny_drafter(), seed=3, dtype=torch.bfloat16, device=dev)
     a.train()
     b.train()
+    init = {n: p.detach().float().cpu().clone() for n, p in a.named_parameters() if n.startswith("model.layers.")}
     z = Zero3Layers(b.model.layers, lr=1e-3, weight_decay=0.01)
     oa = ShardedAdamW(list(a.parameters()), lr=1e-3, weight_decay=0.01)
     ob = ShardedAdamW(list(b.parameters()), lr=1e-3, weight_decay=0.01)
@@ -51,11 +52,16 @@ def _steps(dev, rank, world):
         ob.zero_grad()
         norms.append((na, nb))
     full = z.full_state("model.layers.")
-    worst = 0.0
+    # Adam's first steps move each weight by about lr * sign(g), so a gradient
+    # element near zero whose last bits differ (non-deterministic attention
+    # backward) flips a whole update: compare the update vectors in norm
+    diff = upd = 0.0
     for n, p in a.named_parameters():
         if n.startswith("model.layers."):
-            worst = max(worst, (full[n].float() - p.detach().float().cpu()).abs().max().item())
-    out = {"worst": worst, "norms": norms, "status": int(z.status.item())}
+            w = p.detach().float().cpu()
+            diff += (full[n].float() - w).square().sum().item()
+            upd += (w - init[n]).square().sum().item()
+    out = {"rel": (diff / max(upd, 1e-30)) ** 0.5, "norms": norms, "status": int(z.status.item())}
     z.close()
     return out
 
@@ -65,8 +71,7 @@ def test_sharded_layers_one_gpu():
     assert r["status"] == 0
     for na, nb in r["norms"]:
         assert abs(na - nb) <= 1e-3 * max(1.0, na)
-    # bf16 weights after three AdamW steps of lr 1e-3 agree to a bf16 ulp of the update
-    assert r["worst"] < 2e-3
+    assert r["rel"] < 0.05
 
 
 def _worker(rank, port, out_path):
@@ -95,4 +100,4 @@ def test_sharded_layers_two_gpus():
     assert r["status"] == 0
     for na, nb in r["norms"]:
         assert abs(na - nb) <= 1e-3 * max(1.0, na)
-    assert r["worst"] < 2e-3
+    assert r["rel"] < 0.05
