@@ -35,6 +35,7 @@ memory, so the coordinator reads it after one stream synchronize.
 """
 from __future__ import annotations
 
+import os
 import traceback
 from typing import Dict, List, Optional
 
@@ -130,7 +131,8 @@ class P2PTargetServer:
         hb.copy_(hidden.to(torch.bfloat16).reshape(-1).cpu())
         self._reply_host((ho + 2 * n * self.H + 7) // 8)
 
-    def _verify(self, h) -> None:
+    def _verify(self, h) -> list:
+        """Run one VERIFY; returns its sequences (in request order)."""
         B, K = int(h[1]), int(h[2])
         meta = self.req[HDR:HDR + 2 * B].view(B, 2).tolist()
         blocks = self.req[HDR + 2 * B:HDR + 2 * B + B * K].view(B, K).clone()
@@ -144,7 +146,7 @@ class P2PTargetServer:
                 self.be.submit_verify(group, blocks, sink=lambda ids, post, xn: None)
             else:
                 self.be.verify(group, blocks)
-            return
+            return group
         if not self.fused:
             r = self.be.verify(group, blocks)
             words = _verify_words(B, K)
@@ -158,7 +160,7 @@ class P2PTargetServer:
             if r.hidden is not None:
                 hb.copy_(r.hidden.to(torch.bfloat16).reshape(-1).cpu())
             self._reply_host((ho + 2 * B * self.H + 7) // 8)
-            return
+            return group
         seq = self.link.send_seq + 1
         self.link.send_seq = seq
         out_ptr = self.link.outbox.slot_ptr(seq)
@@ -170,12 +172,72 @@ class P2PTargetServer:
             E.accept_send(ids, post, xn, out_ptr, hid_ptr, flag_ptr, seq)
 
         self.be.submit_verify(group, blocks, sink=sink)
+        return group
+
+    # ------------------------------------------------------ armed verifies
+    def _can_arm(self) -> bool:
+        return (self.fused and self.replies == "all" and getattr(self.be, "supports_arm", False)
+                and os.environ.get("D3D_ARMED_VERIFY", "1") != "0")
+
+    def _arm(self, group: list, K: int):
+        """Enqueue the verify of ``group``'s next block before its request
+        exists (``FastTarget.arm_verify``): the request is read from the inbox
+        on the device, and the reply goes out from the device as before."""
+        lk = self.link
+        seq_in, seq_out = lk.recv_seq + 1, lk.send_seq + 1
+        B = len(group)
+        src = torch.tensor([[lk.inbox.flag.data_ptr()], [lk.inbox.slot(seq_in).data_ptr()],
+                            [self.req.data_ptr()], [seq_in]], dtype=torch.int64)
+        rows_of = torch.tensor([[0], [B]], dtype=torch.int64)
+        out_ptr = lk.outbox.slot_ptr(seq_out)
+        hid_ptr = out_ptr + hidden_offset(_verify_words(B, K))
+        flag_ptr = lk.outbox.flag_ptr
+        E = ops.ext()
+
+        def sink(ids, post, xn, gate):
+            E.accept_send(ids, post, xn, out_ptr, hid_ptr, flag_ptr, seq_out, gate)
+
+        arm = self.be.arm_verify(group, K, [s.index for s in group], src, rows_of, sink, HEAD_WORDS)
+        return arm, group, seq_in, seq_out
+
+    def _armed_outcome(self, armed) -> str:
+        """``"verified"`` (the armed verify ran on the request and replied),
+        ``"message"`` (another message arrived: its head is in ``req``) or
+        ``"none"`` (nothing arrived within the kernel's bounded wait)."""
+        arm, group, seq_in, seq_out = armed
+        arm["ev"].synchronize()
+        st0, overall = int(arm["status"][0]), int(arm["status"][1])
+        if overall == 0:
+            self.link.recv_seq, self.link.send_seq = seq_in, seq_out
+            B = len(group)
+            for (sid, prefix), s in zip(self.req[HDR:HDR + 2 * B].view(B, 2).tolist(), group):
+                s.prefix = prefix
+            return "verified"
+        if st0 == 1:
+            self.link.recv_seq = seq_in
+            return "message"
+        return "none"
 
     def serve(self, poll=None) -> None:
         """Answer requests until CLOSE.  ``poll()`` is called whenever a
-        bounded wait for the next request ran out (it may raise to stop)."""
+        bounded wait for the next request ran out (it may raise to stop).
+        On a GPU link with a greedy single-GPU target, every VERIFY is
+        followed at once by an armed verify of the same sequences, so the
+        next request starts verifying the moment it lands."""
+        armed = None
         while True:
-            self.link.recv(self.req[:HEAD_WORDS], self.stream, deadline_s=self.deadline_s, poll=poll)
+            have = False
+            if armed is not None:
+                kind = self._armed_outcome(armed)
+                group = armed[1]
+                armed = None
+                if kind == "verified":
+                    self.served += 1
+                    armed = self._arm(group, int(self.req[2]))
+                    continue
+                have = kind == "message"
+            if not have:
+                self.link.recv(self.req[:HEAD_WORDS], self.stream, deadline_s=self.deadline_s, poll=poll)
             h = self.req[:HDR].tolist()
             cmd = h[0]
             chk = getattr(self.be, "check_tp", None)
@@ -189,7 +251,9 @@ class P2PTargetServer:
                 return
             try:
                 if cmd == CMD_VERIFY:
-                    self._verify(h)
+                    group = self._verify(h)
+                    if self._can_arm():
+                        armed = self._arm(group, int(h[2]))
                 elif cmd == CMD_PREFILL:
                     self._prefill(h)
                 elif cmd == CMD_RELEASE:
@@ -238,6 +302,14 @@ class P2PTarget(TargetBackend):
         self.supports_gather = gpu and draft_stream is not None
         self.dev_req = torch.zeros(words, dtype=torch.int64, device=self.device) if self.supports_gather \
             else None
+        # device branch select (``arm_select``): pinned status, table buffers
+        self._armed: Optional[tuple] = None
+        self._sent = False
+        if self.supports_gather:
+            self.sel_status = torch.zeros(2, dtype=torch.int32, pin_memory=True)
+            self.sel_ev = torch.cuda.Event()
+            self._tab_h = torch.zeros(4096, dtype=torch.int64, pin_memory=True)
+            self._tab_d = torch.zeros(4096, dtype=torch.int64, device=self.device)
 
     def _send(self, n_words: int) -> None:
         n = (n_words + 1) // 2 * 2
@@ -324,13 +396,82 @@ class P2PTarget(TargetBackend):
                 lk.send(self.dev_req[:n], self.stream)
         self._pending = (B, K)
 
+    @property
+    def supports_select(self) -> bool:
+        return self.supports_gather and os.environ.get("D3D_DEVICE_SELECT", "1") != "0"
+
+    def arm_select(self, B: int, K: int, nk: int, a0: bool, n_eos: int, ctrl: bool, top, tab: List[int]) -> bool:
+        """Enqueue the ``select_send`` kernel for the outstanding verify: behind
+        the drafter's forward (whose ``top`` ids it reads), it waits for the
+        reply and, when every row continues on a drafted branch, sends the
+        next VERIFY to the target itself.  ``tab`` is the kernel's table
+        (sequence ids, prefixes, finishing limits, branch keys and rows, stop
+        tokens, controlled drafts).  ``receive`` then reads the reply the
+        kernel copied; ``select_sent`` says whether the request went out."""
+        if self._pending is None or self._armed is not None or not self.supports_select:
+            return False
+        n = len(tab)
+        if n > self._tab_h.numel():
+            self._tab_h = torch.zeros(2 * n, dtype=torch.int64, pin_memory=True)
+            self._tab_d = torch.zeros(2 * n, dtype=torch.int64, device=self.device)
+        self._tab_h[:n] = torch.tensor(tab, dtype=torch.int64)
+        lk = self.link
+        rseq = lk.recv_seq + 1
+        words = _verify_words(B, K)
+        hw = words + words % 2
+        outs = torch.tensor([[l.outbox.slot_ptr(l.send_seq + 1) for l in self.links],
+                             [l.outbox.flag_ptr for l in self.links],
+                             [l.send_seq + 1 for l in self.links]], dtype=torch.int64)
+        self.sel_status.fill_(-1)
+        E = ops.ext()
+        with torch.cuda.stream(self.stream):
+            self.stream.wait_stream(self.draft_stream)
+            self._tab_d[:n].copy_(self._tab_h[:n], non_blocking=True)
+            E.select_send(lk.inbox.flag, lk.inbox.slot(rseq).view(torch.int64), rseq, self.rep[:hw], B, K, nk, a0,
+                          n_eos, ctrl, top, self._tab_d, outs, self.sel_status)
+            self.sel_ev.record(self.stream)
+        self._armed = (rseq, B, K)
+        return True
+
+    def select_sent(self) -> bool:
+        """Whether the device sent the next VERIFY (valid after ``receive``)."""
+        return self._sent
+
+    def adopt_sent(self, B: int, K: int) -> None:
+        """Record the request the device sent as the outstanding verify."""
+        if self._pending is not None:
+            raise RuntimeError("target already has an outstanding verify")
+        self._sent = False
+        self._pending = (B, K)
+
     def receive(self) -> VerifyResult:
         if self._pending is None:
             raise RuntimeError("no outstanding target request")
         B, K = self._pending
         self._pending = None
         words = _verify_words(B, K)
-        r = self._recv(CMD_VERIFY, words)
+        armed, self._armed = self._armed, None
+        self._sent = False
+        if armed is not None:
+            rseq = armed[0]
+            self.sel_ev.synchronize()
+            if int(self.sel_status[0]) == 0:
+                # the reply is in; its head is in ``rep`` already
+                self.link.recv_seq = rseq
+                if int(self.rep[0]) == CMD_ERROR:
+                    self.link.recv_seq -= 1     # re-read it through the error path below
+                    r = self._recv(CMD_VERIFY, words)
+                if int(self.rep[0]) != CMD_VERIFY:
+                    raise RuntimeError(f"target protocol error: expected {CMD_VERIFY}, got {int(self.rep[0])}")
+                r = self.rep
+                if int(self.sel_status[1]) == 1:
+                    self._sent = True
+                    for lk in self.links:
+                        lk.send_seq += 1
+            else:
+                r = self._recv(CMD_VERIFY, words)
+        else:
+            r = self._recv(CMD_VERIFY, words)
         res = r[HDR:words].view(B, 2 + K).clone()
         hid = self._bf16_block(words, B, words + words % 2).clone() if self.want_hidden else None
         return VerifyResult(res[:, 0], res[:, 1], res[:, 2:], hid)
@@ -451,6 +592,7 @@ class BatchedTargetServer:
             spans.append((d, len(group) - B, B))
         blocks = torch.cat(blocks)
         fused = self.subs[0].fused
+        self._last_verify = (group, K)
         if self.replies != "all":
             if fused:
                 self.be.submit_verify(group, blocks, sink=lambda ids, post, xn: None)
@@ -490,6 +632,70 @@ class BatchedTargetServer:
 
         self.be.submit_verify(group, blocks, sink=sink)
 
+    # ------------------------------------------------------ armed rounds
+    def _arm_round(self, ds: List[int], group: list, K: int):
+        """Enqueue the next round's merged verify before its requests exist
+        (``FastTarget.arm_verify`` over every drafter's inbox, rows in the
+        order of the round just enqueued); each drafter's reply goes out from
+        the device behind it, gated on all requests matching."""
+        src = [[], [], [], []]
+        rows_of = [[], []]
+        exp, outs, r0 = [], [], 0
+        for d in ds:
+            sub = self.subs[d]
+            lk = sub.link
+            B = sum(1 for s in group if s.index // self.ID_STRIDE == d)
+            seq_in, seq_out = lk.recv_seq + 1, lk.send_seq + 1
+            for col, v in zip(src, (lk.inbox.flag.data_ptr(), lk.inbox.slot(seq_in).data_ptr(),
+                                   sub.req.data_ptr(), seq_in)):
+                col.append(v)
+            rows_of[0].append(r0)
+            rows_of[1].append(B)
+            exp += [s.index % self.ID_STRIDE for s in group[r0:r0 + B]]
+            out_ptr = lk.outbox.slot_ptr(seq_out)
+            outs.append((d, r0, B, out_ptr, out_ptr + hidden_offset(_verify_words(B, K)), lk.outbox.flag_ptr,
+                         seq_out, seq_in))
+            r0 += B
+        if r0 != len(group):
+            return None
+        E = ops.ext()
+
+        def sink(ids, post, xn, gate):
+            for d, q0, B, out_ptr, hid_ptr, flag_ptr, seq_out, _ in outs:
+                E.accept_send(ids[q0:q0 + B], post[q0:q0 + B], xn[q0 * K:(q0 + B) * K], out_ptr, hid_ptr,
+                              flag_ptr, seq_out, gate)
+
+        arm = self.be.arm_verify(group, K, exp, torch.tensor(src, dtype=torch.int64),
+                                 torch.tensor(rows_of, dtype=torch.int64), sink, HEAD_WORDS)
+        return arm, ds, group, K, outs
+
+    def _armed_round(self, armed):
+        """Outcome of an armed round: ``(True, {})`` when its verify ran on
+        every drafter's request, else ``(False, heads)`` with the headers of
+        the messages that did arrive (the others are still to be received)."""
+        arm, ds, group, K, outs = armed
+        arm["ev"].synchronize()
+        st = arm["status"]
+        if int(st[len(ds)]) == 0:
+            for d, q0, B, _, _, _, seq_out, seq_in in outs:
+                sub = self.subs[d]
+                sub.link.recv_seq, sub.link.send_seq = seq_in, seq_out
+                for (sid, prefix), s in zip(sub.req[HDR:HDR + 2 * B].view(B, 2).tolist(), group[q0:q0 + B]):
+                    s.prefix = prefix
+            return True, {}
+        heads = {}
+        for i, (d, _, _, _, _, _, _, seq_in) in enumerate(outs):
+            if int(st[i]) == 1:
+                sub = self.subs[d]
+                sub.link.recv_seq = seq_in
+                h = sub.req[:HDR].tolist()
+                if h[0] == CMD_PREFILL:
+                    words = HDR + 2 * h[1] + h[2]
+                    if words > HEAD_WORDS:
+                        sub.link.fetch(sub.req[HEAD_WORDS:words], 8 * HEAD_WORDS, sub.stream)
+                heads[d] = h
+        return False, heads
+
     def _release(self, d: int, sid: int) -> None:
         s = self.seqs.pop(self._gid(d, sid), None)
         if s is not None:
@@ -501,8 +707,20 @@ class BatchedTargetServer:
 
     def serve(self, poll=None) -> None:
         active = list(range(len(self.subs)))
+        can_arm = (self.replies == "all" and self.subs[0].fused and getattr(self.be, "supports_arm", False)
+                   and os.environ.get("D3D_ARMED_VERIFY", "1") != "0")
+        armed = None
         while active:
-            msgs = [(d, self._recv(d, poll)) for d in active]
+            heads = {}
+            if armed is not None:
+                done, heads = self._armed_round(armed)
+                prev, armed = armed, None
+                if done:
+                    self.rounds += 1
+                    self.served += len(prev[1])
+                    armed = self._arm_round(prev[1], prev[2], prev[3])
+                    continue
+            msgs = [(d, heads[d] if d in heads else self._recv(d, poll)) for d in active]
             chk = getattr(self.be, "check_tp", None)
             if chk is not None:
                 chk()   # a failed tensor-parallel exchange ends serving loudly
@@ -515,6 +733,9 @@ class BatchedTargetServer:
             for d, h in by.pop(CMD_VERIFY, []):     # one batched verify per block size
                 by_k.setdefault(int(h[2]), []).append((d, h))
             batches += [(self._verify, by_k[k]) for k in sorted(by_k)]
+            # a round of nothing but one verify from every open drafter arms the next
+            arm_next = (can_arm and len(by_k) == 1 and not batches[0][1] and len(by) == 0
+                        and len(next(iter(by_k.values()))) == len(active))
             for run, items in batches:
                 if not items:
                     continue
@@ -524,6 +745,7 @@ class BatchedTargetServer:
                 except Exception as exc:  # every drafter of the batch hears about it
                     if self.replies != "all":
                         raise
+                    arm_next = False
                     for d, _ in items:
                         self.subs[d]._send_error(exc)
             for d, h in by.pop(CMD_RELEASE, []):
@@ -535,3 +757,6 @@ class BatchedTargetServer:
                     if self.replies == "all":
                         self.subs[d]._send_error(ValueError(f"unknown target command {kind}"))
             active = [d for d in active if d not in closed]
+            if arm_next and active:
+                group, K = self._last_verify
+                armed = self._arm_round([d for d, _ in next(iter(by_k.values()))], group, K)

@@ -213,6 +213,8 @@ class FastTarget(_FastModelBackend, TargetBackend):
         self.hidden_size = self.cfg.hidden_size
         self.tp = tp
         self._pending = None
+        self._arm_bufs: Dict[int, dict] = {}
+        self.scratch = self.kv.scratch_slot()
         self._accept_bufs: Dict[tuple, dict] = {}
         self.verify_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
         self.time_verify = False
@@ -343,6 +345,67 @@ class FastTarget(_FastModelBackend, TargetBackend):
         return fn
 
     supports_gather = True
+
+    @property
+    def supports_arm(self) -> bool:
+        """Greedy verification on one GPU can be armed ahead of its request."""
+        return not self.sampled and self.tp is None
+
+    @torch.inference_mode()
+    def arm_verify(self, seqs, K: int, exp_sids, sources, rows_of, sink, head_words: int) -> dict:
+        """Enqueue the next greedy verify of ``seqs`` (in the order of the
+        last verify of this shape) before its request has arrived: the
+        ``verify_arm`` kernel waits for the request messages, writes the
+        graph's inputs from them (or placeholders and a cleared gate when a
+        message does not match), then the captured verify graph and
+        ``sink(ids, posterior, hidden, gate)`` run.  ``exp_sids``: the
+        sequence ids the messages must carry, per row; ``sources`` int64
+        [4, n_src] (inbox flag, message slot, pinned head copy, sequence
+        number) and ``rows_of`` [2, n_src] (first row, rows) as the kernel
+        takes them; ``head_words`` of each message are copied to its pinned
+        head buffer.  Returns the arm's buffers: ``status`` (pinned; [n_src]
+        is 0 when the armed verify is valid) is final once ``ev`` has
+        completed."""
+        B = len(seqs)
+        if not self.supports_arm:
+            raise RuntimeError("only greedy single-GPU verification can be armed")
+        b = self.runner.buffers(B, K, 1)
+        a = self._abufs(B, K)
+        arm = self._arm_bufs.get(B)
+        if arm is None:
+            arm = dict(tab=torch.zeros(2 * B, dtype=torch.int64, device=self.device),
+                       tab_h=torch.zeros(2 * B, dtype=torch.int64, pin_memory=True),
+                       gate=torch.zeros(1, dtype=torch.int32, device=self.device),
+                       status=torch.zeros(9, dtype=torch.int32, pin_memory=True),
+                       ev=torch.cuda.Event())
+            self._arm_bufs[B] = arm
+        th = arm["tab_h"]
+        th[:B] = torch.tensor([int(x) for x in exp_sids], dtype=torch.int64)
+        th[B:] = torch.tensor([len(self.kv.tables.get(s.index, ())) * self.kv.page_size for s in seqs],
+                              dtype=torch.int64)
+        arm["status"].fill_(-1)
+        E = ops.ext()
+        with torch.cuda.stream(self.stream):
+            arm["tab"].copy_(th, non_blocking=True)
+            E.verify_arm(sources, rows_of, K, head_words, self.kv.page_size, arm["tab"], self.kv.block_table,
+                         b.seq_rows, self.scratch, b.ids, b.pos, b.slots, b.rows.view(-1), b.kv_end, arm["gate"],
+                         arm["status"])
+            arm["ev"].record(self.stream)
+            ev0 = ev1 = None
+            if self.time_verify:     # the verify proper: from its request's arrival to its reply
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record(self.stream)
+        launches.add(2)
+        tok = self.prof.dev_begin(f"verify_B{B}_K{K}", self.stream)
+        self.graphs.run(("verify", B, K), b, self._verify_fn(a))
+        self.prof.dev_end(tok)
+        with torch.cuda.stream(self.stream):
+            sink(b.ids.view(B, K), b.top_i[:, 0].view(B, K), b.xn, arm["gate"])
+            if ev1 is not None:
+                ev1.record(self.stream)
+                self.verify_events.append((ev0, ev1))
+        launches.add(1)
+        return arm
 
     @torch.inference_mode()
     def submit_verify(self, seqs, blocks, q=None, sink=None, gather=None):

@@ -265,6 +265,60 @@ class SpecDecoder:
                 results[s.index] = _Outcomes(lay, out, i, q)
         return results
 
+    def _arm_select(self, running: List[SeqState], predictions, block_t: torch.Tensor) -> bool:
+        """Hand the choice of verify(t+1)'s blocks to the drafter GPU (the
+        target backend's ``arm_select``): per row the sequence id, prefix,
+        the commit length at which the row finishes (output budget, or a stop
+        token among the block's drafts), the packed forward's branch keys
+        with the first row of each branch, the stop tokens, and -- in
+        acceptance-controlled mode -- the controlled drafts of the positions
+        the next block can cover.  The kernel sends only when every row
+        continues on a drafted branch, exactly when the host loop would
+        enqueue verify(t+1) ahead; otherwise the host takes the step."""
+        cfg, k = self.cfg, self.cfg.block_size
+        B = len(running)
+        if B == 0 or B > 64:
+            return False
+        ctrl = running[0].controlled is not None
+        if any((s.controlled is not None) != ctrl for s in running):
+            return False
+        prs = [predictions.get(s.index) for s in running]
+        if any(p is None for p in prs):
+            return False
+        top = None
+        for p in prs:
+            src = p._out["dev_top"] if isinstance(p._out, dict) else getattr(p._out, "dev_top", None)
+            if src is None or (top is not None and src is not top):
+                return False
+            top = src
+        nk = max(len(p.lay.keys) for p in prs)
+        eos = [] if cfg.ignore_eos else [int(t) for t in cfg.eos]
+        sid, pref, lim, keys, krows, ctl = [], [], [], [], [], []
+        for r, (s, p) in enumerate(zip(running, prs)):
+            for j, key in enumerate(p.lay.keys):
+                sl = p.lay.segment(j)
+                if sl.stop - sl.start != k:
+                    return False
+                keys += [int(key[0]), -1 if key[1] is None else int(key[1])]
+                krows.append(p.i * p.q_len + sl.start)
+            pad = nk - len(p.lay.keys)
+            keys += [-1, -1] * pad
+            krows += [0] * pad
+            room = s.budget - len(s.generated)
+            first_stop = k
+            if eos:
+                for j, tok in enumerate(block_t[r, :k].tolist()):
+                    if tok in cfg.eos:
+                        first_stop = j
+                        break
+            lim.append(min(room, first_stop + 1))
+            sid.append(int(s.index))
+            pref.append(int(s.prefix))
+            if ctrl:
+                ctl += [int(s.controlled.draft_at(s.prefix + 1 + m)) for m in range(2 * k)]
+        tab = sid + pref + lim + keys + krows + eos + ctl
+        return self.t.arm_select(B, k, nk, cfg.anchor_num == 0, len(eos), ctrl, top, tab)
+
     # ------------------------------------------------------------ main loop
     def generate(self, prompts: Sequence[Sequence[int]], concurrency: int = 1,
                  controlled: Optional[Callable[[int], object]] = None,
@@ -336,8 +390,12 @@ class SpecDecoder:
             pipe = self._pipelined()
             with self.prof.phase("predict"):
                 predictions = self.predict(running, wait=not pipe) if width == k else {}
+            armed = (pipe and width == k and (exhausted or len(running) >= concurrency)
+                     and getattr(self.t, "supports_select", False)
+                     and self._arm_select(running, predictions, block_t))
             with self.prof.phase("receive"):
                 res = self.t.receive()
+            dev_sent = bool(armed) and self.t.select_sent()
             steps += 1
             verify_tokens += width * len(running)
             remaining, recover = [], []
@@ -375,7 +433,20 @@ class SpecDecoder:
             # admitted: enqueue verify(t+1) now, behind draft(t) on the same
             # stream, so the GPU goes straight on while the host selects.
             nxt = None
-            if pipe and cont and (exhausted or len(cont) >= concurrency) and all(
+            if dev_sent:
+                # the drafter GPU already picked every row's branch and sent
+                # verify(t+1); the host mirrors that choice for its records
+                if len(cont) != len(running) or not all(
+                        predictions.get(c[0].index) is not None and predictions[c[0].index].has(c[3])
+                        for c in cont):
+                    raise RuntimeError("device branch select disagrees with the host's selection")
+                nxt = torch.zeros(len(cont), k, dtype=torch.long)
+                for r, (s, n, corr, key) in enumerate(cont):
+                    nxt[r, 0] = corr
+                    if s.controlled is not None:
+                        self._controlled(s, nxt[r], None, s.prefix)
+                self.t.adopt_sent(len(cont), k)
+            elif pipe and cont and (exhausted or len(cont) >= concurrency) and all(
                     predictions.get(c[0].index) is not None and predictions[c[0].index].has(c[3])
                     for c in cont):
                 nxt = torch.zeros(len(cont), k, dtype=torch.long)

@@ -204,6 +204,16 @@ class PagedKV:
         self.max_seqs = max_seqs
         self.block_table = torch.zeros(max_seqs, max_pages_per_seq, dtype=torch.int32, device=device)
         self.device = device
+        self.scratch: List[int] = []    # pages held outside any sequence (placeholder KV stores)
+
+    def scratch_slot(self) -> int:
+        """A KV slot of a page no sequence ever owns: where the KV stores of a
+        forward run on placeholder inputs go."""
+        if not self.scratch:
+            if not self.free:
+                raise RuntimeError("out of KV pages for the scratch page")
+            self.scratch.append(self.free.pop())
+        return self.scratch[0] * self.page_size
 
     def reserve(self, sid: int, row: int, length: int) -> None:
         """Make sequence ``sid`` (block-table row ``row``) cover ``length`` slots."""
@@ -238,7 +248,7 @@ class PagedKV:
 
     @property
     def leaked(self) -> int:
-        return self.num_pages - len(self.free) - sum(len(t) for t in self.tables.values())
+        return self.num_pages - len(self.free) - sum(len(t) for t in self.tables.values()) - len(self.scratch)
 
 
 # --------------------------------------------------------------------------
@@ -468,7 +478,8 @@ class FastRunner:
             ti = torch.empty(T * nt * 2, dtype=torch.int32, device=dev)
             xh = x[:, : self.cfg.hidden_size]
             best = None
-            for bt in sorted({base, ops.bt_for((T + 1) // 2), ops.bt_for((T + 2) // 3)}):
+            for bt in sorted({b for b in (base, ops.bt_for((T + 1) // 2), ops.bt_for((T + 2) // 3), 96, 64, 48)
+                              if b <= base}):
                 t = timed(lambda i: E.gemm_topk(xh, lm.data, tv, ti, 2, bt, st, lm.n))
                 if best is None or t < best[0]:
                     best = (t, bt)

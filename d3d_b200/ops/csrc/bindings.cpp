@@ -450,7 +450,7 @@ void handoff_wait(Tensor flag, int64_t seq, c10::optional<Tensor> src, c10::opti
                     nbytes, status.data_ptr<int>(), kTimeoutNs, cur_stream());
 }
 void accept_send(Tensor blocks, Tensor post, c10::optional<Tensor> hidden, int64_t out_ptr, int64_t hid_ptr,
-                 int64_t flag_ptr, int64_t seq) {
+                 int64_t flag_ptr, int64_t seq, c10::optional<Tensor> gate) {
   const c10::cuda::CUDAGuard g(blocks.device());
   CHECK_DT(blocks, torch::kInt64);
   CHECK_DT(post, torch::kInt64);
@@ -460,7 +460,118 @@ void accept_send(Tensor blocks, Tensor post, c10::optional<Tensor> hidden, int64
   const int H = hidden ? static_cast<int>(hidden->size(-1)) : 0;
   d3d::accept_send(blocks.data_ptr<int64_t>(), post.data_ptr<int64_t>(), B, K, hidden ? cbf(*hidden) : nullptr, H,
                    reinterpret_cast<int64_t*>(out_ptr), reinterpret_cast<__nv_bfloat16*>(hid_ptr),
-                   reinterpret_cast<int64_t*>(flag_ptr), seq, cur_stream());
+                   reinterpret_cast<int64_t*>(flag_ptr), seq, gate ? gate->data_ptr<int>() : nullptr, cur_stream());
+}
+
+// ``src``: int64 CPU [4, n_src] = inbox flag, message slot, pinned head copy
+// (addresses) and expected sequence number per source; ``rows``: int64 CPU
+// [2, n_src] = first merged row and row count per source.
+void verify_arm(Tensor src, Tensor rows_of, int64_t K, int64_t head_words, int64_t page, Tensor tab,
+                Tensor block_table, Tensor seq_rows, int64_t scratch_slot, Tensor ids, Tensor pos, Tensor slots,
+                Tensor rows, Tensor kv_end, Tensor gate, Tensor status) {
+  const c10::cuda::CUDAGuard g(ids.device());
+  CHECK_DT(src, torch::kInt64);
+  CHECK_DT(rows_of, torch::kInt64);
+  CHECK_DT(tab, torch::kInt64);
+  CHECK_DT(block_table, torch::kInt32);
+  CHECK_DT(seq_rows, torch::kInt64);
+  CHECK_DT(rows, torch::kInt32);
+  CHECK_DT(kv_end, torch::kInt32);
+  CHECK_DT(gate, torch::kInt32);
+  CHECK_DT(status, torch::kInt32);
+  TORCH_CHECK(status.is_pinned(), "verify_arm: status must be pinned host memory");
+  const int n = static_cast<int>(src.size(1));
+  TORCH_CHECK(src.dim() == 2 && src.size(0) == 4 && n >= 1 && n <= d3d::ARM_MAX_SRC, "verify_arm: bad source table");
+  TORCH_CHECK(rows_of.dim() == 2 && rows_of.size(0) == 2 && rows_of.size(1) == n, "verify_arm: bad row table");
+  TORCH_CHECK(status.numel() >= n + 1, "verify_arm: status too small");
+  d3d::ArmArgs a{};
+  auto sp = src.contiguous();
+  auto rp = rows_of.contiguous();
+  const int64_t* v = sp.data_ptr<int64_t>();
+  const int64_t* rv = rp.data_ptr<int64_t>();
+  int B = 0;
+  for (int d = 0; d < n; ++d) {
+    a.flag[d] = reinterpret_cast<const int64_t*>(v[d]);
+    a.msg[d] = reinterpret_cast<const int64_t*>(v[n + d]);
+    a.head[d] = reinterpret_cast<int64_t*>(v[2 * n + d]);
+    a.seq[d] = v[3 * n + d];
+    a.row0[d] = static_cast<int>(rv[d]);
+    a.nb[d] = static_cast<int>(rv[n + d]);
+    TORCH_CHECK(a.row0[d] == B, "verify_arm: sources must cover the rows in order");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(a.msg[d]) % 16 == 0 && reinterpret_cast<uintptr_t>(a.head[d]) % 16 == 0,
+                "verify_arm: 16-byte aligned messages");
+    B += a.nb[d];
+  }
+  TORCH_CHECK(tab.numel() >= 2 * B && seq_rows.numel() >= B && kv_end.numel() >= B, "verify_arm: row tables");
+  TORCH_CHECK(ids.numel() >= B * K && pos.numel() >= B * K && slots.numel() >= B * K && rows.numel() >= 3 * B * K,
+              "verify_arm: input buffers too small");
+  a.n_src = n;
+  a.K = static_cast<int>(K);
+  a.head_words = static_cast<int>(head_words);
+  a.page = static_cast<int>(page);
+  a.bt_stride = static_cast<int>(block_table.size(1));
+  a.tab = tab.data_ptr<int64_t>();
+  a.block_table = block_table.data_ptr<int32_t>();
+  a.seq_rows = seq_rows.data_ptr<int64_t>();
+  a.scratch_slot = scratch_slot;
+  a.ids = ids.data_ptr<int64_t>();
+  a.pos = pos.data_ptr<int64_t>();
+  a.slots = slots.data_ptr<int64_t>();
+  a.rows = rows.data_ptr<int32_t>();
+  a.kv_end = kv_end.data_ptr<int32_t>();
+  a.gate = gate.data_ptr<int>();
+  a.status = status.data_ptr<int>();
+  a.limit_ns = kTimeoutNs;
+  d3d::verify_arm(a, cur_stream());
+}
+
+// ``outs``: int64 CPU [3, n_out] = destination slot, destination flag
+// (peer addresses mapped in this process) and sequence number per target rank.
+void select_send(Tensor rflag, Tensor reply, int64_t rseq, Tensor reply_host, int64_t B, int64_t K, int64_t nk,
+                 bool a0, int64_t n_eos, bool ctrl, c10::optional<Tensor> top, Tensor tab, Tensor outs,
+                 Tensor status) {
+  const c10::cuda::CUDAGuard g(tab.device());
+  CHECK_DT(rflag, torch::kInt64);
+  CHECK_DT(reply, torch::kInt64);
+  CHECK_DT(reply_host, torch::kInt64);
+  CHECK_DT(tab, torch::kInt64);
+  CHECK_DT(outs, torch::kInt64);
+  CHECK_DT(status, torch::kInt32);
+  TORCH_CHECK(status.is_pinned() && reply_host.is_pinned(), "select_send: status and reply copy must be pinned");
+  TORCH_CHECK(reply_host.numel() % 2 == 0 && reply.numel() >= reply_host.numel(), "select_send: reply sizes");
+  TORCH_CHECK(ctrl || (top && top->dim() == 2), "select_send: the drafts' top ids are needed without controlled drafts");
+  const int n = static_cast<int>(outs.size(1));
+  TORCH_CHECK(outs.dim() == 2 && outs.size(0) == 3 && n >= 1 && n <= d3d::ARM_MAX_SRC, "select_send: bad outputs");
+  TORCH_CHECK(tab.numel() >= 3 * B + B * nk * 3 + n_eos + (ctrl ? 2 * B * K : 0), "select_send: table too small");
+  d3d::SelectArgs a{};
+  a.rflag = rflag.data_ptr<int64_t>();
+  a.reply = reply.data_ptr<int64_t>();
+  a.rseq = rseq;
+  a.reply_host = reply_host.data_ptr<int64_t>();
+  a.head_words = static_cast<int>(reply_host.numel());
+  a.B = static_cast<int>(B);
+  a.K = static_cast<int>(K);
+  a.nk = static_cast<int>(nk);
+  a.a0 = a0 ? 1 : 0;
+  a.n_eos = static_cast<int>(n_eos);
+  a.ctrl = ctrl ? 1 : 0;
+  if (top) {
+    CHECK_DT(*top, torch::kInt64);
+    a.top = top->data_ptr<int64_t>();
+    a.top_stride = static_cast<int>(top->stride(0));
+  }
+  a.tab = tab.data_ptr<int64_t>();
+  auto op = outs.contiguous();
+  const int64_t* v = op.data_ptr<int64_t>();
+  for (int o = 0; o < n; ++o) {
+    a.out_slot[o] = reinterpret_cast<int64_t*>(v[o]);
+    a.out_flag[o] = reinterpret_cast<int64_t*>(v[n + o]);
+    a.out_seq[o] = v[2 * n + o];
+  }
+  a.n_out = n;
+  a.status = status.data_ptr<int>();
+  a.limit_ns = kTimeoutNs;
+  d3d::select_send(a, cur_stream());
 }
 
 // ------------------------------------------------------------ tensor parallel
@@ -670,7 +781,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ticket") = py::none());
   m.def("handoff_wait", &handoff_wait, py::arg("flag"), py::arg("seq"), py::arg("src"), py::arg("dst"),
         py::arg("status"));
-  m.def("accept_send", &accept_send);
+  m.def("accept_send", &accept_send, py::arg("blocks"), py::arg("post"), py::arg("hidden"), py::arg("out_ptr"),
+        py::arg("hid_ptr"), py::arg("flag_ptr"), py::arg("seq"), py::arg("gate") = py::none());
+  m.def("verify_arm", &verify_arm);
+  m.def("select_send", &select_send);
   m.def("tp_epoch_bump", &tp_epoch_bump);
   m.def("gemm_partial_tp", &gemm_partial_tp, py::arg("x"), py::arg("w"), py::arg("ptrs"), py::arg("rank"),
         py::arg("epoch"), py::arg("ticket"), py::arg("xidx"), py::arg("part_off"), py::arg("splits"),

@@ -53,6 +53,7 @@ constexpr int GBN = 128;  // weight rows per tile (MMA M)
 constexpr int GBK = 64;   // K per stage (one 128-byte swizzle atom of bf16)
 constexpr int A_TILE_BYTES = GBN * GBK * 2;
 constexpr int GEMM_THREADS = 192;
+constexpr int TSCR_WORDS = 32 * 33;   // MODE 2 transpose scratch per epilogue warp
 
 __host__ __device__ inline int acc_cols_for(int bt) {
   if (bt > 256) return 512;
@@ -90,7 +91,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
   const int marea = MODE == 2 ? 4 * bt * KT : 0;
   float* mval = reinterpret_cast<float*>(smem + stages * stage_bytes);
   int* midx = reinterpret_cast<int*>(mval + 2 * marea);
-  uint64_t* full = reinterpret_cast<uint64_t*>(midx + 2 * marea);
+  // MODE 2: per-epilogue-warp transpose scratch, 32 rows x 33 words (padded: conflict-free both ways)
+  uint32_t* tscr = reinterpret_cast<uint32_t*>(midx + 2 * marea);
+  uint64_t* full = reinterpret_cast<uint64_t*>(tscr + (MODE == 2 && bt > 32 ? 4 * TSCR_WORDS : 0));
   uint64_t* empty = full + stages;
   uint64_t* accf = empty + stages;  // [2] accumulator ready for the epilogue
   uint64_t* acce = accf + 2;        // [2] accumulator drained by the epilogue
@@ -358,37 +361,85 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
         }
       } else {
         // ------------------------------------------ MODE 2: per-tile top-KT
-        // Per token column: KT rounds of a warp max (redux.sync on an
-        // order-preserving key) over the warp's 32 rows, the lowest row
-        // winning ties.  The four warps' candidates go to a shared-memory
-        // merge area (double-buffered by unit); warp 2 merges them, one
-        // column per lane, and writes the tile's top-KT.  The hand-offs are
-        // mbarriers with bounded waits, never an unbounded named barrier.
+        // More than 32 token columns: per 32-column chunk, each epilogue warp stores its 32 rows x 32
+        // columns of order-preserving keys (0 = row past N) into its padded
+        // shared-memory scratch and reads them back transposed: lane j then
+        // scans column j's 32 rows in row order, keeping the top KT with the
+        // lowest row winning ties (strict >) -- independent per lane, no
+        // cross-lane chains.  The four warps' candidates go to a merge area
+        // (double-buffered by unit); warp 2 merges them, one column per lane,
+        // and writes the tile's top-KT.  The hand-offs are mbarriers with
+        // bounded waits, never an unbounded named barrier.
         const int cols = min(bt, p.M - m0);
         const int b2 = ti & 1, use2 = ti >> 1;
         float* mv = mval + b2 * marea;
         int* mi = midx + b2 * marea;
+        uint32_t* ts = tscr + q * TSCR_WORDS;
         if (!mbar_wait(&mempty[b2], (use2 & 1) ^ 1, lim)) {
           fail(ERR_TIMEOUT_EPILOGUE);
           break;
         }
-        for (int c = 0; c < cols; c += 16) {
-          float v[16];
-          tmem_ld16(tacc + c, v);
+        if (bt <= 32) {
+          // few token columns (verify / AR): KT rounds of a warp max (redux.sync
+          // on the keys) per column, lowest row winning ties -- same result
+          for (int c = 0; c < cols; c += 16) {
+            float v[16];
+            tmem_ld16(tacc + c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            uint32_t key = n_ok ? float_key(v[j]) : 0u;
+            for (int j = 0; j < 16; ++j) {
+              uint32_t key = n_ok ? float_key(v[j]) : 0u;
 #pragma unroll
-            for (int r = 0; r < KT; ++r) {
-              const uint32_t mx = __reduce_max_sync(0xffffffffu, key);
-              const uint32_t win = __ballot_sync(0xffffffffu, key == mx && mx != 0u);
-              const int wl = win ? __ffs(win) - 1 : 0;
-              if (lane == 0) {
-                const int o = (q * bt + c + j) * KT + r;
-                mv[o] = mx ? key_float(mx) : -INFINITY;
-                mi[o] = mx ? n0 + q * 32 + wl : 0x7fffffff;
+              for (int r = 0; r < KT; ++r) {
+                const uint32_t mx = __reduce_max_sync(0xffffffffu, key);
+                const uint32_t win = __ballot_sync(0xffffffffu, key == mx && mx != 0u);
+                const int wl = win ? __ffs(win) - 1 : 0;
+                if (lane == 0) {
+                  const int o = (q * bt + c + j) * KT + r;
+                  mv[o] = mx ? key_float(mx) : -INFINITY;
+                  mi[o] = mx ? n0 + q * 32 + wl : 0x7fffffff;
+                }
+                if (lane == wl && win) key = 0u;
               }
-              if (lane == wl && win) key = 0u;
+            }
+          }
+        }
+        for (int c0 = 0; bt > 32 && c0 < cols; c0 += 32) {
+          float v[32];
+          tmem_ld16(tacc + c0, v);
+          tmem_ld16(tacc + c0 + 16, v + 16);   // accumulators span >= 32 columns, a multiple of 32
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ts[lane * 33 + j] = n_ok ? float_key(v[j]) : 0u;
+          __syncwarp();
+          uint32_t bk[KT];
+          int br[KT];
+#pragma unroll
+          for (int z = 0; z < KT; ++z) {
+            bk[z] = 0u;
+            br[z] = 0;
+          }
+#pragma unroll 8
+          for (int r = 0; r < 32; ++r) {
+            uint32_t kk = ts[r * 33 + lane];
+            int rr = r;
+#pragma unroll
+            for (int z = 0; z < KT; ++z) {
+              if (kk > bk[z]) {
+                const uint32_t tk = bk[z];
+                const int tr = br[z];
+                bk[z] = kk;
+                br[z] = rr;
+                kk = tk;
+                rr = tr;
+              }
+            }
+          }
+          __syncwarp();   // the scratch is rewritten by the next chunk
+          if (c0 + lane < cols) {
+#pragma unroll
+            for (int z = 0; z < KT; ++z) {
+              const int o = (q * bt + c0 + lane) * KT + z;
+              mv[o] = bk[z] ? key_float(bk[z]) : -INFINITY;
+              mi[o] = bk[z] ? n0 + q * 32 + br[z] : 0x7fffffff;
             }
           }
         }
@@ -611,7 +662,7 @@ void gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   make_tmap_bf16_2d(&tx, a.x, a.K, a.M, a.ldx, GBK, a.bt > 256 ? a.bt / 2 : a.bt);
   const int kt = a.mode == 2 ? (a.topk <= 1 ? 1 : (a.topk <= 2 ? 2 : 4)) : 1;
   if (a.mode == 2 && a.topk > 4) throw std::runtime_error("gemm: fused top-k supports k <= 4");
-  const int reserve = a.mode == 2 ? 2 * 4 * a.bt * kt * 8 : 0;
+  const int reserve = a.mode == 2 ? 2 * 4 * a.bt * kt * 8 + (a.bt > 32 ? 4 * TSCR_WORDS * 4 : 0) : 0;
   GemmParams p{};
   p.M = a.M;
   p.N = a.N;

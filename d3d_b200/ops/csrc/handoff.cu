@@ -111,8 +111,11 @@ void handoff_wait(const int64_t* flag, int64_t seq, const void* src, void* dst, 
 // and then publishes seq.  One block; the commit scan is K steps per row.
 __global__ void accept_send_kernel(const int64_t* __restrict__ blocks, const int64_t* __restrict__ post, int B, int K,
                                    const __nv_bfloat16* __restrict__ hidden, int H, int64_t* out_i64,
-                                   __nv_bfloat16* hid_out, int64_t* flag, int64_t seq) {
+                                   __nv_bfloat16* hid_out, int64_t* flag, int64_t seq, const int* gate) {
   __shared__ int s_commit;
+  // an armed verify whose request did not match ran on placeholder inputs:
+  // nothing is sent (the host answers the message that did arrive)
+  if (gate != nullptr && *reinterpret_cast<const volatile int*>(gate) == 0) return;
   if (threadIdx.x == 0) {
     out_i64[0] = 2;
     out_i64[1] = B;
@@ -144,8 +147,219 @@ __global__ void accept_send_kernel(const int64_t* __restrict__ blocks, const int
 }
 
 void accept_send(const int64_t* blocks, const int64_t* post, int B, int K, const __nv_bfloat16* hidden, int H,
-                 int64_t* out_peer, __nv_bfloat16* hid_peer, int64_t* flag_peer, int64_t seq, cudaStream_t st) {
-  accept_send_kernel<<<1, 256, 0, st>>>(blocks, post, B, K, hidden, H, out_peer, hid_peer, flag_peer, seq);
+                 int64_t* out_peer, __nv_bfloat16* hid_peer, int64_t* flag_peer, int64_t seq, const int* gate,
+                 cudaStream_t st) {
+  accept_send_kernel<<<1, 256, 0, st>>>(blocks, post, B, K, hidden, H, out_peer, hid_peer, flag_peer, seq, gate);
+}
+
+// ------------------------------------------------------- armed verify (target)
+// The target enqueues the next verify before its request exists: this kernel
+// (first on the stream, ahead of the verify graph) waits -- bounded -- for
+// message ``seq`` of every source inbox, copies each message's first
+// ``head_words`` into pinned host memory for the host's bookkeeping, and, when
+// every source sent a VERIFY of the expected shape and sequences whose
+// positions lie inside the KV pages reserved for them, writes the verify
+// graph's integer inputs (token ids, positions, KV slots, causal row limits,
+// key ends) straight from the messages -- the host never touches the request
+// on the critical path.  Otherwise the inputs become placeholders (every KV
+// store goes to one scratch slot, keys end at K) and ``gate`` is cleared, so
+// the reply kernels after the graph send nothing and the host handles the
+// messages.  Status per source (pinned): 0 matched, 1 another message
+// arrived, 2 nothing arrived in time; [n_src] is 0 when the verify is valid.
+__global__ void verify_arm_kernel(ArmArgs a) {
+  __shared__ int arrived[ARM_MAX_SRC];
+  __shared__ int valid;
+  const int tid = threadIdx.x;
+  if (tid < a.n_src) {
+    arrived[tid] = 1;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(a.flag[tid]) < a.seq[tid]) {
+      if (globaltimer_ns() - t0 > a.limit_ns) {
+        arrived[tid] = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  for (int d = 0; d < a.n_src; ++d) {
+    if (!arrived[d]) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(a.msg[d]);
+    uint4* dst = reinterpret_cast<uint4*>(a.head[d]);
+    for (int i = tid; i < a.head_words / 2; i += blockDim.x) dst[i] = __ldcv(src + i);
+  }
+  const int B = a.row0[a.n_src - 1] + a.nb[a.n_src - 1];
+  const int64_t* exp_sid = a.tab;
+  const int64_t* reserved = a.tab + B;
+  if (tid == 0) {
+    int ok = 1;
+    for (int d = 0; d < a.n_src && ok; ++d) {
+      const volatile int64_t* m = a.msg[d];
+      if (!arrived[d] || m[0] != 2 || m[1] != a.nb[d] || m[2] != a.K) {
+        ok = 0;
+        break;
+      }
+      for (int b = 0; b < a.nb[d]; ++b) {
+        const int r = a.row0[d] + b;
+        const int64_t p = m[8 + 2 * b + 1];
+        if (m[8 + 2 * b] != exp_sid[r] || p < 0 || p + a.K > reserved[r]) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+    valid = ok;
+  }
+  __syncthreads();
+  const int T = B * a.K;
+  for (int t = tid; t < T; t += blockDim.x) {
+    const int r = t / a.K, i = t - r * a.K;
+    if (valid) {
+      int d = 0;
+      while (d + 1 < a.n_src && r >= a.row0[d + 1]) ++d;
+      const int b = r - a.row0[d];
+      const int64_t* m = a.msg[d];
+      const int64_t p = __ldcv(m + 8 + 2 * b + 1) + i;
+      const int64_t row = a.seq_rows[r];
+      a.ids[t] = __ldcv(m + 8 + 2 * a.nb[d] + static_cast<int64_t>(b) * a.K + i);
+      a.pos[t] = p;
+      const int64_t page = a.block_table[row * a.bt_stride + p / a.page];
+      a.slots[t] = page * a.page + p % a.page;
+      a.rows[3 * t] = static_cast<int32_t>(p + 1);
+      if (i == 0) a.kv_end[r] = static_cast<int32_t>(p + a.K);
+    } else {
+      a.ids[t] = 0;
+      a.pos[t] = i;
+      a.slots[t] = a.scratch_slot;
+      a.rows[3 * t] = i + 1;
+      if (i == 0) a.kv_end[r] = a.K;
+    }
+    a.rows[3 * t + 1] = 0;
+    a.rows[3 * t + 2] = 0;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (tid == 0) {
+    *a.gate = valid;
+    for (int d = 0; d < a.n_src; ++d) {
+      int st = 2;
+      if (arrived[d]) st = valid ? 0 : 1;
+      reinterpret_cast<volatile int*>(a.status)[d] = st;
+    }
+    __threadfence_system();
+    reinterpret_cast<volatile int*>(a.status)[a.n_src] = valid ? 0 : 1;
+  }
+}
+
+void verify_arm(const ArmArgs& a, cudaStream_t st) {
+  if (a.n_src < 1 || a.n_src > ARM_MAX_SRC) throw std::runtime_error("verify_arm: 1..8 sources");
+  if (a.head_words % 2) throw std::runtime_error("verify_arm: head_words must be even");
+  verify_arm_kernel<<<1, 256, 0, st>>>(a);
+}
+
+// ------------------------------------------------ device branch select (drafter)
+// The drafter enqueues this behind its packed forward, before the target's
+// reply exists: it waits -- bounded -- for reply ``rseq``, copies its first
+// ``head_words`` into pinned host memory (the host's receive reads it there),
+// and for every row looks up the drafted branch keyed by the outcome
+// (commit length, and the correction token unless the whole block was
+// accepted or no anchor branches are drafted).  When every row continues
+// (commit below its finishing limit, correction not a stop token) and has a
+// branch, it writes the next VERIFY request -- correction + the branch's
+// drafts 1..K-1 (from the forward's top-1 ids, or the controlled-acceptance
+// drafts of the row's positions) -- into the target rank(s)' inboxes with
+// peer stores and raises their flags.  Otherwise it sends nothing and the
+// host takes the step.  status (pinned): [0] 0 reply arrived / 2 not in time,
+// [1] 1 request sent / 0 not.
+__global__ void select_send_kernel(SelectArgs a) {
+  __shared__ int ok, arrived;
+  __shared__ int sn[SEL_MAX_ROWS], sj[SEL_MAX_ROWS];
+  __shared__ int64_t scorr[SEL_MAX_ROWS];
+  const int tid = threadIdx.x;
+  const int B = a.B, K = a.K;
+  if (tid == 0) {
+    arrived = 1;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(a.rflag) < a.rseq) {
+      if (globaltimer_ns() - t0 > a.limit_ns) {
+        arrived = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (arrived) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.reply);
+    uint4* dst = reinterpret_cast<uint4*>(a.reply_host);
+    for (int i = tid; i < a.head_words / 2; i += blockDim.x) dst[i] = __ldcv(src + i);
+  }
+  const int64_t* sid = a.tab;
+  const int64_t* prefix = a.tab + B;
+  const int64_t* n_limit = a.tab + 2 * B;
+  const int64_t* keys = a.tab + 3 * B;
+  const int64_t* key_rows = keys + static_cast<size_t>(B) * a.nk * 2;
+  const int64_t* eos = key_rows + static_cast<size_t>(B) * a.nk;
+  const int64_t* ctrl = eos + a.n_eos;
+  if (tid == 0) {
+    const volatile int64_t* r = a.reply;
+    int good = arrived && B <= SEL_MAX_ROWS && r[0] == 2 && r[1] == B && r[2] == K;
+    for (int b = 0; b < B && good; ++b) {
+      const int64_t n = r[8 + static_cast<int64_t>(b) * (2 + K)];
+      const int64_t corr = r[8 + static_cast<int64_t>(b) * (2 + K) + 1];
+      if (n < 1 || n > K || n >= n_limit[b]) good = 0;
+      for (int e = 0; e < a.n_eos && good; ++e)
+        if (corr == eos[e]) good = 0;
+      const int64_t key = (n == K || a.a0) ? -1 : corr;
+      int j = -1;
+      for (int q = 0; q < a.nk && good; ++q) {
+        const int64_t* kq = keys + (static_cast<size_t>(b) * a.nk + q) * 2;
+        if (kq[0] == n && kq[1] == key) {
+          j = q;
+          break;
+        }
+      }
+      if (j < 0) good = 0;
+      sn[b] = static_cast<int>(n);
+      sj[b] = j;
+      scorr[b] = corr;
+    }
+    ok = good;
+  }
+  __syncthreads();
+  if (ok) {
+    const int words = 8 + 2 * B + B * K;
+    for (int w = tid; w < words; w += blockDim.x) {
+      int64_t v = 0;
+      if (w < 8) {
+        v = w == 0 ? 2 : (w == 1 ? B : (w == 2 ? K : 0));
+      } else if (w < 8 + 2 * B) {
+        const int b = (w - 8) >> 1;
+        v = ((w - 8) & 1) ? prefix[b] + sn[b] : sid[b];
+      } else {
+        const int idx = w - 8 - 2 * B;
+        const int b = idx / K, i = idx - b * K;
+        if (i == 0) v = scorr[b];
+        else if (a.ctrl) v = ctrl[static_cast<size_t>(b) * 2 * K + sn[b] + i - 1];
+        else v = a.top[(key_rows[static_cast<size_t>(b) * a.nk + sj[b]] + i) * a.top_stride];
+      }
+      for (int o = 0; o < a.n_out; ++o) a.out_slot[o][w] = v;
+    }
+    __threadfence_system();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    if (ok)
+      for (int o = 0; o < a.n_out; ++o) st_release_sys(a.out_flag[o], a.out_seq[o]);
+    reinterpret_cast<volatile int*>(a.status)[0] = arrived ? 0 : 2;
+    __threadfence_system();
+    reinterpret_cast<volatile int*>(a.status)[1] = ok;
+  }
+}
+
+void select_send(const SelectArgs& a, cudaStream_t st) {
+  if (a.n_out < 1 || a.n_out > ARM_MAX_SRC) throw std::runtime_error("select_send: 1..8 destinations");
+  if (a.B < 1 || a.B > SEL_MAX_ROWS) throw std::runtime_error("select_send: 1..64 rows");
+  if (a.head_words % 2) throw std::runtime_error("select_send: head_words must be even");
+  select_send_kernel<<<1, 256, 0, st>>>(a);
 }
 
 // ---------------------------------------------------------------- CUDA IPC

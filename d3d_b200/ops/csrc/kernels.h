@@ -99,7 +99,48 @@ void handoff_put(const void* src, void* dst_peer, size_t nbytes, int64_t* flag_p
 void handoff_wait(const int64_t* flag, int64_t seq, const void* src, void* dst, size_t nbytes, int* status,
                   unsigned long long limit_ns, cudaStream_t st);
 void accept_send(const int64_t* blocks, const int64_t* post, int B, int K, const __nv_bfloat16* hidden, int H,
-                 int64_t* out_peer, __nv_bfloat16* hid_peer, int64_t* flag_peer, int64_t seq, cudaStream_t st);
+                 int64_t* out_peer, __nv_bfloat16* hid_peer, int64_t* flag_peer, int64_t seq, const int* gate,
+                 cudaStream_t st);
+constexpr int ARM_MAX_SRC = 8;
+constexpr int SEL_MAX_ROWS = 64;
+struct ArmArgs {
+  const int64_t* flag[ARM_MAX_SRC];  // source inbox flags
+  const int64_t* msg[ARM_MAX_SRC];   // the slot message seq lands in
+  int64_t* head[ARM_MAX_SRC];        // pinned host copy of each message's first head_words
+  int64_t seq[ARM_MAX_SRC];
+  int row0[ARM_MAX_SRC];             // first merged row of each source
+  int nb[ARM_MAX_SRC];               // rows expected from each source
+  int n_src, K, head_words, page, bt_stride;
+  const int64_t* tab;                // [B] expected sequence ids | [B] KV slots reserved per row
+  const int32_t* block_table;
+  const int64_t* seq_rows;
+  int64_t scratch_slot;
+  int64_t* ids;
+  int64_t* pos;
+  int64_t* slots;
+  int32_t* rows;
+  int32_t* kv_end;
+  int* gate;
+  int* status;                       // pinned [n_src + 1]
+  unsigned long long limit_ns;
+};
+void verify_arm(const ArmArgs& a, cudaStream_t st);
+struct SelectArgs {
+  const int64_t* rflag;
+  const int64_t* reply;
+  int64_t rseq;
+  int64_t* reply_host;
+  int head_words, B, K, nk, a0, n_eos, ctrl, top_stride;
+  const int64_t* tab;  // sid[B] | prefix[B] | n_limit[B] | keys[B][nk][2] | key_rows[B][nk] | eos | ctrl[B][2K]
+  const int64_t* top;
+  int64_t* out_slot[ARM_MAX_SRC];
+  int64_t* out_flag[ARM_MAX_SRC];
+  int64_t out_seq[ARM_MAX_SRC];
+  int n_out;
+  int* status;         // pinned [2]
+  unsigned long long limit_ns;
+};
+void select_send(const SelectArgs& a, cudaStream_t st);
 void* mailbox_alloc(size_t nbytes);
 void mailbox_free(void* p);
 void ipc_get_handle(void* p, unsigned char* out64);

@@ -81,6 +81,23 @@ def test_gemm_topk(E, k, m):
         assert ((oi == ri) | ~clear).all()
 
 
+@pytest.mark.parametrize("k", [1, 2, 4])
+def test_gemm_topk_epilogues_agree(E, k):
+    """The column-scan epilogue (token tiles above 32) and the warp-max
+    epilogue (tiles of up to 32) give bit-identical candidates, exact ties
+    included (duplicated weight rows): the lower row wins."""
+    from d3d_b200 import ops
+    m = 96
+    x = _bf(m, 512, seed=16)
+    w = _bf(4096, 512, scale=0.05, seed=17)
+    w[1::2] = w[0::2]           # every logit appears twice, in rows 2i and 2i+1
+    a = ops.gemm_topk(x, w, k, bt=32)
+    b = ops.gemm_topk(x, w, k, bt=96)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    if k >= 2:
+        assert (b[1][:, 0] % 2 == 0).all() and (b[1][:, 1] == b[1][:, 0] + 1).all()
+
+
 def test_gemm_batch_invariance(E):
     """A row's partial sums are bit-identical for any M and token tile."""
     from d3d_b200 import ops
