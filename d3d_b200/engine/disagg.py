@@ -176,7 +176,7 @@ class P2PTargetServer:
 
     # ------------------------------------------------------ armed verifies
     def _can_arm(self) -> bool:
-        return (self.fused and self.replies == "all" and getattr(self.be, "supports_arm", False)
+        return (self.fused and getattr(self.be, "supports_arm", False)
                 and os.environ.get("D3D_ARMED_VERIFY", "1") != "0")
 
     def _arm(self, group: list, K: int):
@@ -195,7 +195,8 @@ class P2PTargetServer:
         E = ops.ext()
 
         def sink(ids, post, xn, gate):
-            E.accept_send(ids, post, xn, out_ptr, hid_ptr, flag_ptr, seq_out, gate)
+            if self.replies == "all":     # other tensor-parallel ranks run the verify, rank 0 answers
+                E.accept_send(ids, post, xn, out_ptr, hid_ptr, flag_ptr, seq_out, gate)
 
         arm = self.be.arm_verify(group, K, [s.index for s in group], src, rows_of, sink, HEAD_WORDS)
         return arm, group, seq_in, seq_out
@@ -207,8 +208,12 @@ class P2PTargetServer:
         arm, group, seq_in, seq_out = armed
         arm["ev"].synchronize()
         st0, overall = int(arm["status"][0]), int(arm["status"][1])
+        if overall == 3:
+            raise RuntimeError("armed verify: no decision from tensor-parallel rank 0, or messages unlike it")
         if overall == 0:
-            self.link.recv_seq, self.link.send_seq = seq_in, seq_out
+            self.link.recv_seq = seq_in
+            if self.replies == "all":
+                self.link.send_seq = seq_out
             B = len(group)
             for (sid, prefix), s in zip(self.req[HDR:HDR + 2 * B].view(B, 2).tolist(), group):
                 s.prefix = prefix
@@ -661,6 +666,8 @@ class BatchedTargetServer:
         E = ops.ext()
 
         def sink(ids, post, xn, gate):
+            if self.replies != "all":    # other tensor-parallel ranks run the verify, rank 0 answers
+                return
             for d, q0, B, out_ptr, hid_ptr, flag_ptr, seq_out, _ in outs:
                 E.accept_send(ids[q0:q0 + B], post[q0:q0 + B], xn[q0 * K:(q0 + B) * K], out_ptr, hid_ptr,
                               flag_ptr, seq_out, gate)
@@ -676,10 +683,14 @@ class BatchedTargetServer:
         arm, ds, group, K, outs = armed
         arm["ev"].synchronize()
         st = arm["status"]
+        if int(st[len(ds)]) == 3:
+            raise RuntimeError("armed verify: no decision from tensor-parallel rank 0, or messages unlike it")
         if int(st[len(ds)]) == 0:
             for d, q0, B, _, _, _, seq_out, seq_in in outs:
                 sub = self.subs[d]
-                sub.link.recv_seq, sub.link.send_seq = seq_in, seq_out
+                sub.link.recv_seq = seq_in
+                if self.replies == "all":
+                    sub.link.send_seq = seq_out
                 for (sid, prefix), s in zip(sub.req[HDR:HDR + 2 * B].view(B, 2).tolist(), group[q0:q0 + B]):
                     s.prefix = prefix
             return True, {}
@@ -707,7 +718,7 @@ class BatchedTargetServer:
 
     def serve(self, poll=None) -> None:
         active = list(range(len(self.subs)))
-        can_arm = (self.replies == "all" and self.subs[0].fused and getattr(self.be, "supports_arm", False)
+        can_arm = (self.subs[0].fused and getattr(self.be, "supports_arm", False)
                    and os.environ.get("D3D_ARMED_VERIFY", "1") != "0")
         armed = None
         while active:

@@ -214,6 +214,7 @@ class FastTarget(_FastModelBackend, TargetBackend):
         self.tp = tp
         self._pending = None
         self._arm_bufs: Dict[int, dict] = {}
+        self._arm_epoch = 0       # armed verifies so far: the same count on every tensor-parallel rank
         self.scratch = self.kv.scratch_slot()
         self._accept_bufs: Dict[tuple, dict] = {}
         self.verify_events: List[Tuple[torch.cuda.Event, torch.cuda.Event]] = []
@@ -348,8 +349,9 @@ class FastTarget(_FastModelBackend, TargetBackend):
 
     @property
     def supports_arm(self) -> bool:
-        """Greedy verification on one GPU can be armed ahead of its request."""
-        return not self.sampled and self.tp is None
+        """Greedy verification can be armed ahead of its request (on a
+        tensor-parallel target every rank arms, rank 0 decides)."""
+        return not self.sampled and getattr(self.tp, "local_only", False) is False
 
     @torch.inference_mode()
     def arm_verify(self, seqs, K: int, exp_sids, sources, rows_of, sink, head_words: int) -> dict:
@@ -368,7 +370,7 @@ class FastTarget(_FastModelBackend, TargetBackend):
         completed."""
         B = len(seqs)
         if not self.supports_arm:
-            raise RuntimeError("only greedy single-GPU verification can be armed")
+            raise RuntimeError("only greedy verification can be armed")
         b = self.runner.buffers(B, K, 1)
         a = self._abufs(B, K)
         arm = self._arm_bufs.get(B)
@@ -387,9 +389,13 @@ class FastTarget(_FastModelBackend, TargetBackend):
         E = ops.ext()
         with torch.cuda.stream(self.stream):
             arm["tab"].copy_(th, non_blocking=True)
+            self._arm_epoch += 1
+            role, dec = 0, None
+            if self.tp is not None and self.tp.size > 1:
+                role, dec = (1 if self.tp.rank == 0 else 2), self.tp.decision_records()
             E.verify_arm(sources, rows_of, K, head_words, self.kv.page_size, arm["tab"], self.kv.block_table,
                          b.seq_rows, self.scratch, b.ids, b.pos, b.slots, b.rows.view(-1), b.kv_end, arm["gate"],
-                         arm["status"])
+                         arm["status"], role, dec, self._arm_epoch)
             arm["ev"].record(self.stream)
             ev0 = ev1 = None
             if self.time_verify:     # the verify proper: from its request's arrival to its reply

@@ -468,7 +468,8 @@ void accept_send(Tensor blocks, Tensor post, c10::optional<Tensor> hidden, int64
 // [2, n_src] = first merged row and row count per source.
 void verify_arm(Tensor src, Tensor rows_of, int64_t K, int64_t head_words, int64_t page, Tensor tab,
                 Tensor block_table, Tensor seq_rows, int64_t scratch_slot, Tensor ids, Tensor pos, Tensor slots,
-                Tensor rows, Tensor kv_end, Tensor gate, Tensor status) {
+                Tensor rows, Tensor kv_end, Tensor gate, Tensor status, int64_t role, c10::optional<Tensor> dec,
+                int64_t epoch) {
   const c10::cuda::CUDAGuard g(ids.device());
   CHECK_DT(src, torch::kInt64);
   CHECK_DT(rows_of, torch::kInt64);
@@ -522,6 +523,22 @@ void verify_arm(Tensor src, Tensor rows_of, int64_t K, int64_t head_words, int64
   a.gate = gate.data_ptr<int>();
   a.status = status.data_ptr<int>();
   a.limit_ns = kTimeoutNs;
+  TORCH_CHECK(role >= 0 && role <= 2, "verify_arm: role 0 (alone), 1 (leader) or 2 (follower)");
+  a.role = static_cast<int>(role);
+  a.epoch = epoch;
+  if (role != 0) {
+    TORCH_CHECK(dec && dec->dtype() == torch::kInt64 && dec->dim() == 1, "verify_arm: decision record table");
+    auto dp = dec->contiguous();
+    const int64_t* dv = dp.data_ptr<int64_t>();
+    if (role == 1) {
+      TORCH_CHECK(dp.numel() <= d3d::ARM_MAX_SRC, "verify_arm: up to 8 followers");
+      a.n_follow = static_cast<int>(dp.numel());
+      for (int f = 0; f < a.n_follow; ++f) a.dec_out[f] = reinterpret_cast<int64_t*>(dv[f]);
+    } else {
+      TORCH_CHECK(dp.numel() == 1, "verify_arm: a follower reads one decision record");
+      a.dec_in = reinterpret_cast<const int64_t*>(dv[0]);
+    }
+  }
   d3d::verify_arm(a, cur_stream());
 }
 
@@ -783,7 +800,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("status"));
   m.def("accept_send", &accept_send, py::arg("blocks"), py::arg("post"), py::arg("hidden"), py::arg("out_ptr"),
         py::arg("hid_ptr"), py::arg("flag_ptr"), py::arg("seq"), py::arg("gate") = py::none());
-  m.def("verify_arm", &verify_arm);
+  m.def("verify_arm", &verify_arm, py::arg("src"), py::arg("rows_of"), py::arg("K"), py::arg("head_words"),
+        py::arg("page"), py::arg("tab"), py::arg("block_table"), py::arg("seq_rows"), py::arg("scratch_slot"),
+        py::arg("ids"), py::arg("pos"), py::arg("slots"), py::arg("rows"), py::arg("kv_end"), py::arg("gate"),
+        py::arg("status"), py::arg("role") = 0, py::arg("dec") = py::none(), py::arg("epoch") = 0);
   m.def("select_send", &select_send);
   m.def("tp_epoch_bump", &tp_epoch_bump);
   m.def("gemm_partial_tp", &gemm_partial_tp, py::arg("x"), py::arg("w"), py::arg("ptrs"), py::arg("rank"),

@@ -166,11 +166,50 @@ void accept_send(const int64_t* blocks, const int64_t* post, int B, int K, const
 // the reply kernels after the graph send nothing and the host handles the
 // messages.  Status per source (pinned): 0 matched, 1 another message
 // arrived, 2 nothing arrived in time; [n_src] is 0 when the verify is valid.
+// On a tensor-parallel target every rank runs the same graphs, so rank 0
+// alone decides (its bounded waits and checks above) and publishes the
+// decision into each other rank's memory with peer stores and a release
+// flag stamped with the arm's epoch; the other ranks wait (bounded) for it
+// and for their own copies of the messages it saw, and follow it.  A
+// follower that gets no decision, or whose messages disagree with it,
+// reports status 3 and its host ends serving.
 __global__ void verify_arm_kernel(ArmArgs a) {
   __shared__ int arrived[ARM_MAX_SRC];
-  __shared__ int valid;
+  __shared__ int lead_st[ARM_MAX_SRC];
+  __shared__ int valid, lost;
   const int tid = threadIdx.x;
-  if (tid < a.n_src) {
+  if (a.role == 2) {
+    // follower: take rank 0's decision (bounded, well above rank 0's own
+    // bound), then wait for the messages rank 0 saw arrive in this inbox
+    if (tid == 0) {
+      lost = 0;
+      valid = 0;
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(a.dec_in) < a.epoch) {
+        if (globaltimer_ns() - t0 > 3 * a.limit_ns) {
+          lost = 1;
+          break;
+        }
+      }
+      for (int d = 0; d < a.n_src; ++d) {
+        lead_st[d] = lost ? 2 : static_cast<int>(reinterpret_cast<const volatile int64_t*>(a.dec_in)[1 + d]);
+        arrived[d] = 0;
+      }
+      if (!lost) valid = static_cast<int>(reinterpret_cast<const volatile int64_t*>(a.dec_in)[1 + a.n_src]);
+      for (int d = 0; d < a.n_src && !lost; ++d) {
+        if (lead_st[d] == 2) continue;
+        const uint64_t t1 = globaltimer_ns();
+        while (ld_acquire_sys(a.flag[d]) < a.seq[d]) {
+          if (globaltimer_ns() - t1 > a.limit_ns) {
+            lost = 1;
+            break;
+          }
+        }
+        arrived[d] = !lost;
+      }
+      if (lost) valid = 0;
+    }
+  } else if (tid < a.n_src) {
     arrived[tid] = 1;
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire_sys(a.flag[tid]) < a.seq[tid]) {
@@ -191,7 +230,9 @@ __global__ void verify_arm_kernel(ArmArgs a) {
   const int64_t* exp_sid = a.tab;
   const int64_t* reserved = a.tab + B;
   if (tid == 0) {
-    int ok = 1;
+    // the follower checks too (memory safety): a follower that finds the
+    // messages unlike its leader's decision reports the group as lost
+    int ok = a.role == 2 ? valid : 1;
     for (int d = 0; d < a.n_src && ok; ++d) {
       const volatile int64_t* m = a.msg[d];
       if (!arrived[d] || m[0] != 2 || m[1] != a.nb[d] || m[2] != a.K) {
@@ -207,7 +248,18 @@ __global__ void verify_arm_kernel(ArmArgs a) {
         }
       }
     }
+    if (a.role == 2 && valid && !ok) lost = 1;
     valid = ok;
+    if (a.role == 1) {
+      // publish the decision to every follower before this rank's graph runs
+      for (int f = 0; f < a.n_follow; ++f) {
+        int64_t* rec = a.dec_out[f];
+        for (int d = 0; d < a.n_src; ++d) rec[1 + d] = arrived[d] ? (ok ? 0 : 1) : 2;
+        rec[1 + a.n_src] = ok;
+      }
+      __threadfence_system();
+      for (int f = 0; f < a.n_follow; ++f) st_release_sys(a.dec_out[f], a.epoch);
+    }
   }
   __syncthreads();
   const int T = B * a.K;
@@ -239,14 +291,16 @@ __global__ void verify_arm_kernel(ArmArgs a) {
   __threadfence_system();
   __syncthreads();
   if (tid == 0) {
+    const bool gone = a.role == 2 && lost;
     *a.gate = valid;
     for (int d = 0; d < a.n_src; ++d) {
       int st = 2;
-      if (arrived[d]) st = valid ? 0 : 1;
+      if (gone) st = 3;
+      else if (arrived[d]) st = valid ? 0 : 1;
       reinterpret_cast<volatile int*>(a.status)[d] = st;
     }
     __threadfence_system();
-    reinterpret_cast<volatile int*>(a.status)[a.n_src] = valid ? 0 : 1;
+    reinterpret_cast<volatile int*>(a.status)[a.n_src] = gone ? 3 : (valid ? 0 : 1);
   }
 }
 

@@ -123,6 +123,13 @@ struct ArmArgs {
   int* gate;
   int* status;                       // pinned [n_src + 1]
   unsigned long long limit_ns;
+  // tensor-parallel targets: rank 0 (role 1) decides and publishes its
+  // decision to every other rank (role 2), which follows it; role 0 alone
+  int role;
+  int n_follow;
+  int64_t* dec_out[ARM_MAX_SRC];     // leader: each follower's decision record (peer memory)
+  const int64_t* dec_in;             // follower: this rank's decision record
+  int64_t epoch;
 };
 void verify_arm(const ArmArgs& a, cudaStream_t st);
 struct SelectArgs {

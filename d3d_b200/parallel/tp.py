@@ -67,7 +67,9 @@ class TPGroup:
         self.flag_bytes = (self.n_x * self.size * FLAG_BYTES_PER_X + 255) // 256 * 256
         self.part_bytes = (part_bytes + 255) // 256 * 256
         self.cand_off = self.flag_bytes + 2 * self.part_bytes
-        self.nbytes = self.cand_off + cand_bytes
+        # armed-verify decision record (rank 0 writes it into every other rank)
+        self.dec_off = self.cand_off + (cand_bytes + 255) // 256 * 256
+        self.nbytes = self.dec_off + 256
         E = ops.ext()
         self.ext = E
         self.base = E.mailbox_alloc(self.nbytes, self.device.index)     # zero-filled
@@ -116,6 +118,13 @@ class TPGroup:
             raise ValueError(f"partials of {4 * n_floats} bytes exceed the {self.part_bytes}-byte buffer")
         off = self.part_offset(parity)
         return self.mem[off:off + 4 * n_floats].view(torch.float32)
+
+    def decision_records(self) -> torch.Tensor:
+        """Where this rank's armed-verify decisions go (int64 addresses): on
+        rank 0 every other rank's record, elsewhere this rank's own."""
+        if self.rank == 0:
+            return torch.tensor([b + self.dec_off for b in self.peer_bases[1:]], dtype=torch.int64)
+        return torch.tensor([self.base + self.dec_off], dtype=torch.int64)
 
     def cand_view(self) -> torch.Tensor:
         return self.mem[self.cand_off:]
