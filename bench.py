@@ -64,7 +64,8 @@ def parse():
                    help="N>1: 'tp' = target tensor-parallel over N/2 GPUs + one drafter per other GPU; "
                         "'disagg' = pairs of GPUs (target GPU + drafter GPU, NVLink handoff); "
                         "'replica' = target and drafter co-located on every GPU; "
-                        "auto = replica for N=1, disagg for N=2, tp for even N >= 4")
+                        "auto = replica for N=1, disagg pairs for even N (the tp layout's bench run at "
+                        "N=4 stopped during target set-up, before serving, in its last run)")
     return p.parse_args()
 
 
@@ -663,7 +664,7 @@ def main():
         else:
             layout = args.layout
             if layout == "auto":
-                layout = "replica" if world == 1 or world % 2 else ("disagg" if world == 2 else "tp")
+                layout = "replica" if world == 1 or world % 2 else "disagg"
             if layout in ("disagg", "tp") and (world < 2 or world % 2):
                 raise SystemExit(f"--layout {layout} needs an even number of GPUs")
             run = {"disagg": run_disagg, "tp": run_tp_layout, "replica": run_ours}[layout]
@@ -674,6 +675,17 @@ def main():
             if args.json_out:
                 with open(args.json_out, "w") as f:
                     f.write(line + "\n")
+    except BaseException:
+        if world > 1:
+            # say why at once and leave: the other ranks' next collective
+            # fails instead of every rank waiting out the process-group timeout
+            import traceback
+            print(f"[rank {rank}] bench failed:", file=sys.stderr)
+            traceback.print_exc()
+            sys.stderr.flush()
+            sys.stdout.flush()
+            os._exit(1)
+        raise
     finally:
         import torch.distributed as dist
         if dist.is_initialized():

@@ -235,7 +235,8 @@ def bench_forward(iters, peaks, rows, layers=36, drafter=False):
         byts = w.nbytes()
         rows.append(dict(kernel="forward (graph)", shape=f"{'drafter' if drafter else 'Qwen3-8B'} M={m}", M=m, launches=n,
                          us=round(us, 1), GBps=round(byts / us / 1e3, 1),
-                         hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3)))
+                         hbm_frac=round(byts / us / 1e3 / peaks["hbm_gbs"], 3),
+                         plan={g: v for g, v in r.plan(m).items()}))
 
 
 def forward_eager(layers, drafter, context=1000):

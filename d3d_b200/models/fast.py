@@ -422,8 +422,11 @@ class FastRunner:
         """Time candidate (token tile, split-K, direct) configurations of each
         GEMM at T tokens on this device and keep the fastest.  Weights cycle
         over the model's layers so every timed launch streams from HBM; a
-        partial-reducing configuration is charged for reading its partials
-        back (at 6 TB/s)."""
+        partial-reducing configuration is timed together with a split-K
+        reduction of its partials (``residual_split_reduce``, standing in for
+        the consumer kernel), so it pays its partials' round trip where they
+        really live -- L2 for small token counts, HBM otherwise
+        (``D3D_AUTOTUNE_CONSUMER=0``: a fixed 6 TB/s charge instead)."""
         E = ops.ext()
         dev = self.device
         L = self.w.layers
@@ -450,24 +453,36 @@ class FastRunner:
         bts = sorted({b for b in (base, ops.bt_for((T + 1) // 2), ops.bt_for((T + 2) // 3), 96, 64, 48, 32)
                       if b <= max(base, 16)}, reverse=True)
         plan: Dict[str, object] = {}
+        consumer = os.environ.get("D3D_AUTOTUNE_CONSUMER", "1") != "0"
         for g, (n, k) in shapes.items():
             w = lambda i: getattr(L[i % len(L)], g)
             xk = x[:, :k]
             kb = math.ceil(k / 64)
             best = None
+            xr = torch.zeros(T, n, dtype=torch.bfloat16, device=dev)
+            ss = torch.zeros(math.ceil(n / 128) * T, device=dev)
+            # a direct (bf16-output) GEMM's consumer still reads its T x n
+            # outputs: charge it one single-split pass over the same size
+            t_read = timed(lambda i: E.residual_split_reduce(part, 1, xr, ss)) if consumer else 0.0
             for bt in bts:
                 for s in range(1, 17):
                     if s > 1 and kb // s < 4:
                         break
-                    t = timed(lambda i: E.gemm_partial(xk, w(i).data, part, s, bt, st, n))
-                    t += s * T * n * 4 / 6e12
+                    if consumer:
+                        def fn(i, bt=bt, s=s):
+                            E.gemm_partial(xk, w(i).data, part, s, bt, st, n)
+                            E.residual_split_reduce(part, s, xr, ss)
+                        t = timed(fn)
+                    else:
+                        t = timed(lambda i: E.gemm_partial(xk, w(i).data, part, s, bt, st, n))
+                        t += s * T * n * 4 / 6e12
                     if best is None or t < best[0]:
                         best = (t, bt, s, False)
                 if g == "gate_up":
                     h = yb[:, : n // 2]
-                    t = timed(lambda i: E.gemm_swiglu(xk, w(i).data, h, bt, st, n))
+                    t = timed(lambda i: E.gemm_swiglu(xk, w(i).data, h, bt, st, n)) + t_read / 2
                 else:
-                    t = timed(lambda i: E.gemm_bf16(xk, w(i).data, yb[:, :n], None, bt, st, n))
+                    t = timed(lambda i: E.gemm_bf16(xk, w(i).data, yb[:, :n], None, bt, st, n)) + t_read
                 if t < best[0]:
                     best = (t, bt, 1, True)
             plan[g] = best[1:]
