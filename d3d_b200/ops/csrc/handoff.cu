@@ -363,13 +363,10 @@ __global__ void select_send_kernel(SelectArgs a) {
       for (int e = 0; e < a.n_eos && good; ++e)
         if (corr == eos[e]) good = 0;
       const int64_t key = (n == K || a.a0) ? -1 : corr;
-      int j = -1;
+      int j = -1;   // the last branch with this key, as the host's key -> branch map keeps
       for (int q = 0; q < a.nk && good; ++q) {
         const int64_t* kq = keys + (static_cast<size_t>(b) * a.nk + q) * 2;
-        if (kq[0] == n && kq[1] == key) {
-          j = q;
-          break;
-        }
+        if (kq[0] == n && kq[1] == key) j = q;
       }
       if (j < 0) good = 0;
       sn[b] = static_cast<int>(n);

@@ -44,7 +44,9 @@ def test_fast_spec_matches_fast_ar(fast_pair, mode, anchors, conc, graphs):
     for o, ref in zip(res["outputs"], ar["outputs"]):
         assert o.tokens == ref
     assert len(t.kv.tables) == 0 and len(d.kv.tables) == 0
-    assert len(t.kv.free) == t.kv.num_pages and len(d.kv.free) == d.kv.num_pages
+    # every page is free again, apart from the target's scratch page (placeholder KV stores)
+    assert len(t.kv.free) + len(t.kv.scratch) == t.kv.num_pages and len(d.kv.free) == d.kv.num_pages
+    assert t.kv.leaked == 0 and d.kv.leaked == 0
 
 
 def test_fast_forward_tracks_oracle(fast_pair):
