@@ -302,8 +302,10 @@ class Qwen3LM(nn.Module):
                 if hidden_states is not None:
                     hidden_states.append(x)
                 continue
-            if self.gradient_checkpointing and self.training and cache is None:
-                x = torch.utils.checkpoint.checkpoint(layer, x, cos, sin, mask, None, False,
+            if self.gradient_checkpointing and self.training and not store_kv and torch.is_grad_enabled():
+                # per-layer recomputation; a clean-prefix cache is only read
+                # here, so the recomputed layer sees the same keys and values
+                x = torch.utils.checkpoint.checkpoint(layer, x, cos, sin, mask, cache, False,
                                                       use_reentrant=False)
             else:
                 x = layer(x, cos, sin, mask, cache, store_kv)

@@ -39,6 +39,9 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--draft-layers", type=int, default=None)
     p.add_argument("--mask-token-id", type=int, default=None)
     p.add_argument("--freeze-embeddings", action="store_true")
+    p.add_argument("--gradient-checkpointing", action="store_true",
+                   help="recompute each decoder layer in backward instead of keeping its activations "
+                        "(the clean-prefix KV stays cached)")
     p.add_argument("--fsdp", action="store_true",
                    help="shard decoder-layer parameters over the ranks (gathered per layer, "
                         "recomputed in backward, gradients reduce-scattered per layer)")

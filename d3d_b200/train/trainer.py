@@ -168,6 +168,7 @@ def train(args) -> dict:
             del module
     if args.freeze_embeddings:
         student.model.embed_tokens.weight.requires_grad_(False)
+    student.gradient_checkpointing = bool(getattr(args, "gradient_checkpointing", False))
     z3 = None
     if getattr(args, "fsdp", False):
         # decoder layers live as per-rank shards; the optimizer below sees the rest

@@ -199,3 +199,31 @@ def test_rank_with_empty_batches_keeps_collectives_matched(tmp_path):
     assert all(r.get("empty_rank") for r in l1) and not any(r.get("empty_rank") for r in l0)
     assert all(a["grad_norm"] == b["grad_norm"] for a, b in zip(l0, l1))
     assert (tmp_path / "trainer_state.json").exists() or any(tmp_path.glob("**/trainer_state.json"))
+
+
+def test_gradient_checkpointing_keeps_clean_prefix_cache():
+    """Per-layer recomputation with a clean-prefix KV cache gives the same
+    outputs and gradients as keeping the activations."""
+    from d3d_b200.cli.common import model_config
+    from d3d_b200.models.qwen3 import DenseKVCache, build_model
+    torch.manual_seed(0)
+    clean = torch.randint(0, 1000, (2, 20))
+    draft = torch.randint(0, 1000, (2, 8))
+    pos = torch.arange(20, 28)[None].expand(2, 8)
+    mask = torch.ones(2, 8, 28, dtype=torch.bool)
+    outs = []
+    for ckpt in (False, True):
+        m = build_model(model_config("tiny-drafter"), seed=3, dtype=torch.float32, device="cpu")
+        m.eval()
+        cache = DenseKVCache(m.cfg.num_hidden_layers)
+        with torch.no_grad():
+            m(clean, cache=cache, store_kv=True)
+        m.train()
+        m.gradient_checkpointing = ckpt
+        h = m(draft, pos, mask=mask, cache=cache, store_kv=False)
+        h.square().mean().backward()
+        outs.append((h.detach(), [p.grad.clone() for p in m.parameters() if p.grad is not None]))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert len(outs[0][1]) == len(outs[1][1]) > 0
+    for a, b in zip(outs[0][1], outs[1][1]):
+        torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-7)
