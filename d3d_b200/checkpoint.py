@@ -114,12 +114,16 @@ def load_model(path: str | Path, device="cpu", dtype=torch.float32, strict: bool
 
 
 def save_model(model: Qwen3LM, path: str | Path, max_shard_bytes: int = 4 << 30,
-               dtype=torch.float32) -> None:
-    """Atomic save: write into a temp dir next to ``path`` and rename."""
+               dtype=torch.float32, extra: Optional[Dict[str, torch.Tensor]] = None) -> None:
+    """Atomic save: write into a temp dir next to ``path`` and rename.
+    ``extra``: tensors the module does not hold itself (the gathered weights
+    of sharded decoder layers), stored under their own names."""
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
     tmp = Path(tempfile.mkdtemp(prefix=path.name + ".tmp", dir=str(path.parent)))
     state = {k: v.detach().to("cpu", dtype).contiguous() for k, v in model.state_dict().items()}
+    for k, v in (extra or {}).items():
+        state[k] = v.detach().to("cpu", dtype).contiguous()
     if model.cfg.tie_word_embeddings:
         state.pop("lm_head.weight", None)
     write_state(state, tmp, max_shard_bytes)

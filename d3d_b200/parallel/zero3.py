@@ -51,8 +51,11 @@ class _LayerSpec:
 
 
 class _ShardedLayerFn(torch.autograd.Function):
+    # ``anchor``: an empty tensor that requires grad, so the layer's output
+    # takes part in autograd even when its input does not (frozen embeddings):
+    # the layer's own weights are gathered inside and are no inputs here
     @staticmethod
-    def forward(ctx, z, idx, x, cos, sin, mask, cache, store_kv):
+    def forward(ctx, z, idx, anchor, x, cos, sin, mask, cache, store_kv):
         params = z.views(idx, z.gather(idx))
         with torch.no_grad():
             y = functional_call(z.mods[idx], params, (x, cos, sin, mask, cache, store_kv))
@@ -75,7 +78,7 @@ class _ShardedLayerFn(torch.autograd.Function):
             y = functional_call(z.mods[idx], leaves, (xl, cos, sin, mask, ctx.cache, False))
             torch.autograd.backward(y, gy)
         z.reduce_scatter(idx, leaves)
-        return None, None, xl.grad if x.requires_grad else None, None, None, None, None, None
+        return None, None, None, xl.grad if x.requires_grad else None, None, None, None, None, None
 
 
 class ShardedLayer(nn.Module):
@@ -89,7 +92,8 @@ class ShardedLayer(nn.Module):
 
     def forward(self, x, cos, sin, mask, cache, store_kv):
         self._z[0].mods[self.idx].train(self.training)
-        return _ShardedLayerFn.apply(self._z[0], self.idx, x, cos, sin, mask, cache, store_kv)
+        z = self._z[0]
+        return _ShardedLayerFn.apply(z, self.idx, z.anchor, x, cos, sin, mask, cache, store_kv)
 
 
 class Zero3Layers:
@@ -147,6 +151,7 @@ class Zero3Layers:
         self.step_count = 0
         self.epoch = 0
         self.gathered = torch.empty(self.max_padded, dtype=self.dtype, device=self.device)
+        self.anchor = torch.zeros(0, device=self.device, requires_grad=True)
         self._part = torch.empty(max(s.shard for s in self.specs), dtype=torch.float32, device=self.device)
         for i in range(len(layers)):
             layers[i] = ShardedLayer(self, i)

@@ -104,6 +104,11 @@ def _recovery(a) -> list:
     child = load_model(a.child, device=device)
     prov = json.loads((Path(a.child) / "layer_prune.json").read_text())
     child.model.embed_tokens.weight.requires_grad_(False)
+    z3 = None
+    if getattr(a, "fsdp", False):
+        # the child's decoder layers as per-rank shards (the reference's FSDP2 student)
+        from ..parallel.zero3 import Zero3Layers
+        z3 = Zero3Layers(child.model.layers, lr=a.lr)
     opt = ShardedAdamW(child.parameters(), lr=a.lr)
     rng = random.Random(a.seed * 1000 + rank)
     window = DataWindow(a.data_path, a.seed, min(child.cfg.vocab_size, 151643) - 2)
@@ -111,8 +116,9 @@ def _recovery(a) -> list:
     out = Path(a.output)
 
     def save(dst: Path, log):
+        extra = z3.full_state("model.layers.") if z3 is not None else None   # collective
         if rank == 0:
-            save_model(child, dst)
+            save_model(child, dst, extra=extra)
             (dst / "layer_prune.json").write_text(json.dumps(prov, indent=2))
             write_json(str(dst / "recovery_log.json"), log)
             write_json(str(dst / "trainer_state.json"), {"next_data_cursor": cursor, "steps": len(log)})
@@ -126,12 +132,14 @@ def _recovery(a) -> list:
             break
         cursor += world * a.batch_size
         rec = recovery_step(child, parent, prov["removed_compact_layer"], list(range(parent.cfg.num_hidden_layers)),
-                            exs, opt, block_size=a.block_size, anchors=8, rng=rng)
+                            exs, opt, block_size=a.block_size, anchors=8, rng=rng, z3=z3)
         rec["next_data_cursor"] = cursor
         log.append(rec)
         if a.save_every and (step + 1) % a.save_every == 0:
             save(out.with_name(out.name + f".step{step + 1}"), log)
     save(out, log)
+    if z3 is not None:
+        z3.close()
     if log and rank == 0:
         print(json.dumps(log[-1]))
     return log
@@ -157,6 +165,7 @@ def main(argv=None):
     p.add_argument("--batch-size", type=int, default=2, help="train: sequences per rank per step")
     p.add_argument("--data-cursor", type=int, default=0, help="train: first row of the permuted data window")
     p.add_argument("--save-every", type=int, default=0, help="train: atomic step checkpoints")
+    p.add_argument("--fsdp", action="store_true", help="train: shard the child's decoder layers over the ranks")
     a = p.parse_args(argv)
     if a.stage == "select":
         rank, device = _eval_device(a)

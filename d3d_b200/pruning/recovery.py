@@ -38,7 +38,9 @@ def _block_forward(model: Qwen3LM, batch, cache, hidden: bool = False):
 
 def recovery_step(student: Qwen3LM, teacher: Qwen3LM, removed_original: int, retained_original: Sequence[int],
                   examples: List[Example], opt: ShardedAdamW, *, block_size: int, anchors: int,
-                  rng: random.Random, grad_clip: float = 1.0) -> dict:
+                  rng: random.Random, grad_clip: float = 1.0, z3=None) -> dict:
+    """One recovery step; ``z3``: the student's sharded decoder layers
+    (``parallel.zero3``), stepped with the same clip factor as ``opt``."""
     mask_id = int(student.cfg.mask_token_id)
     batch = build_packed_block_batch(examples, block_size=block_size, mask_token_id=mask_id,
                                      max_anchors=anchors, rng=rng)
@@ -69,7 +71,8 @@ def recovery_step(student: Qwen3LM, teacher: Qwen3LM, removed_original: int, ret
                      distributed=True)
     loss = LAMBDA_AR * ar + LAMBDA_CE * ce + LAMBDA_KL * kl + LAMBDA_H * hmse
     loss.backward()
-    norm = opt.step(grad_clip)
+    from ..train.trainer import _opt_step
+    norm = _opt_step(opt, z3, grad_clip, None)
     opt.zero_grad()
     return {"loss": float(loss.detach()), "ar": float(ar.detach()), "ce": float(ce.detach()),
             "kl": float(kl.detach()), "hidden_mse": float(hmse.detach()),

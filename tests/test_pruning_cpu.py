@@ -165,3 +165,48 @@ def test_data_parallel_selection_equals_single_process(tmp_path):
     b1 = json.loads((tmp_path / "best1.json").read_text())
     b2 = json.loads((tmp_path / "best2.json").read_text())
     assert b1["ranking"] == b2["ranking"]
+
+
+def _recovery_fsdp_worker(rank, port, root, tag, extra):
+    import os
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["RANK"], os.environ["WORLD_SIZE"], os.environ["LOCAL_RANK"] = str(rank), "2", str(rank)
+    import torch.distributed as dist
+    from d3d_b200.pruning.__main__ import main
+    main(["train", "--parent", f"{root}/parent", "--child", f"{root}/child", "--output", f"{root}/{tag}",
+          "--data-path", f"{root}/data.jsonl", "--batch-size", "1", "--steps", "3", "--block-size", "8",
+          "--device", "cpu", "--lr", "1e-3"] + extra)
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def test_recovery_with_sharded_layers_equals_replicated(tmp_path):
+    """Recovery training of the pruned child with its decoder layers sharded
+    over two gloo ranks (``--fsdp``) ends with the same weights and log as the
+    replicated run."""
+    import socket
+    import torch.multiprocessing as mp
+    m = _model()
+    save_model(m, tmp_path / "parent")
+    prune_checkpoint(tmp_path / "parent", tmp_path / "child", removed=1)
+    rng = random.Random(3)
+    rows = [json.dumps({"prompt_ids": [rng.randrange(2, 1000) for _ in range(10)],
+                        "response_ids": [rng.randrange(2, 1000) for _ in range(20)]}) for _ in range(8)]
+    (tmp_path / "data.jsonl").write_text("\n".join(rows) + "\n")
+    for tag, extra in (("rep", []), ("fsdp", ["--fsdp"])):
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+        s.close()
+        mp.spawn(_recovery_fsdp_worker, args=(port, str(tmp_path), tag, extra), nprocs=2, join=True)
+    la = json.loads((tmp_path / "rep" / "recovery_log.json").read_text())
+    lb = json.loads((tmp_path / "fsdp" / "recovery_log.json").read_text())
+    assert len(la) == len(lb) == 3
+    for x, y in zip(la, lb):
+        assert abs(x["loss"] - y["loss"]) <= 1e-5 * max(1.0, abs(x["loss"]))
+    ma, mb = load_model(tmp_path / "rep"), load_model(tmp_path / "fsdp")
+    sa, sb = dict(ma.named_parameters()), dict(mb.named_parameters())
+    assert sa.keys() == sb.keys()
+    for n in sa:
+        torch.testing.assert_close(sb[n], sa[n], rtol=1e-5, atol=1e-6, msg=n)

@@ -127,3 +127,20 @@ def test_two_ranks_with_an_empty_rank_and_ar_loss(tmp_path):
     b = _run(tmp_path, extra + ["--fsdp"], "fsdp")
     assert all(r.get("empty_rank") for r in b[1])
     _compare(tmp_path, a, b)
+
+
+def test_frozen_embeddings_still_train_sharded_layers():
+    """The first layer's input needs no gradient when the embeddings are
+    frozen; the sharded layers must get their gradients all the same."""
+    ref, sh = _tiny(), _tiny()
+    for m in (ref, sh):
+        m.model.embed_tokens.weight.requires_grad_(False)
+    z = Zero3Layers(sh.model.layers, lr=1e-3)
+    ids = torch.randint(0, 1000, (2, 16))
+    ref(ids).square().mean().backward()
+    sh(ids).square().mean().backward()
+    for i, lay in enumerate(ref.model.layers):
+        s = z.specs[i]
+        flat = torch.cat([p.grad.reshape(-1) for p in lay.parameters()])
+        assert flat.abs().sum() > 0
+        torch.testing.assert_close(z.grad[s.offset:s.offset + s.numel], flat, rtol=0, atol=0)
