@@ -200,13 +200,23 @@ class _FusedLMHeadLoss(torch.autograd.Function):
             dz = torch.empty(N, chunk, dtype=torch.bfloat16, device=hs.device)
             dzT = torch.zeros(chunk, npad, dtype=torch.bfloat16, device=hs.device)
             dwc = torch.empty(chunk * Hs, device=hs.device)
+            # dh = dz @ W contracts over the vocabulary: the tcgen05 GEMM reads
+            # W transposed ([Hs, V], made once per backward), each chunk a
+            # column window of it
+            tc_dh = V % 8 == 0 and chunk % 8 == 0 and Hs % 8 == 0    # 16-byte TMA rows
+            wsT = ws.t().contiguous() if tc_dh else None
+            dhc = torch.empty(N * Hs, device=hs.device)
         for v0 in range(0, V, chunk):
             c = min(chunk, V - v0)
             zs = _chunk_logits(hs, ws, v0, c, bs if cuda else None)
             zt = _chunk_logits(ht, wt, v0, c, bt if cuda else None) if has_t else None
             if cuda:
                 E.kl_ce_grad(zt, zs, c, v0, tgt, lse_t, lse_s, wkl, wce, dz[:, :c], dzT[:c] if need_w else None)
-                dh += (dz[:, :c] @ ws[v0:v0 + c]).float()
+                if tc_dh:
+                    E.gemm_partial(dz[:, :c], wsT[:, v0:v0 + c], dhc, 1, ops.bt_for(N), None, 0)
+                    dh += dhc.view(N, Hs)
+                else:
+                    dh += (dz[:, :c] @ ws[v0:v0 + c]).float()
                 if need_w:
                     out = dwc[: c * Hs].view(c, Hs)
                     E.gemm_partial(dzT[:c], hsT, out, 1, ops.bt_for(c), None, 0)
