@@ -1,11 +1,12 @@
-"""Host-side state machine of the target server's armed verifies
-(``P2PTargetServer.serve``), with the device parts replaced by fakes that
+"""Host-side state machine of the target servers' armed verifies
+(``P2PTargetServer.serve``, ``BatchedTargetServer.serve``), with the device parts replaced by fakes that
 behave as the ``verify_arm`` kernel does: it takes the next message if one
 arrives, and the armed verify is valid only for a VERIFY of the armed shape
 and sequences.  Checks the order of backend calls and that the mailbox
 sequence numbers stay in step with the messages and replies exchanged --
 for valid arms, a RELEASE or CLOSE meeting an arm, a request that arrives
-only after the arm's wait ran out, and a change of batch shape."""
+only after the arm's wait ran out, a change of batch shape, and rounds of
+several drafters where one is late, releases or closes."""
 import torch
 
 from d3d_b200.engine import disagg
@@ -183,3 +184,79 @@ def test_armed_prefix_updates_reach_the_sequences(monkeypatch):
     srv, be, link = _serve(monkeypatch, msgs)
     assert srv.seqs[7].prefix == 6
     assert be.log[-1] == ("arm-placeholder", 0)
+
+
+class _BatchedBackend(_Backend):
+    """``arm_verify`` over several drafters' inboxes, as the kernel does it:
+    valid only when every source sent a VERIFY of the armed shape."""
+
+    def __init__(self, links):
+        super().__init__(links[0])
+        self.links = links
+        self.subs = None
+
+    def arm_verify(self, group, K, sids, src, rows_of, sink, head_words):
+        self.arms += 1
+        n = src.shape[1]
+        st = torch.full((9,), -1, dtype=torch.int32)
+        msgs = []
+        for d in range(n):
+            sub = next(s for s in self.subs if s.req.data_ptr() == int(src[2, d]))
+            lk = sub.link
+            assert int(src[3, d]) == lk.recv_seq + 1
+            if (self.arms, d) in self.late or not lk.queue:
+                msgs.append(None)
+                continue
+            m = lk.queue.pop(0)
+            sub.req.zero_()
+            sub.req[:len(m)] = torch.tensor(m, dtype=torch.int64)
+            msgs.append(m)
+        ok = all(m is not None for m in msgs)
+        r = 0
+        for d, m in enumerate(msgs):
+            B = int(rows_of[1, d])
+            if ok:
+                ok = m[0] == 2 and m[1] == B and m[2] == K and all(m[8 + 2 * b] == sids[r + b] for b in range(B))
+            r += B
+        for d, m in enumerate(msgs):
+            st[d] = 2 if m is None else (0 if ok else 1)
+        st[n] = 0 if ok else 1
+        self.log.append(("armed", [[m[9 + 2 * b] for b in range(m[1])] for m in msgs]) if ok else
+                        ("arm-placeholder", [None if m is None else m[0] for m in msgs]))
+        return {"ev": _Ev(), "status": st}
+
+
+def _serve_batched(monkeypatch, streams, late=()):
+    monkeypatch.setattr(disagg, "ops", _Ops)
+    links = [_Link(s) for s in streams]
+    be = _BatchedBackend(links)
+    be.late = set(late)
+    srv = disagg.BatchedTargetServer(be, links)
+    for sub in srv.subs:
+        sub.fused = True
+    be.subs = srv.subs
+    srv.serve()
+    return srv, be, links
+
+
+def test_batched_armed_rounds(monkeypatch):
+    d0 = [_prefill(1, [5, 6]), _verify([(1, 2)], 4), _verify([(1, 5)], 4), _verify([(1, 9)], 4),
+          _verify([(1, 12)], 4), _verify([(1, 15)], 4), _release(1), CLOSE]
+    d1 = [_prefill(1, [7, 8, 9]), _verify([(1, 3)], 4), _verify([(1, 6)], 4), _verify([(1, 8)], 4),
+          _release(1), CLOSE]
+    srv, be, links = _serve_batched(monkeypatch, [d0, d1], late={(2, 1)})
+    g0, g1 = 0 * srv.ID_STRIDE + 1, 1 * srv.ID_STRIDE + 1
+    assert be.log == [
+        ("prefill", [g0, g1]),
+        ("verify", [2, 3]),                # round 2 on the host, then the next round is armed
+        ("armed", [[5], [6]]),             # round 3 on the device
+        ("arm-placeholder", [2, None]),    # drafter 1's request lands after the wait ...
+        ("verify", [9, 8]),                # ... so round 4 runs on the host
+        ("arm-placeholder", [2, 3]),       # drafter 1 releases: round 5 on the host
+        ("verify", [12]), ("release", g1),
+        ("verify", [15]),                  # drafter 1 closes in this round: nothing armed
+        ("release", g0),
+    ]
+    assert all(lk.recv_seq == n for lk, n in zip(links, (len(d0), len(d1))))
+    assert [lk.send_seq for lk in links] == [1 + 5 + 1, 1 + 3 + 1]
+    assert srv.seqs == {}
