@@ -25,7 +25,6 @@ import os
 import random
 import statistics
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))

@@ -20,14 +20,14 @@ end to end.
 from __future__ import annotations
 
 import time
-from dataclasses import dataclass, field
-from typing import Callable, Dict, Iterable, List, Optional, Sequence, Tuple
+from dataclasses import dataclass
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 
 from ..utils.timing import StepProfiler
 from .backends import DraftBackend, SeqState, TargetBackend
-from .layout import BranchKey, branch_specs, full_rows, packed_layout
+from .layout import branch_specs, full_rows, packed_layout
 from .sampling import is_greedy
 
 EOS_DEFAULT = (151643, 151645)

@@ -23,8 +23,7 @@ IPC and keeps the device epoch counter the kernels use as flag values.
 """
 from __future__ import annotations
 
-import math
-from typing import List, Optional
+from typing import List
 
 import torch
 import torch.distributed as dist

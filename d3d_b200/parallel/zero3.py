@@ -31,7 +31,7 @@ that the forward reads (the same values a per-layer gather would return).
 from __future__ import annotations
 
 import math
-from typing import Dict, List, Optional, Tuple
+from typing import Dict, List, Optional
 
 import torch
 import torch.distributed as dist

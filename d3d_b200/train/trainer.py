@@ -23,14 +23,14 @@ import os
 import random
 import time
 from pathlib import Path
-from typing import List, Optional
+from typing import Optional
 
 import torch
 import torch.distributed as dist
 
 from ..checkpoint import expected_keys, write_state
 from .data import IndexedExamples, Prefetcher, RowLimits, worker_rng
-from .blocks import Example, build_packed_block_batch, synthetic_examples
+from .blocks import build_packed_block_batch, synthetic_examples
 from . import trajectory
 from .losses import ce_aux_per_token, decay_weights, lmhead_distill_loss, normalize_objective
 from .model_utils import clean_prefill, student_hidden, teacher_hidden

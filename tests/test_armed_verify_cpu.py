@@ -10,7 +10,6 @@ several drafters where one is late, releases or closes."""
 import torch
 
 from d3d_b200.engine import disagg
-from d3d_b200.engine.backends import SeqState
 
 
 def _verify(sids_prefixes, K):
