@@ -23,7 +23,11 @@ def add_model_args(p: argparse.ArgumentParser, target_flag: str, draft_flag: str
 
 
 def add_data_args(p: argparse.ArgumentParser) -> None:
-    p.add_argument("--dataset", default="synthetic", help="'synthetic' or a JSONL file of prompts")
+    p.add_argument("--dataset", default="synthetic",
+                   help="'synthetic', a JSONL file of prompts, or an evaluation set by name "
+                        "(gsm8k, math500, aime25, humaneval, mbpp, mt-bench, livecodebench-v6; read from "
+                        "$D3D_DATA_CACHE / $D3D_ANSWER_CACHE, rendered with the tokenizer's chat template)")
+    p.add_argument("--enable-thinking", action="store_true", help="evaluation sets: thinking chat template")
     p.add_argument("--max-samples", type=int, default=8)
     p.add_argument("--prompt-min", type=int, default=128)
     p.add_argument("--prompt-max", type=int, default=512)
@@ -39,7 +43,35 @@ def load_prompts(args) -> List[List[int]]:
     if args.tokenizer:
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(args.tokenizer)
+    from ..utils.benchsets import SETS, load_set
+    if args.dataset in SETS and not Path(args.dataset).is_file():
+        if tok is None:
+            raise ValueError(f"--dataset {args.dataset} needs --tokenizer (questions are text)")
+        from ..utils.text import chat_prompt
+        exs, meta = load_set(args.dataset, args.max_samples)
+        args.eval_examples, args.eval_meta, args.eval_tokenizer = exs, meta, tok
+        return [tok.encode(chat_prompt(tok, e.question, thinking=getattr(args, "enable_thinking", False)),
+                           add_special_tokens=False) for e in exs]
     return load_jsonl_prompts(args.dataset, tok, args.max_samples)
+
+
+def score_outputs(args, outputs: List[List[int]]) -> Optional[dict]:
+    """Exact-answer accuracy of decoded outputs on a scored evaluation set
+    (``None`` for other prompt sources); fills ``pred`` / ``correct`` per row."""
+    exs = getattr(args, "eval_examples", None)
+    if not exs:
+        return None
+    from ..utils.benchsets import score
+    tok = args.eval_tokenizer
+    rows, hits, scored = [], 0, 0
+    for e, toks in zip(exs, outputs):
+        pred, ok = score(e.dataset, tok.decode(toks, skip_special_tokens=True), e.gold)
+        rows.append({"index": e.index, "gold": e.gold, "pred": pred, "correct": ok})
+        if ok is not None:
+            scored += 1
+            hits += bool(ok)
+    return {"set": args.eval_meta, "scored": scored, "correct": hits,
+            "accuracy": hits / scored if scored else None, "rows": rows}
 
 
 def is_preset(name: str) -> bool:

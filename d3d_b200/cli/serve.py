@@ -15,7 +15,7 @@ from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
 from ..engine.spec import DecodeConfig
 from ..utils.io import write_json
 from ..utils.runtime import check_paged_capacity
-from .common import add_data_args, add_model_args, build_engine, load_prompts
+from .common import add_data_args, add_model_args, build_engine, load_prompts, score_outputs
 
 
 def parser():
@@ -75,6 +75,11 @@ def main(argv=None):
                "max_batch": max(r["decode_batch_sizes"]) if r["decode_batch_sizes"] else 0}
         if ar is not None:
             row["token_identical_to_ar"] = all(o.tokens == ar["outputs"][o.index] for o in r["outputs"])
+        scores = score_outputs(a, [o.tokens for o in sorted(r["outputs"], key=lambda o: o.index)])
+        if scores is not None:
+            scores.pop("rows")
+            row["accuracy"] = scores["accuracy"]
+            row["scored"] = scores["scored"]
         if a.baseline:
             t0 = time.perf_counter()
             b = eng.generate_ar(prompts, concurrency=c, max_new=budgets)
@@ -82,7 +87,8 @@ def main(argv=None):
             row["speedup"] = row["tps"] / row["ar_tps"] if row["ar_tps"] else None
         rows.append(row)
         print(row, flush=True)
-    write_json(a.output_json, {"rows": rows, "config": vars(a)})
+    write_json(a.output_json, {"rows": rows, "config": {k: v for k, v in vars(a).items() if not k.startswith("eval_")},
+                               "eval_set": getattr(a, "eval_meta", None)})
     return rows
 
 

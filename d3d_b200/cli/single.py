@@ -15,7 +15,7 @@ from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
 from ..engine.spec import DecodeConfig
 from ..utils.io import write_json
 from ..utils.metrics import headline, source_stats, steps_from_output, summarize_acceptance
-from .common import add_data_args, add_model_args, build_engine, load_prompts
+from .common import add_data_args, add_model_args, build_engine, load_prompts, score_outputs
 
 
 def parser() -> argparse.ArgumentParser:
@@ -98,6 +98,12 @@ def main(argv=None):
                "config": vars(a)}
     if a.collect_stage_timings:
         summary["stage_timings"] = eng.decoder.prof.summary()
+    scores = score_outputs(a, [x["tokens"] for x in per])
+    if scores is not None:
+        for x, r in zip(per, scores.pop("rows")):
+            x.update(pred=r["pred"], gold=r["gold"], correct=r["correct"])
+        summary["accuracy"] = scores
+    summary["config"] = {k: v for k, v in vars(a).items() if not k.startswith("eval_")}
     write_json(a.output_json, {"summary": summary, "per_prompt": per})
     write_json(a.summary_json, summary)
     print(summary["headline"])

@@ -1,10 +1,10 @@
 """Prompt sources.
 
-The reference evaluates on seven public datasets (``common/data.py:73-200``);
-this build runs without network access, so prompts come from either a local
-JSONL file (one ``{"prompt": ...}`` or ``{"input_ids": [...]}`` object per
-line) or the synthetic seeded random-token generator used by every
-benchmark configuration.
+Prompts come from a local JSONL file (one ``{"prompt": ...}`` or
+``{"input_ids": [...]}`` object per line), the synthetic seeded random-token
+generator used by every benchmark configuration, or an evaluation set by
+name (``utils/benchsets.py``: the reference's seven sets, read from a local
+cache, with answer scoring).
 """
 from __future__ import annotations
 
