@@ -40,7 +40,7 @@ class DecodeConfig:
     attention_mask_mode: str = "causal"
     max_new_tokens: int = 512
     temperature: float = 0.0
-    top_k: int = 0            # proposal top-k (sampling)
+    top_k: int = 0            # proposal top-k (sampling; 0 = full vocabulary, kernel drafter 1..4)
     top_p: float = 1.0
     target_top_k: int = 0     # target sampling truncation (0 = full vocabulary)
     target_top_p: float = 1.0
@@ -58,8 +58,8 @@ class DecodeConfig:
             raise ValueError("--block-size must be > 1")
         if self.anchor_num < 0:
             raise ValueError("--anchor-num must be non-negative")
-        if not is_greedy(self.temperature) and self.top_k <= 0:
-            raise ValueError("temperature > 0 async sampling requires --proposal-top-k > 0")
+        if self.top_k < 0:
+            raise ValueError("--proposal-top-k must be >= 0 (0 = the drafter's full distribution)")
         if self.backup not in ("neural", "fast"):
             raise ValueError("--backup must be neural or fast")
         if self.backup == "fast" and not is_greedy(self.temperature):

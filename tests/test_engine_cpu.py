@@ -60,11 +60,14 @@ def test_controlled_acceptance_matches_ar_and_rate(pair):
     assert res["mean_accept_length"] > 2.0
 
 
-def test_sampling_runs(pair):
+@pytest.mark.parametrize("proposal_top_k", [8, 0])
+def test_sampling_runs(pair, proposal_top_k):
+    """Sampled decoding with top-k proposals and with proposals from the
+    drafter's full distribution (top-k 0, the reference's default)."""
     t, d = pair
     prompts = _prompts(n=2, seed=5)
     cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=24, ignore_eos=True,
-                       temperature=0.8, top_k=8)
+                       temperature=0.8, top_k=proposal_top_k)
     res = SpecDecoder(TorchTarget(t, temperature=0.8, top_k=0, seed=1), TorchDraft(d, seed=2),
                       cfg).generate(prompts)
     for o in res["outputs"]:
@@ -277,3 +280,28 @@ def test_fast_backup_on_misses_keeps_token_identity():
     assert any("fast_backup" in o.sources for o in res["outputs"])
     with pytest.raises(ValueError):
         DecodeConfig(backup="fast", temperature=0.7, top_k=2).validate()
+
+
+def test_full_support_proposals_are_lossless():
+    """``pq_accept_sparse`` with proposals over the whole vocabulary (the
+    support is every token): the first token it emits follows the target's
+    distribution whatever the proposal, checked with a chi-square bound."""
+    import math
+    from d3d_b200.engine.sampling import pq_accept_sparse
+    g = torch.Generator().manual_seed(3)
+    V, K, B = 12, 3, 40000
+    p = torch.softmax(torch.randn(K, V, generator=g) * 1.5, -1)
+    q = torch.softmax(torch.randn(K - 1, V, generator=g) * 1.5, -1)
+    drafts = torch.stack([torch.multinomial(q[i], B, replacement=True, generator=g) for i in range(K - 1)], 1)
+    blocks = torch.cat([torch.full((B, 1), 5), drafts], 1)
+    q_ids = torch.arange(V).expand(B, K - 1, V)
+    q_probs = q.expand(B, K - 1, V)
+    u = torch.rand(B, K - 1, generator=g)
+    cu = torch.rand(B, generator=g)
+    commit, corr = pq_accept_sparse(blocks, p.expand(B, K, V), q_ids, q_probs, u, cu)
+    first = torch.where(commit >= 2, blocks[:, 1], corr)
+    counts = torch.bincount(first, minlength=V).double()
+    exp = p[0].double() * B
+    chi = (((counts - exp) ** 2) / exp).sum().item()
+    dof = V - 1
+    assert chi < dof + 6 * math.sqrt(2 * dof), chi
