@@ -12,7 +12,7 @@ from ..engine.backends import TorchTarget
 from ..engine.sync import sync_generate, sync_generate_nocache
 from ..utils.io import write_json
 from ..utils.metrics import steps_from_output, summarize_acceptance
-from .common import add_data_args, add_model_args, load_module, load_prompts
+from .common import add_data_args, add_model_args, load_module, load_prompts, score_outputs
 
 
 def main(argv=None):
@@ -45,7 +45,12 @@ def main(argv=None):
                      "summary": summarize_acceptance(steps_from_output(st.acceptance_lengths, a.block_size,
                                                                        st.output_tokens), a.block_size - 1),
                      "matches_ar": (st.output_tokens == ar["outputs"][i]) if ar else None})
-    write_json(a.output_json, {"rows": rows, "config": vars(a)})
+    scores = score_outputs(a, [r["tokens"] for r in rows])
+    if scores is not None:
+        for r, sc in zip(rows, scores.pop("rows")):
+            r.update(pred=sc["pred"], gold=sc["gold"], correct=sc["correct"])
+    write_json(a.output_json, {"rows": rows, "accuracy": scores,
+                               "config": {k: v for k, v in vars(a).items() if not k.startswith("eval_")}})
     print({"samples": len(rows), "matches_ar": [r["matches_ar"] for r in rows]})
     return rows
 

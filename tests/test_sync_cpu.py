@@ -58,3 +58,19 @@ def test_sync_sampling_runs(pair):
     t, d = pair
     st = sync_generate(t, d, _prompts(1)[0], 20, block_size=8, temperature=0.7, top_k=20, seed=3)
     assert len(st.output_tokens) == 20
+
+
+def test_sync_cli_tiny_pair(tmp_path):
+    """The synchronous denoising CLI end to end on the tiny pair, cached and
+    uncached, with the AR baseline and its JSON summary."""
+    import json
+    from d3d_b200.cli import sync
+    for extra in ([], ["--no-kvcache"]):
+        out = tmp_path / f"sync{len(extra)}.json"
+        rows = sync.main(["--verifier", "tiny-target", "--drafter", "tiny-drafter", "--device", "cpu",
+                          "--max-new-tokens", "10", "--block-size", "4", "--denoising-steps", "2",
+                          "--max-samples", "2", "--prompt-min", "6", "--prompt-max", "12", "--baseline",
+                          "--output-json", str(out)] + extra)
+        assert len(rows) == 2 and all(r["tokens"] for r in rows)
+        d = json.loads(out.read_text())
+        assert len(d["rows"]) == 2 and "config" in d
