@@ -10,7 +10,6 @@ baseline every speedup is measured against.
 """
 from __future__ import annotations
 
-from dataclasses import replace
 from typing import Callable, List, Optional, Sequence
 
 import torch
@@ -111,11 +110,13 @@ class D3DEngine:
     def generate(self, prompts: Sequence[Sequence[int]], *, max_new_tokens: Optional[int] = None,
                  concurrency: int = 1, controlled: Optional[Callable[[int], object]] = None,
                  max_new: Optional[Sequence[int]] = None) -> dict:
-        """Speculative decoding.  ``max_new``: per-request output budgets."""
-        if max_new_tokens is not None and max_new_tokens != self.decoder.cfg.max_new_tokens:
-            self.decoder.cfg = replace(self.decoder.cfg, max_new_tokens=int(max_new_tokens))
+        """Speculative decoding.  ``max_new``: per-request output budgets;
+        ``max_new_tokens``: one budget for every request of this call (the
+        engine's default stays as configured)."""
         if isinstance(prompts, torch.Tensor):
             prompts = prompts.tolist()
+        if max_new is None and max_new_tokens is not None:
+            max_new = [int(max_new_tokens)] * len(prompts)
         return self.decoder.generate(prompts, concurrency=concurrency, controlled=controlled, max_new=max_new)
 
     def generate_ar(self, prompts: Sequence[Sequence[int]], *, max_new_tokens: Optional[int] = None,

@@ -118,3 +118,27 @@ def build_engine(args, decode, max_seqs: int, max_context: int, pages: Optional[
     t = load_module(args.target, dev, args.seed)
     d = load_module(args.draft, dev, args.seed, args.draft_layers, args.mask_token_id)
     return D3DEngine.from_modules(t, d, decode)
+
+
+def hf_greedy_agreement(target: str, device, prompts: List[List[int]], outputs: List[List[int]],
+                        budgets: List[int]) -> dict:
+    """Greedy continuations of ``transformers``' own Qwen3 implementation for
+    the same checkpoint (the reference's validation oracle): the fraction of
+    requests whose output is identical, and each request's first divergent
+    position (``None`` when identical).  On bf16 kernels an early divergence
+    can be a near-tie, not an error; fp32 models agree exactly."""
+    import transformers
+    dt = torch.bfloat16 if torch.device(device).type == "cuda" else torch.float32
+    hf = transformers.AutoModelForCausalLM.from_pretrained(target, dtype=dt).to(device).eval()
+    first = []
+    for p, o, n in zip(prompts, outputs, budgets):
+        with torch.no_grad():
+            ref = hf.generate(torch.tensor([p], device=device), max_new_tokens=int(n), do_sample=False,
+                              pad_token_id=0)[0, len(p):].tolist()
+        k = next((i for i, (x, y) in enumerate(zip(o, ref)) if x != y), None)
+        if k is None and len(o) != len(ref):
+            k = min(len(o), len(ref))
+        first.append(k)
+    same = sum(k is None for k in first)
+    return {"identical": same, "requests": len(first), "rate": same / max(1, len(first)),
+            "first_divergence": first}

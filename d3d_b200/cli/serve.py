@@ -15,7 +15,8 @@ from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
 from ..engine.spec import DecodeConfig
 from ..utils.io import write_json
 from ..utils.runtime import check_paged_capacity
-from .common import add_data_args, add_model_args, build_engine, load_prompts, score_outputs
+from .common import (add_data_args, add_model_args, build_engine, hf_greedy_agreement, is_preset,
+                     load_prompts, score_outputs)
 
 
 def parser():
@@ -35,6 +36,8 @@ def parser():
     p.add_argument("--backup", choices=["neural", "fast"], default="neural",
                    help="on a branch miss: redraft (neural) or verify a random block at once (fast)")
     p.add_argument("--validate", action="store_true", help="check token identity against AR decoding")
+    p.add_argument("--validate-hf", action="store_true",
+                   help="compare the outputs with transformers' greedy generate on the target checkpoint")
     p.add_argument("--baseline", action="store_true", help="AR baseline at each concurrency")
     p.add_argument("--controlled-accept-mean", type=float, default=None)
     p.add_argument("--output-json", default=None)
@@ -75,7 +78,13 @@ def main(argv=None):
                "max_batch": max(r["decode_batch_sizes"]) if r["decode_batch_sizes"] else 0}
         if ar is not None:
             row["token_identical_to_ar"] = all(o.tokens == ar["outputs"][o.index] for o in r["outputs"])
-        scores = score_outputs(a, [o.tokens for o in sorted(r["outputs"], key=lambda o: o.index)])
+        outs = [o.tokens for o in sorted(r["outputs"], key=lambda o: o.index)]
+        if a.validate_hf:
+            if is_preset(a.target):
+                raise SystemExit("--validate-hf needs a target checkpoint directory, not a preset")
+            row["hf_greedy"] = hf_greedy_agreement(a.target, a.device, prompts, outs,
+                                                   budgets or [a.max_new_tokens] * len(prompts))
+        scores = score_outputs(a, outs)
         if scores is not None:
             scores.pop("rows")
             row["accuracy"] = scores["accuracy"]

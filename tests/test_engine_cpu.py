@@ -305,3 +305,15 @@ def test_full_support_proposals_are_lossless():
     chi = (((counts - exp) ** 2) / exp).sum().item()
     dof = V - 1
     assert chi < dof + 6 * math.sqrt(2 * dof), chi
+
+
+def test_call_budget_does_not_change_the_engine_default(pair):
+    """A per-call ``max_new_tokens`` (a short warm-up, say) leaves the
+    engine's configured budget for later calls."""
+    from d3d_b200.api import D3DEngine
+    t, d = pair
+    eng = D3DEngine.from_modules(t, d, DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=20,
+                                                    ignore_eos=True))
+    prompts = _prompts(n=1, seed=9)
+    assert len(eng.generate(prompts, max_new_tokens=5)["outputs"][0].tokens) == 5
+    assert len(eng.generate(prompts)["outputs"][0].tokens) == 20

@@ -27,3 +27,14 @@ def test_logits_and_greedy_match_transformers(tmp_path):
             ref = hf.generate(torch.tensor([p]), max_new_tokens=16, do_sample=False, min_new_tokens=16,
                               pad_token_id=0)[0, len(p):].tolist()
         assert o == ref
+
+
+def test_serve_cli_validates_against_transformers(tmp_path):
+    from d3d_b200.cli import serve
+    save_model(build_model(tiny_target(), seed=0), tmp_path / "t")
+    rows = serve.main(["--target", str(tmp_path / "t"), "--draft", "tiny-drafter", "--device", "cpu",
+                       "--pages", "256", "--concurrency", "2", "--max-new-tokens", "12", "--block-size", "8",
+                       "--max-samples", "2", "--prompt-min", "8", "--prompt-max", "14", "--ignore-eos",
+                       "--validate-hf"])
+    hf = rows[0]["hf_greedy"]
+    assert hf["identical"] == hf["requests"] == 2 and hf["first_divergence"] == [None, None]
