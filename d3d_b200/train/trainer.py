@@ -151,7 +151,10 @@ def train(args) -> dict:
     torch.manual_seed(args.seed + rank)
     rng = random.Random(args.seed * 1000 + rank)
     cdt = torch.bfloat16 if (device.type == "cuda" and args.dtype == "bf16") else torch.float32
-    student = _build(args.draft_model, device, cdt, args.seed, args.draft_layers, args.mask_token_id)
+    # resuming starts from the checkpoint's weights (its fp32 master values);
+    # the optimizer shards and moments come from its per-rank files below
+    student = (_build(args.resume, device, cdt, args.seed, None, args.mask_token_id) if args.resume else
+               _build(args.draft_model, device, cdt, args.seed, args.draft_layers, args.mask_token_id))
     student.train()
     teacher = None
     objective = normalize_objective(args.objective)

@@ -227,3 +227,27 @@ def test_gradient_checkpointing_keeps_clean_prefix_cache():
     assert len(outs[0][1]) == len(outs[1][1]) > 0
     for a, b in zip(outs[0][1], outs[1][1]):
         torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("extra", [[], ["--fsdp"]])
+def test_resume_continues_exactly(tmp_path, extra):
+    """Two steps, a checkpoint, then the third step from it: the same weights
+    as three uninterrupted steps (weights, optimizer shards and moments, data
+    cursor all restored)."""
+    from d3d_b200.checkpoint import load_model
+    from d3d_b200.train.args import parser
+    from d3d_b200.train.trainer import train
+
+    def run(out, steps, more):
+        train(parser().parse_args([
+            "--draft-model", "tiny-drafter", "--target-model", "tiny-target", "--output-dir", str(out),
+            "--seq-len", "80", "--batch-size", "2", "--parallel-anchors-per-example", "3",
+            "--max-steps", str(steps), "--block-size", "8", "--vocab-chunk", "256", "--device", "cpu",
+            "--dtype", "fp32", "--min-lr-ratio", "1.0", "--log-every", "0"] + extra + more))
+
+    run(tmp_path / "a", 3, ["--save-final"])
+    run(tmp_path / "b", 2, ["--save-every", "2"])
+    run(tmp_path / "b", 3, ["--save-final", "--resume", str(tmp_path / "b" / "step_0000002")])
+    ma = dict(load_model(tmp_path / "a" / "step_0000003").named_parameters())
+    mb = dict(load_model(tmp_path / "b" / "step_0000003").named_parameters())
+    assert all(torch.equal(ma[n], mb[n]) for n in ma)
