@@ -247,11 +247,11 @@ def test_batched_armed_rounds(monkeypatch):
     g0, g1 = 0 * srv.ID_STRIDE + 1, 1 * srv.ID_STRIDE + 1
     assert be.log == [
         ("prefill", [g0, g1]),
-        ("verify", [2, 3]),                # round 2 on the host, then the next round is armed
-        ("armed", [[5], [6]]),             # round 3 on the device
+        ("verify", [2, 3]),                # the second serving round runs on the host; the next is armed
+        ("armed", [[5], [6]]),             # the third on the device
         ("arm-placeholder", [2, None]),    # drafter 1's request lands after the wait ...
-        ("verify", [9, 8]),                # ... so round 4 runs on the host
-        ("arm-placeholder", [2, 3]),       # drafter 1 releases: round 5 on the host
+        ("verify", [9, 8]),                # ... so the fourth runs on the host
+        ("arm-placeholder", [2, 3]),       # drafter 1 releases: the fifth runs on the host
         ("verify", [12]), ("release", g1),
         ("verify", [15]),                  # drafter 1 closes in this round: nothing armed
         ("release", g0),
