@@ -142,3 +142,31 @@ def hf_greedy_agreement(target: str, device, prompts: List[List[int]], outputs: 
     same = sum(k is None for k in first)
     return {"identical": same, "requests": len(first), "rate": same / max(1, len(first)),
             "first_divergence": first}
+
+
+def parse_cpu_list(value: Optional[str]) -> List[int]:
+    """CPU ids from a list such as ``"0-3,8,10-11"`` (empty for ``None``)."""
+    out: List[int] = []
+    for part in (value or "").replace(" ", "").split(","):
+        if not part:
+            continue
+        if "-" in part:
+            lo, hi = (int(x) for x in part.split("-", 1))
+            if hi < lo:
+                raise ValueError(f"bad CPU range {part!r}")
+            out.extend(range(lo, hi + 1))
+        else:
+            out.append(int(part))
+    return sorted(set(out))
+
+
+def pin_host_threads(*cpu_lists: Optional[str]) -> Optional[List[int]]:
+    """Restrict this process to the union of the given CPU lists (the
+    reference pins its verifier and drafter processes; here the target's
+    host work runs in the coordinator's process, so both sets apply to it)."""
+    import os
+    cpus = sorted(set(c for v in cpu_lists for c in parse_cpu_list(v)))
+    if not cpus:
+        return None
+    os.sched_setaffinity(0, set(cpus))
+    return cpus

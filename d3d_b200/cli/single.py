@@ -15,7 +15,7 @@ from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
 from ..engine.spec import DecodeConfig
 from ..utils.io import write_json
 from ..utils.metrics import headline, source_stats, steps_from_output, summarize_acceptance
-from .common import add_data_args, add_model_args, build_engine, load_prompts, score_outputs
+from .common import add_data_args, add_model_args, build_engine, load_prompts, pin_host_threads, score_outputs
 
 
 def parser() -> argparse.ArgumentParser:
@@ -44,11 +44,14 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--warmup-new-tokens", type=int, default=32)
     p.add_argument("--output-json", default=None)
     p.add_argument("--summary-json", default=None)
+    p.add_argument("--verifier-cpu-affinity", default=None, help="CPU list, e.g. 0-7 (host threads)")
+    p.add_argument("--draft-cpu-affinity", default=None, help="CPU list, e.g. 8-15 (host threads)")
     return p
 
 
 def main(argv=None):
     a = parser().parse_args(argv)
+    pin_host_threads(a.verifier_cpu_affinity, a.draft_cpu_affinity)
     counts = None if a.packed_accepted_counts == "all" else tuple(int(x) for x in a.packed_accepted_counts.split(","))
     decode = DecodeConfig(block_size=a.block_size, anchor_num=a.anchor_num, attention_mask_mode=a.attention_mask_mode,
                           max_new_tokens=a.max_new_tokens, temperature=a.temperature, top_k=a.proposal_top_k,

@@ -84,3 +84,20 @@ def test_host_profiler_phases():
     with off.phase("x"):
         pass
     assert off.summary()["calls"] == {} and off.dev_begin("v", None) is None
+
+
+def test_cpu_lists_and_pinning():
+    import os
+    from d3d_b200.cli.common import parse_cpu_list, pin_host_threads
+    assert parse_cpu_list("0-3,8, 10-11") == [0, 1, 2, 3, 8, 10, 11]
+    assert parse_cpu_list(None) == [] and parse_cpu_list("") == []
+    with pytest.raises(ValueError):
+        parse_cpu_list("5-2")
+    before = os.sched_getaffinity(0)
+    try:
+        one = str(min(before))
+        assert pin_host_threads(one, None) == [int(one)]
+        assert os.sched_getaffinity(0) == {int(one)}
+        assert pin_host_threads(None, None) is None
+    finally:
+        os.sched_setaffinity(0, before)
