@@ -52,6 +52,7 @@ class DecodeConfig:
     use_cond: bool = True     # feed target hidden to a conditioned drafter
     backup: str = "neural"    # on a branch miss: "neural" redraft, or "fast" random block (greedy only)
     backup_seed: int = 42
+    fast_miss_anchors: int = 0  # fast backup: anchors of a fast-seeded block's drafts (0 = anchor_num)
 
     def validate(self):
         if self.block_size <= 1:
@@ -62,6 +63,8 @@ class DecodeConfig:
             raise ValueError("--proposal-top-k must be >= 0 (0 = the drafter's full distribution)")
         if self.backup not in ("neural", "fast"):
             raise ValueError("--backup must be neural or fast")
+        if self.fast_miss_anchors < 0:
+            raise ValueError("--fast-miss-anchors must be non-negative")
         if self.backup == "fast" and not is_greedy(self.temperature):
             raise ValueError("the fast backup (random block on a miss) is greedy only")
         return self
@@ -209,7 +212,8 @@ class SpecDecoder:
             ids[:, 0] = torch.tensor([s.anchor for s in group])
             pos = torch.stack([torch.arange(s.prefix, s.prefix + k) for s in group])
             rows = torch.stack([full_rows(s.prefix + k, k) for s in group])
-            out = self.d.forward(group, ids, pos, rows, store=False, topk=a + 1 if a else 0,
+            wide = max(a, self.cfg.fast_miss_anchors) if a else 0
+            out = self.d.forward(group, ids, pos, rows, store=False, topk=wide + 1 if a else 0,
                                  cond_rows=self._cond_rows(b, k, [0]))
             for i, s in enumerate(group):
                 top = out["top"][i].clone().cpu() if "top" in out else None
@@ -240,13 +244,25 @@ class SpecDecoder:
         seeds = [s for s in seqs if s.extra.get("needs_seed")]
         if seeds:
             self._seed_tops(seeds)
+        # A sequence whose block was a random fast-backup block almost surely
+        # commits only its anchor: its packed forward drafts only the commit
+        # length 1 outcomes, with ``fast_miss_anchors`` anchors (default: the
+        # anchor count), in micro-batches of its own (``serving/engine.py:88-104``)
+        shallow_ids = {s.index for s in seeds} if self.cfg.backup == "fast" else set()
+        parts = [([s for s in seqs if s.index not in shallow_ids], False),
+                 ([s for s in seqs if s.index in shallow_ids], True)]
+        fanout = self.cfg.fast_miss_anchors or a
+        groups = [(part[off:off + self.cfg.draft_microbatch], shallow) for part, shallow in parts
+                  for off in range(0, len(part), self.cfg.draft_microbatch)]
         results: Dict[int, _Outcomes] = {}
-        for off in range(0, len(seqs), self.cfg.draft_microbatch):
-            group = seqs[off:off + self.cfg.draft_microbatch]
+        for group, shallow in groups:
             layouts = []
             for s in group:
                 top = None if s.top is None else s.top.tolist()
-                specs = branch_specs(s.current.tolist(), top, a, self.cfg.packed_accepted_counts)
+                if shallow:
+                    specs = branch_specs(s.current.tolist(), top, fanout if a else 0, (1,))
+                else:
+                    specs = branch_specs(s.current.tolist(), top, a, self.cfg.packed_accepted_counts)
                 layouts.append(packed_layout(s.current, specs, s.prefix, k, self.d.mask_id,
                                              self.cfg.attention_mask_mode))
             q = layouts[0].q_len

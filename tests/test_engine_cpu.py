@@ -261,10 +261,12 @@ def test_gemm_policies():
     assert s * 272 * 2048 * 4 <= 2048 * 2048 * 2 * 2
 
 
-def test_fast_backup_on_misses_keeps_token_identity():
+@pytest.mark.parametrize("miss_anchors", [0, 3])
+def test_fast_backup_on_misses_keeps_token_identity(miss_anchors):
     """backup="fast": a miss verifies [anchor, random...] immediately (no
-    redraft) and seeds the next step's branches off the critical path;
-    greedy output still equals AR."""
+    redraft) and seeds the next step's branches off the critical path (a
+    shallow packed forward: commit-1 outcomes only, ``fast_miss_anchors``
+    anchors); greedy output still equals AR."""
     from d3d_b200.config import tiny_drafter, tiny_target
     from d3d_b200.engine.backends import TorchDraft, TorchTarget
     from d3d_b200.engine.spec import DecodeConfig, SpecDecoder, ar_generate
@@ -273,8 +275,19 @@ def test_fast_backup_on_misses_keeps_token_identity():
     prompts = [[rng.randrange(2, 1000) for _ in range(rng.randint(12, 30))] for _ in range(3)]
     tgt = TorchTarget(build_model(tiny_target(), seed=0))
     drf = TorchDraft(build_model(tiny_drafter(cond=True), seed=1))
-    cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=40, ignore_eos=True, backup="fast")
-    res = SpecDecoder(tgt, drf, cfg).generate(prompts, concurrency=2)
+    cfg = DecodeConfig(block_size=8, anchor_num=1, max_new_tokens=40, ignore_eos=True, backup="fast",
+                       fast_miss_anchors=miss_anchors)
+    dec = SpecDecoder(tgt, drf, cfg)
+    shapes = []
+    orig = dec.d.forward
+
+    def spy(group, ids, *a, **k):
+        shapes.append(tuple(ids.shape))
+        return orig(group, ids, *a, **k)
+    dec.d.forward = spy
+    res = dec.generate(prompts, concurrency=2)
+    fan = miss_anchors or 1
+    assert (1, 8 + fan * 8) in shapes or (2, 8 + fan * 8) in shapes    # a shallow packed forward ran
     ar = ar_generate(tgt, prompts, 40, ignore_eos=True)["outputs"]
     assert [o.tokens for o in res["outputs"]] == ar
     assert any("fast_backup" in o.sources for o in res["outputs"])
