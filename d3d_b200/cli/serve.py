@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import argparse
 import time
+from typing import Dict
 
 from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
 from ..engine.spec import DecodeConfig
@@ -23,81 +24,120 @@ def parser():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     add_model_args(p, "--target", "--draft")
     add_data_args(p)
+    p.add_argument("--datasets", nargs="+", default=None,
+                   help="several prompt sources in one run (names or files, as --dataset); one row per "
+                        "(dataset, concurrency, repeat)")
     p.add_argument("--pages", type=int, default=4096)
     p.add_argument("--page-size", type=int, default=16)
     p.add_argument("--concurrency", default="1,4,8,16")
     p.add_argument("--max-new-tokens", type=int, default=256)
     p.add_argument("--max-new-tokens-range", default=None,
                    help="LO,HI: per-request output budgets drawn uniformly (seeded), e.g. 128,512")
+    p.add_argument("--repeats", type=int, default=1, help="timed runs per (dataset, concurrency)")
     p.add_argument("--block-size", type=int, default=16)
     p.add_argument("--anchor-num", type=int, default=1)
     p.add_argument("--draft-microbatch", type=int, default=4)
     p.add_argument("--ignore-eos", action="store_true")
-    p.add_argument("--backup", choices=["neural", "fast"], default="neural",
-                   help="on a branch miss: redraft (neural) or verify a random block at once (fast)")
+    p.add_argument("--backup", choices=["neural", "fast", "fast_legacy"], default="neural",
+                   help="on a branch miss: redraft (neural) or verify a random block at once (fast: the "
+                        "block's drafts cover commit length 1 only; fast_legacy: every commit length)")
+    p.add_argument("--fast-miss-anchors", type=int, default=0,
+                   help="fast backup: anchors drafted after a random block (0 = --anchor-num)")
     p.add_argument("--validate", action="store_true", help="check token identity against AR decoding")
     p.add_argument("--validate-hf", action="store_true",
                    help="compare the outputs with transformers' greedy generate on the target checkpoint")
     p.add_argument("--baseline", action="store_true", help="AR baseline at each concurrency")
     p.add_argument("--controlled-accept-mean", type=float, default=None)
-    p.add_argument("--output-json", default=None)
+    p.add_argument("--output-json", "--output", dest="output_json", default=None)
     return p
+
+
+def _load_sets(a) -> Dict[str, dict]:
+    """Prompts (and evaluation-set scoring state) of every requested source."""
+    sets, first = {}, a.dataset
+    for name in a.datasets or [a.dataset]:
+        a.dataset = name
+        for k in ("eval_examples", "eval_meta", "eval_tokenizer"):
+            if hasattr(a, k):
+                delattr(a, k)
+        prompts = load_prompts(a)
+        if not prompts:
+            raise ValueError(f"dataset {name} has no prompts")
+        sets[name] = {"prompts": prompts, "eval": {k: getattr(a, k) for k in
+                                                   ("eval_examples", "eval_meta", "eval_tokenizer")
+                                                   if hasattr(a, k)}}
+    a.dataset = first
+    return sets
 
 
 def main(argv=None):
     a = parser().parse_args(argv)
     conc = [int(c) for c in a.concurrency.split(",")]
-    prompts = load_prompts(a)
-    budgets = None
+    if min(conc + [a.max_samples, a.max_new_tokens, a.repeats, a.pages]) < 1:
+        raise SystemExit("concurrency, samples, token count, repeats and pages must be positive")
+    sets = _load_sets(a)
+    budgets = {}
     if a.max_new_tokens_range:
         import random
         lo, hi = (int(x) for x in a.max_new_tokens_range.split(","))
         rng = random.Random(a.seed + 17)
-        budgets = [rng.randint(lo, hi) for _ in prompts]
+        budgets = {n: [rng.randint(lo, hi) for _ in d["prompts"]] for n, d in sets.items()}
         a.max_new_tokens = hi
-    check_paged_capacity([len(p) for p in prompts], a.max_new_tokens, conc, a.pages, a.page_size,
-                         a.block_size, a.anchor_num)
+    lens = [len(p) for d in sets.values() for p in d["prompts"]]
+    check_paged_capacity(lens, a.max_new_tokens, conc, a.pages, a.page_size, a.block_size, a.anchor_num)
     decode = DecodeConfig(block_size=a.block_size, anchor_num=a.anchor_num, max_new_tokens=a.max_new_tokens,
-                          draft_microbatch=a.draft_microbatch, ignore_eos=a.ignore_eos, backup=a.backup)
-    eng = build_engine(a, decode, max_seqs=max(conc), max_context=max(len(p) for p in prompts) + a.max_new_tokens + 64,
-                       pages=a.pages)
-    ar = None
-    if a.validate or a.baseline or a.controlled_accept_mean is not None:
-        ar = eng.generate_ar(prompts, concurrency=max(conc), max_new=budgets)
-    ctl = None
-    if a.controlled_accept_mean is not None:
-        rate = rate_for_mean_accept(a.controlled_accept_mean, a.block_size)
-        ctl = lambda i: ControlledAcceptance(prompts[i] + ar["outputs"][i], rate, int(eng.draft.vocab_size),
-                                             seed=a.seed, stream=i)
-    eng.generate(prompts[:1], max_new_tokens=16, controlled=ctl)           # warm-up
-    rows = []
-    for c in conc:
-        r = eng.generate(prompts, concurrency=c, controlled=ctl, max_new=budgets)
-        row = {"concurrency": c, "tps": r["tps"], "elapsed_s": r["elapsed_s"], "output_tokens": r["output_tokens"],
-               "mean_accept_length": r["mean_accept_length"], "miss_rounds": r["miss_rounds"],
-               "max_batch": max(r["decode_batch_sizes"]) if r["decode_batch_sizes"] else 0}
-        if ar is not None:
-            row["token_identical_to_ar"] = all(o.tokens == ar["outputs"][o.index] for o in r["outputs"])
-        outs = [o.tokens for o in sorted(r["outputs"], key=lambda o: o.index)]
-        if a.validate_hf:
-            if is_preset(a.target):
-                raise SystemExit("--validate-hf needs a target checkpoint directory, not a preset")
-            row["hf_greedy"] = hf_greedy_agreement(a.target, a.device, prompts, outs,
-                                                   budgets or [a.max_new_tokens] * len(prompts))
-        scores = score_outputs(a, outs)
-        if scores is not None:
-            scores.pop("rows")
-            row["accuracy"] = scores["accuracy"]
-            row["scored"] = scores["scored"]
-        if a.baseline:
-            t0 = time.perf_counter()
-            b = eng.generate_ar(prompts, concurrency=c, max_new=budgets)
-            row["ar_tps"] = b["output_tokens"] / (time.perf_counter() - t0)
-            row["speedup"] = row["tps"] / row["ar_tps"] if row["ar_tps"] else None
-        rows.append(row)
-        print(row, flush=True)
+                          draft_microbatch=a.draft_microbatch, ignore_eos=a.ignore_eos, backup=a.backup,
+                          fast_miss_anchors=a.fast_miss_anchors)
+    eng = build_engine(a, decode, max_seqs=max(conc), max_context=max(lens) + a.max_new_tokens + 64, pages=a.pages)
+    rows, warm = [], False
+    for name, d in sets.items():
+        prompts, bud = d["prompts"], budgets.get(name)
+        for k, v in d["eval"].items():
+            setattr(a, k, v)
+        if not d["eval"]:
+            a.eval_examples = None
+        ar = None
+        if a.validate or a.baseline or a.controlled_accept_mean is not None:
+            ar = eng.generate_ar(prompts, concurrency=max(conc), max_new=bud)
+        ctl = None
+        if a.controlled_accept_mean is not None:
+            rate = rate_for_mean_accept(a.controlled_accept_mean, a.block_size)
+            ctl = (lambda ps, outs: lambda i: ControlledAcceptance(ps[i] + outs[i], rate, int(eng.draft.vocab_size),
+                                                                   seed=a.seed, stream=i))(prompts, ar["outputs"])
+        if not warm:
+            eng.generate(prompts[:1], max_new_tokens=16, controlled=ctl)           # warm-up
+            warm = True
+        for c in conc:
+            ar_tps = None
+            if a.baseline:
+                t0 = time.perf_counter()
+                b = eng.generate_ar(prompts, concurrency=c, max_new=bud)
+                ar_tps = b["output_tokens"] / (time.perf_counter() - t0)
+            for rep in range(a.repeats):
+                r = eng.generate(prompts, concurrency=c, controlled=ctl, max_new=bud)
+                row = {"dataset": name, "concurrency": c, "repeat": rep, "requests": len(prompts), "tps": r["tps"],
+                       "elapsed_s": r["elapsed_s"], "output_tokens": r["output_tokens"],
+                       "mean_accept_length": r["mean_accept_length"], "miss_rounds": r["miss_rounds"],
+                       "max_batch": max(r["decode_batch_sizes"]) if r["decode_batch_sizes"] else 0}
+                if ar is not None:
+                    row["token_identical_to_ar"] = all(o.tokens == ar["outputs"][o.index] for o in r["outputs"])
+                outs = [o.tokens for o in sorted(r["outputs"], key=lambda o: o.index)]
+                if a.validate_hf and rep == 0:
+                    if is_preset(a.target):
+                        raise SystemExit("--validate-hf needs a target checkpoint directory, not a preset")
+                    row["hf_greedy"] = hf_greedy_agreement(a.target, a.device, prompts, outs,
+                                                           bud or [a.max_new_tokens] * len(prompts))
+                scores = score_outputs(a, outs)
+                if scores is not None:
+                    row["accuracy"] = scores["accuracy"]
+                    row["scored"] = scores["scored"]
+                if ar_tps is not None:
+                    row["ar_tps"] = ar_tps
+                    row["speedup"] = row["tps"] / ar_tps if ar_tps else None
+                rows.append(row)
+                print(row, flush=True)
     write_json(a.output_json, {"rows": rows, "config": {k: v for k, v in vars(a).items() if not k.startswith("eval_")},
-                               "eval_set": getattr(a, "eval_meta", None)})
+                               "eval_sets": {n: d["eval"].get("eval_meta") for n, d in sets.items()}})
     return rows
 
 

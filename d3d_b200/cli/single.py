@@ -36,8 +36,11 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--collect-stage-timings", action="store_true",
                    help="host time per coordinator phase and device time per captured forward")
     p.add_argument("--ignore-eos", action="store_true")
-    p.add_argument("--backup", choices=["neural", "fast"], default="neural",
-                   help="on a branch miss: redraft (neural) or verify a random block at once (fast)")
+    p.add_argument("--backup", choices=["neural", "fast", "fast_legacy"], default="neural",
+                   help="on a branch miss: redraft (neural) or verify a random block at once (fast: the "
+                        "block's drafts cover commit length 1 only; fast_legacy: every commit length)")
+    p.add_argument("--fast-miss-anchors", type=int, default=0,
+                   help="fast backup: anchors drafted after a random block (0 = --anchor-num)")
     p.add_argument("--baseline", action="store_true", help="also run target-only AR decoding")
     p.add_argument("--controlled-accept-mean", type=float, default=None,
                    help="acceptance-controlled mode (needs --baseline's AR oracle)")
@@ -56,7 +59,8 @@ def main(argv=None):
     decode = DecodeConfig(block_size=a.block_size, anchor_num=a.anchor_num, attention_mask_mode=a.attention_mask_mode,
                           max_new_tokens=a.max_new_tokens, temperature=a.temperature, top_k=a.proposal_top_k,
                           top_p=a.proposal_top_p, ignore_eos=a.ignore_eos, packed_accepted_counts=counts,
-                          target_top_k=a.target_top_k, target_top_p=a.target_top_p, backup=a.backup)
+                          target_top_k=a.target_top_k, target_top_p=a.target_top_p, backup=a.backup,
+                          fast_miss_anchors=a.fast_miss_anchors)
     prompts = load_prompts(a)
     eng = build_engine(a, decode, max_seqs=2, max_context=max(len(p) for p in prompts) + a.max_new_tokens + 64)
     ar = None

@@ -50,7 +50,7 @@ class DecodeConfig:
     eos: Tuple[int, ...] = EOS_DEFAULT
     packed_accepted_counts: Optional[Tuple[int, ...]] = None
     use_cond: bool = True     # feed target hidden to a conditioned drafter
-    backup: str = "neural"    # on a branch miss: "neural" redraft, or "fast" random block (greedy only)
+    backup: str = "neural"    # on a branch miss: "neural" redraft; "fast" / "fast_legacy" random block (greedy only)
     backup_seed: int = 42
     fast_miss_anchors: int = 0  # fast backup: anchors of a fast-seeded block's drafts (0 = anchor_num)
 
@@ -61,11 +61,11 @@ class DecodeConfig:
             raise ValueError("--anchor-num must be non-negative")
         if self.top_k < 0:
             raise ValueError("--proposal-top-k must be >= 0 (0 = the drafter's full distribution)")
-        if self.backup not in ("neural", "fast"):
-            raise ValueError("--backup must be neural or fast")
+        if self.backup not in ("neural", "fast", "fast_legacy"):
+            raise ValueError("--backup must be neural, fast or fast_legacy")
         if self.fast_miss_anchors < 0:
             raise ValueError("--fast-miss-anchors must be non-negative")
-        if self.backup == "fast" and not is_greedy(self.temperature):
+        if self.backup != "neural" and not is_greedy(self.temperature):
             raise ValueError("the fast backup (random block on a miss) is greedy only")
         return self
 
@@ -212,7 +212,7 @@ class SpecDecoder:
             ids[:, 0] = torch.tensor([s.anchor for s in group])
             pos = torch.stack([torch.arange(s.prefix, s.prefix + k) for s in group])
             rows = torch.stack([full_rows(s.prefix + k, k) for s in group])
-            wide = max(a, self.cfg.fast_miss_anchors) if a else 0
+            wide = max(a, self.cfg.fast_miss_anchors) if a and self.cfg.backup == "fast" else a
             out = self.d.forward(group, ids, pos, rows, store=False, topk=wide + 1 if a else 0,
                                  cond_rows=self._cond_rows(b, k, [0]))
             for i, s in enumerate(group):
@@ -247,7 +247,8 @@ class SpecDecoder:
         # A sequence whose block was a random fast-backup block almost surely
         # commits only its anchor: its packed forward drafts only the commit
         # length 1 outcomes, with ``fast_miss_anchors`` anchors (default: the
-        # anchor count), in micro-batches of its own (``serving/engine.py:88-104``)
+        # anchor count), in micro-batches of its own (``serving/engine.py:88-104``).
+        # ``fast_legacy`` drafts every outcome of such a block at full depth.
         shallow_ids = {s.index for s in seeds} if self.cfg.backup == "fast" else set()
         parts = [([s for s in seqs if s.index not in shallow_ids], False),
                  ([s for s in seqs if s.index in shallow_ids], True)]
@@ -504,7 +505,7 @@ class SpecDecoder:
             running = remaining
             miss_rounds += bool(recover)
             with self.prof.phase("recover"):
-                if cfg.backup == "fast":
+                if cfg.backup != "neural":
                     self.fast_backup(recover)
                 else:
                     self.recover(recover)

@@ -225,6 +225,30 @@ def test_serve_cli_tiny_pair(tmp_path):
     assert all(r["token_identical_to_ar"] for r in rows)
 
 
+def test_serve_cli_datasets_repeats_and_fast_backup(tmp_path):
+    """Several prompt sources in one run, repeated cells, and both fast-miss
+    policies (shallow drafts with their own anchor count, and full-depth
+    ``fast_legacy``) stay token-identical to AR."""
+    import json
+    from d3d_b200.cli import serve
+    src = tmp_path / "p.jsonl"
+    src.write_text("\n".join(json.dumps({"input_ids": list(range(5 + i, 17 + i))}) for i in range(3)))
+    for backup, extra in (("fast", ["--fast-miss-anchors", "2"]), ("fast_legacy", [])):
+        out = tmp_path / f"{backup}.json"
+        rows = serve.main(["--target", "tiny-target", "--draft", "tiny-drafter", "--device", "cpu",
+                           "--pages", "256", "--concurrency", "2", "--max-new-tokens", "12", "--block-size", "8",
+                           "--anchor-num", "1", "--max-samples", "2", "--prompt-min", "10", "--prompt-max", "20",
+                           "--datasets", "synthetic", str(src), "--repeats", "2", "--backup", backup, *extra,
+                           "--validate", "--ignore-eos", "--output", str(out)])
+        assert [(r["dataset"], r["repeat"]) for r in rows] == [("synthetic", 0), ("synthetic", 1),
+                                                                (str(src), 0), (str(src), 1)]
+        assert all(r["token_identical_to_ar"] for r in rows)
+        d = json.loads(out.read_text())
+        assert d["config"]["backup"] == backup and len(d["rows"]) == 4
+    with pytest.raises(SystemExit):
+        serve.main(["--target", "tiny-target", "--draft", "tiny-drafter", "--device", "cpu", "--repeats", "0"])
+
+
 def test_single_cli_controlled_with_stage_timings(tmp_path):
     """The single-request CLI in controlled mode on the tiny pair (the
     corruption draws stay inside the model's vocabulary) with stage timings."""
