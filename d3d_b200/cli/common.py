@@ -3,7 +3,7 @@ from __future__ import annotations
 
 import argparse
 from pathlib import Path
-from typing import List, Optional
+from typing import List, Optional, Sequence
 
 import torch
 
@@ -11,12 +11,13 @@ from .. import config as C
 from ..utils.data import load_jsonl_prompts, synthetic_prompts
 
 
-def add_model_args(p: argparse.ArgumentParser, target_flag: str, draft_flag: str) -> None:
+def add_model_args(p: argparse.ArgumentParser, target_flag: str, draft_flag: str,
+                   dtypes: Sequence[str] = ("bf16",)) -> None:
     p.add_argument(target_flag, dest="target", required=True,
                    help="target checkpoint directory or preset name")
     p.add_argument(draft_flag, dest="draft", required=True, help="drafter checkpoint directory or preset name")
     p.add_argument("--seed", type=int, default=0)
-    p.add_argument("--dtype", default="bf16", choices=["bf16"])
+    p.add_argument("--dtype", default="bf16", choices=list(dtypes))
     p.add_argument("--device", default="cuda:0" if torch.cuda.is_available() else "cpu")
     p.add_argument("--mask-token-id", type=int, default=None)
     p.add_argument("--draft-layers", type=int, default=None, help="preset drafters only")

@@ -155,6 +155,8 @@ class Linear(nn.Linear):
 
 
 class Attention(nn.Module):
+    impl = "sdpa"   # "sdpa" (torch's fused attention) or "eager" (explicit fp32 softmax)
+
     def __init__(self, cfg: ModelConfig, layer_idx: int):
         super().__init__()
         self.cfg = cfg
@@ -190,8 +192,15 @@ class Attention(nn.Module):
         attn_mask = None
         if mask is not None:
             attn_mask = mask[:, None, :, : ks.shape[2]]
-        out = F.scaled_dot_product_attention(qs, ks, vs, attn_mask=attn_mask,
-                                             scale=1.0 / math.sqrt(d))
+        if self.impl == "eager":
+            sc = torch.matmul(qs.float(), ks.float().transpose(-1, -2)) / math.sqrt(d)
+            if attn_mask is not None:
+                sc = (sc.masked_fill(~attn_mask, float("-inf")) if attn_mask.dtype == torch.bool
+                      else sc + attn_mask.float())
+            out = torch.matmul(torch.softmax(sc, -1), vs.float()).to(vs.dtype)
+        else:
+            out = F.scaled_dot_product_attention(qs, ks, vs, attn_mask=attn_mask,
+                                                 scale=1.0 / math.sqrt(d))
         out = out.transpose(1, 2).reshape(b, q, -1)
         return self.o_proj(out)
 
@@ -249,6 +258,19 @@ class Qwen3LM(nn.Module):
         self.gradient_checkpointing = False
 
     # ------------------------------------------------------------------ init
+    def set_attn_implementation(self, name: Optional[str]) -> str:
+        """Attention math of this module: ``sdpa`` (default) or ``eager``.
+        ``flash_attention_2`` (the Hugging Face name) selects ``sdpa``, whose
+        dispatcher picks the fused flash kernel where the mask allows.
+        Returns the implementation in effect."""
+        impl = {None: "sdpa", "sdpa": "sdpa", "flash_attention_2": "sdpa", "eager": "eager"}.get(name)
+        if impl is None:
+            raise ValueError(f"unknown attention implementation {name!r} (sdpa, eager, flash_attention_2)")
+        for m in self.modules():
+            if isinstance(m, Attention):
+                m.impl = impl
+        return impl
+
     @torch.no_grad()
     def init_weights(self, seed: int = 0, std: Optional[float] = None) -> "Qwen3LM":
         """Seeded N(0, std) init of every linear/embedding; norms at 1."""
