@@ -64,7 +64,7 @@ class D3DEngine:
                                     FastWeights.from_module(draft_m, dev), decode, device=dev, **kw)
         from .engine.backends import TorchDraft, TorchTarget
         decode = decode or DecodeConfig()
-        return cls(TorchTarget(target_m, decode.temperature), TorchDraft(draft_m), decode)
+        return cls(TorchTarget(target_m, decode.temperature, decode.target_top_k, decode.target_top_p), TorchDraft(draft_m), decode)
 
     @classmethod
     def from_pretrained(cls, target_path: str, draft_path: str,

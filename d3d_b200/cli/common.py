@@ -56,6 +56,23 @@ def load_prompts(args) -> List[List[int]]:
     return load_jsonl_prompts(args.dataset, tok, args.max_samples)
 
 
+def load_selected_prompts(args) -> List[List[int]]:
+    """``load_prompts``, restricted to example ``args.sample_index`` when set
+    (an evaluation set's own example index; the position otherwise)."""
+    idx = getattr(args, "sample_index", None)
+    if idx is None:
+        return load_prompts(args)
+    args.max_samples = idx + 1 if args.dataset == "synthetic" else None
+    prompts = load_prompts(args)
+    exs = getattr(args, "eval_examples", None)
+    keep = [i for i in range(len(prompts)) if (exs[i].index if exs else i) == idx][:1]
+    if not keep:
+        raise ValueError(f"--sample-index {idx} not found in {args.dataset}")
+    if exs:
+        args.eval_examples = [exs[i] for i in keep]
+    return [prompts[i] for i in keep]
+
+
 def score_outputs(args, outputs: List[List[int]]) -> Optional[dict]:
     """Exact-answer accuracy of decoded outputs on a scored evaluation set
     (``None`` for other prompt sources); fills ``pred`` / ``correct`` per row."""
@@ -114,8 +131,7 @@ def build_engine(args, decode, max_seqs: int, max_context: int, pages: Optional[
         tw = load_fast_weights(args.target, dev, args.seed)
         dw = load_fast_weights(args.draft, dev, args.seed, args.draft_layers, args.mask_token_id)
         return D3DEngine.from_weights(tw, dw, decode, max_seqs=max_seqs, max_context=max_context,
-                                      target_pages=pages, draft_pages=None if pages is None else None,
-                                      device=dev)
+                                      target_pages=pages, device=dev)
     t = load_module(args.target, dev, args.seed)
     d = load_module(args.draft, dev, args.seed, args.draft_layers, args.mask_token_id)
     return D3DEngine.from_modules(t, d, decode)

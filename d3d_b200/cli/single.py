@@ -8,14 +8,18 @@
 from __future__ import annotations
 
 import argparse
+import json
 import statistics
 import time
 
+import torch
+
 from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
-from ..engine.spec import DecodeConfig
+from ..engine.spec import EOS_DEFAULT, DecodeConfig
 from ..utils.io import write_json
 from ..utils.metrics import headline, source_stats, steps_from_output, summarize_acceptance
-from .common import add_data_args, add_model_args, build_engine, load_prompts, pin_host_threads, score_outputs
+from .common import (add_data_args, add_model_args, build_engine, load_selected_prompts, pin_host_threads,
+                     score_outputs)
 
 
 def parser() -> argparse.ArgumentParser:
@@ -41,7 +45,8 @@ def parser() -> argparse.ArgumentParser:
                         "block's drafts cover commit length 1 only; fast_legacy: every commit length)")
     p.add_argument("--fast-miss-anchors", type=int, default=0,
                    help="fast backup: anchors drafted after a random block (0 = --anchor-num)")
-    p.add_argument("--baseline", action="store_true", help="also run target-only AR decoding")
+    p.add_argument("--baseline", action=argparse.BooleanOptionalAction, default=True,
+                   help="also run target-only AR decoding (on the verifier) and report the speedup")
     p.add_argument("--controlled-accept-mean", type=float, default=None,
                    help="acceptance-controlled mode (needs --baseline's AR oracle)")
     p.add_argument("--warmup-new-tokens", type=int, default=32)
@@ -49,20 +54,82 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--summary-json", default=None)
     p.add_argument("--verifier-cpu-affinity", default=None, help="CPU list, e.g. 0-7 (host threads)")
     p.add_argument("--draft-cpu-affinity", default=None, help="CPU list, e.g. 8-15 (host threads)")
+    p.add_argument("--verifier-device", default=None,
+                   help="target device (default: --device); a different --draft-device runs the target in "
+                        "its own process on its own GPU, linked over NVLink")
+    p.add_argument("--draft-device", default=None, help="drafter device (default: the verifier's)")
+    p.add_argument("--verifier-process", action="store_true",
+                   help="run the target in its own process even on one device (CPU only)")
+    p.add_argument("--model-type", default=None, choices=["d3d"], help="drafter family (D3D drafters only)")
+    p.add_argument("--drafter-tag", default=None, help="label recorded in the summary (default: the drafter)")
+    p.add_argument("--sample-index", type=int, default=None, help="decode only this example of the set")
+    p.add_argument("--draft-tokens", type=int, default=None,
+                   help="drafted tokens per block for the acceptance summary (default: block size - 1)")
+    p.add_argument("--eos-token-id", type=int, action="append", default=None,
+                   help="stop token (repeatable; default: Qwen3's end tokens)")
+    p.add_argument("--verbose", action="store_true", help="print one line per prompt")
+    p.add_argument("--use-kvcache", action="store_true", default=True,
+                   help="accepted for compatibility: the asynchronous engine always keeps paged KV caches")
+    p.add_argument("--denoising-steps", type=int, default=1,
+                   help="must be 1: asynchronous drafting is single-step (as in the reference)")
+    p.add_argument("--remasking-strategy", default="low_confidence", choices=["low_confidence", "dynamic"],
+                   help="no effect with one denoising step (recorded)")
+    p.add_argument("--confidence-threshold", type=float, default=0.9, help="no effect with one denoising step")
+    p.add_argument("--target-attn-implementation", default=None, choices=["sdpa", "eager", "flash_attention_2"],
+                   help="PyTorch backends (CPU) only; the GPU path runs this framework's attention kernels")
+    p.add_argument("--draft-attn-implementation", default=None, choices=["sdpa", "eager", "flash_attention_2"])
     return p
+
+
+def _check(a) -> None:
+    if a.denoising_steps != 1:
+        raise SystemExit("--denoising-steps must be 1: asynchronous drafting denoises in one step "
+                         "(multi-step denoising runs in python -m d3d_b200.cli.sync)")
+    if a.draft_tokens is not None and a.draft_tokens <= 0:
+        raise SystemExit("--draft-tokens must be positive")
+
+
+def _engine(a, decode, max_context):
+    """Co-located engine, or the drafter here and the target in a verifier
+    process when the devices differ (or ``--verifier-process``)."""
+    vdev = torch.device(a.verifier_device or a.device)
+    ddev = torch.device(a.draft_device or vdev)
+    if vdev == ddev and not a.verifier_process:
+        a.device = str(vdev)
+        eng = build_engine(a, decode, max_seqs=2, max_context=max_context)
+        for be, impl in ((eng.target, a.target_attn_implementation), (eng.draft, a.draft_attn_implementation)):
+            if impl is not None and hasattr(be, "model"):
+                be.model.set_attn_implementation(impl)
+        return eng, None
+    if vdev == ddev and vdev.type == "cuda":
+        raise SystemExit("--verifier-process on one GPU is not supported: the two processes' kernels would wait "
+                         "on each other on one device; give --draft-device another GPU")
+    from .pair import VerifierProcess
+    vp = VerifierProcess(a, decode, max_seqs=2, max_context=max_context)
+    return vp.engine, vp
 
 
 def main(argv=None):
     a = parser().parse_args(argv)
+    _check(a)
     pin_host_threads(a.verifier_cpu_affinity, a.draft_cpu_affinity)
     counts = None if a.packed_accepted_counts == "all" else tuple(int(x) for x in a.packed_accepted_counts.split(","))
+    eos = tuple(sorted(set(a.eos_token_id))) if a.eos_token_id else EOS_DEFAULT
     decode = DecodeConfig(block_size=a.block_size, anchor_num=a.anchor_num, attention_mask_mode=a.attention_mask_mode,
                           max_new_tokens=a.max_new_tokens, temperature=a.temperature, top_k=a.proposal_top_k,
                           top_p=a.proposal_top_p, ignore_eos=a.ignore_eos, packed_accepted_counts=counts,
                           target_top_k=a.target_top_k, target_top_p=a.target_top_p, backup=a.backup,
-                          fast_miss_anchors=a.fast_miss_anchors)
-    prompts = load_prompts(a)
-    eng = build_engine(a, decode, max_seqs=2, max_context=max(len(p) for p in prompts) + a.max_new_tokens + 64)
+                          fast_miss_anchors=a.fast_miss_anchors, eos=eos)
+    prompts = load_selected_prompts(a)
+    eng, vp = _engine(a, decode, max(len(p) for p in prompts) + a.max_new_tokens + 64)
+    try:
+        return _run(a, eng, prompts)
+    finally:
+        if vp is not None:
+            vp.close()
+
+
+def _run(a, eng, prompts):
     ar = None
     baseline_tps = None
     if a.baseline or a.controlled_accept_mean is not None:
@@ -80,6 +147,7 @@ def main(argv=None):
         eng.decoder.prof.enabled = True
         eng.decoder.prof.reset()
     per = []
+    draft_tokens = a.draft_tokens if a.draft_tokens is not None else a.block_size - 1
     t0 = time.perf_counter()
     for i, p in enumerate(prompts):
         s0 = time.perf_counter()
@@ -92,9 +160,12 @@ def main(argv=None):
                     "decode_tokens": max(len(o.tokens) - 1, 0), "decode_elapsed_s": dt,
                     "tokens_per_s": max(len(o.tokens) - 1, 0) / dt if dt > 0 else 0.0,
                     "tokens": o.tokens, "hits": o.hits, "recoveries": o.recoveries,
-                    "summary": summarize_acceptance(steps, a.block_size - 1),
+                    "summary": summarize_acceptance(steps, draft_tokens),
                     "sources": source_stats(o.sources, [a.block_size] * len(o.accepts), o.accepts),
                     "matches_ar": (o.tokens == ar["outputs"][i]) if ar else None})
+        if a.verbose:
+            print(json.dumps({"index": i, "output_tokens": len(o.tokens), "decode_elapsed_s": dt,
+                              **per[-1]["summary"]}), flush=True)
     elapsed = time.perf_counter() - t0
     dec = sum(x["decode_tokens"] for x in per)
     dtime = sum(x["decode_elapsed_s"] for x in per)
@@ -102,7 +173,8 @@ def main(argv=None):
     acc = statistics.fmean(s for x in per for s in [x["summary"]["avg_accept_length"]]) if per else 0.0
     summary = {"headline": headline(tps, baseline_tps or 0.0, acc), "elapsed_s": elapsed,
                "token_identical_to_ar": all(x["matches_ar"] for x in per) if ar else None,
-               "config": vars(a)}
+               "drafter_tag": a.drafter_tag or a.draft, "draft_tokens": draft_tokens, "model_type": "d3d",
+               "layout": "verifier_process" if hasattr(eng.target, "links") else "colocated"}
     if a.collect_stage_timings:
         summary["stage_timings"] = eng.decoder.prof.summary()
     scores = score_outputs(a, [x["tokens"] for x in per])

@@ -24,7 +24,7 @@ from ..engine.sync import sync_generate, sync_generate_nocache
 from ..utils.io import write_json
 from ..utils.metrics import AcceptanceStep, step_dicts, summarize_acceptance, summarize_timing
 from ..utils.runtime import resolve_dtype
-from .common import add_data_args, add_model_args, load_module, load_prompts, score_outputs
+from .common import add_data_args, add_model_args, load_module, load_selected_prompts, score_outputs
 
 DTYPES = ("auto", "bf16", "bfloat16", "fp16", "float16", "fp32", "float32")
 
@@ -81,16 +81,6 @@ def _steps(st, n_out: int):
     return out
 
 
-def _select_sample(a, prompts):
-    exs = getattr(a, "eval_examples", None)
-    keep = [i for i in range(len(prompts)) if (exs[i].index if exs else i) == a.sample_index][:1]
-    if not keep:
-        raise ValueError(f"--sample-index {a.sample_index} not found in {a.dataset}")
-    if exs:
-        a.eval_examples = [exs[i] for i in keep]
-    return [prompts[i] for i in keep]
-
-
 def _stop_ids(a):
     if a.eos_token_id:
         return sorted(set(a.eos_token_id))
@@ -119,11 +109,7 @@ def main(argv=None):
         d.to(resolve_dtype(a.dtype))
     attn = {"target": t.set_attn_implementation(a.target_attn_implementation),
             "draft": d.set_attn_implementation(a.draft_attn_implementation)}
-    if a.sample_index is not None:
-        a.max_samples = a.sample_index + 1 if a.dataset == "synthetic" else None
-    prompts = load_prompts(a)
-    if a.sample_index is not None:
-        prompts = _select_sample(a, prompts)
+    prompts = load_selected_prompts(a)
     stop = _stop_ids(a)
     ar = ar_generate(TorchTarget(t), prompts, a.max_new_tokens, eos=tuple(stop)) if a.baseline else None
     run = sync_generate if a.kvcache else sync_generate_nocache

@@ -133,22 +133,28 @@ class P2PTargetServer:
 
     def _verify(self, h) -> list:
         """Run one VERIFY; returns its sequences (in request order)."""
-        B, K = int(h[1]), int(h[2])
+        B, K, S = int(h[1]), int(h[2]), int(h[3])
         meta = self.req[HDR:HDR + 2 * B].view(B, 2).tolist()
-        blocks = self.req[HDR + 2 * B:HDR + 2 * B + B * K].view(B, K).clone()
+        end = HDR + 2 * B + B * K
+        blocks = self.req[HDR + 2 * B:end].view(B, K).clone()
+        q = None
+        if S:       # sampled verify: the drafts' sparse proposal follows the blocks
+            n = B * (K - 1) * S
+            q = (self.req[end:end + n].view(B, K - 1, S).clone(),
+                 self.req[end + n:end + 2 * n].clone().view(torch.float64).view(B, K - 1, S).float())
         group = []
         for sid, prefix in meta:
             s = self.seqs[sid]
             s.prefix = prefix
             group.append(s)
         if self.replies != "all":
-            if self.fused:
+            if self.fused and q is None:
                 self.be.submit_verify(group, blocks, sink=lambda ids, post, xn: None)
             else:
-                self.be.verify(group, blocks)
+                self.be.verify(group, blocks, q)
             return group
-        if not self.fused:
-            r = self.be.verify(group, blocks)
+        if not self.fused or q is not None:
+            r = self.be.verify(group, blocks, q)
             words = _verify_words(B, K)
             ho = hidden_offset(words)
             self.rep_host[:HDR] = 0
@@ -248,10 +254,13 @@ class P2PTargetServer:
             chk = getattr(self.be, "check_tp", None)
             if chk is not None:
                 chk()   # a failed tensor-parallel exchange ends serving loudly
+            words = 0
             if cmd == CMD_PREFILL:
                 words = HDR + 2 * h[1] + h[2]
-                if words > HEAD_WORDS:
-                    self.link.fetch(self.req[HEAD_WORDS:words], 8 * HEAD_WORDS, self.stream)
+            elif cmd == CMD_VERIFY:
+                words = HDR + 2 * h[1] + h[1] * h[2] + 2 * h[1] * (h[2] - 1) * h[3]
+            if words > HEAD_WORDS:
+                self.link.fetch(self.req[HEAD_WORDS:words], 8 * HEAD_WORDS, self.stream)
             if cmd == CMD_CLOSE:
                 return
             try:
@@ -368,18 +377,29 @@ class P2PTarget(TargetBackend):
         the request is ordered after the drafter's work enqueued so far, its
         listed block entries are taken on the device from the drafter's
         output, and the put kernels send it from device memory."""
-        if q is not None:
-            raise NotImplementedError("the disaggregated target verifies greedily (temperature 0)")
         if self._pending is not None:
             raise RuntimeError("target already has an outstanding verify")
         B, K = blocks.shape
         need = HDR + 2 * B + B * K
+        S = 0 if q is None else int(q[0].shape[-1])
+        if S and gather is not None:
+            raise RuntimeError("sampled verifies are sent from the host (no device-assembled request)")
+        total = need + 2 * B * (K - 1) * S
+        if 8 * total > self.link.slot_bytes:
+            raise ValueError(f"verify request of {8 * total} bytes exceeds the {self.link.slot_bytes}-byte slot "
+                             "(raise slot_bytes, or sample drafts from a proposal top-k)")
         self.req[:HDR] = 0
-        self.req[0], self.req[1], self.req[2] = CMD_VERIFY, B, K
+        self.req[0], self.req[1], self.req[2], self.req[3] = CMD_VERIFY, B, K, S
         meta = np.array([[s.index, s.prefix] for s in seqs], dtype=np.int64).reshape(-1)
         rn = self.req.numpy()
         rn[HDR:HDR + 2 * B] = meta
         rn[HDR + 2 * B:need] = blocks.numpy().reshape(-1)
+        if S:
+            # sparse proposal of drafts 1..K-1: support ids, then probabilities as float64 bit patterns
+            n = B * (K - 1) * S
+            rn[need:need + n] = q[0].to(torch.int64).cpu().numpy().reshape(-1)
+            rn[need + n:need + 2 * n] = q[1].to(torch.float64).cpu().numpy().reshape(-1).view(np.int64)
+            need = total
         if gather is None:
             self._send(need)
         else:
@@ -497,13 +517,12 @@ class P2PTarget(TargetBackend):
 
     def close(self) -> None:
         """Ends the server's current ``serve()`` call (it may be called again)."""
-        if True:
-            self.closed = True
-            self.req[:HDR] = 0
-            self.req[0] = CMD_CLOSE
-            self._send(HDR)
-            if self.stream is not None:
-                self.stream.synchronize()
+        self.closed = True
+        self.req[:HDR] = 0
+        self.req[0] = CMD_CLOSE
+        self._send(HDR)
+        if self.stream is not None:
+            self.stream.synchronize()
 
 
 class BatchedTargetServer:
@@ -585,6 +604,8 @@ class BatchedTargetServer:
         for d, h in items:
             sub = self.subs[d]
             B, k = int(h[1]), int(h[2])
+            if int(h[3]):
+                raise NotImplementedError("the batched target verifies greedily (no proposal in the request)")
             if K is not None and k != K:
                 raise ValueError("drafters verify blocks of different sizes in one round")
             K = k

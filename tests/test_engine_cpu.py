@@ -265,6 +265,36 @@ def test_single_cli_controlled_with_stage_timings(tmp_path):
     assert "host_ms" in d["summary"]["stage_timings"]
 
 
+def test_single_cli_verifier_process(tmp_path):
+    """The single-request CLI with the target in its own process (the
+    reference's verifier process; here the ``gloo`` host link on CPU): greedy
+    output is token-identical to AR decoding through the same remote target,
+    and a sampled run sends the drafts' sparse proposals in its requests."""
+    import json
+    from d3d_b200.cli import single
+    base = ["--verifier", "tiny-target", "--drafter", "tiny-drafter", "--device", "cpu", "--verifier-process",
+            "--max-new-tokens", "12", "--block-size", "8", "--anchor-num", "1", "--max-samples", "2",
+            "--prompt-min", "8", "--prompt-max", "16", "--ignore-eos", "--warmup-new-tokens", "4"]
+    out = tmp_path / "pair.json"
+    summ = single.main(base + ["--drafter-tag", "tiny", "--verbose", "--output-json", str(out)])
+    assert summ["layout"] == "verifier_process" and summ["token_identical_to_ar"] is True
+    d = json.loads(out.read_text())
+    assert len(d["per_prompt"]) == 2 and all(len(x["tokens"]) == 12 for x in d["per_prompt"])
+    sampled = ["--no-baseline", "--temperature", "0.8", "--proposal-top-k", "8", "--target-top-k", "20",
+               "--sample-index", "1"]
+    outs = []
+    for extra in (["--verifier-process"], []):
+        out = tmp_path / f"sampled{len(extra)}.json"
+        args = [x for x in base if x != "--verifier-process"] + extra + sampled + ["--output-json", str(out)]
+        summ = single.main(args)
+        assert summ["token_identical_to_ar"] is None
+        outs.append([x["tokens"] for x in json.loads(out.read_text())["per_prompt"]])
+    # same seeds on both sides: the remote target draws exactly what a local one does
+    assert outs[0] == outs[1] and len(outs[0]) == 1
+    with pytest.raises(SystemExit):
+        single.main(base + ["--denoising-steps", "2"])
+
+
 def test_gemm_policies():
     """Token tiles and split-K choices: tiles cover the tokens within the MMA
     limits, and the target's split depends on the weight shape only."""
