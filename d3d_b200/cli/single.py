@@ -68,6 +68,9 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--eos-token-id", type=int, action="append", default=None,
                    help="stop token (repeatable; default: Qwen3's end tokens)")
     p.add_argument("--verbose", action="store_true", help="print one line per prompt")
+    p.add_argument("--async-blocks", type=int, default=1,
+                   help="block-size chunks drafted per packed outcome; this engine drafts one (the reference's "
+                        "default)")
     p.add_argument("--use-kvcache", action="store_true", default=True,
                    help="accepted for compatibility: the asynchronous engine always keeps paged KV caches")
     p.add_argument("--denoising-steps", type=int, default=1,
@@ -85,6 +88,8 @@ def _check(a) -> None:
     if a.denoising_steps != 1:
         raise SystemExit("--denoising-steps must be 1: asynchronous drafting denoises in one step "
                          "(multi-step denoising runs in python -m d3d_b200.cli.sync)")
+    if a.async_blocks != 1:
+        raise SystemExit("--async-blocks: only 1 is supported (each packed outcome drafts one block)")
     if a.draft_tokens is not None and a.draft_tokens <= 0:
         raise SystemExit("--draft-tokens must be positive")
 

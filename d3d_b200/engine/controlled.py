@@ -31,12 +31,15 @@ import torch
 _M = (1 << 61) - 1
 
 
-def _mix(x: int) -> int:
-    # splitmix64, written out from its published definition
+def splitmix64(x: int) -> int:
+    """splitmix64's output function, written out from its published definition."""
     x = (x + 0x9E3779B97F4A7C15) & 0xFFFFFFFFFFFFFFFF
     x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & 0xFFFFFFFFFFFFFFFF
     x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & 0xFFFFFFFFFFFFFFFF
     return x ^ (x >> 31)
+
+
+_mix = splitmix64
 
 
 def uniform(seed: int, stream: int, pos: int) -> float:

@@ -3,7 +3,9 @@
 Rewrites a checkpoint without one decoder layer: tensors
 ``model.layers.N.*`` are renamed to their new compact index, the config's
 ``num_hidden_layers`` is decremented, and ``layer_prune.json`` records the
-provenance (parent, removed layer, original indices of retained layers).
+provenance (original teacher and depth, parent, removed layer, original
+indices of retained layers; the reference's ``layer_prune.json`` fields, so
+checkpoints pruned by either implementation feed the other's later stages).
 The output is built in a temporary directory and renamed into place; an
 existing output is never overwritten.
 """
@@ -35,20 +37,30 @@ def renamed_key(name: str, old_to_new: Dict[int, int]) -> Optional[str]:
     return f"model.layers.{old_to_new[old]}.{m.group(2)}"
 
 
+# files of a parent that describe the parent itself, not the child
+_NOT_COPIED = {"config.json", "model.safetensors.index.json", "layer_prune.json", "recovery_info.json",
+               "layer_schedule.json", "checkpoint_validation.json"}
+
+
 def prune_checkpoint(parent: str | Path, output: str | Path, removed: int,
-                     retained_original: Optional[Sequence[int]] = None) -> Path:
-    parent, output = Path(parent), Path(output)
+                     retained_original: Optional[Sequence[int]] = None, *, block_size: int = 16,
+                     mask_token_id: Optional[int] = None, selection_file: Optional[str] = None) -> Path:
+    """Write ``parent`` without compact layer ``removed`` to ``output`` and
+    record the provenance the later stages read: the original teacher and
+    depth, the parent and child depths, the removed layer in parent and
+    original numbering, the retained layers in both numberings, the block
+    size and the parameter count."""
+    from .common import provenance
+    parent, output = Path(parent).resolve(), Path(output).resolve()
     if output.exists():
         raise FileExistsError(f"Refusing to overwrite {output}")
-    cfg = ModelConfig.from_pretrained(parent)
+    cfg = ModelConfig.from_pretrained(parent, mask_token_id=mask_token_id)
     depth = cfg.num_hidden_layers
     if not 0 <= removed < depth:
         raise ValueError(f"removed layer {removed} outside [0, {depth})")
+    teacher, original_depth, parent_orig = provenance(parent)
     keep = [i for i in range(depth) if i != removed]
     old_to_new = {old: new for new, old in enumerate(keep)}
-    prov_path = parent / "layer_prune.json"
-    parent_orig = (json.loads(prov_path.read_text())["retained_original_layers"]
-                   if prov_path.exists() else list(range(depth)))
     retained_original = list(retained_original) if retained_original is not None else \
         [parent_orig[i] for i in keep]
     if len(retained_original) != depth - 1:
@@ -64,14 +76,21 @@ def prune_checkpoint(parent: str | Path, output: str | Path, removed: int,
                 new_state[nk] = v
         write_state(new_state, tmp)
         for f in parent.iterdir():
-            if f.suffix in (".json", ".txt", ".model", ".py") and f.name not in (
-                    "config.json", "model.safetensors.index.json", "layer_prune.json"):
+            if (f.is_file() and f.name not in _NOT_COPIED and f.suffix != ".safetensors"
+                    and not f.name.startswith(("compact_model_", "progressive_checkpoint_", "recovery_checkpoint_"))):
                 shutil.copy2(f, tmp / f.name)
-        cfg.replace(num_hidden_layers=depth - 1).save(tmp)
+        child = cfg.replace(num_hidden_layers=depth - 1)
+        if "max_window_layers" in child.extra:
+            child.extra["max_window_layers"] = min(int(child.extra["max_window_layers"]), depth - 1)
+        child.save(tmp)
         (tmp / "layer_prune.json").write_text(json.dumps({
-            "parent_checkpoint": str(parent), "parent_depth": depth, "child_depth": depth - 1,
-            "removed_compact_layer": removed, "removed_original_layer": parent_orig[removed],
-            "retained_original_layers": retained_original}, indent=2))
+            "format_version": 1, "method": "progressive_single_layer_pruning",
+            "parent_checkpoint": str(parent), "teacher_checkpoint": str(teacher), "original_depth": original_depth,
+            "parent_depth": depth, "child_depth": depth - 1, "removed_parent_layer": removed,
+            "removed_original_layer": parent_orig[removed], "retained_parent_layers": keep,
+            "retained_original_layers": retained_original, "block_size": int(block_size),
+            "selection_file": selection_file, "parameters": int(sum(v.numel() for v in new_state.values()))},
+            indent=2, sort_keys=True))
         os.replace(tmp, output)
     except BaseException:
         shutil.rmtree(tmp, ignore_errors=True)
@@ -80,12 +99,19 @@ def prune_checkpoint(parent: str | Path, output: str | Path, removed: int,
 
 
 def prune_from_selection(selection: str | Path, output: str | Path) -> Path:
-    sel = json.loads(Path(selection).read_text())
+    """Carry out a ``selection.json`` (``pruning/prune.py:114-178``)."""
+    selection = Path(selection).resolve()
+    sel = json.loads(selection.read_text())
     parent = Path(sel["parent_checkpoint"])
-    if ModelConfig.from_pretrained(parent).num_hidden_layers != int(sel["parent_depth"]):
+    depth = int(sel["parent_depth"])
+    removed = int(sel["removed_compact_layer"])
+    if ModelConfig.from_pretrained(parent).num_hidden_layers != depth:
         raise ValueError("The selected parent no longer has the recorded depth")
-    return prune_checkpoint(parent, output, int(sel["removed_compact_layer"]),
-                            sel.get("child_retained_original_layers"))
+    if int(sel.get("child_depth", depth - 1)) != depth - 1 or not 0 <= removed < depth:
+        raise ValueError("selection.json does not describe one valid layer removal")
+    return prune_checkpoint(parent, output, removed, sel.get("child_retained_original_layers"),
+                            block_size=int(sel.get("block_size", 16)), mask_token_id=sel.get("mask_token_id"),
+                            selection_file=str(selection))
 
 
 def drop_layers_inplace(model, compact_indices: Sequence[int]) -> None:

@@ -55,22 +55,27 @@ class PackedTrainBatch:
         return PackedTrainBatch(**kw)
 
 
-def select_anchor_starts(response_len: int, max_anchors: int, rng: random.Random) -> List[int]:
-    starts = list(range(0, max(int(response_len) - 1, 0)))
+def select_anchor_starts(response_len: int, max_anchors: int, rng: random.Random,
+                         full_block: int = 0) -> List[int]:
+    """Response offsets of the anchors: every offset that leaves at least one
+    target token (or, with ``full_block=K``, a whole block of K-1 targets),
+    ``max_anchors`` of them drawn from ``rng`` when there are more."""
+    last = int(response_len) - (full_block - 1 if full_block else 1)
+    starts = list(range(0, max(last, 0)))
     if max_anchors > 0 and len(starts) > max_anchors:
         starts = sorted(rng.sample(starts, max_anchors))
     return starts
 
 
 def build_packed_block_batch(examples: Sequence[Example], *, block_size: int, mask_token_id: int,
-                             max_anchors: int, rng: Optional[random.Random] = None
+                             max_anchors: int, rng: Optional[random.Random] = None, full_blocks: bool = False
                              ) -> Optional[PackedTrainBatch]:
     if max_anchors <= 0:
         raise ValueError("max_anchors must be > 0")
     rng = rng or random.Random(0)
     prepared = []
     for ex in examples:
-        starts = select_anchor_starts(len(ex.response_ids), max_anchors, rng)
+        starts = select_anchor_starts(len(ex.response_ids), max_anchors, rng, block_size if full_blocks else 0)
         if starts:
             prepared.append((list(ex.prompt_ids), list(ex.response_ids), starts))
     if not prepared:
