@@ -13,6 +13,8 @@ Shapes: ``[B, NB, K, ...]`` -- sequences x blocks x block rows.
 """
 from __future__ import annotations
 
+from typing import Optional
+
 import torch
 import torch.nn.functional as F
 
@@ -37,13 +39,34 @@ def relation(h: torch.Tensor) -> torch.Tensor:
     return u @ u.transpose(-1, -2)
 
 
+def shuffle_among_equal_length(rt: torch.Tensor, selected: torch.Tensor, active_len: torch.Tensor,
+                               gen: torch.Generator) -> torch.Tensor:
+    """Teacher relation matrices permuted among the selected blocks that have
+    the same number of valid rows (the reference's negative control: the
+    targets keep their shape statistics but lose their pairing)."""
+    k = rt.shape[-1]
+    flat = rt.reshape(-1, k, k)
+    sel = selected.reshape(-1).bool()
+    ln = active_len.reshape(-1)
+    out = flat.clone()
+    for length in torch.unique(ln[sel]).tolist():
+        idx = torch.nonzero(sel & (ln == length), as_tuple=True)[0]
+        perm = torch.randperm(len(idx), generator=gen).to(idx.device)
+        out[idx] = flat[idx[perm]]
+    return out.view_as(rt)
+
+
 def relational_loss(student_h: torch.Tensor, teacher_h: torch.Tensor, valid: torch.Tensor,
-                    selected: torch.Tensor):
+                    selected: torch.Tensor, shuffle: Optional[torch.Generator] = None):
     """Sum over selected blocks of the mean SmoothL1 between the student's and
     the (detached) teacher's relation matrices over off-diagonal valid pairs.
-    Returns ``(loss_sum, selected_count)``; divide by the global count."""
+    Returns ``(loss_sum, selected_count)``; divide by the global count.
+    ``shuffle``: permute the teacher targets among selected blocks of equal
+    active length first (:func:`shuffle_among_equal_length`)."""
     rs = relation(student_h)
     rt = relation(teacher_h.detach())
+    if shuffle is not None:
+        rt = shuffle_among_equal_length(rt, selected, valid.sum(-1), shuffle)
     k = rs.shape[-1]
     pair = valid.unsqueeze(-1) & valid.unsqueeze(-2) & ~torch.eye(k, dtype=torch.bool, device=rs.device)
     per_pair = F.smooth_l1_loss(rs, rt, reduction="none") * pair

@@ -61,7 +61,8 @@ def test_trainer_step_bf16_gpu(tmp_path):
     a = parser().parse_args(["--draft-model", "tiny-drafter", "--target-model", "tiny-target",
                              "--output-dir", str(tmp_path), "--seq-len", "256", "--batch-size", "2",
                              "--parallel-anchors-per-example", "8", "--max-steps", "3", "--block-size", "8",
-                             "--vocab-chunk", "512", "--device", "cuda"])
+                             "--vocab-chunk", "512", "--device", "cuda", "--objective", "kl_ce",
+                             "--warmup-steps", "0", "--lr", "1e-4"])
     r = train(a)
     losses = [x["loss"] for x in r["log"]]
     assert all(torch.isfinite(torch.tensor(l)) for l in losses)
