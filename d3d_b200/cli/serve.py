@@ -46,6 +46,9 @@ def parser():
     p.add_argument("--validate", action="store_true", help="check token identity against AR decoding")
     p.add_argument("--validate-hf", action="store_true",
                    help="compare the outputs with transformers' greedy generate on the target checkpoint")
+    p.add_argument("--validate-draft", action="store_true",
+                   help="compare the engine's drafter with the PyTorch drafter module on the first prompt "
+                        "(recovery block equal, packed drafts >= 99%% equal)")
     p.add_argument("--baseline", action="store_true", help="AR baseline at each concurrency")
     p.add_argument("--controlled-accept-mean", type=float, default=None)
     p.add_argument("--output-json", "--output", dest="output_json", default=None)
@@ -90,6 +93,19 @@ def main(argv=None):
                           fast_miss_anchors=a.fast_miss_anchors)
     eng = build_engine(a, decode, max_seqs=max(conc), max_context=max(lens) + a.max_new_tokens + 64, pages=a.pages)
     rows, warm = [], False
+    draft_check = None
+    if a.validate_draft:
+        import torch
+        from ..engine.validation import validate_draft
+        from .common import load_module
+        dev = torch.device(a.device)
+        oracle = load_module(a.draft, dev, a.seed, a.draft_layers, a.mask_token_id).eval()
+        if dev.type == "cuda":
+            oracle = oracle.to(torch.bfloat16)
+        first = next(iter(sets.values()))["prompts"][0]
+        draft_check = validate_draft(eng.decoder, oracle, first)
+        del oracle
+        print({k: v for k, v in draft_check.items() if k != "differences"}, flush=True)
     for name, d in sets.items():
         prompts, bud = d["prompts"], budgets.get(name)
         for k, v in d["eval"].items():
@@ -137,7 +153,8 @@ def main(argv=None):
                 rows.append(row)
                 print(row, flush=True)
     write_json(a.output_json, {"rows": rows, "config": {k: v for k, v in vars(a).items() if not k.startswith("eval_")},
-                               "eval_sets": {n: d["eval"].get("eval_meta") for n, d in sets.items()}})
+                               "eval_sets": {n: d["eval"].get("eval_meta") for n, d in sets.items()},
+                               "draft_validation": draft_check})
     return rows
 
 

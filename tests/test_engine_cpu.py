@@ -239,12 +239,13 @@ def test_serve_cli_datasets_repeats_and_fast_backup(tmp_path):
                            "--pages", "256", "--concurrency", "2", "--max-new-tokens", "12", "--block-size", "8",
                            "--anchor-num", "1", "--max-samples", "2", "--prompt-min", "10", "--prompt-max", "20",
                            "--datasets", "synthetic", str(src), "--repeats", "2", "--backup", backup, *extra,
-                           "--validate", "--ignore-eos", "--output", str(out)])
+                           "--validate", "--validate-draft", "--ignore-eos", "--output", str(out)])
         assert [(r["dataset"], r["repeat"]) for r in rows] == [("synthetic", 0), ("synthetic", 1),
                                                                 (str(src), 0), (str(src), 1)]
         assert all(r["token_identical_to_ar"] for r in rows)
         d = json.loads(out.read_text())
         assert d["config"]["backup"] == backup and len(d["rows"]) == 4
+        assert d["draft_validation"]["agreement"] == 1.0
     with pytest.raises(SystemExit):
         serve.main(["--target", "tiny-target", "--draft", "tiny-drafter", "--device", "cpu", "--repeats", "0"])
 
@@ -384,3 +385,22 @@ def test_call_budget_does_not_change_the_engine_default(pair):
     prompts = _prompts(n=1, seed=9)
     assert len(eng.generate(prompts, max_new_tokens=5)["outputs"][0].tokens) == 5
     assert len(eng.generate(prompts)["outputs"][0].tokens) == 20
+
+
+def test_draft_validation_against_oracle_module():
+    """The engine's drafter agrees with its own oracle module exactly; a
+    perturbed oracle is reported (recovery block or packed tokens differ)."""
+    import copy
+    from d3d_b200.engine.validation import validate_draft
+    tgt = TorchTarget(build_model(tiny_target(), seed=0))
+    dm = build_model(tiny_drafter(cond=True), seed=1)
+    dec = SpecDecoder(tgt, TorchDraft(dm), DecodeConfig(block_size=8, anchor_num=2, max_new_tokens=16))
+    prompt = list(range(30, 60))
+    r = validate_draft(dec, copy.deepcopy(dm), prompt)
+    assert r["recovery_equal"] and r["agreement"] == 1.0 and r["candidate_keys"] > 8
+    bad = copy.deepcopy(dm)
+    with torch.no_grad():
+        for p in bad.model.layers[-1].parameters():
+            p.add_(torch.randn_like(p) * 0.5)
+    with pytest.raises(RuntimeError, match="differs materially"):
+        validate_draft(dec, bad, prompt)
