@@ -203,6 +203,11 @@ class TorchTarget(TargetBackend):
     def release(self, seq):
         self.kv.release(seq)
 
+    def leak_check(self) -> None:
+        """Raise if a sequence still holds a KV cache after a finished run."""
+        if self.kv.caches:
+            raise RuntimeError(f"KV caches leaked: {len(self.kv.caches)} sequences still allocated")
+
 
 class TorchDraft(DraftBackend):
     """Drafter forwards in PyTorch with dense masks (``models/d3d/modeling_d3d.py``)."""

@@ -535,17 +535,30 @@ class SpecDecoder:
 
 def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new_tokens: int,
                 eos: Tuple[int, ...] = EOS_DEFAULT, ignore_eos: bool = False,
-                concurrency: int = 1, max_new: Optional[Sequence[int]] = None) -> dict:
+                concurrency: int = 1, max_new: Optional[Sequence[int]] = None, prefill_group: int = 4) -> dict:
     """Target-only autoregressive decoding through the same verify path
     (``single/eval_async_packed.py:1489-1535``; ``serving/baseline_ar.py``,
     ``serving/baseline_concurrency.py``): up to ``concurrency`` requests in
     flight, a finished request's place refilled at once (closed loop, like
-    :meth:`SpecDecoder.generate`).  ``max_new``: per-request budgets."""
+    :meth:`SpecDecoder.generate`), admitted requests prefilled in groups of
+    ``prefill_group`` as the speculative engine does.  ``max_new``:
+    per-request budgets.  Besides the outputs: per-request latency (admission
+    to completion) and finish reason, the largest number in flight and every
+    decode step's batch size."""
     started = time.perf_counter()
     waiting = iter(enumerate(prompts))
     exhausted = False
     results: Dict[int, List[int]] = {}
+    latency: Dict[int, float] = {}
+    reason: Dict[int, str] = {}
     live: List[SeqState] = []
+    max_active, batches = 0, []
+
+    def finish(s: SeqState, toks: List[int], why: str) -> None:
+        results[s.index] = toks
+        latency[s.index] = time.perf_counter() - s.born
+        reason[s.index] = why
+        target.release(s)
 
     def budget(i: int) -> int:
         return int(max_new[i]) if max_new is not None else int(max_new_tokens)
@@ -558,19 +571,24 @@ def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new
             except StopIteration:
                 exhausted = True
                 break
-            new.append(SeqState(index=i, prompt=[int(t) for t in p], prefix=len(p), budget=budget(i)))
-        if new:
-            anchors, _ = target.prefill(new)
-            for s, a in zip(new, anchors.tolist()):
+            new.append(SeqState(index=i, prompt=[int(t) for t in p], prefix=len(p), budget=budget(i),
+                                born=time.perf_counter()))
+        max_active = max(max_active, len(live) + len(new))
+        for off in range(0, len(new), max(1, prefill_group)):
+            group = new[off:off + max(1, prefill_group)]
+            anchors, _ = target.prefill(group)
+            for s, a in zip(group, anchors.tolist()):
                 s.anchor = int(a)
                 s.generated = [s.anchor]
-                if (not ignore_eos and s.anchor in eos) or s.budget <= 1:
-                    results[s.index] = s.generated[:s.budget]
-                    target.release(s)
+                if not ignore_eos and s.anchor in eos:
+                    finish(s, s.generated[:s.budget], "eos")
+                elif s.budget <= 1:
+                    finish(s, s.generated[:s.budget], "length")
                 else:
                     live.append(s)
         if not live:
             continue
+        batches.append(len(live))
         blocks = torch.tensor([[s.anchor] for s in live], dtype=torch.long)
         res = target.verify(live, blocks)
         nxt = []
@@ -578,14 +596,23 @@ def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new
             s.prefix += 1
             s.anchor = int(res.correction[i])
             s.generated.append(s.anchor)
-            if (not ignore_eos and s.anchor in eos) or len(s.generated) >= s.budget:
-                results[s.index] = s.generated
-                target.release(s)
+            if not ignore_eos and s.anchor in eos:
+                finish(s, s.generated, "eos")
+            elif len(s.generated) >= s.budget:
+                finish(s, s.generated, "length")
             else:
                 nxt.append(s)
         live = nxt
     elapsed = time.perf_counter() - started
     outs = [results[i] for i in range(len(prompts))]
     total = sum(len(o) for o in outs)
+    lat = sorted(latency.values())
+    n = len(outs)
     return dict(outputs=outs, elapsed_s=elapsed, output_tokens=total,
-                tps=total / elapsed if elapsed > 0 else 0.0)
+                tps=total / elapsed if elapsed > 0 else 0.0, requests=n, max_active=max_active,
+                decode_batch_sizes=batches, latency_s=[latency[i] for i in range(n)],
+                finish_reasons=[reason[i] for i in range(n)],
+                latency_p50_s=lat[len(lat) // 2] if lat else 0.0,
+                latency_p95_s=lat[min(len(lat) - 1, int(0.95 * len(lat)))] if lat else 0.0,
+                length_limit_fraction=sum(r == "length" for r in reason.values()) / max(1, n),
+                mean_output_tokens=total / max(1, n))

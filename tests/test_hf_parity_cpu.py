@@ -38,3 +38,31 @@ def test_serve_cli_validates_against_transformers(tmp_path):
                        "--validate-hf"])
     hf = rows[0]["hf_greedy"]
     assert hf["identical"] == hf["requests"] == 2 and hf["first_divergence"] == [None, None]
+
+
+def test_ar_baseline_cli_validation_retests_and_records(tmp_path):
+    """The AR baseline CLI: transformers validation passes, every attempt is
+    recorded with telemetry, a strict slow fraction forces the retest, and
+    the summary and table cover each concurrency."""
+    import json
+    from d3d_b200.cli import baseline
+    save_model(build_model(tiny_target(), seed=0), tmp_path / "t")
+    out = baseline.main(["--target", str(tmp_path / "t"), "--device", "cpu", "--datasets", "synthetic",
+                         "--concurrency", "1", "2", "--max-new-tokens", "6", "--warmup-new-tokens", "2",
+                         "--max-samples", "3", "--prompt-min", "8", "--prompt-max", "14", "--ignore-eos",
+                         "--repeats", "2", "--max-retests", "1", "--slow-fraction", "0.999999",
+                         "--pages", "64", "--run-id", "r1", "--output-root", str(tmp_path / "res")])
+    d = tmp_path / "res" / "synthetic" / "r1"
+    bench = json.loads((d / "benchmark.json").read_text())
+    assert bench["status"] == "complete" and bench["validation"] == "passed"
+    assert all(c["equal"] for c in json.loads((d / "validation.json").read_text()))
+    for c in ("1", "2"):
+        s = bench["summary"][c]
+        assert s["attempts"] in (2, 3) and s["min_tps"] <= s["median_tps"] <= s["max_tps"]
+    raw = json.loads((d / "c2_attempt0.json").read_text())
+    assert raw["max_active"] <= 2 and len(raw["outputs"]) == 3 and all(len(o) == 6 for o in raw["outputs"])
+    assert raw["length_limit_fraction"] == 1.0 and "telemetry_before" in raw
+    assert "| 2 |" in (d / "table.md").read_text()
+    assert out["synthetic"]["requests"] == 3
+    assert baseline.slow_attempts([{"attempt": 0, "tps": 10.0}, {"attempt": 1, "tps": 5.0}], 0.85) == [1]
+    assert baseline.slow_attempts([{"attempt": i, "tps": t} for i, t in enumerate((10.0, 9.0, 2.0))], 0.85) == [2]
