@@ -242,6 +242,32 @@ def _wandb_run(args, rank: int):
                       config={k: v for k, v in vars(args).items() if isinstance(v, (int, float, str, bool))})
 
 
+class _TensorBoard:
+    """Scalars of every step record under ``<output>/tensorboard`` (rank 0,
+    when TensorBoard is installed), as the reference's writer does."""
+
+    def __init__(self, log_dir: Path, rank: int):
+        self.w = None
+        if rank != 0:
+            return
+        try:
+            from torch.utils.tensorboard import SummaryWriter
+        except ImportError:
+            return
+        self.w = SummaryWriter(log_dir=str(log_dir))
+
+    def log(self, rec: dict, step: int) -> None:
+        if self.w is None:
+            return
+        for k, v in rec.items():
+            if isinstance(v, (int, float)) and not isinstance(v, bool) and v is not None and k != "step":
+                self.w.add_scalar(f"train/{k}", float(v), step)
+
+    def close(self) -> None:
+        if self.w is not None:
+            self.w.close()
+
+
 def train(args) -> dict:
     device = torch.device(args.device)
     rank, world = _init_dist(device.type)
@@ -326,6 +352,7 @@ def train(args) -> dict:
     if rank == 0:
         out_dir.mkdir(parents=True, exist_ok=True)
     run = _wandb_run(args, rank)
+    tb = _TensorBoard(out_dir / "tensorboard", rank)
     a_kl = args.kl_weight if (teacher is not None and objective in ("forward_kl", "kl_ce")) else 0.0
     a_rkl = args.kl_weight if (teacher is not None and objective == "reverse_kl") else 0.0
     a_ce = args.ce_weight if objective in ("ce", "kl_ce") else 0.0
@@ -439,6 +466,7 @@ def train(args) -> dict:
                 f.write(json.dumps(rec) + "\n")
             if run is not None:
                 run.log(rec, step=step + 1)
+            tb.log(rec, step + 1)
             if args.log_every and (step + 1) % args.log_every == 0:
                 print(json.dumps(rec), flush=True)
         if args.save_every and (step + 1) % args.save_every == 0:
@@ -448,6 +476,7 @@ def train(args) -> dict:
     prefetch.close()
     if run is not None:
         run.finish()
+    tb.close()
     if z3 is not None:
         z3.close()
     return {"log": log, "elapsed_s": time.perf_counter() - t_start, "world": world, "steps": total}

@@ -83,6 +83,7 @@ def test_schedule_from_epochs_micro_steps_and_accumulation(tmp_path):
     assert r["steps"] == 4 and len(r["log"]) == 4                  # 2 x 6 micro-steps / 3
     r = _run(tmp_path, "cap", ["--data-path", d, "--epochs", "2", "--max-micro-steps", "5"])
     assert r["steps"] == 5
+    assert any((tmp_path / "cap" / "tensorboard").glob("events.out.tfevents.*"))
     r = _run(tmp_path, "acc", ["--data-path", d, "--max-steps", "2", "--gradient-accumulation-steps", "2",
                                "--save-final"])
     st = json.loads(next((tmp_path / "acc").glob("step_*/trainer_state.json")).read_text())
