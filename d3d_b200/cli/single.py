@@ -138,9 +138,10 @@ def _run(a, eng, prompts):
     ar = None
     baseline_tps = None
     if a.baseline or a.controlled_accept_mean is not None:
-        t0 = time.perf_counter()
         ar = eng.generate_ar(prompts)
-        baseline_tps = ar["output_tokens"] / (time.perf_counter() - t0)
+        # decode-only, as the single-request metric: the prefill and its first token excluded
+        dec_t = sum(ar["decode_s"])
+        baseline_tps = sum(max(len(o) - 1, 0) for o in ar["outputs"]) / dec_t if dec_t > 0 else 0.0
     ctl = None
     if a.controlled_accept_mean is not None:
         rate = rate_for_mean_accept(a.controlled_accept_mean, a.block_size)
@@ -159,10 +160,11 @@ def _run(a, eng, prompts):
         r = eng.generate([p], max_new_tokens=a.max_new_tokens,
                          controlled=(lambda j, i=i: ctl(i)) if ctl else None)
         o = r["outputs"][0]
-        dt = time.perf_counter() - s0
+        wall = time.perf_counter() - s0
+        dt = o.decode_s             # after the prefill (which emits the first token) to the last token
         steps = steps_from_output(o.accepts, a.block_size, o.tokens)
         per.append({"index": i, "input_tokens": len(p), "output_tokens": len(o.tokens),
-                    "decode_tokens": max(len(o.tokens) - 1, 0), "decode_elapsed_s": dt,
+                    "decode_tokens": max(len(o.tokens) - 1, 0), "decode_elapsed_s": dt, "wall_s": wall,
                     "tokens_per_s": max(len(o.tokens) - 1, 0) / dt if dt > 0 else 0.0,
                     "tokens": o.tokens, "hits": o.hits, "recoveries": o.recoveries,
                     "summary": summarize_acceptance(steps, draft_tokens),

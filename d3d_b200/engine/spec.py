@@ -78,7 +78,8 @@ class RequestOutput:
     sources: List[str]
     hits: int
     recoveries: int
-    latency_s: float
+    latency_s: float            # admission to completion
+    decode_s: float = 0.0       # after the request's prefill to completion (the single-request metric)
 
 
 class _Outcomes:
@@ -374,8 +375,10 @@ class SpecDecoder:
                 group = admitted[off:off + cfg.prefill_group]
                 anchors, hidden = self.t.prefill(group)
                 self.d.prefill(group, cfg.attention_mask_mode, k)
+                t_decode = time.perf_counter()
                 ready = []
                 for i, s in enumerate(group):
+                    s.extra["t_decode"] = t_decode
                     s.anchor = int(anchors[i])
                     s.cond = None if hidden is None or not cfg.use_cond else hidden[i]
                     if not cfg.ignore_eos and s.anchor in cfg.eos:
@@ -526,9 +529,10 @@ class SpecDecoder:
                     decode_batch_sizes=batch_sizes)
 
     def _finish(self, s: SeqState, outputs: List[RequestOutput]) -> None:
+        now = time.perf_counter()
         outputs.append(RequestOutput(s.index, list(s.generated), list(s.accepts),
-                                     list(s.sources), s.hits, s.recoveries,
-                                     time.perf_counter() - s.born))
+                                     list(s.sources), s.hits, s.recoveries, now - s.born,
+                                     now - s.extra.get("t_decode", now)))
         self.t.release(s)
         self.d.release(s)
 
@@ -554,9 +558,13 @@ def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new
     live: List[SeqState] = []
     max_active, batches = 0, []
 
+    decode: Dict[int, float] = {}
+
     def finish(s: SeqState, toks: List[int], why: str) -> None:
         results[s.index] = toks
-        latency[s.index] = time.perf_counter() - s.born
+        now = time.perf_counter()
+        latency[s.index] = now - s.born
+        decode[s.index] = now - s.extra.get("t_decode", now)
         reason[s.index] = why
         target.release(s)
 
@@ -577,7 +585,9 @@ def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new
         for off in range(0, len(new), max(1, prefill_group)):
             group = new[off:off + max(1, prefill_group)]
             anchors, _ = target.prefill(group)
+            t_decode = time.perf_counter()
             for s, a in zip(group, anchors.tolist()):
+                s.extra["t_decode"] = t_decode
                 s.anchor = int(a)
                 s.generated = [s.anchor]
                 if not ignore_eos and s.anchor in eos:
@@ -611,6 +621,7 @@ def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new
     return dict(outputs=outs, elapsed_s=elapsed, output_tokens=total,
                 tps=total / elapsed if elapsed > 0 else 0.0, requests=n, max_active=max_active,
                 decode_batch_sizes=batches, latency_s=[latency[i] for i in range(n)],
+                decode_s=[decode[i] for i in range(n)],
                 finish_reasons=[reason[i] for i in range(n)],
                 latency_p50_s=lat[len(lat) // 2] if lat else 0.0,
                 latency_p95_s=lat[min(len(lat) - 1, int(0.95 * len(lat)))] if lat else 0.0,
