@@ -152,7 +152,7 @@ def _run(a, eng, prompts):
     if a.collect_stage_timings:
         eng.decoder.prof.enabled = True
         eng.decoder.prof.reset()
-    per = []
+    per, outs = [], []
     draft_tokens = a.draft_tokens if a.draft_tokens is not None else a.block_size - 1
     t0 = time.perf_counter()
     for i, p in enumerate(prompts):
@@ -160,6 +160,7 @@ def _run(a, eng, prompts):
         r = eng.generate([p], max_new_tokens=a.max_new_tokens,
                          controlled=(lambda j, i=i: ctl(i)) if ctl else None)
         o = r["outputs"][0]
+        outs.append(o)
         wall = time.perf_counter() - s0
         dt = o.decode_s             # after the prefill (which emits the first token) to the last token
         steps = steps_from_output(o.accepts, a.block_size, o.tokens)
@@ -182,6 +183,15 @@ def _run(a, eng, prompts):
                "token_identical_to_ar": all(x["matches_ar"] for x in per) if ar else None,
                "drafter_tag": a.drafter_tag or a.draft, "draft_tokens": draft_tokens, "model_type": "d3d",
                "layout": "verifier_process" if hasattr(eng.target, "links") else "colocated"}
+    hits = sum(x["hits"] for x in per)
+    recov = sum(x["recoveries"] for x in per)
+    verifies = sum(x["summary"]["num_verify_steps"] for x in per)
+    all_src = [src for o in outs for src in o.sources]
+    all_acc = [n for o in outs for n in o.accepts]
+    summary["async"] = {"verify_steps": verifies, "packed_outcome_hits": hits, "redraft_steps": recov,
+                        "packed_hit_rate": hits / max(1, hits + recov),
+                        "all_pass_steps": sum(1 for n in all_acc if n == a.block_size),
+                        "sources": source_stats(all_src, [a.block_size] * len(all_acc), all_acc)}
     if a.collect_stage_timings:
         summary["stage_timings"] = eng.decoder.prof.summary()
     scores = score_outputs(a, [x["tokens"] for x in per])

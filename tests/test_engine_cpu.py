@@ -279,6 +279,7 @@ def test_single_cli_verifier_process(tmp_path):
     out = tmp_path / "pair.json"
     summ = single.main(base + ["--drafter-tag", "tiny", "--verbose", "--output-json", str(out)])
     assert summ["layout"] == "verifier_process" and summ["token_identical_to_ar"] is True
+    assert summ["async"]["verify_steps"] == sum(v["count"] for v in summ["async"]["sources"].values())
     d = json.loads(out.read_text())
     assert len(d["per_prompt"]) == 2 and all(len(x["tokens"]) == 12 for x in d["per_prompt"])
     sampled = ["--no-baseline", "--temperature", "0.8", "--proposal-top-k", "8", "--target-top-k", "20",
