@@ -8,6 +8,7 @@
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import statistics
 import time
@@ -78,9 +79,11 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--remasking-strategy", default="low_confidence", choices=["low_confidence", "dynamic"],
                    help="no effect with one denoising step (recorded)")
     p.add_argument("--confidence-threshold", type=float, default=0.9, help="no effect with one denoising step")
-    p.add_argument("--target-attn-implementation", default=None, choices=["sdpa", "eager", "flash_attention_2"],
+    p.add_argument("--target-attn-implementation", default=os.environ.get("TARGET_ATTN_IMPLEMENTATION"),
+                   choices=["sdpa", "eager", "flash_attention_2"],
                    help="PyTorch backends (CPU) only; the GPU path runs this framework's attention kernels")
-    p.add_argument("--draft-attn-implementation", default=None, choices=["sdpa", "eager", "flash_attention_2"])
+    p.add_argument("--draft-attn-implementation", default=os.environ.get("DRAFT_ATTN_IMPLEMENTATION"),
+                   choices=["sdpa", "eager", "flash_attention_2"])
     return p
 
 

@@ -13,6 +13,7 @@ an overall summary, evaluation-set accuracy where the set has answers.
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import time
 
@@ -57,8 +58,10 @@ def parser():
     cache = p.add_mutually_exclusive_group()
     cache.add_argument("--use-kvcache", dest="kvcache", action="store_true", default=True)
     cache.add_argument("--no-kvcache", dest="kvcache", action="store_false")
-    p.add_argument("--target-attn-implementation", default=None, choices=["sdpa", "eager", "flash_attention_2"])
-    p.add_argument("--draft-attn-implementation", default=None, choices=["sdpa", "eager", "flash_attention_2"])
+    p.add_argument("--target-attn-implementation", default=os.environ.get("TARGET_ATTN_IMPLEMENTATION"),
+                   choices=["sdpa", "eager", "flash_attention_2"])
+    p.add_argument("--draft-attn-implementation", default=os.environ.get("DRAFT_ATTN_IMPLEMENTATION"),
+                   choices=["sdpa", "eager", "flash_attention_2"])
     p.add_argument("--collect-stage-timings", action="store_true",
                    help="per-verify records with wall and device time of each draft and verify")
     p.add_argument("--baseline", action="store_true", help="also run target-only AR decoding")
