@@ -53,6 +53,9 @@ def parser() -> argparse.ArgumentParser:
     p.add_argument("--device", default="cuda:0" if torch.cuda.is_available() else "cpu")
     p.add_argument("--reference-device", default=None, help="device of the transformers reference (default --device)")
     p.add_argument("--skip-reference-validation", action="store_true")
+    p.add_argument("--batch-sizes", type=int, nargs="+", default=None,
+                   help="fixed-batch decode-only mode (serving/baseline_ar.py): each batch size decodes "
+                        "--max-new-tokens steps with no stop condition, prefill excluded")
     p.add_argument("--run-id", default=datetime.now(timezone.utc).strftime("%Y%m%d_%H%M%S"))
     p.add_argument("--output-root", type=Path, default=Path("results_baseline"))
     return p
@@ -124,6 +127,29 @@ def _table(summary: Dict[str, dict]) -> str:
     return "\n".join(lines) + "\n"
 
 
+def _fixed_batch(a, target, sets, dirs, meta) -> dict:
+    """Decode-only throughput at fixed batch sizes (prompts reused cyclically
+    when a batch is larger than the set)."""
+    from ..engine.spec import ar_decode_fixed
+    out = {}
+    for name, prompts in sets.items():
+        payload = {**meta, "mode": "fixed_batch_decode_only", "dataset": name, "cells": []}
+        for b in a.batch_sizes:
+            batch = [prompts[i % len(prompts)] for i in range(b)]
+            ar_decode_fixed(target, batch, min(8, a.max_new_tokens))          # warm-up
+            for rep in range(a.repeats):
+                r = ar_decode_fixed(target, batch, a.max_new_tokens)
+                if hasattr(target, "leak_check"):
+                    target.leak_check()
+                r.pop("outputs")
+                payload["cells"].append({"batch_size": b, "repeat": rep, **r})
+                print(f"DECODE {name} B={b} repeat={rep} TPS={r['tps']:.2f}", flush=True)
+        payload["status"] = "complete"
+        write_json(str(dirs[name] / "benchmark.json"), payload)
+        out[name] = payload
+    return out
+
+
 def main(argv=None) -> dict:
     from ..utils.runtime import required_pages
     a = parser().parse_args(argv)
@@ -168,6 +194,8 @@ def main(argv=None) -> dict:
             raise RuntimeError("admission invariant failed")
         return r
 
+    if a.batch_sizes:
+        return _fixed_batch(a, target, sets, dirs, meta)
     checks = []
     if not a.skip_reference_validation and not is_preset(a.target):
         for name, prompts in sets.items():

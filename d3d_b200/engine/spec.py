@@ -627,3 +627,29 @@ def ar_generate(target: TargetBackend, prompts: Sequence[Sequence[int]], max_new
                 latency_p95_s=lat[min(len(lat) - 1, int(0.95 * len(lat)))] if lat else 0.0,
                 length_limit_fraction=sum(r == "length" for r in reason.values()) / max(1, n),
                 mean_output_tokens=total / max(1, n))
+
+
+def ar_decode_fixed(target: TargetBackend, prompts: Sequence[Sequence[int]], steps: int,
+                    capture: bool = False) -> dict:
+    """Fixed-batch decode-only AR throughput (``serving/baseline_ar.py:23-47``):
+    every prompt is prefilled, then the whole batch decodes ``steps`` tokens
+    with no stop condition.  The prefill and its first token are excluded
+    from the time and the token count."""
+    seqs = [SeqState(index=i, prompt=[int(t) for t in p], prefix=len(p)) for i, p in enumerate(prompts)]
+    anchors, _ = target.prefill(seqs)
+    cur = [int(a) for a in anchors.tolist()]
+    toks = [[a] for a in cur] if capture else None
+    started = time.perf_counter()
+    for _ in range(int(steps)):
+        res = target.verify(seqs, torch.tensor([[a] for a in cur], dtype=torch.long))
+        cur = [int(c) for c in res.correction.tolist()]
+        for i, s in enumerate(seqs):
+            s.prefix += 1
+            if capture:
+                toks[i].append(cur[i])
+    elapsed = time.perf_counter() - started
+    for s in seqs:
+        target.release(s)
+    n = len(prompts) * int(steps)
+    return dict(elapsed_s=elapsed, tokens=n, requests=len(prompts), tps=n / elapsed if elapsed > 0 else 0.0,
+                outputs=toks)

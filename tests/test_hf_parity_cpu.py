@@ -66,3 +66,14 @@ def test_ar_baseline_cli_validation_retests_and_records(tmp_path):
     assert out["synthetic"]["requests"] == 3
     assert baseline.slow_attempts([{"attempt": 0, "tps": 10.0}, {"attempt": 1, "tps": 5.0}], 0.85) == [1]
     assert baseline.slow_attempts([{"attempt": i, "tps": t} for i, t in enumerate((10.0, 9.0, 2.0))], 0.85) == [2]
+
+
+def test_ar_baseline_fixed_batch_mode(tmp_path):
+    import json
+    from d3d_b200.cli import baseline
+    out = baseline.main(["--target", "tiny-target", "--device", "cpu", "--datasets", "synthetic", "--max-samples", "2",
+                         "--prompt-min", "8", "--prompt-max", "12", "--batch-sizes", "1", "3", "--max-new-tokens", "5",
+                         "--repeats", "1", "--pages", "64", "--run-id", "fb", "--output-root", str(tmp_path)])
+    cells = out["synthetic"]["cells"]
+    assert [(c["batch_size"], c["tokens"]) for c in cells] == [(1, 5), (3, 15)]
+    assert json.loads((tmp_path / "synthetic" / "fb" / "benchmark.json").read_text())["status"] == "complete"
