@@ -17,7 +17,7 @@ import torch
 
 from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
 from ..engine.spec import EOS_DEFAULT, DecodeConfig
-from ..utils.io import write_json
+from ..utils.io import label, write_json
 from ..utils.metrics import headline, source_stats, steps_from_output, summarize_acceptance
 from .common import (add_data_args, add_model_args, build_engine, load_selected_prompts, pin_host_threads,
                      score_outputs)
@@ -184,7 +184,7 @@ def _run(a, eng, prompts):
     acc = statistics.fmean(s for x in per for s in [x["summary"]["avg_accept_length"]]) if per else 0.0
     summary = {"headline": headline(tps, baseline_tps or 0.0, acc), "elapsed_s": elapsed,
                "token_identical_to_ar": all(x["matches_ar"] for x in per) if ar else None,
-               "drafter_tag": a.drafter_tag or a.draft, "draft_tokens": draft_tokens, "model_type": "d3d",
+               "drafter_tag": label(a.drafter_tag or a.draft), "draft_tokens": draft_tokens, "model_type": "d3d",
                "layout": "verifier_process" if hasattr(eng.target, "links") else "colocated"}
     hits = sum(x["hits"] for x in per)
     recov = sum(x["recoveries"] for x in per)

@@ -22,7 +22,7 @@ import torch
 from ..engine.backends import TorchTarget
 from ..engine.spec import EOS_DEFAULT, ar_generate
 from ..engine.sync import sync_generate, sync_generate_nocache
-from ..utils.io import write_json
+from ..utils.io import label, write_json
 from ..utils.metrics import AcceptanceStep, step_dicts, summarize_acceptance, summarize_timing
 from ..utils.runtime import resolve_dtype
 from .common import add_data_args, add_model_args, load_module, load_selected_prompts, score_outputs
@@ -153,7 +153,7 @@ def main(argv=None):
             r.update(pred=sc["pred"], gold=sc["gold"], correct=sc["correct"])
     summary = summarize_acceptance(all_steps, draft_tokens)
     summary.update(dataset=a.dataset, eval_set=getattr(a, "eval_meta", None), model_type="d3d",
-                   drafter_tag=a.drafter_tag or a.draft, num_prompts=len(rows),
+                   drafter_tag=label(a.drafter_tag or a.draft), num_prompts=len(rows),
                    total_output_tokens=sum(r["output_tokens"] for r in rows), elapsed_s=elapsed,
                    **summarize_timing(rows, elapsed_s=elapsed), target_model=a.target, draft_model=a.draft,
                    draft_tokens=draft_tokens, block_size=a.block_size, denoising_steps=a.denoising_steps,
