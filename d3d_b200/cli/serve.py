@@ -95,13 +95,12 @@ def main(argv=None):
     rows, warm = [], False
     draft_check = None
     if a.validate_draft:
-        import torch
+        import copy
         from ..engine.validation import validate_draft
-        from .common import load_module
-        dev = torch.device(a.device)
-        oracle = load_module(a.draft, dev, a.seed, a.draft_layers, a.mask_token_id).eval()
-        if dev.type == "cuda":
-            oracle = oracle.to(torch.bfloat16)
+        # the oracle holds exactly the engine drafter's weights: unpacked from the
+        # kernel layout on a GPU, a copy of the PyTorch module on the CPU
+        d = eng.decoder.d
+        oracle = d.w.to_module() if hasattr(d, "w") else copy.deepcopy(d.model)
         first = next(iter(sets.values()))["prompts"][0]
         draft_check = validate_draft(eng.decoder, oracle, first)
         del oracle

@@ -169,6 +169,45 @@ class FastWeights:
         cp = prnd(h, cfg.cond_hidden_size) if cfg.cond_hidden_size else None
         return cls(cfg, embed, layers, ones(h), lm, cp)
 
+    @torch.no_grad()
+    def to_module(self, device=None, dtype=torch.bfloat16) -> Qwen3LM:
+        """The PyTorch module holding these weights (unpacked; the gate|up
+        rows put back in order; folded norm scales divided out again), e.g.
+        as the oracle that the kernel path is validated against."""
+        cfg = self.cfg
+        dev = device if device is not None else self.embed.device
+        m = Qwen3LM(cfg).to(device=dev, dtype=dtype)
+        cast = lambda t: t.to(device=dev, dtype=dtype)
+        q, kv = cfg.q_size, cfg.kv_size
+        order = ops.gate_up_order(cfg.intermediate_size).to(self.embed.device)
+        for L, dst in zip(self.layers, m.model.layers):
+            qkv = L.qkv.unpack().float()
+            gu = L.gate_up.unpack().float()
+            if self.folded:
+                qkv = qkv / L.in_norm.float()[None, :]
+                gu = gu / L.post_norm.float()[None, :]
+            rows = torch.empty_like(gu)
+            rows[order] = gu
+            a = dst.self_attn
+            a.q_proj.weight.copy_(cast(qkv[:q]))
+            a.k_proj.weight.copy_(cast(qkv[q:q + kv]))
+            a.v_proj.weight.copy_(cast(qkv[q + kv:]))
+            a.o_proj.weight.copy_(cast(L.o.unpack()))
+            a.q_norm.weight.copy_(cast(L.q_norm))
+            a.k_norm.weight.copy_(cast(L.k_norm))
+            dst.mlp.gate_proj.weight.copy_(cast(rows[:cfg.intermediate_size]))
+            dst.mlp.up_proj.weight.copy_(cast(rows[cfg.intermediate_size:]))
+            dst.mlp.down_proj.weight.copy_(cast(L.down.unpack()))
+            dst.input_layernorm.weight.copy_(cast(L.in_norm))
+            dst.post_attention_layernorm.weight.copy_(cast(L.post_norm))
+        m.model.embed_tokens.weight.copy_(cast(self.embed))
+        m.model.norm.weight.copy_(cast(self.final_norm))
+        if not cfg.tie_word_embeddings:
+            m.lm_head.weight.copy_(cast(self.lm_head.unpack()))
+        if self.cond_proj is not None and getattr(m, "cond_proj", None) is not None:
+            m.cond_proj.weight.copy_(cast(self.cond_proj.unpack()))
+        return m.eval()
+
     def drop_layers(self, idx) -> "FastWeights":
         keep = [L for j, L in enumerate(self.layers) if j not in set(idx)]
         cfg = self.cfg.replace(num_hidden_layers=len(keep))

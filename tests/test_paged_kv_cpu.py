@@ -35,3 +35,28 @@ def test_reserve_trim_release_slots_and_scratch():
     assert kv.tables == {} and kv.leaked == 0 and len(kv.free) + len(kv.scratch) == kv.num_pages
     assert kv.k[0].shape == (10 * 4, tiny_target().num_key_value_heads, tiny_target().head_dim)
     assert kv.k[0].dtype == torch.bfloat16
+
+
+def test_fast_weights_round_trip_to_module():
+    """Kernel-layout weights back to a PyTorch module (tiles unpacked, gate|up
+    rows re-ordered, folded norm scales divided out) equal the source within
+    bf16 rounding."""
+    import torch
+    from d3d_b200.config import tiny_drafter
+    from d3d_b200.models.fast import FastWeights
+    from d3d_b200.models.qwen3 import build_model
+    m = build_model(tiny_drafter(cond=True), seed=3)
+    with torch.no_grad():
+        for L in m.model.layers:
+            L.input_layernorm.weight.mul_(1.5)
+            L.post_attention_layernorm.weight.add_(0.25)
+    fw = FastWeights.from_module(m, "cpu")
+    for fold in (False, True):
+        if fold:
+            fw.fold_norms()
+        back = fw.to_module(dtype=torch.float32)
+        sa, sb = m.state_dict(), back.state_dict()
+        assert sa.keys() == sb.keys()
+        for k in sa:
+            scale = sa[k].float().abs().max().item() + 1e-9
+            assert (sa[k].float() - sb[k].float()).abs().max().item() <= 1e-2 * scale, k
