@@ -218,7 +218,7 @@ class TorchDraft(DraftBackend):
         self.kv = _DenseKVPool(model.cfg.num_hidden_layers)
         self.vocab_size = model.cfg.vocab_size
         self.mask_id = int(model.cfg.mask_token_id)
-        self.record_gaps = False      # also return each row's runner-up token and top-2 logit gap
+        self.record_logits = False    # also return every row's logits
         self.last: Dict[str, torch.Tensor] = {}
         self.gen = torch.Generator(device="cpu").manual_seed(seed)
 
@@ -235,7 +235,7 @@ class TorchDraft(DraftBackend):
     @torch.inference_mode()
     def forward(self, seqs, ids, positions, rows, *, store, topk, cond_rows=None, sample=None):
         out: Dict[str, List[torch.Tensor]] = {"greedy": [], "top": [], "tokens": [],
-                                              "q_ids": [], "q_probs": [], "second": [], "gap": []}
+                                              "q_ids": [], "q_probs": [], "logits": []}
         for b, s in enumerate(seqs):
             cache = self.kv.get(s)
             cache.crop(s.prefix)
@@ -247,10 +247,8 @@ class TorchDraft(DraftBackend):
                            mask=mask, cache=cache, store_kv=store, cond=cond, cond_rows=cr)
             logits = self.model.logits(h)[0].float()
             out["greedy"].append(logits.argmax(-1))
-            if self.record_gaps:       # runner-up token and its logit gap (near-tie analysis)
-                v, ix = torch.topk(logits, k=2, dim=-1)
-                out["second"].append(ix[:, 1])
-                out["gap"].append(v[:, 0] - v[:, 1])
+            if self.record_logits:     # every row's logits (near-tie analysis of a validation)
+                out["logits"].append(logits)
             if topk:
                 out["top"].append(torch.topk(logits, k=topk, dim=-1).indices)
             if sample is not None:

@@ -21,12 +21,13 @@ from .backends import SeqState, TorchDraft
 from .spec import SpecDecoder
 
 
-def _ties(ours, ref, second, gap, tol: float):
+def _ties(ours, ref, logits, tol: float):
     """Positions (after the anchor) where ``ours`` differs from the oracle's
-    argmax ``ref`` but is the oracle's runner-up within ``tol`` logits."""
+    argmax ``ref``, those whose logit regret under the oracle (argmax logit
+    minus the logit of our token) is at most ``tol``, and every regret."""
     diff = [j for j in range(1, len(ref)) if ours[j] != ref[j]]
-    ties = [j for j in diff if ours[j] == int(second[j]) and float(gap[j]) <= tol]
-    return diff, ties
+    regret = {j: float(logits[j, ref[j]] - logits[j, ours[j]]) for j in diff}
+    return diff, [j for j in diff if regret[j] <= tol], regret
 
 
 @torch.inference_mode()
@@ -35,14 +36,14 @@ def validate_draft(decoder: SpecDecoder, oracle, prompt: Sequence[int], *, min_a
     """Compare ``decoder``'s drafter with ``oracle`` (a ``Qwen3LM``) on
     ``prompt``; raises ``RuntimeError`` when the recovery blocks differ or the
     packed-token agreement is below ``min_agreement``.  A differing token
-    that is the oracle's runner-up within ``tie_tolerance`` logits of its
-    argmax is a near-tie (bf16 rounding can flip it; the reference's AR
+    whose logit under the oracle is within ``tie_tolerance`` of the oracle's
+    argmax logit is a near-tie (bf16 rounding can flip it; the reference's AR
     baseline makes the same distinction with a teacher-forced logit regret):
     near-ties are reported and counted as agreement."""
     cfg = decoder.cfg
     k = cfg.block_size
     ref_draft = TorchDraft(oracle)
-    ref_draft.record_gaps = True
+    ref_draft.record_logits = True
     ref = SpecDecoder(decoder.t, ref_draft, cfg)
     ours_s = SeqState(index=index, prompt=list(prompt), prefix=len(prompt))
     ref_s = SeqState(index=index + 1, prompt=list(prompt), prefix=len(prompt))
@@ -57,8 +58,8 @@ def validate_draft(decoder: SpecDecoder, oracle, prompt: Sequence[int], *, min_a
         ref.recover([ref_s])
         rec = ref_draft.last
         recovery_equal = ours_s.current.tolist() == ref_s.current.tolist()
-        rdiff, rties = _ties(ours_s.current.tolist(), ref_s.current.tolist(), rec["second"][0], rec["gap"][0],
-                             tie_tolerance)
+        rdiff, rties, rregret = _ties(ours_s.current.tolist(), ref_s.current.tolist(), rec["logits"][0],
+                                      tie_tolerance)
         # same pending block and top tokens on both sides: the packed forward alone
         ref_s.current = ours_s.current.clone()
         ref_s.top = None if ours_s.top is None else ours_s.top.clone()
@@ -77,14 +78,16 @@ def validate_draft(decoder: SpecDecoder, oracle, prompt: Sequence[int], *, min_a
             total += len(y)
             if x != y:
                 sl = exp.lay.segment(exp.index[key])
-                _, ties = _ties(x, y, out["second"][exp.i, sl], out["gap"][exp.i, sl], tie_tolerance)
+                _, ties, regret = _ties(x, y, out["logits"][exp.i, sl], tie_tolerance)
                 near += len(ties)
-                diffs.append({"key": [key[0], key[1]], "actual": x, "expected": y, "near_ties": ties})
+                diffs.append({"key": [key[0], key[1]], "actual": x, "expected": y, "near_ties": ties,
+                              "max_logit_regret": max(regret.values())})
     finally:
         decoder.t.release(ours_s)
         decoder.d.release(ours_s)
         ref_draft.release(ref_s)
-    result = {"recovery_equal": recovery_equal, "recovery_near_ties": rties, "candidate_keys": len(keys_ref),
+    result = {"recovery_equal": recovery_equal, "recovery_near_ties": rties,
+              "recovery_max_logit_regret": max(rregret.values()) if rregret else 0.0, "candidate_keys": len(keys_ref),
               "packed_tokens_equal": equal, "packed_tokens_total": total,
               "agreement": equal / total if total else 1.0, "packed_near_ties": near,
               "agreement_up_to_near_ties": (equal + near) / total if total else 1.0, "tie_tolerance": tie_tolerance,
@@ -92,6 +95,7 @@ def validate_draft(decoder: SpecDecoder, oracle, prompt: Sequence[int], *, min_a
     recovery_ok = recovery_equal or len(rties) == len(rdiff)
     if not recovery_ok or result["agreement_up_to_near_ties"] < min_agreement:
         raise RuntimeError(f"drafter differs materially from the oracle module: recovery_equal={recovery_equal} "
-                           f"({len(rdiff) - len(rties)} non-tie differences), agreement={result['agreement']:.4f}, "
+                           f"({len(rdiff) - len(rties)} non-tie differences, max logit regret "
+                           f"{result['recovery_max_logit_regret']:.4f}), agreement={result['agreement']:.4f}, "
                            f"up to near-ties={result['agreement_up_to_near_ties']:.4f}")
     return result
