@@ -150,15 +150,19 @@ def load_target_shard(path: str, tp: int, rank: int, device="cuda"):
 
 def target_server(target_w, link, *, max_seqs: int = 16, max_context: int = 4096,
                   target_pages: Optional[int] = None, page_size: int = 16, device="cuda",
-                  use_graphs: bool = True, deadline_s: float = 600.0, tp=None, replies: str = "all"):
+                  use_graphs: bool = True, deadline_s: float = 600.0, tp=None, replies: str = "all",
+                  temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0):
     """The target side of a disaggregated pair: call ``.serve()`` on the result;
     it returns when the drafter side calls :meth:`D3DEngine.close`, and raises
     ``TimeoutError`` after ``deadline_s`` without a request.  For one rank of
     a tensor-parallel target pass its ``TPGroup`` as ``tp`` (and
-    ``replies="ack"`` on every rank but 0)."""
+    ``replies="ack"`` on every rank but 0).  ``temperature`` / ``top_k`` /
+    ``top_p``: the target's sampling (sampled verifies carry the drafts'
+    proposals in their requests)."""
     from .engine.disagg import P2PTargetServer
     from .engine.fast import FastTarget
     pages = target_pages or max_seqs * (max_context + 64 + page_size) // page_size + 8
     t = FastTarget(target_w, pages=pages, page_size=page_size, max_seqs=max_seqs,
-                   max_context=max_context, use_graphs=use_graphs, device=device, tp=tp)
+                   max_context=max_context, use_graphs=use_graphs, device=device, tp=tp,
+                   temperature=temperature, top_k=top_k, top_p=top_p)
     return P2PTargetServer(t, link, deadline_s=deadline_s, replies=replies)

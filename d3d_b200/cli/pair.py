@@ -50,7 +50,8 @@ def _verifier_main(port: int, target: str, device: str, seed: int, max_seqs: int
             torch.cuda.set_device(dev)
             link = open_pair_link(1, dev)
             srv = target_server(load_fast_weights(target, dev, seed), link, max_seqs=max_seqs,
-                                max_context=max_context, device=dev, deadline_s=timeout_s)
+                                max_context=max_context, device=dev, deadline_s=timeout_s,
+                                temperature=temperature, top_k=top_k, top_p=top_p)
         else:
             from ..engine.backends import TorchTarget
             from ..engine.disagg import P2PTargetServer
