@@ -32,6 +32,7 @@ import torch
 
 from ..engine.spec import EOS_DEFAULT, ar_generate
 from ..utils.io import write_json
+from ..utils.runtime import runtime_metadata
 from .common import add_data_args, is_preset, load_fast_weights, load_module, load_prompts
 
 
@@ -184,7 +185,8 @@ def main(argv=None) -> dict:
             "slowdown_policy": f"an attempt below {a.slow_fraction} of the faster of two (median of more) "
                                f"triggers up to {a.max_retests} retests", "device": str(a.device),
             "hardware": torch.cuda.get_device_name(0) if torch.cuda.is_available() else "cpu",
-            "torch": torch.__version__, "eos_ids": list(eos), "temperature": 0}
+            "torch": torch.__version__, "eos_ids": list(eos), "temperature": 0,
+            "runtime": runtime_metadata({"target": a.target})}
 
     def run(prompts, c, n):
         r = ar_generate(target, prompts, n, eos=eos or EOS_DEFAULT, ignore_eos=a.ignore_eos, concurrency=c)

@@ -15,7 +15,7 @@ from typing import Dict
 from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
 from ..engine.spec import DecodeConfig
 from ..utils.io import write_json
-from ..utils.runtime import check_paged_capacity
+from ..utils.runtime import check_paged_capacity, runtime_metadata
 from .common import (add_data_args, add_model_args, build_engine, hf_greedy_agreement, is_preset,
                      load_prompts, score_outputs)
 
@@ -153,7 +153,8 @@ def main(argv=None):
                 print(row, flush=True)
     write_json(a.output_json, {"rows": rows, "config": {k: v for k, v in vars(a).items() if not k.startswith("eval_")},
                                "eval_sets": {n: d["eval"].get("eval_meta") for n, d in sets.items()},
-                               "draft_validation": draft_check})
+                               "draft_validation": draft_check,
+                               "runtime": runtime_metadata({"target": a.target, "draft": a.draft})})
     return rows
 
 

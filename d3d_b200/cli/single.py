@@ -18,6 +18,7 @@ import torch
 from ..engine.controlled import ControlledAcceptance, rate_for_mean_accept
 from ..engine.spec import EOS_DEFAULT, DecodeConfig
 from ..utils.io import label, write_json
+from ..utils.runtime import runtime_metadata
 from ..utils.metrics import headline, source_stats, steps_from_output, summarize_acceptance
 from .common import (add_data_args, add_model_args, build_engine, load_selected_prompts, pin_host_threads,
                      score_outputs)
@@ -203,7 +204,8 @@ def _run(a, eng, prompts):
             x.update(pred=r["pred"], gold=r["gold"], correct=r["correct"])
         summary["accuracy"] = scores
     summary["config"] = {k: v for k, v in vars(a).items() if not k.startswith("eval_")}
-    write_json(a.output_json, {"summary": summary, "per_prompt": per})
+    write_json(a.output_json, {"summary": summary, "per_prompt": per,
+                               "runtime": runtime_metadata({"target": a.target, "draft": a.draft})})
     write_json(a.summary_json, summary)
     print(summary["headline"])
     return summary

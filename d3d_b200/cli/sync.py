@@ -24,7 +24,7 @@ from ..engine.spec import EOS_DEFAULT, ar_generate
 from ..engine.sync import sync_generate, sync_generate_nocache
 from ..utils.io import label, write_json
 from ..utils.metrics import AcceptanceStep, step_dicts, summarize_acceptance, summarize_timing
-from ..utils.runtime import resolve_dtype
+from ..utils.runtime import resolve_dtype, runtime_metadata
 from .common import add_data_args, add_model_args, load_module, load_selected_prompts, score_outputs
 
 DTYPES = ("auto", "bf16", "bfloat16", "fp16", "float16", "fp32", "float32")
@@ -166,7 +166,8 @@ def main(argv=None):
                    accuracy=None if scores is None else scores["accuracy"],
                    matches_ar=None if ar is None else all(r["matches_ar"] for r in rows))
     config = {k: v for k, v in vars(a).items() if not k.startswith("eval_")}
-    write_json(a.output_json, {"summary": summary, "rows": rows, "accuracy": scores, "config": config})
+    write_json(a.output_json, {"summary": summary, "rows": rows, "accuracy": scores, "config": config,
+                               "runtime": runtime_metadata({"target": a.target, "draft": a.draft})})
     compact = {k: summary[k] for k in ("dataset", "drafter_tag", "num_prompts", "total_output_tokens",
                                        "avg_accept_length", "avg_accepted_draft_tokens", "draft_accept_rate",
                                        "aggregate_decode_tokens_per_s", "mean_time_per_output_token",
