@@ -405,3 +405,20 @@ def test_draft_validation_against_oracle_module():
             p.add_(torch.randn_like(p) * 0.5)
     with pytest.raises(RuntimeError, match="differs materially"):
         validate_draft(dec, bad, prompt)
+
+
+@pytest.mark.parametrize("counts", [None, (1, 3)])
+def test_unanchored_outcomes_keep_token_identity(counts):
+    """``anchor_num=0``: each commit length drafts one unanchored outcome whose
+    first token is replaced by the target's correction on reuse
+    (``single/eval_async_packed.py:1797-1803``); output equals AR and the
+    outcomes are reused."""
+    tgt = TorchTarget(build_model(tiny_target(), seed=0))
+    drf = TorchDraft(build_model(tiny_drafter(cond=True), seed=1))
+    rng = random.Random(3)
+    prompts = [[rng.randrange(2, 1000) for _ in range(rng.randint(10, 30))] for _ in range(3)]
+    cfg = DecodeConfig(block_size=8, anchor_num=0, max_new_tokens=24, ignore_eos=True,
+                       packed_accepted_counts=counts)
+    r = SpecDecoder(tgt, drf, cfg).generate(prompts, concurrency=2)
+    assert [o.tokens for o in r["outputs"]] == ar_generate(tgt, prompts, 24, ignore_eos=True)["outputs"]
+    assert sum(o.hits for o in r["outputs"]) > 0
