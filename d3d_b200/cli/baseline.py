@@ -155,7 +155,7 @@ def main(argv=None) -> dict:
     from ..utils.runtime import required_pages
     a = parser().parse_args(argv)
     if (min(a.concurrency + [a.repeats, a.max_new_tokens, a.warmup_new_tokens, a.pages]) < 1
-            or a.max_samples < 0 or a.max_retests < 0):
+            or (a.max_samples or 0) < 0 or a.max_retests < 0):
         raise SystemExit("invalid numeric parameter")
     if not 0 < a.slow_fraction < 1:
         raise SystemExit("--slow-fraction must be between zero and one")

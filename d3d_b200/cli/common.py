@@ -23,13 +23,16 @@ def add_model_args(p: argparse.ArgumentParser, target_flag: str, draft_flag: str
     p.add_argument("--draft-layers", type=int, default=None, help="preset drafters only")
 
 
-def add_data_args(p: argparse.ArgumentParser) -> None:
+def add_data_args(p: argparse.ArgumentParser, max_samples: Optional[int] = None) -> None:
+    """Prompt-source flags.  ``--max-samples`` defaults to ``max_samples``;
+    ``None`` reads every example of a file or evaluation set (and draws 8
+    synthetic prompts)."""
     p.add_argument("--dataset", default="synthetic",
                    help="'synthetic', a JSONL file of prompts, or an evaluation set by name "
                         "(gsm8k, math500, aime25, humaneval, mbpp, mt-bench, livecodebench-v6; read from "
                         "$D3D_DATA_CACHE / $D3D_ANSWER_CACHE, rendered with the tokenizer's chat template)")
     p.add_argument("--enable-thinking", action="store_true", help="evaluation sets: thinking chat template")
-    p.add_argument("--max-samples", type=int, default=8)
+    p.add_argument("--max-samples", type=int, default=max_samples)
     p.add_argument("--prompt-min", type=int, default=128)
     p.add_argument("--prompt-max", type=int, default=512)
     p.add_argument("--tokenizer", default=None, help="tokenizer directory for text prompts")
@@ -38,7 +41,8 @@ def add_data_args(p: argparse.ArgumentParser) -> None:
 def load_prompts(args) -> List[List[int]]:
     if args.dataset == "synthetic":
         vocab = min(151643, model_config(args.target).vocab_size - 2)
-        return synthetic_prompts(args.max_samples, args.prompt_min, args.prompt_max, seed=1000 + args.seed,
+        n = args.max_samples if args.max_samples else 8
+        return synthetic_prompts(n, args.prompt_min, args.prompt_max, seed=1000 + args.seed,
                                  vocab=vocab)
     tok = None
     if args.tokenizer:

@@ -23,7 +23,7 @@ from .common import (add_data_args, add_model_args, build_engine, hf_greedy_agre
 def parser():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     add_model_args(p, "--target", "--draft")
-    add_data_args(p)
+    add_data_args(p, max_samples=128)
     p.add_argument("--datasets", nargs="+", default=None,
                    help="several prompt sources in one run (names or files, as --dataset); one row per "
                         "(dataset, concurrency, repeat)")
