@@ -30,12 +30,12 @@ def parser():
     p.add_argument("--pages", type=int, default=4096)
     p.add_argument("--page-size", type=int, default=16)
     p.add_argument("--concurrency", default="1,4,8,16")
-    p.add_argument("--max-new-tokens", type=int, default=256)
+    p.add_argument("--max-new-tokens", type=int, default=2048)
     p.add_argument("--max-new-tokens-range", default=None,
                    help="LO,HI: per-request output budgets drawn uniformly (seeded), e.g. 128,512")
     p.add_argument("--repeats", type=int, default=1, help="timed runs per (dataset, concurrency)")
     p.add_argument("--block-size", type=int, default=16)
-    p.add_argument("--anchor-num", type=int, default=1)
+    p.add_argument("--anchor-num", type=int, default=3)
     p.add_argument("--draft-microbatch", type=int, default=4)
     p.add_argument("--ignore-eos", action="store_true")
     p.add_argument("--backup", choices=["neural", "fast", "fast_legacy"], default="neural",

@@ -28,10 +28,11 @@ def parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     add_model_args(p, "--verifier", "--drafter")
     add_data_args(p)
-    p.add_argument("--max-new-tokens", type=int, default=512)
-    p.add_argument("--block-size", type=int, default=16)
-    p.add_argument("--anchor-num", type=int, default=3)
-    p.add_argument("--attention-mask-mode", choices=["causal", "block_causal"], default="causal")
+    p.add_argument("--max-new-tokens", type=int, default=2048)
+    p.add_argument("--block-size", type=int, default=32)
+    p.add_argument("--anchor-num", type=int, default=0,
+                   help="non-primary anchors per rejection position (0: unanchored outcomes)")
+    p.add_argument("--attention-mask-mode", choices=["causal", "block_causal"], default="block_causal")
     p.add_argument("--packed-accepted-counts", default="all",
                    help="'all' or a comma list of commit lengths to pre-draft")
     p.add_argument("--temperature", type=float, default=0.0)

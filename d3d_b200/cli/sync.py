@@ -38,7 +38,7 @@ def parser():
                    help="drafter family (read from the drafter's config when omitted; D3D drafters only)")
     p.add_argument("--drafter-tag", default=None, help="label recorded in the summary (default: the drafter name)")
     p.add_argument("--sample-index", type=int, default=None, help="decode only this example of the set")
-    p.add_argument("--max-new-tokens", type=int, default=128)
+    p.add_argument("--max-new-tokens", type=int, default=2048)
     p.add_argument("--draft-tokens", type=int, default=None,
                    help="drafted tokens per block for the acceptance summary (default: block size - 1)")
     p.add_argument("--block-size", type=int, default=32)
