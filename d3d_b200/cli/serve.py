@@ -43,7 +43,8 @@ def parser():
                         "block's drafts cover commit length 1 only; fast_legacy: every commit length)")
     p.add_argument("--fast-miss-anchors", type=int, default=0,
                    help="fast backup: anchors drafted after a random block (0 = --anchor-num)")
-    p.add_argument("--validate", action="store_true", help="check token identity against AR decoding")
+    p.add_argument("--validate", action="store_true",
+                   help="check token identity against AR decoding (an error when any request differs)")
     p.add_argument("--validate-hf", action="store_true",
                    help="compare the outputs with transformers' greedy generate on the target checkpoint")
     p.add_argument("--validate-draft", action="store_true",
@@ -155,6 +156,8 @@ def main(argv=None):
                                "eval_sets": {n: d["eval"].get("eval_meta") for n, d in sets.items()},
                                "draft_validation": draft_check,
                                "runtime": runtime_metadata({"target": a.target, "draft": a.draft})})
+    if a.validate and not all(r.get("token_identical_to_ar", True) for r in rows):
+        raise RuntimeError("speculative output differs from AR decoding; see token_identical_to_ar in the JSON")
     return rows
 
 
