@@ -67,7 +67,9 @@ def _batch_source(args, rank: int, world: int, vocab: int, rng: random.Random, m
     ``train/dataset.py:157-231``)."""
     state = {"cursor": cursor}
     if args.data_path == "synthetic":
-        pool = synthetic_examples(args.batch_size * max(1, n_micro), args.seq_len, 0.25, vocab, rng)
+        # a bounded pool of seeded sequences, read cyclically (long synthetic runs
+        # would otherwise hold every step's tokens in host memory)
+        pool = synthetic_examples(min(args.batch_size * max(1, n_micro), 1024), args.seq_len, 0.25, vocab, rng)
 
         def take(c, n):
             return [pool[(c + i) % len(pool)] for i in range(n)], c + n
