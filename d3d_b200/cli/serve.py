@@ -9,6 +9,8 @@ Requests arrive all at once (closed loop); throughput is end to end
 from __future__ import annotations
 
 import argparse
+import hashlib
+import json
 import time
 from typing import Dict
 
@@ -108,6 +110,7 @@ def main(argv=None):
         print({k: v for k, v in draft_check.items() if k != "differences"}, flush=True)
     for name, d in sets.items():
         prompts, bud = d["prompts"], budgets.get(name)
+        digest = hashlib.sha256(json.dumps(prompts).encode()).hexdigest()
         for k, v in d["eval"].items():
             setattr(a, k, v)
         if not d["eval"]:
@@ -133,8 +136,12 @@ def main(argv=None):
                 r = eng.generate(prompts, concurrency=c, controlled=ctl, max_new=bud)
                 row = {"dataset": name, "concurrency": c, "repeat": rep, "requests": len(prompts), "tps": r["tps"],
                        "elapsed_s": r["elapsed_s"], "output_tokens": r["output_tokens"],
-                       "mean_accept_length": r["mean_accept_length"], "miss_rounds": r["miss_rounds"],
-                       "max_batch": max(r["decode_batch_sizes"]) if r["decode_batch_sizes"] else 0}
+                       "mean_accept_length": r["mean_accept_length"], "accept_length": r["mean_accept_length"],
+                       "miss_rounds": r["miss_rounds"],
+                       "max_batch": max(r["decode_batch_sizes"]) if r["decode_batch_sizes"] else 0,
+                       "max_active": max(r["decode_batch_sizes"]) if r["decode_batch_sizes"] else 0,
+                       "timing_boundary": "end to end: admission, prefill, decode and release",
+                       "input_sha256": digest}
                 if ar is not None:
                     row["token_identical_to_ar"] = all(o.tokens == ar["outputs"][o.index] for o in r["outputs"])
                 outs = [o.tokens for o in sorted(r["outputs"], key=lambda o: o.index)]
@@ -148,7 +155,7 @@ def main(argv=None):
                     row["accuracy"] = scores["accuracy"]
                     row["scored"] = scores["scored"]
                 if ar_tps is not None:
-                    row["ar_tps"] = ar_tps
+                    row["ar_tps"] = row["baseline_tps"] = ar_tps
                     row["speedup"] = row["tps"] / ar_tps if ar_tps else None
                 rows.append(row)
                 print(row, flush=True)
