@@ -104,6 +104,9 @@ def _engine(a, decode, max_context):
     process when the devices differ (or ``--verifier-process``)."""
     vdev = torch.device(a.verifier_device or a.device)
     ddev = torch.device(a.draft_device or vdev)
+    for dev in (vdev, ddev):       # the reference's hardware check (common/runtime.py:31-43)
+        if dev.type == "cuda" and (not torch.cuda.is_available() or (dev.index or 0) >= torch.cuda.device_count()):
+            raise SystemExit(f"device {dev} is not available ({torch.cuda.device_count()} CUDA devices)")
     if vdev == ddev and not a.verifier_process:
         a.device = str(vdev)
         eng = build_engine(a, decode, max_seqs=2, max_context=max_context)
