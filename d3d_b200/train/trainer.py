@@ -283,6 +283,11 @@ def train(args) -> dict:
     objective = normalize_objective(args.objective)
     if objective in ("forward_kl", "reverse_kl") and not args.target_model:
         raise ValueError(f"objective {objective} needs --target-model")
+    probe_steps = int(getattr(args, "trajectory_gradient_probe_steps", 0) or 0)
+    if probe_steps < 0:
+        raise ValueError("--trajectory-gradient-probe-steps must be >= 0")
+    if probe_steps and not getattr(args, "trajectory_weight", 0.0):
+        raise ValueError("--trajectory-gradient-probe-steps requires --trajectory-weight > 0")
     if getattr(args, "trajectory_weight", 0.0) and not (args.target_model or args.trajectory_teacher_model):
         raise ValueError("--trajectory-weight needs --trajectory-teacher-model or --target-model")
     cls = getattr(args, "fsdp_transformer_layer_cls", None) or []
@@ -443,6 +448,9 @@ def train(args) -> dict:
                     probe = {"trajectory_grad_norm": nt, "ce_grad_norm": nc,
                              "trajectory_to_ce_grad_ratio": nt / nc if nc > 0 else None}
                     probe_left -= 1
+                    if rank == 0:
+                        print(f"  trajectory_grad | ce_hidden {nc:.6e} | unit_traj_hidden {nt:.6e} | "
+                              f"unit/ce {probe['trajectory_to_ce_grad_ratio'] or 0.0:.4f}", flush=True)
                 loss = loss + args.trajectory_weight * unit
             (loss / accum).backward()
             tot["loss"] += float(loss.item())
