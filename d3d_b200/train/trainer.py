@@ -156,13 +156,49 @@ def save_checkpoint(model, opt: ShardedAdamW, out_dir: Path, step: int, cursor: 
         torch.save(z3.state_dict(), ck / f"layers_rank{rank:03d}.pt")
 
 
+def validate_args(args) -> None:
+    """The reference's checks of the training flags (``train/trainer.py:470-515``)."""
+    checks = [
+        (args.block_size > 1, "--block-size must be > 1"),
+        (args.batch_size > 0, "--batch-size must be > 0"),
+        (args.parallel_anchors_per_example > 0, "--parallel-anchors-per-example must be > 0"),
+        (args.workers >= 0, "--workers must be >= 0"),
+        (args.workers == 0 or args.prefetch > 0, "--prefetch must be > 0 when workers are enabled"),
+        (args.loss_decay_gamma > 0, "--loss-decay-gamma must be > 0"),
+        (args.gradient_accumulation_steps > 0, "--gradient-accumulation-steps must be > 0"),
+        (0.0 <= args.min_lr_ratio <= 1.0, "--min-lr-ratio must be in [0, 1]"),
+        (args.ce_weight >= 0 and args.kl_weight >= 0, "--ce-weight / --kl-weight must be >= 0"),
+        (args.hnce_weight >= 0 and args.hnce_top_k > 0, "--hnce-weight must be >= 0 and --hnce-top-k > 0"),
+        (args.margin_weight >= 0 and args.margin_top_k > 0, "--margin-weight must be >= 0 and --margin-top-k > 0"),
+        (args.ar_weight >= 0 and args.ar_logit_chunk_size >= 0,
+         "--ar-loss-weight and --ar-logit-chunk-size must be >= 0"),
+        (args.trajectory_weight >= 0, "--trajectory-weight must be >= 0"),
+        (not args.trajectory_shuffle_teacher_blocks or args.trajectory_weight > 0,
+         "--trajectory-shuffle-teacher-blocks requires --trajectory-weight > 0"),
+        (args.epochs > 0 and args.max_micro_steps >= 0 and args.max_steps >= 0,
+         "--epochs must be > 0, --max-micro-steps and --max-steps >= 0"),
+    ]
+    for ok, msg in checks:
+        if not ok:
+            raise ValueError(msg)
+
+
 def _tokenizer(args):
-    """The data tokenizer, or ``None`` when no tokenizer directory is set."""
-    if not getattr(args, "tokenizer", None):
+    """The data tokenizer: ``--tokenizer-model``, else the target's or the
+    drafter's checkpoint directory when it holds one (the reference's
+    fallback order); ``None`` for synthetic data without one."""
+    from ..cli.common import is_preset
+    path = getattr(args, "tokenizer", None)
+    if not path:
+        for cand in (args.target_model, args.draft_model):
+            if cand and not is_preset(cand) and (Path(cand) / "tokenizer_config.json").is_file():
+                path = cand
+                break
+    if not path:
         return None
     from transformers import AutoTokenizer
     kw = {"fix_mistral_regex": True} if getattr(args, "fix_mistral_regex", False) else {}
-    return AutoTokenizer.from_pretrained(args.tokenizer, **kw)
+    return AutoTokenizer.from_pretrained(path, **kw)
 
 
 def _mask_id(args, tok) -> Optional[int]:
@@ -279,6 +315,7 @@ def train(args) -> dict:
     torch.manual_seed(args.seed + rank)
     rng = random.Random(args.seed * 1000 + rank)
     cdt = torch.bfloat16 if (device.type == "cuda" and args.dtype == "bf16") else torch.float32
+    validate_args(args)
     accum = max(1, int(getattr(args, "gradient_accumulation_steps", 1)))
     objective = normalize_objective(args.objective)
     if objective in ("forward_kl", "reverse_kl") and not args.target_model:
@@ -358,6 +395,9 @@ def train(args) -> dict:
     out_dir = Path(args.output_dir)
     if rank == 0:
         out_dir.mkdir(parents=True, exist_ok=True)
+        (out_dir / "args.json").write_text(json.dumps({**{k: v for k, v in vars(args).items()
+                                                          if isinstance(v, (int, float, str, bool, list, type(None)))},
+                                                       "world_size": world}, indent=2, sort_keys=True))
     run = _wandb_run(args, rank)
     tb = _TensorBoard(out_dir / "tensorboard", rank)
     a_kl = args.kl_weight if (teacher is not None and objective in ("forward_kl", "kl_ce")) else 0.0

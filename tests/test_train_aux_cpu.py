@@ -169,3 +169,14 @@ def test_random_init_and_mask_token_lookup(tmp_path):
     assert _mask_id(a, tok) == 77
     a.mask_token_id = 5
     assert _mask_id(a, tok) == 5
+
+
+def test_training_flag_checks(tmp_path):
+    import pytest
+    for bad in (["--block-size", "1"], ["--workers", "-1"], ["--min-lr-ratio", "2"], ["--loss-decay-gamma", "0"],
+                ["--trajectory-shuffle-teacher-blocks"], ["--trajectory-gradient-probe-steps", "2"]):
+        with pytest.raises(ValueError):
+            _run(tmp_path, "bad", ["--max-steps", "1", "--seq-len", "64"] + bad)
+    _run(tmp_path, "ok", ["--max-steps", "1", "--seq-len", "64"])
+    import json
+    assert json.loads((tmp_path / "ok" / "args.json").read_text())["world_size"] == 1
