@@ -57,7 +57,8 @@ def parser() -> argparse.ArgumentParser:
 
     s = sub.add_parser("train", help="fixed-budget recovery training of a pruned child")
     s.add_argument("--student", type=Path, required=True)
-    s.add_argument("--dataset", required=True, help="JSONL rows (chat, text or prompt_ids/response_ids), or 'synthetic'")
+    s.add_argument("--dataset", required=True,
+                   help="JSONL rows (chat, text or prompt_ids/response_ids), or 'synthetic'")
     s.add_argument("--output-dir", type=Path, required=True)
     s.add_argument("--data-cursor", type=int, default=0)
     s.add_argument("--max-steps", type=int, required=True)
