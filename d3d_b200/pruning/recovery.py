@@ -265,7 +265,11 @@ def run_recovery(a, rank: int = 0, world: int = 1, device: Optional[torch.device
                            rows or 1 << 30)
     window["seed"] = a.seed
     torch.manual_seed(a.seed + rank)
-    teacher = load_model(teacher_path, device=device, mask_token_id=mask_id).eval()
+    # bf16 mixed precision on a GPU, as the reference's Accelerate run: a bf16
+    # frozen teacher, fp32 student parameters and master weights, bf16 matmuls
+    cuda = device.type == "cuda"
+    teacher = load_model(teacher_path, device=device, mask_token_id=mask_id,
+                         dtype=torch.bfloat16 if cuda else torch.float32).eval()
     for p in teacher.parameters():
         p.requires_grad_(False)
     student = load_model(student_path, device=device, mask_token_id=mask_id)
@@ -329,8 +333,9 @@ def run_recovery(a, rank: int = 0, world: int = 1, device: Optional[torch.device
                                          rng=random.Random(f"d3d-prune-{a.seed}-{pos}"), full_blocks=True)
         if batch is None:
             continue
-        terms = recovery_losses(student, teacher, retained, batch.to(device),
-                                torch.tensor([len(ex.prompt_ids)]))
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cuda):
+            terms = recovery_losses(student, teacher, retained, batch.to(device),
+                                    torch.tensor([len(ex.prompt_ids)]))
         loss = (LAMBDA_AR * terms["autoregressive_loss"] + LAMBDA_CE * terms["cross_entropy"]
                 + LAMBDA_KL * terms["kl"] + LAMBDA_H * terms["hidden"])
         (loss / a.gradient_accumulation_steps).backward()

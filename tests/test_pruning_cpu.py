@@ -327,3 +327,26 @@ def test_eight_bit_moments_track_fp32_adam():
     assert o2.step_count == 300
     with pytest.raises(ValueError):
         ShardedAdamW([q], state_bits=8, offload=True)
+
+
+def test_recovery_losses_under_bf16_autocast():
+    """The recovery objective runs under bf16 autocast with a bf16 teacher and
+    an fp32 student (the GPU configuration) and stays close to fp32."""
+    from d3d_b200.pruning.recovery import make_student, recovery_losses
+    from d3d_b200.train.blocks import build_packed_block_batch, synthetic_examples
+    parent = _model()
+    student = make_student(parent, 1)
+    exs = synthetic_examples(1, 48, 0.25, 1000, random.Random(4))
+    batch = build_packed_block_batch(exs, block_size=8, mask_token_id=int(parent.cfg.mask_token_id), max_anchors=3,
+                                     rng=random.Random(0), full_blocks=True)
+    plen = torch.tensor([len(exs[0].prompt_ids)])
+    ref = recovery_losses(student, parent, [0, 2, 3], batch, plen)
+    teacher16 = _model().to(torch.bfloat16)
+    with torch.autocast("cpu", dtype=torch.bfloat16):
+        got = recovery_losses(student, teacher16, [0, 2, 3], batch, plen)
+    loss = sum(got[k] for k in ("autoregressive_loss", "cross_entropy", "kl", "hidden"))
+    loss.backward()
+    assert all(p.grad is None or torch.isfinite(p.grad).all() for p in student.parameters())
+    for k in ("autoregressive_loss", "cross_entropy"):
+        g, r = float(got[k].detach()), float(ref[k].detach())
+        assert abs(g - r) < 0.05 * abs(r) + 0.05, k
