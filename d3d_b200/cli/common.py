@@ -96,6 +96,15 @@ def score_outputs(args, outputs: List[List[int]]) -> Optional[dict]:
             "accuracy": hits / scored if scored else None, "rows": rows}
 
 
+def check_devices(*devices) -> None:
+    """Exit with a clear message when a requested GPU does not exist (the
+    reference's hardware check, ``common/runtime.py:31-43``)."""
+    for d in devices:
+        dev = torch.device(d)
+        if dev.type == "cuda" and (not torch.cuda.is_available() or (dev.index or 0) >= torch.cuda.device_count()):
+            raise SystemExit(f"device {dev} is not available ({torch.cuda.device_count()} CUDA devices)")
+
+
 def is_preset(name: str) -> bool:
     return name in C.PRESETS and not Path(name).is_dir()
 

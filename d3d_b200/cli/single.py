@@ -20,8 +20,8 @@ from ..engine.spec import EOS_DEFAULT, DecodeConfig
 from ..utils.io import label, write_json
 from ..utils.runtime import runtime_metadata
 from ..utils.metrics import headline, source_stats, steps_from_output, summarize_acceptance
-from .common import (add_data_args, add_model_args, build_engine, load_selected_prompts, pin_host_threads,
-                     score_outputs)
+from .common import (add_data_args, add_model_args, build_engine, check_devices, load_selected_prompts,
+                     pin_host_threads, score_outputs)
 
 
 def parser() -> argparse.ArgumentParser:
@@ -104,9 +104,7 @@ def _engine(a, decode, max_context):
     process when the devices differ (or ``--verifier-process``)."""
     vdev = torch.device(a.verifier_device or a.device)
     ddev = torch.device(a.draft_device or vdev)
-    for dev in (vdev, ddev):       # the reference's hardware check (common/runtime.py:31-43)
-        if dev.type == "cuda" and (not torch.cuda.is_available() or (dev.index or 0) >= torch.cuda.device_count()):
-            raise SystemExit(f"device {dev} is not available ({torch.cuda.device_count()} CUDA devices)")
+    check_devices(vdev, ddev)
     if vdev == ddev and not a.verifier_process:
         a.device = str(vdev)
         eng = build_engine(a, decode, max_seqs=2, max_context=max_context)

@@ -25,7 +25,8 @@ from ..engine.sync import sync_generate, sync_generate_nocache
 from ..utils.io import label, write_json
 from ..utils.metrics import AcceptanceStep, step_dicts, summarize_acceptance, summarize_timing
 from ..utils.runtime import resolve_dtype, runtime_metadata
-from .common import add_data_args, add_model_args, load_module, load_selected_prompts, score_outputs
+from .common import (add_data_args, add_model_args, check_devices, load_module, load_selected_prompts,
+                     score_outputs)
 
 DTYPES = ("auto", "bf16", "bfloat16", "fp16", "float16", "fp32", "float32")
 
@@ -103,6 +104,7 @@ def main(argv=None):
     draft_tokens = a.draft_tokens if a.draft_tokens is not None else a.block_size - 1
     vdev = torch.device(a.verifier_device or a.device)
     ddev = torch.device(a.draft_device or vdev)
+    check_devices(vdev, ddev)
     t = load_module(a.target, vdev, a.seed).eval()
     d = load_module(a.draft, ddev, a.seed, a.draft_layers, a.mask_token_id).eval()
     if not getattr(d.cfg, "d3d_draft", False) and d.cfg.mask_token_id is None:
